@@ -1,0 +1,251 @@
+/*
+ * ti_b200.h — C ABI of the B200-native decode path (libti_b200.so).
+ *
+ * carbon-os/tensor-inference (the reference) has no C ABI (its README.md:32
+ * only announces one); its compute boundary is the C++ interface
+ * tensor::backend::{Device, Tensor, ops} (include/tensor/backend/*.hpp) and
+ * the models::CausalLM concept (include/tensor/models/concepts.hpp:16-23).
+ * Each entry point below names the reference interface it replaces.
+ *
+ * Conventions
+ *  - Every entry returns ti_status (0 = TI_OK) and never throws; on error a
+ *    thread-local message is available from ti_last_error().
+ *  - "device pointer" arguments are CUDA global-memory addresses on the
+ *    engine's / op's device; "host pointer" arguments are ordinary (optionally
+ *    pinned) host memory.  bf16 values travel as uint16_t bit patterns.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *  - Shapes are validated on the host before any launch; invalid arguments
+ *    return TI_ERR_INVALID and launch nothing.
+ */
+#ifndef TI_B200_H
+#define TI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int ti_status;
+enum {
+    TI_OK = 0,
+    TI_ERR_INVALID = 1,     /* bad argument / shape (reference: std::invalid_argument, ops.cu:144,552,561) */
+    TI_ERR_CUDA = 2,        /* CUDA runtime error (reference: std::runtime_error from cuda_check, ops.cu:19-22) */
+    TI_ERR_OOM = 3,         /* device or page-pool allocation failed */
+    TI_ERR_UNSUPPORTED = 4, /* valid request this build does not support (dtype, head_dim ...) */
+    TI_ERR_STATE = 5,       /* wrong object state (unknown sequence, KV cache full, ...) */
+    TI_ERR_TIMEOUT = 6,     /* a bounded device-side wait gave up (see ti_engine_check) */
+    TI_ERR_NOT_FOUND = 7    /* unknown tensor name (reference: parser::TensorNotFound, errors.hpp) */
+};
+
+const char* ti_last_error(void);
+int ti_version(void); /* major*10000 + minor*100 + patch */
+
+/* ================================================================= device
+ * replaces tensor::backend::Device (include/tensor/backend/device.hpp:10-42,
+ * src/backend/cuda/device.cu:15-43) and the allocation inside Tensor
+ * (src/backend/cuda/tensor.cu:72-121).  Allocations come from a
+ * stream-ordered caching pool, so per-op temporaries cost no cudaMalloc. */
+ti_status ti_device_count(int* count);
+ti_status ti_device_info(int device, char* name, size_t name_len, size_t* total_mem);
+ti_status ti_set_device(int device);
+ti_status ti_malloc(int device, size_t bytes, void** ptr);
+ti_status ti_free(int device, void* ptr);
+ti_status ti_memset(void* dst, int value, size_t bytes, void* stream);
+ti_status ti_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream);
+ti_status ti_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream);
+ti_status ti_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream);
+ti_status ti_stream_sync(void* stream);
+
+/* ================================================================= ops
+ * One entry per tensor::backend::ops function (include/tensor/backend/ops.hpp:19-117).
+ * All tensors are contiguous, row-major, device pointers; `out` never aliases
+ * an input unless stated.  Arithmetic and rounding points follow the
+ * reference kernel cited beside each entry. */
+enum { TI_DTYPE_F32 = 0, TI_DTYPE_BF16 = 1, TI_DTYPE_F16 = 2, TI_DTYPE_I32 = 3,
+       TI_DTYPE_Q4_0 = 16, TI_DTYPE_Q8_0 = 17 };
+
+/* ops.hpp:27 / ops.cu:46-88. ids: HOST array of n token ids. */
+ti_status ti_op_embedding(const void* weight, int vocab, int hidden, const int32_t* ids_host, int n,
+                          void* out, void* stream);
+/* ops.hpp:34 / ops.cu:94-148: c[M,N] = a[M,K] @ b[N,K]^T, fp32 accumulate; dtype BF16 or F32. */
+ti_status ti_op_matmul_t(int dtype, const void* a, const void* b, void* c, int M, int N, int K, void* stream);
+/* ops.hpp:40,114 / ops.cu:154-204,726-774: offset=1 adds 1 to the weight (Gemma). */
+ti_status ti_op_rms_norm(const void* x, const void* w, void* out, int rows, int hidden, float eps, int offset,
+                         void* stream);
+typedef struct {
+    int   apply_scaling;
+    float factor;
+    float low_freq_factor;
+    float high_freq_factor;
+    int   original_max_pos;
+} ti_rope_scaling;
+/* ops.hpp:46-62 / ops.cu:210-312. x: [seq, heads, head_dim]; scaling may be NULL (plain RoPE). */
+ti_status ti_op_rope(const void* x, void* out, int seq, int heads, int head_dim, int seq_offset, float theta,
+                     const ti_rope_scaling* scaling, void* stream);
+/* ops.hpp:67-73,111,117 / ops.cu:318-381,707-724,776-788 (bf16 in/out, fp32 math). */
+enum { TI_EW_SILU = 0, TI_EW_GELU = 1, TI_EW_MUL = 2, TI_EW_ADD = 3, TI_EW_MUL_SCALAR = 4 };
+ti_status ti_op_elementwise(int kind, const void* a, const void* b, float scalar, void* out, size_t n, void* stream);
+/* ops.hpp:106 / ops.cu:671-701: x [rows, hidden] + bias [hidden]. */
+ti_status ti_op_add_bias(const void* x, const void* bias, void* out, int rows, int hidden, void* stream);
+/* ops.hpp:78 / ops.cu:387-438: fp32 row softmax; x may be F32 or BF16, out is F32. */
+ti_status ti_op_softmax(int dtype, const void* x, float* out, int rows, int cols, void* stream);
+/* ops.hpp:87 / ops.cu:444-544: GQA attention, bf16 in/out, fp32 inside.
+ * q [seq, n_heads, hd], k/v [kv_len, n_kv, hd]; mask only when causal && seq > 1. */
+ti_status ti_op_attention(const void* q, const void* k, const void* v, void* out, int seq, int n_heads,
+                          int kv_len, int n_kv, int head_dim, int causal, int sliding_window, void* stream);
+/* ops.hpp:98 / ops.cu:586-616 (BF16<->F32; same dtype = copy). */
+ti_status ti_op_cast(int src_dtype, int dst_dtype, const void* x, void* out, size_t n, void* stream);
+/* ops.hpp:95 / ops.cu:559-584: 2-D transpose [rows, cols] -> [cols, rows], F32 or BF16. */
+ti_status ti_op_transpose2d(int dtype, const void* x, void* out, int rows, int cols, void* stream);
+
+/* ================================================================= engine
+ * The fused decode engine.  Replaces the per-token call chain
+ * Generator::generate -> Model::forward -> layer_forward -> ops::*
+ * (src/inference/generator.cpp:24-84, src/models/llama/llama_model.cpp:103-238,
+ * src/models/qwen/qwen_model.cpp:73-146, src/models/qwen/qwen_adapter_model.cpp:22-193,
+ * src/models/gemma/gemma_model.cpp:57-129, src/models/mistral/mistral_model.cpp:109-178)
+ * and the contiguous KVCache (include/tensor/models/kv_cache.hpp:24-59) with a
+ * paged bf16 KV cache of 16-token pages. */
+enum { TI_ARCH_LLAMA = 0, TI_ARCH_QWEN2 = 1, TI_ARCH_GEMMA = 2, TI_ARCH_MISTRAL = 3 };
+enum { TI_WFMT_BF16 = 0, TI_WFMT_Q4_0 = 1, TI_WFMT_Q8_0 = 2 };
+enum { TI_PROJ_Q = 1, TI_PROJ_K = 2, TI_PROJ_V = 4, TI_PROJ_O = 8, TI_PROJ_GATE = 16, TI_PROJ_UP = 32,
+       TI_PROJ_DOWN = 64 };
+
+typedef struct {
+    int   arch;                 /* TI_ARCH_* */
+    int   hidden, n_layers, n_heads, n_kv_heads, head_dim, intermediate, vocab;
+    float rms_eps, rope_theta;
+    ti_rope_scaling rope;
+    int   qkv_bias;             /* Qwen2: q/k/v carry a bias */
+    int   sliding_window;       /* Mistral; <= 0 = none */
+    int   weight_format;        /* TI_WFMT_*: storage of the layers' linear weights */
+} ti_model_desc;
+
+typedef struct {
+    int device;                 /* CUDA device index */
+    int max_batch;              /* sequences per decode step */
+    int max_seqs;               /* live sequences */
+    int max_seq_len;            /* tokens per sequence (page-table width = ceil(/16)) */
+    int kv_pages;               /* pages in the pool; 0 = max_seqs * ceil(max_seq_len/16) */
+    int max_adapters;           /* LoRA adapter slots resident in HBM (0 = LoRA off) */
+    int max_lora_rank;
+    int lora_proj_mask;         /* TI_PROJ_* the adapter slots reserve room for */
+    int tp_size, tp_rank;       /* tensor parallel group (1, 0 = single GPU) */
+    const void* nccl_id;        /* 128-byte ncclUniqueId shared by the TP group (NULL when tp_size == 1) */
+} ti_engine_opts;
+
+typedef struct ti_engine ti_engine;
+
+ti_status ti_engine_create(const ti_model_desc* desc, const ti_engine_opts* opts, ti_engine** out);
+ti_status ti_engine_destroy(ti_engine* e);
+/* device bytes held by weights / KV pool / adapters / work buffers */
+ti_status ti_engine_memory(const ti_engine* e, size_t* weights, size_t* kv, size_t* adapters, size_t* work);
+
+/* Upload one checkpoint tensor by its reference name ("model.embed_tokens.weight",
+ * "model.layers.{i}.self_attn.q_proj.weight", "...q_proj.bias", "lm_head.weight", ...),
+ * the names LlamaModel::load / QwenModel::load read (llama_model.cpp:47-72,
+ * qwen_model.cpp:28-52).  dtype TI_DTYPE_BF16 for every tensor; for the
+ * linear weights of a TI_WFMT_Q4_0 / Q8_0 engine, TI_DTYPE_Q4_0 / Q8_0 GGUF
+ * blocks (row-major, K/32 blocks per row) are accepted as well.  Under tensor
+ * parallelism the full tensor is passed and the engine keeps its shard. */
+ti_status ti_engine_load_tensor(ti_engine* e, const char* name, int dtype, const void* host_data, size_t bytes);
+/* Fill every weight on the device with the synthetic generator
+ * (element i of tensor `name` = f(seed, FNV-1a(name), i) ~ N(0, std)). */
+ti_status ti_engine_init_synthetic(ti_engine* e, uint64_t seed, float std_);
+/* Read back one weight (bf16, full tensor for TP rank 0 layouts) — tests. */
+ti_status ti_engine_read_tensor(ti_engine* e, const char* name, void* host_out, size_t bytes);
+
+/* sequences: replaces KVCache construction / clear (kv_cache.cpp:5-21, kv_cache.hpp:46-47) */
+ti_status ti_seq_create(ti_engine* e, int* seq_id);
+ti_status ti_seq_free(ti_engine* e, int seq_id);
+ti_status ti_seq_reset(ti_engine* e, int seq_id);
+ti_status ti_seq_len(ti_engine* e, int seq_id, int* len);
+/* pre-allocate pages so the sequence can grow to n_tokens without host work */
+ti_status ti_seq_reserve(ti_engine* e, int seq_id, int n_tokens);
+/* copy K or V (which = 0/1) of one layer for positions [0, len) into host memory
+ * as [len, n_kv_local, head_dim] bf16 (tests) */
+ti_status ti_seq_read_kv(ti_engine* e, int seq_id, int layer, int which, void* host_out, int len);
+
+enum { TI_LOGITS_NONE = 0, TI_LOGITS_BF16 = 1, TI_LOGITS_F32 = 2 };
+
+/* Run the prompt `ids[0..n)` through sequence `seq_id` (Model::forward with
+ * seq_len = n, llama_model.cpp:210).  Writes the greedy next id (argmax of the
+ * fp32 logits of the last row, lowest index on ties) to *next_id (host) and,
+ * if logits_out != NULL, the last row's logits (host, format logits_mode). */
+ti_status ti_engine_prefill(ti_engine* e, int seq_id, const int32_t* ids, int n, int adapter_id,
+                            int32_t* next_id, int logits_mode, void* logits_out);
+
+/* One decode step for `batch` sequences (Model::forward with one token each,
+ * generator.cpp:78; Greedy::sample, greedy.cpp:11-36, becomes a device argmax).
+ * Host pointers: tokens[batch], seq_ids[batch], adapter_ids[batch] (NULL = no
+ * adapter; -1 entries = none), next_ids[batch] out.  logits_out (host,
+ * [batch, vocab] in logits_mode) may be NULL.  Synchronous on `stream`. */
+ti_status ti_engine_decode(ti_engine* e, int batch, const int32_t* seq_ids, const int32_t* tokens,
+                           const int32_t* adapter_ids, int32_t* next_ids, int logits_mode, void* logits_out,
+                           void* stream);
+
+/* Device-resident chained decode: bind `batch` sequences once, then every
+ * ti_engine_decode_device call runs one step whose input tokens are the
+ * previous step's greedy ids, all on the device (no host synchronisation).
+ * Sequences must have pages reserved (ti_seq_reserve) for the steps run. */
+ti_status ti_engine_bind(ti_engine* e, int batch, const int32_t* seq_ids, const int32_t* first_tokens,
+                         const int32_t* adapter_ids);
+ti_status ti_engine_decode_device(ti_engine* e, void* stream);
+/* after a chain of device steps: read the last greedy ids (host) and commit
+ * the number of steps run to the sequences' lengths */
+ti_status ti_engine_unbind(ti_engine* e, int steps_run, int32_t* last_ids, void* stream);
+/* device pointer to the [batch, vocab] bf16 logits of the last step */
+ti_status ti_engine_logits_device(ti_engine* e, void** ptr);
+/* 0 if no bounded device wait has timed out since the last call, else TI_ERR_TIMEOUT */
+ti_status ti_engine_check(ti_engine* e);
+/* Diagnostic: launch ONE kernel of a decode step alone on `stream`, with the
+ * buffers of the last step (kind: 0 embed, 1 qkv GEMV, 2 attention, 3 o GEMV,
+ * 4 gate|up GEMV, 5 down GEMV, 6 LM head; layer ignored for 0 and 6).  Used to
+ * time and profile single kernels; no reference counterpart. */
+enum { TI_KERNEL_EMBED = 0, TI_KERNEL_QKV = 1, TI_KERNEL_ATTN = 2, TI_KERNEL_O = 3, TI_KERNEL_GATEUP = 4,
+       TI_KERNEL_DOWN = 5, TI_KERNEL_LMHEAD = 6 };
+ti_status ti_engine_launch_kernel(ti_engine* e, int kind, int layer, int batch, void* stream);
+/* kernels launched per decode step at this batch size (for launch accounting) */
+ti_status ti_engine_launches_per_step(ti_engine* e, int batch, int* launches);
+
+/* ================================================================= LoRA adapters
+ * replaces AdapterLoader / AdapterWeights (src/adapter/adapter_loader.cpp:132-236,
+ * include/tensor/adapter/adapter_weights.hpp:22-88) and apply_lora
+ * (qwen_adapter_model.cpp:22-43): delta = bf16(bf16(bf16(x A^T) B^T) * alpha/rank). */
+ti_status ti_adapter_create(ti_engine* e, int rank, float alpha, int proj_mask, int* adapter_id);
+/* names as the adapter checkpoint: "layers.{i}.self_attn.q_proj.lora_A" (A [rank, in]),
+ * "...lora_B" (B [out, rank]); 1-D flat tensors are accepted (adapter_loader.cpp:67-95). */
+ti_status ti_adapter_load_tensor(ti_engine* e, int adapter_id, const char* name, const void* host_bf16,
+                                 size_t bytes);
+ti_status ti_adapter_init_synthetic(ti_engine* e, int adapter_id, uint64_t seed, float std_a, float std_b);
+/* Async pinned host -> HBM fetch on the engine's side stream: the adapter's
+ * weights are staged in pinned host memory (ti_adapter_stage_host) and copied
+ * into a resident slot; decode steps that use it wait on the copy's event. */
+ti_status ti_adapter_stage_host(ti_engine* e, int adapter_id);
+ti_status ti_adapter_evict(ti_engine* e, int adapter_id);
+ti_status ti_adapter_prefetch_async(ti_engine* e, int adapter_id);
+ti_status ti_adapter_is_resident(ti_engine* e, int adapter_id, int* resident);
+
+/* ================================================================= PKM router
+ * Spec only in the reference (README.md:58-72,157-180): two codebooks of
+ * n_codes x half_dim fp32; a query [2*half_dim] is split in halves, each half
+ * takes the argmin squared-L2 code (canonical fp32 order: d = q-c,
+ * acc = fma(d, d, acc) over t = 0..half_dim-1; lowest index on ties);
+ * address = i * n_codes + j; adapter = registry[address] or -1. */
+typedef struct ti_pkm ti_pkm;
+ti_status ti_pkm_create(int device, int n_codes, int half_dim, const float* c1_host, const float* c2_host,
+                        ti_pkm** out);
+ti_status ti_pkm_destroy(ti_pkm* p);
+/* register adapters by centroid ([n, 2*half_dim] host fp32); collisions keep the lowest id */
+ti_status ti_pkm_register(ti_pkm* p, const float* centroids_host, const int32_t* adapter_ids, int n);
+/* device pointers: queries [n, 2*half_dim] fp32 -> addr[n], adapter[n] int32 */
+ti_status ti_pkm_query(ti_pkm* p, const float* queries, int n, int32_t* addr, int32_t* adapter, void* stream);
+/* same with host buffers (copies inside, synchronous) */
+ti_status ti_pkm_query_host(ti_pkm* p, const float* queries, int n, int32_t* addr, int32_t* adapter);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TI_B200_H */

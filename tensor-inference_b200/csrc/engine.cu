@@ -1,0 +1,895 @@
+// engine.cu — the fused decode engine behind the ti_engine_* / ti_seq_* C ABI.
+//
+// Replaces, per generated token, Generator::generate -> Model::forward ->
+// layer_forward -> ops::* (generator.cpp:24-84, llama_model.cpp:103-238,
+// qwen_model.cpp:73-146, qwen_adapter_model.cpp:66-193, gemma_model.cpp:57-129,
+// mistral_model.cpp:109-178) with one CUDA graph per batch size:
+//   embed -> L x [qkv GEMV (+RMSNorm, +bias, +LoRA), attention (+RoPE, +KV append),
+//   o GEMV (+residual), gate|up GEMV (+RMSNorm, +SiLU*up), down GEMV (+residual)]
+//   -> LM-head GEMV (+final RMSNorm, +greedy argmax)
+// every launch chained by programmatic dependent launch.
+//
+// HBM layout (per engine):
+//   weights    embed [V, H]; per layer norm1, norm2 [H], Wqkv [(nq+2nkv)hd, H]
+//              (q rows, k rows, v rows of this rank), bqkv, Wo [H, nq*hd],
+//              Wgu [2*I, H] (gate rows then up rows), Wdown [H, I]; final norm;
+//              lm_head [V_local, H].
+//   KV pool    K and V each [L][n_pages][nkv][16][hd] bf16 — a 16-token page of
+//              one kv head is 16*hd*2 bytes contiguous; pages are shared by all
+//              layers (one page id per 16 positions of a sequence).
+//   page table [max_seqs][ceil(max_seq_len/16)] int32, -1 = unallocated.
+#include <algorithm>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+#include "kernels.h"
+#include "synth.cuh"
+
+using namespace ti;
+
+namespace {
+
+constexpr int kPageTokens = 16;
+
+struct Slot {
+    // a checkpoint tensor [rows, cols] of which this rank holds the window
+    // rows [r0, r0+nr) x cols [c0, c0+nc), stored at dst with row stride ld
+    std::string name;
+    size_t rows = 0, cols = 0;
+    size_t r0 = 0, nr = 0, c0 = 0, nc = 0;
+    uint16_t* dst = nullptr;
+    size_t ld = 0;
+    bool linear = false;
+};
+
+struct LayerW {
+    uint16_t *norm1 = nullptr, *norm2 = nullptr, *wqkv = nullptr, *bqkv = nullptr, *wo = nullptr, *wgu = nullptr,
+             *wdown = nullptr;
+};
+
+struct SeqState {
+    bool live = false;
+    int len = 0;
+    std::vector<int> pages;
+};
+
+struct GraphEntry {
+    cudaGraphExec_t exec = nullptr;
+    int launches = 0;
+};
+
+}  // namespace
+
+struct ti_engine {
+    ti_model_desc d{};
+    ti_engine_opts o{};
+    int dev = 0, sms = 148;
+    int H = 0, nq = 0, nkv = 0, hd = 0, I = 0, V = 0, Vl = 0, qkv_rows = 0;
+    cudaStream_t cap = nullptr;  // capture stream
+
+    // device memory
+    std::vector<void*> allocs;
+    size_t bytes_w = 0, bytes_kv = 0, bytes_ad = 0, bytes_work = 0;
+    uint16_t *embed = nullptr, *final_norm = nullptr, *lm_head = nullptr;
+    std::vector<LayerW> layers;
+    float* freqs = nullptr;
+    uint16_t *kpool = nullptr, *vpool = nullptr;
+    size_t kv_layer_elems = 0;
+    int n_pages = 0, pt_stride = 0;
+    int32_t* page_table = nullptr;
+    std::vector<int> free_pages;
+    std::vector<SeqState> seqs;
+
+    // step descriptor: [n_updates, window, 0, 0][tokens B][seq B][pos B][adapter B][updates 3B]
+    int32_t *d_desc = nullptr, *h_desc = nullptr;
+    int desc_ints = 0;
+    uint16_t *hidden = nullptr, *res1 = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr;
+    unsigned long long* amax = nullptr;
+    unsigned int* done = nullptr;
+    int32_t* out = nullptr;  // [ids B][err]
+    int32_t* h_out = nullptr;
+    int* err = nullptr;
+    float *part_o = nullptr, *part_ml = nullptr;
+    unsigned int* counters = nullptr;
+    int attn_splits_n = 1, attn_max_chunk = 0;
+
+    std::vector<Slot> slots;
+    std::map<std::string, size_t> slot_index;
+    std::map<int, GraphEntry> graphs;
+
+    int bound_batch = 0;
+    std::vector<int> bound_seqs;
+
+    int32_t* dd_tokens() const { return d_desc + 4; }
+    int32_t* dd_seq() const { return d_desc + 4 + o.max_batch; }
+    int32_t* dd_pos() const { return d_desc + 4 + 2 * o.max_batch; }
+    int32_t* dd_adapter() const { return d_desc + 4 + 3 * o.max_batch; }
+    int32_t* dd_updates() const { return d_desc + 4 + 4 * o.max_batch; }
+};
+
+namespace {
+
+ti_status dalloc(ti_engine* e, void** p, size_t bytes, size_t* acct) {
+    cudaError_t err = cudaMalloc(p, bytes ? bytes : 16);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(TI_ERR_OOM, "engine: cudaMalloc(%zu bytes) failed: %s", bytes, cudaGetErrorString(err));
+    }
+    e->allocs.push_back(*p);
+    if (acct) *acct += bytes;
+    return TI_OK;
+}
+
+template <class T>
+ti_status dalloc_t(ti_engine* e, T** p, size_t count, size_t* acct) {
+    return dalloc(e, reinterpret_cast<void**>(p), count * sizeof(T), acct);
+}
+
+void free_all(ti_engine* e) {
+    for (auto& kv : e->graphs)
+        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    e->graphs.clear();
+    for (void* p : e->allocs) cudaFree(p);
+    e->allocs.clear();
+    if (e->h_desc) cudaFreeHost(e->h_desc);
+    if (e->h_out) cudaFreeHost(e->h_out);
+    e->h_desc = nullptr;
+    e->h_out = nullptr;
+    if (e->cap) cudaStreamDestroy(e->cap);
+    e->cap = nullptr;
+}
+
+void add_slot(ti_engine* e, const std::string& name, size_t rows, size_t cols, size_t r0, size_t nr, size_t c0,
+              size_t nc, uint16_t* dst, size_t ld, bool linear) {
+    Slot s;
+    s.name = name;
+    s.rows = rows;
+    s.cols = cols;
+    s.r0 = r0;
+    s.nr = nr;
+    s.c0 = c0;
+    s.nc = nc;
+    s.dst = dst;
+    s.ld = ld;
+    s.linear = linear;
+    e->slot_index[name] = e->slots.size();
+    e->slots.push_back(s);
+}
+
+ti_status validate_desc(const ti_model_desc* d, const ti_engine_opts* o) {
+    TI_CHECK(d && o, TI_ERR_INVALID, "engine: null desc/opts");
+    TI_CHECK(d->arch >= TI_ARCH_LLAMA && d->arch <= TI_ARCH_MISTRAL, TI_ERR_INVALID, "engine: unknown arch %d",
+             d->arch);
+    TI_CHECK(d->hidden > 0 && d->n_layers > 0 && d->n_heads > 0 && d->n_kv_heads > 0 && d->head_dim > 0 &&
+                 d->intermediate > 0 && d->vocab > 0,
+             TI_ERR_INVALID, "engine: non-positive dimension");
+    TI_CHECK(d->n_heads % d->n_kv_heads == 0, TI_ERR_INVALID, "engine: n_heads %% n_kv_heads != 0");
+    TI_CHECK(d->n_heads / d->n_kv_heads <= 16, TI_ERR_UNSUPPORTED, "engine: GQA group > 16");
+    TI_CHECK(d->head_dim == 64 || d->head_dim == 128 || d->head_dim == 256, TI_ERR_UNSUPPORTED,
+             "engine: head_dim %d (64/128/256 supported)", d->head_dim);
+    TI_CHECK(d->hidden % 64 == 0 && d->intermediate % 64 == 0 && (d->n_heads * d->head_dim) % 64 == 0,
+             TI_ERR_UNSUPPORTED, "engine: hidden, intermediate and n_heads*head_dim must be multiples of 64");
+    TI_CHECK(d->weight_format == TI_WFMT_BF16, TI_ERR_UNSUPPORTED, "engine: weight format %d not built yet",
+             d->weight_format);
+    TI_CHECK(o->max_batch >= 1 && o->max_batch <= 256, TI_ERR_INVALID, "engine: max_batch out of range");
+    TI_CHECK(o->max_seqs >= 1, TI_ERR_INVALID, "engine: max_seqs < 1");
+    TI_CHECK(o->max_seq_len >= 1, TI_ERR_INVALID, "engine: max_seq_len < 1");
+    const int tp = o->tp_size <= 0 ? 1 : o->tp_size;
+    TI_CHECK(tp == 1, TI_ERR_UNSUPPORTED, "engine: tensor parallelism is driven by ti_engine_create with tp_size 1 "
+                                          "in this build");
+    return TI_OK;
+}
+
+ti_status build(ti_engine* e) {
+    const ti_model_desc& d = e->d;
+    DeviceGuard g(e->dev);
+    e->sms = num_sms(e->dev);
+    e->H = d.hidden;
+    e->nq = d.n_heads;
+    e->nkv = d.n_kv_heads;
+    e->hd = d.head_dim;
+    e->I = d.intermediate;
+    e->V = d.vocab;
+    e->Vl = d.vocab;
+    e->qkv_rows = (e->nq + 2 * e->nkv) * e->hd;
+    const int H = e->H, I = e->I, hd = e->hd, nq = e->nq, nkv = e->nkv;
+    const size_t QW = (size_t)nq * hd;
+
+    TI_CUDA(cudaStreamCreateWithFlags(&e->cap, cudaStreamNonBlocking));
+
+    // ---- weights
+    TI_CHECK(dalloc_t(e, &e->embed, (size_t)e->V * H, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+    add_slot(e, "model.embed_tokens.weight", e->V, H, 0, e->V, 0, H, e->embed, H, false);
+    TI_CHECK(dalloc_t(e, &e->final_norm, H, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+    add_slot(e, "model.norm.weight", 1, H, 0, 1, 0, H, e->final_norm, H, false);
+    TI_CHECK(dalloc_t(e, &e->lm_head, (size_t)e->Vl * H, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+    add_slot(e, "lm_head.weight", e->V, H, 0, e->Vl, 0, H, e->lm_head, H, false);
+    e->layers.resize(d.n_layers);
+    for (int i = 0; i < d.n_layers; ++i) {
+        LayerW& l = e->layers[i];
+        const std::string p = "model.layers." + std::to_string(i) + ".";
+        TI_CHECK(dalloc_t(e, &l.norm1, H, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+        TI_CHECK(dalloc_t(e, &l.norm2, H, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+        TI_CHECK(dalloc_t(e, &l.wqkv, (size_t)e->qkv_rows * H, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s",
+                 ti_last_error());
+        TI_CHECK(dalloc_t(e, &l.wo, (size_t)H * QW, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+        TI_CHECK(dalloc_t(e, &l.wgu, (size_t)2 * I * H, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+        TI_CHECK(dalloc_t(e, &l.wdown, (size_t)H * I, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+        add_slot(e, p + "input_layernorm.weight", 1, H, 0, 1, 0, H, l.norm1, H, false);
+        add_slot(e, p + "post_attention_layernorm.weight", 1, H, 0, 1, 0, H, l.norm2, H, false);
+        add_slot(e, p + "self_attn.q_proj.weight", QW, H, 0, QW, 0, H, l.wqkv, H, true);
+        add_slot(e, p + "self_attn.k_proj.weight", (size_t)nkv * hd, H, 0, (size_t)nkv * hd, 0, H,
+                 l.wqkv + QW * H, H, true);
+        add_slot(e, p + "self_attn.v_proj.weight", (size_t)nkv * hd, H, 0, (size_t)nkv * hd, 0, H,
+                 l.wqkv + (QW + (size_t)nkv * hd) * H, H, true);
+        add_slot(e, p + "self_attn.o_proj.weight", H, QW, 0, H, 0, QW, l.wo, QW, true);
+        add_slot(e, p + "mlp.gate_proj.weight", I, H, 0, I, 0, H, l.wgu, H, true);
+        add_slot(e, p + "mlp.up_proj.weight", I, H, 0, I, 0, H, l.wgu + (size_t)I * H, H, true);
+        add_slot(e, p + "mlp.down_proj.weight", H, I, 0, H, 0, I, l.wdown, I, true);
+        if (d.qkv_bias) {
+            TI_CHECK(dalloc_t(e, &l.bqkv, e->qkv_rows, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+            add_slot(e, p + "self_attn.q_proj.bias", 1, QW, 0, 1, 0, QW, l.bqkv, QW, false);
+            add_slot(e, p + "self_attn.k_proj.bias", 1, (size_t)nkv * hd, 0, 1, 0, (size_t)nkv * hd, l.bqkv + QW,
+                     (size_t)nkv * hd, false);
+            add_slot(e, p + "self_attn.v_proj.bias", 1, (size_t)nkv * hd, 0, 1, 0, (size_t)nkv * hd,
+                     l.bqkv + QW + (size_t)nkv * hd, (size_t)nkv * hd, false);
+        }
+    }
+    std::vector<float> fr(hd / 2);
+    rope_freqs(hd, d.rope_theta, &d.rope, fr.data());
+    TI_CHECK(dalloc_t(e, &e->freqs, hd / 2, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+    TI_CUDA(cudaMemcpy(e->freqs, fr.data(), fr.size() * 4, cudaMemcpyHostToDevice));
+
+    // ---- KV pool and page table
+    e->pt_stride = (e->o.max_seq_len + kPageTokens - 1) / kPageTokens;
+    e->n_pages = e->o.kv_pages > 0 ? e->o.kv_pages : e->o.max_seqs * e->pt_stride;
+    e->kv_layer_elems = (size_t)e->n_pages * nkv * kPageTokens * hd;
+    TI_CHECK(dalloc_t(e, &e->kpool, e->kv_layer_elems * d.n_layers, &e->bytes_kv) == TI_OK, TI_ERR_OOM, "%s",
+             ti_last_error());
+    TI_CHECK(dalloc_t(e, &e->vpool, e->kv_layer_elems * d.n_layers, &e->bytes_kv) == TI_OK, TI_ERR_OOM, "%s",
+             ti_last_error());
+    TI_CHECK(dalloc_t(e, &e->page_table, (size_t)e->o.max_seqs * e->pt_stride, &e->bytes_kv) == TI_OK, TI_ERR_OOM,
+             "%s", ti_last_error());
+    TI_CUDA(cudaMemset(e->page_table, 0xff, (size_t)e->o.max_seqs * e->pt_stride * 4));
+    e->free_pages.resize(e->n_pages);
+    for (int i = 0; i < e->n_pages; ++i) e->free_pages[i] = e->n_pages - 1 - i;
+    e->seqs.assign(e->o.max_seqs, SeqState{});
+
+    // ---- step buffers
+    const int B = e->o.max_batch;
+    e->desc_ints = 4 + 7 * B;
+    TI_CHECK(dalloc_t(e, &e->d_desc, e->desc_ints, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+    TI_CUDA(cudaMemset(e->d_desc, 0, e->desc_ints * 4));
+    TI_CUDA(cudaMallocHost(&e->h_desc, e->desc_ints * 4));
+    TI_CUDA(cudaMallocHost(&e->h_out, (B + 1) * 4));
+    TI_CHECK(dalloc_t(e, &e->hidden, (size_t)B * H, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+    TI_CHECK(dalloc_t(e, &e->res1, (size_t)B * H, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+    TI_CHECK(dalloc_t(e, &e->qkv, (size_t)B * e->qkv_rows, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
+             ti_last_error());
+    TI_CHECK(dalloc_t(e, &e->attn, (size_t)B * QW, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+    TI_CHECK(dalloc_t(e, &e->act, (size_t)B * I, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+    TI_CHECK(dalloc_t(e, &e->logits, (size_t)B * e->Vl, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
+             ti_last_error());
+    TI_CHECK(dalloc_t(e, &e->amax, B, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+    TI_CUDA(cudaMemset(e->amax, 0, B * 8));
+    TI_CHECK(dalloc_t(e, &e->done, 16, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+    TI_CUDA(cudaMemset(e->done, 0, 64));
+    TI_CHECK(dalloc_t(e, &e->out, B + 1, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+    TI_CUDA(cudaMemset(e->out, 0, (B + 1) * 4));
+    e->err = reinterpret_cast<int*>(e->out + B);
+    e->attn_splits_n = attn_splits(B, nkv, e->o.max_seq_len, e->sms, &e->attn_max_chunk);
+    // partials sized for the largest batch; smaller batches use more splits per (token, head)
+    int max_parts = 0;
+    for (int b = 1; b <= B; ++b) {
+        int mc = 0;
+        int n = attn_splits(b, nkv, e->o.max_seq_len, e->sms, &mc);
+        max_parts = std::max(max_parts, b * n);
+    }
+    const int G = nq / nkv;
+    TI_CHECK(dalloc_t(e, &e->part_o, (size_t)max_parts * nkv * G * hd, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
+             ti_last_error());
+    TI_CHECK(dalloc_t(e, &e->part_ml, (size_t)max_parts * nkv * G * 2, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
+             ti_last_error());
+    TI_CHECK(dalloc_t(e, &e->counters, (size_t)B * nkv, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+    TI_CUDA(cudaMemset(e->counters, 0, (size_t)B * nkv * 4));
+    TI_CUDA(cudaDeviceSynchronize());
+    return TI_OK;
+}
+
+// ------------------------------------------------------------------ the kernels of one step
+enum KernelKind { kKEmbed = 0, kKQkv = 1, kKAttn = 2, kKO = 3, kKGateUp = 4, kKDown = 5, kKLmHead = 6 };
+
+// Enqueue one kernel of a B-token step on `s` (graph capture or a plain launch).
+ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, int* launches) {
+    const ti_model_desc& d = e->d;
+    const int H = e->H, I = e->I, nq = e->nq, nkv = e->nkv, hd = e->hd;
+    const int QW = nq * hd;
+    const bool gemma = d.arch == TI_ARCH_GEMMA;
+    std::string why;
+
+    // SIMT GEMV: batch chunks of <= 8 tokens
+    auto gemv_all = [&](GemvArgs a, int epi, int x_stride_elems, int out_stride, int resid_stride) -> ti_status {
+        for (int b0 = 0; b0 < B; b0 += 8) {
+            GemvArgs c = a;
+            c.nb = std::min(8, B - b0);
+            c.x = a.x + (size_t)b0 * x_stride_elems;
+            c.out = a.out + (size_t)b0 * out_stride;
+            if (a.resid) c.resid = a.resid + (size_t)b0 * resid_stride;
+            if (epi == kEpiLmHead) {
+                c.amax = a.amax + b0;
+                c.done = a.done + (b0 / 8) % 16;  // one completion counter per launch
+                c.out_ids = a.out_ids + b0;
+                if (a.chain_tokens) c.chain_tokens = a.chain_tokens + b0;
+                if (a.chain_pos) c.chain_pos = a.chain_pos + b0;
+            }
+            GemvPlan plan;
+            if (!gemv_plan(c, epi, e->dev, &plan, &why)) return fail(TI_ERR_UNSUPPORTED, "%s", why.c_str());
+            TI_CUDA(gemv_launch(c, epi, plan, s, true));
+            if (launches) ++*launches;
+        }
+        return TI_OK;
+    };
+
+    if (kind == kKEmbed) {
+        EmbedArgs ea;
+        ea.table = e->embed;
+        ea.vocab = e->V;
+        ea.hidden = H;
+        ea.nb = B;
+        ea.tokens = e->dd_tokens();
+        ea.out = e->hidden;
+        ea.scale = gemma ? std::sqrt((float)H) : 0.f;
+        ea.pt_updates = e->dd_updates();
+        ea.n_updates = e->d_desc;
+        ea.page_table = e->page_table;
+        ea.pt_stride = e->pt_stride;
+        ea.err = e->err;
+        TI_CUDA(embed_launch(ea, s, true));
+        if (launches) ++*launches;
+        return TI_OK;
+    }
+    if (kind == kKLmHead) {
+        GemvArgs lm;
+        lm.W = e->lm_head;
+        lm.N = e->Vl;
+        lm.K = H;
+        lm.x = e->hidden;
+        lm.x_stride = H;
+        lm.norm_w = e->final_norm;
+        lm.eps = d.rms_eps;
+        lm.norm_offset = gemma;
+        lm.out = e->logits;
+        lm.out_stride = e->Vl;
+        lm.amax = e->amax;
+        lm.done = e->done;
+        lm.out_ids = e->out;
+        lm.chain_tokens = e->dd_tokens();
+        lm.chain_pos = e->dd_pos();
+        lm.err = e->err;
+        return gemv_all(lm, kEpiLmHead, H, e->Vl, 0);
+    }
+    TI_CHECK(li >= 0 && li < d.n_layers, TI_ERR_INVALID, "layer %d out of range", li);
+    const LayerW& l = e->layers[li];
+    switch (kind) {
+        case kKQkv: {
+            GemvArgs q;
+            q.W = l.wqkv;
+            q.N = e->qkv_rows;
+            q.K = H;
+            q.x = e->hidden;
+            q.x_stride = H;
+            q.norm_w = l.norm1;
+            q.eps = d.rms_eps;
+            q.norm_offset = gemma;
+            q.out = e->qkv;
+            q.out_stride = e->qkv_rows;
+            q.bias = l.bqkv;
+            q.err = e->err;
+            return gemv_all(q, kEpiStore, H, e->qkv_rows, 0);
+        }
+        case kKAttn: {
+            int mc = 0;
+            const int splits = attn_splits(B, nkv, e->o.max_seq_len, e->sms, &mc);
+            AttnArgs at;
+            at.qkv = e->qkv;
+            at.qkv_stride = e->qkv_rows;
+            at.nb = B;
+            at.nq = nq;
+            at.nkv = nkv;
+            at.hd = hd;
+            at.pos = e->dd_pos();
+            at.seq = e->dd_seq();
+            at.page_table = e->page_table;
+            at.pt_stride = e->pt_stride;
+            at.kc = e->kpool + (size_t)li * e->kv_layer_elems;
+            at.vc = e->vpool + (size_t)li * e->kv_layer_elems;
+            at.freqs = e->freqs;
+            at.scale = 1.0f / sqrtf((float)hd);  // ops.cu:455
+            at.window = d.arch == TI_ARCH_MISTRAL ? e->d_desc + 1 : nullptr;
+            at.n_pages = e->n_pages;
+            at.n_splits = splits;
+            at.max_chunk = mc;
+            at.part_o = e->part_o;
+            at.part_ml = e->part_ml;
+            at.counters = e->counters;
+            at.out = e->attn;
+            at.out_stride = QW;
+            at.err = e->err;
+            TI_CUDA(attn_launch(at, s, true));
+            if (launches) ++*launches;
+            return TI_OK;
+        }
+        case kKO: {
+            GemvArgs ov;
+            ov.W = l.wo;
+            ov.N = H;
+            ov.K = QW;
+            ov.x = e->attn;
+            ov.x_stride = QW;
+            ov.out = e->res1;
+            ov.out_stride = H;
+            ov.resid = e->hidden;
+            ov.resid_stride = H;
+            ov.err = e->err;
+            return gemv_all(ov, kEpiResid, QW, H, H);
+        }
+        case kKGateUp: {
+            GemvArgs gu;
+            gu.W = l.wgu;
+            gu.N = I;
+            gu.K = H;
+            gu.x = e->res1;
+            gu.x_stride = H;
+            gu.norm_w = l.norm2;
+            gu.eps = d.rms_eps;
+            gu.norm_offset = gemma;
+            gu.out = e->act;
+            gu.out_stride = I;
+            gu.act = gemma ? 1 : 0;
+            gu.err = e->err;
+            return gemv_all(gu, kEpiGlu, H, I, 0);
+        }
+        case kKDown: {
+            GemvArgs dn;
+            dn.W = l.wdown;
+            dn.N = H;
+            dn.K = I;
+            dn.x = e->act;
+            dn.x_stride = I;
+            dn.out = e->hidden;
+            dn.out_stride = H;
+            dn.resid = e->res1;
+            dn.resid_stride = H;
+            dn.err = e->err;
+            return gemv_all(dn, kEpiResid, I, H, H);
+        }
+        default: return fail(TI_ERR_INVALID, "unknown kernel kind %d", kind);
+    }
+}
+
+ti_status enqueue_step(ti_engine* e, int B, cudaStream_t s, int* launches) {
+    if (ti_status st = enqueue_kernel(e, B, kKEmbed, 0, s, launches)) return st;
+    for (int li = 0; li < e->d.n_layers; ++li)
+        for (int k : {kKQkv, kKAttn, kKO, kKGateUp, kKDown})
+            if (ti_status st = enqueue_kernel(e, B, k, li, s, launches)) return st;
+    return enqueue_kernel(e, B, kKLmHead, 0, s, launches);
+}
+
+ti_status capture_step(ti_engine* e, int B, GraphEntry* out) {
+    cudaStream_t s = e->cap;
+    int launches = 0;
+    TI_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    ti_status st = enqueue_step(e, B, s, &launches);
+    cudaGraph_t graph = nullptr;
+    cudaError_t ce = cudaStreamEndCapture(s, &graph);
+    if (st) {
+        if (graph) cudaGraphDestroy(graph);
+        cudaGetLastError();
+        return st;
+    }
+    TI_CHECK(ce == cudaSuccess, TI_ERR_CUDA, "cudaStreamEndCapture: %s", cudaGetErrorString(ce));
+    cudaGraphExec_t exec = nullptr;
+    cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    TI_CHECK(ie == cudaSuccess, TI_ERR_CUDA, "cudaGraphInstantiate: %s", cudaGetErrorString(ie));
+    out->exec = exec;
+    out->launches = launches;
+    return TI_OK;
+}
+
+ti_status get_graph(ti_engine* e, int B, GraphEntry** g) {
+    auto it = e->graphs.find(B);
+    if (it == e->graphs.end()) {
+        GraphEntry ge;
+        if (ti_status st = capture_step(e, B, &ge)) return st;
+        it = e->graphs.emplace(B, ge).first;
+    }
+    *g = &it->second;
+    return TI_OK;
+}
+
+ti_status seq_check(ti_engine* e, int sid) {
+    TI_CHECK(sid >= 0 && sid < (int)e->seqs.size() && e->seqs[sid].live, TI_ERR_STATE, "unknown sequence %d", sid);
+    return TI_OK;
+}
+
+// ensure pages cover positions [0, upto); page ids appended to `updates` as (seq, idx, page)
+ti_status ensure_pages(ti_engine* e, int sid, int upto, std::vector<int32_t>* updates) {
+    SeqState& s = e->seqs[sid];
+    const int need = (upto + kPageTokens - 1) / kPageTokens;
+    TI_CHECK(need <= e->pt_stride, TI_ERR_STATE, "sequence %d: %d tokens exceed max_seq_len %d", sid, upto,
+             e->o.max_seq_len);
+    while ((int)s.pages.size() < need) {
+        TI_CHECK(!e->free_pages.empty(), TI_ERR_OOM, "KV page pool exhausted (%d pages)", e->n_pages);
+        const int p = e->free_pages.back();
+        e->free_pages.pop_back();
+        updates->push_back(sid);
+        updates->push_back((int)s.pages.size());
+        updates->push_back(p);
+        s.pages.push_back(p);
+    }
+    return TI_OK;
+}
+
+ti_status read_err(ti_engine* e, int32_t word) {
+    if (word) {
+        int zero = 0;
+        cudaMemcpy(e->err, &zero, 4, cudaMemcpyHostToDevice);
+        return fail(word & (kErrTimeoutFull | kErrTimeoutEmpty | kErrTimeoutPeer) ? TI_ERR_TIMEOUT : TI_ERR_STATE,
+                    "device reported error bits 0x%x", word);
+    }
+    return TI_OK;
+}
+
+// One step for `B` sequences with host inputs; `window` is the sliding window
+// applied (prefill semantics) or -1 (decode semantics, as the reference).
+ti_status run_step(ti_engine* e, int B, const int32_t* seq_ids, const int32_t* tokens, const int32_t* adapters,
+                   int window, int32_t* next_ids, int logits_mode, void* logits_out, cudaStream_t stream) {
+    TI_CHECK(B >= 1 && B <= e->o.max_batch, TI_ERR_INVALID, "batch %d out of range [1, %d]", B, e->o.max_batch);
+    TI_CHECK(seq_ids && tokens, TI_ERR_INVALID, "null seq_ids/tokens");
+    TI_CHECK(e->bound_batch == 0, TI_ERR_STATE, "engine is bound to a device chain; unbind first");
+    std::vector<int32_t> upd;
+    for (int b = 0; b < B; ++b) {
+        if (ti_status st = seq_check(e, seq_ids[b])) return st;
+        for (int c = 0; c < b; ++c)
+            TI_CHECK(seq_ids[c] != seq_ids[b], TI_ERR_INVALID, "sequence %d appears twice in one step", seq_ids[b]);
+        TI_CHECK(tokens[b] >= 0 && tokens[b] < e->V, TI_ERR_INVALID, "token %d out of range [0, %d)", tokens[b], e->V);
+        TI_CHECK(!adapters || adapters[b] < 0, TI_ERR_UNSUPPORTED, "LoRA adapters are not built in this engine yet");
+        const int len = e->seqs[seq_ids[b]].len;
+        TI_CHECK(len < e->o.max_seq_len, TI_ERR_STATE, "sequence %d is full (%d tokens)", seq_ids[b], len);
+        if (ti_status st = ensure_pages(e, seq_ids[b], len + 1, &upd)) return st;
+    }
+    const int MB = e->o.max_batch;
+    int32_t* h = e->h_desc;
+    h[0] = (int32_t)(upd.size() / 3);
+    h[1] = window;
+    h[2] = h[3] = 0;
+    for (int b = 0; b < B; ++b) {
+        h[4 + b] = tokens[b];
+        h[4 + MB + b] = seq_ids[b];
+        h[4 + 2 * MB + b] = e->seqs[seq_ids[b]].len;
+        h[4 + 3 * MB + b] = adapters ? adapters[b] : -1;
+    }
+    TI_CHECK((int)upd.size() <= 3 * MB, TI_ERR_STATE, "too many page updates in one step");
+    std::memcpy(h + 4 + 4 * MB, upd.data(), upd.size() * 4);
+    GraphEntry* g = nullptr;
+    if (ti_status st = get_graph(e, B, &g)) return st;
+    TI_CUDA(cudaMemcpyAsync(e->d_desc, h, (size_t)e->desc_ints * 4, cudaMemcpyHostToDevice, stream));
+    TI_CUDA(cudaGraphLaunch(g->exec, stream));
+    TI_CUDA(cudaMemcpyAsync(e->h_out, e->out, (size_t)(MB + 1) * 4, cudaMemcpyDeviceToHost, stream));
+    if (logits_out && logits_mode == TI_LOGITS_BF16)
+        TI_CUDA(cudaMemcpyAsync(logits_out, e->logits, (size_t)B * e->Vl * 2, cudaMemcpyDeviceToHost, stream));
+    TI_CUDA(cudaStreamSynchronize(stream));
+    if (logits_out && logits_mode == TI_LOGITS_F32) {
+        std::vector<uint16_t> tmp((size_t)B * e->Vl);
+        TI_CUDA(cudaMemcpy(tmp.data(), e->logits, tmp.size() * 2, cudaMemcpyDeviceToHost));
+        float* f = reinterpret_cast<float*>(logits_out);
+        for (size_t i = 0; i < tmp.size(); ++i) {
+            uint32_t u = (uint32_t)tmp[i] << 16;
+            std::memcpy(&f[i], &u, 4);
+        }
+    }
+    if (ti_status st = read_err(e, e->h_out[MB])) return st;
+    for (int b = 0; b < B; ++b) {
+        e->seqs[seq_ids[b]].len += 1;
+        if (next_ids) next_ids[b] = e->h_out[b];
+    }
+    return TI_OK;
+}
+
+}  // namespace
+
+// ==================================================================== C ABI
+extern "C" {
+
+ti_status ti_engine_create(const ti_model_desc* desc, const ti_engine_opts* opts, ti_engine** out) {
+    clear_error();
+    TI_CHECK(out, TI_ERR_INVALID, "ti_engine_create: null out");
+    *out = nullptr;
+    if (ti_status st = validate_desc(desc, opts)) return st;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return fail(TI_ERR_CUDA, "ti_engine_create: no CUDA device");
+    }
+    TI_CHECK(opts->device >= 0 && opts->device < ndev, TI_ERR_INVALID, "ti_engine_create: device %d of %d",
+             opts->device, ndev);
+    auto* e = new ti_engine();
+    e->d = *desc;
+    e->o = *opts;
+    if (e->o.tp_size <= 0) e->o.tp_size = 1;
+    e->dev = opts->device;
+    ti_status st = build(e);
+    if (st) {
+        std::string msg = ti_last_error();
+        free_all(e);
+        delete e;
+        return fail(st, "%s", msg.c_str());
+    }
+    *out = e;
+    return TI_OK;
+}
+
+ti_status ti_engine_destroy(ti_engine* e) {
+    if (!e) return TI_OK;
+    DeviceGuard g(e->dev);
+    cudaDeviceSynchronize();
+    free_all(e);
+    delete e;
+    return TI_OK;
+}
+
+ti_status ti_engine_memory(const ti_engine* e, size_t* w, size_t* kv, size_t* ad, size_t* work) {
+    TI_CHECK(e, TI_ERR_INVALID, "null engine");
+    if (w) *w = e->bytes_w;
+    if (kv) *kv = e->bytes_kv;
+    if (ad) *ad = e->bytes_ad;
+    if (work) *work = e->bytes_work;
+    return TI_OK;
+}
+
+ti_status ti_engine_load_tensor(ti_engine* e, const char* name, int dtype, const void* host, size_t bytes) {
+    clear_error();
+    TI_CHECK(e && name && host, TI_ERR_INVALID, "ti_engine_load_tensor: null argument");
+    auto it = e->slot_index.find(name);
+    TI_CHECK(it != e->slot_index.end(), TI_ERR_NOT_FOUND, "unknown tensor '%s'", name);
+    const Slot& s = e->slots[it->second];
+    TI_CHECK(dtype == TI_DTYPE_BF16, TI_ERR_UNSUPPORTED, "tensor '%s': dtype %d (bf16 expected)", name, dtype);
+    TI_CHECK(bytes == s.rows * s.cols * 2, TI_ERR_INVALID, "tensor '%s': %zu bytes, expected %zu", name, bytes,
+             s.rows * s.cols * 2);
+    DeviceGuard g(e->dev);
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(host) + (s.r0 * s.cols + s.c0) * 2;
+    TI_CUDA(cudaMemcpy2D(s.dst, s.ld * 2, src, s.cols * 2, s.nc * 2, s.nr, cudaMemcpyHostToDevice));
+    return TI_OK;
+}
+
+ti_status ti_engine_read_tensor(ti_engine* e, const char* name, void* host, size_t bytes) {
+    clear_error();
+    TI_CHECK(e && name && host, TI_ERR_INVALID, "ti_engine_read_tensor: null argument");
+    auto it = e->slot_index.find(name);
+    TI_CHECK(it != e->slot_index.end(), TI_ERR_NOT_FOUND, "unknown tensor '%s'", name);
+    const Slot& s = e->slots[it->second];
+    TI_CHECK(bytes == s.nr * s.nc * 2, TI_ERR_INVALID, "tensor '%s': %zu bytes, local window is %zu", name, bytes,
+             s.nr * s.nc * 2);
+    DeviceGuard g(e->dev);
+    TI_CUDA(cudaMemcpy2D(host, s.nc * 2, s.dst, s.ld * 2, s.nc * 2, s.nr, cudaMemcpyDeviceToHost));
+    return TI_OK;
+}
+
+ti_status ti_engine_init_synthetic(ti_engine* e, uint64_t seed, float std_) {
+    clear_error();
+    TI_CHECK(e, TI_ERR_INVALID, "null engine");
+    DeviceGuard g(e->dev);
+    const float c = synth_scale(std_);
+    for (const Slot& s : e->slots)
+        TI_CUDA(synth_bf16_launch(s.dst, s.nr, s.nc, s.ld, s.r0, s.c0, s.cols, seed, fnv1a(s.name.c_str()), c,
+                                  (cudaStream_t)0));
+    TI_CUDA(cudaDeviceSynchronize());
+    return TI_OK;
+}
+
+ti_status ti_seq_create(ti_engine* e, int* sid) {
+    clear_error();
+    TI_CHECK(e && sid, TI_ERR_INVALID, "null argument");
+    for (int i = 0; i < (int)e->seqs.size(); ++i)
+        if (!e->seqs[i].live) {
+            e->seqs[i] = SeqState{};
+            e->seqs[i].live = true;
+            *sid = i;
+            return TI_OK;
+        }
+    return fail(TI_ERR_OOM, "all %d sequence slots in use", (int)e->seqs.size());
+}
+
+static void release_pages(ti_engine* e, int sid) {
+    SeqState& s = e->seqs[sid];
+    for (int p : s.pages) e->free_pages.push_back(p);
+    if (!s.pages.empty()) {
+        DeviceGuard g(e->dev);
+        std::vector<int32_t> neg(s.pages.size(), -1);
+        cudaMemcpy(e->page_table + (size_t)sid * e->pt_stride, neg.data(), neg.size() * 4, cudaMemcpyHostToDevice);
+    }
+    s.pages.clear();
+    s.len = 0;
+}
+
+ti_status ti_seq_free(ti_engine* e, int sid) {
+    clear_error();
+    TI_CHECK(e, TI_ERR_INVALID, "null engine");
+    if (ti_status st = seq_check(e, sid)) return st;
+    release_pages(e, sid);
+    e->seqs[sid].live = false;
+    return TI_OK;
+}
+
+ti_status ti_seq_reset(ti_engine* e, int sid) {
+    clear_error();
+    TI_CHECK(e, TI_ERR_INVALID, "null engine");
+    if (ti_status st = seq_check(e, sid)) return st;
+    release_pages(e, sid);
+    return TI_OK;
+}
+
+ti_status ti_seq_len(ti_engine* e, int sid, int* len) {
+    TI_CHECK(e && len, TI_ERR_INVALID, "null argument");
+    if (ti_status st = seq_check(e, sid)) return st;
+    *len = e->seqs[sid].len;
+    return TI_OK;
+}
+
+ti_status ti_seq_reserve(ti_engine* e, int sid, int n_tokens) {
+    clear_error();
+    TI_CHECK(e, TI_ERR_INVALID, "null engine");
+    if (ti_status st = seq_check(e, sid)) return st;
+    std::vector<int32_t> upd;
+    if (ti_status st = ensure_pages(e, sid, n_tokens, &upd)) return st;
+    DeviceGuard g(e->dev);
+    for (size_t i = 0; i < upd.size(); i += 3)
+        TI_CUDA(cudaMemcpy(e->page_table + (size_t)upd[i] * e->pt_stride + upd[i + 1], &upd[i + 2], 4,
+                           cudaMemcpyHostToDevice));
+    return TI_OK;
+}
+
+ti_status ti_seq_read_kv(ti_engine* e, int sid, int layer, int which, void* host, int len) {
+    clear_error();
+    TI_CHECK(e && host, TI_ERR_INVALID, "null argument");
+    if (ti_status st = seq_check(e, sid)) return st;
+    TI_CHECK(layer >= 0 && layer < e->d.n_layers, TI_ERR_INVALID, "layer %d out of range", layer);
+    const SeqState& s = e->seqs[sid];
+    TI_CHECK(len >= 0 && len <= s.len, TI_ERR_INVALID, "len %d > sequence length %d", len, s.len);
+    DeviceGuard g(e->dev);
+    const uint16_t* pool = (which ? e->vpool : e->kpool) + (size_t)layer * e->kv_layer_elems;
+    uint16_t* out = reinterpret_cast<uint16_t*>(host);
+    const int hd = e->hd, nkv = e->nkv;
+    std::vector<uint16_t> page((size_t)nkv * kPageTokens * hd);
+    for (int p = 0; p * kPageTokens < len; ++p) {
+        TI_CUDA(cudaMemcpy(page.data(), pool + (size_t)s.pages[p] * nkv * kPageTokens * hd, page.size() * 2,
+                           cudaMemcpyDeviceToHost));
+        for (int t = 0; t < kPageTokens && p * kPageTokens + t < len; ++t)
+            for (int h = 0; h < nkv; ++h)
+                std::memcpy(out + ((size_t)(p * kPageTokens + t) * nkv + h) * hd,
+                            page.data() + ((size_t)h * kPageTokens + t) * hd, (size_t)hd * 2);
+    }
+    return TI_OK;
+}
+
+ti_status ti_engine_prefill(ti_engine* e, int sid, const int32_t* ids, int n, int adapter_id, int32_t* next_id,
+                            int logits_mode, void* logits_out) {
+    clear_error();
+    TI_CHECK(e && ids, TI_ERR_INVALID, "null argument");
+    TI_CHECK(n >= 1, TI_ERR_INVALID, "prefill: empty prompt");  // llama_model.cpp:212
+    DeviceGuard g(e->dev);
+    const int window = e->d.arch == TI_ARCH_MISTRAL ? e->d.sliding_window : -1;
+    int32_t ad = adapter_id;
+    for (int i = 0; i < n; ++i) {
+        const bool last = i == n - 1;
+        ti_status st = run_step(e, 1, &sid, ids + i, adapter_id >= 0 ? &ad : nullptr, window, last ? next_id : nullptr,
+                                last ? logits_mode : TI_LOGITS_NONE, last ? logits_out : nullptr, e->cap);
+        if (st) return st;
+    }
+    return TI_OK;
+}
+
+ti_status ti_engine_decode(ti_engine* e, int batch, const int32_t* seq_ids, const int32_t* tokens,
+                           const int32_t* adapter_ids, int32_t* next_ids, int logits_mode, void* logits_out,
+                           void* stream) {
+    clear_error();
+    TI_CHECK(e, TI_ERR_INVALID, "null engine");
+    DeviceGuard g(e->dev);
+    return run_step(e, batch, seq_ids, tokens, adapter_ids, -1, next_ids, logits_mode, logits_out,
+                    (cudaStream_t)stream);
+}
+
+ti_status ti_engine_bind(ti_engine* e, int B, const int32_t* seq_ids, const int32_t* first_tokens,
+                         const int32_t* adapter_ids) {
+    clear_error();
+    TI_CHECK(e && seq_ids && first_tokens, TI_ERR_INVALID, "null argument");
+    TI_CHECK(B >= 1 && B <= e->o.max_batch, TI_ERR_INVALID, "batch %d out of range", B);
+    TI_CHECK(e->bound_batch == 0, TI_ERR_STATE, "engine already bound");
+    DeviceGuard g(e->dev);
+    const int MB = e->o.max_batch;
+    int32_t* h = e->h_desc;
+    std::memset(h, 0, (size_t)e->desc_ints * 4);
+    h[1] = -1;
+    for (int b = 0; b < B; ++b) {
+        if (ti_status st = seq_check(e, seq_ids[b])) return st;
+        TI_CHECK(first_tokens[b] >= 0 && first_tokens[b] < e->V, TI_ERR_INVALID, "token out of range");
+        TI_CHECK(!adapter_ids || adapter_ids[b] < 0, TI_ERR_UNSUPPORTED, "LoRA adapters are not built yet");
+        const SeqState& s = e->seqs[seq_ids[b]];
+        TI_CHECK((int)s.pages.size() * kPageTokens > s.len, TI_ERR_STATE,
+                 "sequence %d has no reserved page for its next token (ti_seq_reserve)", seq_ids[b]);
+        h[4 + b] = first_tokens[b];
+        h[4 + MB + b] = seq_ids[b];
+        h[4 + 2 * MB + b] = s.len;
+        h[4 + 3 * MB + b] = adapter_ids ? adapter_ids[b] : -1;
+    }
+    GraphEntry* gr = nullptr;
+    if (ti_status st = get_graph(e, B, &gr)) return st;
+    TI_CUDA(cudaMemcpy(e->d_desc, h, (size_t)e->desc_ints * 4, cudaMemcpyHostToDevice));
+    e->bound_batch = B;
+    e->bound_seqs.assign(seq_ids, seq_ids + B);
+    return TI_OK;
+}
+
+ti_status ti_engine_decode_device(ti_engine* e, void* stream) {
+    TI_CHECK(e && e->bound_batch > 0, TI_ERR_STATE, "engine not bound");
+    GraphEntry* g = nullptr;
+    if (ti_status st = get_graph(e, e->bound_batch, &g)) return st;
+    TI_CUDA(cudaGraphLaunch(g->exec, (cudaStream_t)stream));
+    return TI_OK;
+}
+
+ti_status ti_engine_unbind(ti_engine* e, int steps, int32_t* last_ids, void* stream) {
+    clear_error();
+    TI_CHECK(e && e->bound_batch > 0, TI_ERR_STATE, "engine not bound");
+    DeviceGuard g(e->dev);
+    const int MB = e->o.max_batch;
+    TI_CUDA(cudaMemcpyAsync(e->h_out, e->out, (size_t)(MB + 1) * 4, cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+    TI_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+    const int B = e->bound_batch;
+    for (int b = 0; b < B; ++b) {
+        SeqState& s = e->seqs[e->bound_seqs[b]];
+        s.len = std::min(s.len + steps, e->o.max_seq_len);
+        if (last_ids) last_ids[b] = e->h_out[b];
+    }
+    e->bound_batch = 0;
+    e->bound_seqs.clear();
+    return read_err(e, e->h_out[MB]);
+}
+
+ti_status ti_engine_logits_device(ti_engine* e, void** ptr) {
+    TI_CHECK(e && ptr, TI_ERR_INVALID, "null argument");
+    *ptr = e->logits;
+    return TI_OK;
+}
+
+ti_status ti_engine_check(ti_engine* e) {
+    TI_CHECK(e, TI_ERR_INVALID, "null engine");
+    DeviceGuard g(e->dev);
+    int32_t w = 0;
+    TI_CUDA(cudaMemcpy(&w, e->err, 4, cudaMemcpyDeviceToHost));
+    return read_err(e, w);
+}
+
+ti_status ti_engine_launch_kernel(ti_engine* e, int kind, int layer, int batch, void* stream) {
+    TI_CHECK(e, TI_ERR_INVALID, "null engine");
+    TI_CHECK(batch >= 1 && batch <= e->o.max_batch, TI_ERR_INVALID, "batch %d out of range", batch);
+    DeviceGuard g(e->dev);
+    return enqueue_kernel(e, batch, kind, layer, (cudaStream_t)stream, nullptr);
+}
+
+ti_status ti_engine_launches_per_step(ti_engine* e, int batch, int* launches) {
+    TI_CHECK(e && launches, TI_ERR_INVALID, "null argument");
+    DeviceGuard g(e->dev);
+    GraphEntry* gr = nullptr;
+    if (ti_status st = get_graph(e, batch, &gr)) return st;
+    *launches = gr->launches;
+    return TI_OK;
+}
+
+}  // extern "C"

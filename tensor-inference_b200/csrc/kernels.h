@@ -1,0 +1,127 @@
+// kernels.h — host-side launch interface of the sm_100a kernels (internal).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace ti {
+
+// ----------------------------------------------------------------- launch helper
+// Launch with the programmatic-stream-serialization attribute (PDL) so the
+// kernel's weight prefetch overlaps the tail of the previous kernel.
+cudaError_t launch_pdl(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t s, void** args, bool pdl);
+
+int num_sms(int device);
+
+// ----------------------------------------------------------------- weight-streaming GEMV
+enum GemvEpi : int {
+    kEpiStore = 0,   // out = bf16(acc) [+ bias -> bf16]
+    kEpiResid = 1,   // out = bf16(resid + bf16(acc))
+    kEpiGlu = 2,     // units are (gate row n, up row n + N): out = bf16(bf16(act(bf16(g))) * bf16(u))
+    kEpiLmHead = 3,  // logits = bf16(acc); greedy argmax over fp32 acc (lowest index on ties)
+};
+
+struct GemvLora {
+    // per-token low-rank expansion added after the base projection (and bias):
+    // out = bf16(out + bf16(bf16(sum_r B[n, r] * t[b, r]) * scale[b]))
+    const uint16_t* const* B = nullptr;  // [nb] device pointers to B [N_total, rank] bf16 (nullptr = none)
+    const float* t = nullptr;            // [nb, t_stride] bf16-exact fp32 values of x A^T
+    int t_stride = 0;
+    int rank = 0;
+    const float* scale = nullptr;        // [nb]
+    // fused q|k|v rows: rows [0,sec1) use t[0:rank), [sec1,sec2) t[rank:2rank), the rest t[2rank:3rank)
+    int sec1 = 1 << 30, sec2 = 1 << 30;
+};
+
+struct GemvArgs {
+    const uint16_t* W = nullptr;  // bf16 [rows, K]; kEpiGlu: gate rows [0,N) then up rows [N,2N)
+    int N = 0;                    // output units
+    int K = 0;
+    int nb = 1;                   // tokens
+    const uint16_t* x = nullptr;  // bf16 [nb, x_stride]
+    int x_stride = 0;
+    const uint16_t* norm_w = nullptr;  // RMSNorm prologue over x when set
+    float eps = 1e-5f;
+    int norm_offset = 0;
+    uint16_t* out = nullptr;  // bf16 [nb, out_stride]
+    int out_stride = 0;
+    const uint16_t* bias = nullptr;   // [N]
+    const uint16_t* resid = nullptr;  // [nb, resid_stride]
+    int resid_stride = 0;
+    int act = 0;  // kEpiGlu: 0 = SiLU, 1 = tanh-GELU
+    // LM head
+    unsigned long long* amax = nullptr;  // [nb] argmax keys (zero before the step)
+    unsigned int* done = nullptr;        // CTA completion counter (zero before the step)
+    int32_t* out_ids = nullptr;          // [nb] greedy ids
+    int32_t* chain_tokens = nullptr;     // [nb] next-step input tokens (optional)
+    int32_t* chain_pos = nullptr;        // [nb] positions incremented after the step (optional)
+    float* logits_f32 = nullptr;         // [nb, out_stride] optional fp32 logits
+    GemvLora lora;
+    int* err = nullptr;
+};
+
+struct GemvPlan {
+    int rows_per_stage = 1;
+    int stages = 3;
+    int grid = 0;
+    size_t smem = 0;
+    const void* func = nullptr;
+};
+
+// Chooses stage geometry, grid and kernel instance; false if unsupported.
+bool gemv_plan(const GemvArgs& a, int epi, int device, GemvPlan* plan, std::string* why);
+cudaError_t gemv_launch(const GemvArgs& a, int epi, const GemvPlan& plan, cudaStream_t s, bool pdl);
+
+// ----------------------------------------------------------------- paged decode attention
+struct AttnArgs {
+    const uint16_t* qkv = nullptr;  // [nb, qkv_stride] (q heads, k heads, v heads), pre-RoPE
+    int qkv_stride = 0;
+    int nb = 1;
+    int nq = 0, nkv = 0, hd = 0;    // local heads
+    const int32_t* pos = nullptr;   // [nb] position of the new token (= tokens already cached)
+    const int32_t* seq = nullptr;   // [nb] sequence slot -> page-table row
+    const int32_t* page_table = nullptr;  // [max_seqs, pt_stride]
+    int pt_stride = 0;
+    uint16_t* kc = nullptr;  // this layer's K pages: [n_pages, nkv, 16, hd]
+    uint16_t* vc = nullptr;
+    const float* freqs = nullptr;  // [hd/2]
+    float scale = 1.f;
+    const int32_t* window = nullptr;  // device scalar: attend to j > pos - window when > 0 (nullptr = none)
+    int n_pages = 0;                  // pool size, bounds-checks page ids
+    int n_splits = 1;
+    int max_chunk = 0;   // tokens per split the smem is sized for
+    float* part_o = nullptr;   // [nb, nkv, n_splits, group, hd]
+    float* part_ml = nullptr;  // [nb, nkv, n_splits, group, 2]
+    unsigned int* counters = nullptr;  // [nb, nkv] (zero; reset by the last CTA)
+    uint16_t* out = nullptr;  // [nb, out_stride]
+    int out_stride = 0;
+    int* err = nullptr;
+};
+int attn_splits(int nb, int nkv, int max_len, int sms, int* max_chunk);
+cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s, bool pdl);
+
+// ----------------------------------------------------------------- small kernels
+struct EmbedArgs {
+    const uint16_t* table = nullptr;  // [vocab, hidden]
+    int vocab = 0, hidden = 0, nb = 1;
+    const int32_t* tokens = nullptr;  // [nb]
+    uint16_t* out = nullptr;          // [nb, hidden]
+    float scale = 0.f;                // Gemma: embeddings times sqrt(hidden) (0 = none)
+    // page-table updates applied before the step: (seq, index, page) triples
+    const int32_t* pt_updates = nullptr;  // device [3 * max]
+    const int32_t* n_updates = nullptr;   // device scalar
+    int32_t* page_table = nullptr;
+    int pt_stride = 0;
+    int* err = nullptr;
+};
+cudaError_t embed_launch(const EmbedArgs& a, cudaStream_t s, bool pdl);
+
+// synthetic init of a [rows, cols] window (row stride dst_ld) of a full tensor
+// with row length full_ld: dst[r][c] = gen(index (r0 + r) * full_ld + c0 + c)
+cudaError_t synth_bf16_launch(uint16_t* dst, size_t rows, size_t cols, size_t dst_ld, size_t r0, size_t c0,
+                              size_t full_ld, uint64_t seed, uint64_t name_hash, float scale_c, cudaStream_t s);
+cudaError_t synth_f32_launch(float* dst, size_t n, uint64_t seed, uint64_t name_hash, float scale_c,
+                             cudaStream_t s);
+
+}  // namespace ti

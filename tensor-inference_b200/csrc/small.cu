@@ -1,0 +1,97 @@
+// small.cu — launch helper, embedding gather, synthetic initialisers.
+#include "common.cuh"
+#include "kernels.h"
+#include "synth.cuh"
+
+namespace ti {
+
+cudaError_t launch_pdl(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t s, void** args, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelExC(&cfg, func, args);
+}
+
+int num_sms(int device) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+    return n > 0 ? n : 1;
+}
+
+// ops.cu:46-88 (row gather) + gemma_model.cpp:117 (times sqrt(hidden), bf16);
+// first kernel of a step: also applies the step's page-table updates.
+__global__ void k_embed(const EmbedArgs a) {
+    pdl_wait();
+    if (blockIdx.x == 0 && a.n_updates) {
+        const int nu = *a.n_updates;
+        for (int i = threadIdx.x; i < nu; i += blockDim.x) {
+            const int seq = a.pt_updates[3 * i], idx = a.pt_updates[3 * i + 1], page = a.pt_updates[3 * i + 2];
+            a.page_table[(size_t)seq * a.pt_stride + idx] = page;
+        }
+    }
+    const int b = blockIdx.x;
+    int tok = a.tokens[b];
+    if (tok < 0 || tok >= a.vocab) {
+        if (threadIdx.x == 0 && a.err) atomicOr(a.err, kErrBadIndex);
+        tok = 0;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(a.table + (size_t)tok * a.hidden);
+    uint4* dst = reinterpret_cast<uint4*>(a.out + (size_t)b * a.hidden);
+    for (int i = threadIdx.x; i < a.hidden / 8; i += blockDim.x) {
+        uint4 v = src[i];
+        if (a.scale != 0.f) {
+            uint32_t* p = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) p[e] = pack_bf2(bf_lo(p[e]) * a.scale, bf_hi(p[e]) * a.scale);
+        }
+        dst[i] = v;
+    }
+    if (threadIdx.x == 0) pdl_trigger();
+}
+
+cudaError_t embed_launch(const EmbedArgs& a, cudaStream_t s, bool pdl) {
+    if (a.hidden % 8) return cudaErrorInvalidValue;
+    EmbedArgs args = a;
+    void* params[] = {&args};
+    return launch_pdl(reinterpret_cast<const void*>(&k_embed), dim3(a.nb), dim3(256), 0, s, params, pdl);
+}
+
+__global__ void k_synth_bf16(uint16_t* dst, size_t rows, size_t cols, size_t dst_ld, size_t r0, size_t c0,
+                             size_t full_ld, uint64_t key, float c) {
+    const size_t total = rows * cols;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = i / cols, col = i - r * cols;
+        const size_t gi = (r0 + r) * full_ld + c0 + col;
+        const float v = __fmul_rn((float)synth_centered(key, gi), c);
+        dst[r * dst_ld + col] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+    }
+}
+
+__global__ void k_synth_f32(float* dst, size_t n, uint64_t key, float c) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        dst[i] = __fmul_rn((float)synth_centered(key, i), c);
+}
+
+cudaError_t synth_bf16_launch(uint16_t* dst, size_t rows, size_t cols, size_t dst_ld, size_t r0, size_t c0,
+                              size_t full_ld, uint64_t seed, uint64_t name_hash, float scale_c, cudaStream_t s) {
+    if (rows == 0 || cols == 0) return cudaSuccess;
+    const uint64_t key = mix64(seed ^ name_hash);
+    k_synth_bf16<<<4 * 148, 256, 0, s>>>(dst, rows, cols, dst_ld, r0, c0, full_ld, key, scale_c);
+    return cudaGetLastError();
+}
+
+cudaError_t synth_f32_launch(float* dst, size_t n, uint64_t seed, uint64_t name_hash, float scale_c, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    const uint64_t key = mix64(seed ^ name_hash);
+    k_synth_f32<<<4 * 148, 256, 0, s>>>(dst, n, key, scale_c);
+    return cudaGetLastError();
+}
+
+}  // namespace ti
