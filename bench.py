@@ -162,11 +162,9 @@ def prefill_lockstep(eng, sids, prompts):
 def measure_batch(ti, torch, eng, B, steps, warmup, stream, peak, measure_e2e=True):
     import numpy as np
 
-    import oracle  # only for the seeded prompt ids (same generator as the tests)
-
     desc = eng.desc
     sids = [eng.seq_create() for _ in range(B)]
-    prompts = np.stack([oracle.fill_ids(f"prompt{b}", PROMPT, b, desc.vocab) for b in range(B)])
+    prompts = np.random.default_rng(0).integers(0, desc.vocab, size=(B, PROMPT), dtype=np.int32)
     t0 = time.perf_counter()
     first = prefill_lockstep(eng, sids, prompts)
     t_prefill = time.perf_counter() - t0
@@ -238,6 +236,46 @@ def kernel_roofline(ti, torch, eng, stream, peak, iters=64):
     return {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
             "traffic": None, "kernel": "k_gemv<1,kEpiGlu> (gate|up + RMSNorm + SiLU*up, 8B layer)",
             "bytes_per_launch": nbytes, "us_per_launch": round(ms * 1e3, 2)}
+
+
+def run_profile(args):
+    """Short, self-contained workload for ncu: a few decode steps (or repeated
+    launches of one kernel) of the 8B shape with `--layers` layers after a
+    `--prompt`-token prefill.  Prints timing only; never a bench number."""
+    import numpy as np
+    import torch
+
+    import ti_b200 as ti
+
+    torch.cuda.set_device(0)
+    ts = torch.cuda.Stream()
+    torch.cuda.set_stream(ts)
+    desc = ti.model_desc(**dict(ti.PRESETS["llama3_8b"], n_layers=args.layers))
+    eng = ti.Engine(desc, device=0, max_batch=args.batch, max_seqs=args.batch,
+                    max_seq_len=args.prompt + args.warmup + args.steps + 64)
+    eng.init_synthetic(0, 0.02)
+    sids = [eng.seq_create() for _ in range(args.batch)]
+    prompts = np.random.default_rng(0).integers(0, desc.vocab, size=(args.batch, args.prompt), dtype=np.int32)
+    first = prefill_lockstep(eng, sids, prompts)
+    for s in sids:
+        eng.seq_reserve(s, args.prompt + args.warmup + args.steps + 8)
+    eng.bind(sids, first)
+    for _ in range(args.warmup):
+        eng.decode_device(ts.cuda_stream)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    if args.kernel is None:
+        for _ in range(args.steps):
+            eng.decode_device(ts.cuda_stream)
+    else:
+        for i in range(args.steps):
+            eng.launch_kernel(args.kernel, i % args.layers, args.batch, ts.cuda_stream)
+    torch.cuda.synchronize()
+    dt = (time.perf_counter() - t0) / args.steps
+    eng.unbind(args.warmup + (args.steps if args.kernel is None else 0), ts.cuda_stream)
+    eng.check()
+    print(f"profile: layers={args.layers} batch={args.batch} kernel={args.kernel} {dt * 1e3:.3f} ms/iter")
+    eng.close()
 
 
 def run_ours(args, rank, world):
@@ -328,11 +366,18 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-b32", dest="b32", action="store_false")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true", help="short ncu workload (see run_profile)")
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--prompt", type=int, default=32)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--kernel", type=int, default=None, help="profile: launch only this kernel kind")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if args.impl == "reference":
+    if args.profile:
+        run_profile(args)
+    elif args.impl == "reference":
         run_reference(args, rank, world)
     else:
         run_ours(args, rank, world)

@@ -103,6 +103,13 @@ TI_DEVICE_INLINE void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint6
         "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
         : "memory");
 }
+TI_DEVICE_INLINE void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
 TI_DEVICE_INLINE void prefetch_l2_bulk(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
@@ -138,6 +145,25 @@ TI_DEVICE_INLINE float dot8_bf16(const uint4 w, const uint4 x, float acc) {
     acc = fmaf(bf_hi(w.z), bf_hi(x.z), acc);
     acc = fmaf(bf_lo(w.w), bf_lo(x.w), acc);
     acc = fmaf(bf_hi(w.w), bf_hi(x.w), acc);
+    return acc;
+}
+
+// packed fp32 FMA (sm_100 FFMA2): two independent round-to-nearest FMAs
+TI_DEVICE_INLINE float2 ffma2(float2 a, float2 b, float2 c) {
+    unsigned long long av = *reinterpret_cast<unsigned long long*>(&a);
+    unsigned long long bv = *reinterpret_cast<unsigned long long*>(&b);
+    unsigned long long cv = *reinterpret_cast<unsigned long long*>(&c);
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(cv) : "l"(av), "l"(bv));
+    return *reinterpret_cast<float2*>(&cv);
+}
+TI_DEVICE_INLINE float2 bf2_to_f2(uint32_t u) { return make_float2(bf_lo(u), bf_hi(u)); }
+// 8 bf16 weights x 8 fp32 activations (pairs); even and odd elements accumulate
+// in the two lanes of `acc`, each in element order
+TI_DEVICE_INLINE float2 dot8_bf16_f2(const uint4 w, const float2* x, float2 acc) {
+    acc = ffma2(bf2_to_f2(w.x), x[0], acc);
+    acc = ffma2(bf2_to_f2(w.y), x[1], acc);
+    acc = ffma2(bf2_to_f2(w.z), x[2], acc);
+    acc = ffma2(bf2_to_f2(w.w), x[3], acc);
     return acc;
 }
 

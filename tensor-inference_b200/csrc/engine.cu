@@ -172,8 +172,8 @@ ti_status validate_desc(const ti_model_desc* d, const ti_engine_opts* o) {
     TI_CHECK(d->n_heads / d->n_kv_heads <= 16, TI_ERR_UNSUPPORTED, "engine: GQA group > 16");
     TI_CHECK(d->head_dim == 64 || d->head_dim == 128 || d->head_dim == 256, TI_ERR_UNSUPPORTED,
              "engine: head_dim %d (64/128/256 supported)", d->head_dim);
-    TI_CHECK(d->hidden % 64 == 0 && d->intermediate % 64 == 0 && (d->n_heads * d->head_dim) % 64 == 0,
-             TI_ERR_UNSUPPORTED, "engine: hidden, intermediate and n_heads*head_dim must be multiples of 64");
+    TI_CHECK(d->hidden % 128 == 0 && d->intermediate % 128 == 0 && (d->n_heads * d->head_dim) % 128 == 0,
+             TI_ERR_UNSUPPORTED, "engine: hidden, intermediate and n_heads*head_dim must be multiples of 128");
     TI_CHECK(d->weight_format == TI_WFMT_BF16, TI_ERR_UNSUPPORTED, "engine: weight format %d not built yet",
              d->weight_format);
     TI_CHECK(o->max_batch >= 1 && o->max_batch <= 256, TI_ERR_INVALID, "engine: max_batch out of range");

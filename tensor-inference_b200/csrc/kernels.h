@@ -64,6 +64,7 @@ struct GemvArgs {
 struct GemvPlan {
     int rows_per_stage = 1;
     int stages = 3;
+    int prefetch = 0;  // L2 prefetch window, in stages beyond the smem ring
     int grid = 0;
     size_t smem = 0;
     const void* func = nullptr;

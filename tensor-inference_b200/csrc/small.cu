@@ -28,6 +28,7 @@ int num_sms(int device) {
 // ops.cu:46-88 (row gather) + gemma_model.cpp:117 (times sqrt(hidden), bf16);
 // first kernel of a step: also applies the step's page-table updates.
 __global__ void k_embed(const EmbedArgs a) {
+    if (threadIdx.x == 0) pdl_trigger();
     pdl_wait();
     if (blockIdx.x == 0 && a.n_updates) {
         const int nu = *a.n_updates;
@@ -53,7 +54,6 @@ __global__ void k_embed(const EmbedArgs a) {
         }
         dst[i] = v;
     }
-    if (threadIdx.x == 0) pdl_trigger();
 }
 
 cudaError_t embed_launch(const EmbedArgs& a, cudaStream_t s, bool pdl) {

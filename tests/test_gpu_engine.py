@@ -130,7 +130,7 @@ def test_8b_layer_shapes_two_layers():
 
 
 def test_device_chain_matches_host_steps():
-    eng, _ = _pair(SMALL, seed=4, max_batch=2)
+    eng, _ = _pair(SMALL, seed=4, max_batch=2, max_seqs=4)
     V = SMALL["vocab"]
     a, b = eng.seq_create(), eng.seq_create()
     p0 = oracle.fill_ids("pa", 5, 1, V)
