@@ -23,6 +23,7 @@
 #include "kernels.h"
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace ti {
 
@@ -342,10 +343,13 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnArgs a) 
 }
 
 int attn_splits(int nb, int nkv, int max_len, int sms, int* max_chunk) {
+    // tokens per CTA are capped by the shared-memory K/V tile (env TI_ATTN_CHUNK, <= 64)
+    const char* env = std::getenv("TI_ATTN_CHUNK");
+    const int cap = env && std::atoi(env) >= 16 ? std::min(std::atoi(env), kAttnChunkCap) : kAttnChunkCap;
     const int work = std::max(1, nb * nkv);
     const int target = std::max(1, (sms + work - 1) / work);                // about one CTA per SM
     const int by_len = std::max(1, (max_len + 31) / 32);                    // at least ~32 tokens per CTA
-    const int min_splits = (max_len + kAttnChunkCap - 1) / kAttnChunkCap;  // smem tile bound
+    const int min_splits = (max_len + cap - 1) / cap;                      // smem tile bound
     const int n = std::max(std::min(target, by_len), min_splits);
     *max_chunk = (max_len + n - 1) / n;
     return n;

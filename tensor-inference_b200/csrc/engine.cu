@@ -19,6 +19,7 @@
 //              layers (one page id per 16 positions of a sequence).
 //   page table [max_seqs][ceil(max_seq_len/16)] int32, -1 = unallocated.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -353,6 +354,17 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         if (launches) ++*launches;
         return TI_OK;
     }
+    // L2 warm-up target: the next GEMV of the step (qkv -> o -> gate|up -> down ->
+    // next layer's qkv or the LM head; the LM head warms layer 0 for the next step)
+    const char* next_env = std::getenv("TI_GEMV_NEXT_KB");
+    const int next_kb = next_env ? std::atoi(next_env) : 640;
+    auto set_next = [&](GemvArgs& a, const uint16_t* w, int N, int K, int U) {
+        a.next_w = w;
+        a.next_N = N;
+        a.next_K = K;
+        a.next_U = U;
+        a.next_bytes = next_kb * 1024;
+    };
     if (kind == kKLmHead) {
         GemvArgs lm;
         lm.W = e->lm_head;
@@ -371,6 +383,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         lm.chain_tokens = e->dd_tokens();
         lm.chain_pos = e->dd_pos();
         lm.err = e->err;
+        set_next(lm, e->layers[0].wqkv, e->qkv_rows, H, 1);
         return gemv_all(lm, kEpiLmHead, H, e->Vl, 0);
     }
     TI_CHECK(li >= 0 && li < d.n_layers, TI_ERR_INVALID, "layer %d out of range", li);
@@ -390,6 +403,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             q.out_stride = e->qkv_rows;
             q.bias = l.bqkv;
             q.err = e->err;
+            set_next(q, l.wo, H, QW, 1);
             return gemv_all(q, kEpiStore, H, e->qkv_rows, 0);
         }
         case kKAttn: {
@@ -436,6 +450,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             ov.resid = e->hidden;
             ov.resid_stride = H;
             ov.err = e->err;
+            set_next(ov, l.wgu, I, H, 2);
             return gemv_all(ov, kEpiResid, QW, H, H);
         }
         case kKGateUp: {
@@ -452,6 +467,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             gu.out_stride = I;
             gu.act = gemma ? 1 : 0;
             gu.err = e->err;
+            set_next(gu, l.wdown, H, I, 1);
             return gemv_all(gu, kEpiGlu, H, I, 0);
         }
         case kKDown: {
@@ -466,6 +482,8 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             dn.resid = e->res1;
             dn.resid_stride = H;
             dn.err = e->err;
+            if (li + 1 < d.n_layers) set_next(dn, e->layers[li + 1].wqkv, e->qkv_rows, H, 1);
+            else set_next(dn, e->lm_head, e->Vl, H, 1);
             return gemv_all(dn, kEpiResid, I, H, H);
         }
         default: return fail(TI_ERR_INVALID, "unknown kernel kind %d", kind);

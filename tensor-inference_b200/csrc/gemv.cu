@@ -189,6 +189,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                              &full[s], pol);
                 if (g + stages + pf < n_groups) prefetch(g + stages + pf);
             }
+            if (a.next_w && a.next_bytes > 0) {
+                const int G2 = min(G, a.next_N);
+                if (cta < G2) {
+                    const int r0 = (int)((long long)cta * a.next_N / G2);
+                    const int r1 = (int)((long long)(cta + 1) * a.next_N / G2);
+                    const size_t rb = (size_t)a.next_K * 2;
+                    const int rows = min(r1 - r0, max(1, (int)(a.next_bytes / (rb * a.next_U))));
+                    const uint8_t* NW = reinterpret_cast<const uint8_t*>(a.next_w);
+                    prefetch_l2_bulk(NW + (size_t)r0 * rb, (uint32_t)(rows * rb));
+                    if (a.next_U == 2) prefetch_l2_bulk(NW + ((size_t)a.next_N + r0) * rb, (uint32_t)(rows * rb));
+                }
+            }
         }
         return;
     }
@@ -369,9 +381,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     // the (normalised, bf16-exact) activation slice unpacked to fp32 pairs once
-    float2 xf[XRR][4];
+    constexpr bool XF = !XS && XR <= 4;  // fp32 pairs for small slices, packed bf16 otherwise
+    float2 xf[XF ? XRR : 1][4];
 #pragma unroll
-    for (int j = 0; j < XRR; ++j) {
+    for (int j = 0; j < (XF ? XRR : 0); ++j) {
         xf[j][0] = bf2_to_f2(xr[j].x);
         xf[j][1] = bf2_to_f2(xr[j].y);
         xf[j][2] = bf2_to_f2(xr[j].z);
@@ -411,7 +424,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                             for (int u = 0; u < U; ++u) {
                                 const uint4 w =
                                     lds128(stage + (((size_t)u * rows_per_stage + r) * K + col0 + sc * 8) * 2);
-                                acc2[r][u] = dot8_bf16_f2(w, xf[j], acc2[r][u]);
+                                if constexpr (XF) {
+                                    acc2[r][u] = dot8_bf16_f2(w, xf[j], acc2[r][u]);
+                                } else {
+                                    acc2[r][u].x = dot8_bf16(w, xr[j], acc2[r][u].x);
+                                }
                             }
                 }
             }
@@ -476,8 +493,8 @@ static const void* pick(int nb, int xr) {
         switch (xr) {
             case 1: return fn<1, EPI, 1, kRowsMax / U>();
             case 2: return fn<1, EPI, 2, kRowsMax / U>();
-            case 4: return fn<1, EPI, 4, kRowsMax / U>();
-            case 8: return fn<1, EPI, 8, kRowsMax / U>();
+            case 4: return fn<1, EPI, 4, (4 / U > 0 ? 4 / U : 1)>();
+            case 8: return fn<1, EPI, 8, (2 / U > 0 ? 2 / U : 1)>();
             default: return fn<1, EPI, 0, kRowsMax / U>();
         }
     }
@@ -488,8 +505,12 @@ static const void* pick(int nb, int xr) {
 }
 
 static int nb_tmpl(int nb) { return nb == 1 ? 1 : nb == 2 ? 2 : nb <= 4 ? 4 : 8; }
-static int rg_tmpl(int nbt, int U) {
-    if (nbt == 1) return kRowsMax / U;
+static int rg_tmpl(int nbt, int U, int xr) {
+    if (nbt == 1) {
+        if (xr == 4) return std::max(1, 4 / U);
+        if (xr == 8) return std::max(1, 2 / U);
+        return kRowsMax / U;
+    }
     if (nbt == 2) return std::max(1, 4 / U);
     if (nbt == 4) return std::max(1, 2 / U);
     return 1;
@@ -514,8 +535,6 @@ bool gemv_plan(const GemvArgs& a, int epi, int device, GemvPlan* plan, std::stri
     const int U = epi == kEpiGlu ? 2 : 1;
     const int nbt = nb_tmpl(a.nb);
     const size_t row_bytes = (size_t)a.K * 2 * U;
-    int rps = (int)std::max<size_t>(1, (size_t)tune_kb("TI_GEMV_STAGE_KB", 96) * 1024 / row_bytes);
-    rps = std::min(rps, rg_tmpl(nbt, U));
     // register slice: sub-chunks per lane = ceil(K / 128 / 32)
     const int need = (a.K / (8 * kConsumerWarps) + 31) / 32;
     int xr = 0;
@@ -526,6 +545,8 @@ bool gemv_plan(const GemvArgs& a, int epi, int device, GemvPlan* plan, std::stri
                 break;
             }
     }
+    int rps = (int)std::max<size_t>(1, (size_t)tune_kb("TI_GEMV_STAGE_KB", 96) * 1024 / row_bytes);
+    rps = std::min(rps, rg_tmpl(nbt, U, xr));
     const bool xs = xr == 0;
     const size_t stage_bytes = ((size_t)rps * row_bytes + 127) & ~size_t(127);
     int stages = (int)std::min<size_t>(8, std::max<size_t>(2, (size_t)tune_kb("TI_GEMV_RING_KB", 200) * 1024 / stage_bytes));

@@ -58,6 +58,11 @@ struct GemvArgs {
     int32_t* chain_pos = nullptr;        // [nb] positions incremented after the step (optional)
     float* logits_f32 = nullptr;         // [nb, out_stride] optional fp32 logits
     GemvLora lora;
+    // L2 warm-up of the next GEMV of the step: once this CTA's producer has
+    // issued its own copies it prefetches the first `next_bytes` of the rows the
+    // next kernel's CTA with the same index will stream first
+    const uint16_t* next_w = nullptr;
+    int next_N = 0, next_K = 0, next_U = 1, next_bytes = 0;
     int* err = nullptr;
 };
 
