@@ -95,6 +95,21 @@ ti_status ti_op_softmax(int dtype, const void* x, float* out, int rows, int cols
  * q [seq, n_heads, hd], k/v [kv_len, n_kv, hd]; mask only when causal && seq > 1. */
 ti_status ti_op_attention(const void* q, const void* k, const void* v, void* out, int seq, int n_heads,
                           int kv_len, int n_kv, int head_dim, int causal, int sliding_window, void* stream);
+/* Decode attention over a paged KV cache, one new token per sequence: the
+ * work of ops::rope x2 + the cache cudaMemcpy + ops::slice x2 + ops::attention
+ * for one layer (llama_model.cpp:147-182, ops.cu:210-312,444-544).
+ * qkv [batch, (n_heads + 2*n_kv)*head_dim] bf16 holds each token's q|k|v before
+ * RoPE; pos[b] = tokens already cached for sequence seq[b]; the rotated k and v
+ * are appended at position pos[b] of the sequence's pages; the token attends
+ * to positions [max(0, pos - sliding_window + 1) or 0, pos].
+ * page_table [*, pt_stride] int32 page ids (16 tokens per page);
+ * k_pages / v_pages [n_pages, n_kv, 16, head_dim] bf16; out [batch, n_heads*head_dim].
+ * max_len bounds pos + 1 (it sizes the split-KV work).  Split partials live in
+ * scratch taken from the device's stream-ordered memory pool. */
+ti_status ti_op_paged_attention(const void* qkv, int batch, int n_heads, int n_kv, int head_dim,
+                                const int32_t* pos, const int32_t* seq, const int32_t* page_table, int pt_stride,
+                                void* k_pages, void* v_pages, int n_pages, int max_len, float theta,
+                                const ti_rope_scaling* scaling, int sliding_window, void* out, void* stream);
 /* ops.hpp:98 / ops.cu:586-616 (BF16<->F32; same dtype = copy). */
 ti_status ti_op_cast(int src_dtype, int dst_dtype, const void* x, void* out, size_t n, void* stream);
 /* ops.hpp:95 / ops.cu:559-584: 2-D transpose [rows, cols] -> [cols, rows], F32 or BF16. */

@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnArgs a) 
     const int pos = a.pos[b];
     const int* pt = a.page_table + (size_t)a.seq[b] * a.pt_stride;
     const int L1 = pos + 1;
-    const int window = a.window ? *a.window : -1;
+    const int window = a.window ? *a.window : a.window_const;
     const int lo = window > 0 ? max(0, pos - window + 1) : 0;
     const int span = L1 - lo;
     const int chunk = (span + a.n_splits - 1) / a.n_splits;
@@ -353,6 +353,11 @@ int attn_splits(int nb, int nkv, int max_len, int sms, int* max_chunk) {
     const int n = std::max(std::min(target, by_len), min_splits);
     *max_chunk = (max_len + n - 1) / n;
     return n;
+}
+
+size_t attn_scratch_floats(int nb, int nq, int nkv, int hd, int n_splits) {
+    const size_t G = (size_t)(nq / nkv);
+    return (size_t)nb * nkv * n_splits * G * (hd + 2);
 }
 
 cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s, bool pdl) {

@@ -93,7 +93,8 @@ struct AttnArgs {
     uint16_t* vc = nullptr;
     const float* freqs = nullptr;  // [hd/2]
     float scale = 1.f;
-    const int32_t* window = nullptr;  // device scalar: attend to j > pos - window when > 0 (nullptr = none)
+    const int32_t* window = nullptr;  // device scalar: attend to j > pos - window when > 0
+    int window_const = -1;            // used when `window` is null
     int n_pages = 0;                  // pool size, bounds-checks page ids
     int n_splits = 1;
     int max_chunk = 0;   // tokens per split the smem is sized for
@@ -105,6 +106,8 @@ struct AttnArgs {
     int* err = nullptr;
 };
 int attn_splits(int nb, int nkv, int max_len, int sms, int* max_chunk);
+// scratch floats / counters one launch needs: part_o + part_ml, and nb*nkv counters
+size_t attn_scratch_floats(int nb, int nq, int nkv, int hd, int n_splits);
 cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s, bool pdl);
 
 // ----------------------------------------------------------------- small kernels
@@ -129,5 +132,8 @@ cudaError_t synth_bf16_launch(uint16_t* dst, size_t rows, size_t cols, size_t ds
                               size_t full_ld, uint64_t seed, uint64_t name_hash, float scale_c, cudaStream_t s);
 cudaError_t synth_f32_launch(float* dst, size_t n, uint64_t seed, uint64_t name_hash, float scale_c,
                              cudaStream_t s);
+
+// rope frequency table on the device, cached per (device, head_dim, theta, scaling)
+const float* rope_table(int dev, int hd, float theta, const void* scaling /* const ti_rope_scaling* */);
 
 }  // namespace ti

@@ -277,7 +277,8 @@ __global__ void k_transpose(const T* __restrict__ x, T* __restrict__ out, int ro
 }
 
 // rope tables cached per (device, head_dim, theta, scaling)
-static const float* rope_table(int dev, int hd, float theta, const ti_rope_scaling* sc) {
+const float* rope_table(int dev, int hd, float theta, const void* scv) {
+    const ti_rope_scaling* sc = reinterpret_cast<const ti_rope_scaling*>(scv);
     static std::mutex mu;
     static std::map<std::tuple<int, int, float, int, float, float, float, int>, float*> cache;
     ti_rope_scaling z = {0, 1.f, 1.f, 1.f, 8192};

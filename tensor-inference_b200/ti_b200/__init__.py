@@ -77,6 +77,9 @@ _SIGS = {
     "ti_op_attention": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                   C.c_int, C.c_int, C.c_int, C.c_void_p]),
     "ti_op_cast": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "ti_op_paged_attention": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                        C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_float,
+                                        C.POINTER(RopeScaling), C.c_int, C.c_void_p, C.c_void_p]),
     "ti_op_transpose2d": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "ti_engine_create": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(EngineOpts), C.POINTER(C.c_void_p)]),
     "ti_engine_destroy": (C.c_int, [C.c_void_p]),

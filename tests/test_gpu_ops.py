@@ -145,3 +145,66 @@ def test_cast_and_transpose():
     np.testing.assert_array_equal(db.to_array(x.shape, np.uint16), oracle.f32_to_bf16(x))
     ti.check(lib().ti_op_transpose2d(ti.DTYPE_F32, dx.ptr, dt.ptr, 33, 65, None))
     np.testing.assert_array_equal(dt.to_array((65, 33), np.float32), x.T)
+
+
+def paged_case(seed=12, B=3, nq=8, nkv=2, hd=128, pos=(0, 17, 40), max_len=64, theta=10000.0):
+    """random paged K/V state (shuffled page ids) plus the oracle's expected output
+    for one decode-attention call"""
+    rng = np.random.default_rng(seed)
+    pt_stride = (max_len + 15) // 16
+    n_pages = B * pt_stride + 3
+    table = rng.permutation(n_pages)[: B * pt_stride].reshape(B, pt_stride).astype(np.int32)
+    kpool = np.zeros((n_pages, nkv, 16, hd), np.uint16)
+    vpool = np.zeros_like(kpool)
+    cached = []
+    for b in range(B):
+        kc = oracle.f32_to_bf16(rng.standard_normal((pos[b], nkv, hd)).astype(np.float32))
+        vc = oracle.f32_to_bf16(rng.standard_normal((pos[b], nkv, hd)).astype(np.float32))
+        for j in range(pos[b]):
+            kpool[table[b, j // 16], :, j % 16] = kc[j]
+            vpool[table[b, j // 16], :, j % 16] = vc[j]
+        cached.append((kc, vc))
+    qkv = oracle.f32_to_bf16(rng.standard_normal((B, (nq + 2 * nkv) * hd)).astype(np.float32))
+    fr = np.empty(hd // 2, np.float32)
+    oracle.lib().orc_rope_freqs(hd, theta, None, oracle.ptr(fr))
+    ref, knew = [], []
+    for b in range(B):
+        q = np.ascontiguousarray(qkv[b, : nq * hd].reshape(1, nq, hd))
+        k = np.ascontiguousarray(qkv[b, nq * hd:(nq + nkv) * hd].reshape(1, nkv, hd))
+        v = np.ascontiguousarray(qkv[b, (nq + nkv) * hd:].reshape(1, nkv, hd))
+        qr, kr = np.empty_like(q), np.empty_like(k)
+        oracle.lib().orc_rope(oracle.ptr(q), oracle.ptr(qr), 1, nq, hd, pos[b], oracle.ptr(fr))
+        oracle.lib().orc_rope(oracle.ptr(k), oracle.ptr(kr), 1, nkv, hd, pos[b], oracle.ptr(fr))
+        K = np.ascontiguousarray(np.concatenate([cached[b][0], kr]))
+        V = np.ascontiguousarray(np.concatenate([cached[b][1], v]))
+        o = np.empty((1, nq, hd), np.uint16)
+        oracle.lib().orc_attention(oracle.ptr(qr), oracle.ptr(K), oracle.ptr(V), oracle.ptr(o), 1, nq, pos[b] + 1,
+                                   nkv, hd, 0, -1)
+        ref.append(o.reshape(-1))
+        knew.append(kr.reshape(nkv, hd))
+    return dict(qkv=qkv, table=table, kpool=kpool, vpool=vpool, pos=np.array(pos, np.int32),
+                seq=np.arange(B, dtype=np.int32), ref=np.stack(ref), knew=knew, B=B, nq=nq, nkv=nkv, hd=hd,
+                pt_stride=pt_stride, n_pages=n_pages, max_len=max_len, theta=theta)
+
+
+def run_paged(c, fn="ti_op_paged_attention"):
+    bufs = {k: DevBuf.from_array(c[k]) for k in ("qkv", "table", "kpool", "vpool", "pos", "seq")}
+    out = DevBuf(c["B"] * c["nq"] * c["hd"] * 2)
+    ti.check(getattr(lib(), fn)(bufs["qkv"].ptr, c["B"], c["nq"], c["nkv"], c["hd"], bufs["pos"].ptr,
+                                bufs["seq"].ptr, bufs["table"].ptr, c["pt_stride"], bufs["kpool"].ptr,
+                                bufs["vpool"].ptr, c["n_pages"], c["max_len"], c["theta"], None, -1, out.ptr, None))
+    return (out.to_array((c["B"], c["nq"] * c["hd"]), np.uint16),
+            bufs["kpool"].to_array(c["kpool"].shape, np.uint16), bufs["vpool"].to_array(c["vpool"].shape, np.uint16))
+
+
+@pytest.mark.parametrize("hd,nq,nkv", [(128, 8, 2), (64, 4, 4), (128, 28, 4)])
+def test_paged_attention_op(hd, nq, nkv):
+    c = paged_case(hd=hd, nq=nq, nkv=nkv)
+    out, kp, vp = run_paged(c)
+    assert rel_err(f32(out), f32(c["ref"])) < 1e-2
+    for b in range(c["B"]):
+        p = int(c["pos"][b])
+        page = c["table"][b, p // 16]
+        assert rel_err(f32(kp[page, :, p % 16]), f32(c["knew"][b])) < 1e-2
+        np.testing.assert_array_equal(vp[page, :, p % 16],
+                                      c["qkv"][b, (nq + nkv) * hd:].reshape(nkv, hd))
