@@ -110,6 +110,20 @@ ti_status ti_op_paged_attention(const void* qkv, int batch, int n_heads, int n_k
                                 const int32_t* pos, const int32_t* seq, const int32_t* page_table, int pt_stride,
                                 void* k_pages, void* v_pages, int n_pages, int max_len, float theta,
                                 const ti_rope_scaling* scaling, int sliding_window, void* out, void* stream);
+/* Same computation and arguments as ti_op_paged_attention, for callers that
+ * cannot allocate device memory where they run it (a plugin whose host
+ * application owns the device-memory budget, or a process whose memory is
+ * fully reserved by another framework's allocator).  No counterpart in the
+ * reference.  Calls no allocator: the scratch is a fixed 8 MiB array that every
+ * GPU loading this library holds until exit.  The first call on a device looks
+ * up that array's device address (make it before any stream capture).  Sizes
+ * whose scratch exceeds 8 MiB return TI_ERR_INVALID.  All calls share the
+ * array, so calls that overlap on the GPU race; order them on one stream. */
+ti_status ti_op_paged_attention_noalloc(const void* qkv, int batch, int n_heads, int n_kv, int head_dim,
+                                        const int32_t* pos, const int32_t* seq, const int32_t* page_table,
+                                        int pt_stride, void* k_pages, void* v_pages, int n_pages, int max_len,
+                                        float theta, const ti_rope_scaling* scaling, int sliding_window, void* out,
+                                        void* stream);
 /* ops.hpp:98 / ops.cu:586-616 (BF16<->F32; same dtype = copy). */
 ti_status ti_op_cast(int src_dtype, int dst_dtype, const void* x, void* out, size_t n, void* stream);
 /* ops.hpp:95 / ops.cu:559-584: 2-D transpose [rows, cols] -> [cols, rows], F32 or BF16. */

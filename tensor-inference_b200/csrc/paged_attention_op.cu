@@ -6,6 +6,7 @@
 // merge needs scratch memory (per-split partial outputs and completion
 // counters); this entry takes it from the device's stream-ordered pool.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "internal.h"
@@ -88,5 +89,97 @@ extern "C" ti_status ti_op_paged_attention(const void* qkv, int batch, int n_hea
     cudaError_t f = cudaFreeAsync(scratch, s);
     TI_CHECK(e == cudaSuccess, TI_ERR_CUDA, "paged_attention: %s", cudaGetErrorString(e));
     TI_CUDA(f);
+    return TI_OK;
+}
+
+// ----------------------------------------------------------------------------
+// Allocation-free variant.
+//
+// Some callers cannot allocate device memory at the point where they run this
+// op: a plugin whose host application owns the whole device-memory budget and
+// forbids allocation inside its execute call, or a process whose memory is
+// fully reserved up front by another framework's caching allocator, so any
+// cudaMalloc (or pool growth) would fail or stall.  For them this entry takes
+// its scratch (split partials, merge counters, the RoPE table) from the
+// fixed-size array below instead of the memory pool.
+//
+// The array is a file-scope __device__ variable: every GPU that loads this
+// library holds kNoAllocScratchBytes of it until the process exits.  Host code
+// cannot use the symbol as a device address, so the address is looked up once
+// per device with cudaGetSymbolAddress, with that device current, on the first
+// call made on that device; make that first call before any stream capture.
+// All calls share the one array and it keeps the last call's contents, so
+// calls that overlap on the GPU (different streams, or different host threads
+// without ordering) race on it; order them on one stream.
+constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB per device
+static __device__ __align__(256) unsigned char g_paged_attn_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+std::mutex g_scratch_mu;
+void* g_scratch_addr[64] = {};
+
+ti_status scratch_address(int dev, void** out) {
+    TI_CHECK(dev >= 0 && dev < 64, TI_ERR_UNSUPPORTED, "paged_attention_noalloc: device index %d >= 64", dev);
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (!g_scratch_addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_paged_attn_scratch);
+        TI_CHECK(e == cudaSuccess && p, TI_ERR_CUDA, "paged_attention_noalloc: cudaGetSymbolAddress: %s",
+                 cudaGetErrorString(e));
+        g_scratch_addr[dev] = p;
+    }
+    *out = g_scratch_addr[dev];
+    return TI_OK;
+}
+
+}  // namespace
+
+extern "C" ti_status ti_op_paged_attention_noalloc(const void* qkv, int batch, int n_heads, int n_kv, int head_dim,
+                                                   const int32_t* pos, const int32_t* seq,
+                                                   const int32_t* page_table, int pt_stride, void* k_pages,
+                                                   void* v_pages, int n_pages, int max_len, float theta,
+                                                   const ti_rope_scaling* scaling, int sliding_window, void* out,
+                                                   void* stream) {
+    if (ti_status st = check_paged_args(qkv, batch, n_heads, n_kv, head_dim, pos, seq, page_table, pt_stride, k_pages,
+                                        v_pages, n_pages, max_len, out))
+        return st;
+    int dev = 0;
+    TI_CUDA(cudaGetDevice(&dev));
+    void* base = nullptr;
+    if (ti_status st = scratch_address(dev, &base)) return st;
+
+    AttnArgs a = make_args(qkv, batch, n_heads, n_kv, head_dim, pos, seq, page_table, pt_stride, k_pages, v_pages,
+                           n_pages, max_len, nullptr, sliding_window, out, num_sms(dev));
+    // scratch layout: [rope table][merge counters][split partials], 256-byte aligned parts
+    const size_t freq_bytes = ((size_t)head_dim / 2 * 4 + 255) & ~size_t(255);
+    const size_t nctr = (size_t)batch * n_kv;
+    const size_t ctr_bytes = (nctr * 4 + 255) & ~size_t(255);
+    const size_t part_bytes = attn_scratch_floats(batch, n_heads, n_kv, head_dim, a.n_splits) * 4;
+    const size_t need = freq_bytes + ctr_bytes + part_bytes;
+    TI_CHECK(need <= kNoAllocScratchBytes, TI_ERR_INVALID,
+             "paged_attention_noalloc: needs %zu scratch bytes for batch %d, %d kv heads, max_len %d; the fixed "
+             "scratch holds %zu (use ti_op_paged_attention)",
+             need, batch, n_kv, max_len, kNoAllocScratchBytes);
+
+    uint8_t* p = reinterpret_cast<uint8_t*>(base);
+    float* freqs = reinterpret_cast<float*>(p);
+    unsigned int* counters = reinterpret_cast<unsigned int*>(p + freq_bytes);
+    float* parts = reinterpret_cast<float*>(p + freq_bytes + ctr_bytes);
+    const size_t G = (size_t)(n_heads / n_kv);
+    a.freqs = freqs;
+    a.counters = counters;
+    a.part_o = parts;
+    a.part_ml = parts + (size_t)batch * n_kv * a.n_splits * G * head_dim;
+    a.err = nullptr;
+
+    cudaStream_t s = (cudaStream_t)stream;
+    // the same host-computed table as the pool-backed entry (ops.cu:235-278)
+    float host_freqs[128];
+    rope_freqs(head_dim, theta, scaling, host_freqs);
+    TI_CUDA(cudaMemcpyAsync(freqs, host_freqs, (size_t)head_dim / 2 * 4, cudaMemcpyHostToDevice, s));
+    // the merge counters must start at zero whatever the previous call left
+    TI_CUDA(cudaMemsetAsync(counters, 0, nctr * 4, s));
+    TI_CUDA(attn_launch(a, s, false));
     return TI_OK;
 }
