@@ -1,0 +1,91 @@
+// ref_shim.cpp — C entry points around the reference's own model code.
+//
+// TEST INFRASTRUCTURE: linked only into oracle/_ref/libref.so together with
+// the reference's unchanged sources (backend, parser, models, adapter loader),
+// compiled where they lie.  Used on the GPU box to produce golden logits that
+// pin the CPU oracle (tests/golden/make_golden.py).  The product never loads it.
+#include <tensor/adapter/adapter_loader.hpp>
+#include <tensor/backend/ops.hpp>
+#include <tensor/models/gemma/gemma_model.hpp>
+#include <tensor/models/llama/llama_model.hpp>
+#include <tensor/models/mistral/mistral_model.hpp>
+#include <tensor/models/qwen/qwen_adapter_model.hpp>
+#include <tensor/models/qwen/qwen_model.hpp>
+#include <tensor/parser/config.hpp>
+#include <tensor/parser/weight_map.hpp>
+
+#include <cstdio>
+#include <cstring>
+#include <exception>
+#include <vector>
+
+namespace ops = tensor::backend::ops;
+
+namespace {
+
+// logits [seq, vocab] bf16 -> fp32 last row (the row Generator samples from)
+void last_row(const tensor::backend::Tensor& lg, float* out, int vocab) {
+    auto f = ops::cast(lg, tensor::backend::DType::F32);
+    std::vector<float> h = f.to_host_f32();
+    std::memcpy(out, h.data() + (h.size() - (size_t)vocab), (size_t)vocab * 4);
+}
+
+template <class M>
+void run(M& model, const int32_t* prompt, int n_prompt, const int32_t* feed, int n_steps, int max_seq, float* logits,
+         int vocab) {
+    auto cache = model.make_cache((std::size_t)max_seq);
+    std::vector<int32_t> ids(prompt, prompt + n_prompt);
+    auto lg = model.forward(ids, cache);
+    last_row(lg, logits, vocab);
+    for (int i = 0; i < n_steps; ++i) {
+        lg = model.forward(std::vector<int32_t>{feed[i]}, cache);
+        last_row(lg, logits + (size_t)(i + 1) * vocab, vocab);
+    }
+}
+
+}  // namespace
+
+// arch: 0 llama, 1 qwen2, 2 gemma, 3 mistral; adapter_dir (qwen2 only) may be NULL.
+// logits: (1 + n_steps) x vocab fp32 — the prompt's last row, then one row per fed token.
+extern "C" int ref_run(const char* model_dir, int arch, const char* adapter_dir, const int32_t* prompt, int n_prompt,
+                       const int32_t* feed, int n_steps, int max_seq, float* logits, int vocab, char* err,
+                       int err_len) {
+    try {
+        const auto dev = tensor::backend::Device::cuda(0);
+        auto wm = tensor::parser::WeightMap::open(model_dir);
+        auto cfg = tensor::parser::ModelConfig::from_dir(model_dir);
+        switch (arch) {
+            case 0: {
+                auto m = tensor::models::llama::LlamaModel::load(wm, cfg, dev);
+                run(m, prompt, n_prompt, feed, n_steps, max_seq, logits, vocab);
+                break;
+            }
+            case 1: {
+                auto m = tensor::models::qwen::QwenModel::load(wm, cfg, dev);
+                if (adapter_dir) {
+                    auto aw = tensor::adapter::AdapterLoader::load(adapter_dir, "qwen2", cfg.num_hidden_layers(), dev);
+                    tensor::models::qwen::QwenAdapterModel am(std::move(m), std::move(aw));
+                    run(am, prompt, n_prompt, feed, n_steps, max_seq, logits, vocab);
+                } else {
+                    run(m, prompt, n_prompt, feed, n_steps, max_seq, logits, vocab);
+                }
+                break;
+            }
+            case 2: {
+                auto m = tensor::models::gemma::GemmaModel::load(wm, cfg, dev);
+                run(m, prompt, n_prompt, feed, n_steps, max_seq, logits, vocab);
+                break;
+            }
+            case 3: {
+                auto m = tensor::models::mistral::MistralModel::load(wm, model_dir, dev);
+                run(m, prompt, n_prompt, feed, n_steps, max_seq, logits, vocab);
+                break;
+            }
+            default: std::snprintf(err, err_len, "unknown arch %d", arch); return 2;
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        std::snprintf(err, err_len, "%s", e.what());
+        return 1;
+    }
+}

@@ -1,0 +1,47 @@
+"""The oracle against the reference's own outputs (tests/golden/*.npz).
+
+The fixtures hold the last-row logits the reference's unchanged CUDA model code
+produced on a B200 for seeded synthetic checkpoints (tests/golden/make_golden.py).
+Here the CPU oracle re-derives the same checkpoint, prompt and fed tokens and
+must match: BASELINE tolerance 2e-2 max-abs relative on logits, and the same
+greedy id wherever the reference's top-2 margin exceeds the logit error.
+"""
+import glob
+import json
+import os
+import sys
+
+import numpy as np
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "golden"))
+FIXTURES = sorted(glob.glob(os.path.join(HERE, "golden", "*.npz")))
+TOL = 2e-2
+
+
+def load(path):
+    z = np.load(path)
+    return json.loads(str(z["kw"])), z
+
+
+@pytest.mark.parametrize("path", FIXTURES, ids=[os.path.basename(p)[:-4] for p in FIXTURES])
+def test_oracle_matches_reference_goldens(orc, path):
+    import make_golden as mg
+
+    kw, z = load(path)
+    np.testing.assert_array_equal(mg.case_inputs(kw)[0], z["prompt"])
+    got = mg.oracle_logits(kw)
+    ref = z["ref_logits"]
+    assert got.shape == ref.shape
+    for i in range(len(ref)):
+        err = np.abs(got[i] - ref[i]).max() / np.abs(ref[i]).max()
+        assert err <= TOL, (i, err)
+        s = np.sort(ref[i])
+        if s[-1] - s[-2] > 2 * np.abs(got[i] - ref[i]).max():
+            assert int(np.argmax(got[i])) == int(np.argmax(ref[i])), i
+
+
+def test_fixtures_present():
+    names = {os.path.basename(p)[:-4] for p in FIXTURES}
+    assert {"llama_small", "qwen2_bias", "qwen2_bias_lora", "gemma", "mistral_window", "llama_rope_scaled"} <= names
