@@ -19,6 +19,7 @@
 //              layers (one page id per 16 positions of a sequence).
 //   page table [max_seqs][ceil(max_seq_len/16)] int32, -1 = unallocated.
 #include <algorithm>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -104,7 +105,29 @@ struct ti_engine {
     std::map<int, GraphEntry> graphs;
 
     int bound_batch = 0;
+    bool bound_lora = false;
     std::vector<int> bound_seqs;
+
+    // ---- LoRA adapter pool (padded rank R, S slots; padding rows/cols are zero)
+    struct AdapterMeta {
+        bool live = false;
+        int rank = 0, mask = 0;
+        float alpha = 0.f;
+        bool resident = true;
+        void* host = nullptr;        // pinned host copy (ti_adapter_stage_host)
+        cudaEvent_t ready = nullptr;  // completion of the last async prefetch
+        bool pending = false;
+    };
+    int R = 0, S = 0, lmask = 0;
+    // per kind (0 qkv, 1 o, 2 gate|up, 3 down): A / B pools, elements per layer per adapter
+    uint16_t* lA[4] = {};
+    uint16_t* lB[4] = {};
+    size_t lA_layer[4] = {}, lB_layer[4] = {};
+    int lK[4] = {}, lT[4] = {}, lRows[4] = {};  // A row length, A rows (sections*R), B rows
+    float* lscale = nullptr;
+    float* lt[4] = {};  // shrink outputs [B][T]
+    std::vector<AdapterMeta> adapters;
+    cudaStream_t side = nullptr;
 
     int32_t* dd_tokens() const { return d_desc + 4; }
     int32_t* dd_seq() const { return d_desc + 4 + o.max_batch; }
@@ -141,6 +164,14 @@ void free_all(ti_engine* e) {
     if (e->h_out) cudaFreeHost(e->h_out);
     e->h_desc = nullptr;
     e->h_out = nullptr;
+    for (auto& a : e->adapters) {
+        if (a.host) cudaFreeHost(a.host);
+        if (a.ready) cudaEventDestroy(a.ready);
+        a.host = nullptr;
+        a.ready = nullptr;
+    }
+    if (e->side) cudaStreamDestroy(e->side);
+    e->side = nullptr;
     if (e->cap) cudaStreamDestroy(e->cap);
     e->cap = nullptr;
 }
@@ -180,6 +211,12 @@ ti_status validate_desc(const ti_model_desc* d, const ti_engine_opts* o) {
     TI_CHECK(o->max_batch >= 1 && o->max_batch <= 256, TI_ERR_INVALID, "engine: max_batch out of range");
     TI_CHECK(o->max_seqs >= 1, TI_ERR_INVALID, "engine: max_seqs < 1");
     TI_CHECK(o->max_seq_len >= 1, TI_ERR_INVALID, "engine: max_seq_len < 1");
+    TI_CHECK(o->max_adapters >= 0 && o->max_adapters <= 4096, TI_ERR_INVALID, "engine: max_adapters out of range");
+    if (o->max_adapters > 0) {
+        TI_CHECK(o->max_lora_rank >= 1 && o->max_lora_rank <= 256, TI_ERR_INVALID, "engine: max_lora_rank 1..256");
+        TI_CHECK((o->lora_proj_mask & 0x7f) != 0 && (o->lora_proj_mask & ~0x7f) == 0, TI_ERR_INVALID,
+                 "engine: lora_proj_mask must name projections (TI_PROJ_*)");
+    }
     const int tp = o->tp_size <= 0 ? 1 : o->tp_size;
     TI_CHECK(tp == 1, TI_ERR_UNSUPPORTED, "engine: tensor parallelism is driven by ti_engine_create with tp_size 1 "
                                           "in this build");
@@ -283,6 +320,35 @@ ti_status build(ti_engine* e) {
     TI_CHECK(dalloc_t(e, &e->out, B + 1, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
     TI_CUDA(cudaMemset(e->out, 0, (B + 1) * 4));
     e->err = reinterpret_cast<int*>(e->out + B);
+    if (e->o.max_adapters > 0) {
+        e->S = e->o.max_adapters;
+        e->R = (e->o.max_lora_rank + 7) / 8 * 8;  // padded to whole 16-byte rows
+        e->lmask = e->o.lora_proj_mask;
+        const int R = e->R;
+        const bool on[4] = {(e->lmask & 7) != 0, (e->lmask & 8) != 0, (e->lmask & 48) != 0, (e->lmask & 64) != 0};
+        const int K[4] = {H, (int)QW, H, I};
+        const int T[4] = {3 * R, R, 2 * R, R};
+        const int rows[4] = {e->qkv_rows, H, 2 * I, H};
+        for (int k = 0; k < 4; ++k) {
+            if (!on[k]) continue;
+            e->lK[k] = K[k];
+            e->lT[k] = T[k];
+            e->lRows[k] = rows[k];
+            e->lA_layer[k] = (size_t)T[k] * K[k];
+            e->lB_layer[k] = (size_t)rows[k] * R;
+            const size_t na = e->lA_layer[k] * d.n_layers * e->S, nbb = e->lB_layer[k] * d.n_layers * e->S;
+            TI_CHECK(dalloc_t(e, &e->lA[k], na, &e->bytes_ad) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+            TI_CHECK(dalloc_t(e, &e->lB[k], nbb, &e->bytes_ad) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+            TI_CUDA(cudaMemset(e->lA[k], 0, na * 2));
+            TI_CUDA(cudaMemset(e->lB[k], 0, nbb * 2));
+            TI_CHECK(dalloc_t(e, &e->lt[k], (size_t)B * T[k], &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
+                     ti_last_error());
+        }
+        TI_CHECK(dalloc_t(e, &e->lscale, e->S, &e->bytes_ad) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+        TI_CUDA(cudaMemset(e->lscale, 0, (size_t)e->S * 4));
+        e->adapters.assign(e->S, ti_engine::AdapterMeta{});
+        TI_CUDA(cudaStreamCreateWithFlags(&e->side, cudaStreamNonBlocking));
+    }
     e->attn_splits_n = attn_splits(B, nkv, e->o.max_seq_len, e->sms, &e->attn_max_chunk);
     // partials sized for the largest batch; smaller batches use more splits per (token, head)
     int max_parts = 0;
@@ -306,7 +372,7 @@ ti_status build(ti_engine* e) {
 enum KernelKind { kKEmbed = 0, kKQkv = 1, kKAttn = 2, kKO = 3, kKGateUp = 4, kKDown = 5, kKLmHead = 6 };
 
 // Enqueue one kernel of a B-token step on `s` (graph capture or a plain launch).
-ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, int* launches) {
+ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, int* launches, bool lora) {
     const ti_model_desc& d = e->d;
     const int H = e->H, I = e->I, nq = e->nq, nkv = e->nkv, hd = e->hd;
     const int QW = nq * hd;
@@ -321,6 +387,10 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             c.x = a.x + (size_t)b0 * x_stride_elems;
             c.out = a.out + (size_t)b0 * out_stride;
             if (a.resid) c.resid = a.resid + (size_t)b0 * resid_stride;
+            if (a.lora.adapter) {
+                c.lora.adapter = a.lora.adapter + b0;
+                c.lora.t = a.lora.t + (size_t)b0 * a.lora.t_stride;
+            }
             if (epi == kEpiLmHead) {
                 c.amax = a.amax + b0;
                 c.done = a.done + (b0 / 8) % 16;  // one completion counter per launch
@@ -388,6 +458,43 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
     }
     TI_CHECK(li >= 0 && li < d.n_layers, TI_ERR_INVALID, "layer %d out of range", li);
     const LayerW& l = e->layers[li];
+    // LoRA (qwen_adapter_model.cpp:22-43): shrink t = bf16(x A^T) for each token's
+    // adapter right before the adapted GEMV, whose epilogue adds bf16(bf16(B t) * s)
+    auto lora_on = [&](int k) { return lora && e->lA[k] != nullptr; };
+    auto shrink = [&](int k, const uint16_t* x, int x_stride, const uint16_t* norm_w) -> ti_status {
+        LoraShrinkArgs la;
+        la.x = x;
+        la.x_stride = x_stride;
+        la.K = e->lK[k];
+        la.nb = B;
+        la.norm_w = norm_w;
+        la.eps = d.rms_eps;
+        la.norm_offset = gemma;
+        la.A = e->lA[k] + (size_t)li * e->lA_layer[k];
+        la.A_adapter_stride = e->lA_layer[k] * d.n_layers;
+        la.T = e->lT[k];
+        la.adapter = e->dd_adapter();
+        la.n_adapters = e->S;
+        la.t = e->lt[k];
+        la.t_stride = e->lT[k];
+        TI_CUDA(lora_shrink_launch(la, s, true));
+        if (launches) ++*launches;
+        return TI_OK;
+    };
+    auto set_lora = [&](GemvArgs& g, int k) {
+        g.lora.adapter = e->dd_adapter();
+        g.lora.B = e->lB[k] + (size_t)li * e->lB_layer[k];
+        g.lora.B_adapter_stride = e->lB_layer[k] * d.n_layers;
+        g.lora.t = e->lt[k];
+        g.lora.t_stride = e->lT[k];
+        g.lora.rank = e->R;
+        g.lora.scale = e->lscale;
+        g.lora.n_adapters = e->S;
+        if (k == 0) {
+            g.lora.sec1 = QW;
+            g.lora.sec2 = QW + nkv * hd;
+        }
+    };
     switch (kind) {
         case kKQkv: {
             GemvArgs q;
@@ -404,6 +511,10 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             q.bias = l.bqkv;
             q.err = e->err;
             set_next(q, l.wo, H, QW, 1);
+            if (lora_on(0)) {
+                if (ti_status st = shrink(0, e->hidden, H, l.norm1)) return st;
+                set_lora(q, 0);
+            }
             return gemv_all(q, kEpiStore, H, e->qkv_rows, 0);
         }
         case kKAttn: {
@@ -451,6 +562,10 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             ov.resid_stride = H;
             ov.err = e->err;
             set_next(ov, l.wgu, I, H, 2);
+            if (lora_on(1)) {
+                if (ti_status st = shrink(1, e->attn, QW, nullptr)) return st;
+                set_lora(ov, 1);
+            }
             return gemv_all(ov, kEpiResid, QW, H, H);
         }
         case kKGateUp: {
@@ -468,6 +583,10 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             gu.act = gemma ? 1 : 0;
             gu.err = e->err;
             set_next(gu, l.wdown, H, I, 1);
+            if (lora_on(2)) {
+                if (ti_status st = shrink(2, e->res1, H, l.norm2)) return st;
+                set_lora(gu, 2);
+            }
             return gemv_all(gu, kEpiGlu, H, I, 0);
         }
         case kKDown: {
@@ -484,25 +603,29 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             dn.err = e->err;
             if (li + 1 < d.n_layers) set_next(dn, e->layers[li + 1].wqkv, e->qkv_rows, H, 1);
             else set_next(dn, e->lm_head, e->Vl, H, 1);
+            if (lora_on(3)) {
+                if (ti_status st = shrink(3, e->act, I, nullptr)) return st;
+                set_lora(dn, 3);
+            }
             return gemv_all(dn, kEpiResid, I, H, H);
         }
         default: return fail(TI_ERR_INVALID, "unknown kernel kind %d", kind);
     }
 }
 
-ti_status enqueue_step(ti_engine* e, int B, cudaStream_t s, int* launches) {
-    if (ti_status st = enqueue_kernel(e, B, kKEmbed, 0, s, launches)) return st;
+ti_status enqueue_step(ti_engine* e, int B, cudaStream_t s, int* launches, bool lora) {
+    if (ti_status st = enqueue_kernel(e, B, kKEmbed, 0, s, launches, lora)) return st;
     for (int li = 0; li < e->d.n_layers; ++li)
         for (int k : {kKQkv, kKAttn, kKO, kKGateUp, kKDown})
-            if (ti_status st = enqueue_kernel(e, B, k, li, s, launches)) return st;
-    return enqueue_kernel(e, B, kKLmHead, 0, s, launches);
+            if (ti_status st = enqueue_kernel(e, B, k, li, s, launches, lora)) return st;
+    return enqueue_kernel(e, B, kKLmHead, 0, s, launches, lora);
 }
 
-ti_status capture_step(ti_engine* e, int B, GraphEntry* out) {
+ti_status capture_step(ti_engine* e, int B, bool lora, GraphEntry* out) {
     cudaStream_t s = e->cap;
     int launches = 0;
     TI_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-    ti_status st = enqueue_step(e, B, s, &launches);
+    ti_status st = enqueue_step(e, B, s, &launches, lora);
     cudaGraph_t graph = nullptr;
     cudaError_t ce = cudaStreamEndCapture(s, &graph);
     if (st) {
@@ -520,14 +643,34 @@ ti_status capture_step(ti_engine* e, int B, GraphEntry* out) {
     return TI_OK;
 }
 
-ti_status get_graph(ti_engine* e, int B, GraphEntry** g) {
-    auto it = e->graphs.find(B);
+// one graph per (batch size, LoRA on/off)
+ti_status get_graph(ti_engine* e, int B, bool lora, GraphEntry** g) {
+    lora = lora && e->S > 0;
+    const int key = B * 2 + (lora ? 1 : 0);
+    auto it = e->graphs.find(key);
     if (it == e->graphs.end()) {
         GraphEntry ge;
-        if (ti_status st = capture_step(e, B, &ge)) return st;
-        it = e->graphs.emplace(B, ge).first;
+        if (ti_status st = capture_step(e, B, lora, &ge)) return st;
+        it = e->graphs.emplace(key, ge).first;
     }
     *g = &it->second;
+    return TI_OK;
+}
+
+// adapters a step uses must exist and be resident; pending prefetches are
+// ordered before the step on `stream`
+ti_status adapters_ready(ti_engine* e, int B, const int32_t* adapters, cudaStream_t stream, bool* any) {
+    *any = false;
+    if (!adapters) return TI_OK;
+    for (int b = 0; b < B; ++b) {
+        const int a = adapters[b];
+        if (a < 0) continue;
+        TI_CHECK(a < e->S && e->adapters[a].live, TI_ERR_STATE, "unknown adapter %d", a);
+        auto& m = e->adapters[a];
+        TI_CHECK(m.resident, TI_ERR_STATE, "adapter %d is not resident (ti_adapter_prefetch_async)", a);
+        if (m.pending) TI_CUDA(cudaStreamWaitEvent(stream, m.ready, 0));
+        *any = true;
+    }
     return TI_OK;
 }
 
@@ -577,7 +720,6 @@ ti_status run_step(ti_engine* e, int B, const int32_t* seq_ids, const int32_t* t
         for (int c = 0; c < b; ++c)
             TI_CHECK(seq_ids[c] != seq_ids[b], TI_ERR_INVALID, "sequence %d appears twice in one step", seq_ids[b]);
         TI_CHECK(tokens[b] >= 0 && tokens[b] < e->V, TI_ERR_INVALID, "token %d out of range [0, %d)", tokens[b], e->V);
-        TI_CHECK(!adapters || adapters[b] < 0, TI_ERR_UNSUPPORTED, "LoRA adapters are not built in this engine yet");
         const int len = e->seqs[seq_ids[b]].len;
         TI_CHECK(len < e->o.max_seq_len, TI_ERR_STATE, "sequence %d is full (%d tokens)", seq_ids[b], len);
         if (ti_status st = ensure_pages(e, seq_ids[b], len + 1, &upd)) return st;
@@ -595,8 +737,10 @@ ti_status run_step(ti_engine* e, int B, const int32_t* seq_ids, const int32_t* t
     }
     TI_CHECK((int)upd.size() <= 3 * MB, TI_ERR_STATE, "too many page updates in one step");
     std::memcpy(h + 4 + 4 * MB, upd.data(), upd.size() * 4);
+    bool any_lora = false;
+    if (ti_status st = adapters_ready(e, B, adapters, stream, &any_lora)) return st;
     GraphEntry* g = nullptr;
-    if (ti_status st = get_graph(e, B, &g)) return st;
+    if (ti_status st = get_graph(e, B, any_lora, &g)) return st;
     TI_CUDA(cudaMemcpyAsync(e->d_desc, h, (size_t)e->desc_ints * 4, cudaMemcpyHostToDevice, stream));
     TI_CUDA(cudaGraphLaunch(g->exec, stream));
     TI_CUDA(cudaMemcpyAsync(e->h_out, e->out, (size_t)(MB + 1) * 4, cudaMemcpyDeviceToHost, stream));
@@ -837,7 +981,6 @@ ti_status ti_engine_bind(ti_engine* e, int B, const int32_t* seq_ids, const int3
     for (int b = 0; b < B; ++b) {
         if (ti_status st = seq_check(e, seq_ids[b])) return st;
         TI_CHECK(first_tokens[b] >= 0 && first_tokens[b] < e->V, TI_ERR_INVALID, "token out of range");
-        TI_CHECK(!adapter_ids || adapter_ids[b] < 0, TI_ERR_UNSUPPORTED, "LoRA adapters are not built yet");
         const SeqState& s = e->seqs[seq_ids[b]];
         TI_CHECK((int)s.pages.size() * kPageTokens > s.len, TI_ERR_STATE,
                  "sequence %d has no reserved page for its next token (ti_seq_reserve)", seq_ids[b]);
@@ -846,10 +989,13 @@ ti_status ti_engine_bind(ti_engine* e, int B, const int32_t* seq_ids, const int3
         h[4 + 2 * MB + b] = s.len;
         h[4 + 3 * MB + b] = adapter_ids ? adapter_ids[b] : -1;
     }
+    bool any_lora = false;
+    if (ti_status st = adapters_ready(e, B, adapter_ids, (cudaStream_t)0, &any_lora)) return st;
     GraphEntry* gr = nullptr;
-    if (ti_status st = get_graph(e, B, &gr)) return st;
+    if (ti_status st = get_graph(e, B, any_lora, &gr)) return st;
     TI_CUDA(cudaMemcpy(e->d_desc, h, (size_t)e->desc_ints * 4, cudaMemcpyHostToDevice));
     e->bound_batch = B;
+    e->bound_lora = any_lora;
     e->bound_seqs.assign(seq_ids, seq_ids + B);
     return TI_OK;
 }
@@ -857,7 +1003,7 @@ ti_status ti_engine_bind(ti_engine* e, int B, const int32_t* seq_ids, const int3
 ti_status ti_engine_decode_device(ti_engine* e, void* stream) {
     TI_CHECK(e && e->bound_batch > 0, TI_ERR_STATE, "engine not bound");
     GraphEntry* g = nullptr;
-    if (ti_status st = get_graph(e, e->bound_batch, &g)) return st;
+    if (ti_status st = get_graph(e, e->bound_batch, e->bound_lora, &g)) return st;
     TI_CUDA(cudaGraphLaunch(g->exec, (cudaStream_t)stream));
     return TI_OK;
 }
@@ -898,15 +1044,230 @@ ti_status ti_engine_launch_kernel(ti_engine* e, int kind, int layer, int batch, 
     TI_CHECK(e, TI_ERR_INVALID, "null engine");
     TI_CHECK(batch >= 1 && batch <= e->o.max_batch, TI_ERR_INVALID, "batch %d out of range", batch);
     DeviceGuard g(e->dev);
-    return enqueue_kernel(e, batch, kind, layer, (cudaStream_t)stream, nullptr);
+    return enqueue_kernel(e, batch, kind, layer, (cudaStream_t)stream, nullptr, false);
 }
 
 ti_status ti_engine_launches_per_step(ti_engine* e, int batch, int* launches) {
     TI_CHECK(e && launches, TI_ERR_INVALID, "null argument");
     DeviceGuard g(e->dev);
     GraphEntry* gr = nullptr;
-    if (ti_status st = get_graph(e, batch, &gr)) return st;
+    if (ti_status st = get_graph(e, batch, false, &gr)) return st;
     *launches = gr->launches;
+    return TI_OK;
+}
+
+}  // extern "C"
+
+// ==================================================================== LoRA adapters
+namespace {
+
+const char* kLoraProj[7] = {"self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj",
+                            "mlp.gate_proj",    "mlp.up_proj",      "mlp.down_proj"};
+const int kLoraKind[7] = {0, 0, 0, 1, 2, 2, 3};
+
+// projection p's (out, in) and where its A section / B rows sit in the kind's pool
+void lora_geometry(const ti_engine* e, int p, int* out, int* in, int* a_sec, int* b_row0) {
+    const int QW = e->nq * e->hd, KW = e->nkv * e->hd;
+    const int outs[7] = {QW, KW, KW, e->H, e->I, e->I, e->H};
+    const int ins[7] = {e->H, e->H, e->H, QW, e->H, e->H, e->I};
+    const int secs[7] = {0, 1, 2, 0, 0, 1, 0};
+    const int rows0[7] = {0, QW, QW + KW, 0, 0, e->I, 0};
+    *out = outs[p];
+    *in = ins[p];
+    *a_sec = secs[p];
+    *b_row0 = rows0[p];
+}
+
+uint16_t* lora_A(ti_engine* e, int ad, int layer, int p) {
+    const int k = kLoraKind[p];
+    int out, in, sec, row0;
+    lora_geometry(e, p, &out, &in, &sec, &row0);
+    return e->lA[k] + ((size_t)ad * e->d.n_layers + layer) * e->lA_layer[k] + (size_t)sec * e->R * e->lK[k];
+}
+uint16_t* lora_B(ti_engine* e, int ad, int layer, int p) {
+    const int k = kLoraKind[p];
+    int out, in, sec, row0;
+    lora_geometry(e, p, &out, &in, &sec, &row0);
+    return e->lB[k] + ((size_t)ad * e->d.n_layers + layer) * e->lB_layer[k] + (size_t)row0 * e->R;
+}
+
+ti_status adapter_check(ti_engine* e, int id) {
+    TI_CHECK(e, TI_ERR_INVALID, "null engine");
+    TI_CHECK(e->S > 0, TI_ERR_STATE, "engine created without adapter slots (max_adapters = 0)");
+    TI_CHECK(id >= 0 && id < e->S && e->adapters[id].live, TI_ERR_STATE, "unknown adapter %d", id);
+    return TI_OK;
+}
+
+// the adapter's device regions, kind by kind (A then B): (pointer, elements)
+std::vector<std::pair<uint16_t*, size_t>> adapter_regions(ti_engine* e, int id) {
+    std::vector<std::pair<uint16_t*, size_t>> r;
+    for (int k = 0; k < 4; ++k) {
+        if (!e->lA[k]) continue;
+        const size_t na = e->lA_layer[k] * e->d.n_layers, nb = e->lB_layer[k] * e->d.n_layers;
+        r.push_back({e->lA[k] + (size_t)id * na, na});
+        r.push_back({e->lB[k] + (size_t)id * nb, nb});
+    }
+    return r;
+}
+
+}  // namespace
+
+extern "C" {
+
+ti_status ti_adapter_create(ti_engine* e, int rank, float alpha, int proj_mask, int* adapter_id) {
+    clear_error();
+    TI_CHECK(e && adapter_id, TI_ERR_INVALID, "null argument");
+    TI_CHECK(e->S > 0, TI_ERR_STATE, "engine created without adapter slots (max_adapters = 0)");
+    TI_CHECK(rank >= 1 && rank <= e->R, TI_ERR_INVALID, "adapter rank %d outside [1, %d]", rank, e->R);
+    TI_CHECK(proj_mask != 0 && (proj_mask & ~e->lmask) == 0, TI_ERR_INVALID,
+             "adapter projections 0x%x not within the engine's lora_proj_mask 0x%x", proj_mask, e->lmask);
+    int id = -1;
+    for (int i = 0; i < e->S; ++i)
+        if (!e->adapters[i].live) {
+            id = i;
+            break;
+        }
+    TI_CHECK(id >= 0, TI_ERR_OOM, "all %d adapter slots in use", e->S);
+    DeviceGuard g(e->dev);
+    for (auto& reg : adapter_regions(e, id)) TI_CUDA(cudaMemset(reg.first, 0, reg.second * 2));
+    const float scale = alpha / (float)rank;  // AdapterWeights::scale, adapter_weights.hpp:85
+    TI_CUDA(cudaMemcpy(e->lscale + id, &scale, 4, cudaMemcpyHostToDevice));
+    auto& m = e->adapters[id];
+    m.live = true;
+    m.rank = rank;
+    m.alpha = alpha;
+    m.mask = proj_mask;
+    m.resident = true;
+    m.pending = false;
+    *adapter_id = id;
+    return TI_OK;
+}
+
+ti_status ti_adapter_load_tensor(ti_engine* e, int id, const char* name, const void* host, size_t bytes) {
+    clear_error();
+    if (ti_status st = adapter_check(e, id)) return st;
+    TI_CHECK(name && host, TI_ERR_INVALID, "null argument");
+    // "layers.{i}.{proj}.lora_A|B" (adapter_loader.cpp:180-222)
+    const std::string nm(name);
+    int layer = -1, p = -1;
+    char which = 0;
+    if (nm.rfind("layers.", 0) == 0 && nm.size() > 14 && nm.compare(nm.size() - 7, 6, ".lora_") == 0) {
+        which = nm.back();
+        const size_t dot = nm.find('.', 7);
+        if (dot != std::string::npos) {
+            layer = std::atoi(nm.substr(7, dot - 7).c_str());
+            const std::string pr = nm.substr(dot + 1, nm.size() - 7 - dot - 1);
+            for (int i = 0; i < 7; ++i)
+                if (pr == kLoraProj[i]) p = i;
+        }
+    }
+    TI_CHECK(p >= 0 && (which == 'A' || which == 'B') && layer >= 0 && layer < e->d.n_layers, TI_ERR_NOT_FOUND,
+             "unknown adapter tensor '%s'", name);
+    const auto& m = e->adapters[id];
+    TI_CHECK(m.mask & (1 << p), TI_ERR_INVALID, "adapter %d does not inject %s", id, kLoraProj[p]);
+    int out, in, sec, row0;
+    lora_geometry(e, p, &out, &in, &sec, &row0);
+    DeviceGuard g(e->dev);
+    if (which == 'A') {  // [rank, in], flat accepted (adapter_loader.cpp:67-81)
+        TI_CHECK(bytes == (size_t)m.rank * in * 2, TI_ERR_INVALID, "%s: %zu bytes, expected %zu", name, bytes,
+                 (size_t)m.rank * in * 2);
+        TI_CUDA(cudaMemcpy(lora_A(e, id, layer, p), host, bytes, cudaMemcpyHostToDevice));
+    } else {  // [out, rank] into rows of padded width R (adapter_loader.cpp:83-95)
+        TI_CHECK(bytes == (size_t)out * m.rank * 2, TI_ERR_INVALID, "%s: %zu bytes, expected %zu", name, bytes,
+                 (size_t)out * m.rank * 2);
+        TI_CUDA(cudaMemcpy2D(lora_B(e, id, layer, p), (size_t)e->R * 2, host, (size_t)m.rank * 2, (size_t)m.rank * 2,
+                             out, cudaMemcpyHostToDevice));
+    }
+    return TI_OK;
+}
+
+ti_status ti_adapter_init_synthetic(ti_engine* e, int id, uint64_t seed, float std_a, float std_b) {
+    clear_error();
+    if (ti_status st = adapter_check(e, id)) return st;
+    DeviceGuard g(e->dev);
+    const auto& m = e->adapters[id];
+    const float ca = synth_scale(std_a), cb = synth_scale(std_b);
+    for (int layer = 0; layer < e->d.n_layers; ++layer)
+        for (int p = 0; p < 7; ++p) {
+            if (!(m.mask & (1 << p))) continue;
+            int out, in, sec, row0;
+            lora_geometry(e, p, &out, &in, &sec, &row0);
+            const std::string base = "layers." + std::to_string(layer) + "." + kLoraProj[p];
+            TI_CUDA(synth_bf16_launch(lora_A(e, id, layer, p), m.rank, in, in, 0, 0, in, seed,
+                                      fnv1a((base + ".lora_A").c_str()), ca, (cudaStream_t)0));
+            TI_CUDA(synth_bf16_launch(lora_B(e, id, layer, p), out, m.rank, e->R, 0, 0, m.rank, seed,
+                                      fnv1a((base + ".lora_B").c_str()), cb, (cudaStream_t)0));
+        }
+    TI_CUDA(cudaDeviceSynchronize());
+    return TI_OK;
+}
+
+ti_status ti_adapter_stage_host(ti_engine* e, int id) {
+    clear_error();
+    if (ti_status st = adapter_check(e, id)) return st;
+    DeviceGuard g(e->dev);
+    auto& m = e->adapters[id];
+    TI_CHECK(m.resident, TI_ERR_STATE, "adapter %d is not resident", id);
+    const auto regs = adapter_regions(e, id);
+    size_t total = 0;
+    for (auto& r : regs) total += r.second * 2;
+    if (!m.host) TI_CUDA(cudaMallocHost(&m.host, total));
+    size_t off = 0;
+    for (auto& r : regs) {
+        TI_CUDA(cudaMemcpy(static_cast<uint8_t*>(m.host) + off, r.first, r.second * 2, cudaMemcpyDeviceToHost));
+        off += r.second * 2;
+    }
+    return TI_OK;
+}
+
+ti_status ti_adapter_evict(ti_engine* e, int id) {
+    clear_error();
+    if (ti_status st = adapter_check(e, id)) return st;
+    auto& m = e->adapters[id];
+    TI_CHECK(m.host, TI_ERR_STATE, "adapter %d has no host copy (ti_adapter_stage_host first)", id);
+    DeviceGuard g(e->dev);
+    if (m.pending) TI_CUDA(cudaEventSynchronize(m.ready));
+    for (auto& r : adapter_regions(e, id)) TI_CUDA(cudaMemset(r.first, 0, r.second * 2));
+    TI_CUDA(cudaDeviceSynchronize());
+    m.resident = false;
+    m.pending = false;
+    return TI_OK;
+}
+
+// pinned host -> HBM on the engine's side stream; steps that use the adapter
+// wait on the copy's event (adapters_ready) instead of the host
+ti_status ti_adapter_prefetch_async(ti_engine* e, int id) {
+    clear_error();
+    if (ti_status st = adapter_check(e, id)) return st;
+    auto& m = e->adapters[id];
+    TI_CHECK(m.host, TI_ERR_STATE, "adapter %d has no host copy (ti_adapter_stage_host first)", id);
+    if (m.resident && !m.pending) return TI_OK;
+    DeviceGuard g(e->dev);
+    size_t off = 0;
+    for (auto& r : adapter_regions(e, id)) {
+        TI_CUDA(cudaMemcpyAsync(r.first, static_cast<const uint8_t*>(m.host) + off, r.second * 2,
+                                cudaMemcpyHostToDevice, e->side));
+        off += r.second * 2;
+    }
+    if (!m.ready) TI_CUDA(cudaEventCreateWithFlags(&m.ready, cudaEventDisableTiming));
+    TI_CUDA(cudaEventRecord(m.ready, e->side));
+    m.resident = true;
+    m.pending = true;
+    return TI_OK;
+}
+
+ti_status ti_adapter_is_resident(ti_engine* e, int id, int* resident) {
+    clear_error();
+    if (ti_status st = adapter_check(e, id)) return st;
+    TI_CHECK(resident, TI_ERR_INVALID, "null argument");
+    auto& m = e->adapters[id];
+    if (m.pending) {
+        const cudaError_t q = cudaEventQuery(m.ready);
+        if (q == cudaSuccess) m.pending = false;
+        else if (q != cudaErrorNotReady) return fail(TI_ERR_CUDA, "adapter %d copy: %s", id, cudaGetErrorString(q));
+        else cudaGetLastError();
+    }
+    *resident = (m.resident && !m.pending) ? 1 : 0;
     return TI_OK;
 }
 

@@ -87,15 +87,22 @@ TI_DEVICE_INLINE float glu_act(float g, int act) {
 }
 
 // LoRA expansion of one output element (qwen_adapter_model.cpp:27-29 + :42)
-TI_DEVICE_INLINE float lora_delta(const GemvLora& L, int b, int row, int t_off, float base) {
-    const uint16_t* B = L.B[b];
-    if (B == nullptr) return base;
-    const uint16_t* br = B + (size_t)row * L.rank;
+TI_DEVICE_INLINE float lora_delta(const GemvLora& L, int ad, int b, int row, int t_off, float base) {
+    if (ad < 0 || ad >= L.n_adapters) return base;
+    const uint16_t* br = L.B + (size_t)ad * L.B_adapter_stride + (size_t)row * L.rank;
     const float* t = L.t + (size_t)b * L.t_stride + t_off;
     float s = 0.f;
-    for (int i = 0; i < L.rank; ++i) s = fmaf(__uint_as_float((uint32_t)br[i] << 16), t[i], s);
+    for (int i = 0; i < L.rank; i += 8) {
+        const uint4 w = *reinterpret_cast<const uint4*>(br + i);
+        const uint32_t* wp = reinterpret_cast<const uint32_t*>(&w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            s = fmaf(bf_lo(wp[e]), t[i + 2 * e], s);
+            s = fmaf(bf_hi(wp[e]), t[i + 2 * e + 1], s);
+        }
+    }
     const float up = round_bf(s);
-    const float delta = round_bf(up * L.scale[b]);
+    const float delta = round_bf(up * L.scale[ad]);
     return round_bf(base + delta);
 }
 
@@ -231,6 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int r = lane / NB, b = lane % NB;
             if (lane < rows_per_stage * NB && r < nr && b < a.nb) {
                 const int n = row0 + r;
+                const int ad = a.lora.adapter ? a.lora.adapter[b] : -1;
                 float accu[U];
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
@@ -243,23 +251,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (EPI == kEpiStore) {
                     float v = round_bf(accu[0]);
                     if (a.bias) v = round_bf(v + __uint_as_float((uint32_t)e_bias[n - u0] << 16));
-                    if (a.lora.B) {
+                    if (ad >= 0) {
                         // sections of the fused q|k|v rows: t offset = section * rank
                         const int sec = (n >= a.lora.sec1) + (n >= a.lora.sec2);
-                        v = lora_delta(a.lora, b, n, sec * a.lora.rank, v);
+                        v = lora_delta(a.lora, ad, b, n, sec * a.lora.rank, v);
                     }
                     reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + n] = f2bf(v);
                 } else if (EPI == kEpiResid) {
                     float v = round_bf(accu[0]);
-                    if (a.lora.B) v = lora_delta(a.lora, b, n, 0, v);
+                    if (ad >= 0) v = lora_delta(a.lora, ad, b, n, 0, v);
                     const float rr = __uint_as_float((uint32_t)e_res[b * rows_cap + (n - u0)] << 16);
                     reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + n] = f2bf(rr + v);
                 } else if (EPI == kEpiGlu) {
                     float gv = round_bf(accu[0]);
                     float uv = round_bf(accu[U - 1]);
-                    if (a.lora.B) {
-                        gv = lora_delta(a.lora, b, n, 0, gv);
-                        uv = lora_delta(a.lora, b, a.N + n, a.lora.rank, uv);
+                    if (ad >= 0) {
+                        gv = lora_delta(a.lora, ad, b, n, 0, gv);
+                        uv = lora_delta(a.lora, ad, b, a.N + n, a.lora.rank, uv);
                     }
                     const float hv = glu_act(gv, a.act);
                     reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + n] = f2bf(hv * uv);

@@ -24,15 +24,35 @@ enum GemvEpi : int {
 
 struct GemvLora {
     // per-token low-rank expansion added after the base projection (and bias):
-    // out = bf16(out + bf16(bf16(sum_r B[n, r] * t[b, r]) * scale[b]))
-    const uint16_t* const* B = nullptr;  // [nb] device pointers to B [N_total, rank] bf16 (nullptr = none)
-    const float* t = nullptr;            // [nb, t_stride] bf16-exact fp32 values of x A^T
+    // out = bf16(out + bf16(bf16(sum_r B[n, r] * t[b, r]) * scale[adapter[b]]))
+    const int32_t* adapter = nullptr;  // [nb] adapter id per token (device); < 0 = none; nullptr = LoRA off
+    const uint16_t* B = nullptr;       // adapter 0's B rows for this layer: [rows, rank]
+    size_t B_adapter_stride = 0;       // elements from one adapter's rows to the next's
+    const float* t = nullptr;          // [nb, t_stride] bf16-exact fp32 values of x A^T
     int t_stride = 0;
-    int rank = 0;
-    const float* scale = nullptr;        // [nb]
+    int rank = 0;                      // padded rank (padding rows of A / cols of B are zero)
+    const float* scale = nullptr;      // [n_adapters] alpha / rank
+    int n_adapters = 0;
     // fused q|k|v rows: rows [0,sec1) use t[0:rank), [sec1,sec2) t[rank:2rank), the rest t[2rank:3rank)
     int sec1 = 1 << 30, sec2 = 1 << 30;
 };
+
+// LoRA shrink: t[b, r] = bf16(x_b . A[adapter[b]][r]), optional RMSNorm of x first
+struct LoraShrinkArgs {
+    const uint16_t* x = nullptr;  // [nb, x_stride] bf16
+    int x_stride = 0, K = 0, nb = 1;
+    const uint16_t* norm_w = nullptr;
+    float eps = 1e-5f;
+    int norm_offset = 0;
+    const uint16_t* A = nullptr;  // adapter 0's A rows for this layer: [T, K]
+    size_t A_adapter_stride = 0;
+    int T = 0;                    // rows: sections x padded rank
+    const int32_t* adapter = nullptr;
+    int n_adapters = 0;
+    float* t = nullptr;           // [nb, t_stride]
+    int t_stride = 0;
+};
+cudaError_t lora_shrink_launch(const LoraShrinkArgs& a, cudaStream_t s, bool pdl);
 
 struct GemvArgs {
     const uint16_t* W = nullptr;  // bf16 [rows, K]; kEpiGlu: gate rows [0,N) then up rows [N,2N)

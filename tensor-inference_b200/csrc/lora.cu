@@ -1,0 +1,98 @@
+// lora.cu — LoRA "shrink" step: t[b, :] = bf16(x_b @ A^T) for each token's adapter.
+//
+// The reference's apply_lora (qwen_adapter_model.cpp:22-30) computes
+// down = matmul_t(x, lora_A) (rounded to bf16), up = matmul_t(down, lora_B),
+// delta = up * (alpha / rank), and add_if_present adds it to the base
+// projection (:35-43).  Here `down` is this kernel's output; the weight-streaming
+// GEMV that produces the base projection applies the expansion in its epilogue.
+// Per-token adapters make it a segmented gather: token b reads the A rows of
+// adapter[b] (no adapter: nothing is written and the GEMV skips the delta).
+// x is the projection's input: RMSNorm(hidden) for q|k|v and gate|up (the same
+// normalised row the reference passes to both the base and the LoRA matmul),
+// the attention output for o, the SwiGLU activation for down.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ti {
+
+constexpr int kShrinkThreads = 256;
+constexpr int kShrinkRowsPerCta = 16;
+
+__global__ void __launch_bounds__(kShrinkThreads) k_lora_shrink(const LoraShrinkArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint16_t* xs = reinterpret_cast<uint16_t*>(smem);  // [K] normalised bf16 row
+    __shared__ float red[kShrinkThreads / 32];
+    const int b = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) pdl_trigger();
+    const int ad = a.adapter[b];
+    pdl_wait();
+    if (ad < 0 || ad >= a.n_adapters) return;
+    const int K = a.K;
+    const uint16_t* x = a.x + (size_t)b * a.x_stride;
+    // load (and normalise) the row: 8 bf16 per thread-iteration
+    float ss = 0.f;
+    for (int c = tid * 8; c < K; c += kShrinkThreads * 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(x + c);
+        *reinterpret_cast<uint4*>(xs + c) = v;
+        const uint32_t* vp = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            ss = fmaf(bf_lo(vp[e]), bf_lo(vp[e]), ss);
+            ss = fmaf(bf_hi(vp[e]), bf_hi(vp[e]), ss);
+        }
+    }
+    if (a.norm_w) {
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < kShrinkThreads / 32; ++w) tot += red[w];
+        const float scale = rsqrtf(tot / (float)K + a.eps);  // ops.cu:179
+        const float off = a.norm_offset ? 1.0f : 0.0f;
+        for (int c = tid * 8; c < K; c += kShrinkThreads * 8) {
+            uint4 v = *reinterpret_cast<const uint4*>(xs + c);
+            const uint4 wn = *reinterpret_cast<const uint4*>(a.norm_w + c);
+            uint32_t* vp = reinterpret_cast<uint32_t*>(&v);
+            const uint32_t* wp = reinterpret_cast<const uint32_t*>(&wn);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float lo = bf_lo(vp[e]) * scale * (bf_lo(wp[e]) + off);
+                const float hi = bf_hi(vp[e]) * scale * (bf_hi(wp[e]) + off);
+                vp[e] = pack_bf2(lo, hi);
+            }
+            *reinterpret_cast<uint4*>(xs + c) = v;
+        }
+    }
+    __syncthreads();
+    // rows of this CTA: warp w takes rows r0 + w, r0 + w + 8
+    const uint16_t* A = a.A + (size_t)ad * a.A_adapter_stride;
+    const int r0 = blockIdx.x * kShrinkRowsPerCta;
+    for (int r = r0 + warp; r < min(a.T, r0 + kShrinkRowsPerCta); r += kShrinkThreads / 32) {
+        const uint16_t* ar = A + (size_t)r * K;
+        float acc = 0.f;
+        for (int c = lane * 8; c < K; c += 32 * 8) {
+            const uint4 w = *reinterpret_cast<const uint4*>(ar + c);
+            const uint4 xv = *reinterpret_cast<const uint4*>(xs + c);
+            acc = dot8_bf16(w, xv, acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) a.t[(size_t)b * a.t_stride + r] = round_bf(acc);
+    }
+}
+
+cudaError_t lora_shrink_launch(const LoraShrinkArgs& a, cudaStream_t s, bool pdl) {
+    if (a.K % 8 != 0 || a.T <= 0) return cudaErrorInvalidValue;
+    LoraShrinkArgs args = a;
+    void* params[] = {&args};
+    const size_t smem = (size_t)a.K * 2;
+    const void* f = reinterpret_cast<const void*>(&k_lora_shrink);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    return launch_pdl(f, dim3((a.T + kShrinkRowsPerCta - 1) / kShrinkRowsPerCta, a.nb), dim3(kShrinkThreads), smem, s,
+                      params, pdl);
+}
+
+}  // namespace ti

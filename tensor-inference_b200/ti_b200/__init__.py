@@ -108,6 +108,13 @@ _SIGS = {
     "ti_engine_check": (C.c_int, [C.c_void_p]),
     "ti_engine_launches_per_step": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_int)]),
     "ti_engine_launch_kernel": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "ti_adapter_create": (C.c_int, [C.c_void_p, C.c_int, C.c_float, C.c_int, C.POINTER(C.c_int)]),
+    "ti_adapter_load_tensor": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_void_p, C.c_size_t]),
+    "ti_adapter_init_synthetic": (C.c_int, [C.c_void_p, C.c_int, C.c_uint64, C.c_float, C.c_float]),
+    "ti_adapter_stage_host": (C.c_int, [C.c_void_p, C.c_int]),
+    "ti_adapter_evict": (C.c_int, [C.c_void_p, C.c_int]),
+    "ti_adapter_prefetch_async": (C.c_int, [C.c_void_p, C.c_int]),
+    "ti_adapter_is_resident": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_int)]),
 }
 
 
@@ -380,6 +387,33 @@ class Engine:
 
     def launch_kernel(self, kind, layer, batch, stream=None):
         check(lib().ti_engine_launch_kernel(self.h, kind, layer, batch, C.c_void_p(stream) if stream else None))
+
+    # ---- LoRA adapters
+    def adapter_create(self, rank, alpha, proj_mask):
+        a = C.c_int()
+        check(lib().ti_adapter_create(self.h, rank, alpha, proj_mask, C.byref(a)))
+        return a.value
+
+    def adapter_load_tensor(self, adapter, name, arr):
+        arr = np.ascontiguousarray(arr, np.uint16)
+        check(lib().ti_adapter_load_tensor(self.h, adapter, name.encode(), _ptr(arr), arr.nbytes))
+
+    def adapter_init_synthetic(self, adapter, seed, std_a=0.02, std_b=0.001):
+        check(lib().ti_adapter_init_synthetic(self.h, adapter, seed, std_a, std_b))
+
+    def adapter_stage_host(self, adapter):
+        check(lib().ti_adapter_stage_host(self.h, adapter))
+
+    def adapter_evict(self, adapter):
+        check(lib().ti_adapter_evict(self.h, adapter))
+
+    def adapter_prefetch_async(self, adapter):
+        check(lib().ti_adapter_prefetch_async(self.h, adapter))
+
+    def adapter_is_resident(self, adapter):
+        r = C.c_int()
+        check(lib().ti_adapter_is_resident(self.h, adapter, C.byref(r)))
+        return bool(r.value)
 
     def launches_per_step(self, batch):
         n = C.c_int()
