@@ -379,11 +379,15 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
     const bool gemma = d.arch == TI_ARCH_GEMMA;
     std::string why;
 
-    // SIMT GEMV: batch chunks of <= 8 tokens
+    // SIMT GEMV: batch chunks of <= 8 tokens, fewer when the tokens' activation
+    // rows (kept in shared memory) would crowd out a two-stage weight ring
     auto gemv_all = [&](GemvArgs a, int epi, int x_stride_elems, int out_stride, int resid_stride) -> ti_status {
-        for (int b0 = 0; b0 < B; b0 += 8) {
+        const size_t U = epi == kEpiGlu ? 2 : 1;
+        int chunk = 8;
+        while (chunk > 1 && (size_t)chunk * a.K * 2 + 2 * U * (size_t)a.K * 2 + 16 * 1024 > 220 * 1024) chunk /= 2;
+        for (int b0 = 0; b0 < B; b0 += chunk) {
             GemvArgs c = a;
-            c.nb = std::min(8, B - b0);
+            c.nb = std::min(chunk, B - b0);
             c.x = a.x + (size_t)b0 * x_stride_elems;
             c.out = a.out + (size_t)b0 * out_stride;
             if (a.resid) c.resid = a.resid + (size_t)b0 * resid_stride;
@@ -393,7 +397,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             }
             if (epi == kEpiLmHead) {
                 c.amax = a.amax + b0;
-                c.done = a.done + (b0 / 8) % 16;  // one completion counter per launch
+                c.done = a.done + (b0 / chunk) % 16;  // one completion counter per launch
                 c.out_ids = a.out_ids + b0;
                 if (a.chain_tokens) c.chain_tokens = a.chain_tokens + b0;
                 if (a.chain_pos) c.chain_pos = a.chain_pos + b0;

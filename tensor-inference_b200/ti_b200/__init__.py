@@ -108,6 +108,11 @@ _SIGS = {
     "ti_engine_check": (C.c_int, [C.c_void_p]),
     "ti_engine_launches_per_step": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_int)]),
     "ti_engine_launch_kernel": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "ti_pkm_create": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
+    "ti_pkm_destroy": (C.c_int, [C.c_void_p]),
+    "ti_pkm_register": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]),
+    "ti_pkm_query": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "ti_pkm_query_host": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     "ti_adapter_create": (C.c_int, [C.c_void_p, C.c_int, C.c_float, C.c_int, C.POINTER(C.c_int)]),
     "ti_adapter_load_tensor": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_void_p, C.c_size_t]),
     "ti_adapter_init_synthetic": (C.c_int, [C.c_void_p, C.c_int, C.c_uint64, C.c_float, C.c_float]),
@@ -419,3 +424,46 @@ class Engine:
         n = C.c_int()
         check(lib().ti_engine_launches_per_step(self.h, batch, C.byref(n)))
         return n.value
+
+
+# ---------------------------------------------------------------- PKM router
+class Pkm:
+    """two-codebook product-key router (ti_pkm_*)"""
+
+    def __init__(self, c1, c2, device=0):
+        c1 = np.ascontiguousarray(c1, np.float32)
+        c2 = np.ascontiguousarray(c2, np.float32)
+        assert c1.shape == c2.shape and c1.ndim == 2
+        self.n_codes, self.half_dim = c1.shape
+        h = C.c_void_p()
+        check(lib().ti_pkm_create(device, self.n_codes, self.half_dim, _ptr(c1), _ptr(c2), C.byref(h)))
+        self.h = h
+
+    def close(self):
+        if self.h:
+            lib().ti_pkm_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def register(self, centroids, adapter_ids):
+        centroids = np.ascontiguousarray(centroids, np.float32)
+        ids = np.ascontiguousarray(adapter_ids, np.int32)
+        check(lib().ti_pkm_register(self.h, _ptr(centroids), _ptr(ids), len(ids)))
+
+    def query_host(self, queries):
+        q = np.ascontiguousarray(queries, np.float32)
+        n = q.shape[0]
+        addr = np.empty(n, np.int32)
+        ad = np.empty(n, np.int32)
+        check(lib().ti_pkm_query_host(self.h, _ptr(q), n, _ptr(addr), _ptr(ad)))
+        return addr, ad
+
+    def query(self, q_dev, n, addr_dev, adapter_dev, stream=None):
+        check(lib().ti_pkm_query(self.h, C.c_void_p(q_dev), n, C.c_void_p(addr_dev), C.c_void_p(adapter_dev),
+                                 C.c_void_p(stream) if stream else None))
+
