@@ -99,6 +99,13 @@ struct ti_engine {
     float *part_o = nullptr, *part_ml = nullptr;
     unsigned int* counters = nullptr;
     int attn_splits_n = 1, attn_max_chunk = 0;
+    // tensor-core path (batches of tc_min..256 tokens): RMSNorm'd rows, split-K
+    // partials and per-tile tickets
+    int tc_min = 16;
+    uint16_t* xn = nullptr;
+    float* tc_ws = nullptr;
+    size_t tc_ws_floats = 0;
+    unsigned int* tc_ctr = nullptr;
 
     std::vector<Slot> slots;
     std::map<std::string, size_t> slot_index;
@@ -320,6 +327,22 @@ ti_status build(ti_engine* e) {
     TI_CHECK(dalloc_t(e, &e->out, B + 1, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
     TI_CUDA(cudaMemset(e->out, 0, (B + 1) * 4));
     e->err = reinterpret_cast<int*>(e->out + B);
+    {
+        const char* env = std::getenv("TI_TC_MIN_BATCH");
+        e->tc_min = env ? std::atoi(env) : 16;
+        if (B >= e->tc_min && e->tc_min > 0) {
+            const int kmax = std::max(H, std::max((int)QW, I));
+            TI_CHECK(dalloc_t(e, &e->xn, (size_t)std::min(B, 256) * kmax, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
+                     ti_last_error());
+            e->tc_ws_floats = (size_t)8 << 20;  // 32 MB of split-K partials
+            TI_CHECK(dalloc(e, reinterpret_cast<void**>(&e->tc_ws), e->tc_ws_floats * 4, &e->bytes_work) == TI_OK,
+                     TI_ERR_OOM, "%s", ti_last_error());
+            const size_t ntiles = (size_t)std::max(e->Vl, std::max(2 * I, e->qkv_rows)) / 64 + 64;
+            TI_CHECK(dalloc(e, reinterpret_cast<void**>(&e->tc_ctr), ntiles * 4, &e->bytes_work) == TI_OK,
+                     TI_ERR_OOM, "%s", ti_last_error());
+            TI_CUDA(cudaMemset(e->tc_ctr, 0, ntiles * 4));
+        }
+    }
     if (e->o.max_adapters > 0) {
         e->S = e->o.max_adapters;
         e->R = (e->o.max_lora_rank + 7) / 8 * 8;  // padded to whole 16-byte rows
@@ -410,6 +433,26 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         return TI_OK;
     };
 
+    // batches of tc_min..256 tokens: RMSNorm pass (when the GEMV would fuse it)
+    // + tcgen05 GEMM; projections with LoRA on stay on the GEMV
+    auto gemm = [&](GemvArgs a, int epi, int x_stride_elems, int out_stride, int resid_stride) -> ti_status {
+        if (!(e->xn && B >= e->tc_min && B <= 256 && !a.lora.adapter))
+            return gemv_all(a, epi, x_stride_elems, out_stride, resid_stride);
+        a.nb = B;
+        if (a.norm_w) {
+            TI_CUDA(rms_rows_launch(a.x, a.x_stride, a.norm_w, a.eps, a.norm_offset, a.K, B, e->xn, a.K, s, true));
+            if (launches) ++*launches;
+            a.x = e->xn;
+            a.x_stride = a.K;
+            a.norm_w = nullptr;
+        }
+        TcPlan plan;
+        if (!tc_plan(a, epi, e->dev, e->tc_ws_floats, &plan, &why)) return fail(TI_ERR_UNSUPPORTED, "%s", why.c_str());
+        TI_CUDA(tc_launch(a, epi, plan, e->tc_ws, e->tc_ctr, s, true));
+        if (launches) ++*launches;
+        return TI_OK;
+    };
+
     if (kind == kKEmbed) {
         EmbedArgs ea;
         ea.table = e->embed;
@@ -458,7 +501,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         lm.chain_pos = e->dd_pos();
         lm.err = e->err;
         set_next(lm, e->layers[0].wqkv, e->qkv_rows, H, 1);
-        return gemv_all(lm, kEpiLmHead, H, e->Vl, 0);
+        return gemm(lm, kEpiLmHead, H, e->Vl, 0);
     }
     TI_CHECK(li >= 0 && li < d.n_layers, TI_ERR_INVALID, "layer %d out of range", li);
     const LayerW& l = e->layers[li];
@@ -519,7 +562,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
                 if (ti_status st = shrink(0, e->hidden, H, l.norm1)) return st;
                 set_lora(q, 0);
             }
-            return gemv_all(q, kEpiStore, H, e->qkv_rows, 0);
+            return gemm(q, kEpiStore, H, e->qkv_rows, 0);
         }
         case kKAttn: {
             int mc = 0;
@@ -570,7 +613,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
                 if (ti_status st = shrink(1, e->attn, QW, nullptr)) return st;
                 set_lora(ov, 1);
             }
-            return gemv_all(ov, kEpiResid, QW, H, H);
+            return gemm(ov, kEpiResid, QW, H, H);
         }
         case kKGateUp: {
             GemvArgs gu;
@@ -591,7 +634,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
                 if (ti_status st = shrink(2, e->res1, H, l.norm2)) return st;
                 set_lora(gu, 2);
             }
-            return gemv_all(gu, kEpiGlu, H, I, 0);
+            return gemm(gu, kEpiGlu, H, I, 0);
         }
         case kKDown: {
             GemvArgs dn;
@@ -611,7 +654,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
                 if (ti_status st = shrink(3, e->act, I, nullptr)) return st;
                 set_lora(dn, 3);
             }
-            return gemv_all(dn, kEpiResid, I, H, H);
+            return gemm(dn, kEpiResid, I, H, H);
         }
         default: return fail(TI_ERR_INVALID, "unknown kernel kind %d", kind);
     }

@@ -99,6 +99,25 @@ struct GemvPlan {
 bool gemv_plan(const GemvArgs& a, int epi, int device, GemvPlan* plan, std::string* why);
 cudaError_t gemv_launch(const GemvArgs& a, int epi, const GemvPlan& plan, cudaStream_t s, bool pdl);
 
+// ----------------------------------------------------------------- tensor-core GEMM (tcgen05)
+// Same arguments and epilogues as the GEMV (no RMSNorm prologue, no LoRA: the
+// caller normalises rows with rms_rows_launch first); batches of 1..256 tokens.
+struct TcPlan {
+    int np = 0;  // tokens padded to a multiple of 32 (MMA N)
+    int tiles = 0, splits = 1, kblocks = 0, kb_split = 0, units = 0, grid = 0, stages = 0;
+    uint32_t stage_bytes = 0, tmem_cols = 0;
+    size_t smem = 0;
+    size_t ws_floats = 0;  // split-K partial workspace this launch needs
+    const void* func = nullptr;
+};
+bool tc_plan(const GemvArgs& a, int epi, int device, size_t ws_floats_cap, TcPlan* plan, std::string* why);
+// ws: >= plan.ws_floats floats; tile_ctr: >= plan.tiles zeroed counters (both only when splits > 1)
+cudaError_t tc_launch(const GemvArgs& a, int epi, const TcPlan& plan, float* ws, unsigned int* tile_ctr,
+                      cudaStream_t s, bool pdl);
+// out[b, :K] = bf16 RMSNorm(x[b, :K]) * (w [+ 1])
+cudaError_t rms_rows_launch(const uint16_t* x, int x_stride, const uint16_t* w, float eps, int offset, int K, int nb,
+                            uint16_t* out, int out_stride, cudaStream_t s, bool pdl);
+
 // ----------------------------------------------------------------- paged decode attention
 struct AttnArgs {
     const uint16_t* qkv = nullptr;  // [nb, qkv_stride] (q heads, k heads, v heads), pre-RoPE

@@ -299,6 +299,50 @@ const float* rope_table(int dev, int hd, float theta, const void* scv) {
 
 static int grid_for(size_t n) { return (int)std::min<size_t>((n + 255) / 256, 148 * 16); }
 
+// bf16 matmul_t for more than 8 rows of `a` on the tensor cores: chunks of up
+// to 256 rows, each one tcgen05 GEMM launch; split-K scratch from the pool.
+static ti_status matmul_t_tc(const uint16_t* a, const uint16_t* b, uint16_t* c, int M, int N, int K,
+                             cudaStream_t s) {
+    int dev = 0;
+    TI_CUDA(cudaGetDevice(&dev));
+    constexpr size_t kWsCap = 16u << 20;  // floats
+    GemvArgs g;
+    g.W = b;
+    g.N = N;
+    g.K = K;
+    g.nb = std::min(M, 256);
+    g.x = a;
+    g.x_stride = K;
+    g.out = c;
+    g.out_stride = N;
+    TcPlan plan;
+    std::string why;
+    TI_CHECK(tc_plan(g, kEpiStore, dev, kWsCap, &plan, &why), TI_ERR_UNSUPPORTED, "matmul_t: %s", why.c_str());
+    float* ws = nullptr;
+    unsigned int* ctr = nullptr;
+    if (plan.splits > 1) {
+        TI_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), plan.ws_floats * 4 + (size_t)plan.tiles * 4, s));
+        ctr = reinterpret_cast<unsigned int*>(ws + plan.ws_floats);
+        TI_CUDA(cudaMemsetAsync(ctr, 0, (size_t)plan.tiles * 4, s));
+    }
+    cudaError_t err = cudaSuccess;
+    for (int m0 = 0; m0 < M && err == cudaSuccess; m0 += 256) {
+        GemvArgs gc = g;
+        gc.nb = std::min(256, M - m0);
+        gc.x = a + (size_t)m0 * K;
+        gc.out = c + (size_t)m0 * N;
+        TcPlan pc;
+        if (!tc_plan(gc, kEpiStore, dev, plan.ws_floats, &pc, &why)) {
+            err = cudaErrorInvalidValue;
+            break;
+        }
+        err = tc_launch(gc, kEpiStore, pc, ws, ctr, s, false);
+    }
+    if (ws) cudaFreeAsync(ws, s);
+    TI_CHECK(err == cudaSuccess, TI_ERR_CUDA, "matmul_t: %s", cudaGetErrorString(err));
+    return TI_OK;
+}
+
 }  // namespace ti
 
 using namespace ti;
@@ -351,6 +395,8 @@ ti_status ti_op_matmul_t(int dtype, const void* a, const void* b, void* c, int M
                 return TI_OK;
             }
         }
+        if (M > 8 && K % 64 == 0 && ((uintptr_t)a % 16) == 0 && ((uintptr_t)b % 16) == 0)
+            return matmul_t_tc((const uint16_t*)a, (const uint16_t*)b, (uint16_t*)c, M, N, K, s);
         dim3 grid((N + 63) / 64, (M + 63) / 64);
         k_gemm_nt<uint16_t><<<grid, 256, 0, s>>>((const uint16_t*)a, (const uint16_t*)b, (uint16_t*)c, M, N, K);
     } else if (dtype == TI_DTYPE_F32) {

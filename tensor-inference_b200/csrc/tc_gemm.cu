@@ -1,0 +1,702 @@
+// tc_gemm.cu — tensor-core (tcgen05) skinny GEMM for batched decode and prefill.
+//
+// Y[t, n] = sum_k X[t, k] * W[n, k] for up to 256 tokens t: the reference's
+// ops::matmul_t (ops.cu:94-148, cuBLAS GemmEx, fp32 accumulate, bf16 output)
+// for a batch of tokens, with the same fused epilogues as the weight-streaming
+// GEMV (bias, residual add, SwiGLU/GeGLU, LM-head argmax).  Once a decode batch
+// has 16+ tokens the FMA work of a SIMT GEMV outgrows the weight stream; here the
+// 5th-generation tensor cores do it and the kernel stays HBM-bound.
+//
+// Orientation: the weights are the MMA's M side (128 rows per tile, so a tile
+// is a dense 16 KB block per 64-element K step) and the tokens its N side
+// (padded to a multiple of 32; rows past the batch are zero-filled by TMA).
+// D = W_tile (128 x K) * X^T (K x np) accumulates in TMEM, fp32.
+//
+// Structure (one persistent CTA per SM, 192 threads):
+//   warp 0      TMA producer: 2-D tiled bulk-tensor loads (128-byte swizzle) of
+//               the weight tile (L2 evict-first) and the token tile into a
+//               ring of shared-memory stages.  Weight loads of the first ring
+//               are issued before griddepcontrol.wait, overlapping the previous
+//               kernel's tail (weights do not depend on it).
+//   warp 1      allocates TMEM (two accumulators of np columns) and one lane
+//               issues tcgen05.mma (kind::f16, bf16 x bf16 -> fp32, M=128,
+//               N=np, K=16 per instruction, 4 per stage); tcgen05.commit frees
+//               each stage and signals a finished accumulator.
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator (warp w owns TMEM
+//               lanes 32*(w%4)..+31 = 32 weight rows), fused epilogue, stores.
+//               Double-buffered TMEM lets the epilogue of one tile overlap the
+//               main loop of the next.
+// Work units are (row tile, K split).  With more than one split each unit
+// stores its fp32 partial tile; the last unit of a tile (atomic ticket) sums the
+// partials in split order (deterministic) and runs the epilogue.
+//
+// Every mbarrier wait is bounded (2 s): a timeout sets an error bit, the roles
+// stop, the producer waits (bounded) for its copies in flight and TMEM is freed.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "internal.h"
+#include "kernels.h"
+
+namespace ti {
+
+namespace {
+
+constexpr int kTcThreads = 192;
+constexpr int kTcBM = 128;        // weight rows per tile (MMA M)
+constexpr int kTcBK = 64;         // K elements per stage: one 128-byte swizzle row
+constexpr uint32_t kTcABytes = kTcBM * kTcBK * 2;  // 16 KB weight tile per stage
+constexpr int kTcMaxTokens = 256;  // MMA N limit
+constexpr size_t kTcSmemBudget = 220 * 1024;
+
+// ------------------------------------------------------------------ tcgen05 / TMA wrappers
+TI_DEVICE_INLINE void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+TI_DEVICE_INLINE void tma_load_2d_hint(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                       uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+        "{%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+TI_DEVICE_INLINE void tmap_prefetch(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+TI_DEVICE_INLINE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+TI_DEVICE_INLINE void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
+// 128 bytes, 8-row groups 1024 bytes apart (SBO), sm_100 descriptor version 1
+TI_DEVICE_INLINE uint64_t smem_desc_sw128(uint32_t addr) {
+    return (uint64_t)((addr & 0x3FFFFu) >> 4) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+// instruction descriptor, kind::f16: D fp32, A and B bf16, both K-major, M=128, N=n
+__host__ __device__ constexpr uint32_t idesc_bf16(int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTcBM >> 4) << 24);
+}
+TI_DEVICE_INLINE void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n"
+        "}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+TI_DEVICE_INLINE void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+// 32 lanes x 32 consecutive fp32 columns (thread i <- lane base+i)
+TI_DEVICE_INLINE void tmem_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%"
+        "19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+TI_DEVICE_INLINE float tc_act(float g, int act) {
+    if (act == 0) return round_bf(g / (1.0f + expf(-g)));  // ops.cu:326
+    const float c1 = 0.7978845608f, c2 = 0.044715f;        // ops.cu:712-714
+    return round_bf(0.5f * g * (1.0f + tanhf(c1 * (g + c2 * g * g * g))));
+}
+
+}  // namespace
+
+struct TcKernelArgs {
+    int N, K, nb, np;
+    int tiles, splits, kblocks, kb_split, units;
+    int stages;
+    uint32_t stage_bytes, tmem_cols;
+    uint16_t* out;
+    int out_stride;
+    const uint16_t* bias;
+    const uint16_t* resid;
+    int resid_stride;
+    int act;
+    unsigned long long* amax;
+    unsigned int* done;
+    int32_t* out_ids;
+    int32_t* chain_tokens;
+    int32_t* chain_pos;
+    float* logits_f32;
+    float* ws;               // [tiles][splits][np][128] fp32 partials (splits > 1)
+    unsigned int* tile_ctr;  // [tiles], zero; reset by each tile's last unit
+    int* err;
+};
+
+// Shared memory after the stage ring (offsets from the 1024-aligned base).
+struct TcSmem {
+    uint32_t full, empty, tfull, tempty, drain, misc, xch, best, total;
+};
+__host__ __device__ inline TcSmem tc_smem_layout(int stages, uint32_t stage_bytes, int np) {
+    TcSmem L;
+    uint32_t o = (uint32_t)stages * stage_bytes;
+    L.full = o;
+    o += 8u * stages;
+    L.empty = o;
+    o += 8u * stages;
+    L.tfull = o;
+    o += 16;
+    L.tempty = o;
+    o += 16;
+    L.drain = o;
+    o += 8;
+    L.misc = o;  // [0] tmem base, [1] abort flag, [2] split ticket, [3] epilogue stop
+    o += 16;
+    o = (o + 15u) & ~15u;
+    L.xch = o;  // GLU exchange: [2 row groups][32 tokens][32 rows] fp32
+    o += 2 * 32 * 32 * 4;
+    L.best = o;  // LM head: per-token argmax keys of this CTA
+    o += 8u * (uint32_t)np;
+    L.total = o + 1024;  // + alignment slack of the dynamic smem base
+    return L;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    k_tc_gemm(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx, const TcKernelArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const TcSmem L = tc_smem_layout(a.stages, a.stage_bytes, a.np);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.full);
+    uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L.empty);
+    uint64_t* tfull = reinterpret_cast<uint64_t*>(smem + L.tfull);
+    uint64_t* tempty = reinterpret_cast<uint64_t*>(smem + L.tempty);
+    uint64_t* drain = reinterpret_cast<uint64_t*>(smem + L.drain);
+    volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + L.misc);
+    float* xch = reinterpret_cast<float*>(smem + L.xch);
+    unsigned long long* best = reinterpret_cast<unsigned long long*>(smem + L.best);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = a.stages;
+    const int np = a.np;
+    constexpr bool kGlu = EPI == kEpiGlu;
+
+    if (threadIdx.x == 0) {
+        pdl_trigger();
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int j = 0; j < 2; ++j) {
+            mbar_init(&tfull[j], 1);
+            mbar_init(&tempty[j], 4);
+        }
+        mbar_init(drain, 1);
+        misc[1] = 0;
+        fence_barrier_init();
+    }
+    if (EPI == kEpiLmHead)
+        for (int i = threadIdx.x; i < np; i += kTcThreads) best[i] = 0ull;
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32((const void*)&misc[0])),
+                     "r"(a.tmem_cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = misc[0];
+
+    // (tile, k-block) iterations of this CTA in issue order; f returns false to stop
+    auto walk = [&](auto&& f) -> int {
+        int it = 0;
+        for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
+            const int tile = u / a.splits, sp = u % a.splits;
+            const int kb0 = sp * a.kb_split, kb1 = min(a.kblocks, kb0 + a.kb_split);
+            for (int kb = kb0; kb < kb1; ++kb, ++it)
+                if (!f(tile, kb, it)) return it;
+        }
+        return it;
+    };
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            tmap_prefetch(&tmw);
+            tmap_prefetch(&tmx);
+            const uint64_t pol = l2_policy_evict_first();
+            const uint32_t tx = kTcABytes + (uint32_t)np * kTcBK * 2;
+            auto load_w = [&](int tile, int kb, int s) {
+                uint8_t* st = smem + (size_t)s * a.stage_bytes;
+                if (kGlu) {
+                    tma_load_2d_hint(st, &tmw, kb * kTcBK, tile * 64, &full[s], pol);
+                    tma_load_2d_hint(st + kTcABytes / 2, &tmw, kb * kTcBK, a.N + tile * 64, &full[s], pol);
+                } else {
+                    tma_load_2d_hint(st, &tmw, kb * kTcBK, tile * kTcBM, &full[s], pol);
+                }
+            };
+            auto load_x = [&](int kb, int s) {
+                tma_load_2d(smem + (size_t)s * a.stage_bytes + kTcABytes, &tmx, kb * kTcBK, 0, &full[s]);
+            };
+            // 1. weights of the first pass of the ring: they do not depend on the
+            //    previous kernel, so they stream while it finishes
+            const int first = walk([&](int tile, int kb, int it) {
+                if (it >= S) return false;
+                mbar_arrive_expect_tx(&full[it], tx);
+                load_w(tile, kb, it);
+                return true;
+            });
+            // 2. the token tiles of those stages, once the previous kernel is done
+            pdl_wait();
+            walk([&](int, int kb, int it) {
+                if (it >= first) return false;
+                load_x(kb, it);
+                return true;
+            });
+            // 3. steady state
+            int issued = first;
+            walk([&](int tile, int kb, int it) {
+                if (it < first) return true;
+                const int s = it % S;
+                if (misc[1] || !mbar_wait(&empty[s], ((it / S) & 1) ^ 1, a.err, kErrTimeoutEmpty)) {
+                    misc[1] = 1;
+                    return false;
+                }
+                mbar_arrive_expect_tx(&full[s], tx);
+                load_w(tile, kb, s);
+                load_x(kb, s);
+                issued = it + 1;
+                return true;
+            });
+            // copies still in flight land before the CTA exits
+            for (int j = max(0, issued - S); j < issued; ++j)
+                if (!mbar_wait(&full[j % S], (j / S) & 1, a.err, kErrTimeoutFull)) break;
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = idesc_bf16(np);
+            int it = 0, j = 0;
+            bool issued = false;
+            for (int u = blockIdx.x; u < a.units; u += gridDim.x, ++j) {
+                const int sp = u % a.splits;
+                const int kb0 = sp * a.kb_split, kb1 = min(a.kblocks, kb0 + a.kb_split);
+                const int buf = j & 1;
+                if (misc[1] || !mbar_wait(&tempty[buf], ((j >> 1) & 1) ^ 1, a.err, kErrTimeoutEmpty)) {
+                    misc[1] = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(buf * np);
+                bool ok = true;
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                    const int s = it % S;
+                    if (misc[1] || !mbar_wait(&full[s], (it / S) & 1, a.err, kErrTimeoutFull)) {
+                        misc[1] = 1;
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + (size_t)s * a.stage_bytes);
+                    const uint32_t b_addr = a_addr + kTcABytes;
+#pragma unroll
+                    for (int k = 0; k < kTcBK / 16; ++k)
+                        tc_mma(d, smem_desc_sw128(a_addr + k * 32), smem_desc_sw128(b_addr + k * 32), idesc,
+                               (kb > kb0 || k > 0) ? 1u : 0u);
+                    tc_commit(&empty[s]);
+                    issued = true;
+                }
+                if (!ok) break;
+                tc_commit(&tfull[buf]);
+            }
+            // all MMAs retired before TMEM is released
+            if (issued) {
+                tc_commit(drain);
+                mbar_wait(drain, 0, a.err, kErrTimeoutFull);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int q = warp & 3;                 // TMEM lane quarter of this warp
+        const int et = threadIdx.x - 64;        // 0..127 among the epilogue threads
+        const int rl = q * 32 + lane;           // row of the tile (TMEM lane)
+        pdl_wait();  // residual rows are the previous kernel's output
+        int j = 0;
+        for (int u = blockIdx.x; u < a.units; u += gridDim.x, ++j) {
+            const int tile = u / a.splits, sp = u % a.splits;
+            const int buf = j & 1;
+            // one leader waits for the accumulator and the named barrier hands the
+            // outcome to all four warps, so they stop (or go on) together: a
+            // barrier that some warps skip would never complete
+            if (et == 0) {
+                const bool ok = misc[1] == 0 && mbar_wait(&tfull[buf], (j >> 1) & 1, a.err, kErrTimeoutFull);
+                misc[3] = ok ? 0u : 1u;
+                if (!ok) misc[1] = 1;
+            }
+            named_bar(1, 128);
+            if (misc[3]) break;
+            tc_fence_after();
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * np);
+            // row handled by this thread: GLU tiles hold 64 gate rows then the 64 matching up rows
+            const int n = kGlu ? tile * 64 + (rl & 63) : tile * kTcBM + rl;
+            const bool row_ok = n < a.N;
+            const int nchunks = np / 32;
+
+            auto apply = [&](int c, const float* v) {
+                // v[i] = accumulator of (row n, token c*32 + i)
+                if (kGlu) {
+                    float* xq = xch + (size_t)(q & 1) * 32 * 32;
+                    if (q >= 2) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) xq[i * 32 + lane] = round_bf(v[i]);
+                    }
+                    named_bar(1, 128);
+                    if (q < 2 && row_ok) {
+                        for (int i = 0; i < 32; ++i) {
+                            const int b = c * 32 + i;
+                            if (b >= a.nb) break;
+                            const float gv = round_bf(v[i]);
+                            const float uv = xq[i * 32 + lane];
+                            reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + n] = f2bf(tc_act(gv, a.act) * uv);
+                        }
+                    }
+                    named_bar(1, 128);
+                } else if (EPI == kEpiStore) {
+                    if (row_ok) {
+                        const float bv = a.bias ? __uint_as_float((uint32_t)a.bias[n] << 16) : 0.f;
+                        for (int i = 0; i < 32; ++i) {
+                            const int b = c * 32 + i;
+                            if (b >= a.nb) break;
+                            float val = round_bf(v[i]);
+                            if (a.bias) val = round_bf(val + bv);
+                            reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + n] = f2bf(val);
+                        }
+                    }
+                } else if (EPI == kEpiResid) {
+                    if (row_ok) {
+                        for (int i = 0; i < 32; ++i) {
+                            const int b = c * 32 + i;
+                            if (b >= a.nb) break;
+                            const float val = round_bf(v[i]);
+                            const float rr = __uint_as_float((uint32_t)a.resid[(size_t)b * a.resid_stride + n] << 16);
+                            reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + n] = f2bf(rr + val);
+                        }
+                    }
+                } else {  // kEpiLmHead
+                    for (int i = 0; i < 32; ++i) {
+                        const int b = c * 32 + i;
+                        if (b >= a.nb) break;
+                        unsigned long long key = 0ull;
+                        if (row_ok) {
+                            reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + n] = f2bf(v[i]);
+                            if (a.logits_f32) a.logits_f32[(size_t)b * a.out_stride + n] = v[i];
+                            key = argmax_key(v[i], (uint32_t)n);
+                        }
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) {
+                            const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+                            key = other > key ? other : key;
+                        }
+                        if (lane == 0 && key) atomicMax(&best[b], key);
+                    }
+                }
+            };
+
+            if (a.splits == 1) {
+                for (int c = 0; c < nchunks; ++c) {
+                    float v[32];
+                    tmem_ld32(tbase + (uint32_t)(c * 32), v);
+                    if (c == nchunks - 1) {
+                        // accumulator fully read: hand it back to the MMA warp
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[buf]);
+                    }
+                    apply(c, v);
+                }
+            } else {
+                float* wsp = a.ws + ((size_t)tile * a.splits + sp) * (size_t)np * kTcBM;
+                for (int c = 0; c < nchunks; ++c) {
+                    float v[32];
+                    tmem_ld32(tbase + (uint32_t)(c * 32), v);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) __stcg(wsp + (size_t)(c * 32 + i) * kTcBM + rl, v[i]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[buf]);
+                __threadfence();
+                named_bar(1, 128);
+                if (et == 0) misc[2] = atomicAdd(&a.tile_ctr[tile], 1u);
+                named_bar(1, 128);
+                const bool last = misc[2] == (uint32_t)(a.splits - 1);
+                named_bar(1, 128);  // misc[2] is rewritten by the next unit
+                if (last) {
+                    __threadfence();
+                    const float* w0 = a.ws + (size_t)tile * a.splits * (size_t)np * kTcBM;
+                    for (int c = 0; c < nchunks; ++c) {
+                        float v[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+                        for (int s2 = 0; s2 < a.splits; ++s2) {
+                            const float* p = w0 + (size_t)s2 * np * kTcBM;
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) v[i] += __ldcg(p + (size_t)(c * 32 + i) * kTcBM + rl);
+                        }
+                        apply(c, v);
+                    }
+                    if (et == 0) a.tile_ctr[tile] = 0u;
+                }
+            }
+            named_bar(1, 128);  // misc[3] is rewritten for the next unit
+        }
+        if (EPI == kEpiLmHead) {
+            // grid argmax: one 64-bit atomicMax per token per CTA; the last CTA
+            // publishes the ids and re-arms the keys for the next step
+            named_bar(1, 128);
+            for (int b = et; b < a.nb; b += 128)
+                if (best[b]) atomicMax(&a.amax[b], best[b]);
+            __threadfence();
+            named_bar(1, 128);
+            if (et == 0) {
+                const unsigned int ticket = atomicAdd(a.done, 1u);
+                if (ticket == gridDim.x - 1) {
+                    __threadfence();
+                    for (int b = 0; b < a.nb; ++b) {
+                        const unsigned long long key = atomicExch(&a.amax[b], 0ull);
+                        const int32_t id = (int32_t)(~(uint32_t)(key & 0xffffffffull));
+                        a.out_ids[b] = id;
+                        if (a.chain_tokens) a.chain_tokens[b] = id;
+                        if (a.chain_pos) a.chain_pos[b] += 1;
+                    }
+                    atomicExch(a.done, 0u);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols)
+                     : "memory");
+    }
+}
+
+// RMSNorm of whole rows into a bf16 buffer (the tensor-core GEMM reads its
+// operand through TMA, so the norm that the GEMV fuses runs as its own pass):
+// out = bf16(x * rsqrtf(mean(x^2) + eps) * (w [+1])), ops.cu:154-204 / :765-788.
+__global__ void __launch_bounds__(256) k_rms_rows(const uint16_t* x, int x_stride, const uint16_t* w, float eps,
+                                                  int offset, int K, uint16_t* out, int out_stride) {
+    __shared__ float red[8];
+    if (threadIdx.x == 0) pdl_trigger();
+    pdl_wait();
+    const int b = blockIdx.x, tid = threadIdx.x;
+    const uint16_t* xr = x + (size_t)b * x_stride;
+    float ss = 0.f;
+    for (int c = tid * 8; c < K; c += 256 * 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+        const uint32_t* vp = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            ss = fmaf(bf_lo(vp[e]), bf_lo(vp[e]), ss);
+            ss = fmaf(bf_hi(vp[e]), bf_hi(vp[e]), ss);
+        }
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += red[i];
+    const float scale = rsqrtf(tot / (float)K + eps);
+    const float off = offset ? 1.0f : 0.0f;
+    for (int c = tid * 8; c < K; c += 256 * 8) {
+        uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+        const uint4 wn = *reinterpret_cast<const uint4*>(w + c);
+        uint32_t* vp = reinterpret_cast<uint32_t*>(&v);
+        const uint32_t* wp = reinterpret_cast<const uint32_t*>(&wn);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float lo = bf_lo(vp[e]) * scale * (bf_lo(wp[e]) + off);
+            const float hi = bf_hi(vp[e]) * scale * (bf_hi(wp[e]) + off);
+            vp[e] = pack_bf2(lo, hi);
+        }
+        *reinterpret_cast<uint4*>(out + (size_t)b * out_stride + c) = v;
+    }
+}
+
+cudaError_t rms_rows_launch(const uint16_t* x, int x_stride, const uint16_t* w, float eps, int offset, int K, int nb,
+                            uint16_t* out, int out_stride, cudaStream_t s, bool pdl) {
+    if (K % 8 != 0 || nb < 1) return cudaErrorInvalidValue;
+    void* params[] = {&x, &x_stride, &w, &eps, &offset, &K, &out, &out_stride};
+    return launch_pdl(reinterpret_cast<const void*>(&k_rms_rows), dim3(nb), dim3(256), 0, s, params, pdl);
+}
+
+// ------------------------------------------------------------------ host side
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// bf16 [rows, cols] row-major with row pitch `ld` elements; box = 64 columns x box_rows, 128-byte swizzle
+bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {ld * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kTcBK, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+const void* tc_func(int epi) {
+    switch (epi) {
+        case kEpiStore: return reinterpret_cast<const void*>(&k_tc_gemm<kEpiStore>);
+        case kEpiResid: return reinterpret_cast<const void*>(&k_tc_gemm<kEpiResid>);
+        case kEpiGlu: return reinterpret_cast<const void*>(&k_tc_gemm<kEpiGlu>);
+        default: return reinterpret_cast<const void*>(&k_tc_gemm<kEpiLmHead>);
+    }
+}
+
+}  // namespace
+
+bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPlan* p, std::string* why) {
+    if (g.nb < 1 || g.nb > kTcMaxTokens) {
+        if (why) *why = "tc_gemm: batch must be 1..256";
+        return false;
+    }
+    if (g.K % kTcBK != 0 || g.K < kTcBK) {
+        if (why) *why = "tc_gemm: K must be a multiple of 64";
+        return false;
+    }
+    if (epi == kEpiGlu && g.N % 64 != 0) {
+        if (why) *why = "tc_gemm: GLU width must be a multiple of 64";
+        return false;
+    }
+    if (g.norm_w || g.lora.adapter) {
+        if (why) *why = "tc_gemm: RMSNorm prologue and LoRA are applied outside this kernel";
+        return false;
+    }
+    // tokens padded to whole 32-column TMEM loads
+    const int np = (g.nb + 31) / 32 * 32;
+    const int sms = num_sms(device);
+    const int tiles = epi == kEpiGlu ? g.N / 64 : (g.N + kTcBM - 1) / kTcBM;
+    const int kblocks = g.K / kTcBK;
+    // K splits: minimise (waves of units) x (k-blocks per unit); partials must fit the workspace
+    int best_s = 1;
+    long best_cost = -1;
+    for (int s = 1; s <= std::min(16, kblocks); ++s) {
+        const int kbs = (kblocks + s - 1) / s;
+        if ((s - 1) * kbs >= kblocks) continue;  // an empty split
+        if (s > 1 && (size_t)tiles * s * np * kTcBM > ws_floats_cap) break;
+        const long units = (long)tiles * s;
+        const long waves = (units + sms - 1) / sms;
+        const long cost = waves * kbs * 100 + (s > 1 ? 3 * s : 0);
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            best_s = s;
+        }
+    }
+    p->np = np;
+    p->tiles = tiles;
+    p->splits = best_s;
+    p->kblocks = kblocks;
+    p->kb_split = (kblocks + best_s - 1) / best_s;
+    p->units = tiles * best_s;
+    p->grid = std::min(p->units, sms);
+    p->stage_bytes = kTcABytes + (uint32_t)np * kTcBK * 2;
+    const TcSmem L0 = tc_smem_layout(0, p->stage_bytes, np);
+    p->stages = (int)std::min<size_t>(12, (kTcSmemBudget - L0.total) / (p->stage_bytes + 16));
+    if (p->stages < 2) {
+        if (why) *why = "tc_gemm: token tile too large for a two-stage ring";
+        return false;
+    }
+    p->smem = tc_smem_layout(p->stages, p->stage_bytes, np).total;
+    uint32_t cols = 32;
+    while (cols < (uint32_t)(2 * np)) cols <<= 1;
+    p->tmem_cols = cols;
+    p->ws_floats = best_s > 1 ? (size_t)tiles * best_s * np * kTcBM : 0;
+    p->func = tc_func(epi);
+    return true;
+}
+
+cudaError_t tc_launch(const GemvArgs& g, int epi, const TcPlan& p, float* ws, unsigned int* tile_ctr, cudaStream_t s,
+                      bool pdl) {
+    CUtensorMap mw, mx;
+    const uint64_t wrows = epi == kEpiGlu ? 2ull * g.N : (uint64_t)g.N;
+    if (!make_map(&mw, g.W, wrows, g.K, g.K, epi == kEpiGlu ? 64 : kTcBM)) return cudaErrorInvalidValue;
+    if (!make_map(&mx, g.x, g.nb, g.K, g.x_stride, p.np)) return cudaErrorInvalidValue;
+    if (p.splits > 1 && (!ws || !tile_ctr)) return cudaErrorInvalidValue;
+    TcKernelArgs a{};
+    a.N = g.N;
+    a.K = g.K;
+    a.nb = g.nb;
+    a.np = p.np;
+    a.tiles = p.tiles;
+    a.splits = p.splits;
+    a.kblocks = p.kblocks;
+    a.kb_split = p.kb_split;
+    a.units = p.units;
+    a.stages = p.stages;
+    a.stage_bytes = p.stage_bytes;
+    a.tmem_cols = p.tmem_cols;
+    a.out = g.out;
+    a.out_stride = g.out_stride;
+    a.bias = g.bias;
+    a.resid = g.resid;
+    a.resid_stride = g.resid_stride;
+    a.act = g.act;
+    a.amax = g.amax;
+    a.done = g.done;
+    a.out_ids = g.out_ids;
+    a.chain_tokens = g.chain_tokens;
+    a.chain_pos = g.chain_pos;
+    a.logits_f32 = g.logits_f32;
+    a.ws = ws;
+    a.tile_ctr = tile_ctr;
+    a.err = g.err;
+    static std::mutex mu;
+    static bool attr_set[4] = {false, false, false, false};
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!attr_set[epi & 3]) {
+            cudaError_t e = cudaFuncSetAttribute(p.func, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+            if (e != cudaSuccess) return e;
+            attr_set[epi & 3] = true;
+        }
+    }
+    void* params[] = {&mw, &mx, &a};
+    return launch_pdl(p.func, dim3(p.grid), dim3(kTcThreads), p.smem, s, params, pdl);
+}
+
+}  // namespace ti
