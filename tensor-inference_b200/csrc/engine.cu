@@ -99,8 +99,8 @@ struct ti_engine {
     float *part_o = nullptr, *part_ml = nullptr;
     unsigned int* counters = nullptr;
     int attn_splits_n = 1, attn_max_chunk = 0;
-    // tensor-core path (batches of tc_min..256 tokens): RMSNorm'd rows, split-K
-    // partials and per-tile tickets
+    // tensor-core path (batches of tc_min..256 tokens): RMSNorm'd rows, partial
+    // tiles shared between CTAs and their tickets
     int tc_min = 16;
     uint16_t* xn = nullptr;
     float* tc_ws = nullptr;
@@ -334,7 +334,7 @@ ti_status build(ti_engine* e) {
             const int kmax = std::max(H, std::max((int)QW, I));
             TI_CHECK(dalloc_t(e, &e->xn, (size_t)std::min(B, 256) * kmax, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
                      ti_last_error());
-            e->tc_ws_floats = (size_t)8 << 20;  // 32 MB of split-K partials
+            e->tc_ws_floats = (size_t)12 << 20;  // 48 MB: 2 partial tiles per CTA at 256 tokens
             TI_CHECK(dalloc(e, reinterpret_cast<void**>(&e->tc_ws), e->tc_ws_floats * 4, &e->bytes_work) == TI_OK,
                      TI_ERR_OOM, "%s", ti_last_error());
             const size_t ntiles = (size_t)std::max(e->Vl, std::max(2 * I, e->qkv_rows)) / 64 + 64;

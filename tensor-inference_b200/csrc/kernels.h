@@ -104,14 +104,14 @@ cudaError_t gemv_launch(const GemvArgs& a, int epi, const GemvPlan& plan, cudaSt
 // caller normalises rows with rms_rows_launch first); batches of 1..256 tokens.
 struct TcPlan {
     int np = 0;  // tokens padded to a multiple of 32 (MMA N)
-    int tiles = 0, splits = 1, kblocks = 0, kb_split = 0, units = 0, grid = 0, stages = 0;
+    int tiles = 0, kbs = 1, kblocks = 0, kpc = 0, grid = 0, stages = 0;  // kpc: k-blocks per CTA (stream-K)
     uint32_t stage_bytes = 0, tmem_cols = 0;
     size_t smem = 0;
-    size_t ws_floats = 0;  // split-K partial workspace this launch needs
+    size_t ws_floats = 0;  // partial-tile workspace this launch needs
     const void* func = nullptr;
 };
 bool tc_plan(const GemvArgs& a, int epi, int device, size_t ws_floats_cap, TcPlan* plan, std::string* why);
-// ws: >= plan.ws_floats floats; tile_ctr: >= plan.tiles zeroed counters (both only when splits > 1)
+// ws: >= plan.ws_floats floats; tile_ctr: >= plan.tiles zeroed counters
 cudaError_t tc_launch(const GemvArgs& a, int epi, const TcPlan& plan, float* ws, unsigned int* tile_ctr,
                       cudaStream_t s, bool pdl);
 // out[b, :K] = bf16 RMSNorm(x[b, :K]) * (w [+ 1])

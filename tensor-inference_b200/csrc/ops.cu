@@ -3,8 +3,9 @@
 // These back the drop-in tensor::backend shim: the reference's unchanged model
 // code (llama_model.cpp etc.) calls ops::* one op at a time, and each call
 // lands here.  Rounding points and formulas follow src/backend/cuda/ops.cu of
-// the reference, cited per kernel.  Matmuls with few rows (decode) run on the
-// weight-streaming GEMV; larger ones on a tiled fp32-accumulate GEMM.
+// the reference, cited per kernel.  bf16 matmuls with few rows (decode) run on
+// the weight-streaming GEMV, larger ones on the tcgen05 tensor-core GEMM; fp32
+// and unaligned shapes on a tiled fp32-accumulate SIMT GEMM.
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -300,7 +301,7 @@ const float* rope_table(int dev, int hd, float theta, const void* scv) {
 static int grid_for(size_t n) { return (int)std::min<size_t>((n + 255) / 256, 148 * 16); }
 
 // bf16 matmul_t for more than 8 rows of `a` on the tensor cores: chunks of up
-// to 256 rows, each one tcgen05 GEMM launch; split-K scratch from the pool.
+// to 256 rows, each one tcgen05 GEMM launch; partial-tile scratch from the pool.
 static ti_status matmul_t_tc(const uint16_t* a, const uint16_t* b, uint16_t* c, int M, int N, int K,
                              cudaStream_t s) {
     int dev = 0;
@@ -319,12 +320,9 @@ static ti_status matmul_t_tc(const uint16_t* a, const uint16_t* b, uint16_t* c, 
     std::string why;
     TI_CHECK(tc_plan(g, kEpiStore, dev, kWsCap, &plan, &why), TI_ERR_UNSUPPORTED, "matmul_t: %s", why.c_str());
     float* ws = nullptr;
-    unsigned int* ctr = nullptr;
-    if (plan.splits > 1) {
-        TI_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), plan.ws_floats * 4 + (size_t)plan.tiles * 4, s));
-        ctr = reinterpret_cast<unsigned int*>(ws + plan.ws_floats);
-        TI_CUDA(cudaMemsetAsync(ctr, 0, (size_t)plan.tiles * 4, s));
-    }
+    TI_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), plan.ws_floats * 4 + (size_t)plan.tiles * 4, s));
+    unsigned int* ctr = reinterpret_cast<unsigned int*>(ws + plan.ws_floats);
+    TI_CUDA(cudaMemsetAsync(ctr, 0, (size_t)plan.tiles * 4, s));
     cudaError_t err = cudaSuccess;
     for (int m0 = 0; m0 < M && err == cudaSuccess; m0 += 256) {
         GemvArgs gc = g;

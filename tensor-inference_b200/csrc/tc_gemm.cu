@@ -26,15 +26,19 @@
 //               lanes 32*(w%4)..+31 = 32 weight rows), fused epilogue, stores.
 //               Double-buffered TMEM lets the epilogue of one tile overlap the
 //               main loop of the next.
-// Work units are (row tile, K split).  With more than one split each unit
-// stores its fp32 partial tile; the last unit of a tile (atomic ticket) sums the
-// partials in split order (deterministic) and runs the epilogue.
+// Work split (stream-K): the row tiles x k-blocks of the GEMM, tile-major, are
+// cut into equal contiguous ranges, one per CTA, so every SM streams the same
+// number of weight bytes whatever the tile count.  A tile inside one range is
+// finished by its CTA; a tile cut between CTAs has each part's fp32 partial
+// stored, and the last part to finish (atomic ticket) sums them in CTA order
+// (deterministic) and runs the epilogue.
 //
 // Every mbarrier wait is bounded (2 s): a timeout sets an error bit, the roles
 // stop, the producer waits (bounded) for its copies in flight and TMEM is freed.
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -47,8 +51,8 @@ namespace {
 
 constexpr int kTcThreads = 192;
 constexpr int kTcBM = 128;        // weight rows per tile (MMA M)
-constexpr int kTcBK = 64;         // K elements per stage: one 128-byte swizzle row
-constexpr uint32_t kTcABytes = kTcBM * kTcBK * 2;  // 16 KB weight tile per stage
+constexpr int kTcBK = 64;         // K elements per swizzle atom: one 128-byte row
+constexpr uint32_t kTcABytes = kTcBM * kTcBK * 2;  // 16 KB weight atom (128 rows x 64 K)
 constexpr int kTcMaxTokens = 256;  // MMA N limit
 constexpr size_t kTcSmemBudget = 220 * 1024;
 
@@ -124,7 +128,9 @@ TI_DEVICE_INLINE float tc_act(float g, int act) {
 
 struct TcKernelArgs {
     int N, K, nb, np;
-    int tiles, splits, kblocks, kb_split, units;
+    int tiles, kblocks;  // row tiles; k-blocks per tile (a k-block = kbs atoms = kbs * 64 K elements)
+    int kbs;
+    int kpc;             // k-blocks per CTA: CTA c owns global k-blocks [c * kpc, (c + 1) * kpc)
     int stages;
     uint32_t stage_bytes, tmem_cols;
     uint16_t* out;
@@ -139,8 +145,8 @@ struct TcKernelArgs {
     int32_t* chain_tokens;
     int32_t* chain_pos;
     float* logits_f32;
-    float* ws;               // [tiles][splits][np][128] fp32 partials (splits > 1)
-    unsigned int* tile_ctr;  // [tiles], zero; reset by each tile's last unit
+    float* ws;               // [grid][2][np][128] fp32 partials of tiles shared between CTAs
+    unsigned int* tile_ctr;  // [tiles], zero; reset by each shared tile's last unit
     int* err;
 };
 
@@ -220,15 +226,36 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_fence_after();
     const uint32_t tmem = misc[0];
 
+    // Stream-K: the tiles x kblocks k-blocks, tile-major, are cut into equal
+    // contiguous ranges, one per CTA.  A unit is the part of one tile inside the
+    // range: whole tiles are finished by their CTA, a tile cut between CTAs is
+    // summed by the last of them to finish (ticket), in CTA order.
+    const long total = (long)a.tiles * a.kblocks;
+    const long g_begin = (long)blockIdx.x * a.kpc, g_end = min(total, g_begin + a.kpc);
+    // f(tile, k0, k1, first_unit) for each unit of this CTA; false stops
+    auto units = [&](auto&& f) {
+        bool first = true;
+        for (long g = g_begin; g < g_end;) {
+            const int tile = (int)(g / a.kblocks), k0 = (int)(g % a.kblocks);
+            const int k1 = (int)min((long)a.kblocks, k0 + (g_end - g));
+            if (!f(tile, k0, k1, first)) return;
+            first = false;
+            g += k1 - k0;
+        }
+    };
     // (tile, k-block) iterations of this CTA in issue order; f returns false to stop
     auto walk = [&](auto&& f) -> int {
         int it = 0;
-        for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
-            const int tile = u / a.splits, sp = u % a.splits;
-            const int kb0 = sp * a.kb_split, kb1 = min(a.kblocks, kb0 + a.kb_split);
-            for (int kb = kb0; kb < kb1; ++kb, ++it)
-                if (!f(tile, kb, it)) return it;
-        }
+        bool go = true;
+        units([&](int tile, int k0, int k1, bool) {
+            for (int kb = k0; kb < k1; ++kb, ++it)
+                if (!f(tile, kb, it)) {
+                    go = false;
+                    return false;
+                }
+            return true;
+        });
+        (void)go;
         return it;
     };
 
@@ -238,18 +265,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tmap_prefetch(&tmw);
             tmap_prefetch(&tmx);
             const uint64_t pol = l2_policy_evict_first();
-            const uint32_t tx = kTcABytes + (uint32_t)np * kTcBK * 2;
+            const int kbs = a.kbs;
+            const uint32_t xatom = (uint32_t)np * kTcBK * 2;
+            const uint32_t tx = (uint32_t)kbs * (kTcABytes + xatom);
             auto load_w = [&](int tile, int kb, int s) {
+                // kbs adjacent 64-column atoms of each weight row back to back, so
+                // DRAM sees kbs * 128 contiguous bytes per row
                 uint8_t* st = smem + (size_t)s * a.stage_bytes;
-                if (kGlu) {
-                    tma_load_2d_hint(st, &tmw, kb * kTcBK, tile * 64, &full[s], pol);
-                    tma_load_2d_hint(st + kTcABytes / 2, &tmw, kb * kTcBK, a.N + tile * 64, &full[s], pol);
-                } else {
-                    tma_load_2d_hint(st, &tmw, kb * kTcBK, tile * kTcBM, &full[s], pol);
+                for (int j = 0; j < kbs; ++j) {
+                    const int x = (kb * kbs + j) * kTcBK;
+                    uint8_t* at = st + (size_t)j * kTcABytes;
+                    if (kGlu) {
+                        tma_load_2d_hint(at, &tmw, x, tile * 64, &full[s], pol);
+                        tma_load_2d_hint(at + kTcABytes / 2, &tmw, x, a.N + tile * 64, &full[s], pol);
+                    } else {
+                        tma_load_2d_hint(at, &tmw, x, tile * kTcBM, &full[s], pol);
+                    }
                 }
             };
             auto load_x = [&](int kb, int s) {
-                tma_load_2d(smem + (size_t)s * a.stage_bytes + kTcABytes, &tmx, kb * kTcBK, 0, &full[s]);
+                uint8_t* xt = smem + (size_t)s * a.stage_bytes + (size_t)kbs * kTcABytes;
+                for (int j = 0; j < kbs; ++j)
+                    tma_load_2d(xt + (size_t)j * xatom, &tmx, (kb * kbs + j) * kTcBK, 0, &full[s]);
             };
             // 1. weights of the first pass of the ring: they do not depend on the
             //    previous kernel, so they stream while it finishes
@@ -291,37 +328,36 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint32_t idesc = idesc_bf16(np);
             int it = 0, j = 0;
             bool issued = false;
-            for (int u = blockIdx.x; u < a.units; u += gridDim.x, ++j) {
-                const int sp = u % a.splits;
-                const int kb0 = sp * a.kb_split, kb1 = min(a.kblocks, kb0 + a.kb_split);
+            units([&](int, int kb0, int kb1, bool) {
                 const int buf = j & 1;
                 if (misc[1] || !mbar_wait(&tempty[buf], ((j >> 1) & 1) ^ 1, a.err, kErrTimeoutEmpty)) {
                     misc[1] = 1;
-                    break;
+                    return false;
                 }
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)(buf * np);
-                bool ok = true;
                 for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % S;
                     if (misc[1] || !mbar_wait(&full[s], (it / S) & 1, a.err, kErrTimeoutFull)) {
                         misc[1] = 1;
-                        ok = false;
-                        break;
+                        return false;
                     }
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(smem + (size_t)s * a.stage_bytes);
-                    const uint32_t b_addr = a_addr + kTcABytes;
+                    const uint32_t b_addr = a_addr + (uint32_t)a.kbs * kTcABytes;
+                    for (int jj = 0; jj < a.kbs; ++jj)
 #pragma unroll
-                    for (int k = 0; k < kTcBK / 16; ++k)
-                        tc_mma(d, smem_desc_sw128(a_addr + k * 32), smem_desc_sw128(b_addr + k * 32), idesc,
-                               (kb > kb0 || k > 0) ? 1u : 0u);
+                        for (int k = 0; k < kTcBK / 16; ++k)
+                            tc_mma(d, smem_desc_sw128(a_addr + jj * kTcABytes + k * 32),
+                                   smem_desc_sw128(b_addr + jj * (uint32_t)np * kTcBK * 2 + k * 32), idesc,
+                                   (kb > kb0 || jj > 0 || k > 0) ? 1u : 0u);
                     tc_commit(&empty[s]);
                     issued = true;
                 }
-                if (!ok) break;
                 tc_commit(&tfull[buf]);
-            }
+                ++j;
+                return true;
+            });
             // all MMAs retired before TMEM is released
             if (issued) {
                 tc_commit(drain);
@@ -335,8 +371,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int rl = q * 32 + lane;           // row of the tile (TMEM lane)
         pdl_wait();  // residual rows are the previous kernel's output
         int j = 0;
-        for (int u = blockIdx.x; u < a.units; u += gridDim.x, ++j) {
-            const int tile = u / a.splits, sp = u % a.splits;
+        units([&](int tile, int, int, bool first) {
             const int buf = j & 1;
             // one leader waits for the accumulator and the named barrier hands the
             // outcome to all four warps, so they stop (or go on) together: a
@@ -347,7 +382,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (!ok) misc[1] = 1;
             }
             named_bar(1, 128);
-            if (misc[3]) break;
+            if (misc[3]) return false;
             tc_fence_after();
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * np);
             // row handled by this thread: GLU tiles hold 64 gate rows then the 64 matching up rows
@@ -415,7 +450,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             };
 
-            if (a.splits == 1) {
+            // CTAs whose k-block ranges meet this tile
+            const long tg0 = (long)tile * a.kblocks;
+            const int c_lo = (int)(tg0 / a.kpc), c_hi = (int)((tg0 + a.kblocks - 1) / a.kpc);
+            if (c_lo == c_hi) {
                 for (int c = 0; c < nchunks; ++c) {
                     float v[32];
                     tmem_ld32(tbase + (uint32_t)(c * 32), v);
@@ -428,7 +466,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     apply(c, v);
                 }
             } else {
-                float* wsp = a.ws + ((size_t)tile * a.splits + sp) * (size_t)np * kTcBM;
+                // partial slot: 2 per CTA (its first and its last unit may be cut)
+                float* wsp = a.ws + ((size_t)blockIdx.x * 2 + (first ? 0 : 1)) * (size_t)np * kTcBM;
                 for (int c = 0; c < nchunks; ++c) {
                     float v[32];
                     tmem_ld32(tbase + (uint32_t)(c * 32), v);
@@ -442,17 +481,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 named_bar(1, 128);
                 if (et == 0) misc[2] = atomicAdd(&a.tile_ctr[tile], 1u);
                 named_bar(1, 128);
-                const bool last = misc[2] == (uint32_t)(a.splits - 1);
+                const bool last = misc[2] == (uint32_t)(c_hi - c_lo);
                 named_bar(1, 128);  // misc[2] is rewritten by the next unit
                 if (last) {
                     __threadfence();
-                    const float* w0 = a.ws + (size_t)tile * a.splits * (size_t)np * kTcBM;
                     for (int c = 0; c < nchunks; ++c) {
                         float v[32];
 #pragma unroll
                         for (int i = 0; i < 32; ++i) v[i] = 0.f;
-                        for (int s2 = 0; s2 < a.splits; ++s2) {
-                            const float* p = w0 + (size_t)s2 * np * kTcBM;
+                        for (int cc = c_lo; cc <= c_hi; ++cc) {
+                            // this tile is CTA cc's first unit unless cc started in an earlier tile
+                            const bool cc_first = (int)(((long)cc * a.kpc) / a.kblocks) == tile;
+                            const float* p = a.ws + ((size_t)cc * 2 + (cc_first ? 0 : 1)) * (size_t)np * kTcBM;
 #pragma unroll
                             for (int i = 0; i < 32; ++i) v[i] += __ldcg(p + (size_t)(c * 32 + i) * kTcBM + rl);
                         }
@@ -462,7 +502,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
             named_bar(1, 128);  // misc[3] is rewritten for the next unit
-        }
+            ++j;
+            return true;
+        });
         if (EPI == kEpiLmHead) {
             // grid argmax: one 64-bit atomicMax per token per CTA; the last CTA
             // publishes the ids and re-arms the keys for the next step
@@ -595,7 +637,7 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
         if (why) *why = "tc_gemm: batch must be 1..256";
         return false;
     }
-    if (g.K % kTcBK != 0 || g.K < kTcBK) {
+    if (g.K % kTcBK != 0 || g.K < kTcBK) {  // whole 64-element atoms
         if (why) *why = "tc_gemm: K must be a multiple of 64";
         return false;
     }
@@ -611,31 +653,45 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
     const int np = (g.nb + 31) / 32 * 32;
     const int sms = num_sms(device);
     const int tiles = epi == kEpiGlu ? g.N / 64 : (g.N + kTcBM - 1) / kTcBM;
-    const int kblocks = g.K / kTcBK;
-    // K splits: minimise (waves of units) x (k-blocks per unit); partials must fit the workspace
-    int best_s = 1;
-    long best_cost = -1;
-    for (int s = 1; s <= std::min(16, kblocks); ++s) {
-        const int kbs = (kblocks + s - 1) / s;
-        if ((s - 1) * kbs >= kblocks) continue;  // an empty split
-        if (s > 1 && (size_t)tiles * s * np * kTcBM > ws_floats_cap) break;
-        const long units = (long)tiles * s;
-        const long waves = (units + sms - 1) / sms;
-        const long cost = waves * kbs * 100 + (s > 1 ? 3 * s : 0);
-        if (best_cost < 0 || cost < best_cost) {
+    const int atoms = g.K / kTcBK;
+    // atoms per stage: the widest of 4/2/1 that divides K and leaves two stages
+    const char* env = std::getenv("TI_TC_KBS");
+    int kbs_max = env ? std::max(1, std::min(8, std::atoi(env))) : 4;
+    const uint32_t xatom = (uint32_t)np * kTcBK * 2;
+    const TcSmem L0 = tc_smem_layout(0, 0, np);
+    while (kbs_max > 1 && 2 * ((size_t)kbs_max * (kTcABytes + xatom) + 16) > kTcSmemBudget - L0.total) kbs_max /= 2;
+    const int kbs = kbs_max;
+    (void)kbs;
+    // stream-K: equal contiguous ranges of the tiles x k-blocks space, one per
+    // CTA; the atoms per stage (4, 2 or 1) that give the shortest range, in
+    // atoms, wins, with a small bonus for wider (DRAM-friendlier) stages
+    int best_kbs = 0, best_kpc = 0;
+    double best_cost = 0;
+    for (int kb = kbs_max; kb >= 1; kb /= 2) {
+        if (atoms % kb != 0) continue;
+        const long total = (long)tiles * (atoms / kb);
+        const int kpc = (int)((total + sms - 1) / sms);
+        const double cost = (double)kpc * kb * (kb >= 4 ? 1.0 : kb == 2 ? 1.03 : 1.10);
+        if (best_kbs == 0 || cost < best_cost) {
             best_cost = cost;
-            best_s = s;
+            best_kbs = kb;
+            best_kpc = kpc;
         }
     }
+    const int kblocks = atoms / best_kbs;
+    const long total = (long)tiles * kblocks;
     p->np = np;
     p->tiles = tiles;
-    p->splits = best_s;
+    p->kbs = best_kbs;
     p->kblocks = kblocks;
-    p->kb_split = (kblocks + best_s - 1) / best_s;
-    p->units = tiles * best_s;
-    p->grid = std::min(p->units, sms);
-    p->stage_bytes = kTcABytes + (uint32_t)np * kTcBK * 2;
-    const TcSmem L0 = tc_smem_layout(0, p->stage_bytes, np);
+    p->kpc = best_kpc;
+    p->grid = (int)((total + best_kpc - 1) / best_kpc);
+    p->ws_floats = (size_t)p->grid * 2 * np * kTcBM;
+    if (p->ws_floats > ws_floats_cap) {
+        if (why) *why = "tc_gemm: split workspace too small for this batch";
+        return false;
+    }
+    p->stage_bytes = (uint32_t)best_kbs * (kTcABytes + xatom);
     p->stages = (int)std::min<size_t>(12, (kTcSmemBudget - L0.total) / (p->stage_bytes + 16));
     if (p->stages < 2) {
         if (why) *why = "tc_gemm: token tile too large for a two-stage ring";
@@ -645,7 +701,6 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
     uint32_t cols = 32;
     while (cols < (uint32_t)(2 * np)) cols <<= 1;
     p->tmem_cols = cols;
-    p->ws_floats = best_s > 1 ? (size_t)tiles * best_s * np * kTcBM : 0;
     p->func = tc_func(epi);
     return true;
 }
@@ -656,17 +711,16 @@ cudaError_t tc_launch(const GemvArgs& g, int epi, const TcPlan& p, float* ws, un
     const uint64_t wrows = epi == kEpiGlu ? 2ull * g.N : (uint64_t)g.N;
     if (!make_map(&mw, g.W, wrows, g.K, g.K, epi == kEpiGlu ? 64 : kTcBM)) return cudaErrorInvalidValue;
     if (!make_map(&mx, g.x, g.nb, g.K, g.x_stride, p.np)) return cudaErrorInvalidValue;
-    if (p.splits > 1 && (!ws || !tile_ctr)) return cudaErrorInvalidValue;
+    if (!ws || !tile_ctr) return cudaErrorInvalidValue;
     TcKernelArgs a{};
     a.N = g.N;
     a.K = g.K;
     a.nb = g.nb;
     a.np = p.np;
     a.tiles = p.tiles;
-    a.splits = p.splits;
     a.kblocks = p.kblocks;
-    a.kb_split = p.kb_split;
-    a.units = p.units;
+    a.kbs = p.kbs;
+    a.kpc = p.kpc;
     a.stages = p.stages;
     a.stage_bytes = p.stage_bytes;
     a.tmem_cols = p.tmem_cols;
