@@ -8,129 +8,145 @@
 //                                             loop, softmax)
 // Grid (split, kv head, token): each CTA takes one kv head and all q heads of
 // its GQA group (q head g reads kv head g / group, ops.cu:470), so a K/V row is
-// read once per group; the context [lo, pos] is cut into n_splits ranges
+// read once per group; the context is cut into page-aligned ranges
 // ("flash-decoding") whose partial (max, sum, unnormalised output) are merged
 // by the last CTA to finish (atomic ticket), with no second launch.
 //
-// Latency structure: cached K/V rows (positions < pos) were written by earlier
-// steps, so each CTA bulk-copies its page spans (16 tokens x head_dim bf16 are
-// contiguous per kv head) into shared memory BEFORE griddepcontrol.wait; only
-// the new token's q/k/v come from the previous kernel.
-// Arithmetic follows the reference: RoPE in fp32 rounded to bf16,
-// score = scale * dot(q, k) in fp32, exp-normalised fp32 softmax, fp32 P.V,
-// bf16 output.
-#include "common.cuh"
-#include "kernels.h"
-
+// Data movement: a page holds 16 tokens x head_dim bf16 of one kv head,
+// contiguous.  Each CTA loads its pages with 2-D TMA boxes (16 rows x 64 dims,
+// 128-byte swizzle) BEFORE griddepcontrol.wait: cached rows were written by
+// earlier steps, only the new token's q/k/v come from the previous kernel.
+// The swizzle makes both the ldmatrix reads of K and the row reads of V free
+// of shared-memory bank conflicts.
+//
+// Arithmetic follows the reference: RoPE in fp32 rounded to bf16; scores
+// q.k with bf16 operands and fp32 accumulation (on the tensor cores: mma.sync
+// m16n8k16, the group's q heads padded to 16 rows; bf16 x bf16 products are
+// exact in fp32), times 1/sqrt(head_dim); exp-normalised fp32 softmax; fp32
+// P.V on the CUDA cores; bf16 output.
 #include <algorithm>
 #include <cstdlib>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
 
 namespace ti {
 
 constexpr int kAttnThreads = 128;
 constexpr int kAttnMaxGroup = 16;
 constexpr int kPage = 16;
-constexpr int kAttnChunkCap = 64;  // tokens per CTA (shared-memory K/V tiles)
+constexpr int kAttnMaxPages = 8;  // pages per split (128 tokens) the shared-memory tiles hold
 
 struct AttnSmem {
-    uint32_t q, k, v, ml, sc, kbuf, vbuf, bar, total;
+    uint32_t kt, vt, qf, kn, vn, ml, sc, mw, bar, total;
 };
 
-// sc_floats: floats reserved for the score area (also reused by the token-group
-// fold and by the split merge)
-__host__ __device__ inline AttnSmem attn_layout(int G, int HD, int max_chunk, int sc_floats) {
+// C: tokens per split (pages x 16); offsets from a 1024-byte aligned base
+__host__ __device__ inline AttnSmem attn_layout(int G, int HD, int C, int n_splits) {
     AttnSmem L;
     uint32_t o = 0;
-    L.q = o;
-    o += G * HD * 4;
-    L.k = o;
+    L.kt = o;  // K tile [HD/64][C][64] bf16, rows 128-byte swizzled
+    o += (uint32_t)C * HD * 2;
+    L.vt = o;
+    o += (uint32_t)C * HD * 2;
+    L.qf = o;  // q heads after RoPE (bf16 values as fp32) [G][HD]
+    o += (uint32_t)G * HD * 4;
+    L.kn = o;  // new token's k after RoPE, and v
     o += HD * 4;
-    L.v = o;
+    L.vn = o;
     o += HD * 4;
     L.ml = o;
     o += 2 * kAttnMaxGroup * 4;
-    L.sc = o;
-    o += sc_floats * 4;
-    o = (o + 127u) & ~127u;
-    L.kbuf = o;
-    o += max_chunk * HD * 2;
-    L.vbuf = o;
-    o += max_chunk * HD * 2;
+    L.sc = o;  // scores, then probabilities [G][C]
+    o += (uint32_t)G * C * 4;
+    L.mw = o;  // split merge: weights and sums [2][n_splits][G]
+    o += 2u * n_splits * G * 4;
+    o = (o + 15u) & ~15u;
     L.bar = o;
     o += 16;
-    L.total = o;
+    L.total = o + 1024;
     return L;
 }
 
-__host__ __device__ inline int attn_sc_floats(int G, int HD, int max_chunk, int n_splits) {
-    const int TG = HD >= kAttnThreads ? 1 : kAttnThreads / HD;
-    int f = G * max_chunk;
-    if ((TG - 1) * G * HD > f) f = (TG - 1) * G * HD;
-    if (n_splits * G > f) f = n_splits * G;
-    return f;
+TI_DEVICE_INLINE void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+// D(16x8 fp32) += A(16x16 bf16, row) * B(16x8 bf16, col)
+TI_DEVICE_INLINE void mma_16816_bf16(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// byte offset of element (row, d) in a [HD/64][C][64] bf16 tile with 128-byte swizzled rows
+TI_DEVICE_INLINE uint32_t tile_off(int C, int row, int d) {
+    const int hh = d >> 6, cc = (d & 63) >> 3;
+    return (uint32_t)(hh * C + row) * 128u + (uint32_t)((cc ^ (row & 7)) << 4) + (uint32_t)((d & 7) << 1);
 }
 
-template <int HD>
-__global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
+// GP: the GQA group size G rounded up to a power of two (loop bound; heads >= G idle)
+template <int HD, int GP>
+__global__ void __launch_bounds__(kAttnThreads)
+    k_attn_decode(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, const AttnArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     constexpr int HALF = HD / 2;
-    constexpr int DPL = HD / 32;  // dims per lane in the score loop
+    constexpr int NH = HD / 64;  // 64-dim boxes per row
+    constexpr int KS = HD / 16;  // mma k-steps
     const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = a.nq / a.nkv;
-    const AttnSmem L = attn_layout(G, HD, a.max_chunk, attn_sc_floats(G, HD, a.max_chunk, a.n_splits));
-    float* qs = reinterpret_cast<float*>(smem + L.q);
-    float* ks = reinterpret_cast<float*>(smem + L.k);
-    float* vs = reinterpret_cast<float*>(smem + L.v);
+    const int C = a.max_chunk;
+    const AttnSmem L = attn_layout(G, HD, C, a.n_splits);
+    uint8_t* kt = smem + L.kt;
+    uint8_t* vt = smem + L.vt;
+    float* qf = reinterpret_cast<float*>(smem + L.qf);
+    float* kn = reinterpret_cast<float*>(smem + L.kn);
+    float* vn = reinterpret_cast<float*>(smem + L.vn);
     float* ml = reinterpret_cast<float*>(smem + L.ml);
     float* sc = reinterpret_cast<float*>(smem + L.sc);
-    uint16_t* kbuf = reinterpret_cast<uint16_t*>(smem + L.kbuf);
-    uint16_t* vbuf = reinterpret_cast<uint16_t*>(smem + L.vbuf);
+    float* mw = reinterpret_cast<float*>(smem + L.mw);
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);
     __shared__ int s_last;
 
-    // ---- before the dependency wait: state of earlier steps only
+    // ---- this CTA's pages [pg0, pg1) of the attended range [lo, pos]
     const int pos = a.pos[b];
     const int* pt = a.page_table + (size_t)a.seq[b] * a.pt_stride;
     const int L1 = pos + 1;
     const int window = a.window ? *a.window : a.window_const;
     const int lo = window > 0 ? max(0, pos - window + 1) : 0;
-    const int span = L1 - lo;
-    const int chunk = (span + a.n_splits - 1) / a.n_splits;
-    const int t0 = lo + split * chunk;
-    int t1 = min(L1, t0 + chunk);
-    if (t1 - t0 > a.max_chunk) {  // host sizes n_splits so this cannot happen; never overrun smem
-        if (tid == 0 && a.err) atomicOr(a.err, kErrBadIndex);
-        t1 = t0 + a.max_chunk;
-    }
-    const int n = max(0, t1 - t0);
-    const int old_end = min(t1, pos);  // cached tokens [t0, old_end)
+    const int pps = C / kPage;
+    const int pg0 = lo / kPage + split * pps;
+    const int pg1 = min((L1 + kPage - 1) / kPage, pg0 + pps);
+    const int t0 = pg0 * kPage;                    // token of tile row 0
+    const int n_rows = max(0, pg1 - pg0) * kPage;  // tile rows loaded
+    const int vlo = max(lo, t0) - t0, vhi = min(L1, t0 + n_rows) - t0;  // valid rows [vlo, vhi)
+
+    // ---- before the dependency wait: cached pages (earlier steps' state only)
     if (tid == 0) {
         mbar_init(bar, 1);
         fence_barrier_init();
         bool ok = true;
-        uint32_t bytes = 0;
-        for (int j = t0; j < old_end;) {
-            const int p = j / kPage, j_end = min(old_end, (p + 1) * kPage);
+        for (int p = pg0; p < pg1; ++p) {
             const int page = pt[p];
-            if (page < 0 || page >= a.n_pages) {
-                ok = false;
-                break;
-            }
-            bytes += (uint32_t)(j_end - j) * HD * 2 * 2;
-            j = j_end;
+            if (page < 0 || page >= a.n_pages) ok = false;
         }
         if (!ok && a.err) atomicOr(a.err, kErrBadIndex);
-        mbar_arrive_expect_tx(bar, ok ? bytes : 0u);
-        if (ok)
-            for (int j = t0; j < old_end;) {
-                const int p = j / kPage, j_end = min(old_end, (p + 1) * kPage);
-                const size_t src = (((size_t)pt[p] * a.nkv + h) * kPage + (j % kPage)) * HD;
-                const uint32_t nbytes = (uint32_t)(j_end - j) * HD * 2;
-                bulk_g2s_plain(kbuf + (size_t)(j - t0) * HD, a.kc + src, nbytes, bar);
-                bulk_g2s_plain(vbuf + (size_t)(j - t0) * HD, a.vc + src, nbytes, bar);
-                j = j_end;
+        const int npg = ok ? max(0, pg1 - pg0) : 0;
+        mbar_arrive_expect_tx(bar, (uint32_t)npg * 2u * NH * kPage * 128u);
+        for (int p = 0; p < npg; ++p) {
+            const int row = (pt[pg0 + p] * a.nkv + h) * kPage;
+#pragma unroll
+            for (int hh = 0; hh < NH; ++hh) {
+                const uint32_t off = (uint32_t)(hh * C + p * kPage) * 128u;
+                tma_load_2d(kt + off, &tk, hh * 64, row, bar);
+                tma_load_2d(vt + off, &tv, hh * 64, row, bar);
             }
+        }
         pdl_trigger();
     }
 
@@ -145,69 +161,84 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnArgs a) 
         const float x1 = __uint_as_float((uint32_t)src[i + HALF] << 16);
         const float ang = (float)pos * a.freqs[i];
         const float c = cosf(ang), s = sinf(ang);
-        float* dst = hh < G ? qs + hh * HD : ks;
+        float* dst = hh < G ? qf + hh * HD : kn;
         dst[i] = round_bf(x0 * c - x1 * s);
         dst[i + HALF] = round_bf(x0 * s + x1 * c);
     }
     for (int d = tid; d < HD; d += kAttnThreads)
-        vs[d] = __uint_as_float((uint32_t)row[(size_t)(a.nq + a.nkv + h) * HD + d] << 16);
+        vn[d] = __uint_as_float((uint32_t)row[(size_t)(a.nq + a.nkv + h) * HD + d] << 16);
     __syncthreads();
 
-    // ---- the CTA whose range holds `pos` appends the new K/V row to its page
-    if (pos >= t0 && pos < t1) {
+    // ---- the tiles are in; the CTA holding `pos` puts the new K/V row into its
+    //      tile and appends it to its page
+    mbar_wait(bar, 0, a.err, kErrTimeoutFull);
+    if (pos >= t0 && pos < t0 + n_rows) {
+        const int r = pos - t0;
+        for (int d = tid; d < HD; d += kAttnThreads) {
+            const uint32_t off = tile_off(C, r, d);
+            *reinterpret_cast<bf16*>(kt + off) = f2bf(kn[d]);
+            *reinterpret_cast<bf16*>(vt + off) = f2bf(vn[d]);
+        }
         const int page = pt[pos / kPage];
         if (page >= 0 && page < a.n_pages) {
             const size_t off = (((size_t)page * a.nkv + h) * kPage + (pos % kPage)) * HD;
             for (int d = tid; d < HD; d += kAttnThreads) {
-                reinterpret_cast<bf16*>(a.kc)[off + d] = f2bf(ks[d]);
-                reinterpret_cast<bf16*>(a.vc)[off + d] = f2bf(vs[d]);
+                reinterpret_cast<bf16*>(a.kc)[off + d] = f2bf(kn[d]);
+                reinterpret_cast<bf16*>(a.vc)[off + d] = f2bf(vn[d]);
             }
         } else if (tid == 0 && a.err) {
             atomicOr(a.err, kErrBadIndex);
         }
     }
-    mbar_wait(bar, 0, a.err, kErrTimeoutFull);
+    __syncthreads();
 
-    // ---- scores: warp per token, lane per DPL dims, all group heads at once
-    for (int j = t0 + warp; j < t1; j += kAttnThreads / 32) {
-        float kv[DPL];
-        if (j == pos) {
+    // ---- scores S = q K^T on the tensor cores: A = q heads (16 rows, >= G zero),
+    //      B = 8 tokens x 16 dims per mma; warp w takes token octets w, w+4, ...
+    {
+        uint32_t qa[KS][4];
+        const int r = lane >> 2, c2 = (lane & 3) * 2;
 #pragma unroll
-            for (int e = 0; e < DPL; ++e) kv[e] = ks[lane * DPL + e];
-        } else {
-            const uint16_t* kp = kbuf + (size_t)(j - t0) * HD + lane * DPL;
-#pragma unroll
-            for (int e = 0; e < DPL; ++e) kv[e] = __uint_as_float((uint32_t)kp[e] << 16);
+        for (int ks = 0; ks < KS; ++ks) {
+            const int k0 = ks * 16;
+            auto qv = [&](int rr, int cc) { return rr < G ? qf[rr * HD + cc] : 0.f; };
+            qa[ks][0] = pack_bf2(qv(r, k0 + c2), qv(r, k0 + c2 + 1));
+            qa[ks][1] = pack_bf2(qv(r + 8, k0 + c2), qv(r + 8, k0 + c2 + 1));
+            qa[ks][2] = pack_bf2(qv(r, k0 + 8 + c2), qv(r, k0 + 8 + c2 + 1));
+            qa[ks][3] = pack_bf2(qv(r + 8, k0 + 8 + c2), qv(r + 8, k0 + 8 + c2 + 1));
         }
-        float d[kAttnMaxGroup];
+        const uint32_t kbase = smem_u32(kt);
+        for (int nt = warp; nt < n_rows / 8; nt += kAttnThreads / 32) {
+            const int r0 = nt * 8;
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            const int ri = r0 + (lane & 7), mi = lane >> 3;
 #pragma unroll
-        for (int g = 0; g < kAttnMaxGroup; ++g) {
-            d[g] = 0.f;
-            if (g < G)
+            for (int ks = 0; ks < KS; ks += 2) {
+                uint32_t m0, m1, m2, m3;
+                ldsm_x4(kbase + tile_off(C, ri, ks * 16 + mi * 8), m0, m1, m2, m3);
+                mma_16816_bf16(acc, qa[ks], m0, m1);
+                mma_16816_bf16(acc, qa[ks + 1], m2, m3);
+            }
+            // acc[0..1]: head lane/4, rows r0 + 2*(lane%4) + {0,1}; acc[2..3]: head lane/4 + 8
 #pragma unroll
-                for (int e = 0; e < DPL; ++e) d[g] = fmaf(qs[g * HD + lane * DPL + e], kv[e], d[g]);
+            for (int e = 0; e < 2; ++e) {
+                const int jj = r0 + c2 + e;
+                const bool valid = jj >= vlo && jj < vhi;
+                if (r < G) sc[r * C + jj] = valid ? a.scale * acc[e] : -INFINITY;
+                if (r + 8 < G) sc[(r + 8) * C + jj] = valid ? a.scale * acc[2 + e] : -INFINITY;
+            }
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-            for (int g = 0; g < kAttnMaxGroup; ++g)
-                if (g < G) d[g] += __shfl_xor_sync(0xffffffffu, d[g], o);
-        if (lane == 0)
-#pragma unroll
-            for (int g = 0; g < kAttnMaxGroup; ++g)
-                if (g < G) sc[g * a.max_chunk + (j - t0)] = a.scale * d[g];
     }
     __syncthreads();
 
     // ---- softmax statistics per q head (ops.cu:393-419)
     for (int g = warp; g < G; g += kAttnThreads / 32) {
         float m = -INFINITY;
-        for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[g * a.max_chunk + j]);
+        for (int j = lane; j < n_rows; j += 32) m = fmaxf(m, sc[g * C + j]);
         m = warp_max(m);
         float l = 0.f;
-        for (int j = lane; j < n; j += 32) {
-            const float p = expf(sc[g * a.max_chunk + j] - m);
-            sc[g * a.max_chunk + j] = p;
+        for (int j = lane; j < n_rows; j += 32) {
+            const float p = m == -INFINITY ? 0.f : expf(sc[g * C + j] - m);
+            sc[g * C + j] = p;
             l += p;
         }
         l = warp_sum(l);
@@ -218,70 +249,59 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnArgs a) 
     }
     __syncthreads();
 
-    // ---- P.V (ops.cu:526-539): thread -> dims
-    constexpr int TG = HD >= kAttnThreads ? 1 : kAttnThreads / HD;  // token groups
-    constexpr int DPT = HD >= kAttnThreads ? HD / kAttnThreads : 1;  // dims per thread
-    float acc[kAttnMaxGroup][DPT];
+    // ---- P.V (ops.cu:526-539) in fp32: thread -> 4 dims of one head slot
+    constexpr int DG = HD / 4;
+    constexpr int SLOTS = kAttnThreads / DG;
+    constexpr int HPS = (GP + SLOTS - 1) / SLOTS;
+    const int slot = tid / DG, dd = (tid % DG) * 4;
+    float acc[HPS][4];
 #pragma unroll
-    for (int g = 0; g < kAttnMaxGroup; ++g)
+    for (int k = 0; k < HPS; ++k)
 #pragma unroll
-        for (int e = 0; e < DPT; ++e) acc[g][e] = 0.f;
-    const int dbase = HD >= kAttnThreads ? tid : tid % HD;
-    const int tgrp = HD >= kAttnThreads ? 0 : tid / HD;
-    for (int jj = tgrp; jj < n; jj += TG) {
-        const int j = t0 + jj;
-        float v[DPT];
+        for (int e = 0; e < 4; ++e) acc[k][e] = 0.f;
+    {
+        const uint8_t* vcol = vt + (dd >> 6) * C * 128 + ((dd & 7) << 1);
+        const int cc = (dd & 63) >> 3;
+        for (int j = max(vlo, 0); j < vhi; ++j) {
+            const uint2 v = *reinterpret_cast<const uint2*>(vcol + j * 128 + ((cc ^ (j & 7)) << 4));
+            const float2 v01 = bf2_to_f2(v.x), v23 = bf2_to_f2(v.y);
 #pragma unroll
-        for (int e = 0; e < DPT; ++e)
-            v[e] = j == pos ? vs[dbase + e * kAttnThreads]
-                            : __uint_as_float((uint32_t)vbuf[(size_t)jj * HD + dbase + e * kAttnThreads] << 16);
-#pragma unroll
-        for (int g = 0; g < kAttnMaxGroup; ++g) {
-            if (g < G) {
-                const float p = sc[g * a.max_chunk + jj];
-#pragma unroll
-                for (int e = 0; e < DPT; ++e) acc[g][e] = fmaf(p, v[e], acc[g][e]);
+            for (int k = 0; k < HPS; ++k) {
+                const int g = slot + k * SLOTS;
+                if (g < G) {
+                    const float p = sc[g * C + j];
+                    acc[k][0] = fmaf(p, v01.x, acc[k][0]);
+                    acc[k][1] = fmaf(p, v01.y, acc[k][1]);
+                    acc[k][2] = fmaf(p, v23.x, acc[k][2]);
+                    acc[k][3] = fmaf(p, v23.y, acc[k][3]);
+                }
             }
         }
     }
-    if (TG > 1) {
-        // fold token groups into group 0 through shared memory (reuse the score area)
-        __syncthreads();
-        float* red = sc;
-        if (tgrp > 0)
-#pragma unroll
-            for (int g = 0; g < kAttnMaxGroup; ++g)
-                if (g < G) red[((tgrp - 1) * G + g) * HD + dbase] = acc[g][0];
-        __syncthreads();
-        if (tgrp == 0)
-            for (int t = 1; t < TG; ++t)
-#pragma unroll
-                for (int g = 0; g < kAttnMaxGroup; ++g)
-                    if (g < G) acc[g][0] += red[((t - 1) * G + g) * HD + dbase];
-    }
 
     if (a.n_splits == 1) {
-        if (tgrp == 0)
 #pragma unroll
-            for (int g = 0; g < kAttnMaxGroup; ++g)
-                if (g < G) {
-                    const float l = ml[2 * g + 1];
+        for (int k = 0; k < HPS; ++k) {
+            const int g = slot + k * SLOTS;
+            if (g < G) {
+                const float l = ml[2 * g + 1];
+                bf16* dst = reinterpret_cast<bf16*>(a.out) + (size_t)b * a.out_stride + (size_t)(h * G + g) * HD + dd;
 #pragma unroll
-                    for (int e = 0; e < DPT; ++e)
-                        reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + (size_t)(h * G + g) * HD + dbase +
-                                                       e * kAttnThreads] = f2bf(acc[g][e] / l);
-                }
+                for (int e = 0; e < 4; ++e) dst[e] = f2bf(acc[k][e] / l);
+            }
+        }
         return;
     }
 
     // ---- partial results, merged by the last CTA of this (token, kv head)
     const size_t pbase = (((size_t)b * a.nkv + h) * a.n_splits + split) * G;
-    if (tgrp == 0)
 #pragma unroll
-        for (int g = 0; g < kAttnMaxGroup; ++g)
-            if (g < G)
-#pragma unroll
-                for (int e = 0; e < DPT; ++e) a.part_o[(pbase + g) * HD + dbase + e * kAttnThreads] = acc[g][e];
+    for (int k = 0; k < HPS; ++k) {
+        const int g = slot + k * SLOTS;
+        if (g < G)
+            *reinterpret_cast<float4*>(a.part_o + (pbase + g) * HD + dd) =
+                make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
+    }
     if (tid < G) {
         a.part_ml[(pbase + tid) * 2] = ml[2 * tid];
         a.part_ml[(pbase + tid) * 2 + 1] = ml[2 * tid + 1];
@@ -296,9 +316,9 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnArgs a) 
     if (!s_last) return;
     __threadfence();
     const size_t p0 = ((size_t)b * a.nkv + h) * a.n_splits * G;
-    // split weights w[s][g] = exp(m_s - M_g) (0 for empty splits), kept in the score area
-    float* wsg = sc;    // [n_splits][G] maxima, then weights
-    float* lsg = qs;    // [n_splits][G] sums (q no longer needed)
+    // split weights w[s][g] = exp(m_s - M_g) (0 for empty splits)
+    float* wsg = mw;                        // [n_splits][G] maxima, then weights
+    float* lsg = mw + a.n_splits * G;       // [n_splits][G] sums
     for (int idx = tid; idx < a.n_splits * G; idx += kAttnThreads) {
         wsg[idx] = __ldcg(&a.part_ml[(p0 + idx) * 2]);
         lsg[idx] = __ldcg(&a.part_ml[(p0 + idx) * 2 + 1]);
@@ -325,8 +345,9 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnArgs a) 
         float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 8
         for (int s = 0; s < a.n_splits; ++s) {
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(a.part_o + (p0 + (size_t)s * G) * HD + e));
             const float w = wsg[s * G + g];
+            if (w == 0.f) continue;
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(a.part_o + (p0 + (size_t)s * G) * HD + e));
             O.x = fmaf(v.x, w, O.x);
             O.y = fmaf(v.y, w, O.y);
             O.z = fmaf(v.z, w, O.z);
@@ -343,16 +364,19 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnArgs a) 
 }
 
 int attn_splits(int nb, int nkv, int max_len, int sms, int* max_chunk) {
-    // tokens per CTA are capped by the shared-memory K/V tile (env TI_ATTN_CHUNK, <= 64)
-    const char* env = std::getenv("TI_ATTN_CHUNK");
-    const int cap = env && std::atoi(env) >= 16 ? std::min(std::atoi(env), kAttnChunkCap) : kAttnChunkCap;
-    const int work = std::max(1, nb * nkv);
-    const int target = std::max(1, (sms + work - 1) / work);                // about one CTA per SM
-    const int by_len = std::max(1, (max_len + 31) / 32);                    // at least ~32 tokens per CTA
-    const int min_splits = (max_len + cap - 1) / cap;                      // smem tile bound
-    const int n = std::max(std::min(target, by_len), min_splits);
-    *max_chunk = (max_len + n - 1) / n;
-    return n;
+    // pages per split: about two CTAs per SM over the batch's (token, kv head)
+    // pairs at the longest context, at most kAttnMaxPages (env TI_ATTN_PPS overrides)
+    const int max_pages = std::max(1, (max_len + kPage - 1) / kPage);
+    const char* env = std::getenv("TI_ATTN_PPS");
+    int pps;
+    if (env && std::atoi(env) >= 1) {
+        pps = std::min(std::atoi(env), kAttnMaxPages);
+    } else {
+        const long work = (long)std::max(1, nb * nkv) * max_pages;
+        pps = (int)std::min<long>(kAttnMaxPages, std::max<long>(1, (work + 2L * sms - 1) / (2L * sms)));
+    }
+    *max_chunk = pps * kPage;
+    return (max_pages + pps - 1) / pps;
 }
 
 size_t attn_scratch_floats(int nb, int nq, int nkv, int hd, int n_splits) {
@@ -360,26 +384,49 @@ size_t attn_scratch_floats(int nb, int nq, int nkv, int hd, int n_splits) {
     return (size_t)nb * nkv * n_splits * G * (hd + 2);
 }
 
+namespace {
+
+template <int HD>
+const void* attn_func(int gp) {
+    switch (gp) {
+        case 1: return reinterpret_cast<const void*>(&k_attn_decode<HD, 1>);
+        case 2: return reinterpret_cast<const void*>(&k_attn_decode<HD, 2>);
+        case 4: return reinterpret_cast<const void*>(&k_attn_decode<HD, 4>);
+        case 8: return reinterpret_cast<const void*>(&k_attn_decode<HD, 8>);
+        default: return reinterpret_cast<const void*>(&k_attn_decode<HD, 16>);
+    }
+}
+
+}  // namespace
+
 cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s, bool pdl) {
     if (a.nkv <= 0 || a.nq % a.nkv != 0 || a.nq / a.nkv > kAttnMaxGroup) return cudaErrorInvalidValue;
-    if (a.max_chunk > kAttnChunkCap || a.max_chunk < 1) return cudaErrorInvalidValue;
+    if (a.max_chunk < kPage || a.max_chunk > kAttnMaxPages * kPage || a.max_chunk % kPage != 0)
+        return cudaErrorInvalidValue;
+    const int G = a.nq / a.nkv;
+    int gp = 1;
+    while (gp < G) gp <<= 1;
     const void* f = nullptr;
     switch (a.hd) {
-        case 64: f = reinterpret_cast<const void*>(&k_attn_decode<64>); break;
-        case 128: f = reinterpret_cast<const void*>(&k_attn_decode<128>); break;
-        case 256: f = reinterpret_cast<const void*>(&k_attn_decode<256>); break;
+        case 64: f = attn_func<64>(gp); break;
+        case 128: f = attn_func<128>(gp); break;
+        case 256: f = attn_func<256>(gp); break;
         default: return cudaErrorInvalidValue;
     }
-    const int G = a.nq / a.nkv;
-    // the merge also stages n_splits x G sums in the q area
-    if (a.n_splits * G > G * a.hd) return cudaErrorInvalidValue;
-    const size_t smem = attn_layout(G, a.hd, a.max_chunk, attn_sc_floats(G, a.hd, a.max_chunk, a.n_splits)).total;
-    if (smem > 48 * 1024) {
+    CUtensorMap tk, tv;
+    const uint64_t rows = (uint64_t)a.n_pages * a.nkv * kPage;
+    if (!make_tmap_bf16_sw128(&tk, a.kc, rows, a.hd, a.hd, kPage)) return cudaErrorInvalidValue;
+    if (!make_tmap_bf16_sw128(&tv, a.vc, rows, a.hd, a.hd, kPage)) return cudaErrorInvalidValue;
+    const size_t smem = attn_layout(G, a.hd, a.max_chunk, a.n_splits).total;
+    if (smem > 227 * 1024) return cudaErrorInvalidValue;
+    {
+        static std::mutex mu;
+        std::lock_guard<std::mutex> lk(mu);
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
     AttnArgs args = a;
-    void* params[] = {&args};
+    void* params[] = {&tk, &tv, &args};
     return launch_pdl(f, dim3(a.n_splits, a.nkv, a.nb), dim3(kAttnThreads), smem, s, params, pdl);
 }
 

@@ -1,5 +1,6 @@
 // common.cuh — device helpers shared by the sm_100a kernels of libti_b200.
 #pragma once
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -112,6 +113,16 @@ TI_DEVICE_INLINE void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes,
 }
 TI_DEVICE_INLINE void prefetch_l2_bulk(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// 2-D tiled bulk-tensor load (TMA) of one box into shared memory, completing on
+// `bar`; x (innermost coordinate) must be a multiple of 16 bytes.  No multicast.
+TI_DEVICE_INLINE void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
 }
 
 // ------------------------------------------------------------------ loads

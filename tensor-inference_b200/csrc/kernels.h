@@ -1,5 +1,6 @@
 // kernels.h — host-side launch interface of the sm_100a kernels (internal).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -114,6 +115,9 @@ bool tc_plan(const GemvArgs& a, int epi, int device, size_t ws_floats_cap, TcPla
 // ws: >= plan.ws_floats floats; tile_ctr: >= plan.tiles zeroed counters
 cudaError_t tc_launch(const GemvArgs& a, int epi, const TcPlan& plan, float* ws, unsigned int* tile_ctr,
                       cudaStream_t s, bool pdl);
+// 2-D TMA map of a bf16 row-major matrix: boxes of 64 columns x box_rows, 128-byte swizzle
+bool make_tmap_bf16_sw128(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                          uint32_t box_rows);
 // out[b, :K] = bf16 RMSNorm(x[b, :K]) * (w [+ 1])
 cudaError_t rms_rows_launch(const uint16_t* x, int x_stride, const uint16_t* w, float eps, int offset, int K, int nb,
                             uint16_t* out, int out_stride, cudaStream_t s, bool pdl);

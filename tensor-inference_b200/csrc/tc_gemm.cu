@@ -57,13 +57,6 @@ constexpr int kTcMaxTokens = 256;  // MMA N limit
 constexpr size_t kTcSmemBudget = 220 * 1024;
 
 // ------------------------------------------------------------------ tcgen05 / TMA wrappers
-TI_DEVICE_INLINE void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-        "[%4];" ::"r"(smem_u32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
 TI_DEVICE_INLINE void tma_load_2d_hint(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
                                        uint64_t pol) {
     asm volatile(
@@ -608,8 +601,13 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// bf16 [rows, cols] row-major with row pitch `ld` elements; box = 64 columns x box_rows, 128-byte swizzle
-bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
+}  // namespace
+
+// bf16 [rows, cols] row-major with row pitch `ld` elements; box = 64 columns x
+// box_rows, 128-byte swizzle (the K-major operand layout of tcgen05 and the
+// conflict-free layout the attention kernel reads with ldmatrix)
+bool make_tmap_bf16_sw128(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                          uint32_t box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     const cuuint64_t dims[2] = {cols, rows};
@@ -620,6 +618,8 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, ui
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
+
+namespace {
 
 const void* tc_func(int epi) {
     switch (epi) {
@@ -709,8 +709,8 @@ cudaError_t tc_launch(const GemvArgs& g, int epi, const TcPlan& p, float* ws, un
                       bool pdl) {
     CUtensorMap mw, mx;
     const uint64_t wrows = epi == kEpiGlu ? 2ull * g.N : (uint64_t)g.N;
-    if (!make_map(&mw, g.W, wrows, g.K, g.K, epi == kEpiGlu ? 64 : kTcBM)) return cudaErrorInvalidValue;
-    if (!make_map(&mx, g.x, g.nb, g.K, g.x_stride, p.np)) return cudaErrorInvalidValue;
+    if (!make_tmap_bf16_sw128(&mw, g.W, wrows, g.K, g.K, epi == kEpiGlu ? 64 : kTcBM)) return cudaErrorInvalidValue;
+    if (!make_tmap_bf16_sw128(&mx, g.x, g.nb, g.K, g.x_stride, p.np)) return cudaErrorInvalidValue;
     if (!ws || !tile_ctr) return cudaErrorInvalidValue;
     TcKernelArgs a{};
     a.N = g.N;
