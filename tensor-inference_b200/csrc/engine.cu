@@ -47,11 +47,17 @@ struct Slot {
     uint16_t* dst = nullptr;
     size_t ld = 0;
     bool linear = false;
+    // quantised linear weights (wf != kWBf16): rows of wrow_bytes(cols, wf) bytes
+    // starting at qdst (the window's first row); the whole row is held (c0 = 0)
+    int wf = kWBf16;
+    uint8_t* qdst = nullptr;
+    size_t rb = 0;
 };
 
 struct LayerW {
-    uint16_t *norm1 = nullptr, *norm2 = nullptr, *wqkv = nullptr, *bqkv = nullptr, *wo = nullptr, *wgu = nullptr,
-             *wdown = nullptr;
+    uint16_t *norm1 = nullptr, *norm2 = nullptr, *bqkv = nullptr;
+    // linear weights in the engine's weight format (bf16 or quantised rows)
+    uint8_t *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wdown = nullptr;
 };
 
 struct SeqState {
@@ -72,6 +78,7 @@ struct ti_engine {
     ti_engine_opts o{};
     int dev = 0, sms = 148;
     int H = 0, nq = 0, nkv = 0, hd = 0, I = 0, V = 0, Vl = 0, qkv_rows = 0;
+    int wf = kWBf16;  // format of the layers' linear weights
     cudaStream_t cap = nullptr;  // capture stream
 
     // device memory
@@ -200,6 +207,22 @@ void add_slot(ti_engine* e, const std::string& name, size_t rows, size_t cols, s
     e->slots.push_back(s);
 }
 
+// a linear weight: window rows [r0, r0+nr) of a [rows, cols] tensor at row `row`
+// of the layer buffer `base` (bf16 rows of cols elements, or quantised rows)
+void add_linear(ti_engine* e, const std::string& name, size_t rows, size_t cols, size_t r0, size_t nr,
+                uint8_t* base, size_t row) {
+    const size_t rb = wrow_bytes((int)cols, e->wf);
+    if (e->wf == kWBf16) {
+        add_slot(e, name, rows, cols, r0, nr, 0, cols, reinterpret_cast<uint16_t*>(base + row * rb), cols, true);
+        return;
+    }
+    add_slot(e, name, rows, cols, r0, nr, 0, cols, nullptr, cols, true);
+    Slot& s = e->slots.back();
+    s.wf = e->wf;
+    s.qdst = base + row * rb;
+    s.rb = rb;
+}
+
 ti_status validate_desc(const ti_model_desc* d, const ti_engine_opts* o) {
     TI_CHECK(d && o, TI_ERR_INVALID, "engine: null desc/opts");
     TI_CHECK(d->arch >= TI_ARCH_LLAMA && d->arch <= TI_ARCH_MISTRAL, TI_ERR_INVALID, "engine: unknown arch %d",
@@ -213,8 +236,11 @@ ti_status validate_desc(const ti_model_desc* d, const ti_engine_opts* o) {
              "engine: head_dim %d (64/128/256 supported)", d->head_dim);
     TI_CHECK(d->hidden % 128 == 0 && d->intermediate % 128 == 0 && (d->n_heads * d->head_dim) % 128 == 0,
              TI_ERR_UNSUPPORTED, "engine: hidden, intermediate and n_heads*head_dim must be multiples of 128");
-    TI_CHECK(d->weight_format == TI_WFMT_BF16, TI_ERR_UNSUPPORTED, "engine: weight format %d not built yet",
-             d->weight_format);
+    TI_CHECK(d->weight_format == TI_WFMT_BF16 || d->weight_format == TI_WFMT_Q4_0 || d->weight_format == TI_WFMT_Q8_0,
+             TI_ERR_UNSUPPORTED, "engine: unknown weight format %d", d->weight_format);
+    if (d->weight_format != TI_WFMT_BF16)
+        TI_CHECK(d->hidden % 256 == 0 && d->intermediate % 256 == 0 && (d->n_heads * d->head_dim) % 256 == 0,
+                 TI_ERR_UNSUPPORTED, "engine: GGUF weights need hidden, intermediate and n_heads*head_dim % 256 == 0");
     TI_CHECK(o->max_batch >= 1 && o->max_batch <= 256, TI_ERR_INVALID, "engine: max_batch out of range");
     TI_CHECK(o->max_seqs >= 1, TI_ERR_INVALID, "engine: max_seqs < 1");
     TI_CHECK(o->max_seq_len >= 1, TI_ERR_INVALID, "engine: max_seq_len < 1");
@@ -242,6 +268,7 @@ ti_status build(ti_engine* e) {
     e->V = d.vocab;
     e->Vl = d.vocab;
     e->qkv_rows = (e->nq + 2 * e->nkv) * e->hd;
+    e->wf = d.weight_format == TI_WFMT_Q4_0 ? kWQ4 : d.weight_format == TI_WFMT_Q8_0 ? kWQ8 : kWBf16;
     const int H = e->H, I = e->I, hd = e->hd, nq = e->nq, nkv = e->nkv;
     const size_t QW = (size_t)nq * hd;
 
@@ -260,22 +287,25 @@ ti_status build(ti_engine* e) {
         const std::string p = "model.layers." + std::to_string(i) + ".";
         TI_CHECK(dalloc_t(e, &l.norm1, H, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
         TI_CHECK(dalloc_t(e, &l.norm2, H, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
-        TI_CHECK(dalloc_t(e, &l.wqkv, (size_t)e->qkv_rows * H, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s",
-                 ti_last_error());
-        TI_CHECK(dalloc_t(e, &l.wo, (size_t)H * QW, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
-        TI_CHECK(dalloc_t(e, &l.wgu, (size_t)2 * I * H, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
-        TI_CHECK(dalloc_t(e, &l.wdown, (size_t)H * I, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+        const size_t rbH = wrow_bytes(H, e->wf), rbQ = wrow_bytes((int)QW, e->wf), rbI = wrow_bytes(I, e->wf);
+        TI_CHECK(dalloc(e, reinterpret_cast<void**>(&l.wqkv), (size_t)e->qkv_rows * rbH, &e->bytes_w) == TI_OK,
+                 TI_ERR_OOM, "%s", ti_last_error());
+        TI_CHECK(dalloc(e, reinterpret_cast<void**>(&l.wo), (size_t)H * rbQ, &e->bytes_w) == TI_OK, TI_ERR_OOM,
+                 "%s", ti_last_error());
+        TI_CHECK(dalloc(e, reinterpret_cast<void**>(&l.wgu), (size_t)2 * I * rbH, &e->bytes_w) == TI_OK, TI_ERR_OOM,
+                 "%s", ti_last_error());
+        TI_CHECK(dalloc(e, reinterpret_cast<void**>(&l.wdown), (size_t)H * rbI, &e->bytes_w) == TI_OK, TI_ERR_OOM,
+                 "%s", ti_last_error());
         add_slot(e, p + "input_layernorm.weight", 1, H, 0, 1, 0, H, l.norm1, H, false);
         add_slot(e, p + "post_attention_layernorm.weight", 1, H, 0, 1, 0, H, l.norm2, H, false);
-        add_slot(e, p + "self_attn.q_proj.weight", QW, H, 0, QW, 0, H, l.wqkv, H, true);
-        add_slot(e, p + "self_attn.k_proj.weight", (size_t)nkv * hd, H, 0, (size_t)nkv * hd, 0, H,
-                 l.wqkv + QW * H, H, true);
-        add_slot(e, p + "self_attn.v_proj.weight", (size_t)nkv * hd, H, 0, (size_t)nkv * hd, 0, H,
-                 l.wqkv + (QW + (size_t)nkv * hd) * H, H, true);
-        add_slot(e, p + "self_attn.o_proj.weight", H, QW, 0, H, 0, QW, l.wo, QW, true);
-        add_slot(e, p + "mlp.gate_proj.weight", I, H, 0, I, 0, H, l.wgu, H, true);
-        add_slot(e, p + "mlp.up_proj.weight", I, H, 0, I, 0, H, l.wgu + (size_t)I * H, H, true);
-        add_slot(e, p + "mlp.down_proj.weight", H, I, 0, H, 0, I, l.wdown, I, true);
+        const size_t KW = (size_t)nkv * hd;
+        add_linear(e, p + "self_attn.q_proj.weight", QW, H, 0, QW, l.wqkv, 0);
+        add_linear(e, p + "self_attn.k_proj.weight", KW, H, 0, KW, l.wqkv, QW);
+        add_linear(e, p + "self_attn.v_proj.weight", KW, H, 0, KW, l.wqkv, QW + KW);
+        add_linear(e, p + "self_attn.o_proj.weight", H, QW, 0, H, l.wo, 0);
+        add_linear(e, p + "mlp.gate_proj.weight", I, H, 0, I, l.wgu, 0);
+        add_linear(e, p + "mlp.up_proj.weight", I, H, 0, I, l.wgu, I);
+        add_linear(e, p + "mlp.down_proj.weight", H, I, 0, H, l.wdown, 0);
         if (d.qkv_bias) {
             TI_CHECK(dalloc_t(e, &l.bqkv, e->qkv_rows, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
             add_slot(e, p + "self_attn.q_proj.bias", 1, QW, 0, 1, 0, QW, l.bqkv, QW, false);
@@ -436,7 +466,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
     // batches of tc_min..256 tokens: RMSNorm pass (when the GEMV would fuse it)
     // + tcgen05 GEMM; projections with LoRA on stay on the GEMV
     auto gemm = [&](GemvArgs a, int epi, int x_stride_elems, int out_stride, int resid_stride) -> ti_status {
-        if (!(e->xn && B >= e->tc_min && B <= 256 && !a.lora.adapter))
+        if (!(e->xn && B >= e->tc_min && B <= 256 && !a.lora.adapter && a.wfmt == kWBf16))
             return gemv_all(a, epi, x_stride_elems, out_stride, resid_stride);
         a.nb = B;
         if (a.norm_w) {
@@ -475,8 +505,9 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
     // next layer's qkv or the LM head; the LM head warms layer 0 for the next step)
     const char* next_env = std::getenv("TI_GEMV_NEXT_KB");
     const int next_kb = next_env ? std::atoi(next_env) : 640;
-    auto set_next = [&](GemvArgs& a, const uint16_t* w, int N, int K, int U) {
+    auto set_next = [&](GemvArgs& a, const void* w, int N, int K, int U) {
         a.next_w = w;
+        a.next_wfmt = w == e->lm_head ? kWBf16 : e->wf;
         a.next_N = N;
         a.next_K = K;
         a.next_U = U;
@@ -546,6 +577,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         case kKQkv: {
             GemvArgs q;
             q.W = l.wqkv;
+            q.wfmt = e->wf;
             q.N = e->qkv_rows;
             q.K = H;
             q.x = e->hidden;
@@ -599,6 +631,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         case kKO: {
             GemvArgs ov;
             ov.W = l.wo;
+            ov.wfmt = e->wf;
             ov.N = H;
             ov.K = QW;
             ov.x = e->attn;
@@ -618,6 +651,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         case kKGateUp: {
             GemvArgs gu;
             gu.W = l.wgu;
+            gu.wfmt = e->wf;
             gu.N = I;
             gu.K = H;
             gu.x = e->res1;
@@ -639,6 +673,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         case kKDown: {
             GemvArgs dn;
             dn.W = l.wdown;
+            dn.wfmt = e->wf;
             dn.N = H;
             dn.K = I;
             dn.x = e->act;
@@ -862,12 +897,44 @@ ti_status ti_engine_memory(const ti_engine* e, size_t* w, size_t* kv, size_t* ad
     return TI_OK;
 }
 
+// GGUF block bytes of one quantised row of K weights
+static size_t gguf_row_bytes(int K, int wf) { return (size_t)K / 32 * (wf == kWQ4 ? 18 : 34); }
+
+// A linear weight of a Q4_0 / Q8_0 engine: bf16 rows are quantised on the
+// device (the GGUF definition, bit for bit), GGUF blocks are repacked.
+static ti_status load_quantized(ti_engine* e, const Slot& s, const char* name, int dtype, const void* host,
+                                size_t bytes) {
+    const int K = (int)s.cols;
+    const int gguf = s.wf == kWQ4 ? TI_DTYPE_Q4_0 : TI_DTYPE_Q8_0;
+    TI_CHECK(dtype == TI_DTYPE_BF16 || dtype == gguf, TI_ERR_UNSUPPORTED,
+             "tensor '%s': dtype %d (bf16 or this engine's GGUF block type expected)", name, dtype);
+    const size_t in_row = dtype == TI_DTYPE_BF16 ? (size_t)K * 2 : gguf_row_bytes(K, s.wf);
+    TI_CHECK(bytes == s.rows * in_row, TI_ERR_INVALID, "tensor '%s': %zu bytes, expected %zu", name, bytes,
+             s.rows * in_row);
+    void* tmp = nullptr;
+    TI_CUDA(cudaMalloc(&tmp, s.nr * in_row + 16));
+    cudaError_t err = cudaMemcpy(tmp, reinterpret_cast<const uint8_t*>(host) + s.r0 * in_row, s.nr * in_row,
+                                 cudaMemcpyHostToDevice);
+    if (err == cudaSuccess)
+        err = dtype == TI_DTYPE_BF16
+                  ? quantize_rows_launch(reinterpret_cast<const uint16_t*>(tmp), (int)s.nr, K, K, s.qdst, s.rb, s.wf, 0)
+                  : repack_gguf_launch(reinterpret_cast<const uint8_t*>(tmp), (int)s.nr, K, s.qdst, s.rb, s.wf, 0);
+    if (err == cudaSuccess) err = cudaDeviceSynchronize();
+    cudaFree(tmp);
+    TI_CHECK(err == cudaSuccess, TI_ERR_CUDA, "tensor '%s': %s", name, cudaGetErrorString(err));
+    return TI_OK;
+}
+
 ti_status ti_engine_load_tensor(ti_engine* e, const char* name, int dtype, const void* host, size_t bytes) {
     clear_error();
     TI_CHECK(e && name && host, TI_ERR_INVALID, "ti_engine_load_tensor: null argument");
     auto it = e->slot_index.find(name);
     TI_CHECK(it != e->slot_index.end(), TI_ERR_NOT_FOUND, "unknown tensor '%s'", name);
     const Slot& s = e->slots[it->second];
+    if (s.wf != kWBf16) {
+        DeviceGuard g(e->dev);
+        return load_quantized(e, s, name, dtype, host, bytes);
+    }
     TI_CHECK(dtype == TI_DTYPE_BF16, TI_ERR_UNSUPPORTED, "tensor '%s': dtype %d (bf16 expected)", name, dtype);
     TI_CHECK(bytes == s.rows * s.cols * 2, TI_ERR_INVALID, "tensor '%s': %zu bytes, expected %zu", name, bytes,
              s.rows * s.cols * 2);
@@ -883,6 +950,17 @@ ti_status ti_engine_read_tensor(ti_engine* e, const char* name, void* host, size
     auto it = e->slot_index.find(name);
     TI_CHECK(it != e->slot_index.end(), TI_ERR_NOT_FOUND, "unknown tensor '%s'", name);
     const Slot& s = e->slots[it->second];
+    if (s.wf != kWBf16) {
+        // quantised linear weight: the window's rows as GGUF blocks
+        const size_t gb = gguf_row_bytes((int)s.cols, s.wf);
+        TI_CHECK(bytes == s.nr * gb, TI_ERR_INVALID, "tensor '%s': %zu bytes, local window is %zu GGUF bytes", name,
+                 bytes, s.nr * gb);
+        DeviceGuard g(e->dev);
+        std::vector<uint8_t> rows(s.nr * s.rb);
+        TI_CUDA(cudaMemcpy(rows.data(), s.qdst, rows.size(), cudaMemcpyDeviceToHost));
+        gguf_from_rows(rows.data(), (int)s.nr, (int)s.cols, s.rb, s.wf, reinterpret_cast<uint8_t*>(host));
+        return TI_OK;
+    }
     TI_CHECK(bytes == s.nr * s.nc * 2, TI_ERR_INVALID, "tensor '%s': %zu bytes, local window is %zu", name, bytes,
              s.nr * s.nc * 2);
     DeviceGuard g(e->dev);
@@ -895,10 +973,28 @@ ti_status ti_engine_init_synthetic(ti_engine* e, uint64_t seed, float std_) {
     TI_CHECK(e, TI_ERR_INVALID, "null engine");
     DeviceGuard g(e->dev);
     const float c = synth_scale(std_);
+    // quantised slots: the bf16 values the other formats get, then quantised
+    size_t tmp_elems = 0;
     for (const Slot& s : e->slots)
-        TI_CUDA(synth_bf16_launch(s.dst, s.nr, s.nc, s.ld, s.r0, s.c0, s.cols, seed, fnv1a(s.name.c_str()), c,
-                                  (cudaStream_t)0));
-    TI_CUDA(cudaDeviceSynchronize());
+        if (s.wf != kWBf16) tmp_elems = std::max(tmp_elems, s.nr * s.cols);
+    uint16_t* tmp = nullptr;
+    if (tmp_elems) TI_CUDA(cudaMalloc(&tmp, tmp_elems * 2));
+    cudaError_t err = cudaSuccess;
+    for (const Slot& s : e->slots) {
+        if (err != cudaSuccess) break;
+        if (s.wf == kWBf16) {
+            err = synth_bf16_launch(s.dst, s.nr, s.nc, s.ld, s.r0, s.c0, s.cols, seed, fnv1a(s.name.c_str()), c,
+                                    (cudaStream_t)0);
+        } else {
+            err = synth_bf16_launch(tmp, s.nr, s.cols, s.cols, s.r0, 0, s.cols, seed, fnv1a(s.name.c_str()), c,
+                                    (cudaStream_t)0);
+            if (err == cudaSuccess)
+                err = quantize_rows_launch(tmp, (int)s.nr, (int)s.cols, s.cols, s.qdst, s.rb, s.wf, (cudaStream_t)0);
+        }
+    }
+    if (err == cudaSuccess) err = cudaDeviceSynchronize();
+    if (tmp) cudaFree(tmp);
+    TI_CHECK(err == cudaSuccess, TI_ERR_CUDA, "init_synthetic: %s", cudaGetErrorString(err));
     return TI_OK;
 }
 

@@ -1,4 +1,4 @@
-// gemv.cu — weight-streaming GEMV for decode (few tokens, bf16 weights).
+// gemv.cu — weight-streaming GEMV for decode (few tokens; bf16, GGUF Q4_0 or Q8_0 weights).
 //
 // Replaces ops::matmul_t at M = tokens (src/backend/cuda/ops.cu:94-148, one
 // cuBLAS GemmEx per projection) and fuses the ops around it in the model code
@@ -10,6 +10,9 @@
 //             (greedy.cpp:11-36, done on fp32 logits on the device).
 // The bf16 rounding points of the reference are kept: every op output the
 // model code materialises as a bf16 Tensor is rounded to bf16 here too.
+// Quantised weights are dequantised in registers as they are consumed: each
+// element becomes the exact fp32 value d * (q - 8) (Q4_0) or d * q (Q8_0) that
+// GGUF's block formats define, then enters the same fp32 FMAs as a bf16 weight.
 //
 // Structure (one CTA per SM, 16 consumer warps + 1 producer warp + 1 epilogue warp):
 //   producer: streams the CTA's contiguous row range of W from HBM into a ring
@@ -49,10 +52,10 @@ struct GemvSmem {
 
 // rows_cap: most rows one CTA owns; the epilogue warp keeps their residual
 // (nb rows) and bias values in shared memory
-__host__ __device__ inline GemvSmem gemv_smem_layout(int K, int units, int rows_per_stage, int stages, int nb,
-                                                     bool x_in_smem, int rows_cap) {
+__host__ __device__ inline GemvSmem gemv_smem_layout(int K, int wf, int units, int rows_per_stage, int stages,
+                                                     int nb, bool x_in_smem, int rows_cap) {
     GemvSmem L;
-    uint32_t sb = (uint32_t)rows_per_stage * units * K * 2;
+    uint32_t sb = (uint32_t)(rows_per_stage * units * wrow_bytes(K, wf));
     sb = (sb + 127u) & ~127u;
     L.stage_bytes = sb;
     L.stages_off = 0;
@@ -127,10 +130,61 @@ TI_DEVICE_INLINE float sumsq8(const uint4 v, float ss) {
     return ss;
 }
 
+// 8 consecutive weights [c, c+8) of one stage row as fp32 pairs (even, odd):
+// the exact values of the stored format.
+TI_DEVICE_INLINE float2 magic_pair(uint32_t lo, uint32_t hi, uint32_t sel, float bias) {
+    // bytes of lo / hi placed under the exponent of 2^23: float = 2^23 + byte
+    const float a = __uint_as_float(__byte_perm(lo, 0x4B000000u, sel));
+    const float b = __uint_as_float(__byte_perm(hi, 0x4B000000u, sel));
+    return make_float2(a - bias, b - bias);
+}
+template <int WF>
+TI_DEVICE_INLINE void load_w8(const uint8_t* row, int K, int c, float2 w[4]) {
+    if constexpr (WF == kWQ4) {
+        const uint32_t q = *reinterpret_cast<const uint32_t*>(row + (c >> 1));
+        const float d = __half2float(*reinterpret_cast<const __half*>(row + (K >> 1) + ((c >> 5) << 1)));
+        const uint32_t lo = q & 0x0F0F0F0Fu, hi = (q >> 4) & 0x0F0F0F0Fu;  // even / odd elements
+        const float2 dd = make_float2(d, d);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 v = magic_pair(lo, hi, 0x7440u | (uint32_t)k, 8388616.0f);  // 2^23 + 8
+            w[k] = make_float2(v.x * dd.x, v.y * dd.y);
+        }
+    } else {
+        const uint2 q = *reinterpret_cast<const uint2*>(row + c);
+        const float d = __half2float(*reinterpret_cast<const __half*>(row + K + ((c >> 5) << 1)));
+        // int8 -> biased uint8 (q + 128), element pairs (2k, 2k+1)
+        const uint32_t u0 = q.x ^ 0x80808080u, u1 = q.y ^ 0x80808080u;
+        const uint32_t ev = __byte_perm(u0, u1, 0x6420), od = __byte_perm(u0, u1, 0x7531);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 v = magic_pair(ev, od, 0x7440u | (uint32_t)k, 8388736.0f);  // 2^23 + 128
+            w[k] = make_float2(v.x * d, v.y * d);
+        }
+    }
+}
+TI_DEVICE_INLINE float2 dot8_f2(const float2 w[4], const float2* x, float2 acc) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc = ffma2(w[k], x[k], acc);
+    return acc;
+}
+TI_DEVICE_INLINE float dot8_f32w(const float2 w[4], const uint4 x, float acc) {
+    acc = fmaf(w[0].x, bf_lo(x.x), acc);
+    acc = fmaf(w[0].y, bf_hi(x.x), acc);
+    acc = fmaf(w[1].x, bf_lo(x.y), acc);
+    acc = fmaf(w[1].y, bf_hi(x.y), acc);
+    acc = fmaf(w[2].x, bf_lo(x.z), acc);
+    acc = fmaf(w[2].y, bf_hi(x.z), acc);
+    acc = fmaf(w[3].x, bf_lo(x.w), acc);
+    acc = fmaf(w[3].y, bf_hi(x.w), acc);
+    return acc;
+}
+
 // XR > 0: NB == 1, the lane's XR sub-chunks of the activation slice in registers.
 // XR == 0: NB tokens, activation slices in shared memory.
 // RG: compile-time bound on rows per stage (per unit).
-template <int NB, int EPI, int XR, int RG>
+// WF: weight row format (kWBf16 / kWQ4 / kWQ8).
+template <int NB, int EPI, int XR, int RG, int WF>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemv(const GemvArgs a, const int rows_per_stage, const int stages, const int pf) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -139,7 +193,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int XRR = XS ? 1 : XR;
     const int K = a.K;
     const int rows_cap = (a.N + (int)gridDim.x - 1) / (int)gridDim.x;
-    const GemvSmem L = gemv_smem_layout(K, U, rows_per_stage, stages, NB, XS, rows_cap);
+    const GemvSmem L = gemv_smem_layout(K, WF, U, rows_per_stage, stages, NB, XS, rows_cap);
+    const size_t rb = wrow_bytes(K, WF);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.full_off);
     uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L.empty_off);
     uint64_t* pfull = reinterpret_cast<uint64_t*>(smem + L.pfull_off);
@@ -174,7 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0 && n_groups > 0) {
             const uint64_t pol = l2_policy_evict_first();
             const uint8_t* W = reinterpret_cast<const uint8_t*>(a.W);
-            const size_t row_bytes = (size_t)K * 2;
+            const size_t row_bytes = rb;
             auto rows_of = [&](int g) { return min(rows_per_stage, u1 - (u0 + g * rows_per_stage)); };
             auto prefetch = [&](int g) {
                 const int row0 = u0 + g * rows_per_stage;
@@ -201,11 +256,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (cta < G2) {
                     const int r0 = (int)((long long)cta * a.next_N / G2);
                     const int r1 = (int)((long long)(cta + 1) * a.next_N / G2);
-                    const size_t rb = (size_t)a.next_K * 2;
-                    const int rows = min(r1 - r0, max(1, (int)(a.next_bytes / (rb * a.next_U))));
+                    const size_t nrb = wrow_bytes(a.next_K, a.next_wfmt);
+                    const int rows = min(r1 - r0, max(1, (int)(a.next_bytes / (nrb * a.next_U))));
                     const uint8_t* NW = reinterpret_cast<const uint8_t*>(a.next_w);
-                    prefetch_l2_bulk(NW + (size_t)r0 * rb, (uint32_t)(rows * rb));
-                    if (a.next_U == 2) prefetch_l2_bulk(NW + ((size_t)a.next_N + r0) * rb, (uint32_t)(rows * rb));
+                    prefetch_l2_bulk(NW + (size_t)r0 * nrb, (uint32_t)(rows * nrb));
+                    if (a.next_U == 2) prefetch_l2_bulk(NW + ((size_t)a.next_N + r0) * nrb, (uint32_t)(rows * nrb));
                 }
             }
         }
@@ -430,12 +485,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (r < nr)
 #pragma unroll
                             for (int u = 0; u < U; ++u) {
-                                const uint4 w =
-                                    lds128(stage + (((size_t)u * rows_per_stage + r) * K + col0 + sc * 8) * 2);
-                                if constexpr (XF) {
-                                    acc2[r][u] = dot8_bf16_f2(w, xf[j], acc2[r][u]);
+                                const uint8_t* wrow = stage + ((size_t)u * rows_per_stage + r) * rb;
+                                if constexpr (WF == kWBf16) {
+                                    const uint4 w = lds128(wrow + (size_t)(col0 + sc * 8) * 2);
+                                    if constexpr (XF) {
+                                        acc2[r][u] = dot8_bf16_f2(w, xf[j], acc2[r][u]);
+                                    } else {
+                                        acc2[r][u].x = dot8_bf16(w, xr[j], acc2[r][u].x);
+                                    }
                                 } else {
-                                    acc2[r][u].x = dot8_bf16(w, xr[j], acc2[r][u].x);
+                                    float2 wv[4];
+                                    load_w8<WF>(wrow, K, col0 + sc * 8, wv);
+                                    if constexpr (XF) {
+                                        acc2[r][u] = dot8_f2(wv, xf[j], acc2[r][u]);
+                                    } else {
+                                        acc2[r][u].x = dot8_f32w(wv, xr[j], acc2[r][u].x);
+                                    }
                                 }
                             }
                 }
@@ -455,9 +520,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (r < nr)
 #pragma unroll
                         for (int u = 0; u < U; ++u) {
-                            const uint4 w = lds128(stage + (((size_t)u * rows_per_stage + r) * K + c) * 2);
+                            const uint8_t* wrow = stage + ((size_t)u * rows_per_stage + r) * rb;
+                            if constexpr (WF == kWBf16) {
+                                const uint4 w = lds128(wrow + (size_t)c * 2);
 #pragma unroll
-                            for (int b = 0; b < NB; ++b) acc[r][u][b] = dot8_bf16(w, xv[b], acc[r][u][b]);
+                                for (int b = 0; b < NB; ++b) acc[r][u][b] = dot8_bf16(w, xv[b], acc[r][u][b]);
+                            } else {
+                                float2 wv[4];
+                                load_w8<WF>(wrow, K, c, wv);
+#pragma unroll
+                                for (int b = 0; b < NB; ++b) acc[r][u][b] = dot8_f32w(wv, xv[b], acc[r][u][b]);
+                            }
                         }
             }
         }
@@ -489,26 +562,26 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ host side
-template <int NB, int EPI, int XR, int RG>
+template <int NB, int EPI, int XR, int RG, int WF>
 static const void* fn() {
-    return reinterpret_cast<const void*>(&k_gemv<NB, EPI, XR, RG>);
+    return reinterpret_cast<const void*>(&k_gemv<NB, EPI, XR, RG, WF>);
 }
 
-template <int EPI>
+template <int EPI, int WF>
 static const void* pick(int nb, int xr) {
     constexpr int U = EPI == kEpiGlu ? 2 : 1;
     if (nb == 1) {
         switch (xr) {
-            case 1: return fn<1, EPI, 1, kRowsMax / U>();
-            case 2: return fn<1, EPI, 2, kRowsMax / U>();
-            case 4: return fn<1, EPI, 4, (4 / U > 0 ? 4 / U : 1)>();
-            case 8: return fn<1, EPI, 8, (2 / U > 0 ? 2 / U : 1)>();
-            default: return fn<1, EPI, 0, kRowsMax / U>();
+            case 1: return fn<1, EPI, 1, kRowsMax / U, WF>();
+            case 2: return fn<1, EPI, 2, kRowsMax / U, WF>();
+            case 4: return fn<1, EPI, 4, (4 / U > 0 ? 4 / U : 1), WF>();
+            case 8: return fn<1, EPI, 8, (2 / U > 0 ? 2 / U : 1), WF>();
+            default: return fn<1, EPI, 0, kRowsMax / U, WF>();
         }
     }
-    if (nb == 2) return fn<2, EPI, 0, (4 / U > 0 ? 4 / U : 1)>();
-    if (nb <= 4) return fn<4, EPI, 0, (2 / U > 0 ? 2 / U : 1)>();
-    if (nb <= 8) return fn<8, EPI, 0, 1>();
+    if (nb == 2) return fn<2, EPI, 0, (4 / U > 0 ? 4 / U : 1), WF>();
+    if (nb <= 4) return fn<4, EPI, 0, (2 / U > 0 ? 2 / U : 1), WF>();
+    if (nb <= 8) return fn<8, EPI, 0, 1, WF>();
     return nullptr;
 }
 
@@ -542,7 +615,11 @@ bool gemv_plan(const GemvArgs& a, int epi, int device, GemvPlan* plan, std::stri
     }
     const int U = epi == kEpiGlu ? 2 : 1;
     const int nbt = nb_tmpl(a.nb);
-    const size_t row_bytes = (size_t)a.K * 2 * U;
+    if (a.wfmt != kWBf16 && (a.K % 256 != 0 || epi == kEpiLmHead)) {
+        if (why) *why = "gemv: quantised weights need K % 256 == 0 (and not the LM head)";
+        return false;
+    }
+    const size_t row_bytes = wrow_bytes(a.K, a.wfmt) * U;
     // register slice: sub-chunks per lane = ceil(K / 128 / 32)
     const int need = (a.K / (8 * kConsumerWarps) + 31) / 32;
     int xr = 0;
@@ -564,7 +641,7 @@ bool gemv_plan(const GemvArgs& a, int epi, int device, GemvPlan* plan, std::stri
     cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
     GemvSmem L;
     for (;;) {
-        L = gemv_smem_layout(a.K, U, rps, stages, nbt, xs, rows_cap);
+        L = gemv_smem_layout(a.K, a.wfmt, U, rps, stages, nbt, xs, rows_cap);
         if ((int)L.total <= max_smem) break;
         if (stages > 2) --stages;
         else if (rps > 1) --rps;
@@ -574,11 +651,18 @@ bool gemv_plan(const GemvArgs& a, int epi, int device, GemvPlan* plan, std::stri
         }
     }
     const void* f = nullptr;
-    switch (epi) {
-        case kEpiStore: f = pick<kEpiStore>(a.nb, xr); break;
-        case kEpiResid: f = pick<kEpiResid>(a.nb, xr); break;
-        case kEpiGlu: f = pick<kEpiGlu>(a.nb, xr); break;
-        case kEpiLmHead: f = pick<kEpiLmHead>(a.nb, xr); break;
+    switch (a.wfmt * 4 + epi) {
+        case kEpiStore: f = pick<kEpiStore, kWBf16>(a.nb, xr); break;
+        case kEpiResid: f = pick<kEpiResid, kWBf16>(a.nb, xr); break;
+        case kEpiGlu: f = pick<kEpiGlu, kWBf16>(a.nb, xr); break;
+        case kEpiLmHead: f = pick<kEpiLmHead, kWBf16>(a.nb, xr); break;
+        case 4 * kWQ4 + kEpiStore: f = pick<kEpiStore, kWQ4>(a.nb, xr); break;
+        case 4 * kWQ4 + kEpiResid: f = pick<kEpiResid, kWQ4>(a.nb, xr); break;
+        case 4 * kWQ4 + kEpiGlu: f = pick<kEpiGlu, kWQ4>(a.nb, xr); break;
+        case 4 * kWQ8 + kEpiStore: f = pick<kEpiStore, kWQ8>(a.nb, xr); break;
+        case 4 * kWQ8 + kEpiResid: f = pick<kEpiResid, kWQ8>(a.nb, xr); break;
+        case 4 * kWQ8 + kEpiGlu: f = pick<kEpiGlu, kWQ8>(a.nb, xr); break;
+        default: break;
     }
     if (!f) {
         if (why) *why = "gemv: no kernel instance";

@@ -55,8 +55,19 @@ struct LoraShrinkArgs {
 };
 cudaError_t lora_shrink_launch(const LoraShrinkArgs& a, cudaStream_t s, bool pdl);
 
+// Weight row formats the GEMV streams (TI_WFMT_* values).  Quantised rows are
+// [K codes][K/32 fp16 block scales]: Q4_0 codes are 4-bit, element c in byte
+// c/2 (low nibble for even c), value d * (q - 8); Q8_0 codes are int8, value
+// d * q (GGUF's block formats, rows repacked so a lane's 8 elements are one
+// aligned word).
+enum WeightFmt : int { kWBf16 = 0, kWQ4 = 1, kWQ8 = 2 };
+__host__ __device__ inline size_t wrow_bytes(int K, int wf) {
+    return wf == kWQ4 ? (size_t)K / 2 + (size_t)K / 16 : wf == kWQ8 ? (size_t)K + (size_t)K / 16 : (size_t)K * 2;
+}
+
 struct GemvArgs {
-    const uint16_t* W = nullptr;  // bf16 [rows, K]; kEpiGlu: gate rows [0,N) then up rows [N,2N)
+    const void* W = nullptr;  // [rows, K] in format wfmt; kEpiGlu: gate rows [0,N) then up rows [N,2N)
+    int wfmt = kWBf16;
     int N = 0;                    // output units
     int K = 0;
     int nb = 1;                   // tokens
@@ -82,8 +93,8 @@ struct GemvArgs {
     // L2 warm-up of the next GEMV of the step: once this CTA's producer has
     // issued its own copies it prefetches the first `next_bytes` of the rows the
     // next kernel's CTA with the same index will stream first
-    const uint16_t* next_w = nullptr;
-    int next_N = 0, next_K = 0, next_U = 1, next_bytes = 0;
+    const void* next_w = nullptr;
+    int next_N = 0, next_K = 0, next_U = 1, next_bytes = 0, next_wfmt = kWBf16;
     int* err = nullptr;
 };
 
@@ -99,6 +110,16 @@ struct GemvPlan {
 // Chooses stage geometry, grid and kernel instance; false if unsupported.
 bool gemv_plan(const GemvArgs& a, int epi, int device, GemvPlan* plan, std::string* why);
 cudaError_t gemv_launch(const GemvArgs& a, int epi, const GemvPlan& plan, cudaStream_t s, bool pdl);
+
+// ----------------------------------------------------------------- GGUF Q4_0 / Q8_0 rows
+// bf16 [nr, K] (row pitch src_ld) -> quantised engine rows (wrow_bytes(K, wf) apart)
+cudaError_t quantize_rows_launch(const uint16_t* src, int nr, int K, size_t src_ld, uint8_t* dst, size_t dst_rb,
+                                 int wf, cudaStream_t s);
+// GGUF blocks [nr, K/32] (18 / 34 bytes each) -> engine rows
+cudaError_t repack_gguf_launch(const uint8_t* blocks, int nr, int K, uint8_t* dst, size_t dst_rb, int wf,
+                               cudaStream_t s);
+// engine rows (host memory) -> GGUF blocks (host memory)
+void gguf_from_rows(const uint8_t* rows, int nr, int K, size_t rb, int wf, uint8_t* blocks);
 
 // ----------------------------------------------------------------- tensor-core GEMM (tcgen05)
 // Same arguments and epilogues as the GEMV (no RMSNorm prologue, no LoRA: the

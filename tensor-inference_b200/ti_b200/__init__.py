@@ -260,7 +260,9 @@ def algorithmic_bytes_per_step(desc, batch, ctx_total, lora_bytes=0):
     H, I, hd = desc.hidden, desc.intermediate, desc.head_dim
     QW, KW = desc.n_heads * hd, desc.n_kv_heads * hd
     per_layer = (QW + 2 * KW) * H + H * QW + 3 * H * I
-    wbytes = 2 * (desc.n_layers * per_layer + desc.vocab * H)
+    # linear weights per element: bf16 2 bytes; GGUF Q4_0 18 / 32, Q8_0 34 / 32
+    bpe = {WFMT_BF16: 2.0, WFMT_Q4_0: 18 / 32, WFMT_Q8_0: 34 / 32}[desc.weight_format]
+    wbytes = bpe * desc.n_layers * per_layer + 2 * desc.vocab * H
     kv = ctx_total * desc.n_layers * 2 * KW * 2
     return wbytes + kv + lora_bytes
 
