@@ -149,31 +149,33 @@ def run_reference(args, rank, world):
 
 
 # ------------------------------------------------------------------ our arm
-def prefill_lockstep(eng, sids, prompts):
+def prefill_lockstep(eng, sids, prompts, adapters=None):
     """run equal-length prompts through all sequences in lockstep decode steps"""
     import numpy as np
 
     nxt = None
     for t in range(prompts.shape[1]):
-        nxt = eng.decode(sids, np.ascontiguousarray(prompts[:, t]))
+        nxt = eng.decode(sids, np.ascontiguousarray(prompts[:, t]), adapters=adapters)
     return nxt
 
 
-def measure_batch(ti, torch, eng, B, steps, warmup, stream, peak, measure_e2e=True):
+def measure_batch(ti, torch, eng, B, steps, warmup, stream, peak, measure_e2e=True, prompt=None, adapters=None,
+                  lora_bytes=0):
     import numpy as np
 
     desc = eng.desc
+    prompt = prompt or PROMPT
     sids = [eng.seq_create() for _ in range(B)]
-    prompts = np.random.default_rng(0).integers(0, desc.vocab, size=(B, PROMPT), dtype=np.int32)
+    prompts = np.random.default_rng(0).integers(0, desc.vocab, size=(B, prompt), dtype=np.int32)
     t0 = time.perf_counter()
-    first = prefill_lockstep(eng, sids, prompts)
+    first = prefill_lockstep(eng, sids, prompts, adapters)
     t_prefill = time.perf_counter() - t0
-    total = PROMPT + 2 * (warmup + steps) + 8
+    total = prompt + 2 * (warmup + steps) + 8
     for s in sids:
         eng.seq_reserve(s, total)
 
     # ---- device-resident chain (value)
-    eng.bind(sids, first)
+    eng.bind(sids, first, adapters)
     for _ in range(warmup):
         eng.decode_device(stream)
     torch.cuda.synchronize()
@@ -188,7 +190,7 @@ def measure_batch(ti, torch, eng, B, steps, warmup, stream, peak, measure_e2e=Tr
     last = eng.unbind(warmup + steps, stream)
     eng.check()
     ctx_avg = ctx0 + (steps - 1) / 2.0
-    step_bytes = ti.algorithmic_bytes_per_step(desc, B, B * ctx_avg)
+    step_bytes = ti.algorithmic_bytes_per_step(desc, B, B * ctx_avg, lora_bytes)
     res = {"batch": B, "ms_per_step": ms, "tok_s": B * 1e3 / ms, "ctx_avg": ctx_avg, "prefill_s": t_prefill,
            "step_bytes": step_bytes, "step_gbs": step_bytes / (ms * 1e-3) / 1e9}
     res["step_frac_measured"] = res["step_gbs"] / peak
@@ -198,12 +200,12 @@ def measure_batch(ti, torch, eng, B, steps, warmup, stream, peak, measure_e2e=Tr
     if measure_e2e:
         feed = np.ascontiguousarray(last, np.int32)
         for _ in range(2):
-            feed = eng.decode(sids, feed, stream=stream)
+            feed = eng.decode(sids, feed, adapters=adapters, stream=stream)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         ev0.record(torch.cuda.current_stream())
         for _ in range(steps):
-            feed = eng.decode(sids, feed, stream=stream)
+            feed = eng.decode(sids, feed, adapters=adapters, stream=stream)
         ev1.record(torch.cuda.current_stream())
         torch.cuda.synchronize()
         wall = (time.perf_counter() - t0) / steps
@@ -214,6 +216,29 @@ def measure_batch(ti, torch, eng, B, steps, warmup, stream, peak, measure_e2e=Tr
     for s in sids:
         eng.seq_free(s)
     return res
+
+
+def measure_qwen_lora(ti, torch, stream, peak, wf, steps, warmup, dev=0):
+    """Qwen2.5-7B shape, rank-16 LoRA on q/k/v/o (A ~ N(0, 0.02),
+    B ~ N(0, 0.001), alpha 32), batch 8, 256-token prompts; weights bf16 or GGUF Q4_0"""
+    B, P, R = 8, 256, 16
+    desc = ti.model_desc(**dict(ti.PRESETS["qwen25_7b"], weight_format=wf))
+    eng = ti.Engine(desc, device=dev, max_batch=B, max_seqs=B, max_seq_len=P + 2 * (warmup + steps) + 64,
+                    max_adapters=1, max_lora_rank=R, lora_proj_mask=0x0F)
+    try:
+        eng.init_synthetic(0, 0.02)
+        ad = eng.adapter_create(R, 32.0, 0x0F)
+        eng.adapter_init_synthetic(ad, 1, 0.02, 0.001)
+        H, hd = desc.hidden, desc.head_dim
+        qw, kw = desc.n_heads * hd, desc.n_kv_heads * hd
+        lora_bytes = desc.n_layers * 2 * R * (3 * H + (qw + 2 * kw) + qw + H)
+        r = measure_batch(ti, torch, eng, B, steps, warmup, stream, peak, measure_e2e=False, prompt=P,
+                          adapters=[ad] * B, lora_bytes=lora_bytes)
+    finally:
+        eng.close()
+    return {"tok_s": round(r["tok_s"], 1), "ms_per_step": round(r["ms_per_step"], 3),
+            "step_gbs": round(r["step_gbs"], 1), "frac_measured": round(r["step_frac_measured"], 4),
+            "bytes_per_step": r["step_bytes"], "ctx_avg": r["ctx_avg"]}
 
 
 def kernel_roofline(ti, torch, eng, stream, peak, iters=64):
@@ -350,6 +375,11 @@ def run_ours(args, rank, world):
     if args.b32:
         r32 = measure_batch(ti, torch, eng, 32, max(2, args.steps // 4), min(args.warmup, 3), stream, peak,
                             measure_e2e=False)
+    qwen = None
+    if args.qwen and world == 1:
+        eng.close()  # the 8B engine's 15 GB is not needed for the Qwen legs
+        qwen = {name: measure_qwen_lora(ti, torch, stream, peak, wf, max(4, args.steps // 4), 3, dev)
+                for name, wf in (("bf16", ti.WFMT_BF16), ("q4_0", ti.WFMT_Q4_0))}
 
     # every rank runs its own replica; the job's time is the slowest rank's
     ms = r1["ms_per_step"]
@@ -388,6 +418,8 @@ def run_ours(args, rank, world):
             line["b32"] = {"tok_s": round(r32["tok_s"], 1), "ms_per_step": round(r32["ms_per_step"], 3),
                            "step_gbs": round(r32["step_gbs"], 1), "frac_measured": round(r32["step_frac_measured"], 4),
                            "ctx_avg": r32["ctx_avg"]}
+        if qwen:
+            line["qwen7b_lora_b8"] = dict(qwen, config="Qwen2.5-7B shape, rank-16 LoRA q/k/v/o, batch 8, 256-token prompt")
         if pkm:
             # FP32 issue peak: 148 SMs x 128 lanes x SM clock during the run
             clk = (line["clocks"].get("sm_mhz") or 1965.0) * 1e6
@@ -411,6 +443,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-b32", dest="b32", action="store_false")
+    ap.add_argument("--no-qwen", dest="qwen", action="store_false", help="skip the Qwen-7B LoRA legs (config 3)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true", help="short ncu workload (see run_profile)")
     ap.add_argument("--layers", type=int, default=32)

@@ -108,7 +108,7 @@ struct ti_engine {
     int attn_splits_n = 1, attn_max_chunk = 0;
     // tensor-core path (batches of tc_min..256 tokens): RMSNorm'd rows, partial
     // tiles shared between CTAs and their tickets
-    int tc_min = 16;
+    int tc_min = 8;
     uint16_t* xn = nullptr;
     float* tc_ws = nullptr;
     size_t tc_ws_floats = 0;
@@ -359,7 +359,7 @@ ti_status build(ti_engine* e) {
     e->err = reinterpret_cast<int*>(e->out + B);
     {
         const char* env = std::getenv("TI_TC_MIN_BATCH");
-        e->tc_min = env ? std::atoi(env) : 16;
+        e->tc_min = env ? std::atoi(env) : 8;
         if (B >= e->tc_min && e->tc_min > 0) {
             const int kmax = std::max(H, std::max((int)QW, I));
             TI_CHECK(dalloc_t(e, &e->xn, (size_t)std::min(B, 256) * kmax, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
@@ -463,10 +463,10 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         return TI_OK;
     };
 
-    // batches of tc_min..256 tokens: RMSNorm pass (when the GEMV would fuse it)
-    // + tcgen05 GEMM; projections with LoRA on stay on the GEMV
+    // batches of tc_min..256 tokens with bf16 weights: RMSNorm pass (when the
+    // GEMV would fuse it) + tcgen05 GEMM (LoRA expansion in its epilogue)
     auto gemm = [&](GemvArgs a, int epi, int x_stride_elems, int out_stride, int resid_stride) -> ti_status {
-        if (!(e->xn && B >= e->tc_min && B <= 256 && !a.lora.adapter && a.wfmt == kWBf16))
+        if (!(e->xn && B >= e->tc_min && B <= 256 && a.wfmt == kWBf16))
             return gemv_all(a, epi, x_stride_elems, out_stride, resid_stride);
         a.nb = B;
         if (a.norm_w) {

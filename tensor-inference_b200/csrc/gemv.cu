@@ -31,6 +31,7 @@
 //     order (deterministic) and applies the fused epilogue.
 #include "common.cuh"
 #include "kernels.h"
+#include "lora_epi.cuh"
 
 #include <algorithm>
 #include <cstdio>
@@ -87,26 +88,6 @@ TI_DEVICE_INLINE float glu_act(float g, int act) {
     if (act == 0) return round_bf(g / (1.0f + expf(-g)));  // ops.cu:326
     const float c1 = 0.7978845608f, c2 = 0.044715f;        // ops.cu:712-714
     return round_bf(0.5f * g * (1.0f + tanhf(c1 * (g + c2 * g * g * g))));
-}
-
-// LoRA expansion of one output element (qwen_adapter_model.cpp:27-29 + :42)
-TI_DEVICE_INLINE float lora_delta(const GemvLora& L, int ad, int b, int row, int t_off, float base) {
-    if (ad < 0 || ad >= L.n_adapters) return base;
-    const uint16_t* br = L.B + (size_t)ad * L.B_adapter_stride + (size_t)row * L.rank;
-    const float* t = L.t + (size_t)b * L.t_stride + t_off;
-    float s = 0.f;
-    for (int i = 0; i < L.rank; i += 8) {
-        const uint4 w = *reinterpret_cast<const uint4*>(br + i);
-        const uint32_t* wp = reinterpret_cast<const uint32_t*>(&w);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            s = fmaf(bf_lo(wp[e]), t[i + 2 * e], s);
-            s = fmaf(bf_hi(wp[e]), t[i + 2 * e + 1], s);
-        }
-    }
-    const float up = round_bf(s);
-    const float delta = round_bf(up * L.scale[ad]);
-    return round_bf(base + delta);
 }
 
 TI_DEVICE_INLINE void normalise8(uint4& v, const uint4 wn, float scale, float off) {
@@ -522,9 +503,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int u = 0; u < U; ++u) {
                             const uint8_t* wrow = stage + ((size_t)u * rows_per_stage + r) * rb;
                             if constexpr (WF == kWBf16) {
+                                // unpacked once, shared by the tokens
                                 const uint4 w = lds128(wrow + (size_t)c * 2);
+                                const float2 wv[4] = {bf2_to_f2(w.x), bf2_to_f2(w.y), bf2_to_f2(w.z), bf2_to_f2(w.w)};
 #pragma unroll
-                                for (int b = 0; b < NB; ++b) acc[r][u][b] = dot8_bf16(w, xv[b], acc[r][u][b]);
+                                for (int b = 0; b < NB; ++b) acc[r][u][b] = dot8_f32w(wv, xv[b], acc[r][u][b]);
                             } else {
                                 float2 wv[4];
                                 load_w8<WF>(wrow, K, c, wv);
@@ -579,9 +562,9 @@ static const void* pick(int nb, int xr) {
             default: return fn<1, EPI, 0, kRowsMax / U, WF>();
         }
     }
-    if (nb == 2) return fn<2, EPI, 0, (4 / U > 0 ? 4 / U : 1), WF>();
-    if (nb <= 4) return fn<4, EPI, 0, (2 / U > 0 ? 2 / U : 1), WF>();
-    if (nb <= 8) return fn<8, EPI, 0, 1, WF>();
+    if (nb == 2) return fn<2, EPI, 0, 8 / U, WF>();
+    if (nb <= 4) return fn<4, EPI, 0, 4 / U, WF>();
+    if (nb <= 8) return fn<8, EPI, 0, (2 / U > 0 ? 2 / U : 1), WF>();
     return nullptr;
 }
 
@@ -592,9 +575,9 @@ static int rg_tmpl(int nbt, int U, int xr) {
         if (xr == 8) return std::max(1, 2 / U);
         return kRowsMax / U;
     }
-    if (nbt == 2) return std::max(1, 4 / U);
-    if (nbt == 4) return std::max(1, 2 / U);
-    return 1;
+    if (nbt == 2) return std::max(1, 8 / U);
+    if (nbt == 4) return std::max(1, 4 / U);
+    return std::max(1, 2 / U);
 }
 
 // Geometry knobs (KB): stage size, shared-memory ring, L2 prefetch window per CTA.

@@ -44,6 +44,7 @@
 #include "common.cuh"
 #include "internal.h"
 #include "kernels.h"
+#include "lora_epi.cuh"
 
 namespace ti {
 
@@ -140,6 +141,7 @@ struct TcKernelArgs {
     float* logits_f32;
     float* ws;               // [grid][2][np][128] fp32 partials of tiles shared between CTAs
     unsigned int* tile_ctr;  // [tiles], zero; reset by each shared tile's last unit
+    GemvLora lora;           // per-token LoRA expansion (adapter == nullptr: off)
     int* err;
 };
 
@@ -388,15 +390,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (kGlu) {
                     float* xq = xch + (size_t)(q & 1) * 32 * 32;
                     if (q >= 2) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) xq[i * 32 + lane] = round_bf(v[i]);
+                        for (int i = 0; i < 32; ++i) {
+                            const int b = c * 32 + i;
+                            float uv = round_bf(v[i]);
+                            if (a.lora.adapter && b < a.nb && row_ok)
+                                uv = lora_delta(a.lora, a.lora.adapter[b], b, a.N + n, a.lora.rank, uv);
+                            xq[i * 32 + lane] = uv;
+                        }
                     }
                     named_bar(1, 128);
                     if (q < 2 && row_ok) {
                         for (int i = 0; i < 32; ++i) {
                             const int b = c * 32 + i;
                             if (b >= a.nb) break;
-                            const float gv = round_bf(v[i]);
+                            float gv = round_bf(v[i]);
+                            if (a.lora.adapter) gv = lora_delta(a.lora, a.lora.adapter[b], b, n, 0, gv);
                             const float uv = xq[i * 32 + lane];
                             reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + n] = f2bf(tc_act(gv, a.act) * uv);
                         }
@@ -410,6 +418,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             if (b >= a.nb) break;
                             float val = round_bf(v[i]);
                             if (a.bias) val = round_bf(val + bv);
+                            if (a.lora.adapter) {
+                                // sections of the fused q|k|v rows: t offset = section * rank
+                                const int sec = (n >= a.lora.sec1) + (n >= a.lora.sec2);
+                                val = lora_delta(a.lora, a.lora.adapter[b], b, n, sec * a.lora.rank, val);
+                            }
                             reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + n] = f2bf(val);
                         }
                     }
@@ -418,7 +431,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         for (int i = 0; i < 32; ++i) {
                             const int b = c * 32 + i;
                             if (b >= a.nb) break;
-                            const float val = round_bf(v[i]);
+                            float val = round_bf(v[i]);
+                            if (a.lora.adapter) val = lora_delta(a.lora, a.lora.adapter[b], b, n, 0, val);
                             const float rr = __uint_as_float((uint32_t)a.resid[(size_t)b * a.resid_stride + n] << 16);
                             reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + n] = f2bf(rr + val);
                         }
@@ -645,8 +659,12 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
         if (why) *why = "tc_gemm: GLU width must be a multiple of 64";
         return false;
     }
-    if (g.norm_w || g.lora.adapter) {
-        if (why) *why = "tc_gemm: RMSNorm prologue and LoRA are applied outside this kernel";
+    if (g.norm_w) {
+        if (why) *why = "tc_gemm: the RMSNorm prologue runs as its own pass (rms_rows_launch)";
+        return false;
+    }
+    if (g.wfmt != kWBf16) {
+        if (why) *why = "tc_gemm: bf16 weights only";
         return false;
     }
     // tokens padded to whole 32-column TMEM loads
@@ -738,6 +756,7 @@ cudaError_t tc_launch(const GemvArgs& g, int epi, const TcPlan& p, float* ws, un
     a.logits_f32 = g.logits_f32;
     a.ws = ws;
     a.tile_ctr = tile_ctr;
+    a.lora = g.lora;
     a.err = g.err;
     static std::mutex mu;
     static bool attr_set[4] = {false, false, false, false};

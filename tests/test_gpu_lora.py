@@ -131,3 +131,14 @@ def test_evict_and_async_prefetch_roundtrip():
     np.testing.assert_array_equal(before, after)
     assert eng.adapter_is_resident(a)
     eng.close()
+
+
+def test_multi_adapter_tensor_core_batch():
+    # 12 tokens: every projection on the tcgen05 GEMM, LoRA expansion in its epilogue
+    # (bias store, residual, and both halves of the gate|up pair), adapters mixed per token
+    ads = [(8, 8.0, ALL, 41, 0.05, 0.05), (4, 16.0, ALL, 42, 0.05, 0.05), (8, 16.0, 0x0F, 43, 0.05, 0.05)]
+    eng, m, ids = _setup(QWEN, ads, 12)
+    prompts = [oracle.fill_ids(f"tcp{b}", 3 + b % 5, b, 1000) for b in range(12)]
+    per_tok = [ids[b % 3] if b % 4 != 3 else -1 for b in range(12)]
+    _parity(eng, m, prompts, per_tok, steps=3)
+    eng.close()
