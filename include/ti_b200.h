@@ -167,6 +167,22 @@ typedef struct {
 
 typedef struct ti_engine ti_engine;
 
+/* ---- tensor parallelism (no counterpart in the reference, which runs one GPU;
+ * the split is the one the decode path's north star names: q/k/v by heads and
+ * gate/up by rows (column-parallel), o and down by input columns (row-parallel,
+ * NCCL all-reduce of fp32 partial sums), LM head by vocabulary rows (greedy id
+ * by an all-reduce max); embeddings and norms replicated). */
+typedef struct {
+    int tp, rank;
+    int nq, nkv, q0, kv0;   /* local q / kv heads and the first global index of each */
+    int inter, i0;          /* local intermediate rows of gate/up (= input columns of down) */
+    int vocab, v0;          /* local LM-head rows (vocabulary slice) */
+} ti_tp_shard;
+/* the shard of rank tp_rank of tp_size (host only; validates the split) */
+ti_status ti_tp_plan(const ti_model_desc* desc, int tp_size, int tp_rank, ti_tp_shard* out);
+/* a fresh 128-byte NCCL unique id (one rank creates it, all pass it in ti_engine_opts.nccl_id) */
+ti_status ti_nccl_unique_id(void* out128);
+
 ti_status ti_engine_create(const ti_model_desc* desc, const ti_engine_opts* opts, ti_engine** out);
 ti_status ti_engine_destroy(ti_engine* e);
 /* device bytes held by weights / KV pool / adapters / work buffers */

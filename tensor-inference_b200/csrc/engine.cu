@@ -30,6 +30,7 @@
 #include "common.cuh"
 #include "internal.h"
 #include "kernels.h"
+#include "tp.h"
 #include "synth.cuh"
 
 using namespace ti;
@@ -47,8 +48,8 @@ struct Slot {
     uint16_t* dst = nullptr;
     size_t ld = 0;
     bool linear = false;
-    // quantised linear weights (wf != kWBf16): rows of wrow_bytes(cols, wf) bytes
-    // starting at qdst (the window's first row); the whole row is held (c0 = 0)
+    // quantised linear weights (wf != kWBf16): rows of wrow_bytes(nc, wf) bytes
+    // starting at qdst (the window's first row); column windows are whole blocks
     int wf = kWBf16;
     uint8_t* qdst = nullptr;
     size_t rb = 0;
@@ -79,6 +80,12 @@ struct ti_engine {
     int dev = 0, sms = 148;
     int H = 0, nq = 0, nkv = 0, hd = 0, I = 0, V = 0, Vl = 0, qkv_rows = 0;
     int wf = kWBf16;  // format of the layers' linear weights
+    // tensor parallelism: this rank's shard (tp.tp == 1: single GPU), the NCCL
+    // communicator, fp32 partial sums of o / down, gathered logits for the host
+    ti_tp_shard tp{};
+    ncclComm_t comm = nullptr;
+    float* red = nullptr;
+    uint16_t* lgather = nullptr;
     cudaStream_t cap = nullptr;  // capture stream
 
     // device memory
@@ -172,6 +179,11 @@ void free_all(ti_engine* e) {
     for (auto& kv : e->graphs)
         if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
     e->graphs.clear();
+    // graphs holding NCCL calls are gone before the communicator
+    if (e->comm) {
+        if (const NcclApi* n = nccl_api()) n->CommDestroy(e->comm);
+        e->comm = nullptr;
+    }
     for (void* p : e->allocs) cudaFree(p);
     e->allocs.clear();
     if (e->h_desc) cudaFreeHost(e->h_desc);
@@ -209,14 +221,14 @@ void add_slot(ti_engine* e, const std::string& name, size_t rows, size_t cols, s
 
 // a linear weight: window rows [r0, r0+nr) of a [rows, cols] tensor at row `row`
 // of the layer buffer `base` (bf16 rows of cols elements, or quantised rows)
-void add_linear(ti_engine* e, const std::string& name, size_t rows, size_t cols, size_t r0, size_t nr,
-                uint8_t* base, size_t row) {
-    const size_t rb = wrow_bytes((int)cols, e->wf);
+void add_linear(ti_engine* e, const std::string& name, size_t rows, size_t cols, size_t r0, size_t nr, size_t c0,
+                size_t nc, uint8_t* base, size_t row) {
+    const size_t rb = wrow_bytes((int)nc, e->wf);
     if (e->wf == kWBf16) {
-        add_slot(e, name, rows, cols, r0, nr, 0, cols, reinterpret_cast<uint16_t*>(base + row * rb), cols, true);
+        add_slot(e, name, rows, cols, r0, nr, c0, nc, reinterpret_cast<uint16_t*>(base + row * rb), nc, true);
         return;
     }
-    add_slot(e, name, rows, cols, r0, nr, 0, cols, nullptr, cols, true);
+    add_slot(e, name, rows, cols, r0, nr, c0, nc, nullptr, nc, true);
     Slot& s = e->slots.back();
     s.wf = e->wf;
     s.qdst = base + row * rb;
@@ -251,8 +263,13 @@ ti_status validate_desc(const ti_model_desc* d, const ti_engine_opts* o) {
                  "engine: lora_proj_mask must name projections (TI_PROJ_*)");
     }
     const int tp = o->tp_size <= 0 ? 1 : o->tp_size;
-    TI_CHECK(tp == 1, TI_ERR_UNSUPPORTED, "engine: tensor parallelism is driven by ti_engine_create with tp_size 1 "
-                                          "in this build");
+    if (tp > 1) {
+        ti_tp_shard sh;
+        if (ti_status st = tp_plan_make(d, tp, o->tp_rank, &sh)) return st;
+        TI_CHECK(o->nccl_id, TI_ERR_INVALID, "engine: tp_size %d needs opts.nccl_id", tp);
+        TI_CHECK(o->max_adapters == 0, TI_ERR_UNSUPPORTED, "engine: LoRA adapters with tensor parallelism are not built yet");
+        TI_CHECK(nccl_api(), TI_ERR_UNSUPPORTED, "engine: tensor parallelism needs libnccl.so.2");
+    }
     return TI_OK;
 }
 
@@ -261,12 +278,13 @@ ti_status build(ti_engine* e) {
     DeviceGuard g(e->dev);
     e->sms = num_sms(e->dev);
     e->H = d.hidden;
-    e->nq = d.n_heads;
-    e->nkv = d.n_kv_heads;
+    if (ti_status st = tp_plan_make(&d, e->o.tp_size, e->o.tp_size > 1 ? e->o.tp_rank : 0, &e->tp)) return st;
+    e->nq = e->tp.nq;
+    e->nkv = e->tp.nkv;
     e->hd = d.head_dim;
-    e->I = d.intermediate;
+    e->I = e->tp.inter;
     e->V = d.vocab;
-    e->Vl = d.vocab;
+    e->Vl = e->tp.vocab;
     e->qkv_rows = (e->nq + 2 * e->nkv) * e->hd;
     e->wf = d.weight_format == TI_WFMT_Q4_0 ? kWQ4 : d.weight_format == TI_WFMT_Q8_0 ? kWQ8 : kWBf16;
     const int H = e->H, I = e->I, hd = e->hd, nq = e->nq, nkv = e->nkv;
@@ -280,7 +298,7 @@ ti_status build(ti_engine* e) {
     TI_CHECK(dalloc_t(e, &e->final_norm, H, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
     add_slot(e, "model.norm.weight", 1, H, 0, 1, 0, H, e->final_norm, H, false);
     TI_CHECK(dalloc_t(e, &e->lm_head, (size_t)e->Vl * H, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
-    add_slot(e, "lm_head.weight", e->V, H, 0, e->Vl, 0, H, e->lm_head, H, false);
+    add_slot(e, "lm_head.weight", e->V, H, e->tp.v0, e->Vl, 0, H, e->lm_head, H, false);
     e->layers.resize(d.n_layers);
     for (int i = 0; i < d.n_layers; ++i) {
         LayerW& l = e->layers[i];
@@ -298,21 +316,23 @@ ti_status build(ti_engine* e) {
                  "%s", ti_last_error());
         add_slot(e, p + "input_layernorm.weight", 1, H, 0, 1, 0, H, l.norm1, H, false);
         add_slot(e, p + "post_attention_layernorm.weight", 1, H, 0, 1, 0, H, l.norm2, H, false);
+        // local shard: q/k/v heads [q0, q0+nq) / [kv0, kv0+nkv), gate/up rows and
+        // down columns [i0, i0+I), o columns = the local q heads' width
         const size_t KW = (size_t)nkv * hd;
-        add_linear(e, p + "self_attn.q_proj.weight", QW, H, 0, QW, l.wqkv, 0);
-        add_linear(e, p + "self_attn.k_proj.weight", KW, H, 0, KW, l.wqkv, QW);
-        add_linear(e, p + "self_attn.v_proj.weight", KW, H, 0, KW, l.wqkv, QW + KW);
-        add_linear(e, p + "self_attn.o_proj.weight", H, QW, 0, H, l.wo, 0);
-        add_linear(e, p + "mlp.gate_proj.weight", I, H, 0, I, l.wgu, 0);
-        add_linear(e, p + "mlp.up_proj.weight", I, H, 0, I, l.wgu, I);
-        add_linear(e, p + "mlp.down_proj.weight", H, I, 0, H, l.wdown, 0);
+        const size_t QWg = (size_t)d.n_heads * hd, KWg = (size_t)d.n_kv_heads * hd, Ig = (size_t)d.intermediate;
+        const size_t q0 = (size_t)e->tp.q0 * hd, k0 = (size_t)e->tp.kv0 * hd, i0 = (size_t)e->tp.i0;
+        add_linear(e, p + "self_attn.q_proj.weight", QWg, H, q0, QW, 0, H, l.wqkv, 0);
+        add_linear(e, p + "self_attn.k_proj.weight", KWg, H, k0, KW, 0, H, l.wqkv, QW);
+        add_linear(e, p + "self_attn.v_proj.weight", KWg, H, k0, KW, 0, H, l.wqkv, QW + KW);
+        add_linear(e, p + "self_attn.o_proj.weight", H, QWg, 0, H, q0, QW, l.wo, 0);
+        add_linear(e, p + "mlp.gate_proj.weight", Ig, H, i0, I, 0, H, l.wgu, 0);
+        add_linear(e, p + "mlp.up_proj.weight", Ig, H, i0, I, 0, H, l.wgu, I);
+        add_linear(e, p + "mlp.down_proj.weight", H, Ig, 0, H, i0, I, l.wdown, 0);
         if (d.qkv_bias) {
             TI_CHECK(dalloc_t(e, &l.bqkv, e->qkv_rows, &e->bytes_w) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
-            add_slot(e, p + "self_attn.q_proj.bias", 1, QW, 0, 1, 0, QW, l.bqkv, QW, false);
-            add_slot(e, p + "self_attn.k_proj.bias", 1, (size_t)nkv * hd, 0, 1, 0, (size_t)nkv * hd, l.bqkv + QW,
-                     (size_t)nkv * hd, false);
-            add_slot(e, p + "self_attn.v_proj.bias", 1, (size_t)nkv * hd, 0, 1, 0, (size_t)nkv * hd,
-                     l.bqkv + QW + (size_t)nkv * hd, (size_t)nkv * hd, false);
+            add_slot(e, p + "self_attn.q_proj.bias", 1, QWg, 0, 1, q0, QW, l.bqkv, QW, false);
+            add_slot(e, p + "self_attn.k_proj.bias", 1, KWg, 0, 1, k0, KW, l.bqkv + QW, KW, false);
+            add_slot(e, p + "self_attn.v_proj.bias", 1, KWg, 0, 1, k0, KW, l.bqkv + QW + KW, KW, false);
         }
     }
     std::vector<float> fr(hd / 2);
@@ -357,6 +377,17 @@ ti_status build(ti_engine* e) {
     TI_CHECK(dalloc_t(e, &e->out, B + 1, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
     TI_CUDA(cudaMemset(e->out, 0, (B + 1) * 4));
     e->err = reinterpret_cast<int*>(e->out + B);
+    if (e->tp.tp > 1) {
+        TI_CHECK(dalloc_t(e, &e->red, (size_t)B * H, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+        TI_CHECK(dalloc_t(e, &e->lgather, (size_t)B * e->V, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
+                 ti_last_error());
+        const NcclApi* n = nccl_api();
+        ncclUniqueId id;
+        std::memcpy(&id, e->o.nccl_id, sizeof id);
+        const ncclResult_t r = n->CommInitRank(&e->comm, e->tp.tp, id, e->tp.rank);
+        TI_CHECK(r == ncclSuccess, TI_ERR_CUDA, "ncclCommInitRank (rank %d of %d): %s", e->tp.rank, e->tp.tp,
+                 n->GetErrorString(r));
+    }
     {
         const char* env = std::getenv("TI_TC_MIN_BATCH");
         e->tc_min = env ? std::atoi(env) : 8;
@@ -443,6 +474,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             c.nb = std::min(chunk, B - b0);
             c.x = a.x + (size_t)b0 * x_stride_elems;
             c.out = a.out + (size_t)b0 * out_stride;
+            if (a.partial) c.partial = a.partial + (size_t)b0 * out_stride;
             if (a.resid) c.resid = a.resid + (size_t)b0 * resid_stride;
             if (a.lora.adapter) {
                 c.lora.adapter = a.lora.adapter + b0;
@@ -479,6 +511,27 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         TcPlan plan;
         if (!tc_plan(a, epi, e->dev, e->tc_ws_floats, &plan, &why)) return fail(TI_ERR_UNSUPPORTED, "%s", why.c_str());
         TI_CUDA(tc_launch(a, epi, plan, e->tc_ws, e->tc_ctr, s, true));
+        if (launches) ++*launches;
+        return TI_OK;
+    };
+
+    // tensor parallelism: a row-parallel projection stores fp32 partial sums,
+    // NCCL sums them over the group, then out = bf16(resid + bf16(sum))
+    auto nccl_check = [&](ncclResult_t r, const char* what) -> ti_status {
+        if (r == ncclSuccess) return TI_OK;
+        return fail(TI_ERR_CUDA, "%s: %s", what, nccl_api()->GetErrorString(r));
+    };
+    auto row_parallel = [&](GemvArgs a, int x_stride_elems, uint16_t* out, const uint16_t* resid) -> ti_status {
+        a.partial = e->red;
+        a.out = nullptr;
+        a.out_stride = H;
+        a.resid = nullptr;
+        if (ti_status st = gemm(a, kEpiStore, x_stride_elems, H, 0)) return st;
+        if (ti_status st = nccl_check(nccl_api()->AllReduce(e->red, e->red, (size_t)B * H, ncclFloat32, ncclSum,
+                                                            e->comm, s),
+                                      "ncclAllReduce"))
+            return st;
+        TI_CUDA(tp_resid_launch(e->red, resid, out, B, H, s, true));
         if (launches) ++*launches;
         return TI_OK;
     };
@@ -532,7 +585,17 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         lm.chain_pos = e->dd_pos();
         lm.err = e->err;
         set_next(lm, e->layers[0].wqkv, e->qkv_rows, H, 1);
-        return gemm(lm, kEpiLmHead, H, e->Vl, 0);
+        if (e->tp.tp == 1) return gemm(lm, kEpiLmHead, H, e->Vl, 0);
+        // vocabulary-parallel: local keys carry global indices; max over the group
+        lm.key_offset = e->tp.v0;
+        lm.publish = 0;
+        if (ti_status st = gemm(lm, kEpiLmHead, H, e->Vl, 0)) return st;
+        if (ti_status st = nccl_check(
+                nccl_api()->AllReduce(e->amax, e->amax, (size_t)B, ncclUint64, ncclMax, e->comm, s), "ncclAllReduce"))
+            return st;
+        TI_CUDA(tp_ids_launch(e->amax, B, e->out, e->dd_tokens(), e->dd_pos(), s, true));
+        if (launches) ++*launches;
+        return TI_OK;
     }
     TI_CHECK(li >= 0 && li < d.n_layers, TI_ERR_INVALID, "layer %d out of range", li);
     const LayerW& l = e->layers[li];
@@ -646,6 +709,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
                 if (ti_status st = shrink(1, e->attn, QW, nullptr)) return st;
                 set_lora(ov, 1);
             }
+            if (e->tp.tp > 1) return row_parallel(ov, QW, e->res1, e->hidden);
             return gemm(ov, kEpiResid, QW, H, H);
         }
         case kKGateUp: {
@@ -689,6 +753,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
                 if (ti_status st = shrink(3, e->act, I, nullptr)) return st;
                 set_lora(dn, 3);
             }
+            if (e->tp.tp > 1) return row_parallel(dn, I, e->hidden, e->res1);
             return gemm(dn, kEpiResid, I, H, H);
         }
         default: return fail(TI_ERR_INVALID, "unknown kernel kind %d", kind);
@@ -826,15 +891,32 @@ ti_status run_step(ti_engine* e, int B, const int32_t* seq_ids, const int32_t* t
     TI_CUDA(cudaMemcpyAsync(e->d_desc, h, (size_t)e->desc_ints * 4, cudaMemcpyHostToDevice, stream));
     TI_CUDA(cudaGraphLaunch(g->exec, stream));
     TI_CUDA(cudaMemcpyAsync(e->h_out, e->out, (size_t)(MB + 1) * 4, cudaMemcpyDeviceToHost, stream));
-    if (logits_out && logits_mode == TI_LOGITS_BF16)
-        TI_CUDA(cudaMemcpyAsync(logits_out, e->logits, (size_t)B * e->Vl * 2, cudaMemcpyDeviceToHost, stream));
+    // host logits [B, V] bf16: the local rows, or every rank's vocabulary slice gathered
+    std::vector<uint16_t> lg;
+    if (logits_out && logits_mode != TI_LOGITS_NONE) {
+        lg.resize((size_t)B * e->V);
+        if (e->tp.tp == 1) {
+            TI_CUDA(cudaMemcpyAsync(lg.data(), e->logits, lg.size() * 2, cudaMemcpyDeviceToHost, stream));
+        } else {
+            const ncclResult_t r = nccl_api()->AllGather(e->logits, e->lgather, (size_t)B * e->Vl, ncclBfloat16, e->comm,
+                                                         stream);
+            TI_CHECK(r == ncclSuccess, TI_ERR_CUDA, "ncclAllGather: %s", nccl_api()->GetErrorString(r));
+            std::vector<uint16_t> gat(lg.size());
+            TI_CUDA(cudaMemcpyAsync(gat.data(), e->lgather, gat.size() * 2, cudaMemcpyDeviceToHost, stream));
+            TI_CUDA(cudaStreamSynchronize(stream));
+            // gathered [rank][b][j] -> [b][rank * Vl + j]
+            for (int r2 = 0; r2 < e->tp.tp; ++r2)
+                for (int b = 0; b < B; ++b)
+                    std::memcpy(&lg[(size_t)b * e->V + (size_t)r2 * e->Vl], &gat[((size_t)r2 * B + b) * e->Vl],
+                                (size_t)e->Vl * 2);
+        }
+    }
     TI_CUDA(cudaStreamSynchronize(stream));
+    if (logits_out && logits_mode == TI_LOGITS_BF16) std::memcpy(logits_out, lg.data(), lg.size() * 2);
     if (logits_out && logits_mode == TI_LOGITS_F32) {
-        std::vector<uint16_t> tmp((size_t)B * e->Vl);
-        TI_CUDA(cudaMemcpy(tmp.data(), e->logits, tmp.size() * 2, cudaMemcpyDeviceToHost));
         float* f = reinterpret_cast<float*>(logits_out);
-        for (size_t i = 0; i < tmp.size(); ++i) {
-            uint32_t u = (uint32_t)tmp[i] << 16;
+        for (size_t i = 0; i < lg.size(); ++i) {
+            uint32_t u = (uint32_t)lg[i] << 16;
             std::memcpy(&f[i], &u, 4);
         }
     }
@@ -904,17 +986,20 @@ static size_t gguf_row_bytes(int K, int wf) { return (size_t)K / 32 * (wf == kWQ
 // device (the GGUF definition, bit for bit), GGUF blocks are repacked.
 static ti_status load_quantized(ti_engine* e, const Slot& s, const char* name, int dtype, const void* host,
                                 size_t bytes) {
-    const int K = (int)s.cols;
+    const int K = (int)s.nc;  // local row length (a column window of whole blocks under TP)
     const int gguf = s.wf == kWQ4 ? TI_DTYPE_Q4_0 : TI_DTYPE_Q8_0;
     TI_CHECK(dtype == TI_DTYPE_BF16 || dtype == gguf, TI_ERR_UNSUPPORTED,
              "tensor '%s': dtype %d (bf16 or this engine's GGUF block type expected)", name, dtype);
-    const size_t in_row = dtype == TI_DTYPE_BF16 ? (size_t)K * 2 : gguf_row_bytes(K, s.wf);
+    const bool bf = dtype == TI_DTYPE_BF16;
+    const size_t in_row = bf ? s.cols * 2 : gguf_row_bytes((int)s.cols, s.wf);
+    const size_t win = bf ? (size_t)K * 2 : gguf_row_bytes(K, s.wf);
+    const size_t win0 = bf ? s.c0 * 2 : gguf_row_bytes((int)s.c0, s.wf);
     TI_CHECK(bytes == s.rows * in_row, TI_ERR_INVALID, "tensor '%s': %zu bytes, expected %zu", name, bytes,
              s.rows * in_row);
     void* tmp = nullptr;
-    TI_CUDA(cudaMalloc(&tmp, s.nr * in_row + 16));
-    cudaError_t err = cudaMemcpy(tmp, reinterpret_cast<const uint8_t*>(host) + s.r0 * in_row, s.nr * in_row,
-                                 cudaMemcpyHostToDevice);
+    TI_CUDA(cudaMalloc(&tmp, s.nr * win + 16));
+    cudaError_t err = cudaMemcpy2D(tmp, win, reinterpret_cast<const uint8_t*>(host) + s.r0 * in_row + win0, in_row,
+                                   win, s.nr, cudaMemcpyHostToDevice);
     if (err == cudaSuccess)
         err = dtype == TI_DTYPE_BF16
                   ? quantize_rows_launch(reinterpret_cast<const uint16_t*>(tmp), (int)s.nr, K, K, s.qdst, s.rb, s.wf, 0)
@@ -952,13 +1037,13 @@ ti_status ti_engine_read_tensor(ti_engine* e, const char* name, void* host, size
     const Slot& s = e->slots[it->second];
     if (s.wf != kWBf16) {
         // quantised linear weight: the window's rows as GGUF blocks
-        const size_t gb = gguf_row_bytes((int)s.cols, s.wf);
+        const size_t gb = gguf_row_bytes((int)s.nc, s.wf);
         TI_CHECK(bytes == s.nr * gb, TI_ERR_INVALID, "tensor '%s': %zu bytes, local window is %zu GGUF bytes", name,
                  bytes, s.nr * gb);
         DeviceGuard g(e->dev);
         std::vector<uint8_t> rows(s.nr * s.rb);
         TI_CUDA(cudaMemcpy(rows.data(), s.qdst, rows.size(), cudaMemcpyDeviceToHost));
-        gguf_from_rows(rows.data(), (int)s.nr, (int)s.cols, s.rb, s.wf, reinterpret_cast<uint8_t*>(host));
+        gguf_from_rows(rows.data(), (int)s.nr, (int)s.nc, s.rb, s.wf, reinterpret_cast<uint8_t*>(host));
         return TI_OK;
     }
     TI_CHECK(bytes == s.nr * s.nc * 2, TI_ERR_INVALID, "tensor '%s': %zu bytes, local window is %zu", name, bytes,
@@ -976,7 +1061,7 @@ ti_status ti_engine_init_synthetic(ti_engine* e, uint64_t seed, float std_) {
     // quantised slots: the bf16 values the other formats get, then quantised
     size_t tmp_elems = 0;
     for (const Slot& s : e->slots)
-        if (s.wf != kWBf16) tmp_elems = std::max(tmp_elems, s.nr * s.cols);
+        if (s.wf != kWBf16) tmp_elems = std::max(tmp_elems, s.nr * s.nc);
     uint16_t* tmp = nullptr;
     if (tmp_elems) TI_CUDA(cudaMalloc(&tmp, tmp_elems * 2));
     cudaError_t err = cudaSuccess;
@@ -986,10 +1071,10 @@ ti_status ti_engine_init_synthetic(ti_engine* e, uint64_t seed, float std_) {
             err = synth_bf16_launch(s.dst, s.nr, s.nc, s.ld, s.r0, s.c0, s.cols, seed, fnv1a(s.name.c_str()), c,
                                     (cudaStream_t)0);
         } else {
-            err = synth_bf16_launch(tmp, s.nr, s.cols, s.cols, s.r0, 0, s.cols, seed, fnv1a(s.name.c_str()), c,
+            err = synth_bf16_launch(tmp, s.nr, s.nc, s.nc, s.r0, s.c0, s.cols, seed, fnv1a(s.name.c_str()), c,
                                     (cudaStream_t)0);
             if (err == cudaSuccess)
-                err = quantize_rows_launch(tmp, (int)s.nr, (int)s.cols, s.cols, s.qdst, s.rb, s.wf, (cudaStream_t)0);
+                err = quantize_rows_launch(tmp, (int)s.nr, (int)s.nc, s.nc, s.qdst, s.rb, s.wf, (cudaStream_t)0);
         }
     }
     if (err == cudaSuccess) err = cudaDeviceSynchronize();

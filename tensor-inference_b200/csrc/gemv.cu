@@ -284,7 +284,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int w = 0; w < kConsumerWarps; ++w) sum += pv[w];
                     accu[u] = sum;
                 }
-                if (EPI == kEpiStore) {
+                if (EPI == kEpiStore && a.partial) {
+                    a.partial[(size_t)b * a.out_stride + n] = accu[0];
+                } else if (EPI == kEpiStore) {
                     float v = round_bf(accu[0]);
                     if (a.bias) v = round_bf(v + __uint_as_float((uint32_t)e_bias[n - u0] << 16));
                     if (ad >= 0) {
@@ -311,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float v = accu[0];
                     reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + n] = f2bf(v);
                     if (a.logits_f32) a.logits_f32[(size_t)b * a.out_stride + n] = v;
-                    const unsigned long long key = argmax_key(v, (uint32_t)n);
+                    const unsigned long long key = argmax_key(v, (uint32_t)(n + a.key_offset));
 #pragma unroll
                     for (int bb = 0; bb < NB; ++bb)
                         if (bb == b && key > best[bb]) best[bb] = key;
@@ -336,7 +338,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (best[b]) atomicMax(&a.amax[b], best[b]);
                 __threadfence();
                 const unsigned int ticket = atomicAdd(a.done, 1u);
-                if (ticket == gridDim.x - 1) {
+                if (ticket == gridDim.x - 1 && !a.publish) {
+                    atomicExch(a.done, 0u);  // keys stay for the cross-rank reduction
+                } else if (ticket == gridDim.x - 1) {
                     __threadfence();
                     for (int b = 0; b < a.nb && b < NB; ++b) {
                         const unsigned long long key = atomicExch(&a.amax[b], 0ull);

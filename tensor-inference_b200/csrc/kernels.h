@@ -89,6 +89,11 @@ struct GemvArgs {
     int32_t* chain_tokens = nullptr;     // [nb] next-step input tokens (optional)
     int32_t* chain_pos = nullptr;        // [nb] positions incremented after the step (optional)
     float* logits_f32 = nullptr;         // [nb, out_stride] optional fp32 logits
+    int key_offset = 0;                  // LM head: global index of row 0 (vocabulary-parallel shard)
+    int publish = 1;                     // LM head: 0 = leave the keys in amax (reduced across ranks later)
+    // kEpiStore: when set, the unrounded fp32 sums go here instead ([nb, out_stride]);
+    // the row-parallel half of tensor parallelism all-reduces them
+    float* partial = nullptr;
     GemvLora lora;
     // L2 warm-up of the next GEMV of the step: once this CTA's producer has
     // issued its own copies it prefetches the first `next_bytes` of the rows the
@@ -173,6 +178,14 @@ int attn_splits(int nb, int nkv, int max_len, int sms, int* max_chunk);
 // scratch floats / counters one launch needs: part_o + part_ml, and nb*nkv counters
 size_t attn_scratch_floats(int nb, int nq, int nkv, int hd, int n_splits);
 cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s, bool pdl);
+
+// ----------------------------------------------------------------- tensor-parallel glue
+// out[b, n] = bf16(resid[b, n] + bf16(sum[b, n])) after the all-reduce of a row-parallel projection
+cudaError_t tp_resid_launch(const float* sum, const uint16_t* resid, uint16_t* out, int nb, int H, cudaStream_t s,
+                            bool pdl);
+// greedy ids from the all-reduced argmax keys; re-arms the keys (cf. the LM-head epilogue)
+cudaError_t tp_ids_launch(unsigned long long* amax, int nb, int32_t* out_ids, int32_t* chain_tokens,
+                          int32_t* chain_pos, cudaStream_t s, bool pdl);
 
 // ----------------------------------------------------------------- small kernels
 struct EmbedArgs {

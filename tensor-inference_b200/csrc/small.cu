@@ -1,4 +1,6 @@
 // small.cu — launch helper, embedding gather, synthetic initialisers.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "synth.cuh"
@@ -92,6 +94,46 @@ cudaError_t synth_f32_launch(float* dst, size_t n, uint64_t seed, uint64_t name_
     const uint64_t key = mix64(seed ^ name_hash);
     k_synth_f32<<<4 * 148, 256, 0, s>>>(dst, n, key, scale_c);
     return cudaGetLastError();
+}
+
+
+// ---- tensor-parallel glue
+__global__ void k_tp_resid(const float* __restrict__ sum, const uint16_t* __restrict__ resid,
+                           uint16_t* __restrict__ out, int n) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) pdl_trigger();
+    pdl_wait();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float r = __uint_as_float((uint32_t)resid[i] << 16);
+        out[i] = __bfloat16_as_ushort(f2bf(r + round_bf(sum[i])));  // ops.cu:361-381 on the bf16 projection
+    }
+}
+
+cudaError_t tp_resid_launch(const float* sum, const uint16_t* resid, uint16_t* out, int nb, int H, cudaStream_t s,
+                            bool pdl) {
+    int n = nb * H;
+    void* params[] = {&sum, &resid, &out, &n};
+    const int grid = std::min((n + 255) / 256, 1024);
+    return launch_pdl(reinterpret_cast<const void*>(&k_tp_resid), dim3(grid), dim3(256), 0, s, params, pdl);
+}
+
+__global__ void k_tp_ids(unsigned long long* amax, int nb, int32_t* out_ids, int32_t* chain_tokens,
+                         int32_t* chain_pos) {
+    if (threadIdx.x == 0) pdl_trigger();
+    pdl_wait();
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+        const unsigned long long key = amax[b];
+        amax[b] = 0ull;
+        const int32_t id = (int32_t)(~(uint32_t)(key & 0xffffffffull));
+        out_ids[b] = id;
+        if (chain_tokens) chain_tokens[b] = id;
+        if (chain_pos) chain_pos[b] += 1;
+    }
+}
+
+cudaError_t tp_ids_launch(unsigned long long* amax, int nb, int32_t* out_ids, int32_t* chain_tokens,
+                          int32_t* chain_pos, cudaStream_t s, bool pdl) {
+    void* params[] = {&amax, &nb, &out_ids, &chain_tokens, &chain_pos};
+    return launch_pdl(reinterpret_cast<const void*>(&k_tp_ids), dim3(1), dim3(256), 0, s, params, pdl);
 }
 
 }  // namespace ti

@@ -139,6 +139,8 @@ struct TcKernelArgs {
     int32_t* chain_tokens;
     int32_t* chain_pos;
     float* logits_f32;
+    int key_offset, publish;
+    float* partial;
     float* ws;               // [grid][2][np][128] fp32 partials of tiles shared between CTAs
     unsigned int* tile_ctr;  // [tiles], zero; reset by each shared tile's last unit
     GemvLora lora;           // per-token LoRA expansion (adapter == nullptr: off)
@@ -410,6 +412,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         }
                     }
                     named_bar(1, 128);
+                } else if (EPI == kEpiStore && a.partial) {
+                    if (row_ok)
+                        for (int i = 0; i < 32; ++i) {
+                            const int b = c * 32 + i;
+                            if (b >= a.nb) break;
+                            a.partial[(size_t)b * a.out_stride + n] = v[i];
+                        }
                 } else if (EPI == kEpiStore) {
                     if (row_ok) {
                         const float bv = a.bias ? __uint_as_float((uint32_t)a.bias[n] << 16) : 0.f;
@@ -445,7 +454,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         if (row_ok) {
                             reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + n] = f2bf(v[i]);
                             if (a.logits_f32) a.logits_f32[(size_t)b * a.out_stride + n] = v[i];
-                            key = argmax_key(v[i], (uint32_t)n);
+                            key = argmax_key(v[i], (uint32_t)(n + a.key_offset));
                         }
 #pragma unroll
                         for (int o = 16; o > 0; o >>= 1) {
@@ -522,7 +531,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             named_bar(1, 128);
             if (et == 0) {
                 const unsigned int ticket = atomicAdd(a.done, 1u);
-                if (ticket == gridDim.x - 1) {
+                if (ticket == gridDim.x - 1 && !a.publish) {
+                    atomicExch(a.done, 0u);  // keys stay for the cross-rank reduction
+                } else if (ticket == gridDim.x - 1) {
                     __threadfence();
                     for (int b = 0; b < a.nb; ++b) {
                         const unsigned long long key = atomicExch(&a.amax[b], 0ull);
@@ -754,6 +765,9 @@ cudaError_t tc_launch(const GemvArgs& g, int epi, const TcPlan& p, float* ws, un
     a.chain_tokens = g.chain_tokens;
     a.chain_pos = g.chain_pos;
     a.logits_f32 = g.logits_f32;
+    a.key_offset = g.key_offset;
+    a.publish = g.publish;
+    a.partial = g.partial;
     a.ws = ws;
     a.tile_ctr = tile_ctr;
     a.lora = g.lora;

@@ -53,7 +53,14 @@ class EngineOpts(C.Structure):
 
 _lib = None
 
+class TpShard(C.Structure):
+    _fields_ = [("tp", C.c_int), ("rank", C.c_int), ("nq", C.c_int), ("nkv", C.c_int), ("q0", C.c_int),
+                ("kv0", C.c_int), ("inter", C.c_int), ("i0", C.c_int), ("vocab", C.c_int), ("v0", C.c_int)]
+
+
 _SIGS = {
+    "ti_nccl_unique_id": (C.c_int, [C.c_void_p]),
+    "ti_tp_plan": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "ti_last_error": (C.c_char_p, []),
     "ti_version": (C.c_int, []),
     "ti_device_count": (C.c_int, [C.POINTER(C.c_int)]),
@@ -265,6 +272,20 @@ def algorithmic_bytes_per_step(desc, batch, ctx_total, lora_bytes=0):
     wbytes = bpe * desc.n_layers * per_layer + 2 * desc.vocab * H
     kv = ctx_total * desc.n_layers * 2 * KW * 2
     return wbytes + kv + lora_bytes
+
+
+def nccl_unique_id():
+    """128-byte NCCL unique id for a tensor-parallel group (one rank makes it, all use it)"""
+    buf = C.create_string_buffer(128)
+    check(lib().ti_nccl_unique_id(buf))
+    return buf.raw
+
+
+def tp_plan(desc, tp, rank):
+    """the shard of `rank` in a group of `tp` (host only)"""
+    sh = TpShard()
+    check(lib().ti_tp_plan(C.byref(desc), tp, rank, C.byref(sh)))
+    return {k: getattr(sh, k) for k, _ in TpShard._fields_}
 
 
 # ---------------------------------------------------------------- engine

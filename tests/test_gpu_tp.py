@@ -1,0 +1,141 @@
+"""Tensor parallelism (TP=2) against the CPU oracle, on 2 GPUs.
+
+The parent runs the oracle first (teacher-forced: each step feeds the oracle's
+greedy token) and hands the token schedule to two child processes, one per
+GPU and rank, which run the same steps through TP engines that share an NCCL
+communicator.  Checks: both ranks agree on every greedy id; rank 0's gathered
+logits are within the bf16 (2e-2) / Q4_0 (5e-2) tolerance of the oracle's; ids
+equal the oracle's up to recorded near-ties.  Skipped on a box with one GPU.
+NVLS is off in the children (a rank that fails an assertion leaves while its
+peer may still be in a collective)."""
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+import oracle
+import ti_b200 as ti
+from gpu_util import rel_err
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+
+SMALL = dict(arch=ti.ARCH_LLAMA, hidden=256, n_layers=2, n_heads=4, n_kv_heads=2, head_dim=64, intermediate=512,
+             vocab=1000, rms_eps=1e-5, rope_theta=10000.0)
+
+
+def _need(n):
+    import torch
+
+    if torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs")
+
+
+def _oracle_schedule(kw, prompts, steps, seed, std):
+    m = oracle.Model(**kw)
+    m.init_synthetic(seed, std)
+    feeds, ref = [], []
+    seqs = [m.new_seq(128) for _ in prompts]
+    last = []
+    for s, p in zip(seqs, prompts):
+        _, lf = s.forward(p)
+        last.append(lf)
+    ref.append(np.stack(last))
+    feed = [int(np.argmax(lf)) for lf in last]
+    for _ in range(steps):
+        feeds.append(list(feed))
+        rows = [s.forward([t])[1] for s, t in zip(seqs, feed)]
+        ref.append(np.stack(rows))
+        feed = [int(np.argmax(r)) for r in rows]
+    return feeds, ref
+
+
+def _rank(rank, world, nid, kw, prompts, feeds, seed, std, q):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    sys.path.insert(0, os.path.join(ROOT, "tensor-inference_b200"))
+    try:
+        import ti_b200 as tl
+
+        B = len(prompts)
+        eng = tl.Engine(tl.model_desc(**kw), device=rank, max_batch=B, max_seqs=B, max_seq_len=128, tp_size=world,
+                        tp_rank=rank, nccl_id=nid)
+        eng.init_synthetic(seed, std)
+        sids = [eng.seq_create() for _ in prompts]
+        out_ids, out_logits = [], []
+        ids0, lg0 = [], []
+        for sid, p in zip(sids, prompts):
+            nxt, lb = eng.prefill(sid, p, logits=tl.LOGITS_BF16)
+            ids0.append(int(nxt))
+            lg0.append(lb)
+        out_ids.append(ids0)
+        out_logits.append(np.stack(lg0))
+        for f in feeds:
+            nxt, lb = eng.decode(sids, f, logits=tl.LOGITS_BF16)
+            out_ids.append([int(x) for x in nxt])
+            out_logits.append(lb)
+        eng.check()
+        eng.close()
+        q.put((rank, out_ids, out_logits if rank == 0 else None))
+    except BaseException as e:
+        q.put((rank, "error", repr(e)))
+        os._exit(1)
+
+
+def _run_tp(kw, prompts, steps, tol, seed=0, std=0.02, world=2):
+    _need(world)
+    feeds, ref = _oracle_schedule(kw, prompts, steps, seed, std)
+    nid = ti.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, world, nid, kw, prompts, feeds, seed, std, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(world):
+            r = q.get(timeout=600)
+            assert r[1] != "error", r
+            res[r[0]] = r
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    ids = [res[r][1] for r in range(world)]
+    assert all(i == ids[0] for i in ids), "ranks disagree on greedy ids"
+    flips = 0
+    for step, (lb, lf) in enumerate(zip(res[0][2], ref)):
+        for b in range(len(prompts)):
+            g = oracle.bf16_to_f32(lb[b])
+            err = rel_err(g, lf[b])
+            assert err <= tol, (step, b, err)
+            if ids[0][step][b] != int(np.argmax(lf[b])):
+                s = np.sort(lf[b])
+                assert s[-1] - s[-2] <= tol * np.abs(lf[b]).max(), (step, b)
+                flips += 1
+    assert flips <= max(1, (steps + 1) * len(prompts) // 10)
+
+
+def test_tp2_llama_small_ragged():
+    prompts = [oracle.fill_ids(f"tp{b}", n, b, SMALL["vocab"]) for b, n in enumerate((5, 11, 3))]
+    _run_tp(SMALL, prompts, steps=4, tol=2e-2)
+
+
+def test_tp2_tensor_core_batch16():
+    prompts = [oracle.fill_ids(f"tq{b}", 2 + b % 4, b, SMALL["vocab"]) for b in range(16)]
+    _run_tp(SMALL, prompts, steps=2, tol=2e-2)
+
+
+def test_tp2_q4_0():
+    kw = dict(SMALL, hidden=512, n_heads=8, intermediate=1024, weight_format=ti.WFMT_Q4_0)
+    prompts = [oracle.fill_ids(f"tz{b}", n, b, kw["vocab"]) for b, n in enumerate((4, 7))]
+    _run_tp(kw, prompts, steps=3, tol=5e-2)
+
+
+def test_tp2_llama3_8b_shapes():
+    kw = dict(ti.PRESETS["llama3_8b"], n_layers=2)
+    _run_tp(kw, [oracle.fill_ids("t8", 6, 1, kw["vocab"])], steps=2, tol=2e-2)
