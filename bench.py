@@ -141,8 +141,9 @@ def run_reference(args, rank, world):
     cb = cpu_baseline()
     line = {"metric": METRIC, "impl": "reference", "value": cb["value"], "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / cb["value"], "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "Llama-3-8B-shape bf16 greedy decode, batch 1, CPU", "batch": 1},
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "Llama-3-8B-shape bf16 greedy decode, batch 1, 512-token prompt (CPU oracle)",
+                       "batch": 1},
             "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -160,7 +161,7 @@ def prefill_lockstep(eng, sids, prompts, adapters=None):
 
 
 def measure_batch(ti, torch, eng, B, steps, warmup, stream, peak, measure_e2e=True, prompt=None, adapters=None,
-                  lora_bytes=0):
+                  lora_bytes=0, world=1):
     import numpy as np
 
     desc = eng.desc
@@ -193,8 +194,9 @@ def measure_batch(ti, torch, eng, B, steps, warmup, stream, peak, measure_e2e=Tr
     step_bytes = ti.algorithmic_bytes_per_step(desc, B, B * ctx_avg, lora_bytes)
     res = {"batch": B, "ms_per_step": ms, "tok_s": B * 1e3 / ms, "ctx_avg": ctx_avg, "prefill_s": t_prefill,
            "step_bytes": step_bytes, "step_gbs": step_bytes / (ms * 1e-3) / 1e9}
-    res["step_frac_measured"] = res["step_gbs"] / peak
-    res["step_frac_nominal"] = res["step_gbs"] / NOMINAL_HBM_GBS
+    # tensor parallel: the step's bytes are spread over `world` GPUs' HBM
+    res["step_frac_measured"] = res["step_gbs"] / (peak * world)
+    res["step_frac_nominal"] = res["step_gbs"] / (NOMINAL_HBM_GBS * world)
 
     # ---- end to end through the C ABI with host buffers
     if measure_e2e:
@@ -246,7 +248,8 @@ def kernel_roofline(ti, torch, eng, stream, peak, iters=64):
     timed alone with CUDA events on its launch stream, cycling layers so every
     launch streams its weights from HBM"""
     desc = eng.desc
-    nbytes = 2 * desc.intermediate * desc.hidden * 2 + desc.hidden * 2 * 2
+    tp = max(1, eng.opts.tp_size)
+    nbytes = 2 * (desc.intermediate // tp) * desc.hidden * 2 + desc.hidden * 2 * 2  # this rank's shard
     for i in range(4):
         eng.launch_kernel(ti.KERNEL_GATEUP, i % desc.n_layers, 1, stream)
     torch.cuda.synchronize()
@@ -362,46 +365,61 @@ def run_ours(args, rank, world):
     stream = ts.cuda_stream
     max_b = 32 if args.b32 else 1
     desc = ti.model_desc(**ti.PRESETS["llama3_8b"])
+    nid = None
+    if world > 1:
+        # tensor parallel over the job's GPUs: rank 0 makes the NCCL id, all ranks share it
+        import torch.distributed as dist
+
+        box = [ti.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        nid = box[0]
     eng = ti.Engine(desc, device=dev, max_batch=max_b, max_seqs=max_b,
-                    max_seq_len=PROMPT + 2 * (args.warmup + args.steps) + 64)
+                    max_seq_len=PROMPT + 2 * (args.warmup + args.steps) + 64, tp_size=world, tp_rank=rank,
+                    nccl_id=nid)
     eng.init_synthetic(0, 0.02)
     launches = eng.launches_per_step(1)
 
     with ClockSampler(dev) as clk:
-        r1 = measure_batch(ti, torch, eng, 1, args.steps, args.warmup, stream, peak)
+        r1 = measure_batch(ti, torch, eng, 1, args.steps, args.warmup, stream, peak, world=world)
     roof = kernel_roofline(ti, torch, eng, stream, peak)
     pkm = measure_pkm(ti, torch, stream) if world == 1 else None
     r32 = None
     if args.b32:
         r32 = measure_batch(ti, torch, eng, 32, max(2, args.steps // 4), min(args.warmup, 3), stream, peak,
-                            measure_e2e=False)
+                            measure_e2e=False, world=world)
     qwen = None
     if args.qwen and world == 1:
         eng.close()  # the 8B engine's 15 GB is not needed for the Qwen legs
         qwen = {name: measure_qwen_lora(ti, torch, stream, peak, wf, max(4, args.steps // 4), 3, dev)
                 for name, wf in (("bf16", ti.WFMT_BF16), ("q4_0", ti.WFMT_Q4_0))}
 
-    # every rank runs its own replica; the job's time is the slowest rank's
+    # the ranks of the tensor-parallel group step together; the job's time is the slowest rank's
     ms = r1["ms_per_step"]
     e2e_ms = r1["e2e"]["ms_per_step"]
+    ms32 = r32["ms_per_step"] if r32 else 0.0
     if world > 1:
         import torch.distributed as dist
 
-        t = torch.tensor([ms, e2e_ms], device="cuda")
+        t = torch.tensor([ms, e2e_ms, ms32], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms = float(t[0]), float(t[1])
+        ms, e2e_ms, ms32 = float(t[0]), float(t[1]), float(t[2])
+        if r32:
+            r32["ms_per_step"] = ms32
+            r32["tok_s"] = 32 * 1e3 / ms32
+            r32["step_gbs"] = r32["step_bytes"] / (ms32 * 1e-3) / 1e9
+            r32["step_frac_measured"] = r32["step_gbs"] / (peak * world)
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline()
     if rank == 0:
         line = {
-            "metric": METRIC, "value": round(world * 1e3 / ms, 2), "unit": "tok/s", "n_gpus": world,
+            "metric": METRIC, "value": round(1e3 / ms, 2), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,0.02) bf16 weights, uniform random 512-token prompts)",
-            "config": {"workload": "Llama-3-8B-shape bf16 greedy decode, batch 1 per GPU, 512-token prompt",
+            "config": {"workload": "Llama-3-8B-shape bf16 greedy decode, batch 1, 512-token prompt",
                        "batch": 1, "prompt": PROMPT, "ctx_avg": r1["ctx_avg"],
-                       "parallelism": "single" if world == 1 else f"{world} independent replicas",
+                       "parallelism": "single" if world == 1 else f"tp{world} (NCCL all-reduce after o/down)",
                        "l2": "weights (15 GB) >> L2 (126 MB): every step streams from HBM; no flush"},
             "e2e": {k: (round(v, 3) if isinstance(v, float) else v) for k, v in r1["e2e"].items()},
             "roofline": roof,
@@ -413,7 +431,8 @@ def run_ours(args, rank, world):
             "clocks": clk.summary(),
         }
         if world > 1:
-            line["e2e"]["value"] = round(world * 1e3 / e2e_ms, 2)
+            line["e2e"]["value"] = round(1e3 / e2e_ms, 2)
+            line["e2e"]["ms_per_step"] = round(e2e_ms, 3)
         if r32:
             line["b32"] = {"tok_s": round(r32["tok_s"], 1), "ms_per_step": round(r32["ms_per_step"], 3),
                            "step_gbs": round(r32["step_gbs"], 1), "frac_measured": round(r32["step_frac_measured"], 4),
