@@ -125,6 +125,29 @@ TI_DEVICE_INLINE void tma_load_2d(void* dst, const CUtensorMap* map, int x, int 
         : "memory");
 }
 
+// ------------------------------------------------------------------ system-scope flags (peer memory)
+TI_DEVICE_INLINE unsigned int ld_acquire_sys(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+TI_DEVICE_INLINE void st_release_sys(unsigned int* p, unsigned int v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded wait until *p has reached `seq` (wrap-safe); false and err_bit on timeout.
+TI_DEVICE_INLINE bool wait_seq_sys(const unsigned int* p, unsigned int seq, int* err, int err_bit) {
+    if ((int)(ld_acquire_sys(p) - seq) >= 0) return true;
+    // an earlier wait of this step already gave up: do not wait again
+    if (err && (*reinterpret_cast<volatile int*>(err) & err_bit)) return false;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        if ((int)(ld_acquire_sys(p) - seq) >= 0) return true;
+        if ((i & 63u) == 63u && global_ns() - t0 > kWaitNs) break;
+    }
+    if (err) atomicOr(err, err_bit);
+    return false;
+}
+
 // ------------------------------------------------------------------ loads
 TI_DEVICE_INLINE uint4 lds128(const void* p) {
     uint4 v;

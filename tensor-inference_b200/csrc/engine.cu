@@ -86,6 +86,13 @@ struct ti_engine {
     ncclComm_t comm = nullptr;
     float* red = nullptr;
     uint16_t* lgather = nullptr;
+    // all-reduce through peer memory (default; TI_TP_ALLREDUCE=nccl selects NCCL):
+    // one region per rank, mapped into every peer by CUDA IPC, same offsets on all ranks
+    bool peer_ar = false;
+    uint8_t* par = nullptr;
+    std::vector<uint8_t*> peer;  // [tp] region base as seen from this rank (own base at [rank])
+    size_t off_in[2] = {}, off_keys = 0, off_flags[3] = {}, off_ticket = 0;
+    int* epoch = nullptr;
     cudaStream_t cap = nullptr;  // capture stream
 
     // device memory
@@ -179,6 +186,9 @@ void free_all(ti_engine* e) {
     for (auto& kv : e->graphs)
         if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
     e->graphs.clear();
+    for (size_t r = 0; r < e->peer.size(); ++r)
+        if ((int)r != e->tp.rank && e->peer[r]) cudaIpcCloseMemHandle(e->peer[r]);
+    e->peer.clear();
     // graphs holding NCCL calls are gone before the communicator
     if (e->comm) {
         if (const NcclApi* n = nccl_api()) n->CommDestroy(e->comm);
@@ -387,6 +397,52 @@ ti_status build(ti_engine* e) {
         const ncclResult_t r = n->CommInitRank(&e->comm, e->tp.tp, id, e->tp.rank);
         TI_CHECK(r == ncclSuccess, TI_ERR_CUDA, "ncclCommInitRank (rank %d of %d): %s", e->tp.rank, e->tp.tp,
                  n->GetErrorString(r));
+        const char* ar = std::getenv("TI_TP_ALLREDUCE");
+        e->peer_ar = !(ar && std::string(ar) == "nccl") && e->tp.tp <= kMaxTp;
+        if (e->peer_ar) {
+            // [inbox o | inbox down] fp32 [tp][B][H] each, keys u64 [tp][B], flags u32 [3][tp], tickets
+            const int tpn = e->tp.tp;
+            size_t o = 0;
+            auto take = [&](size_t bytes) {
+                const size_t at = o;
+                o = (o + bytes + 255) & ~size_t(255);
+                return at;
+            };
+            e->off_in[0] = take((size_t)tpn * B * H * 4);
+            e->off_in[1] = take((size_t)tpn * B * H * 4);
+            e->off_keys = take((size_t)tpn * B * 8);
+            for (int k = 0; k < 3; ++k) e->off_flags[k] = take((size_t)tpn * 4);
+            e->off_ticket = take(16);
+            TI_CHECK(dalloc(e, reinterpret_cast<void**>(&e->par), o, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
+                     ti_last_error());
+            TI_CUDA(cudaMemset(e->par, 0, o));
+            TI_CHECK(dalloc_t(e, &e->epoch, 1, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+            TI_CUDA(cudaMemset(e->epoch, 0, 4));
+            // exchange the regions' IPC handles over the communicator
+            cudaIpcMemHandle_t mine;
+            TI_CUDA(cudaIpcGetMemHandle(&mine, e->par));
+            uint8_t* stage = nullptr;
+            TI_CHECK(dalloc(e, reinterpret_cast<void**>(&stage), (size_t)(tpn + 1) * sizeof mine, &e->bytes_work) ==
+                         TI_OK,
+                     TI_ERR_OOM, "%s", ti_last_error());
+            TI_CUDA(cudaMemcpy(stage + (size_t)tpn * sizeof mine, &mine, sizeof mine, cudaMemcpyHostToDevice));
+            const ncclResult_t r2 =
+                n->AllGather(stage + (size_t)tpn * sizeof mine, stage, sizeof mine, ncclUint8, e->comm, e->cap);
+            TI_CHECK(r2 == ncclSuccess, TI_ERR_CUDA, "ncclAllGather (IPC handles): %s", n->GetErrorString(r2));
+            TI_CUDA(cudaStreamSynchronize(e->cap));
+            std::vector<cudaIpcMemHandle_t> all(tpn);
+            TI_CUDA(cudaMemcpy(all.data(), stage, (size_t)tpn * sizeof mine, cudaMemcpyDeviceToHost));
+            e->peer.assign(tpn, nullptr);
+            for (int q = 0; q < tpn; ++q) {
+                if (q == e->tp.rank) {
+                    e->peer[q] = e->par;
+                    continue;
+                }
+                void* pp = nullptr;
+                TI_CUDA(cudaIpcOpenMemHandle(&pp, all[q], cudaIpcMemLazyEnablePeerAccess));
+                e->peer[q] = reinterpret_cast<uint8_t*>(pp);
+            }
+        }
     }
     {
         const char* env = std::getenv("TI_TC_MIN_BATCH");
@@ -475,6 +531,10 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             c.x = a.x + (size_t)b0 * x_stride_elems;
             c.out = a.out + (size_t)b0 * out_stride;
             if (a.partial) c.partial = a.partial + (size_t)b0 * out_stride;
+            if (a.ps.tp) {
+                for (int r = 0; r < a.ps.tp; ++r) c.ps.inbox[r] = a.ps.inbox[r] + (size_t)b0 * out_stride;
+                c.ps.signal = b0 + chunk >= B ? a.ps.signal : 0;  // the last chunk publishes
+            }
             if (a.resid) c.resid = a.resid + (size_t)b0 * resid_stride;
             if (a.lora.adapter) {
                 c.lora.adapter = a.lora.adapter + b0;
@@ -522,10 +582,31 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         return fail(TI_ERR_CUDA, "%s: %s", what, nccl_api()->GetErrorString(r));
     };
     auto row_parallel = [&](GemvArgs a, int x_stride_elems, uint16_t* out, const uint16_t* resid) -> ti_status {
-        a.partial = e->red;
         a.out = nullptr;
         a.out_stride = H;
         a.resid = nullptr;
+        if (e->peer_ar) {
+            // the projection's epilogue writes into every rank's inbox; the receive
+            // kernel waits for all ranks and adds the rank-ordered sum to the residual
+            const int ph = kind == kKO ? 0 : 1;
+            const int MB = e->o.max_batch;
+            a.ps.tp = e->tp.tp;
+            for (int r = 0; r < e->tp.tp; ++r) {
+                a.ps.inbox[r] = reinterpret_cast<float*>(e->peer[r] + e->off_in[ph]) + (size_t)e->tp.rank * MB * H;
+                a.ps.flag[r] = reinterpret_cast<unsigned int*>(e->peer[r] + e->off_flags[ph]) + e->tp.rank;
+            }
+            a.ps.epoch = e->epoch;
+            a.ps.seq_mul = d.n_layers;
+            a.ps.seq_add = li + 1;
+            a.ps.ticket = reinterpret_cast<unsigned int*>(e->par + e->off_ticket) + ph;
+            if (ti_status st = gemm(a, kEpiStore, x_stride_elems, H, 0)) return st;
+            TI_CUDA(tp_recv_resid_launch(reinterpret_cast<const float*>(e->par + e->off_in[ph]), (size_t)MB * H,
+                                         reinterpret_cast<const unsigned int*>(e->par + e->off_flags[ph]), e->tp.tp,
+                                         e->epoch, d.n_layers, li + 1, resid, out, B, H, e->err, s, true));
+            if (launches) ++*launches;
+            return TI_OK;
+        }
+        a.partial = e->red;
         if (ti_status st = gemm(a, kEpiStore, x_stride_elems, H, 0)) return st;
         if (ti_status st = nccl_check(nccl_api()->AllReduce(e->red, e->red, (size_t)B * H, ncclFloat32, ncclSum,
                                                             e->comm, s),
@@ -549,6 +630,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         ea.n_updates = e->d_desc;
         ea.page_table = e->page_table;
         ea.pt_stride = e->pt_stride;
+        ea.epoch = e->peer_ar ? e->epoch : nullptr;
         ea.err = e->err;
         TI_CUDA(embed_launch(ea, s, true));
         if (launches) ++*launches;
@@ -590,6 +672,20 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         lm.key_offset = e->tp.v0;
         lm.publish = 0;
         if (ti_status st = gemm(lm, kEpiLmHead, H, e->Vl, 0)) return st;
+        if (e->peer_ar) {
+            std::vector<unsigned long long*> pk(e->tp.tp);
+            std::vector<unsigned int*> pf(e->tp.tp);
+            for (int r = 0; r < e->tp.tp; ++r) {
+                pk[r] = reinterpret_cast<unsigned long long*>(e->peer[r] + e->off_keys);
+                pf[r] = reinterpret_cast<unsigned int*>(e->peer[r] + e->off_flags[2]);
+            }
+            TI_CUDA(tp_keys_launch(e->amax, B, pk.data(), pf.data(), e->tp.tp, e->tp.rank,
+                                   reinterpret_cast<const unsigned long long*>(e->par + e->off_keys),
+                                   reinterpret_cast<const unsigned int*>(e->par + e->off_flags[2]), e->o.max_batch,
+                                   e->epoch, e->out, e->dd_tokens(), e->dd_pos(), e->err, s, true));
+            if (launches) ++*launches;
+            return TI_OK;
+        }
         if (ti_status st = nccl_check(
                 nccl_api()->AllReduce(e->amax, e->amax, (size_t)B, ncclUint64, ncclMax, e->comm, s), "ncclAllReduce"))
             return st;

@@ -284,7 +284,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int w = 0; w < kConsumerWarps; ++w) sum += pv[w];
                     accu[u] = sum;
                 }
-                if (EPI == kEpiStore && a.partial) {
+                if (EPI == kEpiStore && a.ps.tp) {
+                    // tensor-parallel all-reduce: the fp32 sum into every rank's inbox (NVLink stores)
+                    for (int r = 0; r < a.ps.tp; ++r) a.ps.inbox[r][(size_t)b * a.out_stride + n] = accu[0];
+                } else if (EPI == kEpiStore && a.partial) {
                     a.partial[(size_t)b * a.out_stride + n] = accu[0];
                 } else if (EPI == kEpiStore) {
                     float v = round_bf(accu[0]);
@@ -350,6 +353,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (a.chain_pos) a.chain_pos[b] += 1;
                     }
                     atomicExch(a.done, 0u);
+                }
+            }
+        }
+        if (EPI == kEpiStore && a.ps.tp) {
+            // this CTA's peer stores are visible system-wide before it counts itself;
+            // the last CTA publishes the phase to every rank
+            __threadfence_system();
+            __syncwarp();
+            if (lane == 0) {
+                const unsigned int t = atomicAdd(a.ps.ticket, 1u);
+                if (t == gridDim.x - 1) {
+                    __threadfence_system();
+                    if (a.ps.signal) {
+                        const unsigned int seq = peer_seq(*a.ps.epoch, a.ps.seq_mul, a.ps.seq_add);
+                        for (int r = 0; r < a.ps.tp; ++r) st_release_sys(a.ps.flag[r], seq);
+                    }
+                    atomicExch(a.ps.ticket, 0u);
                 }
             }
         }

@@ -65,6 +65,28 @@ __host__ __device__ inline size_t wrow_bytes(int K, int wf) {
     return wf == kWQ4 ? (size_t)K / 2 + (size_t)K / 16 : wf == kWQ8 ? (size_t)K + (size_t)K / 16 : (size_t)K * 2;
 }
 
+// One-shot all-reduce over NVLink peer memory (tensor parallelism).  The
+// producer (a row-parallel projection) stores its fp32 outputs straight into
+// every rank's inbox slot for this sender; every CTA fences system-wide and the
+// last one publishes the phase's sequence number to every rank's flag for this
+// sender.  A receiver waits (bounded) for all flags, then sums the inboxes in
+// rank order, so all ranks get bit-identical results.
+constexpr int kMaxTp = 8;
+struct PeerSend {
+    float* inbox[kMaxTp] = {};        // rank r's inbox block for this sender ([nb, out_stride])
+    unsigned int* flag[kMaxTp] = {};  // rank r's flag for this sender
+    int tp = 0;                       // ranks; 0 = off
+    int signal = 1;                   // 0: store only (an earlier launch of a chunked batch)
+    const int* epoch = nullptr;       // device step counter (the step's first kernel increments it)
+    int seq_mul = 1, seq_add = 0;     // sequence number = (*epoch - 1) * seq_mul + seq_add
+    unsigned int* ticket = nullptr;   // local CTA completion counter (zero; the last CTA resets it)
+};
+
+// sequence number of a phase (wrap-safe comparisons with (int)(a - b) >= 0)
+__host__ __device__ inline unsigned int peer_seq(int epoch, int mul, int add) {
+    return (unsigned int)(epoch - 1) * (unsigned int)mul + (unsigned int)add;
+}
+
 struct GemvArgs {
     const void* W = nullptr;  // [rows, K] in format wfmt; kEpiGlu: gate rows [0,N) then up rows [N,2N)
     int wfmt = kWBf16;
@@ -94,6 +116,7 @@ struct GemvArgs {
     // kEpiStore: when set, the unrounded fp32 sums go here instead ([nb, out_stride]);
     // the row-parallel half of tensor parallelism all-reduces them
     float* partial = nullptr;
+    PeerSend ps;  // kEpiStore: fp32 sums into the ranks' inboxes (tensor-parallel all-reduce)
     GemvLora lora;
     // L2 warm-up of the next GEMV of the step: once this CTA's producer has
     // issued its own copies it prefetches the first `next_bytes` of the rows the
@@ -183,6 +206,17 @@ cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s, bool pdl);
 // out[b, n] = bf16(resid[b, n] + bf16(sum[b, n])) after the all-reduce of a row-parallel projection
 cudaError_t tp_resid_launch(const float* sum, const uint16_t* resid, uint16_t* out, int nb, int H, cudaStream_t s,
                             bool pdl);
+// receive side of the peer all-reduce: wait (bounded) until every sender's flag
+// reaches this phase's sequence number, out = bf16(resid + bf16(sum of the inboxes in rank order))
+cudaError_t tp_recv_resid_launch(const float* inbox, size_t src_stride, const unsigned int* flags, int tp,
+                                 const int* epoch, int seq_mul, int seq_add, const uint16_t* resid, uint16_t* out,
+                                 int nb, int H, int* err, cudaStream_t s, bool pdl);
+// greedy ids over the ranks' vocabulary slices through peer memory: send this
+// rank's keys to every rank, wait for all, take the max (one CTA)
+cudaError_t tp_keys_launch(unsigned long long* amax, int nb, unsigned long long* const* peer_keys,
+                           unsigned int* const* peer_flags, int tp, int rank, const unsigned long long* keys_inbox,
+                           const unsigned int* flags, int max_nb, const int* epoch, int32_t* out_ids,
+                           int32_t* chain_tokens, int32_t* chain_pos, int* err, cudaStream_t s, bool pdl);
 // greedy ids from the all-reduced argmax keys; re-arms the keys (cf. the LM-head epilogue)
 cudaError_t tp_ids_launch(unsigned long long* amax, int nb, int32_t* out_ids, int32_t* chain_tokens,
                           int32_t* chain_pos, cudaStream_t s, bool pdl);
@@ -199,6 +233,7 @@ struct EmbedArgs {
     const int32_t* n_updates = nullptr;   // device scalar
     int32_t* page_table = nullptr;
     int pt_stride = 0;
+    int* epoch = nullptr;  // step counter for tensor-parallel phase sequence numbers (incremented here)
     int* err = nullptr;
 };
 cudaError_t embed_launch(const EmbedArgs& a, cudaStream_t s, bool pdl);

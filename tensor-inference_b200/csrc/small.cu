@@ -39,6 +39,7 @@ __global__ void k_embed(const EmbedArgs a) {
             a.page_table[(size_t)seq * a.pt_stride + idx] = page;
         }
     }
+    if (blockIdx.x == 0 && threadIdx.x == 0 && a.epoch) *a.epoch += 1;
     const int b = blockIdx.x;
     int tok = a.tokens[b];
     if (tok < 0 || tok >= a.vocab) {
@@ -134,6 +135,111 @@ cudaError_t tp_ids_launch(unsigned long long* amax, int nb, int32_t* out_ids, in
                           int32_t* chain_pos, cudaStream_t s, bool pdl) {
     void* params[] = {&amax, &nb, &out_ids, &chain_tokens, &chain_pos};
     return launch_pdl(reinterpret_cast<const void*>(&k_tp_ids), dim3(1), dim3(256), 0, s, params, pdl);
+}
+
+
+// ---- tensor-parallel all-reduce through peer memory (receive side)
+__global__ void k_tp_recv_resid(const float* __restrict__ inbox, size_t src_stride, const unsigned int* flags, int tp,
+                                const int* epoch, int seq_mul, int seq_add, const uint16_t* __restrict__ resid,
+                                uint16_t* __restrict__ out, int n, int* err) {
+    __shared__ int ok;
+    if (blockIdx.x == 0 && threadIdx.x == 0) pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x == 0) {
+        const unsigned int seq = peer_seq(*epoch, seq_mul, seq_add);
+        bool good = true;
+        for (int r = 0; r < tp && good; ++r) good = wait_seq_sys(flags + r, seq, err, kErrTimeoutPeer);
+        ok = good;
+    }
+    __syncthreads();
+    if (!ok) return;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        float sum = 0.f;
+        for (int r = 0; r < tp; ++r) sum += __ldcv(inbox + (size_t)r * src_stride + i);  // rank order
+        const float rr = __uint_as_float((uint32_t)resid[i] << 16);
+        out[i] = __bfloat16_as_ushort(f2bf(rr + round_bf(sum)));
+    }
+}
+
+cudaError_t tp_recv_resid_launch(const float* inbox, size_t src_stride, const unsigned int* flags, int tp,
+                                 const int* epoch, int seq_mul, int seq_add, const uint16_t* resid, uint16_t* out,
+                                 int nb, int H, int* err, cudaStream_t s, bool pdl) {
+    int n = nb * H;
+    void* params[] = {&inbox, &src_stride, &flags, &tp, &epoch, &seq_mul, &seq_add, &resid, &out, &n, &err};
+    const int grid = std::min((n + 255) / 256, 148);
+    return launch_pdl(reinterpret_cast<const void*>(&k_tp_recv_resid), dim3(grid), dim3(256), 0, s, params, pdl);
+}
+
+struct KeysArgs {
+    unsigned long long* amax;
+    int nb, tp, rank, max_nb;
+    unsigned long long* peer_keys[kMaxTp];  // rank r's keys inbox [tp][max_nb]
+    unsigned int* peer_flags[kMaxTp];       // rank r's flags [tp]
+    const unsigned long long* keys_inbox;   // this rank's inbox
+    const unsigned int* flags;              // this rank's flags
+    const int* epoch;
+    int32_t *out_ids, *chain_tokens, *chain_pos;
+    int* err;
+};
+
+__global__ void k_tp_keys(const KeysArgs a) {
+    __shared__ int ok;
+    if (threadIdx.x == 0) pdl_trigger();
+    pdl_wait();
+    const unsigned int seq = (unsigned int)*a.epoch;
+    for (int b = threadIdx.x; b < a.nb; b += blockDim.x) {
+        const unsigned long long key = a.amax[b];
+        a.amax[b] = 0ull;
+        for (int r = 0; r < a.tp; ++r) a.peer_keys[r][(size_t)a.rank * a.max_nb + b] = key;
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int r = 0; r < a.tp; ++r) st_release_sys(a.peer_flags[r] + a.rank, seq);
+        bool good = true;
+        for (int r = 0; r < a.tp && good; ++r) good = wait_seq_sys(a.flags + r, seq, a.err, kErrTimeoutPeer);
+        ok = good;
+    }
+    __syncthreads();
+    if (!ok) return;
+    for (int b = threadIdx.x; b < a.nb; b += blockDim.x) {
+        unsigned long long best = 0ull;
+        for (int r = 0; r < a.tp; ++r) {
+            const unsigned long long k = __ldcv(a.keys_inbox + (size_t)r * a.max_nb + b);
+            best = k > best ? k : best;
+        }
+        const int32_t id = (int32_t)(~(uint32_t)(best & 0xffffffffull));
+        a.out_ids[b] = id;
+        if (a.chain_tokens) a.chain_tokens[b] = id;
+        if (a.chain_pos) a.chain_pos[b] += 1;
+    }
+}
+
+cudaError_t tp_keys_launch(unsigned long long* amax, int nb, unsigned long long* const* peer_keys,
+                           unsigned int* const* peer_flags, int tp, int rank, const unsigned long long* keys_inbox,
+                           const unsigned int* flags, int max_nb, const int* epoch, int32_t* out_ids,
+                           int32_t* chain_tokens, int32_t* chain_pos, int* err, cudaStream_t s, bool pdl) {
+    if (tp < 1 || tp > kMaxTp) return cudaErrorInvalidValue;
+    KeysArgs a{};
+    a.amax = amax;
+    a.nb = nb;
+    a.tp = tp;
+    a.rank = rank;
+    a.max_nb = max_nb;
+    for (int r = 0; r < tp; ++r) {
+        a.peer_keys[r] = peer_keys[r];
+        a.peer_flags[r] = peer_flags[r];
+    }
+    a.keys_inbox = keys_inbox;
+    a.flags = flags;
+    a.epoch = epoch;
+    a.out_ids = out_ids;
+    a.chain_tokens = chain_tokens;
+    a.chain_pos = chain_pos;
+    a.err = err;
+    void* params[] = {&a};
+    return launch_pdl(reinterpret_cast<const void*>(&k_tp_keys), dim3(1), dim3(256), 0, s, params, pdl);
 }
 
 }  // namespace ti

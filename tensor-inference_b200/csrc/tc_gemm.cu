@@ -141,6 +141,7 @@ struct TcKernelArgs {
     float* logits_f32;
     int key_offset, publish;
     float* partial;
+    PeerSend ps;
     float* ws;               // [grid][2][np][128] fp32 partials of tiles shared between CTAs
     unsigned int* tile_ctr;  // [tiles], zero; reset by each shared tile's last unit
     GemvLora lora;           // per-token LoRA expansion (adapter == nullptr: off)
@@ -412,6 +413,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         }
                     }
                     named_bar(1, 128);
+                } else if (EPI == kEpiStore && a.ps.tp) {
+                    // tensor-parallel all-reduce: the fp32 sums into every rank's inbox (NVLink stores)
+                    if (row_ok)
+                        for (int i = 0; i < 32; ++i) {
+                            const int b = c * 32 + i;
+                            if (b >= a.nb) break;
+                            for (int r = 0; r < a.ps.tp; ++r) a.ps.inbox[r][(size_t)b * a.out_stride + n] = v[i];
+                        }
                 } else if (EPI == kEpiStore && a.partial) {
                     if (row_ok)
                         for (int i = 0; i < 32; ++i) {
@@ -521,6 +530,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             ++j;
             return true;
         });
+        if (EPI == kEpiStore && a.ps.tp) {
+            // this CTA's peer stores are visible system-wide before it counts itself;
+            // the last CTA publishes the phase to every rank
+            __threadfence_system();
+            named_bar(1, 128);
+            if (et == 0) {
+                const unsigned int t = atomicAdd(a.ps.ticket, 1u);
+                if (t == gridDim.x - 1) {
+                    __threadfence_system();
+                    if (a.ps.signal) {
+                        const unsigned int seq = peer_seq(*a.ps.epoch, a.ps.seq_mul, a.ps.seq_add);
+                        for (int r = 0; r < a.ps.tp; ++r) st_release_sys(a.ps.flag[r], seq);
+                    }
+                    atomicExch(a.ps.ticket, 0u);
+                }
+            }
+        }
         if (EPI == kEpiLmHead) {
             // grid argmax: one 64-bit atomicMax per token per CTA; the last CTA
             // publishes the ids and re-arms the keys for the next step
@@ -768,6 +794,7 @@ cudaError_t tc_launch(const GemvArgs& g, int epi, const TcPlan& p, float* ws, un
     a.key_offset = g.key_offset;
     a.publish = g.publish;
     a.partial = g.partial;
+    a.ps = g.ps;
     a.ws = ws;
     a.tile_ctr = tile_ctr;
     a.lora = g.lora;

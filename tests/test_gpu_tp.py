@@ -1,6 +1,7 @@
 """Tensor parallelism (TP=2) against the CPU oracle, on 2 GPUs.
 
-The parent runs the oracle first (teacher-forced: each step feeds the oracle's
+Row-parallel sums go through the fused peer-memory all-reduce by default and
+through NCCL in one parametrisation.  The parent runs the oracle first (teacher-forced: each step feeds the oracle's
 greedy token) and hands the token schedule to two child processes, one per
 GPU and rank, which run the same steps through TP engines that share an NCCL
 communicator.  Checks: both ranks agree on every greedy id; rank 0's gathered
@@ -54,8 +55,9 @@ def _oracle_schedule(kw, prompts, steps, seed, std):
     return feeds, ref
 
 
-def _rank(rank, world, nid, kw, prompts, feeds, seed, std, q):
+def _rank(rank, world, nid, kw, prompts, feeds, seed, std, q, mode):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["TI_TP_ALLREDUCE"] = mode
     sys.path.insert(0, os.path.join(ROOT, "tensor-inference_b200"))
     try:
         import ti_b200 as tl
@@ -85,13 +87,13 @@ def _rank(rank, world, nid, kw, prompts, feeds, seed, std, q):
         os._exit(1)
 
 
-def _run_tp(kw, prompts, steps, tol, seed=0, std=0.02, world=2):
+def _run_tp(kw, prompts, steps, tol, seed=0, std=0.02, world=2, mode="peer"):
     _need(world)
     feeds, ref = _oracle_schedule(kw, prompts, steps, seed, std)
     nid = ti.nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, world, nid, kw, prompts, feeds, seed, std, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, nid, kw, prompts, feeds, seed, std, q, mode)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -120,9 +122,11 @@ def _run_tp(kw, prompts, steps, tol, seed=0, std=0.02, world=2):
     assert flips <= max(1, (steps + 1) * len(prompts) // 10)
 
 
-def test_tp2_llama_small_ragged():
+@pytest.mark.parametrize("mode", ["peer", "nccl"])
+def test_tp2_llama_small_ragged(mode):
+    # peer: the fused all-reduce over NVLink peer memory; nccl: ncclAllReduce (the baseline path)
     prompts = [oracle.fill_ids(f"tp{b}", n, b, SMALL["vocab"]) for b, n in enumerate((5, 11, 3))]
-    _run_tp(SMALL, prompts, steps=4, tol=2e-2)
+    _run_tp(SMALL, prompts, steps=4, tol=2e-2, mode=mode)
 
 
 def test_tp2_tensor_core_batch16():
