@@ -91,7 +91,7 @@ struct ti_engine {
     bool peer_ar = false;
     uint8_t* par = nullptr;
     std::vector<uint8_t*> peer;  // [tp] region base as seen from this rank (own base at [rank])
-    size_t off_in[2] = {}, off_keys = 0, off_flags[3] = {}, off_ticket = 0;
+    size_t off_in[2] = {}, off_keys = 0, off_flags[3] = {}, off_ticket = 0, off_tin[2] = {};
     int* epoch = nullptr;
     cudaStream_t cap = nullptr;  // capture stream
 
@@ -277,7 +277,9 @@ ti_status validate_desc(const ti_model_desc* d, const ti_engine_opts* o) {
         ti_tp_shard sh;
         if (ti_status st = tp_plan_make(d, tp, o->tp_rank, &sh)) return st;
         TI_CHECK(o->nccl_id, TI_ERR_INVALID, "engine: tp_size %d needs opts.nccl_id", tp);
-        TI_CHECK(o->max_adapters == 0, TI_ERR_UNSUPPORTED, "engine: LoRA adapters with tensor parallelism are not built yet");
+        const char* ar = std::getenv("TI_TP_ALLREDUCE");
+        TI_CHECK(o->max_adapters == 0 || !(ar && std::string(ar) == "nccl"), TI_ERR_UNSUPPORTED,
+                 "engine: LoRA with tensor parallelism uses the peer-memory all-reduce (TI_TP_ALLREDUCE=nccl)");
         TI_CHECK(nccl_api(), TI_ERR_UNSUPPORTED, "engine: tensor parallelism needs libnccl.so.2");
     }
     return TI_OK;
@@ -411,6 +413,10 @@ ti_status build(ti_engine* e) {
             e->off_in[0] = take((size_t)tpn * B * H * 4);
             e->off_in[1] = take((size_t)tpn * B * H * 4);
             e->off_keys = take((size_t)tpn * B * 8);
+            // row-parallel LoRA: every rank's partial x.A^T (o, down), [tp][B][R]
+            const int Rp = e->o.max_adapters > 0 ? (e->o.max_lora_rank + 7) / 8 * 8 : 0;
+            e->off_tin[0] = take((size_t)tpn * B * Rp * 4);
+            e->off_tin[1] = take((size_t)tpn * B * Rp * 4);
             for (int k = 0; k < 3; ++k) e->off_flags[k] = take((size_t)tpn * 4);
             e->off_ticket = take(16);
             TI_CHECK(dalloc(e, reinterpret_cast<void**>(&e->par), o, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
@@ -581,7 +587,8 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         if (r == ncclSuccess) return TI_OK;
         return fail(TI_ERR_CUDA, "%s: %s", what, nccl_api()->GetErrorString(r));
     };
-    auto row_parallel = [&](GemvArgs a, int x_stride_elems, uint16_t* out, const uint16_t* resid) -> ti_status {
+    auto row_parallel = [&](GemvArgs a, int x_stride_elems, uint16_t* out, const uint16_t* resid,
+                            const GemvLora* lora) -> ti_status {
         a.out = nullptr;
         a.out_stride = H;
         a.resid = nullptr;
@@ -602,7 +609,9 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             if (ti_status st = gemm(a, kEpiStore, x_stride_elems, H, 0)) return st;
             TI_CUDA(tp_recv_resid_launch(reinterpret_cast<const float*>(e->par + e->off_in[ph]), (size_t)MB * H,
                                          reinterpret_cast<const unsigned int*>(e->par + e->off_flags[ph]), e->tp.tp,
-                                         e->epoch, d.n_layers, li + 1, resid, out, B, H, e->err, s, true));
+                                         e->epoch, d.n_layers, li + 1, resid, out, B, H, lora,
+                                         reinterpret_cast<const float*>(e->par + e->off_tin[ph]),
+                                         (size_t)MB * (lora ? lora->rank : 0), e->err, s, true));
             if (launches) ++*launches;
             return TI_OK;
         }
@@ -714,6 +723,14 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         la.n_adapters = e->S;
         la.t = e->lt[k];
         la.t_stride = e->lT[k];
+        if (e->tp.tp > 1 && (k == 1 || k == 3)) {
+            // row-parallel: partial sums over this rank's input columns to every rank
+            const int ph = k == 1 ? 0 : 1;
+            la.tp = e->tp.tp;
+            for (int r = 0; r < e->tp.tp; ++r)
+                la.peer_t[r] = reinterpret_cast<float*>(e->peer[r] + e->off_tin[ph]) +
+                               (size_t)e->tp.rank * e->o.max_batch * e->lT[k];
+        }
         TI_CUDA(lora_shrink_launch(la, s, true));
         if (launches) ++*launches;
         return TI_OK;
@@ -805,7 +822,12 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
                 if (ti_status st = shrink(1, e->attn, QW, nullptr)) return st;
                 set_lora(ov, 1);
             }
-            if (e->tp.tp > 1) return row_parallel(ov, QW, e->res1, e->hidden);
+            if (e->tp.tp > 1) {
+                // the expansion runs after the all-reduce, on the full x.A^T
+                const GemvLora lo = ov.lora;
+                ov.lora = GemvLora{};
+                return row_parallel(ov, QW, e->res1, e->hidden, lo.adapter ? &lo : nullptr);
+            }
             return gemm(ov, kEpiResid, QW, H, H);
         }
         case kKGateUp: {
@@ -849,7 +871,11 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
                 if (ti_status st = shrink(3, e->act, I, nullptr)) return st;
                 set_lora(dn, 3);
             }
-            if (e->tp.tp > 1) return row_parallel(dn, I, e->hidden, e->res1);
+            if (e->tp.tp > 1) {
+                const GemvLora lo = dn.lora;
+                dn.lora = GemvLora{};
+                return row_parallel(dn, I, e->hidden, e->res1, lo.adapter ? &lo : nullptr);
+            }
             return gemm(dn, kEpiResid, I, H, H);
         }
         default: return fail(TI_ERR_INVALID, "unknown kernel kind %d", kind);
@@ -1402,6 +1428,22 @@ void lora_geometry(const ti_engine* e, int p, int* out, int* in, int* a_sec, int
     *b_row0 = rows0[p];
 }
 
+// Under tensor parallelism an adapter tensor is a window of the full one: B rows
+// of the local output rows (q, k, v, gate, up) or A columns of the local input
+// columns (o, down).  Full shapes, window origin.
+void lora_window(const ti_engine* e, int p, int* out_full, int* in_full, int* b_r0, int* a_c0) {
+    const int hd = e->hd, H = e->H;
+    const int QWg = e->d.n_heads * hd, KWg = e->d.n_kv_heads * hd, Ig = e->d.intermediate;
+    const int outs[7] = {QWg, KWg, KWg, H, Ig, Ig, H};
+    const int ins[7] = {H, H, H, QWg, H, H, Ig};
+    const int r0[7] = {e->tp.q0 * hd, e->tp.kv0 * hd, e->tp.kv0 * hd, 0, e->tp.i0, e->tp.i0, 0};
+    const int c0[7] = {0, 0, 0, e->tp.q0 * hd, 0, 0, e->tp.i0};
+    *out_full = outs[p];
+    *in_full = ins[p];
+    *b_r0 = r0[p];
+    *a_c0 = c0[p];
+}
+
 uint16_t* lora_A(ti_engine* e, int ad, int layer, int p) {
     const int k = kLoraKind[p];
     int out, in, sec, row0;
@@ -1489,18 +1531,21 @@ ti_status ti_adapter_load_tensor(ti_engine* e, int id, const char* name, const v
              "unknown adapter tensor '%s'", name);
     const auto& m = e->adapters[id];
     TI_CHECK(m.mask & (1 << p), TI_ERR_INVALID, "adapter %d does not inject %s", id, kLoraProj[p]);
-    int out, in, sec, row0;
+    int out, in, sec, row0, out_f, in_f, b_r0, a_c0;
     lora_geometry(e, p, &out, &in, &sec, &row0);
+    lora_window(e, p, &out_f, &in_f, &b_r0, &a_c0);
     DeviceGuard g(e->dev);
-    if (which == 'A') {  // [rank, in], flat accepted (adapter_loader.cpp:67-81)
-        TI_CHECK(bytes == (size_t)m.rank * in * 2, TI_ERR_INVALID, "%s: %zu bytes, expected %zu", name, bytes,
-                 (size_t)m.rank * in * 2);
-        TI_CUDA(cudaMemcpy(lora_A(e, id, layer, p), host, bytes, cudaMemcpyHostToDevice));
-    } else {  // [out, rank] into rows of padded width R (adapter_loader.cpp:83-95)
-        TI_CHECK(bytes == (size_t)out * m.rank * 2, TI_ERR_INVALID, "%s: %zu bytes, expected %zu", name, bytes,
-                 (size_t)out * m.rank * 2);
-        TI_CUDA(cudaMemcpy2D(lora_B(e, id, layer, p), (size_t)e->R * 2, host, (size_t)m.rank * 2, (size_t)m.rank * 2,
-                             out, cudaMemcpyHostToDevice));
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(host);
+    if (which == 'A') {  // [rank, in], flat accepted (adapter_loader.cpp:67-81); local input columns
+        TI_CHECK(bytes == (size_t)m.rank * in_f * 2, TI_ERR_INVALID, "%s: %zu bytes, expected %zu", name, bytes,
+                 (size_t)m.rank * in_f * 2);
+        TI_CUDA(cudaMemcpy2D(lora_A(e, id, layer, p), (size_t)in * 2, src + (size_t)a_c0 * 2, (size_t)in_f * 2,
+                             (size_t)in * 2, m.rank, cudaMemcpyHostToDevice));
+    } else {  // [out, rank] into rows of padded width R (adapter_loader.cpp:83-95); local output rows
+        TI_CHECK(bytes == (size_t)out_f * m.rank * 2, TI_ERR_INVALID, "%s: %zu bytes, expected %zu", name, bytes,
+                 (size_t)out_f * m.rank * 2);
+        TI_CUDA(cudaMemcpy2D(lora_B(e, id, layer, p), (size_t)e->R * 2, src + (size_t)b_r0 * m.rank * 2,
+                             (size_t)m.rank * 2, (size_t)m.rank * 2, out, cudaMemcpyHostToDevice));
     }
     return TI_OK;
 }
@@ -1514,12 +1559,14 @@ ti_status ti_adapter_init_synthetic(ti_engine* e, int id, uint64_t seed, float s
     for (int layer = 0; layer < e->d.n_layers; ++layer)
         for (int p = 0; p < 7; ++p) {
             if (!(m.mask & (1 << p))) continue;
-            int out, in, sec, row0;
+            int out, in, sec, row0, out_f, in_f, b_r0, a_c0;
             lora_geometry(e, p, &out, &in, &sec, &row0);
+            lora_window(e, p, &out_f, &in_f, &b_r0, &a_c0);
             const std::string base = "layers." + std::to_string(layer) + "." + kLoraProj[p];
-            TI_CUDA(synth_bf16_launch(lora_A(e, id, layer, p), m.rank, in, in, 0, 0, in, seed,
+            // windows of the full tensors' synthetic values (identical to a single-GPU engine's)
+            TI_CUDA(synth_bf16_launch(lora_A(e, id, layer, p), m.rank, in, in, 0, a_c0, in_f, seed,
                                       fnv1a((base + ".lora_A").c_str()), ca, (cudaStream_t)0));
-            TI_CUDA(synth_bf16_launch(lora_B(e, id, layer, p), out, m.rank, e->R, 0, 0, m.rank, seed,
+            TI_CUDA(synth_bf16_launch(lora_B(e, id, layer, p), out, m.rank, e->R, b_r0, 0, m.rank, seed,
                                       fnv1a((base + ".lora_B").c_str()), cb, (cudaStream_t)0));
         }
     TI_CUDA(cudaDeviceSynchronize());

@@ -38,33 +38,6 @@ struct GemvLora {
     int sec1 = 1 << 30, sec2 = 1 << 30;
 };
 
-// LoRA shrink: t[b, r] = bf16(x_b . A[adapter[b]][r]), optional RMSNorm of x first
-struct LoraShrinkArgs {
-    const uint16_t* x = nullptr;  // [nb, x_stride] bf16
-    int x_stride = 0, K = 0, nb = 1;
-    const uint16_t* norm_w = nullptr;
-    float eps = 1e-5f;
-    int norm_offset = 0;
-    const uint16_t* A = nullptr;  // adapter 0's A rows for this layer: [T, K]
-    size_t A_adapter_stride = 0;
-    int T = 0;                    // rows: sections x padded rank
-    const int32_t* adapter = nullptr;
-    int n_adapters = 0;
-    float* t = nullptr;           // [nb, t_stride]
-    int t_stride = 0;
-};
-cudaError_t lora_shrink_launch(const LoraShrinkArgs& a, cudaStream_t s, bool pdl);
-
-// Weight row formats the GEMV streams (TI_WFMT_* values).  Quantised rows are
-// [K codes][K/32 fp16 block scales]: Q4_0 codes are 4-bit, element c in byte
-// c/2 (low nibble for even c), value d * (q - 8); Q8_0 codes are int8, value
-// d * q (GGUF's block formats, rows repacked so a lane's 8 elements are one
-// aligned word).
-enum WeightFmt : int { kWBf16 = 0, kWQ4 = 1, kWQ8 = 2 };
-__host__ __device__ inline size_t wrow_bytes(int K, int wf) {
-    return wf == kWQ4 ? (size_t)K / 2 + (size_t)K / 16 : wf == kWQ8 ? (size_t)K + (size_t)K / 16 : (size_t)K * 2;
-}
-
 // One-shot all-reduce over NVLink peer memory (tensor parallelism).  The
 // producer (a row-parallel projection) stores its fp32 outputs straight into
 // every rank's inbox slot for this sender; every CTA fences system-wide and the
@@ -85,6 +58,37 @@ struct PeerSend {
 // sequence number of a phase (wrap-safe comparisons with (int)(a - b) >= 0)
 __host__ __device__ inline unsigned int peer_seq(int epoch, int mul, int add) {
     return (unsigned int)(epoch - 1) * (unsigned int)mul + (unsigned int)add;
+}
+
+// LoRA shrink: t[b, r] = bf16(x_b . A[adapter[b]][r]), optional RMSNorm of x first
+struct LoraShrinkArgs {
+    const uint16_t* x = nullptr;  // [nb, x_stride] bf16
+    int x_stride = 0, K = 0, nb = 1;
+    const uint16_t* norm_w = nullptr;
+    float eps = 1e-5f;
+    int norm_offset = 0;
+    const uint16_t* A = nullptr;  // adapter 0's A rows for this layer: [T, K]
+    size_t A_adapter_stride = 0;
+    int T = 0;                    // rows: sections x padded rank
+    const int32_t* adapter = nullptr;
+    int n_adapters = 0;
+    float* t = nullptr;           // [nb, t_stride]
+    int t_stride = 0;
+    // tensor parallelism, row-parallel projection: x and A hold this rank's input
+    // columns; the unrounded fp32 partial sums go to every rank's inbox instead of t
+    float* peer_t[kMaxTp] = {};
+    int tp = 0;
+};
+cudaError_t lora_shrink_launch(const LoraShrinkArgs& a, cudaStream_t s, bool pdl);
+
+// Weight row formats the GEMV streams (TI_WFMT_* values).  Quantised rows are
+// [K codes][K/32 fp16 block scales]: Q4_0 codes are 4-bit, element c in byte
+// c/2 (low nibble for even c), value d * (q - 8); Q8_0 codes are int8, value
+// d * q (GGUF's block formats, rows repacked so a lane's 8 elements are one
+// aligned word).
+enum WeightFmt : int { kWBf16 = 0, kWQ4 = 1, kWQ8 = 2 };
+__host__ __device__ inline size_t wrow_bytes(int K, int wf) {
+    return wf == kWQ4 ? (size_t)K / 2 + (size_t)K / 16 : wf == kWQ8 ? (size_t)K + (size_t)K / 16 : (size_t)K * 2;
 }
 
 struct GemvArgs {
@@ -208,9 +212,13 @@ cudaError_t tp_resid_launch(const float* sum, const uint16_t* resid, uint16_t* o
                             bool pdl);
 // receive side of the peer all-reduce: wait (bounded) until every sender's flag
 // reaches this phase's sequence number, out = bf16(resid + bf16(sum of the inboxes in rank order))
+// With `lora` set (lora->adapter != nullptr, row-parallel LoRA): t_inbox holds
+// every rank's partial x.A^T ([tp][t_src_stride]); the rank-ordered sums rounded
+// to bf16 feed the expansion bf16(bf16(t.B^T) * scale) added to the projection.
 cudaError_t tp_recv_resid_launch(const float* inbox, size_t src_stride, const unsigned int* flags, int tp,
                                  const int* epoch, int seq_mul, int seq_add, const uint16_t* resid, uint16_t* out,
-                                 int nb, int H, int* err, cudaStream_t s, bool pdl);
+                                 int nb, int H, const GemvLora* lora, const float* t_inbox, size_t t_src_stride,
+                                 int* err, cudaStream_t s, bool pdl);
 // greedy ids over the ranks' vocabulary slices through peer memory: send this
 // rank's keys to every rank, wait for all, take the max (one CTA)
 cudaError_t tp_keys_launch(unsigned long long* amax, int nb, unsigned long long* const* peer_keys,

@@ -77,8 +77,16 @@ __global__ void __launch_bounds__(kShrinkThreads) k_lora_shrink(const LoraShrink
             acc = dot8_bf16(w, xv, acc);
         }
         acc = warp_sum(acc);
-        if (lane == 0) a.t[(size_t)b * a.t_stride + r] = round_bf(acc);
+        if (lane == 0) {
+            if (a.tp) {
+                // row-parallel under tensor parallelism: fp32 partial to every rank
+                for (int q = 0; q < a.tp; ++q) a.peer_t[q][(size_t)b * a.t_stride + r] = acc;
+            } else {
+                a.t[(size_t)b * a.t_stride + r] = round_bf(acc);
+            }
+        }
     }
+    if (a.tp) __threadfence_system();
 }
 
 cudaError_t lora_shrink_launch(const LoraShrinkArgs& a, cudaStream_t s, bool pdl) {

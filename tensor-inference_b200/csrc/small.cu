@@ -139,10 +139,17 @@ cudaError_t tp_ids_launch(unsigned long long* amax, int nb, int32_t* out_ids, in
 
 
 // ---- tensor-parallel all-reduce through peer memory (receive side)
+struct RecvLora {
+    GemvLora L;                 // adapter ids, B rows [out][R] of adapter 0, strides, rank R, scales
+    const float* t_inbox = nullptr;
+    size_t t_src_stride = 0;    // floats between senders' blocks
+};
+
 __global__ void k_tp_recv_resid(const float* __restrict__ inbox, size_t src_stride, const unsigned int* flags, int tp,
                                 const int* epoch, int seq_mul, int seq_add, const uint16_t* __restrict__ resid,
-                                uint16_t* __restrict__ out, int n, int* err) {
+                                uint16_t* __restrict__ out, int n, int H, const RecvLora rl, int* err) {
     __shared__ int ok;
+    extern __shared__ float tfull[];  // [nb][R] rank-ordered sums of x.A^T, rounded to bf16
     if (blockIdx.x == 0 && threadIdx.x == 0) pdl_trigger();
     pdl_wait();
     if (threadIdx.x == 0) {
@@ -153,21 +160,57 @@ __global__ void k_tp_recv_resid(const float* __restrict__ inbox, size_t src_stri
     }
     __syncthreads();
     if (!ok) return;
+    const bool lora = rl.L.adapter != nullptr;
+    const int R = rl.L.rank, nb = n / H;
+    if (lora) {
+        for (int j = threadIdx.x; j < nb * R; j += blockDim.x) {
+            float t = 0.f;
+            for (int r = 0; r < tp; ++r) t += __ldcv(rl.t_inbox + (size_t)r * rl.t_src_stride + j);
+            tfull[j] = round_bf(t);  // the shrink output x.A^T (qwen_adapter_model.cpp:27)
+        }
+        __syncthreads();
+    }
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         float sum = 0.f;
         for (int r = 0; r < tp; ++r) sum += __ldcv(inbox + (size_t)r * src_stride + i);  // rank order
+        float v = round_bf(sum);
+        if (lora) {
+            const int b = i / H, row = i - b * H;
+            const int ad = rl.L.adapter[b];
+            if (ad >= 0 && ad < rl.L.n_adapters) {
+                const uint16_t* br = rl.L.B + (size_t)ad * rl.L.B_adapter_stride + (size_t)row * R;
+                const float* t = tfull + (size_t)b * R;
+                float s = 0.f;
+                for (int k = 0; k < R; ++k) s = fmaf(__uint_as_float((uint32_t)br[k] << 16), t[k], s);
+                v = round_bf(v + round_bf(round_bf(s) * rl.L.scale[ad]));  // qwen_adapter_model.cpp:28-29, :42
+            }
+        }
         const float rr = __uint_as_float((uint32_t)resid[i] << 16);
-        out[i] = __bfloat16_as_ushort(f2bf(rr + round_bf(sum)));
+        out[i] = __bfloat16_as_ushort(f2bf(rr + v));
     }
 }
 
 cudaError_t tp_recv_resid_launch(const float* inbox, size_t src_stride, const unsigned int* flags, int tp,
                                  const int* epoch, int seq_mul, int seq_add, const uint16_t* resid, uint16_t* out,
-                                 int nb, int H, int* err, cudaStream_t s, bool pdl) {
+                                 int nb, int H, const GemvLora* lora, const float* t_inbox, size_t t_src_stride,
+                                 int* err, cudaStream_t s, bool pdl) {
     int n = nb * H;
-    void* params[] = {&inbox, &src_stride, &flags, &tp, &epoch, &seq_mul, &seq_add, &resid, &out, &n, &err};
+    RecvLora rl;
+    size_t smem = 0;
+    if (lora && lora->adapter) {
+        rl.L = *lora;
+        rl.t_inbox = t_inbox;
+        rl.t_src_stride = t_src_stride;
+        smem = (size_t)nb * lora->rank * 4;
+        if (smem > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&k_tp_recv_resid),
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+        }
+    }
+    void* params[] = {&inbox, &src_stride, &flags, &tp, &epoch, &seq_mul, &seq_add, &resid, &out, &n, &H, &rl, &err};
     const int grid = std::min((n + 255) / 256, 148);
-    return launch_pdl(reinterpret_cast<const void*>(&k_tp_recv_resid), dim3(grid), dim3(256), 0, s, params, pdl);
+    return launch_pdl(reinterpret_cast<const void*>(&k_tp_recv_resid), dim3(grid), dim3(256), smem, s, params, pdl);
 }
 
 struct KeysArgs {

@@ -36,26 +36,29 @@ def _need(n):
         pytest.skip(f"needs {n} GPUs")
 
 
-def _oracle_schedule(kw, prompts, steps, seed, std):
+def _oracle_schedule(kw, prompts, steps, seed, std, adapters=(), per_seq=None):
     m = oracle.Model(**kw)
     m.init_synthetic(seed, std)
+    for i, (rank, alpha, mask, aseed, sa, sb) in enumerate(adapters):
+        m.add_adapter(i, rank, alpha, mask, aseed, sa, sb)
+    per_seq = per_seq or [-1] * len(prompts)
     feeds, ref = [], []
     seqs = [m.new_seq(128) for _ in prompts]
     last = []
-    for s, p in zip(seqs, prompts):
-        _, lf = s.forward(p)
+    for s, p, ad in zip(seqs, prompts, per_seq):
+        _, lf = s.forward(p, adapter=ad)
         last.append(lf)
     ref.append(np.stack(last))
     feed = [int(np.argmax(lf)) for lf in last]
     for _ in range(steps):
         feeds.append(list(feed))
-        rows = [s.forward([t])[1] for s, t in zip(seqs, feed)]
+        rows = [s.forward([t], adapter=ad)[1] for s, t, ad in zip(seqs, feed, per_seq)]
         ref.append(np.stack(rows))
         feed = [int(np.argmax(r)) for r in rows]
     return feeds, ref
 
 
-def _rank(rank, world, nid, kw, prompts, feeds, seed, std, q, mode):
+def _rank(rank, world, nid, kw, prompts, feeds, seed, std, q, mode, adapters, per_seq):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     os.environ["TI_TP_ALLREDUCE"] = mode
     sys.path.insert(0, os.path.join(ROOT, "tensor-inference_b200"))
@@ -63,20 +66,26 @@ def _rank(rank, world, nid, kw, prompts, feeds, seed, std, q, mode):
         import ti_b200 as tl
 
         B = len(prompts)
+        lo = dict(max_adapters=len(adapters), max_lora_rank=max(a[0] for a in adapters), lora_proj_mask=0x7F) \
+            if adapters else {}
         eng = tl.Engine(tl.model_desc(**kw), device=rank, max_batch=B, max_seqs=B, max_seq_len=128, tp_size=world,
-                        tp_rank=rank, nccl_id=nid)
+                        tp_rank=rank, nccl_id=nid, **lo)
         eng.init_synthetic(seed, std)
+        for (arank, alpha, mask, aseed, sa, sb) in adapters:
+            a = eng.adapter_create(arank, alpha, mask)
+            eng.adapter_init_synthetic(a, aseed, sa, sb)
+        per = per_seq or [-1] * B
         sids = [eng.seq_create() for _ in prompts]
         out_ids, out_logits = [], []
         ids0, lg0 = [], []
-        for sid, p in zip(sids, prompts):
-            nxt, lb = eng.prefill(sid, p, logits=tl.LOGITS_BF16)
+        for sid, p, ad in zip(sids, prompts, per):
+            nxt, lb = eng.prefill(sid, p, adapter=ad, logits=tl.LOGITS_BF16)
             ids0.append(int(nxt))
             lg0.append(lb)
         out_ids.append(ids0)
         out_logits.append(np.stack(lg0))
         for f in feeds:
-            nxt, lb = eng.decode(sids, f, logits=tl.LOGITS_BF16)
+            nxt, lb = eng.decode(sids, f, adapters=per if adapters else None, logits=tl.LOGITS_BF16)
             out_ids.append([int(x) for x in nxt])
             out_logits.append(lb)
         eng.check()
@@ -87,13 +96,13 @@ def _rank(rank, world, nid, kw, prompts, feeds, seed, std, q, mode):
         os._exit(1)
 
 
-def _run_tp(kw, prompts, steps, tol, seed=0, std=0.02, world=2, mode="peer"):
+def _run_tp(kw, prompts, steps, tol, seed=0, std=0.02, world=2, mode="peer", adapters=(), per_seq=None):
     _need(world)
-    feeds, ref = _oracle_schedule(kw, prompts, steps, seed, std)
+    feeds, ref = _oracle_schedule(kw, prompts, steps, seed, std, adapters, per_seq)
     nid = ti.nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, world, nid, kw, prompts, feeds, seed, std, q, mode)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, nid, kw, prompts, feeds, seed, std, q, mode, list(adapters), per_seq)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -143,3 +152,16 @@ def test_tp2_q4_0():
 def test_tp2_llama3_8b_shapes():
     kw = dict(ti.PRESETS["llama3_8b"], n_layers=2)
     _run_tp(kw, [oracle.fill_ids("t8", 6, 1, kw["vocab"])], steps=2, tol=2e-2)
+
+
+def test_tp2_lora_all_projections_mixed_adapters():
+    # row-parallel LoRA (o, down): partial x.A^T summed over ranks before the expansion
+    ads = [(8, 16.0, 0x7F, 21, 0.05, 0.05), (4, 8.0, 0x7F, 22, 0.05, 0.05)]
+    prompts = [oracle.fill_ids(f"tl{b}", n, b, SMALL["vocab"]) for b, n in enumerate((5, 8, 3, 6))]
+    _run_tp(SMALL, prompts, steps=3, tol=2e-2, adapters=ads, per_seq=[0, 1, -1, 0])
+
+
+def test_tp2_lora_tensor_core_batch():
+    ads = [(8, 16.0, 0x7F, 31, 0.05, 0.05), (8, 8.0, 0x0F, 32, 0.05, 0.05)]
+    prompts = [oracle.fill_ids(f"tm{b}", 2 + b % 3, b, SMALL["vocab"]) for b in range(12)]
+    _run_tp(SMALL, prompts, steps=2, tol=2e-2, adapters=ads, per_seq=[b % 3 - 1 for b in range(12)])
