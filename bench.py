@@ -243,6 +243,65 @@ def measure_qwen_lora(ti, torch, stream, peak, wf, steps, warmup, dev=0):
             "bytes_per_step": r["step_bytes"], "ctx_avg": r["ctx_avg"]}
 
 
+def measure_70b_tp(ti, torch, stream, peak, world, rank, dev, steps, warmup=3):
+    """Llama-3-70B shape, tensor-parallel over the job's GPUs,
+    batch 64 at 4096 tokens of context (cached K/V filled with seeded synthetic
+    values instead of a 4096-step prefill), 16 rank-64 LoRA adapters (alpha = rank,
+    scale 1) on all seven projections, assigned to sequences round-robin"""
+    import numpy as np
+    import torch.distributed as dist
+
+    B, CTX, R, NAD = 64, 4096, 64, 16
+    box = [ti.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    desc = ti.model_desc(**ti.PRESETS["llama3_70b"])
+    eng = ti.Engine(desc, device=dev, max_batch=B, max_seqs=B, max_seq_len=CTX + warmup + steps + 32,
+                    tp_size=world, tp_rank=rank, nccl_id=box[0], max_adapters=NAD, max_lora_rank=R,
+                    lora_proj_mask=0x7F)
+    try:
+        eng.init_synthetic(0, 0.02)
+        ads = []
+        for i in range(NAD):
+            a = eng.adapter_create(R, float(R), 0x7F)
+            eng.adapter_init_synthetic(a, 100 + i, 0.02, 0.001)
+            ads.append(a)
+        sids = [eng.seq_create() for _ in range(B)]
+        for i, sid in enumerate(sids):
+            eng.seq_fill_synthetic(sid, CTX - 1, seed=i, std=1.0)
+            eng.seq_reserve(sid, CTX + warmup + steps + 8)
+        per = [ads[i % NAD] for i in range(B)]
+        first = np.random.default_rng(0).integers(0, desc.vocab, size=B, dtype=np.int32)
+        eng.bind(sids, first, per)
+        for _ in range(warmup):
+            eng.decode_device(stream)
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(torch.cuda.current_stream())
+        for _ in range(steps):
+            eng.decode_device(stream)
+        ev1.record(torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1) / steps
+        eng.unbind(warmup + steps, stream)
+        eng.check()
+    finally:
+        eng.close()
+    t = torch.tensor([ms], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0])
+    H, I, hd = desc.hidden, desc.intermediate, desc.head_dim
+    qw, kw = desc.n_heads * hd, desc.n_kv_heads * hd
+    ins_outs = [(H, qw), (H, kw), (H, kw), (qw, H), (H, I), (H, I), (I, H)]
+    lora_bytes = NAD * desc.n_layers * sum(2 * R * (i + o) for i, o in ins_outs)
+    ctx_avg = CTX - 1 + warmup + (steps - 1) / 2.0
+    step_bytes = ti.algorithmic_bytes_per_step(desc, B, B * ctx_avg, lora_bytes)
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    return {"tok_s": round(B * 1e3 / ms, 1), "ms_per_step": round(ms, 3), "step_gbs": round(gbs, 1),
+            "frac_measured": round(gbs / (peak * world), 4), "bytes_per_step": step_bytes, "ctx_avg": ctx_avg,
+            "config": f"Llama-3-70B shape, tp{world}, batch 64, context 4096, 16 rank-64 LoRA adapters on all "
+                      "7 projections (round-robin); K/V context synthetic"}
+
+
 def kernel_roofline(ti, torch, eng, stream, peak, iters=64):
     """dominant kernel (gate|up GEMV, 2 x 14336 x 4096 bf16 = 235 MB per launch)
     timed alone with CUDA events on its launch stream, cycling layers so every
@@ -392,6 +451,10 @@ def run_ours(args, rank, world):
         eng.close()  # the 8B engine's 15 GB is not needed for the Qwen legs
         qwen = {name: measure_qwen_lora(ti, torch, stream, peak, wf, max(4, args.steps // 4), 3, dev)
                 for name, wf in (("bf16", ti.WFMT_BF16), ("q4_0", ti.WFMT_Q4_0))}
+    r70 = None
+    if args.big and world > 1:
+        eng.close()
+        r70 = measure_70b_tp(ti, torch, stream, peak, world, rank, dev, max(4, args.steps // 8))
 
     # the ranks of the tensor-parallel group step together; the job's time is the slowest rank's
     ms = r1["ms_per_step"]
@@ -439,6 +502,8 @@ def run_ours(args, rank, world):
                            "ctx_avg": r32["ctx_avg"]}
         if qwen:
             line["qwen7b_lora_b8"] = dict(qwen, config="Qwen2.5-7B shape, rank-16 LoRA q/k/v/o, batch 8, 256-token prompt")
+        if r70:
+            line["llama70b_tp_b64_lora"] = r70
         if pkm:
             # FP32 issue peak: 148 SMs x 128 lanes x SM clock during the run
             clk = (line["clocks"].get("sm_mhz") or 1965.0) * 1e6
@@ -463,6 +528,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-b32", dest="b32", action="store_false")
     ap.add_argument("--no-qwen", dest="qwen", action="store_false", help="skip the Qwen-7B LoRA legs (config 3)")
+    ap.add_argument("--no-70b", dest="big", action="store_false",
+                    help="skip the Llama-3-70B tensor-parallel leg (config 5, N >= 2 only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true", help="short ncu workload (see run_profile)")
     ap.add_argument("--layers", type=int, default=32)

@@ -209,6 +209,11 @@ ti_status ti_seq_reset(ti_engine* e, int seq_id);
 ti_status ti_seq_len(ti_engine* e, int seq_id, int* len);
 /* pre-allocate pages so the sequence can grow to n_tokens without host work */
 ti_status ti_seq_reserve(ti_engine* e, int seq_id, int n_tokens);
+/* Give a sequence n_tokens of synthetic cached context (pages allocated, K/V
+ * of every layer filled from the seeded generator, length set) without running
+ * them through the model: benchmarks of long-context decode.  No counterpart in
+ * the reference. */
+ti_status ti_seq_fill_synthetic(ti_engine* e, int seq_id, int n_tokens, uint64_t seed, float std_);
 /* copy K or V (which = 0/1) of one layer for positions [0, len) into host memory
  * as [len, n_kv_local, head_dim] bf16 (tests) */
 ti_status ti_seq_read_kv(ti_engine* e, int seq_id, int layer, int which, void* host_out, int len);

@@ -39,12 +39,22 @@ constexpr int kPage = 16;
 constexpr int kAttnMaxPages = 8;  // pages per split (128 tokens) the shared-memory tiles hold
 
 struct AttnSmem {
-    uint32_t kt, vt, qf, kn, vn, ml, sc, mw, bar, total;
+    uint32_t kt, vt, qf, kn, vn, ml, sc, mw, red, bar, total;
 };
+
+__host__ __device__ inline int attn_gp(int G) {
+    int gp = 1;
+    while (gp < G) gp <<= 1;
+    return gp;
+}
+// P.V thread layout: DPT consecutive dims x all GP heads per thread, TG token groups
+__host__ __device__ constexpr int attn_dpt(int GP) { return GP <= 8 ? 8 : 4; }
+__host__ __device__ constexpr int attn_tg(int HD, int GP) { return 128 / (HD / attn_dpt(GP)); }
 
 // C: tokens per split (pages x 16); offsets from a 1024-byte aligned base
 __host__ __device__ inline AttnSmem attn_layout(int G, int HD, int C, int n_splits) {
     AttnSmem L;
+    const int GP = attn_gp(G);
     uint32_t o = 0;
     L.kt = o;  // K tile [HD/64][C][64] bf16, rows 128-byte swizzled
     o += (uint32_t)C * HD * 2;
@@ -58,11 +68,20 @@ __host__ __device__ inline AttnSmem attn_layout(int G, int HD, int C, int n_spli
     o += HD * 4;
     L.ml = o;
     o += 2 * kAttnMaxGroup * 4;
-    L.sc = o;  // scores, then probabilities [G][C]
-    o += (uint32_t)G * C * 4;
+    L.sc = o;  // scores, then probabilities [C][GP] (heads >= G hold 0)
+    o += (uint32_t)GP * C * 4;
     L.mw = o;  // split merge: weights and sums [2][n_splits][G]
     o += 2u * n_splits * G * 4;
     o = (o + 15u) & ~15u;
+    // fold of the P.V token groups [TG-1][G][HD] fp32: over the K/V tiles (dead by
+    // then) when they are large enough, else its own region
+    const uint32_t red = (uint32_t)(attn_tg(HD, GP) - 1) * G * HD * 4;
+    if (red <= 2u * C * HD * 2) {
+        L.red = L.kt;
+    } else {
+        L.red = o;
+        o += red;
+    }
     L.bar = o;
     o += 16;
     L.total = o + 1024;
@@ -110,6 +129,7 @@ __global__ void __launch_bounds__(kAttnThreads)
     float* ml = reinterpret_cast<float*>(smem + L.ml);
     float* sc = reinterpret_cast<float*>(smem + L.sc);
     float* mw = reinterpret_cast<float*>(smem + L.mw);
+    float* red = reinterpret_cast<float*>(smem + L.red);
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);
     __shared__ int s_last;
 
@@ -223,8 +243,10 @@ __global__ void __launch_bounds__(kAttnThreads)
             for (int e = 0; e < 2; ++e) {
                 const int jj = r0 + c2 + e;
                 const bool valid = jj >= vlo && jj < vhi;
-                if (r < G) sc[r * C + jj] = valid ? a.scale * acc[e] : -INFINITY;
-                if (r + 8 < G) sc[(r + 8) * C + jj] = valid ? a.scale * acc[2 + e] : -INFINITY;
+                if (r < G) sc[jj * GP + r] = valid ? a.scale * acc[e] : -INFINITY;
+                else if (r < GP) sc[jj * GP + r] = 0.f;  // padding heads: probability 0
+                if (r + 8 < G) sc[jj * GP + r + 8] = valid ? a.scale * acc[2 + e] : -INFINITY;
+                else if (r + 8 < GP) sc[jj * GP + r + 8] = 0.f;
             }
         }
     }
@@ -233,12 +255,12 @@ __global__ void __launch_bounds__(kAttnThreads)
     // ---- softmax statistics per q head (ops.cu:393-419)
     for (int g = warp; g < G; g += kAttnThreads / 32) {
         float m = -INFINITY;
-        for (int j = lane; j < n_rows; j += 32) m = fmaxf(m, sc[g * C + j]);
+        for (int j = lane; j < n_rows; j += 32) m = fmaxf(m, sc[j * GP + g]);
         m = warp_max(m);
         float l = 0.f;
         for (int j = lane; j < n_rows; j += 32) {
-            const float p = m == -INFINITY ? 0.f : expf(sc[g * C + j] - m);
-            sc[g * C + j] = p;
+            const float p = m == -INFINITY ? 0.f : expf(sc[j * GP + g] - m);
+            sc[j * GP + g] = p;
             l += p;
         }
         l = warp_sum(l);
@@ -249,59 +271,102 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
     __syncthreads();
 
-    // ---- P.V (ops.cu:526-539) in fp32: thread -> 4 dims of one head slot
-    constexpr int DG = HD / 4;
-    constexpr int SLOTS = kAttnThreads / DG;
-    constexpr int HPS = (GP + SLOTS - 1) / SLOTS;
-    const int slot = tid / DG, dd = (tid % DG) * 4;
-    float acc[HPS][4];
+    // ---- P.V (ops.cu:526-539) in fp32: thread -> DPT consecutive dims of every
+    //      head of the group, over the tokens of its token group (j = tg mod TG);
+    //      packed f32x2 FMAs; the token groups are folded in order afterwards
+    constexpr int DPT = attn_dpt(GP);
+    constexpr int NDG = HD / DPT;
+    constexpr int TG = kAttnThreads / NDG;
+    const int dg = tid % NDG, tg = tid / NDG, d0 = dg * DPT;
+    float2 acc[GP][DPT / 2];
 #pragma unroll
-    for (int k = 0; k < HPS; ++k)
+    for (int g = 0; g < GP; ++g)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[k][e] = 0.f;
-    {
-        const uint8_t* vcol = vt + (dd >> 6) * C * 128 + ((dd & 7) << 1);
-        const int cc = (dd & 63) >> 3;
-        for (int j = max(vlo, 0); j < vhi; ++j) {
-            const uint2 v = *reinterpret_cast<const uint2*>(vcol + j * 128 + ((cc ^ (j & 7)) << 4));
-            const float2 v01 = bf2_to_f2(v.x), v23 = bf2_to_f2(v.y);
-#pragma unroll
-            for (int k = 0; k < HPS; ++k) {
-                const int g = slot + k * SLOTS;
-                if (g < G) {
-                    const float p = sc[g * C + j];
-                    acc[k][0] = fmaf(p, v01.x, acc[k][0]);
-                    acc[k][1] = fmaf(p, v01.y, acc[k][1]);
-                    acc[k][2] = fmaf(p, v23.x, acc[k][2]);
-                    acc[k][3] = fmaf(p, v23.y, acc[k][3]);
-                }
-            }
+        for (int k = 0; k < DPT / 2; ++k) acc[g][k] = make_float2(0.f, 0.f);
+    for (int j = max(vlo, 0) + tg; j < vhi; j += TG) {
+        float2 vf[DPT / 2];
+        if constexpr (DPT == 8) {
+            const uint4 v = *reinterpret_cast<const uint4*>(vt + tile_off(C, j, d0));
+            vf[0] = bf2_to_f2(v.x);
+            vf[1] = bf2_to_f2(v.y);
+            vf[2] = bf2_to_f2(v.z);
+            vf[3] = bf2_to_f2(v.w);
+        } else {
+            const uint2 v = *reinterpret_cast<const uint2*>(vt + tile_off(C, j, d0));
+            vf[0] = bf2_to_f2(v.x);
+            vf[1] = bf2_to_f2(v.y);
         }
+        float p[GP];
+        if constexpr (GP >= 4) {
+#pragma unroll
+            for (int g = 0; g < GP; g += 4) {
+                const float4 q4 = *reinterpret_cast<const float4*>(sc + j * GP + g);
+                p[g] = q4.x;
+                p[g + 1] = q4.y;
+                p[g + 2] = q4.z;
+                p[g + 3] = q4.w;
+            }
+        } else {
+#pragma unroll
+            for (int g = 0; g < GP; ++g) p[g] = sc[j * GP + g];
+        }
+#pragma unroll
+        for (int g = 0; g < GP; ++g) {
+            const float2 pp = make_float2(p[g], p[g]);
+#pragma unroll
+            for (int k = 0; k < DPT / 2; ++k) acc[g][k] = ffma2(pp, vf[k], acc[g][k]);
+        }
+    }
+    if (TG > 1) {
+        __syncthreads();  // the K/V tiles are dead: the fold area may overlay them
+        if (tg > 0)
+#pragma unroll
+            for (int g = 0; g < GP; ++g)
+                if (g < G)
+#pragma unroll
+                    for (int k = 0; k < DPT / 2; ++k)
+                        *reinterpret_cast<float2*>(red + (((size_t)(tg - 1) * G + g) * HD + d0 + 2 * k)) = acc[g][k];
+        __syncthreads();
+        if (tg == 0)
+            for (int t = 0; t < TG - 1; ++t)
+#pragma unroll
+                for (int g = 0; g < GP; ++g)
+                    if (g < G)
+#pragma unroll
+                        for (int k = 0; k < DPT / 2; ++k) {
+                            const float2 o =
+                                *reinterpret_cast<const float2*>(red + (((size_t)t * G + g) * HD + d0 + 2 * k));
+                            acc[g][k].x += o.x;
+                            acc[g][k].y += o.y;
+                        }
     }
 
     if (a.n_splits == 1) {
+        if (tg == 0)
 #pragma unroll
-        for (int k = 0; k < HPS; ++k) {
-            const int g = slot + k * SLOTS;
-            if (g < G) {
-                const float l = ml[2 * g + 1];
-                bf16* dst = reinterpret_cast<bf16*>(a.out) + (size_t)b * a.out_stride + (size_t)(h * G + g) * HD + dd;
+            for (int g = 0; g < GP; ++g)
+                if (g < G) {
+                    const float l = ml[2 * g + 1];
+                    bf16* dst =
+                        reinterpret_cast<bf16*>(a.out) + (size_t)b * a.out_stride + (size_t)(h * G + g) * HD + d0;
 #pragma unroll
-                for (int e = 0; e < 4; ++e) dst[e] = f2bf(acc[k][e] / l);
-            }
-        }
+                    for (int k = 0; k < DPT / 2; ++k) {
+                        dst[2 * k] = f2bf(acc[g][k].x / l);
+                        dst[2 * k + 1] = f2bf(acc[g][k].y / l);
+                    }
+                }
         return;
     }
 
     // ---- partial results, merged by the last CTA of this (token, kv head)
     const size_t pbase = (((size_t)b * a.nkv + h) * a.n_splits + split) * G;
+    if (tg == 0)
 #pragma unroll
-    for (int k = 0; k < HPS; ++k) {
-        const int g = slot + k * SLOTS;
-        if (g < G)
-            *reinterpret_cast<float4*>(a.part_o + (pbase + g) * HD + dd) =
-                make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
-    }
+        for (int g = 0; g < GP; ++g)
+            if (g < G)
+#pragma unroll
+                for (int k = 0; k < DPT / 2; ++k)
+                    *reinterpret_cast<float2*>(a.part_o + (pbase + g) * HD + d0 + 2 * k) = acc[g][k];
     if (tid < G) {
         a.part_ml[(pbase + tid) * 2] = ml[2 * tid];
         a.part_ml[(pbase + tid) * 2 + 1] = ml[2 * tid + 1];
@@ -404,8 +469,7 @@ cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s, bool pdl) {
     if (a.max_chunk < kPage || a.max_chunk > kAttnMaxPages * kPage || a.max_chunk % kPage != 0)
         return cudaErrorInvalidValue;
     const int G = a.nq / a.nkv;
-    int gp = 1;
-    while (gp < G) gp <<= 1;
+    const int gp = attn_gp(G);
     const void* f = nullptr;
     switch (a.hd) {
         case 64: f = attn_func<64>(gp); break;

@@ -1267,6 +1267,33 @@ ti_status ti_seq_reserve(ti_engine* e, int sid, int n_tokens) {
     return TI_OK;
 }
 
+ti_status ti_seq_fill_synthetic(ti_engine* e, int sid, int n_tokens, uint64_t seed, float std_) {
+    clear_error();
+    TI_CHECK(e, TI_ERR_INVALID, "null engine");
+    if (ti_status st = seq_check(e, sid)) return st;
+    TI_CHECK(n_tokens >= 0 && n_tokens < e->o.max_seq_len, TI_ERR_INVALID, "n_tokens %d out of [0, %d)", n_tokens,
+             e->o.max_seq_len);
+    std::vector<int32_t> upd;
+    if (ti_status st = ensure_pages(e, sid, n_tokens, &upd)) return st;
+    DeviceGuard g(e->dev);
+    for (size_t i = 0; i < upd.size(); i += 3)
+        TI_CUDA(cudaMemcpy(e->page_table + (size_t)upd[i] * e->pt_stride + upd[i + 1], &upd[i + 2], 4,
+                           cudaMemcpyHostToDevice));
+    const std::vector<int>& pages = e->seqs[sid].pages;
+    int32_t* dpages = nullptr;
+    TI_CUDA(cudaMalloc(&dpages, std::max<size_t>(1, pages.size()) * 4));
+    cudaError_t err = cudaMemcpy(dpages, pages.data(), pages.size() * 4, cudaMemcpyHostToDevice);
+    if (err == cudaSuccess)
+        err = fill_kv_launch(e->kpool, e->vpool, e->kv_layer_elems, e->d.n_layers, dpages, n_tokens, e->nkv,
+                             e->tp.kv0, e->d.n_kv_heads, e->hd, mix64(seed ^ fnv1a("kv.k")), mix64(seed ^ fnv1a("kv.v")),
+                             synth_scale(std_), 0);
+    if (err == cudaSuccess) err = cudaDeviceSynchronize();
+    cudaFree(dpages);
+    TI_CHECK(err == cudaSuccess, TI_ERR_CUDA, "seq_fill_synthetic: %s", cudaGetErrorString(err));
+    e->seqs[sid].len = n_tokens;
+    return TI_OK;
+}
+
 ti_status ti_seq_read_kv(ti_engine* e, int sid, int layer, int which, void* host, int len) {
     clear_error();
     TI_CHECK(e && host, TI_ERR_INVALID, "null argument");

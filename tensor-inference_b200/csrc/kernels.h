@@ -246,6 +246,10 @@ struct EmbedArgs {
 };
 cudaError_t embed_launch(const EmbedArgs& a, cudaStream_t s, bool pdl);
 
+// synthetic K/V rows for positions [0, n_tok) of one sequence (its pages[]), all layers
+cudaError_t fill_kv_launch(uint16_t* kpool, uint16_t* vpool, size_t layer_elems, int n_layers, const int32_t* pages,
+                           int n_tok, int nkv, int kv0, int nkv_g, int hd, uint64_t key_k, uint64_t key_v, float c,
+                           cudaStream_t s);
 // synthetic init of a [rows, cols] window (row stride dst_ld) of a full tensor
 // with row length full_ld: dst[r][c] = gen(index (r0 + r) * full_ld + c0 + c)
 cudaError_t synth_bf16_launch(uint16_t* dst, size_t rows, size_t cols, size_t dst_ld, size_t r0, size_t c0,

@@ -285,4 +285,36 @@ cudaError_t tp_keys_launch(unsigned long long* amax, int nb, unsigned long long*
     return launch_pdl(reinterpret_cast<const void*>(&k_tp_keys), dim3(1), dim3(256), 0, s, params, pdl);
 }
 
+
+// synthetic KV cache content: pages of one sequence, every layer, K and V;
+// element (layer, global kv head, position, dim) gets the generator value of its
+// index, so tensor-parallel shards hold the same values as a single-GPU cache
+__global__ void k_fill_kv(uint16_t* kpool, uint16_t* vpool, size_t layer_elems, int n_layers, const int32_t* pages,
+                          int n_tok, int nkv, int kv0, int nkv_g, int hd, uint64_t key_k, uint64_t key_v, float c) {
+    const size_t per_layer = (size_t)n_tok * nkv * hd;
+    const size_t total = per_layer * n_layers;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int layer = (int)(i / per_layer);
+        size_t r = i - (size_t)layer * per_layer;
+        const int pos = (int)(r / ((size_t)nkv * hd));
+        r -= (size_t)pos * nkv * hd;
+        const int h = (int)(r / hd), d = (int)(r - (size_t)h * hd);
+        const size_t dst = (size_t)layer * layer_elems + (((size_t)pages[pos / 16] * nkv + h) * 16 + pos % 16) * hd + d;
+        const size_t gi = (((size_t)layer * nkv_g + kv0 + h) * 1048576u + pos) * hd + d;
+        kpool[dst] = __bfloat16_as_ushort(__float2bfloat16_rn(__fmul_rn((float)synth_centered(key_k, gi), c)));
+        vpool[dst] = __bfloat16_as_ushort(__float2bfloat16_rn(__fmul_rn((float)synth_centered(key_v, gi), c)));
+    }
+}
+
+cudaError_t fill_kv_launch(uint16_t* kpool, uint16_t* vpool, size_t layer_elems, int n_layers, const int32_t* pages,
+                           int n_tok, int nkv, int kv0, int nkv_g, int hd, uint64_t key_k, uint64_t key_v, float c,
+                           cudaStream_t s) {
+    const size_t total = (size_t)n_tok * nkv * hd * n_layers;
+    if (total == 0) return cudaSuccess;
+    const unsigned grid = (unsigned)std::min<size_t>((total + 255) / 256, 148 * 32);
+    k_fill_kv<<<grid, 256, 0, s>>>(kpool, vpool, layer_elems, n_layers, pages, n_tok, nkv, kv0, nkv_g, hd, key_k,
+                                   key_v, c);
+    return cudaGetLastError();
+}
+
 }  // namespace ti

@@ -59,6 +59,7 @@ class TpShard(C.Structure):
 
 
 _SIGS = {
+    "ti_seq_fill_synthetic": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_uint64, C.c_float]),
     "ti_nccl_unique_id": (C.c_int, [C.c_void_p]),
     "ti_tp_plan": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "ti_last_error": (C.c_char_p, []),
@@ -358,6 +359,10 @@ class Engine:
 
     def seq_reserve(self, sid, n_tokens):
         check(lib().ti_seq_reserve(self.h, sid, n_tokens))
+
+    def seq_fill_synthetic(self, sid, n_tokens, seed=0, std=1.0):
+        """n_tokens of synthetic cached context for sequence sid (long-context benchmarks)"""
+        check(lib().ti_seq_fill_synthetic(self.h, sid, n_tokens, seed, std))
 
     def seq_read_kv(self, sid, layer, which, length):
         out = np.empty((length, self.desc.n_kv_heads // max(1, self.opts.tp_size), self.desc.head_dim), np.uint16)
