@@ -154,6 +154,7 @@ struct ti_engine {
     int lK[4] = {}, lT[4] = {}, lRows[4] = {};  // A row length, A rows (sections*R), B rows
     float* lscale = nullptr;
     float* lt[4] = {};  // shrink outputs [B][T]
+    uint16_t* ldval = nullptr;  // expansions ahead of the tensor-core GEMM [B][rows] bf16
     std::vector<AdapterMeta> adapters;
     cudaStream_t side = nullptr;
 
@@ -487,6 +488,11 @@ ti_status build(ti_engine* e) {
             TI_CHECK(dalloc_t(e, &e->lB[k], nbb, &e->bytes_ad) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
             TI_CUDA(cudaMemset(e->lA[k], 0, na * 2));
             TI_CUDA(cudaMemset(e->lB[k], 0, nbb * 2));
+            if (!e->ldval && e->xn) {
+                const size_t rmax = std::max<size_t>(std::max<size_t>(e->qkv_rows, H), 2 * (size_t)I);
+                TI_CHECK(dalloc_t(e, &e->ldval, (size_t)std::min(B, 256) * rmax, &e->bytes_work) == TI_OK, TI_ERR_OOM,
+                         "%s", ti_last_error());
+            }
             TI_CHECK(dalloc_t(e, &e->lt[k], (size_t)B * T[k], &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
                      ti_last_error());
         }
@@ -573,6 +579,14 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             a.x = e->xn;
             a.x_stride = a.K;
             a.norm_w = nullptr;
+        }
+        if (a.lora.adapter && e->ldval) {
+            // LoRA expansion of every (token, row) ahead of the GEMM; its epilogue adds it
+            const int rows = epi == kEpiGlu ? 2 * a.N : a.N;
+            TI_CUDA(lora_expand_launch(a.lora, B, rows, epi == kEpiGlu ? a.N : 0, e->ldval, rows, s, true));
+            if (launches) ++*launches;
+            a.lora.dval = e->ldval;
+            a.lora.dval_stride = rows;
         }
         TcPlan plan;
         if (!tc_plan(a, epi, e->dev, e->tc_ws_floats, &plan, &why)) return fail(TI_ERR_UNSUPPORTED, "%s", why.c_str());

@@ -36,7 +36,17 @@ struct GemvLora {
     int n_adapters = 0;
     // fused q|k|v rows: rows [0,sec1) use t[0:rank), [sec1,sec2) t[rank:2rank), the rest t[2rank:3rank)
     int sec1 = 1 << 30, sec2 = 1 << 30;
+    // when set: the expansion bf16(bf16(t.B^T) * scale) of every (token, row) was
+    // computed ahead by lora_expand_launch ([nb, dval_stride] bf16, rows as the
+    // GEMM's output rows); the epilogue only adds it
+    const uint16_t* dval = nullptr;
+    int dval_stride = 0;
 };
+
+// LoRA expansion ahead of a batched GEMM: dval[b, n] = bf16(bf16(sum_r B[ad_b][n, r] t[b, r']) * scale[ad_b])
+// for rows [0, n_rows) (kEpiGlu: glu_n gate rows then glu_n up rows, t sections 0 / 1)
+cudaError_t lora_expand_launch(const GemvLora& L, int nb, int n_rows, int glu_n, uint16_t* dval, int dval_stride,
+                               cudaStream_t s, bool pdl);
 
 // One-shot all-reduce over NVLink peer memory (tensor parallelism).  The
 // producer (a row-parallel projection) stores its fp32 outputs straight into

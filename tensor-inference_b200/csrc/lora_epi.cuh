@@ -26,4 +26,13 @@ TI_DEVICE_INLINE float lora_delta(const GemvLora& L, int ad, int b, int row, int
     return round_bf(base + delta);
 }
 
+// token b, output row `row`: the expansion precomputed in L.dval when present,
+// else computed here (qwen_adapter_model.cpp:27-29 + :42)
+TI_DEVICE_INLINE float lora_add(const GemvLora& L, int b, int row, int t_off, float base) {
+    const int ad = L.adapter[b];
+    if (ad < 0 || ad >= L.n_adapters) return base;
+    if (L.dval) return round_bf(base + __uint_as_float((uint32_t)L.dval[(size_t)b * L.dval_stride + row] << 16));
+    return lora_delta(L, ad, b, row, t_off, base);
+}
+
 }  // namespace ti

@@ -44,7 +44,6 @@
 #include "common.cuh"
 #include "internal.h"
 #include "kernels.h"
-#include "lora_epi.cuh"
 
 namespace ti {
 
@@ -388,6 +387,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const bool row_ok = n < a.N;
             const int nchunks = np / 32;
 
+            // the LoRA expansion precomputed by lora_expand_launch, added to a bf16 projection
+            auto lora_dval = [&](int b, int row, float base) {
+                const int ad = a.lora.adapter[b];
+                if (ad < 0 || ad >= a.lora.n_adapters) return base;
+                return round_bf(base +
+                                __uint_as_float((uint32_t)a.lora.dval[(size_t)b * a.lora.dval_stride + row] << 16));
+            };
             auto apply = [&](int c, const float* v) {
                 // v[i] = accumulator of (row n, token c*32 + i)
                 if (kGlu) {
@@ -396,8 +402,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         for (int i = 0; i < 32; ++i) {
                             const int b = c * 32 + i;
                             float uv = round_bf(v[i]);
-                            if (a.lora.adapter && b < a.nb && row_ok)
-                                uv = lora_delta(a.lora, a.lora.adapter[b], b, a.N + n, a.lora.rank, uv);
+                            if (a.lora.adapter && b < a.nb && row_ok) uv = lora_dval(b, a.N + n, uv);
                             xq[i * 32 + lane] = uv;
                         }
                     }
@@ -407,7 +412,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             const int b = c * 32 + i;
                             if (b >= a.nb) break;
                             float gv = round_bf(v[i]);
-                            if (a.lora.adapter) gv = lora_delta(a.lora, a.lora.adapter[b], b, n, 0, gv);
+                            if (a.lora.adapter) gv = lora_dval(b, n, gv);
                             const float uv = xq[i * 32 + lane];
                             reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + n] = f2bf(tc_act(gv, a.act) * uv);
                         }
@@ -436,11 +441,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             if (b >= a.nb) break;
                             float val = round_bf(v[i]);
                             if (a.bias) val = round_bf(val + bv);
-                            if (a.lora.adapter) {
-                                // sections of the fused q|k|v rows: t offset = section * rank
-                                const int sec = (n >= a.lora.sec1) + (n >= a.lora.sec2);
-                                val = lora_delta(a.lora, a.lora.adapter[b], b, n, sec * a.lora.rank, val);
-                            }
+                            if (a.lora.adapter) val = lora_dval(b, n, val);
                             reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + n] = f2bf(val);
                         }
                     }
@@ -450,7 +451,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             const int b = c * 32 + i;
                             if (b >= a.nb) break;
                             float val = round_bf(v[i]);
-                            if (a.lora.adapter) val = lora_delta(a.lora, a.lora.adapter[b], b, n, 0, val);
+                            if (a.lora.adapter) val = lora_dval(b, n, val);
                             const float rr = __uint_as_float((uint32_t)a.resid[(size_t)b * a.resid_stride + n] << 16);
                             reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + n] = f2bf(rr + val);
                         }
@@ -702,6 +703,10 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
     }
     if (g.wfmt != kWBf16) {
         if (why) *why = "tc_gemm: bf16 weights only";
+        return false;
+    }
+    if (g.lora.adapter && !g.lora.dval) {
+        if (why) *why = "tc_gemm: the LoRA expansion must be precomputed (lora_expand_launch)";
         return false;
     }
     // tokens padded to whole 32-column TMEM loads
