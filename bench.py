@@ -375,14 +375,21 @@ def run_profile(args):
     ts = torch.cuda.Stream()
     torch.cuda.set_stream(ts)
     desc = ti.model_desc(**dict(ti.PRESETS["llama3_8b"], n_layers=args.layers))
+    ctx = args.ctx or args.prompt
     eng = ti.Engine(desc, device=0, max_batch=args.batch, max_seqs=args.batch,
-                    max_seq_len=args.prompt + args.warmup + args.steps + 64)
+                    max_seq_len=ctx + args.warmup + args.steps + 64)
     eng.init_synthetic(0, 0.02)
     sids = [eng.seq_create() for _ in range(args.batch)]
-    prompts = np.random.default_rng(0).integers(0, desc.vocab, size=(args.batch, args.prompt), dtype=np.int32)
-    first = prefill_lockstep(eng, sids, prompts)
+    if args.ctx:
+        # synthetic cached context instead of a prefill (long-context kernels)
+        for i, s in enumerate(sids):
+            eng.seq_fill_synthetic(s, ctx - 1, seed=i)
+        first = np.random.default_rng(0).integers(0, desc.vocab, size=args.batch, dtype=np.int32)
+    else:
+        prompts = np.random.default_rng(0).integers(0, desc.vocab, size=(args.batch, args.prompt), dtype=np.int32)
+        first = prefill_lockstep(eng, sids, prompts)
     for s in sids:
-        eng.seq_reserve(s, args.prompt + args.warmup + args.steps + 8)
+        eng.seq_reserve(s, ctx + args.warmup + args.steps + 8)
     eng.bind(sids, first)
     for _ in range(args.warmup):
         eng.decode_device(ts.cuda_stream)
@@ -536,6 +543,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=32)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--kernel", type=int, default=None, help="profile: launch only this kernel kind")
+    ap.add_argument("--ctx", type=int, default=0, help="profile: synthetic cached context of this length")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank = int(os.environ.get("RANK", "0"))
