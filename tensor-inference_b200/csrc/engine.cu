@@ -567,10 +567,11 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         return TI_OK;
     };
 
-    // batches of tc_min..256 tokens with bf16 weights: RMSNorm pass (when the
-    // GEMV would fuse it) + tcgen05 GEMM (LoRA expansion in its epilogue)
+    // batches of tc_min..256 tokens: RMSNorm pass (when the GEMV would fuse it) +
+    // tcgen05 GEMM (GGUF weights dequantised to bf16 operands in shared memory;
+    // the LoRA expansion precomputed and added in its epilogue)
     auto gemm = [&](GemvArgs a, int epi, int x_stride_elems, int out_stride, int resid_stride) -> ti_status {
-        if (!(e->xn && B >= e->tc_min && B <= 256 && a.wfmt == kWBf16))
+        if (!(e->xn && B >= e->tc_min && B <= 256))
             return gemv_all(a, epi, x_stride_elems, out_stride, resid_stride);
         a.nb = B;
         if (a.norm_w) {

@@ -170,6 +170,8 @@ struct TcPlan {
     int np = 0;  // tokens padded to a multiple of 32 (MMA N)
     int tiles = 0, kbs = 1, kblocks = 0, kpc = 0, grid = 0, stages = 0;  // kpc: k-blocks per CTA (stream-K)
     uint32_t stage_bytes = 0, tmem_cols = 0;
+    uint32_t w_off = 0, x_off = 0, s_off = 0;  // stage layout (weights / tokens / GGUF scales)
+    int cb = 0, n_abuf = 0, threads = 0;       // GGUF: code bytes per atom row, dequantised buffers
     size_t smem = 0;
     size_t ws_floats = 0;  // partial-tile workspace this launch needs
     const void* func = nullptr;

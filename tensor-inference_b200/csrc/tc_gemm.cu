@@ -49,7 +49,8 @@ namespace ti {
 
 namespace {
 
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 192;    // bf16 weights: TMA, MMA, 4 epilogue warps
+constexpr int kTcThreadsQ = 448;   // GGUF weights: + 8 dequantising warps
 constexpr int kTcBM = 128;        // weight rows per tile (MMA M)
 constexpr int kTcBK = 64;         // K elements per swizzle atom: one 128-byte row
 constexpr uint32_t kTcABytes = kTcBM * kTcBK * 2;  // 16 KB weight atom (128 rows x 64 K)
@@ -125,6 +126,11 @@ struct TcKernelArgs {
     int kbs;
     int kpc;             // k-blocks per CTA: CTA c owns global k-blocks [c * kpc, (c + 1) * kpc)
     int stages;
+    // stage layout: bf16: [kbs weight atoms][kbs token atoms]; GGUF: [kbs token atoms]
+    // [codes: 128 rows x kbs*cb bytes][scales: 128 rows x kbs*4 bytes], dequantised
+    // into n_abuf bf16 operand buffers of kbs atoms after the ring
+    uint32_t w_off, x_off, s_off;
+    int cb, n_abuf;
     uint32_t stage_bytes, tmem_cols;
     uint16_t* out;
     int out_stride;
@@ -149,15 +155,21 @@ struct TcKernelArgs {
 
 // Shared memory after the stage ring (offsets from the 1024-aligned base).
 struct TcSmem {
-    uint32_t full, empty, tfull, tempty, drain, misc, xch, best, total;
+    uint32_t abuf, full, empty, afull, aempty, tfull, tempty, drain, misc, xch, best, total;
 };
-__host__ __device__ inline TcSmem tc_smem_layout(int stages, uint32_t stage_bytes, int np) {
+__host__ __device__ inline TcSmem tc_smem_layout(int stages, uint32_t stage_bytes, int np, int n_abuf, int kbs) {
     TcSmem L;
     uint32_t o = (uint32_t)stages * stage_bytes;
+    L.abuf = o;  // dequantised bf16 weight atoms (GGUF weights)
+    o += (uint32_t)n_abuf * kbs * kTcABytes;
     L.full = o;
     o += 8u * stages;
     L.empty = o;
     o += 8u * stages;
+    L.afull = o;
+    o += 16;
+    L.aempty = o;
+    o += 16;
     L.tfull = o;
     o += 16;
     L.tempty = o;
@@ -175,12 +187,18 @@ __host__ __device__ inline TcSmem tc_smem_layout(int stages, uint32_t stage_byte
     return L;
 }
 
-template <int EPI>
-__global__ void __launch_bounds__(kTcThreads, 1)
-    k_tc_gemm(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx, const TcKernelArgs a) {
+// WF: weight format (bf16 rows through 128-byte-swizzled TMA atoms, or GGUF rows:
+// codes and scales through plain TMA boxes, dequantised to bf16 atoms in shared memory)
+template <int EPI, int WF>
+__global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
+    k_tc_gemm(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
+              const __grid_constant__ CUtensorMap tms, const TcKernelArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const TcSmem L = tc_smem_layout(a.stages, a.stage_bytes, a.np);
+    const TcSmem L = tc_smem_layout(a.stages, a.stage_bytes, a.np, a.n_abuf, a.kbs);
+    uint64_t* afull = reinterpret_cast<uint64_t*>(smem + L.afull);
+    uint64_t* aempty = reinterpret_cast<uint64_t*>(smem + L.aempty);
+    constexpr bool kQ = WF != kWBf16;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.full);
     uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L.empty);
     uint64_t* tfull = reinterpret_cast<uint64_t*>(smem + L.tfull);
@@ -204,13 +222,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int j = 0; j < 2; ++j) {
             mbar_init(&tfull[j], 1);
             mbar_init(&tempty[j], 4);
+            mbar_init(&afull[j], 8);   // the dequantising warps
+            mbar_init(&aempty[j], 1);  // tcgen05.commit
         }
         mbar_init(drain, 1);
         misc[1] = 0;
         fence_barrier_init();
     }
     if (EPI == kEpiLmHead)
-        for (int i = threadIdx.x; i < np; i += kTcThreads) best[i] = 0ull;
+        for (int i = threadIdx.x; i < np; i += blockDim.x) best[i] = 0ull;
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32((const void*)&misc[0])),
@@ -261,14 +281,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0) {
             tmap_prefetch(&tmw);
             tmap_prefetch(&tmx);
+            if (kQ) tmap_prefetch(&tms);
             const uint64_t pol = l2_policy_evict_first();
             const int kbs = a.kbs;
             const uint32_t xatom = (uint32_t)np * kTcBK * 2;
-            const uint32_t tx = (uint32_t)kbs * (kTcABytes + xatom);
+            const uint32_t tx = kQ ? (uint32_t)kbs * xatom + (uint32_t)kTcBM * kbs * (a.cb + 4)
+                                   : (uint32_t)kbs * (kTcABytes + xatom);
             auto load_w = [&](int tile, int kb, int s) {
+                uint8_t* st = smem + (size_t)s * a.stage_bytes;
+                if (kQ) {
+                    // the codes and fp16 scales of kbs*64 columns of 128 rows (two halves of 64 for GLU)
+                    const int xc = kb * kbs * a.cb, xs = kb * kbs * 4;
+                    if (kGlu) {
+                        const uint32_t half_c = 64u * kbs * a.cb, half_s = 64u * kbs * 4;
+                        tma_load_2d_hint(st + a.w_off, &tmw, xc, tile * 64, &full[s], pol);
+                        tma_load_2d_hint(st + a.w_off + half_c, &tmw, xc, a.N + tile * 64, &full[s], pol);
+                        tma_load_2d_hint(st + a.s_off, &tms, xs, tile * 64, &full[s], pol);
+                        tma_load_2d_hint(st + a.s_off + half_s, &tms, xs, a.N + tile * 64, &full[s], pol);
+                    } else {
+                        tma_load_2d_hint(st + a.w_off, &tmw, xc, tile * kTcBM, &full[s], pol);
+                        tma_load_2d_hint(st + a.s_off, &tms, xs, tile * kTcBM, &full[s], pol);
+                    }
+                    return;
+                }
                 // kbs adjacent 64-column atoms of each weight row back to back, so
                 // DRAM sees kbs * 128 contiguous bytes per row
-                uint8_t* st = smem + (size_t)s * a.stage_bytes;
                 for (int j = 0; j < kbs; ++j) {
                     const int x = (kb * kbs + j) * kTcBK;
                     uint8_t* at = st + (size_t)j * kTcABytes;
@@ -281,7 +318,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             };
             auto load_x = [&](int kb, int s) {
-                uint8_t* xt = smem + (size_t)s * a.stage_bytes + (size_t)kbs * kTcABytes;
+                uint8_t* xt = smem + (size_t)s * a.stage_bytes + a.x_off;
                 for (int j = 0; j < kbs; ++j)
                     tma_load_2d(xt + (size_t)j * xatom, &tmx, (kb * kbs + j) * kTcBK, 0, &full[s]);
             };
@@ -339,9 +376,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         misc[1] = 1;
                         return false;
                     }
+                    const int ab = kQ ? it % a.n_abuf : 0;
+                    if (kQ && (misc[1] || !mbar_wait(&afull[ab], (it / a.n_abuf) & 1, a.err, kErrTimeoutFull))) {
+                        misc[1] = 1;
+                        return false;
+                    }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(smem + (size_t)s * a.stage_bytes);
-                    const uint32_t b_addr = a_addr + (uint32_t)a.kbs * kTcABytes;
+                    const uint32_t st_addr = smem_u32(smem + (size_t)s * a.stage_bytes);
+                    const uint32_t a_addr =
+                        kQ ? smem_u32(smem + L.abuf + (size_t)ab * a.kbs * kTcABytes) : st_addr + a.w_off;
+                    const uint32_t b_addr = st_addr + a.x_off;
                     for (int jj = 0; jj < a.kbs; ++jj)
 #pragma unroll
                         for (int k = 0; k < kTcBK / 16; ++k)
@@ -349,6 +393,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                    smem_desc_sw128(b_addr + jj * (uint32_t)np * kTcBK * 2 + k * 32), idesc,
                                    (kb > kb0 || jj > 0 || k > 0) ? 1u : 0u);
                     tc_commit(&empty[s]);
+                    if (kQ) tc_commit(&aempty[ab]);
                     issued = true;
                 }
                 tc_commit(&tfull[buf]);
@@ -361,7 +406,69 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 mbar_wait(drain, 0, a.err, kErrTimeoutFull);
             }
         }
-    } else {
+    } else if (kQ && warp >= 6) {
+        // ------------------------------------------------------------ dequantising warps
+        // thread -> (row, half of the stage's atoms): the exact value d*(q-8) (Q4_0) or
+        // d*q (Q8_0), rounded to bf16, into the 128-byte-swizzled operand atoms
+        const int ct = threadIdx.x - 192;
+        const int row = ct >> 1, half = ct & 1;
+        const int kbs = a.kbs, cb = a.cb;
+        walk([&](int, int, int it) {
+            const int s = it % S, ab = it % a.n_abuf;
+            if (misc[1] || !mbar_wait(&full[s], (it / S) & 1, a.err, kErrTimeoutFull)) {
+                misc[1] = 1;
+                return false;
+            }
+            if (misc[1] || !mbar_wait(&aempty[ab], ((it / a.n_abuf) & 1) ^ 1, a.err, kErrTimeoutEmpty)) {
+                misc[1] = 1;
+                return false;
+            }
+            const uint8_t* st = smem + (size_t)s * a.stage_bytes;
+            const uint8_t* codes = st + a.w_off + (size_t)row * kbs * cb;
+            const uint8_t* scl = st + a.s_off + (size_t)row * kbs * 4;
+            uint8_t* A = smem + L.abuf + (size_t)ab * kbs * kTcABytes;
+            for (int j = half * (kbs / 2); j < (half + 1) * (kbs / 2); ++j) {
+                const float d0 = __half2float(*reinterpret_cast<const __half*>(scl + j * 4));
+                const float d1 = __half2float(*reinterpret_cast<const __half*>(scl + j * 4 + 2));
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const float d = c < 4 ? d0 : d1;  // 8-element chunk c of 32-element block c / 4
+                    const float2 dd = make_float2(d, d);
+                    // code bytes placed under the exponent of 2^23 (float = 2^23 + byte), the
+                    // bias subtracted exactly, times d exactly, rounded once to bf16
+                    uint32_t lo, hi;
+                    float2 bias;
+                    if constexpr (WF == kWQ4) {
+                        const uint32_t q = *reinterpret_cast<const uint32_t*>(codes + j * 32 + c * 4);
+                        lo = q & 0x0F0F0F0Fu;  // elements 0, 2, 4, 6
+                        hi = (q >> 4) & 0x0F0F0F0Fu;  // elements 1, 3, 5, 7
+                        bias = make_float2(-8388616.0f, -8388616.0f);  // 2^23 + 8
+                    } else {
+                        const uint2 q = *reinterpret_cast<const uint2*>(codes + j * 64 + c * 8);
+                        const uint32_t u0 = q.x ^ 0x80808080u, u1 = q.y ^ 0x80808080u;  // int8 -> q + 128
+                        lo = __byte_perm(u0, u1, 0x6420);
+                        hi = __byte_perm(u0, u1, 0x7531);
+                        bias = make_float2(-8388736.0f, -8388736.0f);  // 2^23 + 128
+                    }
+                    uint32_t w[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 m = make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7440u | e)),
+                                                     __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440u | e)));
+                        const float2 v = ffma2(ffma2(m, make_float2(1.f, 1.f), bias), dd, make_float2(0.f, 0.f));
+                        w[e] = pack_bf2(v.x, v.y);
+                    }
+                    *reinterpret_cast<uint4*>(A + (size_t)j * kTcABytes + row * 128 + ((c ^ (row & 7)) << 4)) =
+                        make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
+            // generic-proxy writes -> the tensor cores' async-proxy reads
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&afull[ab]);
+            return true;
+        });
+    } else if (warp >= 2 && warp < 6) {
         // ------------------------------------------------------------ epilogue
         const int q = warp & 3;                 // TMEM lane quarter of this warp
         const int et = threadIdx.x - 64;        // 0..127 among the epilogue threads
@@ -673,13 +780,34 @@ bool make_tmap_bf16_sw128(CUtensorMap* m, const void* base, uint64_t rows, uint6
 
 namespace {
 
-const void* tc_func(int epi) {
-    switch (epi) {
-        case kEpiStore: return reinterpret_cast<const void*>(&k_tc_gemm<kEpiStore>);
-        case kEpiResid: return reinterpret_cast<const void*>(&k_tc_gemm<kEpiResid>);
-        case kEpiGlu: return reinterpret_cast<const void*>(&k_tc_gemm<kEpiGlu>);
-        default: return reinterpret_cast<const void*>(&k_tc_gemm<kEpiLmHead>);
+const void* tc_func(int epi, int wf) {
+    switch (wf * 4 + epi) {
+        case kEpiStore: return reinterpret_cast<const void*>(&k_tc_gemm<kEpiStore, kWBf16>);
+        case kEpiResid: return reinterpret_cast<const void*>(&k_tc_gemm<kEpiResid, kWBf16>);
+        case kEpiGlu: return reinterpret_cast<const void*>(&k_tc_gemm<kEpiGlu, kWBf16>);
+        case kEpiLmHead: return reinterpret_cast<const void*>(&k_tc_gemm<kEpiLmHead, kWBf16>);
+        case 4 * kWQ4 + kEpiStore: return reinterpret_cast<const void*>(&k_tc_gemm<kEpiStore, kWQ4>);
+        case 4 * kWQ4 + kEpiResid: return reinterpret_cast<const void*>(&k_tc_gemm<kEpiResid, kWQ4>);
+        case 4 * kWQ4 + kEpiGlu: return reinterpret_cast<const void*>(&k_tc_gemm<kEpiGlu, kWQ4>);
+        case 4 * kWQ8 + kEpiStore: return reinterpret_cast<const void*>(&k_tc_gemm<kEpiStore, kWQ8>);
+        case 4 * kWQ8 + kEpiResid: return reinterpret_cast<const void*>(&k_tc_gemm<kEpiResid, kWQ8>);
+        case 4 * kWQ8 + kEpiGlu: return reinterpret_cast<const void*>(&k_tc_gemm<kEpiGlu, kWQ8>);
+        default: return nullptr;
     }
+}
+
+// uint8 [rows, cols] with row pitch `pitch` bytes; box = box_cols x box_rows, no swizzle
+bool make_tmap_u8(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch, uint32_t box_cols,
+                  uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {pitch};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
@@ -701,8 +829,9 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
         if (why) *why = "tc_gemm: the RMSNorm prologue runs as its own pass (rms_rows_launch)";
         return false;
     }
-    if (g.wfmt != kWBf16) {
-        if (why) *why = "tc_gemm: bf16 weights only";
+    const bool q = g.wfmt != kWBf16;
+    if (q && (g.K % 256 != 0 || epi == kEpiLmHead)) {
+        if (why) *why = "tc_gemm: GGUF weights need K % 256 == 0 (and not the LM head)";
         return false;
     }
     if (g.lora.adapter && !g.lora.dval) {
@@ -718,8 +847,10 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
     const char* env = std::getenv("TI_TC_KBS");
     int kbs_max = env ? std::max(1, std::min(8, std::atoi(env))) : 4;
     const uint32_t xatom = (uint32_t)np * kTcBK * 2;
-    const TcSmem L0 = tc_smem_layout(0, 0, np);
-    while (kbs_max > 1 && 2 * ((size_t)kbs_max * (kTcABytes + xatom) + 16) > kTcSmemBudget - L0.total) kbs_max /= 2;
+    const TcSmem L0 = tc_smem_layout(0, 0, np, 0, 0);
+    if (q) kbs_max = 4;  // a 16-byte scales box = 4 atoms of 64 columns
+    while (!q && kbs_max > 1 && 2 * ((size_t)kbs_max * (kTcABytes + xatom) + 16) > kTcSmemBudget - L0.total)
+        kbs_max /= 2;
     const int kbs = kbs_max;
     (void)kbs;
     // stream-K: equal contiguous ranges of the tiles x k-blocks space, one per
@@ -727,7 +858,7 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
     // atoms, wins, with a small bonus for wider (DRAM-friendlier) stages
     int best_kbs = 0, best_kpc = 0;
     double best_cost = 0;
-    for (int kb = kbs_max; kb >= 1; kb /= 2) {
+    for (int kb = kbs_max; kb >= (q ? 4 : 1); kb /= 2) {
         if (atoms % kb != 0) continue;
         const long total = (long)tiles * (atoms / kb);
         const int kpc = (int)((total + sms - 1) / sms);
@@ -751,25 +882,63 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
         if (why) *why = "tc_gemm: split workspace too small for this batch";
         return false;
     }
-    p->stage_bytes = (uint32_t)best_kbs * (kTcABytes + xatom);
-    p->stages = (int)std::min<size_t>(12, (kTcSmemBudget - L0.total) / (p->stage_bytes + 16));
+    p->cb = g.wfmt == kWQ4 ? 32 : g.wfmt == kWQ8 ? 64 : 0;  // code bytes per 64-column atom row
+    if (!q) {
+        p->stage_bytes = (uint32_t)best_kbs * (kTcABytes + xatom);
+        p->w_off = 0;
+        p->x_off = (uint32_t)best_kbs * kTcABytes;
+        p->s_off = 0;
+        p->n_abuf = 0;
+    } else {
+        // [token atoms (1024-aligned for the swizzle)][codes][scales]
+        p->x_off = 0;
+        p->w_off = (uint32_t)best_kbs * xatom;
+        p->s_off = p->w_off + (uint32_t)kTcBM * best_kbs * p->cb;
+        const uint32_t raw = p->s_off + (uint32_t)kTcBM * best_kbs * 4;
+        p->stage_bytes = (raw + 1023u) & ~1023u;
+        // two dequantised operand buffers when two raw stages still fit, else one
+        p->n_abuf = 2;
+        const size_t abuf = (size_t)best_kbs * kTcABytes;
+        const TcSmem Lq = tc_smem_layout(0, 0, np, 0, 0);
+        if (2 * abuf + 2 * ((size_t)p->stage_bytes + 16) > kTcSmemBudget - Lq.total) p->n_abuf = 1;
+    }
+    const size_t abuf_bytes = (size_t)p->n_abuf * best_kbs * kTcABytes;
+    p->stages = (int)std::min<size_t>(12, (kTcSmemBudget - L0.total - abuf_bytes) / (p->stage_bytes + 16));
     if (p->stages < 2) {
         if (why) *why = "tc_gemm: token tile too large for a two-stage ring";
         return false;
     }
-    p->smem = tc_smem_layout(p->stages, p->stage_bytes, np).total;
+    p->smem = tc_smem_layout(p->stages, p->stage_bytes, np, p->n_abuf, best_kbs).total;
     uint32_t cols = 32;
     while (cols < (uint32_t)(2 * np)) cols <<= 1;
     p->tmem_cols = cols;
-    p->func = tc_func(epi);
+    p->func = tc_func(epi, g.wfmt);
+    p->threads = q ? kTcThreadsQ : kTcThreads;
+    if (!p->func) {
+        if (why) *why = "tc_gemm: no kernel instance";
+        return false;
+    }
     return true;
 }
 
 cudaError_t tc_launch(const GemvArgs& g, int epi, const TcPlan& p, float* ws, unsigned int* tile_ctr, cudaStream_t s,
                       bool pdl) {
-    CUtensorMap mw, mx;
+    CUtensorMap mw, mx, ms;
     const uint64_t wrows = epi == kEpiGlu ? 2ull * g.N : (uint64_t)g.N;
-    if (!make_tmap_bf16_sw128(&mw, g.W, wrows, g.K, g.K, epi == kEpiGlu ? 64 : kTcBM)) return cudaErrorInvalidValue;
+    const uint32_t box_rows = epi == kEpiGlu ? 64 : kTcBM;
+    if (g.wfmt == kWBf16) {
+        if (!make_tmap_bf16_sw128(&mw, g.W, wrows, g.K, g.K, box_rows)) return cudaErrorInvalidValue;
+        ms = mw;
+    } else {
+        // rows of [codes][scales] (wrow_bytes apart): two uint8 maps over the same rows
+        const uint64_t pitch = wrow_bytes(g.K, g.wfmt);
+        const uint64_t code_bytes = (uint64_t)g.K * p.cb / 64;
+        const uint8_t* base = reinterpret_cast<const uint8_t*>(g.W);
+        if (!make_tmap_u8(&mw, base, wrows, code_bytes, pitch, (uint32_t)p.kbs * p.cb, box_rows))
+            return cudaErrorInvalidValue;
+        if (!make_tmap_u8(&ms, base + code_bytes, wrows, (uint64_t)g.K / 16, pitch, (uint32_t)p.kbs * 4, box_rows))
+            return cudaErrorInvalidValue;
+    }
     if (!make_tmap_bf16_sw128(&mx, g.x, g.nb, g.K, g.x_stride, p.np)) return cudaErrorInvalidValue;
     if (!ws || !tile_ctr) return cudaErrorInvalidValue;
     TcKernelArgs a{};
@@ -783,6 +952,11 @@ cudaError_t tc_launch(const GemvArgs& g, int epi, const TcPlan& p, float* ws, un
     a.kpc = p.kpc;
     a.stages = p.stages;
     a.stage_bytes = p.stage_bytes;
+    a.w_off = p.w_off;
+    a.x_off = p.x_off;
+    a.s_off = p.s_off;
+    a.cb = p.cb;
+    a.n_abuf = p.n_abuf;
     a.tmem_cols = p.tmem_cols;
     a.out = g.out;
     a.out_stride = g.out_stride;
@@ -805,17 +979,18 @@ cudaError_t tc_launch(const GemvArgs& g, int epi, const TcPlan& p, float* ws, un
     a.lora = g.lora;
     a.err = g.err;
     static std::mutex mu;
-    static bool attr_set[4] = {false, false, false, false};
+    static bool attr_set[12] = {};
     {
         std::lock_guard<std::mutex> lk(mu);
-        if (!attr_set[epi & 3]) {
+        const int idx = (g.wfmt * 4 + epi) % 12;
+        if (!attr_set[idx]) {
             cudaError_t e = cudaFuncSetAttribute(p.func, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
             if (e != cudaSuccess) return e;
-            attr_set[epi & 3] = true;
+            attr_set[idx] = true;
         }
     }
-    void* params[] = {&mw, &mx, &a};
-    return launch_pdl(p.func, dim3(p.grid), dim3(kTcThreads), p.smem, s, params, pdl);
+    void* params[] = {&mw, &mx, &ms, &a};
+    return launch_pdl(p.func, dim3(p.grid), dim3(p.threads), p.smem, s, params, pdl);
 }
 
 }  // namespace ti

@@ -3,7 +3,8 @@
 The device quantiser must produce the oracle's GGUF blocks bit for bit (the
 oracle restates ggml's quantize_row_q4_0_ref / q8_0_ref); GGUF blocks loaded
 directly must round-trip; decode through the dequantising weight-streaming
-GEMV must match the oracle's dequantise-then-fp32-dot path within 5e-2
+GEMV (and, for batches of 8+ tokens, the tcgen05 GEMM with in-kernel
+dequantisation) must match the oracle's dequantise-then-fp32-dot path within 5e-2
 max-abs relative for Q4_0 (the tolerance the spec states for Q4_0) and 2e-2
 for Q8_0, with greedy ids equal up to recorded near-ties."""
 import ctypes as C
@@ -124,3 +125,11 @@ def test_q4_qwen7b_shapes_bias():
     # Qwen2.5-7B projection shapes (hidden 3584, intermediate 18944: the packed-activation path), 2 layers
     kw = dict(ti.PRESETS["qwen25_7b"], n_layers=2, weight_format=ti.WFMT_Q4_0)
     _parity(kw, [5], steps=2)
+
+
+@pytest.mark.parametrize("wf", [ti.WFMT_Q4_0, ti.WFMT_Q8_0])
+def test_quantised_tensor_core_batch_qwen7b_shapes(wf):
+    # 12 tokens: every projection on the tcgen05 GEMM with in-kernel dequantisation
+    # (the dequantised weight is rounded to bf16 for the bf16 x bf16 MMA: <= 2^-9 relative)
+    kw = dict(ti.PRESETS["qwen25_7b"], n_layers=2, weight_format=wf)
+    _parity(kw, [2 + b % 3 for b in range(12)], steps=2)
