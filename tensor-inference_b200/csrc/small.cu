@@ -147,9 +147,8 @@ struct RecvLora {
 
 __global__ void k_tp_recv_resid(const float* __restrict__ inbox, size_t src_stride, const unsigned int* flags, int tp,
                                 const int* epoch, int seq_mul, int seq_add, const uint16_t* __restrict__ resid,
-                                uint16_t* __restrict__ out, int n, int H, const RecvLora rl, int* err) {
+                                uint16_t* __restrict__ out, int n, int* err) {
     __shared__ int ok;
-    extern __shared__ float tfull[];  // [nb][R] rank-ordered sums of x.A^T, rounded to bf16
     if (blockIdx.x == 0 && threadIdx.x == 0) pdl_trigger();
     pdl_wait();
     if (threadIdx.x == 0) {
@@ -160,33 +159,86 @@ __global__ void k_tp_recv_resid(const float* __restrict__ inbox, size_t src_stri
     }
     __syncthreads();
     if (!ok) return;
-    const bool lora = rl.L.adapter != nullptr;
-    const int R = rl.L.rank, nb = n / H;
-    if (lora) {
-        for (int j = threadIdx.x; j < nb * R; j += blockDim.x) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        float sum = 0.f;
+        for (int r = 0; r < tp; ++r) sum += __ldcv(inbox + (size_t)r * src_stride + i);  // rank order
+        const float rr = __uint_as_float((uint32_t)resid[i] << 16);
+        out[i] = __bfloat16_as_ushort(f2bf(rr + round_bf(sum)));
+    }
+}
+
+// With LoRA on the row-parallel projection the expansion runs here, on the full
+// x.A^T (the rank-ordered sum of every rank's partial): CTA (row tile, token b),
+// eight lanes per output row, each reading 16 contiguous bytes of the B row, so a
+// warp reads four whole B rows per load (coalesced) and the eight partial sums
+// meet in a 3-step shuffle.
+constexpr int kRecvLoraRows = 128;
+
+__global__ void __launch_bounds__(256)
+    k_tp_recv_resid_lora(const float* __restrict__ inbox, size_t src_stride, const unsigned int* flags, int tp,
+                         const int* epoch, int seq_mul, int seq_add, const uint16_t* __restrict__ resid,
+                         uint16_t* __restrict__ out, int H, const RecvLora rl, int* err) {
+    __shared__ int ok;
+    __shared__ __align__(16) float tfull[256];  // this token's x.A^T rounded to bf16 (rank <= 256)
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) pdl_trigger();
+    const int b = blockIdx.y, tid = threadIdx.x;
+    pdl_wait();
+    if (tid == 0) {
+        const unsigned int seq = peer_seq(*epoch, seq_mul, seq_add);
+        bool good = true;
+        for (int r = 0; r < tp && good; ++r) good = wait_seq_sys(flags + r, seq, err, kErrTimeoutPeer);
+        ok = good;
+    }
+    const int R = rl.L.rank;
+    const int ad = rl.L.adapter[b];
+    const bool has = ad >= 0 && ad < rl.L.n_adapters;
+    __syncthreads();
+    if (!ok) return;
+    if (has) {
+        for (int j = tid; j < R; j += blockDim.x) {
             float t = 0.f;
-            for (int r = 0; r < tp; ++r) t += __ldcv(rl.t_inbox + (size_t)r * rl.t_src_stride + j);
+            for (int r = 0; r < tp; ++r) t += __ldcv(rl.t_inbox + (size_t)r * rl.t_src_stride + (size_t)b * R + j);
             tfull[j] = round_bf(t);  // the shrink output x.A^T (qwen_adapter_model.cpp:27)
         }
         __syncthreads();
     }
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        float sum = 0.f;
-        for (int r = 0; r < tp; ++r) sum += __ldcv(inbox + (size_t)r * src_stride + i);  // rank order
-        float v = round_bf(sum);
-        if (lora) {
-            const int b = i / H, row = i - b * H;
-            const int ad = rl.L.adapter[b];
-            if (ad >= 0 && ad < rl.L.n_adapters) {
-                const uint16_t* br = rl.L.B + (size_t)ad * rl.L.B_adapter_stride + (size_t)row * R;
-                const float* t = tfull + (size_t)b * R;
-                float s = 0.f;
-                for (int k = 0; k < R; ++k) s = fmaf(__uint_as_float((uint32_t)br[k] << 16), t[k], s);
-                v = round_bf(v + round_bf(round_bf(s) * rl.L.scale[ad]));  // qwen_adapter_model.cpp:28-29, :42
+    const int sub = tid & 7;
+    const float scale = has ? rl.L.scale[ad] : 0.f;
+    const uint16_t* B = has ? rl.L.B + (size_t)ad * rl.L.B_adapter_stride : nullptr;
+    const int r_end = min(H, (int)(blockIdx.x + 1) * kRecvLoraRows);
+    for (int r0 = blockIdx.x * kRecvLoraRows; r0 < r_end; r0 += 32) {  // uniform trip count: whole warps shuffle
+        const int row = r0 + (tid >> 3);
+        const bool live = row < r_end;
+        float s = 0.f;
+        if (has && live) {
+            const uint16_t* br = B + (size_t)row * R;
+            for (int k0 = sub * 8; k0 < R; k0 += 64) {
+                const uint4 w = *reinterpret_cast<const uint4*>(br + k0);
+                const uint32_t* wp = reinterpret_cast<const uint32_t*>(&w);
+                const float4 t0 = *reinterpret_cast<const float4*>(tfull + k0);
+                const float4 t1 = *reinterpret_cast<const float4*>(tfull + k0 + 4);
+                s = fmaf(bf_lo(wp[0]), t0.x, s);
+                s = fmaf(bf_hi(wp[0]), t0.y, s);
+                s = fmaf(bf_lo(wp[1]), t0.z, s);
+                s = fmaf(bf_hi(wp[1]), t0.w, s);
+                s = fmaf(bf_lo(wp[2]), t1.x, s);
+                s = fmaf(bf_hi(wp[2]), t1.y, s);
+                s = fmaf(bf_lo(wp[3]), t1.z, s);
+                s = fmaf(bf_hi(wp[3]), t1.w, s);
             }
         }
-        const float rr = __uint_as_float((uint32_t)resid[i] << 16);
-        out[i] = __bfloat16_as_ushort(f2bf(rr + v));
+        s += __shfl_xor_sync(0xffffffffu, s, 4);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        if (sub == 0 && live) {
+            const size_t i = (size_t)b * H + row;
+            float sum = 0.f;
+            for (int r = 0; r < tp; ++r) sum += __ldcv(inbox + (size_t)r * src_stride + i);  // rank order
+            float v = round_bf(sum);
+            if (has) v = round_bf(v + round_bf(round_bf(s) * scale));  // qwen_adapter_model.cpp:28-29, :42
+            const float rr = __uint_as_float((uint32_t)resid[i] << 16);
+            out[i] = __bfloat16_as_ushort(f2bf(rr + v));
+        }
     }
 }
 
@@ -194,23 +246,20 @@ cudaError_t tp_recv_resid_launch(const float* inbox, size_t src_stride, const un
                                  const int* epoch, int seq_mul, int seq_add, const uint16_t* resid, uint16_t* out,
                                  int nb, int H, const GemvLora* lora, const float* t_inbox, size_t t_src_stride,
                                  int* err, cudaStream_t s, bool pdl) {
-    int n = nb * H;
-    RecvLora rl;
-    size_t smem = 0;
     if (lora && lora->adapter) {
+        if (lora->rank % 8 != 0 || lora->rank > 256) return cudaErrorInvalidValue;
+        RecvLora rl;
         rl.L = *lora;
         rl.t_inbox = t_inbox;
         rl.t_src_stride = t_src_stride;
-        smem = (size_t)nb * lora->rank * 4;
-        if (smem > 48 * 1024) {
-            cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&k_tp_recv_resid),
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e != cudaSuccess) return e;
-        }
+        void* params[] = {&inbox, &src_stride, &flags, &tp, &epoch, &seq_mul, &seq_add, &resid, &out, &H, &rl, &err};
+        return launch_pdl(reinterpret_cast<const void*>(&k_tp_recv_resid_lora),
+                          dim3((H + kRecvLoraRows - 1) / kRecvLoraRows, nb), dim3(256), 0, s, params, pdl);
     }
-    void* params[] = {&inbox, &src_stride, &flags, &tp, &epoch, &seq_mul, &seq_add, &resid, &out, &n, &H, &rl, &err};
+    int n = nb * H;
+    void* params[] = {&inbox, &src_stride, &flags, &tp, &epoch, &seq_mul, &seq_add, &resid, &out, &n, &err};
     const int grid = std::min((n + 255) / 256, 148);
-    return launch_pdl(reinterpret_cast<const void*>(&k_tp_recv_resid), dim3(grid), dim3(256), smem, s, params, pdl);
+    return launch_pdl(reinterpret_cast<const void*>(&k_tp_recv_resid), dim3(grid), dim3(256), 0, s, params, pdl);
 }
 
 struct KeysArgs {
