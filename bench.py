@@ -365,7 +365,8 @@ def measure_pkm(ti, torch, stream, iters=20):
 def run_profile(args):
     """Short, self-contained workload for ncu: a few decode steps (or repeated
     launches of one kernel) of the 8B shape with `--layers` layers after a
-    `--prompt`-token prefill.  Prints timing only; never a bench number."""
+    `--prompt`-token prefill (`--preset` picks another model shape).  Prints
+    timing only; never a bench number."""
     import numpy as np
     import torch
 
@@ -374,7 +375,7 @@ def run_profile(args):
     torch.cuda.set_device(0)
     ts = torch.cuda.Stream()
     torch.cuda.set_stream(ts)
-    desc = ti.model_desc(**dict(ti.PRESETS["llama3_8b"], n_layers=args.layers))
+    desc = ti.model_desc(**dict(ti.PRESETS[args.preset], n_layers=args.layers))
     ctx = args.ctx or args.prompt
     eng = ti.Engine(desc, device=0, max_batch=args.batch, max_seqs=args.batch,
                     max_seq_len=ctx + args.warmup + args.steps + 64)
@@ -544,6 +545,7 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--kernel", type=int, default=None, help="profile: launch only this kernel kind")
     ap.add_argument("--ctx", type=int, default=0, help="profile: synthetic cached context of this length")
+    ap.add_argument("--preset", default="llama3_8b", help="profile: model shape (ti_b200.PRESETS)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank = int(os.environ.get("RANK", "0"))

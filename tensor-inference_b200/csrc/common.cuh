@@ -190,6 +190,13 @@ TI_DEVICE_INLINE float2 ffma2(float2 a, float2 b, float2 c) {
     asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(cv) : "l"(av), "l"(bv));
     return *reinterpret_cast<float2*>(&cv);
 }
+TI_DEVICE_INLINE float2 fmul2(float2 a, float2 b) {
+    unsigned long long av = *reinterpret_cast<unsigned long long*>(&a);
+    unsigned long long bv = *reinterpret_cast<unsigned long long*>(&b);
+    unsigned long long dv;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(dv) : "l"(av), "l"(bv));
+    return *reinterpret_cast<float2*>(&dv);
+}
 TI_DEVICE_INLINE float2 bf2_to_f2(uint32_t u) { return make_float2(bf_lo(u), bf_hi(u)); }
 // 8 bf16 weights x 8 fp32 activations (pairs); even and odd elements accumulate
 // in the two lanes of `acc`, each in element order

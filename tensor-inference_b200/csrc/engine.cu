@@ -501,12 +501,12 @@ ti_status build(ti_engine* e) {
         e->adapters.assign(e->S, ti_engine::AdapterMeta{});
         TI_CUDA(cudaStreamCreateWithFlags(&e->side, cudaStreamNonBlocking));
     }
-    e->attn_splits_n = attn_splits(B, nkv, e->o.max_seq_len, e->sms, &e->attn_max_chunk);
+    e->attn_splits_n = attn_splits(B, nkv, hd, e->o.max_seq_len, e->sms, &e->attn_max_chunk);
     // partials sized for the largest batch; smaller batches use more splits per (token, head)
     int max_parts = 0;
     for (int b = 1; b <= B; ++b) {
         int mc = 0;
-        int n = attn_splits(b, nkv, e->o.max_seq_len, e->sms, &mc);
+        int n = attn_splits(b, nkv, hd, e->o.max_seq_len, e->sms, &mc);
         max_parts = std::max(max_parts, b * n);
     }
     const int G = nq / nkv;
@@ -789,7 +789,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         }
         case kKAttn: {
             int mc = 0;
-            const int splits = attn_splits(B, nkv, e->o.max_seq_len, e->sms, &mc);
+            const int splits = attn_splits(B, nkv, hd, e->o.max_seq_len, e->sms, &mc);
             AttnArgs at;
             at.qkv = e->qkv;
             at.qkv_stride = e->qkv_rows;

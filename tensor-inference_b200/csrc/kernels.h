@@ -213,7 +213,7 @@ struct AttnArgs {
     int out_stride = 0;
     int* err = nullptr;
 };
-int attn_splits(int nb, int nkv, int max_len, int sms, int* max_chunk);
+int attn_splits(int nb, int nkv, int hd, int max_len, int sms, int* max_chunk);
 // scratch floats / counters one launch needs: part_o + part_ml, and nb*nkv counters
 size_t attn_scratch_floats(int nb, int nq, int nkv, int hd, int n_splits);
 cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s, bool pdl);

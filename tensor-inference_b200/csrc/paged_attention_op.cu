@@ -52,7 +52,7 @@ AttnArgs make_args(const void* qkv, int batch, int n_heads, int n_kv, int head_d
     a.window = nullptr;
     a.window_const = sliding_window;
     a.n_pages = n_pages;
-    a.n_splits = attn_splits(batch, n_kv, max_len, sms, &a.max_chunk);
+    a.n_splits = attn_splits(batch, n_kv, head_dim, max_len, sms, &a.max_chunk);
     a.out = reinterpret_cast<uint16_t*>(out);
     a.out_stride = n_heads * head_dim;
     return a;

@@ -147,9 +147,9 @@ def test_cast_and_transpose():
     np.testing.assert_array_equal(dt.to_array((65, 33), np.float32), x.T)
 
 
-def paged_case(seed=12, B=3, nq=8, nkv=2, hd=128, pos=(0, 17, 40), max_len=64, theta=10000.0):
+def paged_case(seed=12, B=3, nq=8, nkv=2, hd=128, pos=(0, 17, 40), max_len=64, theta=10000.0, window=-1):
     """random paged K/V state (shuffled page ids) plus the oracle's expected output
-    for one decode-attention call"""
+    for one decode-attention call (with `window` > 0: over the last `window` tokens)"""
     rng = np.random.default_rng(seed)
     pt_stride = (max_len + 15) // 16
     n_pages = B * pt_stride + 3
@@ -175,16 +175,17 @@ def paged_case(seed=12, B=3, nq=8, nkv=2, hd=128, pos=(0, 17, 40), max_len=64, t
         qr, kr = np.empty_like(q), np.empty_like(k)
         oracle.lib().orc_rope(oracle.ptr(q), oracle.ptr(qr), 1, nq, hd, pos[b], oracle.ptr(fr))
         oracle.lib().orc_rope(oracle.ptr(k), oracle.ptr(kr), 1, nkv, hd, pos[b], oracle.ptr(fr))
-        K = np.ascontiguousarray(np.concatenate([cached[b][0], kr]))
-        V = np.ascontiguousarray(np.concatenate([cached[b][1], v]))
+        lo = max(0, pos[b] - window + 1) if window > 0 else 0
+        K = np.ascontiguousarray(np.concatenate([cached[b][0], kr])[lo:])
+        V = np.ascontiguousarray(np.concatenate([cached[b][1], v])[lo:])
         o = np.empty((1, nq, hd), np.uint16)
-        oracle.lib().orc_attention(oracle.ptr(qr), oracle.ptr(K), oracle.ptr(V), oracle.ptr(o), 1, nq, pos[b] + 1,
+        oracle.lib().orc_attention(oracle.ptr(qr), oracle.ptr(K), oracle.ptr(V), oracle.ptr(o), 1, nq, pos[b] + 1 - lo,
                                    nkv, hd, 0, -1)
         ref.append(o.reshape(-1))
         knew.append(kr.reshape(nkv, hd))
     return dict(qkv=qkv, table=table, kpool=kpool, vpool=vpool, pos=np.array(pos, np.int32),
                 seq=np.arange(B, dtype=np.int32), ref=np.stack(ref), knew=knew, B=B, nq=nq, nkv=nkv, hd=hd,
-                pt_stride=pt_stride, n_pages=n_pages, max_len=max_len, theta=theta)
+                pt_stride=pt_stride, n_pages=n_pages, max_len=max_len, theta=theta, window=window)
 
 
 def run_paged(c, fn="ti_op_paged_attention"):
@@ -192,12 +193,42 @@ def run_paged(c, fn="ti_op_paged_attention"):
     out = DevBuf(c["B"] * c["nq"] * c["hd"] * 2)
     ti.check(getattr(lib(), fn)(bufs["qkv"].ptr, c["B"], c["nq"], c["nkv"], c["hd"], bufs["pos"].ptr,
                                 bufs["seq"].ptr, bufs["table"].ptr, c["pt_stride"], bufs["kpool"].ptr,
-                                bufs["vpool"].ptr, c["n_pages"], c["max_len"], c["theta"], None, -1, out.ptr, None))
+                                bufs["vpool"].ptr, c["n_pages"], c["max_len"], c["theta"], None, c["window"], out.ptr,
+                                None))
     return (out.to_array((c["B"], c["nq"] * c["hd"]), np.uint16),
             bufs["kpool"].to_array(c["kpool"].shape, np.uint16), bufs["vpool"].to_array(c["vpool"].shape, np.uint16))
 
 
-@pytest.mark.parametrize("hd,nq,nkv", [(128, 8, 2), (64, 4, 4), (128, 28, 4)])
+def check_paged(c, out, kp, vp):
+    nq, nkv, hd = c["nq"], c["nkv"], c["hd"]
+    assert rel_err(f32(out), f32(c["ref"])) < 1e-2
+    for b in range(c["B"]):
+        p = int(c["pos"][b])
+        page = c["table"][b, p // 16]
+        assert rel_err(f32(kp[page, :, p % 16]), f32(c["knew"][b])) < 1e-2
+        np.testing.assert_array_equal(vp[page, :, p % 16],
+                                      c["qkv"][b, (nq + nkv) * hd:].reshape(nkv, hd))
+
+
+@pytest.mark.parametrize("hd,nq,nkv,spp", [(128, 16, 2, None), (128, 16, 2, 3), (64, 8, 2, 2), (256, 8, 1, 4),
+                                           (128, 4, 4, 16)])
+def test_paged_attention_long(hd, nq, nkv, spp, monkeypatch):
+    """long contexts: many ring stages per split (TI_ATTN_SPP), several splits merged"""
+    if spp:
+        monkeypatch.setenv("TI_ATTN_SPP", str(spp))
+    c = paged_case(seed=5, B=2, nq=nq, nkv=nkv, hd=hd, pos=(1500, 777), max_len=2048)
+    check_paged(c, *run_paged(c))
+
+
+@pytest.mark.parametrize("window", [100, 16, 1])
+def test_paged_attention_window(window, monkeypatch):
+    monkeypatch.setenv("TI_ATTN_SPP", "2")
+    c = paged_case(seed=7, B=3, nq=8, nkv=2, hd=128, pos=(300, 50, 129), max_len=512, window=window)
+    check_paged(c, *run_paged(c))
+
+
+@pytest.mark.parametrize("hd,nq,nkv", [(128, 8, 2), (64, 4, 4), (128, 28, 4), (256, 8, 1), (128, 16, 1), (64, 8, 1),
+                                       (256, 2, 1)])
 def test_paged_attention_op(hd, nq, nkv):
     c = paged_case(hd=hd, nq=nq, nkv=nkv)
     out, kp, vp = run_paged(c)
