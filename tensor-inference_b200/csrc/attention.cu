@@ -23,18 +23,20 @@
 // kernel.  The swizzle makes both the ldmatrix reads of K and the row reads of
 // V free of shared-memory bank conflicts.
 //
-// Work split: warp w owns 16-token blocks of every stage.  Scores S = q K^T come
+// Work split: eight warps; warp w owns one 16-token block of every stage and one
+// 64-dim box of its P.V (head_dim 128: two warps per block, 256: four).  Scores S = q K^T come
 // out of mma.sync m16n8k16 (the group's q heads padded to 16 rows) in exactly
 // the register layout of the A operand of the next mma, so P never leaves the
 // registers: each warp keeps its own running max and sum per q head (quad
 // shuffles), P.V accumulates on the tensor cores with V fragments read by
-// ldmatrix.trans from the swizzled tile, and the four warps are merged once at
+// ldmatrix.trans from the swizzled tile, and the warps are merged once at
 // the end.  A stage is released through an "empty" mbarrier (one arrival per
 // warp), not a block barrier.
 //
 // Arithmetic follows the reference: RoPE in fp32 rounded to bf16; scores
 // q.k with bf16 operands and fp32 accumulation (bf16 x bf16 products are exact
-// in fp32), times 1/sqrt(head_dim); exp-normalised fp32 softmax; bf16 output.
+// in fp32), times 1/sqrt(head_dim); exp-normalised fp32 softmax, evaluated as
+// 2^(s log2(e) - m) with ex2.approx (relative error about 2^-22); bf16 output.
 // The reference's P.V is fp32 x bf16-valued V: here each fp32 probability is
 // split into two bf16 terms p = hi + lo (hi = bf16(p), lo = bf16(p - hi)), each
 // multiplied exactly by V in the fp32 accumulator; what the split drops is at
@@ -48,30 +50,32 @@
 
 namespace ti {
 
-constexpr int kAttnThreads = 128;
+constexpr int kAttnThreads = 256;
 constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kAttnMaxGroup = 16;              // q heads per kv head: the 16 rows of the mma
 constexpr int kPage = 16;
-constexpr int kAttnStages = 3;                 // ring depth
-constexpr uint32_t kAttnStageBytes = 32768;    // K + V of one stage
+constexpr int kAttnStages = 6;                 // ring depth
+constexpr uint32_t kAttnStageBytes = 16384;    // K + V of one stage
 constexpr int kAttnMaxSplits = 512;            // the merge weights fit over the ring
+constexpr int kAttnMaxSplitPages = 1024;       // page ids of a split staged in shared memory
+constexpr float kLog2e = 1.4426950408889634f;  // softmax in base 2: e^x = 2^(x log2 e)
 
-// tokens per stage: 128 / 64 / 32 for head_dim 64 / 128 / 256
+// tokens per stage: 64 / 32 / 16 for head_dim 64 / 128 / 256 (4 / 2 / 1 pages)
 __host__ __device__ constexpr int attn_ct(int HD) { return (int)(kAttnStageBytes / (4u * HD)); }
 
 struct AttnSmem {
-    uint32_t ring, qf, kn, vn, wml, hml, bar, total;
+    uint32_t ring, qs, kn, vn, wml, hml, pgs, cnt, bar, total;
 };
 
 // offsets from a 1024-byte aligned base
-__host__ __device__ inline AttnSmem attn_layout(int G, int HD) {
+__host__ __device__ inline AttnSmem attn_layout(int HD) {
     AttnSmem L;
     uint32_t o = 0;
     L.ring = o;  // [stages] x {K tile [HD/64][CT][64] bf16, V tile}, rows 128-byte swizzled;
     o += kAttnStages * kAttnStageBytes;  // afterwards the warp merge and the split merge weights
-    L.qf = o;    // q heads after RoPE (bf16 values as fp32) [G][HD]
-    o += (uint32_t)G * HD * 4;
-    L.kn = o;    // new token's k after RoPE, and v
+    L.qs = o;    // q heads after RoPE, bf16 [HD/64][16][64] swizzled (rows >= G zero)
+    o += 16u * HD * 2;
+    L.kn = o;    // new token's k after RoPE, and v (fp32)
     o += HD * 4;
     L.vn = o;
     o += HD * 4;
@@ -79,8 +83,13 @@ __host__ __device__ inline AttnSmem attn_layout(int G, int HD) {
     o += kAttnWarps * kAttnMaxGroup * 2 * 4;
     L.hml = o;   // merged (max, sum) per q head [16][2]
     o += kAttnMaxGroup * 2 * 4;
-    L.bar = o;   // full[stages], empty[stages]
-    o += 2 * kAttnStages * 8;
+    L.pgs = o;   // page ids of the split
+    o += kAttnMaxSplitPages * 4;
+    L.cnt = o;   // per slot: warp arrivals so far (WPS per stage)
+    o += kAttnStages * 4;
+    o = (o + 7u) & ~7u;
+    L.bar = o;   // full[stages]
+    o += kAttnStages * 8;
     L.total = o + 1024;
     return L;
 }
@@ -103,10 +112,27 @@ TI_DEVICE_INLINE void mma_16816_bf16(float* c, const uint32_t* a, uint32_t b0, u
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+TI_DEVICE_INLINE float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 // byte offset of element (row, d) in a [HD/64][C][64] bf16 tile with 128-byte swizzled rows
 TI_DEVICE_INLINE uint32_t tile_off(int C, int row, int d) {
     const int hh = d >> 6, cc = (d & 63) >> 3;
     return (uint32_t)(hh * C + row) * 128u + (uint32_t)((cc ^ (row & 7)) << 4) + (uint32_t)((d & 7) << 1);
+}
+// wait (bounded) until a shared counter reaches `need`
+TI_DEVICE_INLINE bool wait_count(const unsigned int* p, unsigned int need, int* err, int err_bit) {
+    const volatile unsigned int* v = p;
+    if (*v >= need) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        if (*v >= need) return true;
+        if ((i & 255u) == 255u && global_ns() - t0 > kWaitNs) break;
+    }
+    if (err) atomicOr(err, err_bit);
+    return false;
 }
 // two fp32 probabilities -> bf16 pair hi and the bf16 pair of what hi left out
 TI_DEVICE_INLINE void split_bf2(float p0, float p1, uint32_t& hi, uint32_t& lo) {
@@ -114,38 +140,41 @@ TI_DEVICE_INLINE void split_bf2(float p0, float p1, uint32_t& hi, uint32_t& lo) 
     lo = pack_bf2(p0 - bf_lo(hi), p1 - bf_hi(hi));
 }
 
-template <int HD>
+// G16: the group has more than 8 q heads (rows 8..15 of the mma are real heads)
+template <int HD, bool G16>
 __global__ void __launch_bounds__(kAttnThreads, 2)
     k_attn_decode(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, const AttnArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     constexpr int HALF = HD / 2;
-    constexpr int NH = HD / 64;  // 64-dim boxes per row
-    constexpr int KS = HD / 16;  // mma k-steps of the scores
-    constexpr int CT = attn_ct(HD);
-    constexpr int CP = CT / kPage;                 // pages per stage
+    constexpr int NH = HD / 64;                    // 64-dim boxes per row
+    constexpr int KS = HD / 16;                    // mma k-steps of the scores
+    constexpr int CT = attn_ct(HD);                // tokens per stage
+    constexpr int CP = CT / kPage;                 // pages (= 16-token blocks) per stage
     constexpr int NS = kAttnStages;
-    constexpr int NTB = CT / 16;                   // 16-token blocks per stage
-    constexpr int DPARTS = NTB >= kAttnWarps ? 1 : kAttnWarps / NTB;  // warps sharing a block split the dims
-    constexpr int WPD = kAttnWarps / DPARTS;       // warps per dim part
-    constexpr int TBW = NTB / WPD;                 // blocks per warp per stage
-    constexpr int DW = HD / DPARTS;                // dims of a warp's P.V
+    constexpr int DW = HD < 128 ? HD : 128;        // dims of a warp's P.V
+    constexpr int DPARTS = HD / DW;                // warps sharing a block split its dims
     constexpr int NT = DW / 8;                     // P.V n-tiles
+    constexpr int WPS = CP * DPARTS;               // warps per stage
+    constexpr int SG = kAttnWarps / WPS;           // stages in progress at once
+    static_assert(SG * WPS == kAttnWarps, "warps cover whole stages");
     constexpr uint32_t VOFF = kAttnStageBytes / 2;  // V tile after the K tile of a stage
     const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int gq = lane >> 2, qq = lane & 3;      // mma fragment row / column pair
-    const int dp = warp / WPD, wi = warp % WPD;
+    const int so = warp / WPS, wi = warp % WPS;   // stage group, place in the stage
+    const int blk = wi % CP, dp = wi / CP;        // block of the stage, dim part
     const int G = a.nq / a.nkv;
-    const AttnSmem L = attn_layout(G, HD);
+    const AttnSmem L = attn_layout(HD);
     uint8_t* ring = smem + L.ring;
-    float* qf = reinterpret_cast<float*>(smem + L.qf);
+    uint8_t* qs = smem + L.qs;
     float* kn = reinterpret_cast<float*>(smem + L.kn);
     float* vn = reinterpret_cast<float*>(smem + L.vn);
     float* wml = reinterpret_cast<float*>(smem + L.wml);
     float* hml = reinterpret_cast<float*>(smem + L.hml);
+    int* pgs = reinterpret_cast<int*>(smem + L.pgs);
+    unsigned int* cnt = reinterpret_cast<unsigned int*>(smem + L.cnt);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar);
-    uint64_t* empty = full + NS;
     __shared__ int s_last;
 
     // ---- this CTA's pages [pg0, pg1) of the attended range [lo, pos]
@@ -162,19 +191,20 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     const int t0 = pg0 * kPage;                                     // token of split row 0
     const int vlo = max(lo, t0) - t0, vhi = min(L1, t0 + npg * kPage) - t0;  // valid rows [vlo, vhi)
 
-    // stage st -> ring slot st % NS: its pages' K and V boxes on one barrier
-    auto issue = [&](int st) {
+    // stage st -> ring slot st % NS: its pages' K and V boxes on one barrier;
+    // ids[i] is the page id of split page i (the page table, or its copy in pgs)
+    auto issue = [&](int st, const int* ids) {
         uint8_t* kt = ring + (uint32_t)(st % NS) * kAttnStageBytes;
-        const int p0 = pg0 + st * CP, pn = min(CP, pg1 - p0);
+        const int i0 = st * CP, pn = min(CP, npg - i0);
         int nv = 0;
         for (int p = 0; p < pn; ++p) {
-            const int page = pt[p0 + p];
+            const int page = ids[i0 + p];
             nv += page >= 0 && page < a.n_pages;
         }
         if (nv < pn && a.err) atomicOr(a.err, kErrBadIndex);
         mbar_arrive_expect_tx(&full[st % NS], (uint32_t)nv * 2u * NH * kPage * 128u);
         for (int p = 0; p < pn; ++p) {
-            const int page = pt[p0 + p];
+            const int page = ids[i0 + p];
             if (page < 0 || page >= a.n_pages) continue;
             const int row = (page * a.nkv + h) * kPage;
 #pragma unroll
@@ -186,18 +216,26 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         }
     };
 
-    // ---- before the dependency wait: cached pages (earlier steps' state only)
+    // ---- before the dependency wait: stages of cached pages.  The page holding
+    //      `pos` may have been allocated in this step (its page-table entry is
+    //      written by the step's first kernel), so a stage holding it waits.
+    const int n_pre = min(NS, n_st);
+    const int last_page = pos / kPage - pg0;  // split page index of pos (may be out of range)
+    auto early = [&](int st) { return st * CP + min(CP, npg - st * CP) - 1 < last_page; };
     if (tid == 0) {
-        for (int s = 0; s < NS; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kAttnWarps);
-        }
+        for (int s = 0; s < NS; ++s) mbar_init(&full[s], 1);
         fence_barrier_init();
-        for (int st = 0; st < min(NS, n_st); ++st) issue(st);
+        for (int st = 0; st < n_pre; ++st)
+            if (early(st)) issue(st, pt + pg0);
         pdl_trigger();
     }
+    if (tid < NS) cnt[tid] = 0u;
 
     pdl_wait();  // the new token's q/k/v are the previous kernel's output
+    for (int i = tid; i < npg; i += kAttnThreads) pgs[i] = pt[pg0 + i];
+    if (tid == 0)
+        for (int st = 0; st < n_pre; ++st)
+            if (!early(st)) issue(st, pt + pg0);
 
     // ---- RoPE on the group's q heads and the new k (ops.cu:224-232); v as is
     const uint16_t* row = a.qkv + (size_t)b * a.qkv_stride;
@@ -208,70 +246,83 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         const float x1 = __uint_as_float((uint32_t)src[i + HALF] << 16);
         const float ang = (float)pos * a.freqs[i];
         const float c = cosf(ang), s = sinf(ang);
-        float* dst = hh < G ? qf + hh * HD : kn;
-        dst[i] = round_bf(x0 * c - x1 * s);
-        dst[i + HALF] = round_bf(x0 * s + x1 * c);
+        const float y0 = x0 * c - x1 * s, y1 = x0 * s + x1 * c;
+        if (hh < G) {
+            *reinterpret_cast<bf16*>(qs + tile_off(16, hh, i)) = f2bf(y0);
+            *reinterpret_cast<bf16*>(qs + tile_off(16, hh, i + HALF)) = f2bf(y1);
+        } else {
+            kn[i] = round_bf(y0);
+            kn[i + HALF] = round_bf(y1);
+        }
+    }
+    for (int task = tid; task < (16 - G) * HD; task += kAttnThreads) {  // padding heads
+        const int hh = G + task / HD, d = task % HD;
+        *reinterpret_cast<bf16*>(qs + tile_off(16, hh, d)) = f2bf(0.f);
     }
     for (int d = tid; d < HD; d += kAttnThreads)
         vn[d] = __uint_as_float((uint32_t)row[(size_t)(a.nq + a.nkv + h) * HD + d] << 16);
     __syncthreads();
 
-    // q fragments of the score mma: A = q heads (16 rows, >= G zero) x head_dim
-    uint32_t qa[KS][4];
-#pragma unroll
-    for (int ks = 0; ks < KS; ++ks) {
-        const int k0 = ks * 16 + qq * 2;
-        auto qv = [&](int rr, int cc) { return rr < G ? qf[rr * HD + cc] : 0.f; };
-        qa[ks][0] = pack_bf2(qv(gq, k0), qv(gq, k0 + 1));
-        qa[ks][1] = pack_bf2(qv(gq + 8, k0), qv(gq + 8, k0 + 1));
-        qa[ks][2] = pack_bf2(qv(gq, k0 + 8), qv(gq, k0 + 9));
-        qa[ks][3] = pack_bf2(qv(gq + 8, k0 + 8), qv(gq + 8, k0 + 9));
-    }
+    // lane-constant parts of the swizzled ldmatrix addresses (the row's low 3 bits
+    // are the lane's, so the chunk XOR only depends on the lane and a constant)
+    const uint32_t x7 = (uint32_t)(lane & 7);
+    const uint32_t q_lane = ((lane & 7) + ((lane >> 3) & 1) * 8) * 128u;               // q: rows
+    const uint32_t q_y = ((uint32_t)(lane >> 4) ^ x7);                                  // q chunk
+    const uint32_t k_lane = (blk * 16 + (lane & 7)) * 128u;                             // K rows
+    const uint32_t k_y = ((uint32_t)(lane >> 3) ^ x7);                                  // K chunk
+    const uint32_t v_lane = (blk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * 128u;    // V rows
+    const uint32_t v_y = ((uint32_t)(lane >> 4) ^ x7);                                  // V chunk
+    const uint32_t qbase = smem_u32(qs);
+    const float scale2 = a.scale * kLog2e;
+    const int j0 = blk * 16;  // this warp's block: stage rows [j0, j0 + 16)
 
-    // this warp's state: P.V accumulators (heads gq, gq+8 x its dims), running max
-    // and this lane's share of the running sum for heads gq and gq+8
     float o[NT][4];
 #pragma unroll
     for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // heads gq, gq + 8 (base-2 units)
 
-    for (int st = 0; st < n_st; ++st) {
+    for (int st = so; st < n_st; st += SG) {
         uint8_t* kt = ring + (uint32_t)(st % NS) * kAttnStageBytes;
         uint8_t* vt = kt + VOFF;
         const int r0 = st * CT;  // split row of stage row 0
         const int rows = min(CP, npg - st * CP) * kPage;
         const int jlo = max(vlo - r0, 0), jhi = min(vhi - r0, rows);  // valid stage rows
+        // stage groups run apart: the slot may still hold stage st - NS (another
+        // group's), whose barrier phase a parity wait cannot tell from this one.
+        // Its WPS arrivals per earlier stage show when it is done.
+        if (st >= NS) wait_count(&cnt[st % NS], (unsigned)WPS * (unsigned)(st / NS), a.err, kErrTimeoutEmpty);
         mbar_wait(&full[st % NS], (uint32_t)(st / NS) & 1u, a.err, kErrTimeoutFull);
         __syncwarp();  // lanes leave the poll apart; ldmatrix and mma need the whole warp
 
-        // the stage holding `pos` takes the new K/V row into its tile and its page
-        if (pos >= t0 + r0 && pos < t0 + r0 + rows) {
+        // the warp(s) of the block holding `pos` put the new K/V row into the tile
+        // (each writes the whole row before reading it) and one of them into the page
+        if (pos >= t0 + r0 + j0 && pos < t0 + r0 + j0 + kPage && j0 < rows) {
             const int r = pos - t0 - r0;
-            for (int d = tid; d < HD; d += kAttnThreads) {
+            for (int d = lane; d < HD; d += 32) {
                 const uint32_t off = tile_off(CT, r, d);
                 *reinterpret_cast<bf16*>(kt + off) = f2bf(kn[d]);
                 *reinterpret_cast<bf16*>(vt + off) = f2bf(vn[d]);
             }
-            const int page = pt[pos / kPage];
-            if (page >= 0 && page < a.n_pages) {
-                const size_t off = (((size_t)page * a.nkv + h) * kPage + (pos % kPage)) * HD;
-                for (int d = tid; d < HD; d += kAttnThreads) {
-                    reinterpret_cast<bf16*>(a.kc)[off + d] = f2bf(kn[d]);
-                    reinterpret_cast<bf16*>(a.vc)[off + d] = f2bf(vn[d]);
+            if (dp == 0) {
+                const int page = pgs[pos / kPage - pg0];
+                if (page >= 0 && page < a.n_pages) {
+                    const size_t off = (((size_t)page * a.nkv + h) * kPage + (pos % kPage)) * HD;
+                    for (int d = lane; d < HD; d += 32) {
+                        reinterpret_cast<bf16*>(a.kc)[off + d] = f2bf(kn[d]);
+                        reinterpret_cast<bf16*>(a.vc)[off + d] = f2bf(vn[d]);
+                    }
+                } else if (lane == 0 && a.err) {
+                    atomicOr(a.err, kErrBadIndex);
                 }
-            } else if (tid == 0 && a.err) {
-                atomicOr(a.err, kErrBadIndex);
             }
             // the slot is refilled by TMA later: order these generic writes before it
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncthreads();
+            __syncwarp();
         }
 
-#pragma unroll
-        for (int tbi = 0; tbi < TBW; ++tbi) {
-            const int j0 = (wi + tbi * WPD) * 16;  // block rows [j0, j0 + 16)
-            if (j0 + 16 <= jlo || j0 >= jhi) continue;  // warp-uniform
-            if (j0 < jlo || j0 + 16 > jhi) {
+        if (j0 + 16 > jlo && j0 < jhi) {  // warp-uniform
+            const bool edge = j0 < jlo || j0 + 16 > jhi;
+            if (edge) {
                 // rows outside [jlo, jhi) get probability 0: make their V finite (zero)
                 for (int t = lane; t < 16 * (DW / 8); t += 32) {
                     const int jr = j0 + t / (DW / 8), d = dp * DW + (t % (DW / 8)) * 8;
@@ -280,95 +331,132 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
             }
-            // ---- scores of 16 tokens: two n-tiles of 8
-            float c[2][4];
-            const uint32_t kbase = smem_u32(kt);
+            // ---- scores of 16 tokens: two n-tiles of 8, two accumulator chains each
+            float c[2][4], c2[2][4];
+            const uint32_t kbase = smem_u32(kt) + k_lane;
 #pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-                c[nt][0] = c[nt][1] = c[nt][2] = c[nt][3] = 0.f;
-                const int ri = j0 + nt * 8 + (lane & 7), mi = lane >> 3;
+            for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-                for (int ks = 0; ks < KS; ks += 2) {
+                for (int e = 0; e < 4; ++e) c[nt][e] = c2[nt][e] = 0.f;
+#pragma unroll
+            for (int ks = 0; ks < KS; ks += 2) {
+                uint32_t qa0[4], qa1[4];
+                const uint32_t qoff = (uint32_t)(ks >> 2) * 16u * 128u;
+                ldsm_x4(qbase + qoff + q_lane + ((((uint32_t)(ks & 3) * 2u) ^ q_y) << 4), qa0[0], qa0[1], qa0[2],
+                        qa0[3]);
+                ldsm_x4(qbase + qoff + q_lane + ((((uint32_t)((ks + 1) & 3) * 2u) ^ q_y) << 4), qa1[0], qa1[1],
+                        qa1[2], qa1[3]);
+                const uint32_t koff = (uint32_t)(ks >> 2) * CT * 128u + ((((uint32_t)(ks & 2) * 2u) ^ k_y) << 4);
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
                     uint32_t b0, b1, b2, b3;
-                    ldsm_x4(kbase + tile_off(CT, ri, ks * 16 + mi * 8), b0, b1, b2, b3);
-                    mma_16816_bf16(c[nt], qa[ks], b0, b1);
-                    mma_16816_bf16(c[nt], qa[ks + 1], b2, b3);
+                    ldsm_x4(kbase + koff + nt * 1024u, b0, b1, b2, b3);
+                    mma_16816_bf16(c[nt], qa0, b0, b1);
+                    mma_16816_bf16(c2[nt], qa1, b2, b3);
                 }
             }
             // c[nt][0..1]: head gq, rows j0 + 8 nt + 2 qq + {0,1}; c[nt][2..3]: head gq + 8
-            float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int jj = j0 + nt * 8 + qq * 2 + e;
-                    const bool valid = jj >= jlo && jj < jhi;
-                    c[nt][e] = valid ? a.scale * c[nt][e] : -INFINITY;
-                    c[nt][2 + e] = valid ? a.scale * c[nt][2 + e] : -INFINITY;
-                    mx0 = fmaxf(mx0, c[nt][e]);
-                    mx1 = fmaxf(mx1, c[nt][2 + e]);
-                }
+                for (int e = 0; e < 4; ++e) c[nt][e] = (c[nt][e] + c2[nt][e]) * scale2;
+            if (edge) {
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int jj = j0 + nt * 8 + qq * 2 + e;
+                        if (jj < jlo || jj >= jhi) c[nt][e] = c[nt][2 + e] = -INFINITY;
+                    }
+            }
+            // ---- online softmax (ops.cu:393-419 over the whole row), base 2
+            float mx0 = fmaxf(fmaxf(c[0][0], c[0][1]), fmaxf(c[1][0], c[1][1]));
             mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
             mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-            // ---- online softmax (ops.cu:393-419 over the whole row)
-            const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-            const float al0 = m0 == -INFINITY ? 0.f : expf(m0 - n0);
-            const float al1 = m1 == -INFINITY ? 0.f : expf(m1 - n1);
+            const float n0 = fmaxf(m0, mx0);
+            const float u0 = n0 == -INFINITY ? 0.f : n0;
+            const float al0 = ex2(m0 - u0);  // 0 while nothing was seen
             m0 = n0;
-            m1 = n1;
-            float s0 = 0.f, s1 = 0.f;
+            float s0 = 0.f;
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
-                    c[nt][e] = n0 == -INFINITY ? 0.f : expf(c[nt][e] - n0);
-                    c[nt][2 + e] = n1 == -INFINITY ? 0.f : expf(c[nt][2 + e] - n1);
+                    c[nt][e] = ex2(c[nt][e] - u0);
                     s0 += c[nt][e];
-                    s1 += c[nt][2 + e];
                 }
             l0 = fmaf(l0, al0, s0);
-            l1 = fmaf(l1, al1, s1);
+            float al1 = 1.f;
+            if constexpr (G16) {
+                float mx1 = fmaxf(fmaxf(c[0][2], c[0][3]), fmaxf(c[1][2], c[1][3]));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+                const float n1 = fmaxf(m1, mx1);
+                const float u1 = n1 == -INFINITY ? 0.f : n1;
+                al1 = ex2(m1 - u1);
+                m1 = n1;
+                float s1 = 0.f;
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int e = 2; e < 4; ++e) {
+                        c[nt][e] = ex2(c[nt][e] - u1);
+                        s1 += c[nt][e];
+                    }
+                l1 = fmaf(l1, al1, s1);
+            } else {
+                c[0][2] = c[0][3] = c[1][2] = c[1][3] = 0.f;  // padding heads
+            }
             if (__any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
 #pragma unroll
                 for (int n = 0; n < NT; ++n) {
                     o[n][0] *= al0;
                     o[n][1] *= al0;
-                    o[n][2] *= al1;
-                    o[n][3] *= al1;
+                    if constexpr (G16) {
+                        o[n][2] *= al1;
+                        o[n][3] *= al1;
+                    }
                 }
             }
             // ---- P.V: A = P (heads x 16 tokens) as hi + lo bf16 pairs, B = V via ldmatrix.trans
             uint32_t ph[4], pl[4];
             split_bf2(c[0][0], c[0][1], ph[0], pl[0]);
-            split_bf2(c[0][2], c[0][3], ph[1], pl[1]);
             split_bf2(c[1][0], c[1][1], ph[2], pl[2]);
-            split_bf2(c[1][2], c[1][3], ph[3], pl[3]);
-            const uint32_t vbase = smem_u32(vt);
-            const int vr = j0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+            if constexpr (G16) {
+                split_bf2(c[0][2], c[0][3], ph[1], pl[1]);
+                split_bf2(c[1][2], c[1][3], ph[3], pl[3]);
+            } else {
+                ph[1] = pl[1] = ph[3] = pl[3] = 0u;
+            }
+            const uint32_t vbase = smem_u32(vt) + v_lane + (uint32_t)(dp * DW / 64) * CT * 128u;
 #pragma unroll
             for (int n = 0; n < NT; n += 2) {
                 uint32_t b0, b1, b2, b3;
-                ldsm_x4_t(vbase + tile_off(CT, vr, dp * DW + n * 8 + (lane >> 4) * 8), b0, b1, b2, b3);
+                ldsm_x4_t(vbase + (uint32_t)(n / 8) * CT * 128u + ((((uint32_t)(n & 7)) ^ v_y) << 4), b0, b1, b2,
+                          b3);
                 mma_16816_bf16(o[n], ph, b0, b1);
-                mma_16816_bf16(o[n], pl, b0, b1);
                 mma_16816_bf16(o[n + 1], ph, b2, b3);
+                mma_16816_bf16(o[n], pl, b0, b1);
                 mma_16816_bf16(o[n + 1], pl, b2, b3);
             }
         }
-        // release the slot: every warp arrives; warp 0 refills it once all have
+        // release the slot: the last of its warps to finish refills it
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st % NS]);
-        if (tid == 0 && st + NS < n_st) {
-            mbar_wait(&empty[st % NS], (uint32_t)(st / NS) & 1u, a.err, kErrTimeoutFull);
-            issue(st + NS);
+        if (lane == 0) {
+            __threadfence_block();
+            // the count only grows: every WPS-th arrival on a slot ends a stage
+            const unsigned int done = atomicAdd(&cnt[st % NS], 1u);
+            if ((done + 1u) % (unsigned)WPS == 0u) {
+                __threadfence_block();
+                if (st + NS < n_st) issue(st + NS, pgs);
+            }
         }
         __syncwarp();
     }
 
-    // ---- merge the warps: per head the max over the warps of a dim part, each
-    //      warp's accumulators and sums rescaled to it, summed in warp order
+    // ---- merge the warps: per head the max over the warps of dim part 0 (they
+    //      saw every block; the other parts saw the same ones), each warp's
+    //      accumulators and sums rescaled to it, summed in warp order
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
@@ -380,14 +468,15 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         wml[(warp * 16 + gq + 8) * 2 + 1] = l1;
     }
     __syncthreads();  // also: every stage consumed, no copy in flight into the ring
+    auto part_of = [&](int w) { return (w % WPS) / CP; };
     if (tid < kAttnMaxGroup) {
-        // warps of dim part 0 saw every token block (the other parts saw the same ones)
         float M = -INFINITY;
-        for (int w = 0; w < WPD; ++w) M = fmaxf(M, wml[(w * 16 + tid) * 2]);
+        for (int w = 0; w < kAttnWarps; ++w)
+            if (part_of(w) == 0) M = fmaxf(M, wml[(w * 16 + tid) * 2]);
         float Ls = 0.f;
-        for (int w = 0; w < WPD; ++w) {
+        for (int w = 0; w < kAttnWarps; ++w) {
             const float mw = wml[(w * 16 + tid) * 2];
-            if (mw != -INFINITY) Ls = fmaf(wml[(w * 16 + tid) * 2 + 1], expf(mw - M), Ls);
+            if (part_of(w) == 0 && mw != -INFINITY) Ls = fmaf(wml[(w * 16 + tid) * 2 + 1], ex2(mw - M), Ls);
         }
         hml[2 * tid] = M;
         hml[2 * tid + 1] = Ls;
@@ -396,8 +485,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     float* red = reinterpret_cast<float*>(ring);  // [warps][16][DW]
     {
         const float M0 = hml[2 * gq], M1 = hml[2 * (gq + 8)];
-        const float f0 = m0 == -INFINITY ? 0.f : expf(m0 - M0);
-        const float f1 = m1 == -INFINITY ? 0.f : expf(m1 - M1);
+        const float f0 = m0 == -INFINITY ? 0.f : ex2(m0 - M0);
+        const float f1 = m1 == -INFINITY ? 0.f : ex2(m1 - M1);
 #pragma unroll
         for (int n = 0; n < NT; ++n) {
             const int d = n * 8 + qq * 2;
@@ -415,8 +504,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         const int part = d / DW, dl = d - part * DW;
         float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int w = 0; w < WPD; ++w) {
-            const float4 v = *reinterpret_cast<const float4*>(red + ((size_t)(part * WPD + w) * 16 + g) * DW + dl);
+        for (int w = 0; w < kAttnWarps; ++w) {
+            if (part_of(w) != part) continue;
+            const float4 v = *reinterpret_cast<const float4*>(red + ((size_t)w * 16 + g) * DW + dl);
             O.x += v.x;
             O.y += v.y;
             O.z += v.z;
@@ -450,7 +540,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     if (!s_last) return;
     __threadfence();
     const size_t p0 = ((size_t)b * a.nkv + h) * a.n_splits * G;
-    // split weights w[s][g] = exp(m_s - M_g) (0 for empty splits), over the ring
+    // split weights w[s][g] = 2^(m_s - M_g) (0 for empty splits), over the ring
     float* wsg = reinterpret_cast<float*>(ring);  // [n_splits][G] maxima, then weights
     float* lsg = wsg + a.n_splits * G;            // [n_splits][G] sums
     for (int idx = tid; idx < a.n_splits * G; idx += kAttnThreads) {
@@ -465,7 +555,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         float Ls = 0.f;
         for (int s = 0; s < a.n_splits; ++s) {
             const float l = lsg[s * G + tid];
-            const float w = l > 0.f ? expf(wsg[s * G + tid] - M) : 0.f;
+            const float w = l > 0.f ? ex2(wsg[s * G + tid] - M) : 0.f;
             wsg[s * G + tid] = w;
             Ls = fmaf(l, w, Ls);
         }
@@ -497,28 +587,40 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
 }
 
 int attn_splits(int nb, int nkv, int hd, int max_len, int sms, int* max_chunk) {
-    // stages per split: about kWaves waves of two CTAs per SM over the batch's
-    // (token, kv head) pairs at the longest context (env TI_ATTN_SPP overrides);
-    // splits of near-equal length, at most kAttnMaxSplits of them
-    const int ct = attn_ct(hd);
+    // Splits per (token, kv head) pair, chosen on a cost model of the grid: CTAs
+    // run two per SM (S = 2 sms slots); while at least `sms` CTAs are active the
+    // grid streams at the HBM rate, below that each CTA is limited by its own
+    // loads in flight.  Cost = (full waves + the last wave's share, counted as at
+    // least sms CTAs) x (stages per split + a fixed start-up cost).  Long splits
+    // amortise the start (first loads, RoPE) and the merge; the model avoids a
+    // last wave of a few long CTAs.  Env TI_ATTN_SPP forces the stages per split.
+    const int ct = attn_ct(hd), cp = ct / kPage;
     const int max_pages = std::max(1, (max_len + kPage - 1) / kPage);
-    const int stages = (max_pages + ct / kPage - 1) / (ct / kPage);
+    const int stages = (max_pages + cp - 1) / cp;
+    const int max_spp = std::max(1, std::min(stages, kAttnMaxSplitPages / cp));
+    const int min_n = std::max((stages + max_spp - 1) / max_spp, 1);
+    int spp = 0;
     const char* env = std::getenv("TI_ATTN_SPP");
-    int spp;
     if (env && std::atoi(env) >= 1) {
-        spp = std::atoi(env);
+        spp = std::min(std::atoi(env), max_spp);
+        spp = std::max(spp, (stages + kAttnMaxSplits - 1) / kAttnMaxSplits);
     } else {
-        const char* wv = std::getenv("TI_ATTN_WAVES");
-        const long waves = wv && std::atoi(wv) >= 1 ? std::atoi(wv) : 4;
-        const long target = waves * 2L * sms;
-        const long work = (long)std::max(1, nb * nkv) * stages;
-        spp = (int)std::max<long>(1, (work + target - 1) / target);
+        constexpr double kStartStages = 3.0;
+        const long pairs = std::max(1, nb * nkv);
+        const long S = 2L * sms, Q = sms;
+        double best = 0.0;
+        for (int n = min_n; n <= std::min(stages, kAttnMaxSplits); ++n) {
+            const int sp = (stages + n - 1) / n;
+            if ((stages + sp - 1) / sp != n) continue;  // the same split as a smaller n
+            const long C = pairs * n, full = (C - 1) / S, r = C - full * S;
+            const double cost = ((double)full + (double)std::max(r, Q) / (double)S) * ((double)sp + kStartStages);
+            if (spp == 0 || cost < best) {
+                best = cost;
+                spp = sp;
+            }
+        }
     }
-    spp = std::max(spp, (stages + kAttnMaxSplits - 1) / kAttnMaxSplits);
-    spp = std::min(spp, stages);
-    int n = (stages + spp - 1) / spp;
-    spp = (stages + n - 1) / n;  // even out the splits
-    n = (stages + spp - 1) / spp;
+    const int n = (stages + spp - 1) / spp;
     *max_chunk = spp * ct;
     return n;
 }
@@ -533,21 +635,26 @@ cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s, bool pdl) {
     if (a.hd != 64 && a.hd != 128 && a.hd != 256) return cudaErrorInvalidValue;
     const int ct = attn_ct(a.hd);
     const int G = a.nq / a.nkv;
-    if (a.max_chunk < ct || a.max_chunk % ct != 0) return cudaErrorInvalidValue;
+    if (a.max_chunk < ct || a.max_chunk % ct != 0 || a.max_chunk / kPage > kAttnMaxSplitPages)
+        return cudaErrorInvalidValue;
     // the merge weights [2][n_splits][G] are laid over the ring
     if (a.n_splits < 1 || (size_t)2 * a.n_splits * G * 4 > (size_t)kAttnStages * kAttnStageBytes)
         return cudaErrorInvalidValue;
     const void* f = nullptr;
+    const bool g16 = G > 8;
     switch (a.hd) {
-        case 64: f = reinterpret_cast<const void*>(&k_attn_decode<64>); break;
-        case 128: f = reinterpret_cast<const void*>(&k_attn_decode<128>); break;
-        default: f = reinterpret_cast<const void*>(&k_attn_decode<256>); break;
+        case 64: f = g16 ? reinterpret_cast<const void*>(&k_attn_decode<64, true>)
+                         : reinterpret_cast<const void*>(&k_attn_decode<64, false>); break;
+        case 128: f = g16 ? reinterpret_cast<const void*>(&k_attn_decode<128, true>)
+                          : reinterpret_cast<const void*>(&k_attn_decode<128, false>); break;
+        default: f = g16 ? reinterpret_cast<const void*>(&k_attn_decode<256, true>)
+                         : reinterpret_cast<const void*>(&k_attn_decode<256, false>); break;
     }
     CUtensorMap tk, tv;
     const uint64_t rows = (uint64_t)a.n_pages * a.nkv * kPage;
     if (!make_tmap_bf16_sw128(&tk, a.kc, rows, a.hd, a.hd, kPage)) return cudaErrorInvalidValue;
     if (!make_tmap_bf16_sw128(&tv, a.vc, rows, a.hd, a.hd, kPage)) return cudaErrorInvalidValue;
-    const size_t smem = attn_layout(G, a.hd).total;
+    const size_t smem = attn_layout(a.hd).total;
     if (smem > 227 * 1024) return cudaErrorInvalidValue;
     {
         static std::mutex mu;

@@ -211,9 +211,10 @@ def check_paged(c, out, kp, vp):
 
 
 @pytest.mark.parametrize("hd,nq,nkv,spp", [(128, 16, 2, None), (128, 16, 2, 3), (64, 8, 2, 2), (256, 8, 1, 4),
-                                           (128, 4, 4, 16)])
+                                           (128, 4, 4, 16), (128, 8, 2, 1000), (64, 4, 1, 1000), (256, 16, 1, 1000)])
 def test_paged_attention_long(hd, nq, nkv, spp, monkeypatch):
-    """long contexts: many ring stages per split (TI_ATTN_SPP), several splits merged"""
+    """long contexts: many ring stages per split (TI_ATTN_SPP), several splits merged
+    or (TI_ATTN_SPP beyond the context) one split per (token, kv head)"""
     if spp:
         monkeypatch.setenv("TI_ATTN_SPP", str(spp))
     c = paged_case(seed=5, B=2, nq=nq, nkv=nkv, hd=hd, pos=(1500, 777), max_len=2048)
