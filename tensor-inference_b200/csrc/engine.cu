@@ -469,7 +469,7 @@ ti_status build(ti_engine* e) {
     }
     if (e->o.max_adapters > 0) {
         e->S = e->o.max_adapters;
-        e->R = (e->o.max_lora_rank + 7) / 8 * 8;  // padded to whole 16-byte rows
+        e->R = (e->o.max_lora_rank + 15) / 16 * 16;  // padded to whole mma k-steps (16)
         e->lmask = e->o.lora_proj_mask;
         const int R = e->R;
         const bool on[4] = {(e->lmask & 7) != 0, (e->lmask & 8) != 0, (e->lmask & 48) != 0, (e->lmask & 64) != 0};

@@ -6,14 +6,52 @@
 // projection (:35-43).  Here `down` is this kernel's output; the weight-streaming
 // GEMV that produces the base projection applies the expansion in its epilogue.
 // Per-token adapters make it a segmented gather: token b reads the A rows of
-// adapter[b] (no adapter: nothing is written and the GEMV skips the delta).
+// adapter[b] (no adapter: nothing is written and the GEMV skips the delta); the
+// grid runs over (row tile, adapter), the adapter's tokens are the rows of
+// tensor-core mma tiles, so an adapter's rows are read once for all its tokens.
 // x is the projection's input: RMSNorm(hidden) for q|k|v and gate|up (the same
 // normalised row the reference passes to both the base and the LoRA matmul),
 // the attention output for o, the SwiGLU activation for down.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
 namespace ti {
+
+// ---- shared helpers
+// Tokens b < nb with adapter[b] == ad, ascending, into list (warp 0; ballot
+// compaction); returns their count to every thread.
+__device__ __forceinline__ int adapter_tokens(const int32_t* adapter, int nb, int ad, int* list, int* s_n) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp == 0) {
+        int n = 0;
+        for (int base = 0; base < nb; base += 32) {
+            const int b = base + lane;
+            const bool m = b < nb && adapter[b] == ad;
+            const unsigned int bal = __ballot_sync(0xffffffffu, m);
+            if (m) list[n + __popc(bal & ((1u << lane) - 1u))] = b;
+            n += __popc(bal);
+        }
+        if (lane == 0) *s_n = n;
+    }
+    __syncthreads();
+    return *s_n;
+}
+TI_DEVICE_INLINE void ldsm_x4_l(uint32_t addr, uint32_t* r) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+// D(16x8 fp32) += A(16x16 bf16, row) * B(16x8 bf16, col)
+TI_DEVICE_INLINE void mma_bf16_16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+TI_DEVICE_INLINE uint32_t ldg_u32(const uint16_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
 constexpr int kShrinkThreads = 256;
 constexpr int kShrinkRowsPerCta = 16;
@@ -104,14 +142,83 @@ cudaError_t lora_shrink_launch(const LoraShrinkArgs& a, cudaStream_t s, bool pdl
 }
 
 
-// ---- expansion ahead of the tensor-core GEMM: CTA (row tile, token b), one output
-//      row per thread, t read as warp-uniform broadcasts.  One CTA per token (rather
-//      than per adapter, rereading nothing) measured faster: the rereads of a B row
-//      by tokens sharing an adapter hit L2, and the extra CTAs hide latency.
+// ---- expansion ahead of the tensor-core GEMM, on the tensor cores:
+//      dval[b, n] = bf16(bf16(sum_r t[b, r] B[ad][n, r]) * scale[ad]) for the
+//      adapter's tokens, 16 at a time (mma rows).  CTA (128 output rows,
+//      adapter), 4 warps of 4 n-tiles; t staged in shared memory as bf16 (its
+//      values are bf16 already), B fragments read straight from global memory:
+//      each B row is read once per adapter.
 constexpr int kExpandThreads = 128;
 
+template <int KS>  // rank / 16 mma k-steps
 __global__ void __launch_bounds__(kExpandThreads)
     k_lora_expand(const GemvLora L, int nb, int n_rows, int glu_n, uint16_t* dval, int dval_stride) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int tw = L.t_stride + 8;                                        // staged row width (bf16)
+    uint16_t* ts = reinterpret_cast<uint16_t*>(smem);                    // [16][tw]
+    int* list = reinterpret_cast<int*>(smem + (size_t)16 * tw * 2);      // [nb]
+    __shared__ int s_n;
+    constexpr int R = KS * 16;
+    const int ad = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, q = lane & 3;
+    if (tid == 0) pdl_trigger();
+    const int n = adapter_tokens(L.adapter, nb, ad, list, &s_n);  // tokens without an adapter: no CTA
+    if (n == 0 || ad >= L.n_adapters) return;
+    const uint16_t* Bad = L.B + (size_t)ad * L.B_adapter_stride;
+    const float sc = L.scale[ad];
+    const int row0 = blockIdx.x * 128 + warp * 32;
+    const int nt_n = max(0, min(4, (n_rows - row0) / 8));  // this warp's n-tiles (n_rows % 8 == 0)
+    // B fragments of the warp's n-tiles (adapter weights: not the previous kernel's output)
+    uint32_t bf[4][KS][2];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+        const uint16_t* br = Bad + (size_t)(row0 + (nt < nt_n ? nt : 0) * 8 + g) * R + 2 * q;
+#pragma unroll
+        for (int k = 0; k < KS; ++k) {
+            bf[nt][k][0] = nt < nt_n ? ldg_u32(br + k * 16) : 0u;
+            bf[nt][k][1] = nt < nt_n ? ldg_u32(br + k * 16 + 8) : 0u;
+        }
+    }
+    const uint32_t tbase = smem_u32(ts) + (uint32_t)(((lane & 7) + ((lane >> 3) & 1) * 8) * tw + (lane >> 4) * 8) * 2u;
+    pdl_wait();  // t is the previous kernel's output
+    for (int m0 = 0; m0 < n; m0 += 16) {
+        const int mt = min(16, n - m0);
+        if (m0 > 0) __syncthreads();
+        for (int i = tid; i < 16 * L.t_stride; i += kExpandThreads) {
+            const int j = i / L.t_stride, k = i - j * L.t_stride;
+            const float v = j < mt ? L.t[(size_t)list[m0 + j] * L.t_stride + k] : 0.f;
+            ts[(size_t)j * tw + k] = __bfloat16_as_ushort(f2bf(v));
+        }
+        __syncthreads();
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+            if (nt >= nt_n) break;  // warp-uniform
+            const int n0 = row0 + nt * 8;
+            int sec = 0;
+            if (glu_n > 0) sec = n0 >= glu_n;
+            else sec = (n0 >= L.sec1) + (n0 >= L.sec2);
+            float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int k = 0; k < KS; ++k) {
+                uint32_t af[4];
+                ldsm_x4_l(tbase + (uint32_t)(sec * R + k * 16) * 2u, af);
+                mma_bf16_16816(c, af, bf[nt][k][0], bf[nt][k][1]);
+            }
+            // c[0..1]: token g, rows n0 + 2q, +1; c[2..3]: token g + 8
+            if (g < mt)
+                *reinterpret_cast<uint32_t*>(dval + (size_t)list[m0 + g] * dval_stride + n0 + 2 * q) =
+                    pack_bf2(round_bf(c[0]) * sc, round_bf(c[1]) * sc);
+            if (g + 8 < mt)
+                *reinterpret_cast<uint32_t*>(dval + (size_t)list[m0 + g + 8] * dval_stride + n0 + 2 * q) =
+                    pack_bf2(round_bf(c[2]) * sc, round_bf(c[3]) * sc);
+        }
+    }
+}
+
+// ranks above 128: one output row per thread, CTA (row tile, token); the same
+// element order as the GEMV epilogue's expansion
+__global__ void __launch_bounds__(kExpandThreads)
+    k_lora_expand_rows(const GemvLora L, int nb, int n_rows, int glu_n, uint16_t* dval, int dval_stride) {
     if (threadIdx.x == 0) pdl_trigger();
     const int b = blockIdx.y;
     const int ad = L.adapter[b];
@@ -139,12 +246,33 @@ __global__ void __launch_bounds__(kExpandThreads)
 
 cudaError_t lora_expand_launch(const GemvLora& L, int nb, int n_rows, int glu_n, uint16_t* dval, int dval_stride,
                                cudaStream_t s, bool pdl) {
-    if (!L.adapter || L.rank % 8 != 0 || nb < 1) return cudaErrorInvalidValue;
+    if (!L.adapter || L.rank % 16 != 0 || nb < 1 || L.n_adapters < 1 || n_rows % 8 != 0 || dval_stride % 2 != 0 ||
+        L.t_stride % 8 != 0)
+        return cudaErrorInvalidValue;
+    const void* f = nullptr;
+    switch (L.rank / 16) {
+        case 1: f = reinterpret_cast<const void*>(&k_lora_expand<1>); break;
+        case 2: f = reinterpret_cast<const void*>(&k_lora_expand<2>); break;
+        case 3: f = reinterpret_cast<const void*>(&k_lora_expand<3>); break;
+        case 4: f = reinterpret_cast<const void*>(&k_lora_expand<4>); break;
+        case 5: f = reinterpret_cast<const void*>(&k_lora_expand<5>); break;
+        case 6: f = reinterpret_cast<const void*>(&k_lora_expand<6>); break;
+        case 7: f = reinterpret_cast<const void*>(&k_lora_expand<7>); break;
+        case 8: f = reinterpret_cast<const void*>(&k_lora_expand<8>); break;
+        default: break;
+    }
     GemvLora args = L;
     void* params[] = {&args, &nb, &n_rows, &glu_n, &dval, &dval_stride};
-    return launch_pdl(reinterpret_cast<const void*>(&k_lora_expand),
-                      dim3((n_rows + kExpandThreads - 1) / kExpandThreads, nb), dim3(kExpandThreads), 0, s, params,
-                      pdl);
+    if (!f)
+        return launch_pdl(reinterpret_cast<const void*>(&k_lora_expand_rows),
+                          dim3((n_rows + kExpandThreads - 1) / kExpandThreads, nb), dim3(kExpandThreads), 0, s, params,
+                          pdl);
+    const size_t smem = (size_t)16 * (L.t_stride + 8) * 2 + (size_t)nb * 4;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    return launch_pdl(f, dim3((n_rows + 127) / 128, L.n_adapters), dim3(kExpandThreads), smem, s, params, pdl);
 }
 
 }  // namespace ti
