@@ -154,6 +154,8 @@ struct ti_engine {
     int lK[4] = {}, lT[4] = {}, lRows[4] = {};  // A row length, A rows (sections*R), B rows
     float* lscale = nullptr;
     float* lt[4] = {};  // shrink outputs [B][T]
+    float* lws[4] = {};          // shrink split-K partials [kLoraMaxSplit][B][T]
+    unsigned int* lctr[4] = {};  // shrink tile counters [S][ceil(T / 32)]
     uint16_t* ldval = nullptr;  // expansions ahead of the tensor-core GEMM [B][rows] bf16
     std::vector<AdapterMeta> adapters;
     cudaStream_t side = nullptr;
@@ -495,6 +497,11 @@ ti_status build(ti_engine* e) {
             }
             TI_CHECK(dalloc_t(e, &e->lt[k], (size_t)B * T[k], &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
                      ti_last_error());
+            TI_CHECK(dalloc_t(e, &e->lws[k], (size_t)kLoraMaxSplit * B * T[k], &e->bytes_work) == TI_OK, TI_ERR_OOM,
+                     "%s", ti_last_error());
+            const size_t nctr = (size_t)e->S * ((T[k] + 31) / 32);
+            TI_CHECK(dalloc_t(e, &e->lctr[k], nctr, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+            TI_CUDA(cudaMemset(e->lctr[k], 0, nctr * 4));
         }
         TI_CHECK(dalloc_t(e, &e->lscale, e->S, &e->bytes_ad) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
         TI_CUDA(cudaMemset(e->lscale, 0, (size_t)e->S * 4));
@@ -593,6 +600,18 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         if (!tc_plan(a, epi, e->dev, e->tc_ws_floats, &plan, &why)) return fail(TI_ERR_UNSUPPORTED, "%s", why.c_str());
         TI_CUDA(tc_launch(a, epi, plan, e->tc_ws, e->tc_ctr, s, true));
         if (launches) ++*launches;
+        return TI_OK;
+    };
+
+    // the tcgen05 path takes normalised rows: one RMSNorm pass ahead of the GEMM
+    // (and of the LoRA shrink, which then reads the same rows)
+    auto prenorm = [&](GemvArgs& a) -> ti_status {
+        if (!(e->xn && B >= e->tc_min && B <= 256) || !a.norm_w) return TI_OK;
+        TI_CUDA(rms_rows_launch(a.x, a.x_stride, a.norm_w, a.eps, a.norm_offset, a.K, B, e->xn, a.K, s, true));
+        if (launches) ++*launches;
+        a.x = e->xn;
+        a.x_stride = a.K;
+        a.norm_w = nullptr;
         return TI_OK;
     };
 
@@ -738,6 +757,8 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         la.n_adapters = e->S;
         la.t = e->lt[k];
         la.t_stride = e->lT[k];
+        la.ws = e->lws[k];
+        la.ctr = e->lctr[k];
         if (e->tp.tp > 1 && (k == 1 || k == 3)) {
             // row-parallel: partial sums over this rank's input columns to every rank
             const int ph = k == 1 ? 0 : 1;
@@ -782,7 +803,8 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             q.err = e->err;
             set_next(q, l.wo, H, QW, 1);
             if (lora_on(0)) {
-                if (ti_status st = shrink(0, e->hidden, H, l.norm1)) return st;
+                if (ti_status st = prenorm(q)) return st;
+                if (ti_status st = shrink(0, q.x, q.x_stride, q.norm_w)) return st;
                 set_lora(q, 0);
             }
             return gemm(q, kEpiStore, H, e->qkv_rows, 0);
@@ -862,7 +884,8 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             gu.err = e->err;
             set_next(gu, l.wdown, H, I, 1);
             if (lora_on(2)) {
-                if (ti_status st = shrink(2, e->res1, H, l.norm2)) return st;
+                if (ti_status st = prenorm(gu)) return st;
+                if (ti_status st = shrink(2, gu.x, gu.x_stride, gu.norm_w)) return st;
                 set_lora(gu, 2);
             }
             return gemm(gu, kEpiGlu, H, I, 0);

@@ -88,7 +88,13 @@ struct LoraShrinkArgs {
     // columns; the unrounded fp32 partial sums go to every rank's inbox instead of t
     float* peer_t[kMaxTp] = {};
     int tp = 0;
+    // split-K workspace: partial sums [kLoraMaxSplit][nb][t_stride] and per
+    // (adapter, 32-row tile) arrival counters [n_adapters][ceil(T / 32)] (zero;
+    // the last CTA of a tile resets its counter)
+    float* ws = nullptr;
+    unsigned int* ctr = nullptr;
 };
+constexpr int kLoraMaxSplit = 16;
 cudaError_t lora_shrink_launch(const LoraShrinkArgs& a, cudaStream_t s, bool pdl);
 
 // Weight row formats the GEMV streams (TI_WFMT_* values).  Quantised rows are

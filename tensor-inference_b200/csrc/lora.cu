@@ -53,92 +53,198 @@ TI_DEVICE_INLINE void mma_bf16_16816(float* c, const uint32_t* a, uint32_t b0, u
 }
 TI_DEVICE_INLINE uint32_t ldg_u32(const uint16_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
+// ---- shrink on the tensor cores: t[b, r] = x_b . A[ad_b][r] for the adapter's
+//      tokens (mma rows, 16 at a time).  Grid (32-row tile of A, adapter,
+//      K slice); warp w of a CTA takes the k-steps (16 columns) w, w + 8, ... of
+//      its slice, with x and A fragments loaded straight from global memory (x
+//      rows are small and L2-resident; each A row is read once per adapter).
+//      The 8 warps' sums are added in warp order, the slices' by the last CTA of
+//      the tile in slice order.  RMSNorm of x (when the projection's input is
+//      the unnormalised hidden state) is applied to the fragments, with the
+//      per-token scale reduced in the base projection's order (ops.cu:179).
 constexpr int kShrinkThreads = 256;
-constexpr int kShrinkRowsPerCta = 16;
+constexpr int kShrinkWarps = kShrinkThreads / 32;
+constexpr int kShrinkRows = 32;  // 4 n-tiles of 8 A rows
+constexpr int kShrinkUnroll = 4;  // k-steps per warp with their loads in flight together
 
-__global__ void __launch_bounds__(kShrinkThreads) k_lora_shrink(const LoraShrinkArgs a) {
+TI_DEVICE_INLINE uint32_t norm_pair(uint32_t v, uint32_t w, float sc, float off) {
+    return pack_bf2(bf_lo(v) * sc * (bf_lo(w) + off), bf_hi(v) * sc * (bf_hi(w) + off));
+}
+
+__global__ void __launch_bounds__(kShrinkThreads) k_lora_shrink(const LoraShrinkArgs a, int ksplit, int kr) {
     extern __shared__ __align__(16) uint8_t smem[];
-    uint16_t* xs = reinterpret_cast<uint16_t*>(smem);  // [K] normalised bf16 row
-    __shared__ float red[kShrinkThreads / 32];
-    const int b = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float* red = reinterpret_cast<float*>(smem);                                  // [warps][16][32]
+    int* list = reinterpret_cast<int*>(red + kShrinkWarps * 16 * kShrinkRows);    // [nb]
+    __shared__ float sred[16][kShrinkWarps];
+    __shared__ float sscale[16];
+    __shared__ int s_n, s_last;
+    const int ad = blockIdx.y, rt = blockIdx.x, ksl = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, q = lane & 3;
     if (tid == 0) pdl_trigger();
-    const int ad = a.adapter[b];
+    // the adapter ids come with the step descriptor, not from the previous kernel
+    const int n = adapter_tokens(a.adapter, a.nb, ad, list, &s_n);
+    if (n == 0 || ad >= a.n_adapters) return;
     pdl_wait();
-    if (ad < 0 || ad >= a.n_adapters) return;
     const int K = a.K;
-    const uint16_t* x = a.x + (size_t)b * a.x_stride;
-    // load (and normalise) the row: 8 bf16 per thread-iteration
-    float ss = 0.f;
-    for (int c = tid * 8; c < K; c += kShrinkThreads * 8) {
-        const uint4 v = *reinterpret_cast<const uint4*>(x + c);
-        *reinterpret_cast<uint4*>(xs + c) = v;
-        const uint32_t* vp = reinterpret_cast<const uint32_t*>(&v);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            ss = fmaf(bf_lo(vp[e]), bf_lo(vp[e]), ss);
-            ss = fmaf(bf_hi(vp[e]), bf_hi(vp[e]), ss);
-        }
-    }
-    if (a.norm_w) {
-        ss = warp_sum(ss);
-        if (lane == 0) red[warp] = ss;
-        __syncthreads();
-        float tot = 0.f;
-#pragma unroll
-        for (int w = 0; w < kShrinkThreads / 32; ++w) tot += red[w];
-        const float scale = rsqrtf(tot / (float)K + a.eps);  // ops.cu:179
-        const float off = a.norm_offset ? 1.0f : 0.0f;
-        for (int c = tid * 8; c < K; c += kShrinkThreads * 8) {
-            uint4 v = *reinterpret_cast<const uint4*>(xs + c);
-            const uint4 wn = *reinterpret_cast<const uint4*>(a.norm_w + c);
-            uint32_t* vp = reinterpret_cast<uint32_t*>(&v);
-            const uint32_t* wp = reinterpret_cast<const uint32_t*>(&wn);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float lo = bf_lo(vp[e]) * scale * (bf_lo(wp[e]) + off);
-                const float hi = bf_hi(vp[e]) * scale * (bf_hi(wp[e]) + off);
-                vp[e] = pack_bf2(lo, hi);
-            }
-            *reinterpret_cast<uint4*>(xs + c) = v;
-        }
-    }
-    __syncthreads();
-    // rows of this CTA: warp w takes rows r0 + w, r0 + w + 8
     const uint16_t* A = a.A + (size_t)ad * a.A_adapter_stride;
-    const int r0 = blockIdx.x * kShrinkRowsPerCta;
-    for (int r = r0 + warp; r < min(a.T, r0 + kShrinkRowsPerCta); r += kShrinkThreads / 32) {
-        const uint16_t* ar = A + (size_t)r * K;
-        float acc = 0.f;
-        for (int c = lane * 8; c < K; c += 32 * 8) {
-            const uint4 w = *reinterpret_cast<const uint4*>(ar + c);
-            const uint4 xv = *reinterpret_cast<const uint4*>(xs + c);
-            acc = dot8_bf16(w, xv, acc);
+    const int r0 = rt * kShrinkRows;
+    const int ntv = min(4, (a.T - r0) / 8);  // n-tiles inside T (T % 16 == 0)
+    const int kb = ksl * kr, ke = min(K, kb + kr);
+    const float off = a.norm_offset ? 1.0f : 0.0f;
+    const uint16_t* arow[4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) arow[nt] = A + (size_t)(r0 + (nt < ntv ? nt : 0) * 8 + g) * K + 2 * q;
+
+    for (int m0 = 0; m0 < n; m0 += 16) {
+        const int mt = min(16, n - m0);
+        if (a.norm_w) {
+            // the tokens' RMSNorm scales: per-thread strided sums, warp butterfly,
+            // warp-ordered total (the base projection's prologue)
+            for (int j = 0; j < mt; ++j) {
+                const uint16_t* x = a.x + (size_t)list[m0 + j] * a.x_stride;
+                float ss = 0.f;
+                for (int c = tid * 8; c < K; c += kShrinkThreads * 8) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(x + c);
+                    const uint32_t* vp = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        ss = fmaf(bf_lo(vp[e]), bf_lo(vp[e]), ss);
+                        ss = fmaf(bf_hi(vp[e]), bf_hi(vp[e]), ss);
+                    }
+                }
+                ss = warp_sum(ss);
+                if (lane == 0) sred[j][warp] = ss;
+            }
+            __syncthreads();
+            if (tid < mt) {
+                float tot = 0.f;
+#pragma unroll
+                for (int w = 0; w < kShrinkWarps; ++w) tot += sred[tid][w];
+                sscale[tid] = rsqrtf(tot / (float)K + a.eps);
+            }
+            __syncthreads();
         }
-        acc = warp_sum(acc);
-        if (lane == 0) {
-            if (a.tp) {
-                // row-parallel under tensor parallelism: fp32 partial to every rank
-                for (int q = 0; q < a.tp; ++q) a.peer_t[q][(size_t)b * a.t_stride + r] = acc;
-            } else {
-                a.t[(size_t)b * a.t_stride + r] = round_bf(acc);
+        // this lane's two token rows (g, g + 8); absent tokens read as zero
+        const bool v0 = g < mt, v1 = g + 8 < mt;
+        const uint16_t* x0 = a.x + (size_t)(v0 ? list[m0 + g] : list[m0]) * a.x_stride + 2 * q;
+        const uint16_t* x1 = a.x + (size_t)(v1 ? list[m0 + g + 8] : list[m0]) * a.x_stride + 2 * q;
+        const float sc0 = a.norm_w && v0 ? sscale[g] : 0.f, sc1 = a.norm_w && v1 ? sscale[g + 8] : 0.f;
+        float acc[4][4];
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+        for (int k0 = kb + warp * 16; k0 < ke; k0 += kShrinkWarps * 16 * kShrinkUnroll) {
+            uint32_t xf[kShrinkUnroll][4], bf[kShrinkUnroll][4][2];
+#pragma unroll
+            for (int u = 0; u < kShrinkUnroll; ++u) {
+                const int k = k0 + u * kShrinkWarps * 16;
+                const bool in = k < ke;
+                xf[u][0] = in && v0 ? ldg_u32(x0 + k) : 0u;
+                xf[u][1] = in && v1 ? ldg_u32(x1 + k) : 0u;
+                xf[u][2] = in && v0 ? ldg_u32(x0 + k + 8) : 0u;
+                xf[u][3] = in && v1 ? ldg_u32(x1 + k + 8) : 0u;
+#pragma unroll
+                for (int nt = 0; nt < 4; ++nt) {
+                    bf[u][nt][0] = in && nt < ntv ? ldg_u32(arow[nt] + k) : 0u;
+                    bf[u][nt][1] = in && nt < ntv ? ldg_u32(arow[nt] + k + 8) : 0u;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kShrinkUnroll; ++u) {
+                const int k = k0 + u * kShrinkWarps * 16;
+                if (k >= ke) break;  // warp-uniform
+                if (a.norm_w) {
+                    const uint32_t w0 = ldg_u32(a.norm_w + k + 2 * q), w1 = ldg_u32(a.norm_w + k + 8 + 2 * q);
+                    xf[u][0] = norm_pair(xf[u][0], w0, sc0, off);
+                    xf[u][1] = norm_pair(xf[u][1], w0, sc1, off);
+                    xf[u][2] = norm_pair(xf[u][2], w1, sc0, off);
+                    xf[u][3] = norm_pair(xf[u][3], w1, sc1, off);
+                }
+#pragma unroll
+                for (int nt = 0; nt < 4; ++nt)
+                    if (nt < ntv) mma_bf16_16816(acc[nt], xf[u], bf[u][nt][0], bf[u][nt][1]);
             }
         }
+        // the 8 warps' sums, added in warp order
+        if (m0 > 0) __syncthreads();  // red of the previous m-tile consumed
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+            float* rw = red + (size_t)warp * 16 * kShrinkRows + nt * 8 + 2 * q;
+            rw[g * kShrinkRows] = acc[nt][0];
+            rw[g * kShrinkRows + 1] = acc[nt][1];
+            rw[(g + 8) * kShrinkRows] = acc[nt][2];
+            rw[(g + 8) * kShrinkRows + 1] = acc[nt][3];
+        }
+        __syncthreads();
+        for (int i = tid; i < mt * kShrinkRows; i += kShrinkThreads) {
+            const int j = i / kShrinkRows, rr = i - j * kShrinkRows, r = r0 + rr;
+            if (r >= a.T) continue;
+            float v = 0.f;
+#pragma unroll
+            for (int w = 0; w < kShrinkWarps; ++w) v += red[((size_t)w * 16 + j) * kShrinkRows + rr];
+            const int b = list[m0 + j];
+            if (ksplit > 1) {
+                a.ws[((size_t)ksl * a.nb + b) * a.t_stride + r] = v;
+            } else if (a.tp) {
+                // row-parallel under tensor parallelism: fp32 partial to every rank
+                for (int qq = 0; qq < a.tp; ++qq) a.peer_t[qq][(size_t)b * a.t_stride + r] = v;
+            } else {
+                a.t[(size_t)b * a.t_stride + r] = round_bf(v);
+            }
+        }
+    }
+    if (ksplit > 1) {
+        // the last CTA of this (tile, adapter) adds the slices in order
+        __threadfence();
+        __syncthreads();
+        unsigned int* ctr = a.ctr + (size_t)ad * ((a.T + kShrinkRows - 1) / kShrinkRows) + rt;
+        if (tid == 0) s_last = atomicAdd(ctr, 1u) == (unsigned)ksplit - 1;
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+        for (int i = tid; i < n * kShrinkRows; i += kShrinkThreads) {
+            const int j = i / kShrinkRows, rr = i - j * kShrinkRows, r = r0 + rr;
+            if (r >= a.T) continue;
+            const int b = list[j];
+            float v = 0.f;
+            for (int s = 0; s < ksplit; ++s) v += __ldcg(&a.ws[((size_t)s * a.nb + b) * a.t_stride + r]);
+            if (a.tp) {
+                for (int qq = 0; qq < a.tp; ++qq) a.peer_t[qq][(size_t)b * a.t_stride + r] = v;
+            } else {
+                a.t[(size_t)b * a.t_stride + r] = round_bf(v);
+            }
+        }
+        if (tid == 0) *ctr = 0u;
     }
     if (a.tp) __threadfence_system();
 }
 
 cudaError_t lora_shrink_launch(const LoraShrinkArgs& a, cudaStream_t s, bool pdl) {
-    if (a.K % 8 != 0 || a.T <= 0) return cudaErrorInvalidValue;
+    if (a.K % 16 != 0 || a.T <= 0 || a.T % 16 != 0 || a.nb < 1 || a.n_adapters < 1) return cudaErrorInvalidValue;
+    const int tiles = (a.T + kShrinkRows - 1) / kShrinkRows;
+    // K slices: about two CTAs per SM over the (tile, adapter) pairs, slices of
+    // at least 1024 columns, a multiple of 16
+    int sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int ksplit = 1;
+    if (a.ws && a.ctr) {
+        const long pairs = (long)tiles * a.n_adapters;
+        ksplit = (int)std::max<long>(1, (2L * sms + pairs - 1) / pairs);
+        ksplit = std::min(ksplit, std::max(1, a.K / 1024));
+        ksplit = std::min(ksplit, kLoraMaxSplit);
+    }
+    int kr = (a.K + ksplit - 1) / ksplit;
+    kr = (kr + 15) / 16 * 16;
+    ksplit = (a.K + kr - 1) / kr;
     LoraShrinkArgs args = a;
-    void* params[] = {&args};
-    const size_t smem = (size_t)a.K * 2;
+    void* params[] = {&args, &ksplit, &kr};
+    const size_t smem = (size_t)kShrinkWarps * 16 * kShrinkRows * 4 + (size_t)a.nb * 4;
     const void* f = reinterpret_cast<const void*>(&k_lora_shrink);
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    return launch_pdl(f, dim3((a.T + kShrinkRowsPerCta - 1) / kShrinkRowsPerCta, a.nb), dim3(kShrinkThreads), smem, s,
-                      params, pdl);
+    return launch_pdl(f, dim3(tiles, a.n_adapters, ksplit), dim3(kShrinkThreads), smem, s, params, pdl);
 }
 
 

@@ -494,22 +494,35 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
             const bool row_ok = n < a.N;
             const int nchunks = np / 32;
 
-            // the LoRA expansion precomputed by lora_expand_launch, added to a bf16 projection
-            auto lora_dval = [&](int b, int row, float base) {
-                const int ad = a.lora.adapter[b];
-                if (ad < 0 || ad >= a.lora.n_adapters) return base;
-                return round_bf(base +
-                                __uint_as_float((uint32_t)a.lora.dval[(size_t)b * a.lora.dval_stride + row] << 16));
+            // the LoRA expansion precomputed by lora_expand_launch, added to a bf16
+            // projection: per 32-token chunk one ballot of which tokens have an
+            // adapter and this row's 32 values loaded together, ahead of the adds
+            uint32_t lmask = 0;
+            float dv[32];
+            auto lora_load = [&](int c, int row) {
+                const int bb = c * 32 + lane;
+                const int ad = bb < a.nb ? a.lora.adapter[bb] : -1;
+                lmask = __ballot_sync(0xffffffffu, ad >= 0 && ad < a.lora.n_adapters);
+                const uint16_t* dp = a.lora.dval + (size_t)c * 32 * a.lora.dval_stride + row;
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    dv[i] = ((lmask >> i) & 1u) && row_ok
+                                ? __uint_as_float((uint32_t)dp[(size_t)i * a.lora.dval_stride] << 16)
+                                : 0.f;
+            };
+            auto lora_dval = [&](int i, float base) {
+                return ((lmask >> i) & 1u) ? round_bf(base + dv[i]) : base;
             };
             auto apply = [&](int c, const float* v) {
                 // v[i] = accumulator of (row n, token c*32 + i)
+                if (a.lora.adapter) lora_load(c, kGlu && q >= 2 ? a.N + n : n);
                 if (kGlu) {
                     float* xq = xch + (size_t)(q & 1) * 32 * 32;
                     if (q >= 2) {
                         for (int i = 0; i < 32; ++i) {
                             const int b = c * 32 + i;
                             float uv = round_bf(v[i]);
-                            if (a.lora.adapter && b < a.nb && row_ok) uv = lora_dval(b, a.N + n, uv);
+                            if (a.lora.adapter && b < a.nb && row_ok) uv = lora_dval(i, uv);
                             xq[i * 32 + lane] = uv;
                         }
                     }
@@ -519,7 +532,7 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                             const int b = c * 32 + i;
                             if (b >= a.nb) break;
                             float gv = round_bf(v[i]);
-                            if (a.lora.adapter) gv = lora_dval(b, n, gv);
+                            if (a.lora.adapter) gv = lora_dval(i, gv);
                             const float uv = xq[i * 32 + lane];
                             reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + n] = f2bf(tc_act(gv, a.act) * uv);
                         }
@@ -548,7 +561,7 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                             if (b >= a.nb) break;
                             float val = round_bf(v[i]);
                             if (a.bias) val = round_bf(val + bv);
-                            if (a.lora.adapter) val = lora_dval(b, n, val);
+                            if (a.lora.adapter) val = lora_dval(i, val);
                             reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + n] = f2bf(val);
                         }
                     }
@@ -558,7 +571,7 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                             const int b = c * 32 + i;
                             if (b >= a.nb) break;
                             float val = round_bf(v[i]);
-                            if (a.lora.adapter) val = lora_dval(b, n, val);
+                            if (a.lora.adapter) val = lora_dval(i, val);
                             const float rr = __uint_as_float((uint32_t)a.resid[(size_t)b * a.resid_stride + n] << 16);
                             reinterpret_cast<bf16*>(a.out)[(size_t)b * a.out_stride + n] = f2bf(rr + val);
                         }
