@@ -180,6 +180,10 @@ ti_status dalloc(ti_engine* e, void** p, size_t bytes, size_t* acct) {
     return TI_OK;
 }
 
+// LoRA rank as stored: padded to whole mma k-steps (16); padding rows of A and
+// columns of B are zero.  Every buffer sized by the rank uses this.
+inline int lora_padded_rank(int max_rank) { return (max_rank + 15) / 16 * 16; }
+
 template <class T>
 ti_status dalloc_t(ti_engine* e, T** p, size_t count, size_t* acct) {
     return dalloc(e, reinterpret_cast<void**>(p), count * sizeof(T), acct);
@@ -417,7 +421,7 @@ ti_status build(ti_engine* e) {
             e->off_in[1] = take((size_t)tpn * B * H * 4);
             e->off_keys = take((size_t)tpn * B * 8);
             // row-parallel LoRA: every rank's partial x.A^T (o, down), [tp][B][R]
-            const int Rp = e->o.max_adapters > 0 ? (e->o.max_lora_rank + 7) / 8 * 8 : 0;
+            const int Rp = e->o.max_adapters > 0 ? lora_padded_rank(e->o.max_lora_rank) : 0;
             e->off_tin[0] = take((size_t)tpn * B * Rp * 4);
             e->off_tin[1] = take((size_t)tpn * B * Rp * 4);
             for (int k = 0; k < 3; ++k) e->off_flags[k] = take((size_t)tpn * 4);
@@ -471,7 +475,7 @@ ti_status build(ti_engine* e) {
     }
     if (e->o.max_adapters > 0) {
         e->S = e->o.max_adapters;
-        e->R = (e->o.max_lora_rank + 15) / 16 * 16;  // padded to whole mma k-steps (16)
+        e->R = lora_padded_rank(e->o.max_lora_rank);
         e->lmask = e->o.lora_proj_mask;
         const int R = e->R;
         const bool on[4] = {(e->lmask & 7) != 0, (e->lmask & 8) != 0, (e->lmask & 48) != 0, (e->lmask & 64) != 0};

@@ -10,7 +10,9 @@ equal the oracle's up to recorded near-ties.  Skipped on a box with one GPU.
 NVLS is off in the children (a rank that fails an assertion leaves while its
 peer may still be in a collective)."""
 import os
+import queue
 import sys
+import time
 
 import numpy as np
 import pytest
@@ -106,14 +108,23 @@ def _run_tp(kw, prompts, steps, tol, seed=0, std=0.02, world=2, mode="peer", ada
     for p in procs:
         p.start()
     res = {}
+    deadline = time.monotonic() + 300
     try:
-        for _ in range(world):
-            r = q.get(timeout=600)
+        while len(res) < world:
+            try:
+                r = q.get(timeout=5)
+            except queue.Empty:
+                # a rank that died without reporting (exit code < 0: the signal) or ranks
+                # that stall fail the test now instead of holding the GPUs
+                gone = [(i, p.exitcode) for i, p in enumerate(procs) if p.exitcode not in (None, 0)]
+                assert not gone, f"rank process(es) exited without a result: {gone}"
+                assert time.monotonic() < deadline, f"ranks did not report within 300 s (have {sorted(res)})"
+                continue
             assert r[1] != "error", r
             res[r[0]] = r
     finally:
         for p in procs:
-            p.join(timeout=120)
+            p.join(timeout=30)
             if p.is_alive():
                 p.kill()
     ids = [res[r][1] for r in range(world)]
