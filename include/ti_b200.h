@@ -196,6 +196,46 @@ ti_status ti_engine_memory(const ti_engine* e, size_t* weights, size_t* kv, size
  * blocks (row-major, K/32 blocks per row) are accepted as well.  Under tensor
  * parallelism the full tensor is passed and the engine keeps its shard. */
 ti_status ti_engine_load_tensor(ti_engine* e, const char* name, int dtype, const void* host_data, size_t bytes);
+/* ---- GGUF model files: the second weight format the reference plans behind
+ * parser::WeightMap (include/tensor/parser/weight_map.hpp:24, "GGUF support
+ * comes next"; WeightMap::open auto-detects .gguf, :31-33).  ti_gguf_open maps a
+ * GGUF v2/v3 file read-only; its handle lists the tensors (llama.cpp names,
+ * ggml types, ne[0] innermost), typed metadata and the model description, and
+ * ti_engine_load_gguf uploads every model tensor under the reference's name
+ * (q/k rows of llama-architecture files put back in the reference's RoPE
+ * order; gemma norm weights stored as 1 + w put back to w; tensors of the
+ * engine's block type passed as blocks, all others converted to bf16). */
+enum { TI_GGML_F32 = 0, TI_GGML_F16 = 1, TI_GGML_Q4_0 = 2, TI_GGML_Q8_0 = 8, TI_GGML_BF16 = 30 };
+typedef struct ti_gguf ti_gguf;
+ti_status ti_gguf_open(const char* path, ti_gguf** out);
+ti_status ti_gguf_close(ti_gguf* g);
+ti_status ti_gguf_tensor_count(const ti_gguf* g, int* n);
+/* tensor i: name, ggml type, dims (ne[0..3], unused = 1), data in the mapping
+ * and its bytes (0 for ggml types this reader does not decode) */
+ti_status ti_gguf_tensor_info(const ti_gguf* g, int i, const char** name, int* ggml_type, int* n_dims,
+                              int64_t* dims, const void** data, size_t* bytes);
+ti_status ti_gguf_find(const ti_gguf* g, const char* name, int* index);
+/* metadata by key: integers and bools, numbers (integers widen), strings, array lengths */
+ti_status ti_gguf_meta_int(const ti_gguf* g, const char* key, int64_t* v);
+ti_status ti_gguf_meta_float(const ti_gguf* g, const char* key, double* v);
+ti_status ti_gguf_meta_string(const ti_gguf* g, const char* key, const char** v);
+ti_status ti_gguf_meta_array_len(const ti_gguf* g, const char* key, int64_t* n);
+/* architecture llama / qwen2 / gemma from "{arch}.*" metadata (block_count,
+ * embedding_length, feed_forward_length, attention.head_count[_kv],
+ * attention.key_length, attention.layer_norm_rms_epsilon, rope.freq_base);
+ * vocab from token_embd.weight; weight_format from blk.0.attn_q.weight */
+ti_status ti_gguf_model_desc(const ti_gguf* g, ti_model_desc* desc);
+/* the reference's name of tensor i ("model.layers.3.self_attn.q_proj.weight"),
+ * TI_ERR_NOT_FOUND for tensors the models do not read */
+ti_status ti_gguf_reference_name(const ti_gguf* g, int i, char* buf, size_t cap);
+/* tensor i as the engine receives it (rows in the reference's order): dtype
+ * TI_DTYPE_BF16 (any supported ggml type, converted) or TI_DTYPE_Q4_0 / Q8_0
+ * (the tensor's own blocks) */
+ti_status ti_gguf_read(const ti_gguf* g, int i, int dtype, void* out, size_t bytes);
+/* upload every model tensor of the file (tied embeddings: token_embd also as
+ * lm_head.weight); *n_loaded (may be NULL) counts the uploads */
+ti_status ti_engine_load_gguf(ti_engine* e, const ti_gguf* g, int* n_loaded);
+
 /* Fill every weight on the device with the synthetic generator
  * (element i of tensor `name` = f(seed, FNV-1a(name), i) ~ N(0, std)). */
 ti_status ti_engine_init_synthetic(ti_engine* e, uint64_t seed, float std_);

@@ -1095,6 +1095,20 @@ ti_status run_step(ti_engine* e, int B, const int32_t* seq_ids, const int32_t* t
 }  // namespace
 
 // ==================================================================== C ABI
+namespace ti {
+// the destination of a reference-named tensor: storage format and full shape
+ti_status engine_slot_info(ti_engine* e, const char* name, int* wfmt, size_t* rows, size_t* cols) {
+    TI_CHECK(e && name && wfmt && rows && cols, TI_ERR_INVALID, "engine_slot_info: null argument");
+    auto it = e->slot_index.find(name);
+    TI_CHECK(it != e->slot_index.end(), TI_ERR_NOT_FOUND, "unknown tensor '%s'", name);
+    const Slot& s = e->slots[it->second];
+    *wfmt = s.wf == kWQ4 ? TI_WFMT_Q4_0 : s.wf == kWQ8 ? TI_WFMT_Q8_0 : TI_WFMT_BF16;
+    *rows = s.rows;
+    *cols = s.cols;
+    return TI_OK;
+}
+}  // namespace ti
+
 extern "C" {
 
 ti_status ti_engine_create(const ti_model_desc* desc, const ti_engine_opts* opts, ti_engine** out) {

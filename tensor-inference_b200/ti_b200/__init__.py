@@ -21,6 +21,7 @@ DTYPE_F32, DTYPE_BF16, DTYPE_F16, DTYPE_I32 = 0, 1, 2, 3
 DTYPE_Q4_0, DTYPE_Q8_0 = 16, 17
 ARCH_LLAMA, ARCH_QWEN2, ARCH_GEMMA, ARCH_MISTRAL = 0, 1, 2, 3
 WFMT_BF16, WFMT_Q4_0, WFMT_Q8_0 = 0, 1, 2
+GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0, GGML_BF16 = 0, 1, 2, 8, 30
 EW_SILU, EW_GELU, EW_MUL, EW_ADD, EW_MUL_SCALAR = range(5)
 LOGITS_NONE, LOGITS_BF16, LOGITS_F32 = 0, 1, 2
 PROJ_Q, PROJ_K, PROJ_V, PROJ_O, PROJ_GATE, PROJ_UP, PROJ_DOWN = 1, 2, 4, 8, 16, 32, 64
@@ -128,6 +129,21 @@ _SIGS = {
     "ti_adapter_evict": (C.c_int, [C.c_void_p, C.c_int]),
     "ti_adapter_prefetch_async": (C.c_int, [C.c_void_p, C.c_int]),
     "ti_adapter_is_resident": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_int)]),
+    "ti_gguf_open": (C.c_int, [C.c_char_p, C.POINTER(C.c_void_p)]),
+    "ti_gguf_close": (C.c_int, [C.c_void_p]),
+    "ti_gguf_tensor_count": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
+    "ti_gguf_tensor_info": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_int),
+                                      C.POINTER(C.c_int), C.POINTER(C.c_int64), C.POINTER(C.c_void_p),
+                                      C.POINTER(C.c_size_t)]),
+    "ti_gguf_find": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_int)]),
+    "ti_gguf_meta_int": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_int64)]),
+    "ti_gguf_meta_float": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_double)]),
+    "ti_gguf_meta_string": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_char_p)]),
+    "ti_gguf_meta_array_len": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_int64)]),
+    "ti_gguf_model_desc": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "ti_gguf_reference_name": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t]),
+    "ti_gguf_read": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t]),
+    "ti_engine_load_gguf": (C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_int)]),
 }
 
 
@@ -290,6 +306,96 @@ def tp_plan(desc, tp, rank):
 
 
 # ---------------------------------------------------------------- engine
+class Gguf:
+    """A GGUF model file mapped read-only (ti_gguf_*): tensors with llama.cpp
+    names and ggml types, metadata, the model description, and each tensor
+    as the engine receives it (reference row order, bf16 or its own blocks)."""
+
+    def __init__(self, path):
+        h = C.c_void_p()
+        check(lib().ti_gguf_open(os.fsencode(path), C.byref(h)))
+        self.h = h
+
+    def close(self):
+        if self.h:
+            lib().ti_gguf_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __len__(self):
+        n = C.c_int()
+        check(lib().ti_gguf_tensor_count(self.h, C.byref(n)))
+        return n.value
+
+    def info(self, i):
+        name, t, nd = C.c_char_p(), C.c_int(), C.c_int()
+        dims = (C.c_int64 * 4)()
+        data, nbytes = C.c_void_p(), C.c_size_t()
+        check(lib().ti_gguf_tensor_info(self.h, i, C.byref(name), C.byref(t), C.byref(nd), dims, C.byref(data),
+                                        C.byref(nbytes)))
+        return dict(name=name.value.decode(), type=t.value, dims=tuple(dims[:nd.value]), bytes=nbytes.value)
+
+    def find(self, name):
+        i = C.c_int()
+        check(lib().ti_gguf_find(self.h, name.encode(), C.byref(i)))
+        return i.value
+
+    def meta_int(self, key):
+        v = C.c_int64()
+        check(lib().ti_gguf_meta_int(self.h, key.encode(), C.byref(v)))
+        return v.value
+
+    def meta_float(self, key):
+        v = C.c_double()
+        check(lib().ti_gguf_meta_float(self.h, key.encode(), C.byref(v)))
+        return v.value
+
+    def meta_str(self, key):
+        v = C.c_char_p()
+        check(lib().ti_gguf_meta_string(self.h, key.encode(), C.byref(v)))
+        return v.value.decode()
+
+    def meta_array_len(self, key):
+        v = C.c_int64()
+        check(lib().ti_gguf_meta_array_len(self.h, key.encode(), C.byref(v)))
+        return v.value
+
+    def model_desc(self):
+        d = ModelDesc()
+        check(lib().ti_gguf_model_desc(self.h, C.byref(d)))
+        return d
+
+    def reference_name(self, i):
+        buf = C.create_string_buffer(256)
+        check(lib().ti_gguf_reference_name(self.h, i, buf, len(buf)))
+        return buf.value.decode()
+
+    def read(self, i, dtype=DTYPE_BF16):
+        """tensor i in the reference's row order: bf16 bits [rows, cols] (uint16) or
+        its own GGUF blocks (uint8, dtype DTYPE_Q4_0 / DTYPE_Q8_0)"""
+        inf = self.info(i)
+        dims = inf["dims"]
+        cols = dims[0]
+        rows = int(np.prod(dims[1:])) if len(dims) > 1 else 1
+        if dtype == DTYPE_BF16:
+            out = np.empty((rows, cols), np.uint16)
+        else:
+            out = np.empty(inf["bytes"], np.uint8)
+        check(lib().ti_gguf_read(self.h, i, dtype, _ptr(out), out.nbytes))
+        return out
+
+
 class Engine:
     def __init__(self, desc, device=0, max_batch=1, max_seqs=None, max_seq_len=4096, kv_pages=0, max_adapters=0,
                  max_lora_rank=0, lora_proj_mask=0, tp_size=1, tp_rank=0, nccl_id=None):
@@ -335,6 +441,12 @@ class Engine:
         out = np.empty(shape, np.uint16)
         check(lib().ti_engine_read_tensor(self.h, name.encode(), _ptr(out), out.nbytes))
         return out
+
+    def load_gguf(self, g):
+        """upload every model tensor of an open Gguf; returns the number of uploads"""
+        n = C.c_int()
+        check(lib().ti_engine_load_gguf(self.h, g.h, C.byref(n)))
+        return n.value
 
     def memory(self):
         v = [C.c_size_t() for _ in range(4)]
