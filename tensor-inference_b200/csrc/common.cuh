@@ -135,14 +135,18 @@ TI_DEVICE_INLINE void st_release_sys(unsigned int* p, unsigned int v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 // Bounded wait until *p has reached `seq` (wrap-safe); false and err_bit on timeout.
+// Waits on another rank are bounded more loosely than waits inside a kernel:
+// a peer may be seconds behind (building or loading a graph) without being dead.
+constexpr uint64_t kPeerWaitNs = 30000000000ull;  // 30 s
+constexpr uint32_t kPeerSpinLimit = 1u << 31;
 TI_DEVICE_INLINE bool wait_seq_sys(const unsigned int* p, unsigned int seq, int* err, int err_bit) {
     if ((int)(ld_acquire_sys(p) - seq) >= 0) return true;
     // an earlier wait of this step already gave up: do not wait again
     if (err && (*reinterpret_cast<volatile int*>(err) & err_bit)) return false;
     const uint64_t t0 = global_ns();
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    for (uint32_t i = 0; i < kPeerSpinLimit; ++i) {
         if ((int)(ld_acquire_sys(p) - seq) >= 0) return true;
-        if ((i & 63u) == 63u && global_ns() - t0 > kWaitNs) break;
+        if ((i & 63u) == 63u && global_ns() - t0 > kPeerWaitNs) break;
     }
     if (err) atomicOr(err, err_bit);
     return false;

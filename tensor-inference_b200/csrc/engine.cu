@@ -159,6 +159,7 @@ struct ti_engine {
     uint16_t* ldval = nullptr;  // expansions ahead of the tensor-core GEMM [B][rows] bf16
     std::vector<AdapterMeta> adapters;
     cudaStream_t side = nullptr;
+    cudaStream_t tp_sync = nullptr;  // host barrier of the ranks (tensor parallelism)
 
     int32_t* dd_tokens() const { return d_desc + 4; }
     int32_t* dd_seq() const { return d_desc + 4 + o.max_batch; }
@@ -215,6 +216,8 @@ void free_all(ti_engine* e) {
     }
     if (e->side) cudaStreamDestroy(e->side);
     e->side = nullptr;
+    if (e->tp_sync) cudaStreamDestroy(e->tp_sync);
+    e->tp_sync = nullptr;
     if (e->cap) cudaStreamDestroy(e->cap);
     e->cap = nullptr;
 }
@@ -406,6 +409,7 @@ ti_status build(ti_engine* e) {
         const ncclResult_t r = n->CommInitRank(&e->comm, e->tp.tp, id, e->tp.rank);
         TI_CHECK(r == ncclSuccess, TI_ERR_CUDA, "ncclCommInitRank (rank %d of %d): %s", e->tp.rank, e->tp.tp,
                  n->GetErrorString(r));
+        TI_CUDA(cudaStreamCreateWithFlags(&e->tp_sync, cudaStreamNonBlocking));
         const char* ar = std::getenv("TI_TP_ALLREDUCE");
         e->peer_ar = !(ar && std::string(ar) == "nccl") && e->tp.tp <= kMaxTp;
         if (e->peer_ar) {
@@ -963,6 +967,17 @@ ti_status get_graph(ti_engine* e, int B, bool lora, GraphEntry** g) {
         GraphEntry ge;
         if (ti_status st = capture_step(e, B, lora, &ge)) return st;
         it = e->graphs.emplace(key, ge).first;
+        if (e->tp.tp > 1 && e->comm) {
+            // Every rank builds a new graph at the same step; capture, instantiation
+            // and first-launch module loading take seconds on large models, so the
+            // ranks meet on the host before the graph's cross-rank waits begin.
+            const NcclApi* n = nccl_api();
+            // one element of the reduction scratch (rewritten before every use in a step);
+            // a zero-element collective would not synchronise
+            const ncclResult_t r = n->AllReduce(e->red, e->red, 1, ncclFloat32, ncclSum, e->comm, e->tp_sync);
+            TI_CHECK(r == ncclSuccess, TI_ERR_CUDA, "ncclAllReduce (rank barrier): %s", n->GetErrorString(r));
+            TI_CUDA(cudaStreamSynchronize(e->tp_sync));
+        }
     }
     *g = &it->second;
     return TI_OK;

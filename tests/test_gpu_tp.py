@@ -95,6 +95,9 @@ def _rank(rank, world, nid, kw, prompts, feeds, seed, std, q, mode, adapters, pe
         q.put((rank, out_ids, out_logits if rank == 0 else None))
     except BaseException as e:
         q.put((rank, "error", repr(e)))
+        # os._exit skips the queue's feeder thread: flush the message first
+        q.close()
+        q.join_thread()
         os._exit(1)
 
 
