@@ -365,7 +365,8 @@ def measure_pkm(ti, torch, stream, iters=20):
 def run_profile(args):
     """Short, self-contained workload for ncu: a few decode steps (or repeated
     launches of one kernel) of the 8B shape with `--layers` layers after a
-    `--prompt`-token prefill (`--preset` picks another model shape).  Prints
+    `--prompt`-token prefill (`--preset` picks another model shape, `--adapters`
+    adds LoRA adapters on all projections, tokens assigned round-robin).  Prints
     timing only; never a bench number."""
     import numpy as np
     import torch
@@ -377,9 +378,20 @@ def run_profile(args):
     torch.cuda.set_stream(ts)
     desc = ti.model_desc(**dict(ti.PRESETS[args.preset], n_layers=args.layers))
     ctx = args.ctx or args.prompt
+    lora = dict(max_adapters=args.adapters, max_lora_rank=args.lora_rank, lora_proj_mask=0x7F) \
+        if args.adapters else {}
     eng = ti.Engine(desc, device=0, max_batch=args.batch, max_seqs=args.batch,
-                    max_seq_len=ctx + args.warmup + args.steps + 64)
+                    max_seq_len=ctx + args.warmup + args.steps + 64, **lora)
     eng.init_synthetic(0, 0.02)
+    per = None
+    if args.adapters:
+        # the config-5 mix: adapters on all projections, tokens assigned round-robin
+        ads = []
+        for i in range(args.adapters):
+            a = eng.adapter_create(args.lora_rank, float(args.lora_rank), 0x7F)
+            eng.adapter_init_synthetic(a, 100 + i, 0.02, 0.001)
+            ads.append(a)
+        per = [ads[b % len(ads)] for b in range(args.batch)]
     sids = [eng.seq_create() for _ in range(args.batch)]
     if args.ctx:
         # synthetic cached context instead of a prefill (long-context kernels)
@@ -388,17 +400,22 @@ def run_profile(args):
         first = np.random.default_rng(0).integers(0, desc.vocab, size=args.batch, dtype=np.int32)
     else:
         prompts = np.random.default_rng(0).integers(0, desc.vocab, size=(args.batch, args.prompt), dtype=np.int32)
-        first = prefill_lockstep(eng, sids, prompts)
+        first = prefill_lockstep(eng, sids, prompts, per)
     for s in sids:
         eng.seq_reserve(s, ctx + args.warmup + args.steps + 8)
-    eng.bind(sids, first)
+    eng.bind(sids, first, per)
     for _ in range(args.warmup):
         eng.decode_device(ts.cuda_stream)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     if args.kernel is None:
-        for _ in range(args.steps):
+        # NVTX range "step" around the first timed step (ncu --nvtx --nvtx-include "step/")
+        for i in range(args.steps):
+            if i == 0:
+                torch.cuda.nvtx.range_push("step")
             eng.decode_device(ts.cuda_stream)
+            if i == 0:
+                torch.cuda.nvtx.range_pop()
     else:
         # NVTX range so a profiler can select exactly these launches (ncu --nvtx --nvtx-include "kernels/")
         torch.cuda.nvtx.range_push("kernels")
@@ -546,6 +563,8 @@ def main():
     ap.add_argument("--kernel", type=int, default=None, help="profile: launch only this kernel kind")
     ap.add_argument("--ctx", type=int, default=0, help="profile: synthetic cached context of this length")
     ap.add_argument("--preset", default="llama3_8b", help="profile: model shape (ti_b200.PRESETS)")
+    ap.add_argument("--adapters", type=int, default=0, help="profile: LoRA adapters on all projections")
+    ap.add_argument("--lora-rank", type=int, default=64, help="profile: rank of those adapters")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank = int(os.environ.get("RANK", "0"))
