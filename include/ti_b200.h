@@ -335,6 +335,39 @@ ti_status ti_pkm_query(ti_pkm* p, const float* queries, int n, int32_t* addr, in
 /* same with host buffers (copies inside, synchronous) */
 ti_status ti_pkm_query_host(ti_pkm* p, const float* queries, int n, int32_t* addr, int32_t* adapter);
 
+/* ================================================================= router pool + scheduler
+ * Spec only in the reference (README.md:170-180: router/pool keeps a VRAM budget
+ * of resident adapters with LRU eviction and async prefetch of a candidate;
+ * router/scheduler switches adapters only once a semantic shift is decisive).
+ * Per sequence, ti_router_observe takes the adapter the PKM router names for its
+ * latest token (ti_pkm_query; -1 = base model): a new candidate is prefetched
+ * after leading prefetch_after consecutive tokens and becomes the sequence's
+ * adapter after switch_after (its first observation is taken at once).
+ * ti_router_prepare makes a step's adapters resident (async copies the step
+ * waits on), evicting least recently used adapters outside the step past
+ * max_resident (speculative prefetches never evict a live sequence's adapter).
+ * Eviction stages a host copy first (once).  A NULL engine records decisions
+ * only (ti_router_actions: (kind, adapter) pairs, 1 = prefetch, 2 = evict). */
+typedef struct ti_router ti_router;
+typedef struct {
+    int max_resident;    /* adapters resident in HBM at once (>= 1) */
+    int prefetch_after;  /* tokens a candidate leads before its async prefetch (>= 1) */
+    int switch_after;    /* tokens before the sequence switches (>= prefetch_after) */
+} ti_router_opts;
+typedef struct {
+    int64_t observations, switches, prefetches, evictions, hits;
+} ti_router_stats;
+ti_status ti_router_create(ti_engine* e, const ti_router_opts* opts, ti_router** out);
+ti_status ti_router_destroy(ti_router* r);
+ti_status ti_router_observe(ti_router* r, int seq, int candidate, int* use_adapter);
+ti_status ti_router_prepare(ti_router* r, const int32_t* adapters, int n);
+ti_status ti_router_forget(ti_router* r, int seq);
+ti_status ti_router_stats_get(const ti_router* r, ti_router_stats* out);
+/* decisions since the last call (removed from the log); *n pairs written */
+ti_status ti_router_actions(ti_router* r, int32_t* out, int cap, int* n);
+/* adapters the router holds resident, most recently used first; *n = their count */
+ti_status ti_router_resident(const ti_router* r, int32_t* out, int cap, int* n);
+
 #ifdef __cplusplus
 }
 #endif

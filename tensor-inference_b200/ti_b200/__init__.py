@@ -144,6 +144,14 @@ _SIGS = {
     "ti_gguf_reference_name": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t]),
     "ti_gguf_read": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t]),
     "ti_engine_load_gguf": (C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_int)]),
+    "ti_router_create": (C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
+    "ti_router_destroy": (C.c_int, [C.c_void_p]),
+    "ti_router_observe": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_int)]),
+    "ti_router_prepare": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
+    "ti_router_forget": (C.c_int, [C.c_void_p, C.c_int]),
+    "ti_router_stats_get": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "ti_router_actions": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.POINTER(C.c_int)]),
+    "ti_router_resident": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.POINTER(C.c_int)]),
 }
 
 
@@ -306,6 +314,72 @@ def tp_plan(desc, tp, rank):
 
 
 # ---------------------------------------------------------------- engine
+class RouterOpts(C.Structure):
+    _fields_ = [("max_resident", C.c_int), ("prefetch_after", C.c_int), ("switch_after", C.c_int)]
+
+
+class RouterStats(C.Structure):
+    _fields_ = [(n, C.c_int64) for n in ("observations", "switches", "prefetches", "evictions", "hits")]
+
+
+class Router:
+    """Adapter pool + swap scheduler (ti_router_*) over an Engine's adapters;
+    engine=None records the decisions only."""
+    PREFETCH, EVICT = 1, 2
+
+    def __init__(self, engine=None, max_resident=4, prefetch_after=2, switch_after=4):
+        o = RouterOpts(max_resident, prefetch_after, switch_after)
+        h = C.c_void_p()
+        check(lib().ti_router_create(engine.h if engine is not None else None, C.byref(o), C.byref(h)))
+        self.h = h
+        self.engine = engine
+
+    def close(self):
+        if self.h:
+            lib().ti_router_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def observe(self, seq, candidate):
+        u = C.c_int()
+        check(lib().ti_router_observe(self.h, seq, int(candidate), C.byref(u)))
+        return u.value
+
+    def prepare(self, adapters):
+        a = np.ascontiguousarray(adapters, np.int32)
+        check(lib().ti_router_prepare(self.h, _ptr(a), a.size))
+
+    def forget(self, seq):
+        check(lib().ti_router_forget(self.h, seq))
+
+    def stats(self):
+        s = RouterStats()
+        check(lib().ti_router_stats_get(self.h, C.byref(s)))
+        return {n: getattr(s, n) for n, _ in RouterStats._fields_}
+
+    def actions(self):
+        out = np.empty(2 * 256, np.int32)
+        n = C.c_int()
+        res = []
+        while True:
+            check(lib().ti_router_actions(self.h, _ptr(out), 256, C.byref(n)))
+            res += [(int(out[2 * i]), int(out[2 * i + 1])) for i in range(n.value)]
+            if n.value < 256:
+                return res
+
+    def resident(self):
+        n = C.c_int()
+        check(lib().ti_router_resident(self.h, None, 0, C.byref(n)))
+        out = np.empty(max(1, n.value), np.int32)
+        check(lib().ti_router_resident(self.h, _ptr(out), out.size, C.byref(n)))
+        return [int(x) for x in out[:n.value]]
+
+
 class Gguf:
     """A GGUF model file mapped read-only (ti_gguf_*): tensors with llama.cpp
     names and ggml types, metadata, the model description, and each tensor
