@@ -104,13 +104,6 @@ TI_DEVICE_INLINE void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint6
         "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
         : "memory");
 }
-TI_DEVICE_INLINE void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
 TI_DEVICE_INLINE void prefetch_l2_bulk(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
@@ -160,13 +153,6 @@ TI_DEVICE_INLINE uint4 lds128(const void* p) {
                  : "r"(smem_u32(p)));
     return v;
 }
-TI_DEVICE_INLINE uint4 ldg128_nc(const void* p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
 
 // named barrier among `count` threads (multiple of 32)
 TI_DEVICE_INLINE void named_bar(int id, int count) {
@@ -193,13 +179,6 @@ TI_DEVICE_INLINE float2 ffma2(float2 a, float2 b, float2 c) {
     unsigned long long cv = *reinterpret_cast<unsigned long long*>(&c);
     asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(cv) : "l"(av), "l"(bv));
     return *reinterpret_cast<float2*>(&cv);
-}
-TI_DEVICE_INLINE float2 fmul2(float2 a, float2 b) {
-    unsigned long long av = *reinterpret_cast<unsigned long long*>(&a);
-    unsigned long long bv = *reinterpret_cast<unsigned long long*>(&b);
-    unsigned long long dv;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(dv) : "l"(av), "l"(bv));
-    return *reinterpret_cast<float2*>(&dv);
 }
 TI_DEVICE_INLINE float2 bf2_to_f2(uint32_t u) { return make_float2(bf_lo(u), bf_hi(u)); }
 // 8 bf16 weights x 8 fp32 activations (pairs); even and odd elements accumulate
