@@ -1,4 +1,4 @@
-"""Benchmark: Llama-3-8B-shape bf16 greedy decode on B200.
+"""Benchmark: Llama-3-8B-shape bf16 greedy decode on B200 (benchmark configuration 2).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B] [--no-b32]
 
@@ -221,7 +221,7 @@ def measure_batch(ti, torch, eng, B, steps, warmup, stream, peak, measure_e2e=Tr
 
 
 def measure_qwen_lora(ti, torch, stream, peak, wf, steps, warmup, dev=0):
-    """Qwen2.5-7B shape, rank-16 LoRA on q/k/v/o (A ~ N(0, 0.02),
+    """Benchmark configuration 3: Qwen2.5-7B shape, rank-16 LoRA on q/k/v/o (A ~ N(0, 0.02),
     B ~ N(0, 0.001), alpha 32), batch 8, 256-token prompts; weights bf16 or GGUF Q4_0"""
     B, P, R = 8, 256, 16
     desc = ti.model_desc(**dict(ti.PRESETS["qwen25_7b"], weight_format=wf))
@@ -244,7 +244,7 @@ def measure_qwen_lora(ti, torch, stream, peak, wf, steps, warmup, dev=0):
 
 
 def measure_70b_tp(ti, torch, stream, peak, world, rank, dev, steps, warmup=3):
-    """Llama-3-70B shape, tensor-parallel over the job's GPUs,
+    """Benchmark configuration 5: Llama-3-70B shape, tensor-parallel over the job's GPUs,
     batch 64 at 4096 tokens of context (cached K/V filled with seeded synthetic
     values instead of a 4096-step prefill), 16 rank-64 LoRA adapters (alpha = rank,
     scale 1) on all seven projections, assigned to sequences round-robin"""
@@ -332,7 +332,7 @@ def kernel_roofline(ti, torch, eng, stream, peak, iters=64):
 
 
 def measure_pkm(ti, torch, stream, iters=20):
-    """65,536 queries of 512 fp32 against two 512 x 256 codebooks,
+    """Benchmark configuration 4: 65,536 queries of 512 fp32 against two 512 x 256 codebooks,
     4,096 registered adapters; queries resident on the device"""
     import numpy as np
 
@@ -356,7 +356,7 @@ def measure_pkm(ti, torch, stream, iters=20):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / iters
     p.close()
-    gemm_flop = 2.0 * 65536 * 2 * 512 * 256  # the GEMM-equivalent count BASELINE quotes (34.4 GFLOP)
+    gemm_flop = 2.0 * 65536 * 2 * 512 * 256  # the GEMM-equivalent count the benchmark quotes (34.4 GFLOP)
     instr = 2.0 * 65536 * 2 * 512 * 256      # one sub + one fma per (query, code, dim)
     return {"queries": 65536, "ms": round(ms, 4), "queries_per_s": round(65536 / (ms * 1e-3), 1),
             "gemm_equiv_tflops": round(gemm_flop / (ms * 1e-3) / 1e12, 2), "fp32_instr_per_s": instr / (ms * 1e-3)}

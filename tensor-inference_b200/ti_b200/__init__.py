@@ -195,7 +195,7 @@ def _ptr(a):
 
 # ---------------------------------------------------------------- model configs
 PRESETS = {
-    # BASELINE configs (shapes only; weights are synthetic)
+    # the benchmark configurations (shapes only; weights are synthetic)
     "tinyllama": dict(arch=ARCH_LLAMA, hidden=2048, n_layers=22, n_heads=32, n_kv_heads=4, head_dim=64,
                       intermediate=5632, vocab=32000, rms_eps=1e-5, rope_theta=10000.0),
     "llama3_8b": dict(arch=ARCH_LLAMA, hidden=4096, n_layers=32, n_heads=32, n_kv_heads=8, head_dim=128,

@@ -7,7 +7,7 @@ import numpy as np
 import ti_b200 as ti
 from oracle import bf16_to_f32
 
-# BASELINE tolerance for bf16 logits: max|y - y_ref| / max|y_ref| <= 2e-2
+# the benchmark tolerance for bf16 logits: max|y - y_ref| / max|y_ref| <= 2e-2
 LOGIT_TOL = 2e-2
 
 

@@ -3,7 +3,7 @@
 The fixtures hold the last-row logits the reference's unchanged CUDA model code
 produced on a B200 for seeded synthetic checkpoints (tests/golden/make_golden.py).
 Here the CPU oracle re-derives the same checkpoint, prompt and fed tokens and
-must match: BASELINE tolerance 2e-2 max-abs relative on logits, and the same
+must match: the benchmark tolerance 2e-2 max-abs relative on logits, and the same
 greedy id wherever the reference's top-2 margin exceeds the logit error.
 """
 import glob

@@ -3,7 +3,7 @@ QwenAdapter/Gemma/Mistral models, adapter loader — compiled from its sources
 against this repo's tensor::backend headers) runs on libti_b200 through the
 tensor::backend shim (tensor-inference_b200/backend), and its logits match the
 reference's own CUDA backend on the same checkpoints (tests/golden/*.npz):
-2e-2 max-abs relative, the BASELINE tolerance."""
+2e-2 max-abs relative, the benchmark tolerance."""
 import ctypes as C
 import glob
 import json

@@ -1,5 +1,5 @@
 """PKM router on the GPU against the oracle: addresses and adapter ids must be
-bit-exact (BASELINE: "Results must match the CPU reference bit-exactly")."""
+bit-exact (the benchmark requires results that match the CPU reference bit-exactly)."""
 import numpy as np
 import pytest
 
@@ -28,7 +28,7 @@ def _oracle_table(c1, c2, cents, ids):
 
 @pytest.mark.parametrize("n_queries", [8192, 65536])
 def test_pkm_bench_shape_bit_exact(n_queries):
-    # two 512 x 256 fp32 codebooks ~ N(0,1), 4096 adapter centroids
+    # benchmark configuration 4: two 512 x 256 fp32 codebooks ~ N(0,1), 4096 adapter centroids
     c1 = oracle.fill_f32("pkm.c1", (512, 256), 0, 1.0)
     c2 = oracle.fill_f32("pkm.c2", (512, 256), 0, 1.0)
     cents = oracle.fill_f32("pkm.centroids", (4096, 512), 0, 1.0)
