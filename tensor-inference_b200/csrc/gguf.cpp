@@ -377,6 +377,8 @@ ti_status ti_gguf_open(const char* path, ti_gguf** out) {
     if (const ti_gguf::Meta* a = find_meta(g, "general.alignment")) align = a->i;
     if (align <= 0 || (align & (align - 1)) != 0) return bad("general.alignment is not a power of two");
     const size_t data0 = ((size_t)(r.p - g->base) + (size_t)align - 1) / (size_t)align * (size_t)align;
+    if (data0 > g->size) return bad("tensor data section beyond the end of the file");
+    const size_t data_bytes = g->size - data0;
     for (size_t i = 0; i < g->tensors.size(); ++i) {
         ti_gguf::Tensor& t = g->tensors[i];
         int64_t n = 1;
@@ -385,9 +387,10 @@ ti_status ti_gguf_open(const char* path, ti_gguf** out) {
             n *= t.ne[d];
         }
         t.bytes = type_bytes(t.type, n);  // 0 for block types this reader does not decode
-        if (t.bytes && (data0 + t.offset > g->size || t.bytes > g->size - data0 - t.offset))
+        // offsets come from the file: compare without forming data0 + offset (no wrap)
+        if (t.bytes && (t.offset > data_bytes || t.bytes > data_bytes - t.offset))
             return bad("tensor data beyond the end of the file");
-        t.data = g->base + data0 + t.offset;
+        t.data = t.bytes ? g->base + data0 + t.offset : nullptr;
         g->by_name[t.name] = (int)i;
     }
     if (const ti_gguf::Meta* a = find_meta(g, "general.architecture")) g->arch = a->s;

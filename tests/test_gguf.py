@@ -198,6 +198,16 @@ def test_rejects_bad_files(tmp_path):
         with pytest.raises(ti.TiError) as ei:
             ti.Gguf(p)
         assert ei.value.status == ti.TI_ERR_INVALID
+    # a tensor offset near 2^64 must not wrap past the bounds check
+    write(p, _llama_meta(), [("token_embd.weight", GGML_F32, (64, 2), bytes(512))])
+    blob = bytearray(open(p, "rb").read())
+    name = b"token_embd.weight"
+    at = blob.index(name) + len(name) + 4 + 16 + 4  # n_dims u32, ne u64 x 2, type u32 -> offset u64
+    blob[at:at + 8] = (2**64 - 64).to_bytes(8, "little")
+    open(p, "wb").write(bytes(blob))
+    with pytest.raises(ti.TiError) as ei:
+        ti.Gguf(p)
+    assert ei.value.status == ti.TI_ERR_INVALID
     write(p, _llama_meta("falcon"), [("token_embd.weight", GGML_F32, (64, 2), bytes(512))])
     with ti.Gguf(p) as g:
         with pytest.raises(ti.TiError) as ei:
