@@ -235,6 +235,13 @@ ti_status ti_gguf_read(const ti_gguf* g, int i, int dtype, void* out, size_t byt
 /* upload every model tensor of the file (tied embeddings: token_embd also as
  * lm_head.weight); *n_loaded (may be NULL) counts the uploads */
 ti_status ti_engine_load_gguf(ti_engine* e, const ti_gguf* g, int* n_loaded);
+/* the RoPE inverse frequencies of the file: theta^(-2i/head_dim) from
+ * "{arch}.rope.freq_base", divided by the per-dimension factors of
+ * rope_freqs.weight when the file has them (ti_engine_load_gguf applies them) */
+ti_status ti_gguf_rope_inv_freq(const ti_gguf* g, float* out, int n);
+/* replace the engine's RoPE inverse-frequency table (head_dim / 2 values; the
+ * reference computes it from rope_theta and llama3 scaling, ops.cu:235-278) */
+ti_status ti_engine_set_rope_freqs(ti_engine* e, const float* inv_freq, int n);
 
 /* Fill every weight on the device with the synthetic generator
  * (element i of tensor `name` = f(seed, FNV-1a(name), i) ~ N(0, std)). */

@@ -1222,6 +1222,16 @@ ti_status ti_engine_load_tensor(ti_engine* e, const char* name, int dtype, const
     return TI_OK;
 }
 
+ti_status ti_engine_set_rope_freqs(ti_engine* e, const float* inv_freq, int n) {
+    clear_error();
+    TI_CHECK(e && inv_freq, TI_ERR_INVALID, "ti_engine_set_rope_freqs: null argument");
+    TI_CHECK(n == e->hd / 2, TI_ERR_INVALID, "ti_engine_set_rope_freqs: %d values, head_dim / 2 = %d expected", n,
+             e->hd / 2);
+    DeviceGuard g(e->dev);
+    TI_CUDA(cudaMemcpy(e->freqs, inv_freq, (size_t)n * 4, cudaMemcpyHostToDevice));
+    return TI_OK;
+}
+
 ti_status ti_engine_read_tensor(ti_engine* e, const char* name, void* host, size_t bytes) {
     clear_error();
     TI_CHECK(e && name && host, TI_ERR_INVALID, "ti_engine_read_tensor: null argument");

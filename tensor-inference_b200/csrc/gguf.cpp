@@ -21,6 +21,8 @@
 //     (j, j + hd/2) (ops.cu:224-232), so the rows are put back.
 //   * gemma files store RMSNorm weights as (1 + w); this engine applies the
 //     reference's (1 + w) itself (rms_norm_offset), so 1 is subtracted.
+// Per-dimension RoPE factors (rope_freqs.weight) divide the base frequencies
+// theta^(-2i/d) and replace the engine's RoPE table.
 // Tensors of the engine's block type (Q4_0 / Q8_0 linear weights of a
 // quantised engine) pass through as blocks; every other tensor is converted to
 // bf16 on the host (f32, f16, bf16, and Q4_0 / Q8_0 dequantised to d * q).
@@ -479,8 +481,6 @@ ti_status ti_gguf_model_desc(const ti_gguf* g, ti_model_desc* d) {
     else if (a == "qwen2") d->arch = TI_ARCH_QWEN2;
     else if (a == "gemma") d->arch = TI_ARCH_GEMMA;
     else return fail(TI_ERR_UNSUPPORTED, "GGUF architecture '%s' (llama, qwen2 or gemma supported)", a.c_str());
-    TI_CHECK(g->by_name.count("rope_freqs.weight") == 0, TI_ERR_UNSUPPORTED,
-             "GGUF file carries per-dimension RoPE factors (rope_freqs.weight): not supported");
     int64_t v = 0;
     auto need = [&](const char* k, int* dst) -> ti_status {
         TI_CHECK(meta_int(g, a + "." + k, &v), TI_ERR_INVALID, "GGUF metadata '%s.%s' missing", a.c_str(), k);
@@ -508,6 +508,28 @@ ti_status ti_gguf_model_desc(const ti_gguf* g, ti_model_desc* d) {
         const int t = g->tensors[q->second].type;
         if (t == TI_GGML_Q4_0) d->weight_format = TI_WFMT_Q4_0;
         else if (t == TI_GGML_Q8_0) d->weight_format = TI_WFMT_Q8_0;
+    }
+    return TI_OK;
+}
+
+ti_status ti_gguf_rope_inv_freq(const ti_gguf* g, float* out, int n) {
+    ti::clear_error();
+    TI_CHECK(g && out && n > 0, TI_ERR_INVALID, "ti_gguf_rope_inv_freq: null argument");
+    const std::string& a = g->arch;
+    double theta = 10000.0;
+    meta_float(g, a + ".rope.freq_base", &theta);
+    ti::rope_freqs(2 * n, (float)theta, nullptr, out);
+    auto it = g->by_name.find("rope_freqs.weight");
+    if (it == g->by_name.end()) return TI_OK;
+    // llama.cpp's per-dimension factors: angle = pos * base_i / factor_i
+    const ti_gguf::Tensor& t = g->tensors[it->second];
+    TI_CHECK(t.bytes > 0 && t.n_dims == 1 && t.ne[0] == n, TI_ERR_INVALID,
+             "rope_freqs.weight has %lld values, head_dim / 2 = %d expected", (long long)t.ne[0], n);
+    std::vector<float> f((size_t)n);
+    row_to_float(t.type, t.data, n, f.data());
+    for (int i = 0; i < n; ++i) {
+        TI_CHECK(f[i] > 0.f, TI_ERR_INVALID, "rope_freqs.weight[%d] = %g (positive factors expected)", i, f[i]);
+        out[i] /= f[i];
     }
     return TI_OK;
 }
@@ -596,6 +618,14 @@ ti_status ti_engine_load_gguf(ti_engine* e, const ti_gguf* g, int* n_loaded) {
         auto it = g->by_name.find("token_embd.weight");
         TI_CHECK(it != g->by_name.end(), TI_ERR_INVALID, "GGUF file has neither output.weight nor token_embd.weight");
         if (ti_status st = load_as(it->second, "lm_head.weight")) return st;
+    }
+    if (g->by_name.count("rope_freqs.weight")) {
+        // per-dimension RoPE factors (llama 3.1 style files) replace the engine's table
+        const auto it = g->by_name.find("rope_freqs.weight");
+        const int n = (int)g->tensors[it->second].ne[0];
+        std::vector<float> inv((size_t)n);
+        if (ti_status st = ti_gguf_rope_inv_freq(g, inv.data(), n)) return st;
+        if (ti_status st = ti_engine_set_rope_freqs(e, inv.data(), n)) return st;
     }
     if (n_loaded) *n_loaded = loaded;
     return TI_OK;

@@ -144,6 +144,8 @@ _SIGS = {
     "ti_gguf_reference_name": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t]),
     "ti_gguf_read": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t]),
     "ti_engine_load_gguf": (C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_int)]),
+    "ti_gguf_rope_inv_freq": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
+    "ti_engine_set_rope_freqs": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
     "ti_router_create": (C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
     "ti_router_destroy": (C.c_int, [C.c_void_p]),
     "ti_router_observe": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_int)]),
@@ -450,6 +452,11 @@ class Gguf:
         check(lib().ti_gguf_model_desc(self.h, C.byref(d)))
         return d
 
+    def rope_inv_freq(self, n):
+        out = np.empty(n, np.float32)
+        check(lib().ti_gguf_rope_inv_freq(self.h, _ptr(out), n))
+        return out
+
     def reference_name(self, i):
         buf = C.create_string_buffer(256)
         check(lib().ti_gguf_reference_name(self.h, i, buf, len(buf)))
@@ -515,6 +522,10 @@ class Engine:
         out = np.empty(shape, np.uint16)
         check(lib().ti_engine_read_tensor(self.h, name.encode(), _ptr(out), out.nbytes))
         return out
+
+    def set_rope_freqs(self, inv_freq):
+        a = np.ascontiguousarray(inv_freq, np.float32)
+        check(lib().ti_engine_set_rope_freqs(self.h, _ptr(a), a.size))
 
     def load_gguf(self, g):
         """upload every model tensor of an open Gguf; returns the number of uploads"""

@@ -214,8 +214,30 @@ def test_rejects_bad_files(tmp_path):
             g.model_desc()
         assert ei.value.status == ti.TI_ERR_UNSUPPORTED
     write(p, _llama_meta(), [("token_embd.weight", GGML_F32, (64, 2), bytes(512)),
-                             ("rope_freqs.weight", GGML_F32, (8,), bytes(32))])
+                             ("rope_freqs.weight", GGML_F32, (8,), bytes(32))])  # zero factors
     with ti.Gguf(p) as g:
         with pytest.raises(ti.TiError) as ei:
-            g.model_desc()
-        assert ei.value.status == ti.TI_ERR_UNSUPPORTED
+            g.rope_inv_freq(8)
+        assert ei.value.status == ti.TI_ERR_INVALID
+
+
+def _rope_table(hd, theta):
+    out = np.empty(hd // 2, np.float32)
+    oracle.lib().orc_rope_freqs(hd, theta, None, oracle.ptr(out))
+    return out
+
+
+def test_rope_factors(tmp_path):
+    hd = 16
+    p = tmp_path / "m.gguf"
+    write(p, _llama_meta(), [("token_embd.weight", GGML_F32, (64, 2), bytes(512))])
+    with ti.Gguf(p) as g:
+        np.testing.assert_array_equal(g.rope_inv_freq(hd // 2), _rope_table(hd, 500000.0))
+    factors = np.linspace(1.0, 8.0, hd // 2).astype(np.float32)  # per-dimension, as llama 3.1 files carry
+    write(p, _llama_meta(), [("token_embd.weight", GGML_F32, (64, 2), bytes(512)),
+                             ("rope_freqs.weight", GGML_F32, (hd // 2,), factors.tobytes())])
+    with ti.Gguf(p) as g:
+        np.testing.assert_array_equal(g.rope_inv_freq(hd // 2), _rope_table(hd, 500000.0) / factors)
+        with pytest.raises(ti.TiError) as ei:
+            g.rope_inv_freq(hd)  # the factor table fixes head_dim
+        assert ei.value.status == ti.TI_ERR_INVALID

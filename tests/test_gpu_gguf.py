@@ -42,7 +42,7 @@ def _is_linear(name):
     return name.startswith("model.layers.") and name.endswith("_proj.weight")
 
 
-def _export(eng, kw, path, wfmt, tied):
+def _export(eng, kw, path, wfmt, tied, extra=()):
     arch = ARCH_NAME[kw["arch"]]
     tensors = []
     for name, shape in _shapes(kw).items():
@@ -76,7 +76,7 @@ def _export(eng, kw, path, wfmt, tied):
             (f"{arch}.attention.layer_norm_rms_epsilon", F32, kw["rms_eps"]),
             (f"{arch}.rope.freq_base", F32, kw["rope_theta"]),
             ("tokenizer.ggml.tokens", ARR, (STR, [f"t{i}" for i in range(4)]))]
-    write(path, meta, tensors)
+    write(path, meta, tensors + list(extra))
 
 
 @pytest.mark.parametrize("arch,wfmt,tied", [(ti.ARCH_LLAMA, ti.WFMT_BF16, False), (ti.ARCH_LLAMA, ti.WFMT_Q4_0, False),
@@ -117,5 +117,52 @@ def test_gguf_roundtrip_bit_identical(tmp_path, arch, wfmt, tied):
     assert outs[0][0] == outs[1][0]
     np.testing.assert_array_equal(outs[0][1], outs[1][1])
     np.testing.assert_array_equal(outs[0][2], outs[1][2])
+    a.close()
+    b.close()
+
+
+def _rope_table(hd, theta, scaling=None):
+    out = np.empty(hd // 2, np.float32)
+    rs = None
+    if scaling:
+        rs = oracle.RopeScaling(1, scaling["factor"], scaling["low_freq_factor"], scaling["high_freq_factor"],
+                                scaling["original_max_pos"])
+    oracle.lib().orc_rope_freqs(hd, theta, ctypes_ref(rs), oracle.ptr(out))
+    return out
+
+
+def ctypes_ref(x):
+    return C.byref(x) if x is not None else None
+
+
+def test_gguf_rope_factors_reproduce_llama3_scaling(tmp_path):
+    # llama 3.1 style files carry per-dimension RoPE factors instead of scaling metadata
+    sc = dict(factor=8.0, low_freq_factor=1.0, high_freq_factor=4.0, original_max_pos=64)
+    kw = dict(SMALL, rope_theta=500000.0, rope_scaling=sc, weight_format=ti.WFMT_BF16)
+    a = ti.Engine(ti.model_desc(**kw), device=0, max_batch=1, max_seqs=1, max_seq_len=64)
+    a.init_synthetic(13, 0.05)
+    hd = kw["head_dim"]
+    factors = (_rope_table(hd, kw["rope_theta"]) / _rope_table(hd, kw["rope_theta"], sc)).astype(np.float32)
+    assert factors.max() > 1.5  # the scaling reaches these dimensions
+    path = tmp_path / "scaled.gguf"
+    _export(a, kw, path, ti.WFMT_BF16, False, [("rope_freqs.weight", GGML_F32, (hd // 2,), factors.tobytes())])
+    with ti.Gguf(path) as g:
+        b = ti.Engine(g.model_desc(), device=0, max_batch=1, max_seqs=1, max_seq_len=64)
+        b.load_gguf(g)
+    prompt = oracle.fill_ids("rs", 9, 4, kw["vocab"])
+    res = []
+    for eng in (a, b):
+        s = eng.seq_create()
+        nxt, lb = eng.prefill(s, prompt, logits=ti.LOGITS_BF16)
+        ids = [int(nxt)]
+        for _ in range(3):
+            nxt, l2 = eng.decode([s], [ids[-1]], logits=ti.LOGITS_BF16)
+            ids.append(int(nxt[0]))
+        res.append((ids, oracle.bf16_to_f32(lb), oracle.bf16_to_f32(l2[0])))
+        eng.check()
+    assert res[0][0] == res[1][0]
+    for k in (1, 2):
+        err = float(np.abs(res[0][k] - res[1][k]).max() / np.abs(res[0][k]).max())
+        assert err <= 1e-2, err  # base / factor equals the scaled table to about one ulp
     a.close()
     b.close()
