@@ -274,6 +274,14 @@ enum { TI_LOGITS_NONE = 0, TI_LOGITS_BF16 = 1, TI_LOGITS_F32 = 2 };
 ti_status ti_engine_prefill(ti_engine* e, int seq_id, const int32_t* ids, int n, int adapter_id,
                             int32_t* next_id, int logits_mode, void* logits_out);
 
+/* Prefill in steps of up to `chunk` tokens (<= max_batch): each step decodes
+ * tokens len .. len + m - 1 of the sequence together (the tcgen05 path for 8+
+ * tokens; every K/V row of the step is written to its page before attention,
+ * each token attends causally up to its own position).  next_id / logits: the
+ * last prompt token's.  No counterpart in the reference, whose prefill is one
+ * forward over the prompt with a host-built causal mask (ops.cu:500-520). */
+ti_status ti_engine_prefill_chunked(ti_engine* e, int seq_id, const int32_t* ids, int n, int adapter_id, int chunk,
+                                    int32_t* next_id, int logits_mode, void* logits_out);
 /* One decode step for `batch` sequences (Model::forward with one token each,
  * generator.cpp:78; Greedy::sample, greedy.cpp:11-36, becomes a device argmax).
  * Host pointers: tokens[batch], seq_ids[batch], adapter_ids[batch] (NULL = no

@@ -221,7 +221,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     //      written by the step's first kernel), so a stage holding it waits.
     const int n_pre = min(NS, n_st);
     const int last_page = pos / kPage - pg0;  // split page index of pos (may be out of range)
-    auto early = [&](int st) { return st * CP + min(CP, npg - st * CP) - 1 < last_page; };
+    // (prefill: pages written by this step's kv_append hold rows of earlier entries)
+    auto early = [&](int st) { return !a.prefill && st * CP + min(CP, npg - st * CP) - 1 < last_page; };
     if (tid == 0) {
         for (int s = 0; s < NS; ++s) mbar_init(&full[s], 1);
         fence_barrier_init();
@@ -584,6 +585,44 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         dst[3] = f2bf(O.w / inv);
     }
     if (tid == 0) a.counters[b * a.nkv + h] = 0u;
+}
+
+// K (RoPE, ops.cu:224-232, the same arithmetic as the attention kernel's) and V
+// rows of every entry into its page: one CTA per entry
+__global__ void __launch_bounds__(128) k_kv_append(const AttnArgs a) {
+    if (threadIdx.x == 0) pdl_trigger();
+    pdl_wait();  // q/k/v are the previous kernel's output
+    const int b = blockIdx.x, hd = a.hd, half = hd / 2;
+    const int pos = a.pos[b];
+    const int page = a.page_table[(size_t)a.seq[b] * a.pt_stride + pos / kPage];
+    if (page < 0 || page >= a.n_pages) {
+        if (threadIdx.x == 0 && a.err) atomicOr(a.err, kErrBadIndex);
+        return;
+    }
+    const uint16_t* row = a.qkv + (size_t)b * a.qkv_stride;
+    for (int task = threadIdx.x; task < a.nkv * half; task += blockDim.x) {
+        const int h = task / half, i = task - h * half;
+        const uint16_t* src = row + (size_t)(a.nq + h) * hd;
+        const float x0 = __uint_as_float((uint32_t)src[i] << 16);
+        const float x1 = __uint_as_float((uint32_t)src[i + half] << 16);
+        const float ang = (float)pos * a.freqs[i];
+        const float c = cosf(ang), sn = sinf(ang);
+        const size_t off = (((size_t)page * a.nkv + h) * kPage + (pos % kPage)) * hd;
+        reinterpret_cast<bf16*>(a.kc)[off + i] = f2bf(round_bf(x0 * c - x1 * sn));
+        reinterpret_cast<bf16*>(a.kc)[off + i + half] = f2bf(round_bf(x0 * sn + x1 * c));
+    }
+    for (int task = threadIdx.x; task < a.nkv * hd; task += blockDim.x) {
+        const int h = task / hd, d = task - h * hd;
+        const size_t off = (((size_t)page * a.nkv + h) * kPage + (pos % kPage)) * hd;
+        a.vc[off + d] = row[(size_t)(a.nq + a.nkv + h) * hd + d];
+    }
+}
+
+cudaError_t kv_append_launch(const AttnArgs& a, cudaStream_t s, bool pdl) {
+    if (a.nkv <= 0 || a.hd % 2 != 0 || a.nb < 1) return cudaErrorInvalidValue;
+    AttnArgs args = a;
+    void* params[] = {&args};
+    return launch_pdl(reinterpret_cast<const void*>(&k_kv_append), dim3(a.nb), dim3(128), 0, s, params, pdl);
 }
 
 int attn_splits(int nb, int nkv, int hd, int max_len, int sms, int* max_chunk) {

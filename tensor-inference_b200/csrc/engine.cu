@@ -539,7 +539,8 @@ ti_status build(ti_engine* e) {
 enum KernelKind { kKEmbed = 0, kKQkv = 1, kKAttn = 2, kKO = 3, kKGateUp = 4, kKDown = 5, kKLmHead = 6 };
 
 // Enqueue one kernel of a B-token step on `s` (graph capture or a plain launch).
-ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, int* launches, bool lora) {
+ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, int* launches, bool lora,
+                         bool prefill = false) {
     const ti_model_desc& d = e->d;
     const int H = e->H, I = e->I, nq = e->nq, nkv = e->nkv, hd = e->hd;
     const int QW = nq * hd;
@@ -845,6 +846,14 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             at.out = e->attn;
             at.out_stride = QW;
             at.err = e->err;
+            if (prefill) {
+                // entries are one sequence at consecutive positions: every K/V row of
+                // the step goes into its page first, attention then loads pages after
+                // its dependency wait
+                TI_CUDA(kv_append_launch(at, s, true));
+                if (launches) ++*launches;
+                at.prefill = 1;
+            }
             TI_CUDA(attn_launch(at, s, true));
             if (launches) ++*launches;
             return TI_OK;
@@ -928,19 +937,19 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
     }
 }
 
-ti_status enqueue_step(ti_engine* e, int B, cudaStream_t s, int* launches, bool lora) {
+ti_status enqueue_step(ti_engine* e, int B, cudaStream_t s, int* launches, bool lora, bool prefill) {
     if (ti_status st = enqueue_kernel(e, B, kKEmbed, 0, s, launches, lora)) return st;
     for (int li = 0; li < e->d.n_layers; ++li)
         for (int k : {kKQkv, kKAttn, kKO, kKGateUp, kKDown})
-            if (ti_status st = enqueue_kernel(e, B, k, li, s, launches, lora)) return st;
+            if (ti_status st = enqueue_kernel(e, B, k, li, s, launches, lora, prefill)) return st;
     return enqueue_kernel(e, B, kKLmHead, 0, s, launches, lora);
 }
 
-ti_status capture_step(ti_engine* e, int B, bool lora, GraphEntry* out) {
+ti_status capture_step(ti_engine* e, int B, bool lora, bool prefill, GraphEntry* out) {
     cudaStream_t s = e->cap;
     int launches = 0;
     TI_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-    ti_status st = enqueue_step(e, B, s, &launches, lora);
+    ti_status st = enqueue_step(e, B, s, &launches, lora, prefill);
     cudaGraph_t graph = nullptr;
     cudaError_t ce = cudaStreamEndCapture(s, &graph);
     if (st) {
@@ -958,14 +967,14 @@ ti_status capture_step(ti_engine* e, int B, bool lora, GraphEntry* out) {
     return TI_OK;
 }
 
-// one graph per (batch size, LoRA on/off)
-ti_status get_graph(ti_engine* e, int B, bool lora, GraphEntry** g) {
+// one graph per (batch size, LoRA on/off, prefill)
+ti_status get_graph(ti_engine* e, int B, bool lora, GraphEntry** g, bool prefill = false) {
     lora = lora && e->S > 0;
-    const int key = B * 2 + (lora ? 1 : 0);
+    const int key = (B * 2 + (lora ? 1 : 0)) * 2 + (prefill ? 1 : 0);
     auto it = e->graphs.find(key);
     if (it == e->graphs.end()) {
         GraphEntry ge;
-        if (ti_status st = capture_step(e, B, lora, &ge)) return st;
+        if (ti_status st = capture_step(e, B, lora, prefill, &ge)) return st;
         it = e->graphs.emplace(key, ge).first;
         if (e->tp.tp > 1 && e->comm) {
             // Every rank builds a new graph at the same step; capture, instantiation
@@ -1035,20 +1044,30 @@ ti_status read_err(ti_engine* e, int32_t word) {
 
 // One step for `B` sequences with host inputs; `window` is the sliding window
 // applied (prefill semantics) or -1 (decode semantics, as the reference).
+// prefill: the B entries are tokens len .. len + B - 1 of one sequence (seq_ids
+// all equal), decoded in one step; otherwise B distinct sequences, one token each
 ti_status run_step(ti_engine* e, int B, const int32_t* seq_ids, const int32_t* tokens, const int32_t* adapters,
-                   int window, int32_t* next_ids, int logits_mode, void* logits_out, cudaStream_t stream) {
+                   int window, int32_t* next_ids, int logits_mode, void* logits_out, cudaStream_t stream,
+                   bool prefill = false) {
     TI_CHECK(B >= 1 && B <= e->o.max_batch, TI_ERR_INVALID, "batch %d out of range [1, %d]", B, e->o.max_batch);
     TI_CHECK(seq_ids && tokens, TI_ERR_INVALID, "null seq_ids/tokens");
     TI_CHECK(e->bound_batch == 0, TI_ERR_STATE, "engine is bound to a device chain; unbind first");
     std::vector<int32_t> upd;
     for (int b = 0; b < B; ++b) {
         if (ti_status st = seq_check(e, seq_ids[b])) return st;
-        for (int c = 0; c < b; ++c)
-            TI_CHECK(seq_ids[c] != seq_ids[b], TI_ERR_INVALID, "sequence %d appears twice in one step", seq_ids[b]);
+        if (prefill) {
+            TI_CHECK(seq_ids[b] == seq_ids[0], TI_ERR_INVALID, "prefill step: entries of one sequence expected");
+        } else {
+            for (int c = 0; c < b; ++c)
+                TI_CHECK(seq_ids[c] != seq_ids[b], TI_ERR_INVALID, "sequence %d appears twice in one step",
+                         seq_ids[b]);
+        }
         TI_CHECK(tokens[b] >= 0 && tokens[b] < e->V, TI_ERR_INVALID, "token %d out of range [0, %d)", tokens[b], e->V);
         const int len = e->seqs[seq_ids[b]].len;
-        TI_CHECK(len < e->o.max_seq_len, TI_ERR_STATE, "sequence %d is full (%d tokens)", seq_ids[b], len);
-        if (ti_status st = ensure_pages(e, seq_ids[b], len + 1, &upd)) return st;
+        const int need = prefill ? len + B : len + 1;
+        TI_CHECK(need <= e->o.max_seq_len, TI_ERR_STATE, "sequence %d is full (%d tokens)", seq_ids[b], len);
+        if (!prefill || b == 0)
+            if (ti_status st = ensure_pages(e, seq_ids[b], need, &upd)) return st;
     }
     const int MB = e->o.max_batch;
     int32_t* h = e->h_desc;
@@ -1058,7 +1077,7 @@ ti_status run_step(ti_engine* e, int B, const int32_t* seq_ids, const int32_t* t
     for (int b = 0; b < B; ++b) {
         h[4 + b] = tokens[b];
         h[4 + MB + b] = seq_ids[b];
-        h[4 + 2 * MB + b] = e->seqs[seq_ids[b]].len;
+        h[4 + 2 * MB + b] = e->seqs[seq_ids[b]].len + (prefill ? b : 0);
         h[4 + 3 * MB + b] = adapters ? adapters[b] : -1;
     }
     TI_CHECK((int)upd.size() <= 3 * MB, TI_ERR_STATE, "too many page updates in one step");
@@ -1066,7 +1085,7 @@ ti_status run_step(ti_engine* e, int B, const int32_t* seq_ids, const int32_t* t
     bool any_lora = false;
     if (ti_status st = adapters_ready(e, B, adapters, stream, &any_lora)) return st;
     GraphEntry* g = nullptr;
-    if (ti_status st = get_graph(e, B, any_lora, &g)) return st;
+    if (ti_status st = get_graph(e, B, any_lora, &g, prefill)) return st;
     TI_CUDA(cudaMemcpyAsync(e->d_desc, h, (size_t)e->desc_ints * 4, cudaMemcpyHostToDevice, stream));
     TI_CUDA(cudaGraphLaunch(g->exec, stream));
     TI_CUDA(cudaMemcpyAsync(e->h_out, e->out, (size_t)(MB + 1) * 4, cudaMemcpyDeviceToHost, stream));
@@ -1101,7 +1120,7 @@ ti_status run_step(ti_engine* e, int B, const int32_t* seq_ids, const int32_t* t
     }
     if (ti_status st = read_err(e, e->h_out[MB])) return st;
     for (int b = 0; b < B; ++b) {
-        e->seqs[seq_ids[b]].len += 1;
+        if (!prefill || b == 0) e->seqs[seq_ids[b]].len += prefill ? B : 1;
         if (next_ids) next_ids[b] = e->h_out[b];
     }
     return TI_OK;
@@ -1411,6 +1430,35 @@ ti_status ti_engine_prefill(ti_engine* e, int sid, const int32_t* ids, int n, in
         ti_status st = run_step(e, 1, &sid, ids + i, adapter_id >= 0 ? &ad : nullptr, window, last ? next_id : nullptr,
                                 last ? logits_mode : TI_LOGITS_NONE, last ? logits_out : nullptr, e->cap);
         if (st) return st;
+    }
+    return TI_OK;
+}
+
+ti_status ti_engine_prefill_chunked(ti_engine* e, int sid, const int32_t* ids, int n, int adapter_id, int chunk,
+                                    int32_t* next_id, int logits_mode, void* logits_out) {
+    clear_error();
+    TI_CHECK(e && ids, TI_ERR_INVALID, "null argument");
+    TI_CHECK(n >= 1, TI_ERR_INVALID, "prefill: empty prompt");  // llama_model.cpp:212
+    TI_CHECK(chunk >= 1, TI_ERR_INVALID, "prefill: chunk must be >= 1");
+    DeviceGuard g(e->dev);
+    chunk = std::min(chunk, e->o.max_batch);
+    const int window = e->d.arch == TI_ARCH_MISTRAL ? e->d.sliding_window : -1;
+    const size_t row_bytes = (size_t)e->V * (logits_mode == TI_LOGITS_F32 ? 4 : 2);
+    std::vector<int32_t> sids((size_t)chunk, sid), ads((size_t)chunk, adapter_id), nexts((size_t)chunk);
+    std::vector<uint8_t> lg;
+    for (int i0 = 0; i0 < n; i0 += chunk) {
+        const int m = std::min(chunk, n - i0);
+        const bool last = i0 + m == n;
+        const bool want = last && logits_out && logits_mode != TI_LOGITS_NONE;
+        if (want) lg.resize((size_t)m * row_bytes);
+        ti_status st = run_step(e, m, sids.data(), ids + i0, adapter_id >= 0 ? ads.data() : nullptr, window,
+                                nexts.data(), want ? logits_mode : TI_LOGITS_NONE, want ? lg.data() : nullptr, e->cap,
+                                m > 1);
+        if (st) return st;
+        if (last) {
+            if (next_id) *next_id = nexts[m - 1];
+            if (want) std::memcpy(logits_out, lg.data() + (size_t)(m - 1) * row_bytes, row_bytes);
+        }
     }
     return TI_OK;
 }

@@ -218,7 +218,15 @@ struct AttnArgs {
     uint16_t* out = nullptr;  // [nb, out_stride]
     int out_stride = 0;
     int* err = nullptr;
+    // prefill: the step's entries may be one sequence at consecutive positions,
+    // whose K/V rows kv_append_launch wrote first; every page is loaded after the
+    // dependency wait
+    int prefill = 0;
 };
+// K (after RoPE) and V rows of every entry of a step into its page (ahead of a
+// prefill step's attention); uses qkv, pos, seq, page_table, kc, vc, freqs,
+// n_pages, nq, nkv, hd, nb, err of `a`
+cudaError_t kv_append_launch(const AttnArgs& a, cudaStream_t s, bool pdl);
 int attn_splits(int nb, int nkv, int hd, int max_len, int sms, int* max_chunk);
 // scratch floats / counters one launch needs: part_o + part_ml, and nb*nkv counters
 size_t attn_scratch_floats(int nb, int nq, int nkv, int hd, int n_splits);

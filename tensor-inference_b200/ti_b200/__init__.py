@@ -106,6 +106,8 @@ _SIGS = {
     "ti_seq_len": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_int)]),
     "ti_seq_reserve": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
     "ti_seq_read_kv": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int]),
+    "ti_engine_prefill_chunked": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                            C.POINTER(C.c_int32), C.c_int, C.c_void_p]),
     "ti_engine_prefill": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_int32), C.c_int,
                                     C.c_void_p]),
     "ti_engine_decode": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
@@ -566,7 +568,9 @@ class Engine:
         check(lib().ti_seq_read_kv(self.h, sid, layer, which, _ptr(out), length))
         return out
 
-    def prefill(self, sid, ids, adapter=-1, logits=LOGITS_NONE):
+    def prefill(self, sid, ids, adapter=-1, logits=LOGITS_NONE, chunk=None):
+        """run a prompt through a sequence; chunk: tokens per step (batched
+        prefill, ti_engine_prefill_chunked) instead of one step per token"""
         ids = np.ascontiguousarray(ids, np.int32)
         nxt = C.c_int32()
         out = None
@@ -574,7 +578,12 @@ class Engine:
             out = np.empty(self.desc.vocab, np.uint16)
         elif logits == LOGITS_F32:
             out = np.empty(self.desc.vocab, np.float32)
-        check(lib().ti_engine_prefill(self.h, sid, _ptr(ids), len(ids), adapter, C.byref(nxt), logits, _ptr(out)))
+        if chunk:
+            check(lib().ti_engine_prefill_chunked(self.h, sid, _ptr(ids), len(ids), adapter, chunk, C.byref(nxt),
+                                                  logits, _ptr(out)))
+        else:
+            check(lib().ti_engine_prefill(self.h, sid, _ptr(ids), len(ids), adapter, C.byref(nxt), logits,
+                                          _ptr(out)))
         return (nxt.value, out) if logits else nxt.value
 
     def decode(self, seq_ids, tokens, adapters=None, logits=LOGITS_NONE, stream=None):
