@@ -91,6 +91,9 @@ _SIGS = {
     "orc_seq_last_hidden": (I, [P, P, I]),
     "orc_seq_read_kv": (I, [P, I, I, P, I]),
     "orc_argmax_f32": (C.c_int32, [P, I]),
+    "orc_sample_top_p": (C.c_int32, [P, I, F, F, F, I]),
+    "orc_sample_top_k": (C.c_int32, [P, I, F, I, F, I]),
+    "orc_sample_draws": (None, [U64, I, P]),
 }
 
 
@@ -252,3 +255,19 @@ class Seq:
 def argmax(x):
     x = np.ascontiguousarray(x, np.float32)
     return int(lib().orc_argmax_f32(ptr(x), x.size))
+
+
+def sample_top_p(logits, temperature, p, u, stable=False):
+    x = np.ascontiguousarray(logits, np.float32)
+    return int(lib().orc_sample_top_p(ptr(x), x.size, temperature, p, u, int(stable)))
+
+
+def sample_top_k(logits, temperature, k, u, stable=False):
+    x = np.ascontiguousarray(logits, np.float32)
+    return int(lib().orc_sample_top_k(ptr(x), x.size, temperature, k, u, int(stable)))
+
+
+def sample_draws(seed, n):
+    u = np.empty(n, np.float32)
+    lib().orc_sample_draws(seed, n, ptr(u))
+    return u

@@ -13,6 +13,7 @@
 #include <cstring>
 #include <functional>
 #include <map>
+#include <random>
 #include <string>
 #include <thread>
 #include <vector>
@@ -491,6 +492,102 @@ extern "C" int32_t orc_argmax_f32(const float* x, int n) {
     for (int i = 1; i < n; ++i)
         if (x[i] > x[best]) best = i;
     return best;
+}
+
+// ============================================================ sampling
+// The reference's stochastic samplers (src/inference/sampling/top_p.cpp), one
+// logits row at a time.  The uniform draw u in [0, 1) is an argument: the
+// reference takes it from std::uniform_real_distribution<float> over
+// std::mt19937_64 (top_p.cpp:84-86, :124-126), which orc_sample_draws
+// reproduces with the same standard-library types.
+namespace {
+
+// token ids ordered by v descending: all of them (first_n < 0, std::sort as
+// top_p.cpp:71-73) or the first first_n (std::partial_sort as top_p.cpp:113-114,
+// also when first_n covers every id: the two order equal values differently).
+// stable == 0 keeps the library's order of equal values (the reference's);
+// stable != 0 orders them by ascending id.
+std::vector<int32_t> order_desc(const std::vector<float>& v, long first_n, int stable) {
+    std::vector<int32_t> idx(v.size());
+    for (size_t i = 0; i < idx.size(); ++i) idx[i] = (int32_t)i;
+    auto gt = [&](int32_t a, int32_t b) { return v[a] > v[b]; };
+    auto gt_stable = [&](int32_t a, int32_t b) { return v[a] > v[b] || (v[a] == v[b] && a < b); };
+    if (first_n < 0) {
+        if (stable) std::sort(idx.begin(), idx.end(), gt_stable);
+        else std::sort(idx.begin(), idx.end(), gt);
+    } else {
+        if (stable) std::partial_sort(idx.begin(), idx.begin() + first_n, idx.end(), gt_stable);
+        else std::partial_sort(idx.begin(), idx.begin() + first_n, idx.end(), gt);
+    }
+    return idx;
+}
+
+}  // namespace
+
+// TopP::sample, top_p.cpp:56-99.
+extern "C" int32_t orc_sample_top_p(const float* logits, int vocab, float temperature, float p, float u,
+                                    int stable) {
+    std::vector<float> v(logits, logits + vocab);
+    if (temperature != 1.0f && temperature > 0.0f)
+        for (float& x : v) x /= temperature;
+    float mx = v[0];
+    for (int i = 1; i < vocab; ++i) mx = std::max(mx, v[i]);
+    float sum = 0.0f;
+    for (float& x : v) {
+        x = std::exp(x - mx);
+        sum += x;
+    }
+    for (float& x : v) x /= sum;
+    std::vector<int32_t> idx = order_desc(v, -1, stable);
+    float cum = 0.0f;
+    int cut = vocab;
+    for (int i = 0; i < vocab; ++i) {
+        cum += v[idx[i]];
+        if (cum >= p) {
+            cut = i + 1;
+            break;
+        }
+    }
+    const float r = u * cum;
+    float acc = 0.0f;
+    for (int i = 0; i < cut; ++i) {
+        acc += v[idx[i]];
+        if (r <= acc) return idx[i];
+    }
+    return idx[0];
+}
+
+// TopK::sample, top_p.cpp:102-134.
+extern "C" int32_t orc_sample_top_k(const float* logits, int vocab, float temperature, int k, float u, int stable) {
+    std::vector<float> v(logits, logits + vocab);
+    const size_t keff = std::min((size_t)(uint32_t)k, (size_t)vocab);
+    if (temperature != 1.0f && temperature > 0.0f)
+        for (float& x : v) x /= temperature;
+    std::vector<int32_t> idx = order_desc(v, (long)keff, stable);
+    const float mx = v[idx[0]];
+    std::vector<float> pr(keff);
+    float sum = 0.0f;
+    for (size_t i = 0; i < keff; ++i) {
+        pr[i] = std::exp(v[idx[i]] - mx);
+        sum += pr[i];
+    }
+    const float r = u * sum;
+    float acc = 0.0f;
+    for (size_t i = 0; i < keff; ++i) {
+        acc += pr[i];
+        if (r <= acc) return idx[i];
+    }
+    return idx[0];
+}
+
+// u[i] = the i-th draw of std::uniform_real_distribution<float>(0, 1) from
+// std::mt19937_64(seed): the sequence a seeded TopP sees on one thread (its
+// engine is thread_local, top_p.cpp:84); a seeded TopK builds a fresh engine
+// per call (top_p.cpp:124), so every one of its calls sees u[0].
+extern "C" void orc_sample_draws(uint64_t seed, int n, float* u) {
+    std::mt19937_64 rng(seed);
+    std::uniform_real_distribution<float> dist(0.0f, 1.0f);
+    for (int i = 0; i < n; ++i) u[i] = dist(rng);
 }
 
 // ============================================================ model

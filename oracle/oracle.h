@@ -152,6 +152,17 @@ int orc_seq_read_kv(const orc_seq* s, int layer, int which, uint16_t* out, int l
 /* argmax with lowest-index tie break */
 int32_t orc_argmax_f32(const float* x, int n);
 
+/* Stochastic sampling of one fp32 logits row, restating
+ * src/inference/sampling/top_p.cpp: TopP::sample (:56-99) and TopK::sample
+ * (:102-134).  u is the uniform draw in [0, 1) the reference takes from its
+ * engine; stable = 0 orders equal values as the reference's std::sort /
+ * std::partial_sort do, stable = 1 by ascending token id. */
+int32_t orc_sample_top_p(const float* logits, int vocab, float temperature, float p, float u, int stable);
+int32_t orc_sample_top_k(const float* logits, int vocab, float temperature, int k, float u, int stable);
+/* the first n draws of std::uniform_real_distribution<float>(0, 1) over
+ * std::mt19937_64(seed) (top_p.cpp:84-86) */
+void orc_sample_draws(uint64_t seed, int n, float* u);
+
 #ifdef __cplusplus
 }
 #endif

@@ -6,6 +6,8 @@
 // pin the CPU oracle (tests/golden/make_golden.py).  The product never loads it.
 #include <tensor/adapter/adapter_loader.hpp>
 #include <tensor/backend/ops.hpp>
+#include <tensor/inference/sampling/greedy.hpp>
+#include <tensor/inference/sampling/top_p.hpp>
 #include <tensor/models/gemma/gemma_model.hpp>
 #include <tensor/models/llama/llama_model.hpp>
 #include <tensor/models/mistral/mistral_model.hpp>
@@ -17,6 +19,7 @@
 #include <cstdio>
 #include <cstring>
 #include <exception>
+#include <thread>
 #include <vector>
 
 namespace ops = tensor::backend::ops;
@@ -88,4 +91,46 @@ extern "C" int ref_run(const char* model_dir, int arch, const char* adapter_dir,
         std::snprintf(err, err_len, "%s", e.what());
         return 1;
     }
+}
+
+// The reference's samplers (src/inference/sampling/greedy.cpp, top_p.cpp) on a
+// host tensor of fp32 logits [rows, vocab]; they read the last row.
+// kind: 0 Greedy, 1 TopP(temperature, p), 2 TopK(temperature, k); seeded = 0
+// leaves the seed unset (std::random_device).  out[i] = the i-th of n_draws
+// sample() calls, all made on one fresh thread: TopP's engine is a
+// thread_local seeded at its first call on a thread (top_p.cpp:84), so a new
+// thread restarts the sequence.  Needs no GPU.
+extern "C" int ref_sample(const float* logits, int rows, int vocab, int kind, float temperature, float p, uint32_t k,
+                          int seeded, uint64_t seed, int n_draws, int32_t* out, char* err, int err_len) {
+    int rc = 0;
+    std::thread th([&] {
+        try {
+            namespace smp = tensor::inference::sampling;
+            tensor::core::TensorView view;
+            view.data = logits;
+            view.dtype = tensor::backend::DType::F32;
+            view.shape = tensor::backend::Shape{(std::size_t)rows, (std::size_t)vocab};
+            auto t = tensor::backend::Tensor::from_view(view, tensor::backend::Device::cpu());
+            smp::TopP tp;
+            tp.temperature = temperature;
+            tp.p = p;
+            smp::TopK tk;
+            tk.temperature = temperature;
+            tk.k = k;
+            if (seeded) tp.seed = tk.seed = seed;
+            for (int i = 0; i < n_draws; ++i) {
+                switch (kind) {
+                    case 0: out[i] = smp::Greedy{}.sample(t); break;
+                    case 1: out[i] = tp.sample(t); break;
+                    case 2: out[i] = tk.sample(t); break;
+                    default: std::snprintf(err, err_len, "unknown sampler %d", kind); rc = 2; return;
+                }
+            }
+        } catch (const std::exception& e) {
+            std::snprintf(err, err_len, "%s", e.what());
+            rc = 1;
+        }
+    });
+    th.join();
+    return rc;
 }
