@@ -94,6 +94,7 @@ _SIGS = {
     "orc_sample_top_p": (C.c_int32, [P, I, F, F, F, I]),
     "orc_sample_top_k": (C.c_int32, [P, I, F, I, F, I]),
     "orc_sample_draws": (None, [U64, I, P]),
+    "orc_sample_exact": (C.c_int32, [P, I, I, F, F, I, F]),
 }
 
 
@@ -271,3 +272,11 @@ def sample_draws(seed, n):
     u = np.empty(n, np.float32)
     lib().orc_sample_draws(seed, n, ptr(u))
     return u
+
+
+SAMPLE_TOP_P, SAMPLE_TOP_K = 1, 2
+
+
+def sample_exact(logits_bf16, kind, temperature, p=1.0, k=1, u=0.0):
+    x = np.ascontiguousarray(logits_bf16, np.uint16)
+    return int(lib().orc_sample_exact(ptr(x), x.size, kind, temperature, p, k, u))

@@ -580,6 +580,159 @@ extern "C" int32_t orc_sample_top_k(const float* logits, int vocab, float temper
     return idx[0];
 }
 
+// ---------------------------------------------------------------- exact form
+// The device sampler's definition of the same two samplers, restated here so
+// that its ids can be checked bit for bit.  Inputs are the bf16 logits the
+// reference's samplers receive from the model (top_p.cpp:31-39 widens them).
+// Tokens are ordered by logit descending, equal logits by ascending id; every
+// token of one logit value has weight w = floor(e * 2^63), e = the fp32
+// rounding of exp(v - vmax) (v = logit / temperature when the temperature is
+// != 1 and > 0, as top_p.cpp:62-64), and all cumulative sums are exact
+// 128-bit integers, so no decision depends on a summation order.
+//   top-p: the cut is the shortest prefix whose weight reaches ceil(p * S),
+//          S the total weight (the cumsum >= p test of top_p.cpp:76-81);
+//   top-k: the first min(k, vocab) tokens (top_p.cpp:111-115);
+//   pick:  the first token whose running weight reaches max(1, ceil(u * W)),
+//          W the cut's weight (r = u * cumsum and the r <= acc walk,
+//          top_p.cpp:88-93, :127-132).
+namespace {
+
+typedef unsigned __int128 u128;
+
+// exp(d) for d in [-45, 0], double: Cody-Waite reduction d = n ln2 + r with ln2
+// split into a 24-bit head and a tail (|r| <= ln2 / 2), exp(r) by its Taylor
+// series to degree 13 in Horner form with fused multiply-adds, times 2^n built
+// from its exponent bits.  Every step is a correctly rounded IEEE operation, so
+// the CUDA sampler (csrc/sample.cu) computes the same bits.
+double exp_taylor(double d) {
+    const double kInvLn2 = 1.4426950408889634;
+    const double kLn2Hi = 0.6931471824645996;     // ln 2 rounded to fp32
+    const double kLn2Lo = -1.904654299957768e-09; // ln 2 - kLn2Hi
+    static const double c[14] = {1.0, 1.0, 0.5, 0.16666666666666666, 0.041666666666666664,
+                                 0.008333333333333333, 0.001388888888888889, 0.0001984126984126984,
+                                 2.48015873015873e-05, 2.7557319223985893e-06, 2.755731922398589e-07,
+                                 2.505210838544172e-08, 2.08767569878681e-09, 1.6059043836821613e-10};
+    const double n = std::nearbyint(d * kInvLn2);
+    const double r = std::fma(-n, kLn2Lo, std::fma(-n, kLn2Hi, d));
+    double p = c[13];
+    for (int i = 12; i >= 0; --i) p = std::fma(p, r, c[i]);
+    const uint64_t bits = (uint64_t)(1023 + (int64_t)n) << 52;
+    double scale;
+    std::memcpy(&scale, &bits, 8);
+    return p * scale;
+}
+
+// bf16 bits -> unsigned key, ordered as the values (-0 and +0 share one key)
+inline uint32_t bf16_key(uint16_t b) {
+    if (b == 0x8000u) b = 0;
+    return (b & 0x8000u) ? (uint32_t)(~b & 0xffffu) : (uint32_t)(b | 0x8000u);
+}
+
+inline uint16_t key_bf16(uint32_t k) { return (k & 0x8000u) ? (uint16_t)(k & 0x7fffu) : (uint16_t)(~k & 0xffffu); }
+
+inline float scaled(uint32_t key, float temperature) {
+    const float l = bf(key_bf16(key));
+    return (temperature != 1.0f && temperature > 0.0f) ? l / temperature : l;
+}
+
+// weight of one token of logit key `key`, vmax the largest scaled logit
+uint64_t key_weight(uint32_t key, float vmax, float temperature) {
+    const float d = scaled(key, temperature) - vmax;
+    if (!(d >= -45.0f)) return 0;  // exp(-45) * 2^63 < 1
+    const float e = (float)exp_taylor((double)d);
+    return (uint64_t)std::ldexp((double)e, 63);
+}
+
+// ceil(f * x) for finite f >= 0 and x < 2^100; f >= 2^23 saturates
+u128 ceil_mul(float f, u128 x) {
+    uint32_t b;
+    std::memcpy(&b, &f, 4);
+    const uint32_t E = (b >> 23) & 0xffu;
+    const u128 m = E ? ((b & 0x7fffffu) | 0x800000u) : (b & 0x7fffffu);
+    const int s = E ? 150 - (int)E : 149;  // f = m * 2^-s
+    if (s <= 0) return ~(u128)0;
+    const u128 prod = m * x;
+    if (s >= 127) return prod ? 1 : 0;
+    return (prod + (((u128)1 << s) - 1)) >> s;
+}
+
+// smallest j in [1, c] with base + j * w >= target (target <= base + c * w)
+uint32_t tie_count(u128 base, uint64_t w, uint32_t c, u128 target) {
+    uint32_t lo = 1, hi = c;
+    while (lo < hi) {
+        const uint32_t mid = lo + (hi - lo) / 2;
+        if (base + (u128)mid * w >= target) hi = mid;
+        else lo = mid + 1;
+    }
+    return lo;
+}
+
+}  // namespace
+
+extern "C" int32_t orc_sample_exact(const uint16_t* logits, int vocab, int kind, float temperature, float p, int k,
+                                    float u) {
+    std::vector<uint32_t> hist(65536, 0);
+    uint32_t kmax = 0;
+    for (int i = 0; i < vocab; ++i) {
+        const uint32_t key = bf16_key(logits[i]);
+        hist[key]++;
+        kmax = std::max(kmax, key);
+    }
+    const float vmax = scaled(kmax, temperature);
+    u128 total = 0;
+    for (int key = (int)kmax; key >= 0; --key)
+        if (hist[key]) total += (u128)hist[key] * key_weight((uint32_t)key, vmax, temperature);
+    // the cut: its weight
+    u128 wcut = total;
+    if (kind == ORC_SAMPLE_TOP_K) {
+        const uint32_t keff = (uint32_t)std::min(std::max(k, 1), vocab);
+        u128 cum = 0;
+        uint32_t n = 0;
+        for (int key = (int)kmax; key >= 0; --key) {
+            const uint32_t c = hist[key];
+            if (!c) continue;
+            const uint64_t w = key_weight((uint32_t)key, vmax, temperature);
+            if (n + c >= keff) {
+                wcut = cum + (u128)(keff - n) * w;
+                break;
+            }
+            n += c;
+            cum += (u128)c * w;
+        }
+    } else {
+        const u128 target = std::max(ceil_mul(p, total), (u128)1);
+        u128 cum = 0;
+        for (int key = (int)kmax; key >= 0; --key) {
+            const uint32_t c = hist[key];
+            if (!c) continue;
+            const uint64_t w = key_weight((uint32_t)key, vmax, temperature);
+            if (cum + (u128)c * w >= target) {
+                wcut = cum + (u128)tie_count(cum, w, c, target) * w;
+                break;
+            }
+            cum += (u128)c * w;
+        }
+    }
+    // the pick: a logit value and the rank of the token among its ids
+    const u128 r = std::max(ceil_mul(u, wcut), (u128)1);
+    u128 cum = 0;
+    uint32_t pick_key = kmax, pick_rank = 1;
+    for (int key = (int)kmax; key >= 0; --key) {
+        const uint32_t c = hist[key];
+        if (!c) continue;
+        const uint64_t w = key_weight((uint32_t)key, vmax, temperature);
+        if (cum + (u128)c * w >= r) {
+            pick_key = (uint32_t)key;
+            pick_rank = tie_count(cum, w, c, r);
+            break;
+        }
+        cum += (u128)c * w;
+    }
+    for (int i = 0; i < vocab; ++i)
+        if (bf16_key(logits[i]) == pick_key && --pick_rank == 0) return i;
+    return -1;  // unreachable: the picked value's count is >= its rank
+}
+
 // u[i] = the i-th draw of std::uniform_real_distribution<float>(0, 1) from
 // std::mt19937_64(seed): the sequence a seeded TopP sees on one thread (its
 // engine is thread_local, top_p.cpp:84); a seeded TopK builds a fresh engine

@@ -31,11 +31,14 @@
  *                        (include/tensor/parser/weight_map.hpp:24)
  *   orc_pkm_*            PKM router spec (README.md:58-72,157-180 and the
  *                        PKM benchmark configuration); no code in the reference
+ *   orc_sample_top_p/k   src/inference/sampling/top_p.cpp:56-134
+ *   orc_sample_exact     the device sampler's exact form of the same samplers
  *
  * Parity pinning: the reference has no tests or golden vectors for this path.
  * The oracle is pinned against the reference's own CUDA implementation, built
  * from its sources into oracle/_ref/libref.so and run on a B200; the committed
- * fixtures in tests/golden/ hold those outputs.
+ * fixtures in tests/golden/ hold those outputs.  The samplers are pinned on the
+ * host against the reference's own sampler code in the same library.
  */
 #pragma once
 #include <stddef.h>
@@ -159,6 +162,13 @@ int32_t orc_argmax_f32(const float* x, int n);
  * std::partial_sort do, stable = 1 by ascending token id. */
 int32_t orc_sample_top_p(const float* logits, int vocab, float temperature, float p, float u, int stable);
 int32_t orc_sample_top_k(const float* logits, int vocab, float temperature, int k, float u, int stable);
+/* The device sampler's exact form of TopP / TopK on bf16 logits: order by
+ * logit descending, equal logits by ascending id; per-token weights
+ * floor(fp32(exp(v - vmax)) * 2^63) with exp evaluated by a fixed sequence of
+ * IEEE operations; cut and pick by exact 128-bit integer sums (oracle.cpp has
+ * the full statement).  kind: ORC_SAMPLE_TOP_P or ORC_SAMPLE_TOP_K. */
+enum { ORC_SAMPLE_TOP_P = 1, ORC_SAMPLE_TOP_K = 2 };
+int32_t orc_sample_exact(const uint16_t* logits, int vocab, int kind, float temperature, float p, int k, float u);
 /* the first n draws of std::uniform_real_distribution<float>(0, 1) over
  * std::mt19937_64(seed) (top_p.cpp:84-86) */
 void orc_sample_draws(uint64_t seed, int n, float* u);
