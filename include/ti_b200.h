@@ -254,6 +254,39 @@ ti_status ti_seq_create(ti_engine* e, int* seq_id);
 ti_status ti_seq_free(ti_engine* e, int seq_id);
 ti_status ti_seq_reset(ti_engine* e, int seq_id);
 ti_status ti_seq_len(ti_engine* e, int seq_id, int* len);
+
+/* Samplers: replaces GenerateOptions::sampler (include/tensor/inference/
+ * generator.hpp:22-38) and the host samplers it visits (greedy.cpp:11-36,
+ * top_p.cpp:56-134), run on the device where the LM head leaves the logits.
+ * Greedy ids are the LM head's fused argmax; top-p / top-k rows are sampled
+ * from the step's bf16 logits by an exact integer-weight form of the reference's
+ * algorithm (tokens by logit descending, equal logits by ascending id).
+ * Draws: std::uniform_real_distribution<float>(0, 1) over std::mt19937_64 as
+ * the reference; a top-p sequence owns one engine seeded when its sampler is
+ * set, advanced once per sampled id (the reference's engine is thread_local,
+ * top_p.cpp:84); top-k builds a fresh engine from the seed at every draw
+ * (top_p.cpp:124).  seeded = 0 seeds from std::random_device. */
+enum { TI_SAMPLE_GREEDY = 0, TI_SAMPLE_TOP_P = 1, TI_SAMPLE_TOP_K = 2 };
+typedef struct ti_sampling {
+    int      kind;         /* TI_SAMPLE_* */
+    float    temperature;  /* logits / temperature when != 1 and > 0 (TopP / TopK::temperature) */
+    float    p;            /* top-p: nucleus mass, finite (TopP::p) */
+    uint32_t k;            /* top-k: candidates, >= 1 (TopK::k) */
+    int      seeded;       /* 1: `seed` (TopP / TopK::seed); 0: std::random_device */
+    uint64_t seed;
+} ti_sampling;
+/* The sampler of the ids ti_engine_decode / ti_engine_prefill(_chunked) return
+ * for this sequence from now on; NULL or TI_SAMPLE_GREEDY restores greedy.
+ * Under tensor parallelism every rank sets the same seeded sampler (ranks then
+ * draw identical ids); a bound device chain (ti_engine_bind) accepts greedy
+ * sequences only.  ti_seq_create starts greedy; ti_seq_reset keeps the sampler. */
+ti_status ti_engine_seq_set_sampler(ti_engine* e, int seq_id, const ti_sampling* s);
+/* The same device sampler on caller-owned rows: logits [rows, vocab] bf16 and
+ * out [rows] int32 in device memory; params and draws (uniform in [0, 1)) are
+ * host arrays of `rows` entries (seed fields unused).  Greedy rows take the
+ * lowest id of the largest logit.  Synchronises `stream` before returning. */
+ti_status ti_op_sample(const void* logits, int rows, int vocab, const ti_sampling* params, const float* draws,
+                       int32_t* out, void* stream);
 /* pre-allocate pages so the sequence can grow to n_tokens without host work */
 ti_status ti_seq_reserve(ti_engine* e, int seq_id, int n_tokens);
 /* Give a sequence n_tokens of synthetic cached context (pages allocated, K/V

@@ -643,8 +643,9 @@ uint64_t key_weight(uint32_t key, float vmax, float temperature) {
     return (uint64_t)std::ldexp((double)e, 63);
 }
 
-// ceil(f * x) for finite f >= 0 and x < 2^100; f >= 2^23 saturates
+// ceil(f * x) for finite f and x < 2^100; f <= 0 gives 0, f >= 2^23 saturates
 u128 ceil_mul(float f, u128 x) {
+    if (!(f > 0.0f)) return 0;
     uint32_t b;
     std::memcpy(&b, &f, 4);
     const uint32_t E = (b >> 23) & 0xffu;

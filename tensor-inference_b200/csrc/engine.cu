@@ -19,11 +19,13 @@
 //              layers (one page id per 16 positions of a sequence).
 //   page table [max_seqs][ceil(max_seq_len/16)] int32, -1 = unallocated.
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
+#include <random>
 #include <string>
 #include <vector>
 
@@ -65,6 +67,10 @@ struct SeqState {
     bool live = false;
     int len = 0;
     std::vector<int> pages;
+    // the sampler of the ids this sequence returns (GenerateOptions::sampler,
+    // include/tensor/inference/generator.hpp:33-38); greedy by default
+    ti_sampling smp{};
+    std::mt19937_64 rng;  // top-p draws: one engine per sequence, seeded when the sampler is set
 };
 
 struct GraphEntry {
@@ -116,6 +122,9 @@ struct ti_engine {
     unsigned int* done = nullptr;
     int32_t* out = nullptr;  // [ids B][err]
     int32_t* h_out = nullptr;
+    // device sampling (allocated at the first sampled step): per-row parameters, value histograms
+    SampleRow *d_srows = nullptr, *h_srows = nullptr;
+    uint32_t* shist = nullptr;
     int* err = nullptr;
     float *part_o = nullptr, *part_ml = nullptr;
     unsigned int* counters = nullptr;
@@ -206,8 +215,10 @@ void free_all(ti_engine* e) {
     e->allocs.clear();
     if (e->h_desc) cudaFreeHost(e->h_desc);
     if (e->h_out) cudaFreeHost(e->h_out);
+    if (e->h_srows) cudaFreeHost(e->h_srows);
     e->h_desc = nullptr;
     e->h_out = nullptr;
+    e->h_srows = nullptr;
     for (auto& a : e->adapters) {
         if (a.host) cudaFreeHost(a.host);
         if (a.ready) cudaEventDestroy(a.ready);
@@ -1046,9 +1057,61 @@ ti_status read_err(ti_engine* e, int32_t word) {
 // applied (prefill semantics) or -1 (decode semantics, as the reference).
 // prefill: the B entries are tokens len .. len + B - 1 of one sequence (seq_ids
 // all equal), decoded in one step; otherwise B distinct sequences, one token each
+// The uniform draw of a sequence's next sampled id: top-p advances the
+// sequence's engine (the reference keeps one thread_local engine per sampling
+// thread, top_p.cpp:84); top-k builds a fresh engine from the seed at every
+// draw, as top_p.cpp:124 does, so a seeded top-k sees the same draw each step.
+float next_draw(SeqState& s) {
+    std::uniform_real_distribution<float> dist(0.0f, 1.0f);  // top_p.cpp:85
+    if (s.smp.kind == TI_SAMPLE_TOP_K) {
+        std::mt19937_64 fresh(s.smp.seeded ? s.smp.seed : (uint64_t)std::random_device{}());
+        return dist(fresh);
+    }
+    return dist(s.rng);
+}
+
+// Replace the argmax of every sampled row (a sequence with a top-p / top-k
+// sampler; in a prefill step only the last entry's id is returned) by the
+// device sampler's pick.  `logits` holds the rows as sample_launch indexes them.
+ti_status sample_rows(ti_engine* e, int B, const int32_t* seq_ids, bool prefill, const uint16_t* logits, int seg,
+                      size_t seg_stride, size_t row_stride, cudaStream_t stream) {
+    const int MB = e->o.max_batch;
+    if (!e->d_srows) {
+        TI_CHECK(dalloc_t(e, &e->d_srows, (size_t)MB, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+        TI_CHECK(dalloc_t(e, &e->shist, sample_scratch_bytes(MB) / 4, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
+                 ti_last_error());
+        TI_CUDA(cudaMallocHost(&e->h_srows, (size_t)MB * sizeof(SampleRow)));
+    }
+    for (int b = 0; b < B; ++b) {
+        SampleRow r{};
+        SeqState& s = e->seqs[seq_ids[b]];
+        if ((!prefill || b == B - 1) && s.smp.kind != TI_SAMPLE_GREEDY) {
+            r.kind = s.smp.kind == TI_SAMPLE_TOP_P ? kSampleTopP : kSampleTopK;
+            r.temperature = s.smp.temperature;
+            r.p = s.smp.p;
+            r.k = (int32_t)std::min<uint32_t>(s.smp.k, 0x7fffffffu);
+            r.u = next_draw(s);
+        }
+        e->h_srows[b] = r;
+    }
+    TI_CUDA(cudaMemcpyAsync(e->d_srows, e->h_srows, (size_t)B * sizeof(SampleRow), cudaMemcpyHostToDevice, stream));
+    SampleArgs a;
+    a.logits = logits;
+    a.vocab = e->V;
+    a.seg = seg;
+    a.seg_stride = seg_stride;
+    a.row_stride = row_stride;
+    a.rows = e->d_srows;
+    a.hist = e->shist;
+    a.out = e->out;
+    a.err = e->err;
+    TI_CUDA(sample_launch(a, B, stream));
+    return TI_OK;
+}
+
 ti_status run_step(ti_engine* e, int B, const int32_t* seq_ids, const int32_t* tokens, const int32_t* adapters,
                    int window, int32_t* next_ids, int logits_mode, void* logits_out, cudaStream_t stream,
-                   bool prefill = false) {
+                   bool prefill = false, bool sample = false) {
     TI_CHECK(B >= 1 && B <= e->o.max_batch, TI_ERR_INVALID, "batch %d out of range [1, %d]", B, e->o.max_batch);
     TI_CHECK(seq_ids && tokens, TI_ERR_INVALID, "null seq_ids/tokens");
     TI_CHECK(e->bound_batch == 0, TI_ERR_STATE, "engine is bound to a device chain; unbind first");
@@ -1088,17 +1151,32 @@ ti_status run_step(ti_engine* e, int B, const int32_t* seq_ids, const int32_t* t
     if (ti_status st = get_graph(e, B, any_lora, &g, prefill)) return st;
     TI_CUDA(cudaMemcpyAsync(e->d_desc, h, (size_t)e->desc_ints * 4, cudaMemcpyHostToDevice, stream));
     TI_CUDA(cudaGraphLaunch(g->exec, stream));
+    bool any_sample = false;
+    if (sample)
+        for (int b = 0; b < B; ++b)
+            any_sample |= (!prefill || b == B - 1) && e->seqs[seq_ids[b]].smp.kind != TI_SAMPLE_GREEDY;
+    const bool want_logits = logits_out && logits_mode != TI_LOGITS_NONE;
+    // tensor parallelism: every rank's vocabulary slice, gathered [rank][b][j]
+    if (e->tp.tp > 1 && (any_sample || want_logits)) {
+        const ncclResult_t r = nccl_api()->AllGather(e->logits, e->lgather, (size_t)B * e->Vl, ncclBfloat16, e->comm,
+                                                     stream);
+        TI_CHECK(r == ncclSuccess, TI_ERR_CUDA, "ncclAllGather: %s", nccl_api()->GetErrorString(r));
+    }
+    if (any_sample) {
+        ti_status st = e->tp.tp == 1
+                           ? sample_rows(e, B, seq_ids, prefill, e->logits, e->V, 0, (size_t)e->V, stream)
+                           : sample_rows(e, B, seq_ids, prefill, e->lgather, e->Vl, (size_t)B * e->Vl, (size_t)e->Vl,
+                                         stream);
+        if (st) return st;
+    }
     TI_CUDA(cudaMemcpyAsync(e->h_out, e->out, (size_t)(MB + 1) * 4, cudaMemcpyDeviceToHost, stream));
     // host logits [B, V] bf16: the local rows, or every rank's vocabulary slice gathered
     std::vector<uint16_t> lg;
-    if (logits_out && logits_mode != TI_LOGITS_NONE) {
+    if (want_logits) {
         lg.resize((size_t)B * e->V);
         if (e->tp.tp == 1) {
             TI_CUDA(cudaMemcpyAsync(lg.data(), e->logits, lg.size() * 2, cudaMemcpyDeviceToHost, stream));
         } else {
-            const ncclResult_t r = nccl_api()->AllGather(e->logits, e->lgather, (size_t)B * e->Vl, ncclBfloat16, e->comm,
-                                                         stream);
-            TI_CHECK(r == ncclSuccess, TI_ERR_CUDA, "ncclAllGather: %s", nccl_api()->GetErrorString(r));
             std::vector<uint16_t> gat(lg.size());
             TI_CUDA(cudaMemcpyAsync(gat.data(), e->lgather, gat.size() * 2, cudaMemcpyDeviceToHost, stream));
             TI_CUDA(cudaStreamSynchronize(stream));
@@ -1347,6 +1425,27 @@ ti_status ti_seq_reset(ti_engine* e, int sid) {
     return TI_OK;
 }
 
+ti_status ti_engine_seq_set_sampler(ti_engine* e, int sid, const ti_sampling* smp) {
+    clear_error();
+    TI_CHECK(e, TI_ERR_INVALID, "null engine");
+    if (ti_status st = seq_check(e, sid)) return st;
+    SeqState& q = e->seqs[sid];
+    if (!smp || smp->kind == TI_SAMPLE_GREEDY) {
+        q.smp = ti_sampling{};
+        return TI_OK;
+    }
+    TI_CHECK(smp->kind == TI_SAMPLE_TOP_P || smp->kind == TI_SAMPLE_TOP_K, TI_ERR_INVALID, "unknown sampler kind %d",
+             smp->kind);
+    TI_CHECK(std::isfinite(smp->temperature), TI_ERR_INVALID, "sampler temperature must be finite");
+    TI_CHECK(smp->kind != TI_SAMPLE_TOP_P || std::isfinite(smp->p), TI_ERR_INVALID, "top-p: p must be finite");
+    TI_CHECK(smp->kind != TI_SAMPLE_TOP_K || smp->k >= 1, TI_ERR_INVALID, "top-k: k must be >= 1");
+    TI_CHECK(e->tp.tp == 1 || smp->seeded, TI_ERR_INVALID,
+             "tensor-parallel ranks draw the same ids only from a seeded sampler");
+    q.smp = *smp;
+    q.rng.seed(smp->seeded ? smp->seed : (uint64_t)std::random_device{}());
+    return TI_OK;
+}
+
 ti_status ti_seq_len(ti_engine* e, int sid, int* len) {
     TI_CHECK(e && len, TI_ERR_INVALID, "null argument");
     if (ti_status st = seq_check(e, sid)) return st;
@@ -1428,7 +1527,7 @@ ti_status ti_engine_prefill(ti_engine* e, int sid, const int32_t* ids, int n, in
     for (int i = 0; i < n; ++i) {
         const bool last = i == n - 1;
         ti_status st = run_step(e, 1, &sid, ids + i, adapter_id >= 0 ? &ad : nullptr, window, last ? next_id : nullptr,
-                                last ? logits_mode : TI_LOGITS_NONE, last ? logits_out : nullptr, e->cap);
+                                last ? logits_mode : TI_LOGITS_NONE, last ? logits_out : nullptr, e->cap, false, last);
         if (st) return st;
     }
     return TI_OK;
@@ -1453,7 +1552,7 @@ ti_status ti_engine_prefill_chunked(ti_engine* e, int sid, const int32_t* ids, i
         if (want) lg.resize((size_t)m * row_bytes);
         ti_status st = run_step(e, m, sids.data(), ids + i0, adapter_id >= 0 ? ads.data() : nullptr, window,
                                 nexts.data(), want ? logits_mode : TI_LOGITS_NONE, want ? lg.data() : nullptr, e->cap,
-                                m > 1);
+                                m > 1, last);
         if (st) return st;
         if (last) {
             if (next_id) *next_id = nexts[m - 1];
@@ -1470,7 +1569,7 @@ ti_status ti_engine_decode(ti_engine* e, int batch, const int32_t* seq_ids, cons
     TI_CHECK(e, TI_ERR_INVALID, "null engine");
     DeviceGuard g(e->dev);
     return run_step(e, batch, seq_ids, tokens, adapter_ids, -1, next_ids, logits_mode, logits_out,
-                    (cudaStream_t)stream);
+                    (cudaStream_t)stream, false, true);
 }
 
 ti_status ti_engine_bind(ti_engine* e, int B, const int32_t* seq_ids, const int32_t* first_tokens,
@@ -1488,6 +1587,8 @@ ti_status ti_engine_bind(ti_engine* e, int B, const int32_t* seq_ids, const int3
         if (ti_status st = seq_check(e, seq_ids[b])) return st;
         TI_CHECK(first_tokens[b] >= 0 && first_tokens[b] < e->V, TI_ERR_INVALID, "token out of range");
         const SeqState& s = e->seqs[seq_ids[b]];
+        TI_CHECK(s.smp.kind == TI_SAMPLE_GREEDY, TI_ERR_UNSUPPORTED,
+                 "sequence %d samples top-p / top-k; a bound device chain feeds greedy ids only", seq_ids[b]);
         TI_CHECK((int)s.pages.size() * kPageTokens > s.len, TI_ERR_STATE,
                  "sequence %d has no reserved page for its next token (ti_seq_reserve)", seq_ids[b]);
         h[4 + b] = first_tokens[b];

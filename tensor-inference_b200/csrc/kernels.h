@@ -272,6 +272,32 @@ struct EmbedArgs {
 };
 cudaError_t embed_launch(const EmbedArgs& a, cudaStream_t s, bool pdl);
 
+// ----------------------------------------------------------------- sampling
+// Top-p / top-k sampling of bf16 logits rows, one CTA per row (sample.cu has
+// the exact definition); rows of kind kSampleGreedy keep out[b] unchanged.
+enum : int32_t { kSampleGreedy = 0, kSampleTopP = 1, kSampleTopK = 2 };
+struct SampleRow {  // per-row parameters in device memory, 32 bytes
+    int32_t kind = kSampleGreedy;
+    float temperature = 1.0f;
+    float p = 1.0f;
+    int32_t k = 1;
+    float u = 0.0f;  // uniform draw in [0, 1)
+    int32_t pad[3] = {};
+};
+struct SampleArgs {
+    // token i of row b at logits[(i / seg) * seg_stride + b * row_stride + i % seg]:
+    // seg = vocab for contiguous rows, the per-rank slice for gathered TP logits
+    const uint16_t* logits = nullptr;
+    int vocab = 0, seg = 0;
+    size_t seg_stride = 0, row_stride = 0;
+    const SampleRow* rows = nullptr;  // [nb]
+    uint32_t* hist = nullptr;         // sample_scratch_bytes(nb)
+    int32_t* out = nullptr;           // [nb] sampled ids
+    int* err = nullptr;               // error bits
+};
+size_t sample_scratch_bytes(int nb);
+cudaError_t sample_launch(const SampleArgs& a, int nb, cudaStream_t s);
+
 // synthetic K/V rows for positions [0, n_tok) of one sequence (its pages[]), all layers
 cudaError_t fill_kv_launch(uint16_t* kpool, uint16_t* vpool, size_t layer_elems, int n_layers, const int32_t* pages,
                            int n_tok, int nkv, int kv0, int nkv_g, int hd, uint64_t key_k, uint64_t key_v, float c,

@@ -24,6 +24,7 @@ WFMT_BF16, WFMT_Q4_0, WFMT_Q8_0 = 0, 1, 2
 GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0, GGML_BF16 = 0, 1, 2, 8, 30
 EW_SILU, EW_GELU, EW_MUL, EW_ADD, EW_MUL_SCALAR = range(5)
 LOGITS_NONE, LOGITS_BF16, LOGITS_F32 = 0, 1, 2
+SAMPLE_GREEDY, SAMPLE_TOP_P, SAMPLE_TOP_K = 0, 1, 2
 PROJ_Q, PROJ_K, PROJ_V, PROJ_O, PROJ_GATE, PROJ_UP, PROJ_DOWN = 1, 2, 4, 8, 16, 32, 64
 KERNEL_EMBED, KERNEL_QKV, KERNEL_ATTN, KERNEL_O, KERNEL_GATEUP, KERNEL_DOWN, KERNEL_LMHEAD = range(7)
 
@@ -37,6 +38,12 @@ class TiError(RuntimeError):
 class RopeScaling(C.Structure):
     _fields_ = [("apply_scaling", C.c_int), ("factor", C.c_float), ("low_freq_factor", C.c_float),
                 ("high_freq_factor", C.c_float), ("original_max_pos", C.c_int)]
+
+
+class Sampling(C.Structure):
+    """ti_sampling: the reference's Greedy / TopP / TopK options (sampling/top_p.hpp)."""
+    _fields_ = [("kind", C.c_int), ("temperature", C.c_float), ("p", C.c_float), ("k", C.c_uint32),
+                ("seeded", C.c_int), ("seed", C.c_uint64)]
 
 
 class ModelDesc(C.Structure):
@@ -104,6 +111,9 @@ _SIGS = {
     "ti_seq_free": (C.c_int, [C.c_void_p, C.c_int]),
     "ti_seq_reset": (C.c_int, [C.c_void_p, C.c_int]),
     "ti_seq_len": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_int)]),
+    "ti_engine_seq_set_sampler": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(Sampling)]),
+    "ti_op_sample": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(Sampling), C.POINTER(C.c_float),
+                               C.c_void_p, C.c_void_p]),
     "ti_seq_reserve": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
     "ti_seq_read_kv": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int]),
     "ti_engine_prefill_chunked": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int,
@@ -555,6 +565,12 @@ class Engine:
         n = C.c_int()
         check(lib().ti_seq_len(self.h, sid, C.byref(n)))
         return n.value
+
+    def set_sampler(self, sid, kind=SAMPLE_GREEDY, temperature=1.0, p=0.95, k=40, seed=None):
+        """The sampler of the ids this sequence's decode / prefill calls return
+        (defaults as TopP / TopK in the reference); seed None = std::random_device."""
+        smp = Sampling(kind, temperature, p, k, 0 if seed is None else 1, 0 if seed is None else seed)
+        check(lib().ti_engine_seq_set_sampler(self.h, sid, C.byref(smp)))
 
     def seq_reserve(self, sid, n_tokens):
         check(lib().ti_seq_reserve(self.h, sid, n_tokens))

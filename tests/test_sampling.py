@@ -211,6 +211,7 @@ def test_exact_form_edges():
     assert oracle.sample_exact(x, P, 1.0, 0.9, 0, 0.0) == 1
     assert oracle.sample_exact(x, P, 1.0, 1e-6, 0, 0.999) == 1
     assert oracle.sample_exact(x, P, 1.0, 0.0, 0, 0.5) == 1
+    assert oracle.sample_exact(x, P, 1.0, -0.5, 0, 0.5) == 1  # cumsum >= p holds at the first token
     # k = 1 is greedy with the lowest id on ties; k above the vocabulary takes all
     assert oracle.sample_exact(x, K, 1.0, 0, 1, 0.7) == 1
     assert oracle.sample_exact(x, K, 0.0, 0, 100, 0.0) == 1
