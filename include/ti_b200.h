@@ -287,6 +287,9 @@ ti_status ti_engine_seq_set_sampler(ti_engine* e, int seq_id, const ti_sampling*
  * lowest id of the largest logit.  Synchronises `stream` before returning. */
 ti_status ti_op_sample(const void* logits, int rows, int vocab, const ti_sampling* params, const float* draws,
                        int32_t* out, void* stream);
+/* The first n uniform draws a sequence with sampler `s` uses (host only, no
+ * device): what ti_engine_seq_set_sampler's per-sequence engine produces. */
+ti_status ti_sampler_draws(const ti_sampling* s, int n, float* out);
 /* pre-allocate pages so the sequence can grow to n_tokens without host work */
 ti_status ti_seq_reserve(ti_engine* e, int seq_id, int n_tokens);
 /* Give a sequence n_tokens of synthetic cached context (pages allocated, K/V

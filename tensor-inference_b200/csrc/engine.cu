@@ -68,9 +68,8 @@ struct SeqState {
     int len = 0;
     std::vector<int> pages;
     // the sampler of the ids this sequence returns (GenerateOptions::sampler,
-    // include/tensor/inference/generator.hpp:33-38); greedy by default
-    ti_sampling smp{};
-    std::mt19937_64 rng;  // top-p draws: one engine per sequence, seeded when the sampler is set
+    // include/tensor/inference/generator.hpp:33-38) and its draws; greedy by default
+    SamplerDraws smp;
 };
 
 struct GraphEntry {
@@ -1057,19 +1056,6 @@ ti_status read_err(ti_engine* e, int32_t word) {
 // applied (prefill semantics) or -1 (decode semantics, as the reference).
 // prefill: the B entries are tokens len .. len + B - 1 of one sequence (seq_ids
 // all equal), decoded in one step; otherwise B distinct sequences, one token each
-// The uniform draw of a sequence's next sampled id: top-p advances the
-// sequence's engine (the reference keeps one thread_local engine per sampling
-// thread, top_p.cpp:84); top-k builds a fresh engine from the seed at every
-// draw, as top_p.cpp:124 does, so a seeded top-k sees the same draw each step.
-float next_draw(SeqState& s) {
-    std::uniform_real_distribution<float> dist(0.0f, 1.0f);  // top_p.cpp:85
-    if (s.smp.kind == TI_SAMPLE_TOP_K) {
-        std::mt19937_64 fresh(s.smp.seeded ? s.smp.seed : (uint64_t)std::random_device{}());
-        return dist(fresh);
-    }
-    return dist(s.rng);
-}
-
 // Replace the argmax of every sampled row (a sequence with a top-p / top-k
 // sampler; in a prefill step only the last entry's id is returned) by the
 // device sampler's pick.  `logits` holds the rows as sample_launch indexes them.
@@ -1085,12 +1071,13 @@ ti_status sample_rows(ti_engine* e, int B, const int32_t* seq_ids, bool prefill,
     for (int b = 0; b < B; ++b) {
         SampleRow r{};
         SeqState& s = e->seqs[seq_ids[b]];
-        if ((!prefill || b == B - 1) && s.smp.kind != TI_SAMPLE_GREEDY) {
-            r.kind = s.smp.kind == TI_SAMPLE_TOP_P ? kSampleTopP : kSampleTopK;
-            r.temperature = s.smp.temperature;
-            r.p = s.smp.p;
-            r.k = (int32_t)std::min<uint32_t>(s.smp.k, 0x7fffffffu);
-            r.u = next_draw(s);
+        const ti_sampling& c = s.smp.cfg;
+        if ((!prefill || b == B - 1) && c.kind != TI_SAMPLE_GREEDY) {
+            r.kind = c.kind == TI_SAMPLE_TOP_P ? kSampleTopP : kSampleTopK;
+            r.temperature = c.temperature;
+            r.p = c.p;
+            r.k = (int32_t)std::min<uint32_t>(c.k, 0x7fffffffu);
+            r.u = s.smp.next();
         }
         e->h_srows[b] = r;
     }
@@ -1154,7 +1141,7 @@ ti_status run_step(ti_engine* e, int B, const int32_t* seq_ids, const int32_t* t
     bool any_sample = false;
     if (sample)
         for (int b = 0; b < B; ++b)
-            any_sample |= (!prefill || b == B - 1) && e->seqs[seq_ids[b]].smp.kind != TI_SAMPLE_GREEDY;
+            any_sample |= (!prefill || b == B - 1) && e->seqs[seq_ids[b]].smp.cfg.kind != TI_SAMPLE_GREEDY;
     const bool want_logits = logits_out && logits_mode != TI_LOGITS_NONE;
     // tensor parallelism: every rank's vocabulary slice, gathered [rank][b][j]
     if (e->tp.tp > 1 && (any_sample || want_logits)) {
@@ -1429,20 +1416,12 @@ ti_status ti_engine_seq_set_sampler(ti_engine* e, int sid, const ti_sampling* sm
     clear_error();
     TI_CHECK(e, TI_ERR_INVALID, "null engine");
     if (ti_status st = seq_check(e, sid)) return st;
-    SeqState& q = e->seqs[sid];
-    if (!smp || smp->kind == TI_SAMPLE_GREEDY) {
-        q.smp = ti_sampling{};
-        return TI_OK;
-    }
-    TI_CHECK(smp->kind == TI_SAMPLE_TOP_P || smp->kind == TI_SAMPLE_TOP_K, TI_ERR_INVALID, "unknown sampler kind %d",
-             smp->kind);
-    TI_CHECK(std::isfinite(smp->temperature), TI_ERR_INVALID, "sampler temperature must be finite");
-    TI_CHECK(smp->kind != TI_SAMPLE_TOP_P || std::isfinite(smp->p), TI_ERR_INVALID, "top-p: p must be finite");
-    TI_CHECK(smp->kind != TI_SAMPLE_TOP_K || smp->k >= 1, TI_ERR_INVALID, "top-k: k must be >= 1");
-    TI_CHECK(e->tp.tp == 1 || smp->seeded, TI_ERR_INVALID,
+    const ti_sampling greedy{};
+    const ti_sampling& s = smp ? *smp : greedy;
+    if (ti_status st = sampler_check(s)) return st;
+    TI_CHECK(e->tp.tp == 1 || s.kind == TI_SAMPLE_GREEDY || s.seeded, TI_ERR_INVALID,
              "tensor-parallel ranks draw the same ids only from a seeded sampler");
-    q.smp = *smp;
-    q.rng.seed(smp->seeded ? smp->seed : (uint64_t)std::random_device{}());
+    e->seqs[sid].smp.reset(s);
     return TI_OK;
 }
 
@@ -1587,7 +1566,7 @@ ti_status ti_engine_bind(ti_engine* e, int B, const int32_t* seq_ids, const int3
         if (ti_status st = seq_check(e, seq_ids[b])) return st;
         TI_CHECK(first_tokens[b] >= 0 && first_tokens[b] < e->V, TI_ERR_INVALID, "token out of range");
         const SeqState& s = e->seqs[seq_ids[b]];
-        TI_CHECK(s.smp.kind == TI_SAMPLE_GREEDY, TI_ERR_UNSUPPORTED,
+        TI_CHECK(s.smp.cfg.kind == TI_SAMPLE_GREEDY, TI_ERR_UNSUPPORTED,
                  "sequence %d samples top-p / top-k; a bound device chain feeds greedy ids only", seq_ids[b]);
         TI_CHECK((int)s.pages.size() * kPageTokens > s.len, TI_ERR_STATE,
                  "sequence %d has no reserved page for its next token (ti_seq_reserve)", seq_ids[b]);

@@ -4,6 +4,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <random>
 #include <string>
 
 #include "../../include/ti_b200.h"
@@ -57,5 +58,20 @@ struct DeviceGuard {
 
 // rope frequency table (ops.cu:235-278) computed on the host in float
 void rope_freqs(int head_dim, float theta, const ti_rope_scaling* sc, float* out);
+
+// The uniform draws of one sequence's sampler, as the reference's engines
+// produce them: std::uniform_real_distribution<float>(0, 1) over
+// std::mt19937_64 (top_p.cpp:84-86).  Top-p keeps one engine, seeded at
+// reset() and advanced per draw (the reference's is thread_local); top-k builds
+// a fresh engine from the seed at every draw (top_p.cpp:124).  Unseeded
+// samplers seed from std::random_device, as an unset seed does.
+struct SamplerDraws {
+    ti_sampling cfg{};  // kind TI_SAMPLE_GREEDY: no draws
+    std::mt19937_64 rng;
+    void reset(const ti_sampling& s);
+    float next();
+};
+// TI_OK when `s` is a valid sampler (sample.cu)
+ti_status sampler_check(const ti_sampling& s);
 
 }  // namespace ti

@@ -314,7 +314,46 @@ cudaError_t sample_launch(const SampleArgs& a, int nb, cudaStream_t s) {
 
 }  // namespace ti
 
+namespace ti {
+
+void SamplerDraws::reset(const ti_sampling& s) {
+    cfg = s;
+    if (s.kind == TI_SAMPLE_TOP_P) rng.seed(s.seeded ? s.seed : (uint64_t)std::random_device{}());
+}
+
+float SamplerDraws::next() {
+    std::uniform_real_distribution<float> dist(0.0f, 1.0f);  // top_p.cpp:85
+    if (cfg.kind == TI_SAMPLE_TOP_K) {
+        std::mt19937_64 fresh(cfg.seeded ? cfg.seed : (uint64_t)std::random_device{}());
+        return dist(fresh);
+    }
+    return dist(rng);
+}
+
+ti_status sampler_check(const ti_sampling& s) {
+    TI_CHECK(s.kind >= TI_SAMPLE_GREEDY && s.kind <= TI_SAMPLE_TOP_K, TI_ERR_INVALID, "unknown sampler kind %d",
+             s.kind);
+    if (s.kind == TI_SAMPLE_GREEDY) return TI_OK;
+    TI_CHECK(std::isfinite(s.temperature), TI_ERR_INVALID, "sampler temperature must be finite");
+    TI_CHECK(s.kind != TI_SAMPLE_TOP_P || std::isfinite(s.p), TI_ERR_INVALID, "top-p: p must be finite");
+    TI_CHECK(s.kind != TI_SAMPLE_TOP_K || s.k >= 1, TI_ERR_INVALID, "top-k: k must be >= 1");
+    return TI_OK;
+}
+
+}  // namespace ti
+
 using namespace ti;
+
+extern "C" ti_status ti_sampler_draws(const ti_sampling* s, int n, float* out) {
+    clear_error();
+    TI_CHECK(s && (out || n == 0) && n >= 0, TI_ERR_INVALID, "sampler_draws: bad argument");
+    if (ti_status st = sampler_check(*s)) return st;
+    TI_CHECK(s->kind != TI_SAMPLE_GREEDY, TI_ERR_INVALID, "sampler_draws: a greedy sampler draws nothing");
+    SamplerDraws d;
+    d.reset(*s);
+    for (int i = 0; i < n; ++i) out[i] = d.next();
+    return TI_OK;
+}
 
 // One sampling call on caller-owned device rows, without an engine: every row's
 // sampler and uniform draw come from the host arrays.  Greedy rows take the
@@ -328,8 +367,7 @@ extern "C" ti_status ti_op_sample(const void* logits, int rows, int vocab, const
     std::vector<SampleRow> h((size_t)rows);
     for (int b = 0; b < rows; ++b) {
         const ti_sampling& q = params[b];
-        TI_CHECK(q.kind >= TI_SAMPLE_GREEDY && q.kind <= TI_SAMPLE_TOP_K, TI_ERR_INVALID,
-                 "sample: row %d: unknown kind %d", b, q.kind);
+        if (ti_status st = sampler_check(q)) return st;
         TI_CHECK(draws[b] >= 0.0f && draws[b] < 1.0f, TI_ERR_INVALID, "sample: row %d: draw outside [0, 1)", b);
         SampleRow& r = h[b];
         if (q.kind == TI_SAMPLE_GREEDY) {
@@ -337,9 +375,6 @@ extern "C" ti_status ti_op_sample(const void* logits, int rows, int vocab, const
             r.k = 1;
             continue;
         }
-        TI_CHECK(std::isfinite(q.temperature), TI_ERR_INVALID, "sample: row %d: temperature not finite", b);
-        TI_CHECK(q.kind != TI_SAMPLE_TOP_P || std::isfinite(q.p), TI_ERR_INVALID, "sample: row %d: p not finite", b);
-        TI_CHECK(q.kind != TI_SAMPLE_TOP_K || q.k >= 1, TI_ERR_INVALID, "sample: row %d: k must be >= 1", b);
         r.kind = q.kind == TI_SAMPLE_TOP_P ? kSampleTopP : kSampleTopK;
         r.temperature = q.temperature;
         r.p = q.p;

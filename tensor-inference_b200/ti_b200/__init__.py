@@ -46,6 +46,14 @@ class Sampling(C.Structure):
                 ("seeded", C.c_int), ("seed", C.c_uint64)]
 
 
+def sampler_draws(kind, n, seed=None, temperature=1.0, p=0.95, k=40):
+    """the first n uniform draws of a sequence sampler (ti_sampler_draws)"""
+    smp = Sampling(kind, temperature, p, k, 0 if seed is None else 1, 0 if seed is None else seed)
+    out = (C.c_float * n)()
+    check(lib().ti_sampler_draws(C.byref(smp), n, out))
+    return np.array(out[:], np.float32)
+
+
 class ModelDesc(C.Structure):
     _fields_ = [("arch", C.c_int), ("hidden", C.c_int), ("n_layers", C.c_int), ("n_heads", C.c_int),
                 ("n_kv_heads", C.c_int), ("head_dim", C.c_int), ("intermediate", C.c_int), ("vocab", C.c_int),
@@ -114,6 +122,7 @@ _SIGS = {
     "ti_engine_seq_set_sampler": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(Sampling)]),
     "ti_op_sample": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(Sampling), C.POINTER(C.c_float),
                                C.c_void_p, C.c_void_p]),
+    "ti_sampler_draws": (C.c_int, [C.POINTER(Sampling), C.c_int, C.POINTER(C.c_float)]),
     "ti_seq_reserve": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
     "ti_seq_read_kv": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int]),
     "ti_engine_prefill_chunked": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int,

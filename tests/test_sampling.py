@@ -235,3 +235,32 @@ def test_exact_form_distribution():
     u = oracle.sample_draws(3, 20000)
     counts = np.bincount([oracle.sample_exact(x, oracle.SAMPLE_TOP_P, T, 1.0, 0, float(v)) for v in u], minlength=6)
     np.testing.assert_allclose(counts / u.size, pr, atol=0.012)
+
+
+# ---------------------------------------------------------------- the engine's draws
+def test_engine_draws_are_the_reference_sequence():
+    """ti_sampler_draws runs the per-sequence draw state the engine uses
+    (host code of libti_b200.so, no device): a seeded top-p sequence sees the
+    reference's u_0, u_1, ...; a seeded top-k one sees u_0 at every step."""
+    import ti_b200 as ti
+    for seed in (0, 7, 2**63 + 5):
+        np.testing.assert_array_equal(ti.sampler_draws(ti.SAMPLE_TOP_P, 64, seed=seed),
+                                      oracle.sample_draws(seed, 64))
+        np.testing.assert_array_equal(ti.sampler_draws(ti.SAMPLE_TOP_K, 5, seed=seed),
+                                      np.full(5, oracle.sample_draws(seed, 1)[0], np.float32))
+    a = ti.sampler_draws(ti.SAMPLE_TOP_P, 16)  # std::random_device
+    b = ti.sampler_draws(ti.SAMPLE_TOP_P, 16)
+    assert (a >= 0).all() and (a < 1).all() and not np.array_equal(a, b)
+    with pytest.raises(ti.TiError):
+        ti.sampler_draws(ti.SAMPLE_TOP_K, 4, seed=1, k=0)
+    with pytest.raises(ti.TiError):
+        ti.sampler_draws(ti.SAMPLE_GREEDY, 4, seed=1)
+
+
+def test_engine_draws_drive_the_reference_sampler_ids(ref):
+    # the reference's TopP on one thread, fed the engine's draws through the oracle
+    x = (np.random.default_rng(4).standard_normal(2000) * 2).astype(np.float32)
+    import ti_b200 as ti
+    u = ti.sampler_draws(ti.SAMPLE_TOP_P, 12, seed=31, temperature=0.9, p=0.9)
+    assert ref(x, TOP_P, temperature=0.9, p=0.9, seed=31, n=12) == [oracle.sample_top_p(x, 0.9, 0.9, float(v))
+                                                                      for v in u]
