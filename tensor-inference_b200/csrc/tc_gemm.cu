@@ -909,11 +909,15 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
         p->s_off = p->w_off + (uint32_t)kTcBM * best_kbs * p->cb;
         const uint32_t raw = p->s_off + (uint32_t)kTcBM * best_kbs * 4;
         p->stage_bytes = (raw + 1023u) & ~1023u;
-        // two dequantised operand buffers when two raw stages still fit, else one
+        // two dequantised operand buffers when two raw stages still fit, else one;
+        // TI_TC_QBUF=1 asks for one (the freed 64 KB holds about two more raw stages:
+        // more weight bytes in flight, dequantisation no longer overlapping the MMA)
         p->n_abuf = 2;
         const size_t abuf = (size_t)best_kbs * kTcABytes;
         const TcSmem Lq = tc_smem_layout(0, 0, np, 0, 0);
         if (2 * abuf + 2 * ((size_t)p->stage_bytes + 16) > kTcSmemBudget - Lq.total) p->n_abuf = 1;
+        const char* qb = std::getenv("TI_TC_QBUF");
+        if (qb && std::atoi(qb) == 1) p->n_abuf = 1;
     }
     const size_t abuf_bytes = (size_t)p->n_abuf * best_kbs * kTcABytes;
     p->stages = (int)std::min<size_t>(12, (kTcSmemBudget - L0.total - abuf_bytes) / (p->stage_bytes + 16));
