@@ -60,7 +60,7 @@ def _oracle_schedule(kw, prompts, steps, seed, std, adapters=(), per_seq=None):
     return feeds, ref
 
 
-def _rank(rank, world, nid, kw, prompts, feeds, seed, std, q, mode, adapters, per_seq):
+def _rank(rank, world, nid, kw, prompts, feeds, seed, std, q, mode, adapters, per_seq, sampler=None):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     os.environ["TI_TP_ALLREDUCE"] = mode
     sys.path.insert(0, os.path.join(ROOT, "tensor-inference_b200"))
@@ -78,6 +78,9 @@ def _rank(rank, world, nid, kw, prompts, feeds, seed, std, q, mode, adapters, pe
             eng.adapter_init_synthetic(a, aseed, sa, sb)
         per = per_seq or [-1] * B
         sids = [eng.seq_create() for _ in prompts]
+        for sid in sids:
+            if sampler:
+                eng.set_sampler(sid, *sampler)  # every rank, every sequence: the same seeded sampler
         out_ids, out_logits = [], []
         ids0, lg0 = [], []
         for sid, p, ad in zip(sids, prompts, per):
@@ -101,13 +104,15 @@ def _rank(rank, world, nid, kw, prompts, feeds, seed, std, q, mode, adapters, pe
         os._exit(1)
 
 
-def _run_tp(kw, prompts, steps, tol, seed=0, std=0.02, world=2, mode="peer", adapters=(), per_seq=None):
+def _run_tp(kw, prompts, steps, tol, seed=0, std=0.02, world=2, mode="peer", adapters=(), per_seq=None,
+            sampler=None):
     _need(world)
     feeds, ref = _oracle_schedule(kw, prompts, steps, seed, std, adapters, per_seq)
     nid = ti.nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, world, nid, kw, prompts, feeds, seed, std, q, mode, list(adapters), per_seq)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, nid, kw, prompts, feeds, seed, std, q, mode, list(adapters),
+                                             per_seq, sampler)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -131,7 +136,18 @@ def _run_tp(kw, prompts, steps, tol, seed=0, std=0.02, world=2, mode="peer", ada
             if p.is_alive():
                 p.kill()
     ids = [res[r][1] for r in range(world)]
-    assert all(i == ids[0] for i in ids), "ranks disagree on greedy ids"
+    assert all(i == ids[0] for i in ids), "ranks disagree on the ids"
+    if sampler:
+        # each id: the exact form on rank 0's gathered logits with the sequence's draw
+        kind, temperature, p, k, sseed = sampler
+        u = oracle.sample_draws(sseed, steps + 1)
+        if kind == ti.SAMPLE_TOP_K:
+            u[:] = u[0]
+        for step, lb in enumerate(res[0][2]):
+            for b in range(len(prompts)):
+                assert ids[0][step][b] == oracle.sample_exact(lb[b], kind, temperature, p, k, float(u[step])), \
+                    (step, b)
+        return
     flips = 0
     for step, (lb, lf) in enumerate(zip(res[0][2], ref)):
         for b in range(len(prompts)):
@@ -179,3 +195,12 @@ def test_tp2_lora_tensor_core_batch():
     ads = [(8, 16.0, 0x7F, 31, 0.05, 0.05), (8, 8.0, 0x0F, 32, 0.05, 0.05)]
     prompts = [oracle.fill_ids(f"tm{b}", 2 + b % 3, b, SMALL["vocab"]) for b in range(12)]
     _run_tp(SMALL, prompts, steps=2, tol=2e-2, adapters=ads, per_seq=[b % 3 - 1 for b in range(12)])
+
+
+@pytest.mark.skipif(os.environ.get("TI_TEST_DEVICE_SAMPLING") != "1",
+                    reason="device sampler not yet run on a B200 (set TI_TEST_DEVICE_SAMPLING=1)")
+@pytest.mark.parametrize("sampler", [(ti.SAMPLE_TOP_P, 0.8, 0.9, 0, 17), (ti.SAMPLE_TOP_K, 1.0, 0.0, 25, 18)])
+def test_tp2_device_sampling(sampler):
+    # vocabulary-parallel logits gathered from both ranks, sampled identically on each
+    prompts = [oracle.fill_ids(f"ts{b}", n, b, SMALL["vocab"]) for b, n in enumerate((4, 9))]
+    _run_tp(SMALL, prompts, steps=3, tol=2e-2, std=0.5, sampler=sampler)
