@@ -273,8 +273,9 @@ bool meta_float(const ti_gguf* g, const std::string& key, double* v) {
     return true;
 }
 
-// head count of the q or k tensor for the row un-permutation (0 = none)
-int permute_heads(const ti_gguf* g, const std::string& gname) {
+// head count of the q or k tensor for the row un-permutation (0 = none); the
+// metadata value unchecked (the caller rejects counts that do not divide the rows)
+int64_t permute_heads(const ti_gguf* g, const std::string& gname) {
     if (g->arch != "llama") return 0;
     const bool q = gname.size() > 14 && gname.compare(gname.size() - 14, 14, ".attn_q.weight") == 0;
     const bool k = gname.size() > 14 && gname.compare(gname.size() - 14, 14, ".attn_k.weight") == 0;
@@ -282,7 +283,7 @@ int permute_heads(const ti_gguf* g, const std::string& gname) {
     int64_t nh = 0, nkv = 0;
     if (!meta_int(g, "llama.attention.head_count", &nh)) return 0;
     if (!meta_int(g, "llama.attention.head_count_kv", &nkv)) nkv = nh;
-    return (int)(q ? nh : nkv);
+    return q ? nh : nkv;
 }
 
 // source row of reference row r: heads of hd rows, HF row t * hd/2 + j of a head
@@ -482,25 +483,36 @@ ti_status ti_gguf_model_desc(const ti_gguf* g, ti_model_desc* d) {
     else if (a == "gemma") d->arch = TI_ARCH_GEMMA;
     else return fail(TI_ERR_UNSUPPORTED, "GGUF architecture '%s' (llama, qwen2 or gemma supported)", a.c_str());
     int64_t v = 0;
-    auto need = [&](const char* k, int* dst) -> ti_status {
-        TI_CHECK(meta_int(g, a + "." + k, &v), TI_ERR_INVALID, "GGUF metadata '%s.%s' missing", a.c_str(), k);
+    // an integer of the description: present (or `dflt` when given), within [lo, INT_MAX]
+    auto get = [&](const char* k, int* dst, int64_t lo, const int* dflt) -> ti_status {
+        if (!meta_int(g, a + "." + k, &v)) {
+            TI_CHECK(dflt, TI_ERR_INVALID, "GGUF metadata '%s.%s' missing", a.c_str(), k);
+            *dst = *dflt;
+            return TI_OK;
+        }
+        TI_CHECK(v >= lo && v <= 0x7fffffff, TI_ERR_INVALID, "GGUF metadata '%s.%s' = %lld out of range", a.c_str(),
+                 k, (long long)v);
         *dst = (int)v;
         return TI_OK;
     };
-    if (ti_status st = need("block_count", &d->n_layers)) return st;
-    if (ti_status st = need("embedding_length", &d->hidden)) return st;
-    if (ti_status st = need("feed_forward_length", &d->intermediate)) return st;
-    if (ti_status st = need("attention.head_count", &d->n_heads)) return st;
-    d->n_kv_heads = meta_int(g, a + ".attention.head_count_kv", &v) ? (int)v : d->n_heads;
-    TI_CHECK(d->n_heads > 0, TI_ERR_INVALID, "GGUF metadata: head_count must be positive");
-    d->head_dim = meta_int(g, a + ".attention.key_length", &v) ? (int)v : d->hidden / d->n_heads;
+    if (ti_status st = get("block_count", &d->n_layers, 1, nullptr)) return st;
+    if (ti_status st = get("embedding_length", &d->hidden, 1, nullptr)) return st;
+    if (ti_status st = get("feed_forward_length", &d->intermediate, 1, nullptr)) return st;
+    if (ti_status st = get("attention.head_count", &d->n_heads, 1, nullptr)) return st;
+    if (ti_status st = get("attention.head_count_kv", &d->n_kv_heads, 1, &d->n_heads)) return st;
+    const int hd_default = d->hidden / d->n_heads;
+    if (ti_status st = get("attention.key_length", &d->head_dim, 1, &hd_default)) return st;
     double f = 0;
     d->rms_eps = meta_float(g, a + ".attention.layer_norm_rms_epsilon", &f) ? (float)f : 1e-6f;
     d->rope_theta = meta_float(g, a + ".rope.freq_base", &f) ? (float)f : 10000.0f;
-    d->sliding_window = meta_int(g, a + ".attention.sliding_window", &v) ? (int)v : 0;
+    const int no_window = 0;
+    if (ti_status st = get("attention.sliding_window", &d->sliding_window, 0, &no_window)) return st;
     auto emb = g->by_name.find("token_embd.weight");
     TI_CHECK(emb != g->by_name.end(), TI_ERR_INVALID, "GGUF file has no token_embd.weight");
-    d->vocab = (int)g->tensors[emb->second].ne[1];
+    const int64_t vocab = g->tensors[emb->second].ne[1];
+    TI_CHECK(vocab >= 1 && vocab <= 0x7fffffff, TI_ERR_INVALID, "GGUF token_embd.weight: %lld rows",
+             (long long)vocab);
+    d->vocab = (int)vocab;
     d->qkv_bias = g->by_name.count("blk.0.attn_q.bias") ? 1 : 0;
     d->weight_format = TI_WFMT_BF16;
     auto q = g->by_name.find("blk.0.attn_q.weight");
@@ -554,10 +566,11 @@ ti_status ti_gguf_read(const ti_gguf* g, int i, int dtype, void* out, size_t byt
     TI_CHECK(t.bytes > 0, TI_ERR_UNSUPPORTED, "GGUF tensor '%s': ggml type %d not supported (f32, f16, bf16, q4_0, q8_0)",
              t.name.c_str(), t.type);
     const int64_t cols = t.ne[0], rows = t.n_dims >= 2 ? t.ne[1] * t.ne[2] * t.ne[3] : 1;
-    const int heads = permute_heads(g, t.name);
+    const int64_t heads = permute_heads(g, t.name);
     const int64_t hd = heads > 0 ? rows / heads : 0;
-    TI_CHECK(heads == 0 || (rows % heads == 0 && hd % 2 == 0), TI_ERR_INVALID,
-             "GGUF tensor '%s': %lld rows do not split into %d heads", t.name.c_str(), (long long)rows, heads);
+    TI_CHECK(heads == 0 || (heads > 0 && rows % heads == 0 && hd >= 2 && hd % 2 == 0), TI_ERR_INVALID,
+             "GGUF tensor '%s': %lld rows do not split into %lld heads of an even size", t.name.c_str(),
+             (long long)rows, (long long)heads);
     const size_t src_row = type_bytes(t.type, cols);
     auto src_of = [&](int64_t r) { return t.data + (size_t)(heads ? source_row(r, hd) : r) * src_row; };
     if (dtype == TI_DTYPE_BF16) {

@@ -441,7 +441,7 @@ class Gguf:
         data, nbytes = C.c_void_p(), C.c_size_t()
         check(lib().ti_gguf_tensor_info(self.h, i, C.byref(name), C.byref(t), C.byref(nd), dims, C.byref(data),
                                         C.byref(nbytes)))
-        return dict(name=name.value.decode(), type=t.value, dims=tuple(dims[:nd.value]), bytes=nbytes.value)
+        return dict(name=name.value.decode(errors="replace"), type=t.value, dims=tuple(dims[:nd.value]), bytes=nbytes.value)
 
     def find(self, name):
         i = C.c_int()
@@ -461,7 +461,7 @@ class Gguf:
     def meta_str(self, key):
         v = C.c_char_p()
         check(lib().ti_gguf_meta_string(self.h, key.encode(), C.byref(v)))
-        return v.value.decode()
+        return v.value.decode(errors="replace")
 
     def meta_array_len(self, key):
         v = C.c_int64()
@@ -481,7 +481,7 @@ class Gguf:
     def reference_name(self, i):
         buf = C.create_string_buffer(256)
         check(lib().ti_gguf_reference_name(self.h, i, buf, len(buf)))
-        return buf.value.decode()
+        return buf.value.decode(errors="replace")
 
     def read(self, i, dtype=DTYPE_BF16):
         """tensor i in the reference's row order: bf16 bits [rows, cols] (uint16) or
