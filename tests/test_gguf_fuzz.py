@@ -12,8 +12,11 @@ writes extreme values (negative, zero, 2^31 - 1) into each integer of the model
 description.  Host-only."""
 import multiprocessing as mp
 import os
+import subprocess
+import sys
 
 import numpy as np
+import pytest
 
 from gguf_writer import (ARR, F32, GGML_BF16, GGML_F16, GGML_F32, GGML_Q4_0, GGML_Q8_0, I32, STR, U32, write)
 
@@ -107,19 +110,37 @@ def _mutate(rng, blob):
     return bytes(b)
 
 
-def _worker(tmp, progress):
-    import sys
+def _import_ti(lib_path=None):
+    """ti_b200, its entry points bound to `lib_path` when given (a sanitizer
+    build of the reader holds the ti_gguf_* entries and the error state only)"""
+    import ctypes as C
 
     sys.path.insert(0, os.path.join(os.path.dirname(HERE), "tensor-inference_b200"))
     import ti_b200 as ti
+
+    if lib_path:
+        L = C.CDLL(lib_path)
+        for name, (res, args) in ti._SIGS.items():
+            try:
+                f = getattr(L, name)
+            except AttributeError:
+                continue
+            f.restype = res
+            f.argtypes = args
+        ti._lib = L
+    return ti
+
+
+def _worker(tmp, progress, lib_path=None, n_cases=N_CASES, seed=2024):
+    ti = _import_ti(lib_path)
 
     src = os.path.join(tmp, "valid.gguf")
     _valid_file(src)
     blob = open(src, "rb").read()
     _exercise(ti, src)
-    rng = np.random.default_rng(2024)
+    rng = np.random.default_rng(seed)
     path = os.path.join(tmp, "case.gguf")
-    for case in range(N_CASES):
+    for case in range(n_cases):
         data = _mutate(rng, blob)
         with open(path, "wb") as f:
             f.write(data)
@@ -130,11 +151,8 @@ def _worker(tmp, progress):
         f.write("done")
 
 
-def _worker_meta(tmp, progress):
-    import sys
-
-    sys.path.insert(0, os.path.join(os.path.dirname(HERE), "tensor-inference_b200"))
-    import ti_b200 as ti
+def _worker_meta(tmp, progress, lib_path=None):
+    ti = _import_ti(lib_path)
 
     path = os.path.join(tmp, "meta.gguf")
     for key in INT_KEYS:
@@ -168,3 +186,40 @@ def test_extreme_metadata_values_fail_cleanly(tmp_path):
 
 def test_corrupted_files_fail_cleanly(tmp_path):
     _run(_worker, tmp_path)
+
+
+def _sanitizer_runtime():
+    libs = []
+    for name in ("libasan.so", "libubsan.so"):
+        r = subprocess.run(["gcc", "-print-file-name=" + name], capture_output=True, text=True)
+        path = r.stdout.strip()
+        if r.returncode != 0 or not os.path.isabs(path) or not os.path.exists(path):
+            return None
+        libs.append(path)
+    return ":".join(libs)
+
+
+def test_sanitized_reader(tmp_path):
+    """gguf.cpp built with AddressSanitizer + UBSan (out-of-bounds reads of the
+    mapping, integer overflow, division by zero abort the child) over the
+    metadata sweep and 5000 mutated files."""
+    preload = _sanitizer_runtime()
+    if not preload:
+        pytest.skip("gcc sanitizer runtimes not available")
+    root = os.path.dirname(HERE)
+    csrc = os.path.join(root, "tensor-inference_b200", "csrc")
+    lib = str(tmp_path / "libgguf_asan.so")
+    cmd = ["g++", "-std=c++17", "-O1", "-g", "-fsanitize=address,undefined", "-fno-sanitize-recover=all",
+           "-fno-omit-frame-pointer", "-fPIC", "-shared", "-I/usr/local/cuda/include", "-I" + csrc,
+           "-I" + os.path.join(root, "include"), os.path.join(csrc, "gguf.cpp"), os.path.join(csrc, "api.cpp"),
+           os.path.join(HERE, "gguf_asan_stub.cpp"), "-o", lib, "-L/usr/local/cuda/lib64", "-lcudart"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]
+    code = (f"import sys; sys.path.insert(0, {HERE!r}); import test_gguf_fuzz as T; "
+            f"T._worker_meta({str(tmp_path)!r}, {str(tmp_path / 'p1')!r}, {lib!r}); "
+            f"T._worker({str(tmp_path)!r}, {str(tmp_path / 'p2')!r}, {lib!r}, 5000, 7)")
+    env = dict(os.environ, LD_PRELOAD=preload, ASAN_OPTIONS="detect_leaks=0:halt_on_error=1",
+               UBSAN_OPTIONS="halt_on_error=1:print_stacktrace=1")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=900)
+    last = [open(tmp_path / f).read() if (tmp_path / f).exists() else "none" for f in ("p1", "p2")]
+    assert r.returncode == 0 and last == ["done", "done"], (last, r.stderr[-3000:])
