@@ -85,3 +85,125 @@ def test_rejects_bad_options():
         with pytest.raises(ti.TiError) as ei:
             ti.Router(None, **args)
         assert ei.value.status == ti.TI_ERR_INVALID
+
+
+# ---------------------------------------------------------------- model-based
+class _Policy:
+    """The router's policy restated from its specification (ti_b200.h: router
+    pool + scheduler), NULL-engine form: per-sequence hysteresis, LRU pool with
+    a budget, step adapters never evicted, speculative prefetches sparing live
+    sequences' adapters and giving up silently when nothing can go."""
+
+    def __init__(self, max_resident, prefetch_after, switch_after):
+        self.max, self.pf, self.sw = max_resident, prefetch_after, switch_after
+        self.lru, self.seqs, self.in_use, self.actions = [], {}, {}, []
+        self.stats = dict(observations=0, switches=0, prefetches=0, evictions=0, hits=0)
+
+    def _evict_one(self, keep, spare_live):
+        for a in reversed(self.lru):
+            if a in keep or (spare_live and self.in_use.get(a, 0) > 0):
+                continue
+            self.lru.remove(a)
+            self.actions.append((E, a))
+            self.stats["evictions"] += 1
+            return
+        raise MemoryError
+
+    def _ensure(self, a, keep, spare_live):
+        keep = keep | {a}
+        if a in self.lru:
+            self.lru.remove(a)
+            self.lru.insert(0, a)
+            self.stats["hits"] += 1
+        else:
+            while len(self.lru) >= self.max:
+                self._evict_one(keep, spare_live)
+            self.lru.insert(0, a)
+            self.actions.append((P, a))
+            self.stats["prefetches"] += 1
+        while len(self.lru) > self.max:
+            self._evict_one(keep, spare_live)
+
+    def _use(self, frm, to):
+        if frm >= 0 and frm in self.in_use:
+            self.in_use[frm] -= 1
+            if self.in_use[frm] == 0:
+                del self.in_use[frm]
+        if to >= 0:
+            self.in_use[to] = self.in_use.get(to, 0) + 1
+
+    def observe(self, seq, c):
+        self.stats["observations"] += 1
+        s = self.seqs.setdefault(seq, dict(current=-2, candidate=-2, lead=0))
+        if s["current"] == -2:
+            s.update(current=c, candidate=c, lead=0)
+            self._use(-1, c)
+            return c
+        if c == s["current"]:
+            s.update(candidate=c, lead=0)
+        else:
+            if c == s["candidate"]:
+                s["lead"] += 1
+            else:
+                s.update(candidate=c, lead=1)
+            if s["lead"] == self.pf and c >= 0:
+                try:
+                    self._ensure(c, set(), True)
+                except MemoryError:
+                    pass
+            if s["lead"] >= self.sw:
+                self._use(s["current"], c)
+                s.update(current=c, lead=0)
+                self.stats["switches"] += 1
+        return s["current"]
+
+    def prepare(self, adapters):
+        step = sorted({a for a in adapters if a >= 0})
+        if len(step) > self.max:
+            raise MemoryError
+        for a in step:
+            self._ensure(a, set(step), False)
+
+    def forget(self, seq):
+        s = self.seqs.pop(seq, None)
+        if s is not None:
+            self._use(s["current"], -1)
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_router_matches_its_policy_model(seed):
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    max_res = int(rng.integers(1, 5))
+    pf = int(rng.integers(1, 4))
+    sw = pf + int(rng.integers(0, 3))
+    r = ti.Router(None, max_resident=max_res, prefetch_after=pf, switch_after=sw)
+    m = _Policy(max_res, pf, sw)
+    for step in range(3000):
+        op = rng.random()
+        if op < 0.7:
+            seq, c = int(rng.integers(0, 6)), int(rng.integers(-1, 7))
+            assert r.observe(seq, c) == m.observe(seq, c), step
+        elif op < 0.95:
+            ads = [int(a) for a in rng.integers(-1, 7, size=int(rng.integers(0, max_res + 2)))]
+            try:
+                m.prepare(ads)
+                want = None
+            except MemoryError:
+                want = ti.TI_ERR_OOM
+            if want is None:
+                r.prepare(ads)
+            else:
+                with pytest.raises(ti.TiError) as ei:
+                    r.prepare(ads)
+                assert ei.value.status == want, step
+        else:
+            seq = int(rng.integers(0, 6))
+            r.forget(seq)
+            m.forget(seq)
+        assert r.actions() == m.actions, step
+        m.actions = []
+        assert r.resident() == m.lru, step
+        assert len(m.lru) <= max_res
+    assert r.stats() == m.stats
