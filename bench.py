@@ -362,6 +362,49 @@ def measure_pkm(ti, torch, stream, iters=20):
             "gemm_equiv_tflops": round(gemm_flop / (ms * 1e-3) / 1e12, 2), "fp32_instr_per_s": instr / (ms * 1e-3)}
 
 
+def timeline_summary(trace_path, steps):
+    """Kernel events of a torch.profiler (CUPTI) trace of graph replays: per
+    kernel, launches, mean duration and mean contribution to the step.  With
+    programmatic dependent launch a kernel starts while its predecessor runs,
+    so durations overlap; every instant the GPU is busy is charged to the
+    running kernel that finishes first (the one the chain is waiting on), so the
+    contributions add up to the busy time and busy + idle = the span."""
+    import heapq
+    import json
+    from collections import defaultdict
+
+    with open(trace_path) as f:
+        ev = [e for e in json.load(f)["traceEvents"] if e.get("cat") == "kernel" and e.get("ph") == "X"]
+    if not ev:
+        return ["timeline: no kernel events recorded"]
+    iv = sorted((e["ts"], e["ts"] + e["dur"], e["name"].split("(")[0]) for e in ev)
+    span = max(b for _, b, _ in iv) - iv[0][0]
+    contrib = defaultdict(float)
+    times = sorted({t for a, b, _ in iv for t in (a, b)})
+    active, nxt, busy = [], 0, 0.0
+    for t0, t1 in zip(times, times[1:]):
+        while nxt < len(iv) and iv[nxt][0] <= t0:
+            heapq.heappush(active, (iv[nxt][1], nxt))
+            nxt += 1
+        while active and active[0][0] <= t0:
+            heapq.heappop(active)
+        if active:
+            contrib[iv[active[0][1]][2]] += t1 - t0
+            busy += t1 - t0
+    count, dur = defaultdict(int), defaultdict(float)
+    for a, b, name in iv:
+        count[name] += 1
+        dur[name] += b - a
+    lines = [f"timeline: {len(iv)} kernels over {steps} steps, {span / steps:.1f} us/step, "
+             f"idle {(span - busy) / steps:.1f} us/step",
+             "kernel | launches/step | mean duration us | mean contribution us | contribution us/step | share"]
+    for name in sorted(count, key=lambda k: -contrib[k]):
+        n = count[name]
+        lines.append(f"{name} | {n / steps:.1f} | {dur[name] / n:.2f} | {contrib[name] / n:.2f} | "
+                     f"{contrib[name] / steps:.1f} | {contrib[name] / max(span, 1e-9):.3f}")
+    return lines
+
+
 def run_profile(args):
     """Short, self-contained workload for ncu: a few decode steps (or repeated
     launches of one kernel) of the 8B shape with `--layers` layers after a
@@ -408,7 +451,17 @@ def run_profile(args):
         eng.decode_device(ts.cuda_stream)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    if args.kernel is None:
+    if args.timeline:
+        # in-graph kernel timeline through the PyTorch profiler's CUPTI tracing
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for _ in range(args.steps):
+                eng.decode_device(ts.cuda_stream)
+            torch.cuda.synchronize()
+        prof.export_chrome_trace(args.timeline)
+        print("\n".join(timeline_summary(args.timeline, args.steps)))
+    elif args.kernel is None:
         # NVTX range "step" around the first timed step (ncu --nvtx --nvtx-include "step/")
         for i in range(args.steps):
             if i == 0:
@@ -424,7 +477,7 @@ def run_profile(args):
         torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     dt = (time.perf_counter() - t0) / args.steps
-    eng.unbind(args.warmup + (args.steps if args.kernel is None else 0), ts.cuda_stream)
+    eng.unbind(args.warmup + (args.steps if args.kernel is None or args.timeline else 0), ts.cuda_stream)
     eng.check()
     print(f"profile: layers={args.layers} batch={args.batch} kernel={args.kernel} {dt * 1e3:.3f} ms/iter")
     eng.close()
@@ -565,6 +618,9 @@ def main():
     ap.add_argument("--preset", default="llama3_8b", help="profile: model shape (ti_b200.PRESETS)")
     ap.add_argument("--adapters", type=int, default=0, help="profile: LoRA adapters on all projections")
     ap.add_argument("--lora-rank", type=int, default=64, help="profile: rank of those adapters")
+    ap.add_argument("--timeline", default=None,
+                    help="profile: trace the decode steps with the PyTorch profiler (CUPTI), write the Chrome trace "
+                         "here and print each kernel's in-graph duration, chain contribution and the idle gaps")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank = int(os.environ.get("RANK", "0"))
