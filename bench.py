@@ -519,7 +519,15 @@ def run_ours(args, rank, world):
     with ClockSampler(dev) as clk:
         r1 = measure_batch(ti, torch, eng, 1, args.steps, args.warmup, stream, peak, world=world)
     roof = kernel_roofline(ti, torch, eng, stream, peak)
-    pkm = measure_pkm(ti, torch, stream) if world == 1 else None
+
+    def extra(fn, *a, **kw):
+        # an extra leg that fails reports its error in the line; the headline stands
+        try:
+            return fn(*a, **kw)
+        except Exception as exc:  # noqa: BLE001 - any failure of an extra leg is reported, not raised
+            return {"error": f"{type(exc).__name__}: {exc}"[:300]}
+
+    pkm = extra(measure_pkm, ti, torch, stream) if world == 1 else None
     r32 = None
     if args.b32:
         r32 = measure_batch(ti, torch, eng, 32, max(2, args.steps // 4), min(args.warmup, 3), stream, peak,
@@ -527,7 +535,7 @@ def run_ours(args, rank, world):
     qwen = None
     if args.qwen and world == 1:
         eng.close()  # the 8B engine's 15 GB is not needed for the Qwen legs
-        qwen = {name: measure_qwen_lora(ti, torch, stream, peak, wf, max(4, args.steps // 4), 3, dev)
+        qwen = {name: extra(measure_qwen_lora, ti, torch, stream, peak, wf, max(4, args.steps // 4), 3, dev)
                 for name, wf in (("bf16", ti.WFMT_BF16), ("q4_0", ti.WFMT_Q4_0))}
     r70 = None
     if args.big and world > 1:
@@ -582,10 +590,12 @@ def run_ours(args, rank, world):
             line["qwen7b_lora_b8"] = dict(qwen, config="Qwen2.5-7B shape, rank-16 LoRA q/k/v/o, batch 8, 256-token prompt")
         if r70:
             line["llama70b_tp_b64_lora"] = r70
-        if pkm:
+        if pkm and "error" not in pkm:
             # FP32 issue peak: 148 SMs x 128 lanes x SM clock during the run
             clk = (line["clocks"].get("sm_mhz") or 1965.0) * 1e6
             pkm["fp32_pipe_frac"] = round(pkm.pop("fp32_instr_per_s") / (148 * 128 * clk), 4)
+            line["pkm"] = pkm
+        elif pkm:
             line["pkm"] = pkm
         if cb:
             line["cpu_baseline"] = cb
