@@ -278,8 +278,11 @@ typedef struct ti_sampling {
 /* The sampler of the ids ti_engine_decode / ti_engine_prefill(_chunked) return
  * for this sequence from now on; NULL or TI_SAMPLE_GREEDY restores greedy.
  * Under tensor parallelism every rank sets the same seeded sampler (ranks then
- * draw identical ids); a bound device chain (ti_engine_bind) accepts greedy
- * sequences only.  ti_seq_create starts greedy; ti_seq_reset keeps the sampler. */
+ * draw identical ids).  A bound device chain (ti_engine_bind, one GPU) samples
+ * too: bind draws every step the sequence's reserved pages allow ahead, from a
+ * copy of its engine, and ti_engine_unbind advances the engine past the steps
+ * taken, so the ids equal those of step-by-step decoding.  ti_seq_create starts
+ * greedy; ti_seq_reset keeps the sampler. */
 ti_status ti_engine_seq_set_sampler(ti_engine* e, int seq_id, const ti_sampling* s);
 /* The same device sampler on caller-owned rows: logits [rows, vocab] bf16 and
  * out [rows] int32 in device memory; params and draws (uniform in [0, 1)) are
@@ -329,8 +332,9 @@ ti_status ti_engine_decode(ti_engine* e, int batch, const int32_t* seq_ids, cons
 
 /* Device-resident chained decode: bind `batch` sequences once, then every
  * ti_engine_decode_device call runs one step whose input tokens are the
- * previous step's greedy ids, all on the device (no host synchronisation).
- * Sequences must have pages reserved (ti_seq_reserve) for the steps run. */
+ * previous step's ids (greedy, or drawn by the sequence's sampler), all on the
+ * device (no host synchronisation).  Sequences must have pages reserved
+ * (ti_seq_reserve) for the steps run. */
 ti_status ti_engine_bind(ti_engine* e, int batch, const int32_t* seq_ids, const int32_t* first_tokens,
                          const int32_t* adapter_ids);
 ti_status ti_engine_decode_device(ti_engine* e, void* stream);

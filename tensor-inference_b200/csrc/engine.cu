@@ -124,6 +124,10 @@ struct ti_engine {
     // device sampling (allocated at the first sampled step): per-row parameters, value histograms
     SampleRow *d_srows = nullptr, *h_srows = nullptr;
     uint32_t* shist = nullptr;
+    // device chains that sample: pre-generated draws [max_batch][draw_cap] and per-row counters
+    float* d_draws = nullptr;
+    int32_t* d_draw_ctr = nullptr;
+    int draw_cap = 0;
     int* err = nullptr;
     float *part_o = nullptr, *part_ml = nullptr;
     unsigned int* counters = nullptr;
@@ -142,6 +146,7 @@ struct ti_engine {
 
     int bound_batch = 0;
     bool bound_lora = false;
+    bool bound_sample = false;
     std::vector<int> bound_seqs;
 
     // ---- LoRA adapter pool (padded rank R, S slots; padding rows/cols are zero)
@@ -947,19 +952,41 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
     }
 }
 
-ti_status enqueue_step(ti_engine* e, int B, cudaStream_t s, int* launches, bool lora, bool prefill) {
+// sample: a device chain with top-p / top-k rows; after the LM head (whose greedy
+// argmax already advanced every row) the sampler replaces the sampled rows' ids
+// in `out` and in the chain's next tokens, each with its row's next pre-generated draw
+ti_status enqueue_step(ti_engine* e, int B, cudaStream_t s, int* launches, bool lora, bool prefill,
+                       bool sample = false) {
     if (ti_status st = enqueue_kernel(e, B, kKEmbed, 0, s, launches, lora)) return st;
     for (int li = 0; li < e->d.n_layers; ++li)
         for (int k : {kKQkv, kKAttn, kKO, kKGateUp, kKDown})
             if (ti_status st = enqueue_kernel(e, B, k, li, s, launches, lora, prefill)) return st;
-    return enqueue_kernel(e, B, kKLmHead, 0, s, launches, lora);
+    if (ti_status st = enqueue_kernel(e, B, kKLmHead, 0, s, launches, lora)) return st;
+    if (!sample) return TI_OK;
+    TI_CHECK(e->tp.tp == 1 && e->d_draws && e->d_srows, TI_ERR_STATE, "sampled device chain: buffers not set up");
+    SampleArgs a;
+    a.logits = e->logits;
+    a.vocab = e->V;
+    a.seg = e->V;
+    a.row_stride = (size_t)e->V;
+    a.rows = e->d_srows;
+    a.hist = e->shist;
+    a.out = e->out;
+    a.err = e->err;
+    a.draws = e->d_draws;
+    a.draw_cap = e->draw_cap;
+    a.draw_ctr = e->d_draw_ctr;
+    a.chain_tokens = e->dd_tokens();
+    TI_CUDA(sample_launch(a, B, s));
+    if (launches) ++*launches;
+    return TI_OK;
 }
 
-ti_status capture_step(ti_engine* e, int B, bool lora, bool prefill, GraphEntry* out) {
+ti_status capture_step(ti_engine* e, int B, bool lora, bool prefill, bool sample, GraphEntry* out) {
     cudaStream_t s = e->cap;
     int launches = 0;
     TI_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-    ti_status st = enqueue_step(e, B, s, &launches, lora, prefill);
+    ti_status st = enqueue_step(e, B, s, &launches, lora, prefill, sample);
     cudaGraph_t graph = nullptr;
     cudaError_t ce = cudaStreamEndCapture(s, &graph);
     if (st) {
@@ -977,14 +1004,14 @@ ti_status capture_step(ti_engine* e, int B, bool lora, bool prefill, GraphEntry*
     return TI_OK;
 }
 
-// one graph per (batch size, LoRA on/off, prefill)
-ti_status get_graph(ti_engine* e, int B, bool lora, GraphEntry** g, bool prefill = false) {
+// one graph per (batch size, LoRA on/off, prefill, sampled device chain)
+ti_status get_graph(ti_engine* e, int B, bool lora, GraphEntry** g, bool prefill = false, bool sample = false) {
     lora = lora && e->S > 0;
-    const int key = (B * 2 + (lora ? 1 : 0)) * 2 + (prefill ? 1 : 0);
+    const int key = ((B * 2 + (lora ? 1 : 0)) * 2 + (prefill ? 1 : 0)) * 2 + (sample ? 1 : 0);
     auto it = e->graphs.find(key);
     if (it == e->graphs.end()) {
         GraphEntry ge;
-        if (ti_status st = capture_step(e, B, lora, prefill, &ge)) return st;
+        if (ti_status st = capture_step(e, B, lora, prefill, sample, &ge)) return st;
         it = e->graphs.emplace(key, ge).first;
         if (e->tp.tp > 1 && e->comm) {
             // Every rank builds a new graph at the same step; capture, instantiation
@@ -1059,24 +1086,37 @@ ti_status read_err(ti_engine* e, int32_t word) {
 // Replace the argmax of every sampled row (a sequence with a top-p / top-k
 // sampler; in a prefill step only the last entry's id is returned) by the
 // device sampler's pick.  `logits` holds the rows as sample_launch indexes them.
+// the sampler's row parameters and histograms (first sampled step or chain)
+ti_status sample_buffers(ti_engine* e) {
+    const int MB = e->o.max_batch;
+    if (e->d_srows) return TI_OK;
+    TI_CHECK(dalloc_t(e, &e->shist, sample_scratch_bytes(MB) / 4, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
+             ti_last_error());
+    TI_CUDA(cudaMallocHost(&e->h_srows, (size_t)MB * sizeof(SampleRow)));
+    TI_CHECK(dalloc_t(e, &e->d_srows, (size_t)MB, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
+    return TI_OK;
+}
+
+// a sequence's sampler as the kernel's row parameters (draw filled by the caller)
+SampleRow sample_row(const SeqState& s) {
+    SampleRow r{};
+    const ti_sampling& c = s.smp.cfg;
+    if (c.kind == TI_SAMPLE_GREEDY) return r;
+    r.kind = c.kind == TI_SAMPLE_TOP_P ? kSampleTopP : kSampleTopK;
+    r.temperature = c.temperature;
+    r.p = c.p;
+    r.k = (int32_t)std::min<uint32_t>(c.k, 0x7fffffffu);
+    return r;
+}
+
 ti_status sample_rows(ti_engine* e, int B, const int32_t* seq_ids, bool prefill, const uint16_t* logits, int seg,
                       size_t seg_stride, size_t row_stride, cudaStream_t stream) {
-    const int MB = e->o.max_batch;
-    if (!e->d_srows) {
-        TI_CHECK(dalloc_t(e, &e->d_srows, (size_t)MB, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
-        TI_CHECK(dalloc_t(e, &e->shist, sample_scratch_bytes(MB) / 4, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
-                 ti_last_error());
-        TI_CUDA(cudaMallocHost(&e->h_srows, (size_t)MB * sizeof(SampleRow)));
-    }
+    if (ti_status st = sample_buffers(e)) return st;
     for (int b = 0; b < B; ++b) {
-        SampleRow r{};
         SeqState& s = e->seqs[seq_ids[b]];
-        const ti_sampling& c = s.smp.cfg;
-        if ((!prefill || b == B - 1) && c.kind != TI_SAMPLE_GREEDY) {
-            r.kind = c.kind == TI_SAMPLE_TOP_P ? kSampleTopP : kSampleTopK;
-            r.temperature = c.temperature;
-            r.p = c.p;
-            r.k = (int32_t)std::min<uint32_t>(c.k, 0x7fffffffu);
+        SampleRow r{};
+        if ((!prefill || b == B - 1) && s.smp.cfg.kind != TI_SAMPLE_GREEDY) {
+            r = sample_row(s);
             r.u = s.smp.next();
         }
         e->h_srows[b] = r;
@@ -1566,8 +1606,8 @@ ti_status ti_engine_bind(ti_engine* e, int B, const int32_t* seq_ids, const int3
         if (ti_status st = seq_check(e, seq_ids[b])) return st;
         TI_CHECK(first_tokens[b] >= 0 && first_tokens[b] < e->V, TI_ERR_INVALID, "token out of range");
         const SeqState& s = e->seqs[seq_ids[b]];
-        TI_CHECK(s.smp.cfg.kind == TI_SAMPLE_GREEDY, TI_ERR_UNSUPPORTED,
-                 "sequence %d samples top-p / top-k; a bound device chain feeds greedy ids only", seq_ids[b]);
+        TI_CHECK(s.smp.cfg.kind == TI_SAMPLE_GREEDY || e->tp.tp == 1, TI_ERR_UNSUPPORTED,
+                 "sequence %d samples top-p / top-k: a bound device chain samples on one GPU only", seq_ids[b]);
         TI_CHECK((int)s.pages.size() * kPageTokens > s.len, TI_ERR_STATE,
                  "sequence %d has no reserved page for its next token (ti_seq_reserve)", seq_ids[b]);
         h[4 + b] = first_tokens[b];
@@ -1577,11 +1617,38 @@ ti_status ti_engine_bind(ti_engine* e, int B, const int32_t* seq_ids, const int3
     }
     bool any_lora = false;
     if (ti_status st = adapters_ready(e, B, adapter_ids, (cudaStream_t)0, &any_lora)) return st;
+    bool any_sample = false;
+    for (int b = 0; b < B; ++b) any_sample |= e->seqs[seq_ids[b]].smp.cfg.kind != TI_SAMPLE_GREEDY;
+    if (any_sample) {
+        // every step the chain can take (up to the sequence's reserved pages) gets its
+        // draw now, from a copy of the sequence's engine; unbind advances the engine itself
+        if (ti_status st = sample_buffers(e)) return st;
+        if (!e->d_draws) {
+            e->draw_cap = e->o.max_seq_len;
+            TI_CHECK(dalloc_t(e, &e->d_draws, (size_t)MB * e->draw_cap, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
+                     ti_last_error());
+            TI_CHECK(dalloc_t(e, &e->d_draw_ctr, (size_t)MB, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
+                     ti_last_error());
+        }
+        std::vector<float> draws((size_t)B * e->draw_cap, 0.0f);
+        for (int b = 0; b < B; ++b) {
+            const SeqState& s = e->seqs[seq_ids[b]];
+            e->h_srows[b] = sample_row(s);
+            if (s.smp.cfg.kind == TI_SAMPLE_GREEDY) continue;
+            SamplerDraws ahead = s.smp;
+            const int n = std::min(e->draw_cap, (int)s.pages.size() * kPageTokens - s.len);
+            for (int i = 0; i < n; ++i) draws[(size_t)b * e->draw_cap + i] = ahead.next();
+        }
+        TI_CUDA(cudaMemcpy(e->d_srows, e->h_srows, (size_t)B * sizeof(SampleRow), cudaMemcpyHostToDevice));
+        TI_CUDA(cudaMemcpy(e->d_draws, draws.data(), draws.size() * 4, cudaMemcpyHostToDevice));
+        TI_CUDA(cudaMemset(e->d_draw_ctr, 0, (size_t)MB * 4));
+    }
     GraphEntry* gr = nullptr;
-    if (ti_status st = get_graph(e, B, any_lora, &gr)) return st;
+    if (ti_status st = get_graph(e, B, any_lora, &gr, false, any_sample)) return st;
     TI_CUDA(cudaMemcpy(e->d_desc, h, (size_t)e->desc_ints * 4, cudaMemcpyHostToDevice));
     e->bound_batch = B;
     e->bound_lora = any_lora;
+    e->bound_sample = any_sample;
     e->bound_seqs.assign(seq_ids, seq_ids + B);
     return TI_OK;
 }
@@ -1589,7 +1656,7 @@ ti_status ti_engine_bind(ti_engine* e, int B, const int32_t* seq_ids, const int3
 ti_status ti_engine_decode_device(ti_engine* e, void* stream) {
     TI_CHECK(e && e->bound_batch > 0, TI_ERR_STATE, "engine not bound");
     GraphEntry* g = nullptr;
-    if (ti_status st = get_graph(e, e->bound_batch, e->bound_lora, &g)) return st;
+    if (ti_status st = get_graph(e, e->bound_batch, e->bound_lora, &g, false, e->bound_sample)) return st;
     TI_CUDA(cudaGraphLaunch(g->exec, (cudaStream_t)stream));
     return TI_OK;
 }
@@ -1606,8 +1673,12 @@ ti_status ti_engine_unbind(ti_engine* e, int steps, int32_t* last_ids, void* str
         SeqState& s = e->seqs[e->bound_seqs[b]];
         s.len = std::min(s.len + steps, e->o.max_seq_len);
         if (last_ids) last_ids[b] = e->h_out[b];
+        // a top-p sequence's engine moves past the draws its chain consumed
+        if (e->bound_sample && s.smp.cfg.kind == TI_SAMPLE_TOP_P)
+            for (int i = 0; i < steps; ++i) s.smp.next();
     }
     e->bound_batch = 0;
+    e->bound_sample = false;
     e->bound_seqs.clear();
     return read_err(e, e->h_out[MB]);
 }

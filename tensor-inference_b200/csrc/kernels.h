@@ -294,6 +294,12 @@ struct SampleArgs {
     uint32_t* hist = nullptr;         // sample_scratch_bytes(nb)
     int32_t* out = nullptr;           // [nb] sampled ids
     int* err = nullptr;               // error bits
+    // device-resident decode chains: row b's draw is draws[b * draw_cap + draw_ctr[b]]
+    // (then draw_ctr[b] advances) instead of rows[b].u, and the id also goes to chain_tokens[b]
+    const float* draws = nullptr;
+    int draw_cap = 0;
+    int32_t* draw_ctr = nullptr;
+    int32_t* chain_tokens = nullptr;
 };
 size_t sample_scratch_bytes(int nb);
 cudaError_t sample_launch(const SampleArgs& a, int nb, cudaStream_t s);

@@ -243,7 +243,13 @@ __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(SampleArgs a) {
     __syncthreads();
 
     // 4. the pick: a logit value and the rank of the token among its ids
-    u128 r = ceil_mul(prm.u, sh.wcut);
+    float u = prm.u;
+    int ctr = 0;
+    if (a.draws) {  // a device chain: the row's next pre-generated draw
+        ctr = a.draw_ctr[b];
+        u = a.draws[(size_t)b * a.draw_cap + min(max(ctr, 0), a.draw_cap - 1)];
+    }
+    u128 r = ceil_mul(u, sh.wcut);
     if (r < 1) r = 1;
     if (tid == 0) {
         sh.pick_key = kmax;
@@ -295,8 +301,16 @@ __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(SampleArgs a) {
     }
     __syncthreads();
     if (tid == 0) {
-        if (sh.pick_id >= 0) a.out[b] = sh.pick_id;
-        else atomicOr(a.err, kErrBadIndex);  // not reached: the picked value holds >= rank ids
+        if (sh.pick_id >= 0) {
+            a.out[b] = sh.pick_id;
+            if (a.chain_tokens) a.chain_tokens[b] = sh.pick_id;
+        } else {
+            atomicOr(a.err, kErrBadIndex);  // not reached: the picked value holds >= rank ids
+        }
+        if (a.draws) {
+            if (ctr < 0 || ctr >= a.draw_cap) atomicOr(a.err, kErrBadIndex);  // ran past its pre-drawn steps
+            a.draw_ctr[b] = ctr + 1;
+        }
     }
 }
 
@@ -306,7 +320,7 @@ size_t sample_scratch_bytes(int nb) { return (size_t)nb * kKeys * sizeof(uint32_
 
 cudaError_t sample_launch(const SampleArgs& a, int nb, cudaStream_t s) {
     if (nb <= 0) return cudaSuccess;
-    if (a.vocab <= 0 || a.seg <= 0) return cudaErrorInvalidValue;
+    if (a.vocab <= 0 || a.seg <= 0 || (a.draws && (a.draw_cap <= 0 || !a.draw_ctr))) return cudaErrorInvalidValue;
     SampleArgs args = a;
     void* p[] = {&args};
     return cudaLaunchKernel(reinterpret_cast<const void*>(&k_sample), dim3(nb), dim3(kSampleThreads), p, 0, s);

@@ -171,6 +171,39 @@ def test_engine_mixed_batch_keeps_greedy_rows():
     b.close()
 
 
+@pytest.mark.parametrize("kind,temperature,p,k", [(ti.SAMPLE_TOP_P, 0.9, 0.8, 0), (ti.SAMPLE_TOP_K, 1.0, 0.0, 30)])
+def test_device_chain_samples_as_host_steps(kind, temperature, p, k):
+    """A bound device chain (no host work per step) draws from pre-generated
+    draws: the same ids, K/V and later host draws as step-by-step decoding."""
+    steps, seed = 7, 555
+    prompt = oracle.fill_ids("chain", 6, 4, SMALL["vocab"])
+    a, b = _engine(), _engine()
+    sa, sb = a.seq_create(), b.seq_create()
+    a.set_sampler(sa, kind, temperature, p, k, seed)
+    b.set_sampler(sb, kind, temperature, p, k, seed)
+    first_a, first_b = a.prefill(sa, prompt), b.prefill(sb, prompt)
+    assert first_a == first_b
+    tok = first_a
+    for _ in range(steps):
+        tok = int(a.decode([sa], [tok])[0])
+    b.seq_reserve(sb, len(prompt) + steps + 1)
+    b.bind([sb], [first_b])
+    for _ in range(steps):
+        b.decode_device()
+    last = b.unbind(steps)
+    assert int(last[0]) == tok
+    n = len(prompt) + steps
+    assert a.seq_len(sa) == b.seq_len(sb) == n
+    for which in (0, 1):
+        np.testing.assert_array_equal(a.seq_read_kv(sa, 0, which, n), b.seq_read_kv(sb, 0, which, n))
+    # after the chain, host steps continue the same draw sequence
+    assert int(a.decode([sa], [tok])[0]) == int(b.decode([sb], [tok])[0])
+    a.check()
+    b.check()
+    a.close()
+    b.close()
+
+
 def test_engine_sampler_errors():
     eng = _engine()
     sid = eng.seq_create()
@@ -180,13 +213,4 @@ def test_engine_sampler_errors():
     with pytest.raises(ti.TiError) as ei:
         eng.set_sampler(sid, ti.SAMPLE_TOP_P, float("nan"), 0.9, 0, 1)
     assert ei.value.status == ti.TI_ERR_INVALID
-    eng.set_sampler(sid, ti.SAMPLE_TOP_P, 1.0, 0.9, 0, 1)
-    eng.prefill(sid, [1, 2, 3])
-    eng.seq_reserve(sid, 8)
-    with pytest.raises(ti.TiError) as ei:
-        eng.bind([sid], [4])
-    assert ei.value.status == ti.TI_ERR_UNSUPPORTED
-    eng.set_sampler(sid, ti.SAMPLE_GREEDY)
-    eng.bind([sid], [4])  # greedy again: the device chain accepts it
-    eng.unbind(0)
     eng.close()
