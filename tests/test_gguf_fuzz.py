@@ -111,23 +111,15 @@ def _mutate(rng, blob):
 
 
 def _import_ti(lib_path=None):
-    """ti_b200, its entry points bound to `lib_path` when given (a sanitizer
-    build of the reader holds the ti_gguf_* entries and the error state only)"""
-    import ctypes as C
-
+    """ti_b200, its entry points bound to `lib_path` when given (the sanitizer build)"""
     sys.path.insert(0, os.path.join(os.path.dirname(HERE), "tensor-inference_b200"))
+    sys.path.insert(0, HERE)
     import ti_b200 as ti
 
     if lib_path:
-        L = C.CDLL(lib_path)
-        for name, (res, args) in ti._SIGS.items():
-            try:
-                f = getattr(L, name)
-            except AttributeError:
-                continue
-            f.restype = res
-            f.argtypes = args
-        ti._lib = L
+        import host_sanitize
+
+        host_sanitize.bind(ti, lib_path)
     return ti
 
 
@@ -188,38 +180,21 @@ def test_corrupted_files_fail_cleanly(tmp_path):
     _run(_worker, tmp_path)
 
 
-def _sanitizer_runtime():
-    libs = []
-    for name in ("libasan.so", "libubsan.so"):
-        r = subprocess.run(["gcc", "-print-file-name=" + name], capture_output=True, text=True)
-        path = r.stdout.strip()
-        if r.returncode != 0 or not os.path.isabs(path) or not os.path.exists(path):
-            return None
-        libs.append(path)
-    return ":".join(libs)
-
-
 def test_sanitized_reader(tmp_path):
     """gguf.cpp built with AddressSanitizer + UBSan (out-of-bounds reads of the
     mapping, integer overflow, division by zero abort the child) over the
     metadata sweep and 5000 mutated files."""
-    preload = _sanitizer_runtime()
-    if not preload:
+    import host_sanitize
+
+    if not host_sanitize.runtime():
         pytest.skip("gcc sanitizer runtimes not available")
-    root = os.path.dirname(HERE)
-    csrc = os.path.join(root, "tensor-inference_b200", "csrc")
-    lib = str(tmp_path / "libgguf_asan.so")
-    cmd = ["g++", "-std=c++17", "-O1", "-g", "-fsanitize=address,undefined", "-fno-sanitize-recover=all",
-           "-fno-omit-frame-pointer", "-fPIC", "-shared", "-I/usr/local/cuda/include", "-I" + csrc,
-           "-I" + os.path.join(root, "include"), os.path.join(csrc, "gguf.cpp"), os.path.join(csrc, "api.cpp"),
-           os.path.join(HERE, "gguf_asan_stub.cpp"), "-o", lib, "-L/usr/local/cuda/lib64", "-lcudart"]
-    r = subprocess.run(cmd, capture_output=True, text=True)
-    assert r.returncode == 0, r.stderr[-2000:]
+    lib = str(tmp_path / "libhost_asan.so")
+    ok, err = host_sanitize.build(lib)
+    assert ok, err
     code = (f"import sys; sys.path.insert(0, {HERE!r}); import test_gguf_fuzz as T; "
             f"T._worker_meta({str(tmp_path)!r}, {str(tmp_path / 'p1')!r}, {lib!r}); "
             f"T._worker({str(tmp_path)!r}, {str(tmp_path / 'p2')!r}, {lib!r}, 5000, 7)")
-    env = dict(os.environ, LD_PRELOAD=preload, ASAN_OPTIONS="detect_leaks=0:halt_on_error=1",
-               UBSAN_OPTIONS="halt_on_error=1:print_stacktrace=1")
-    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=900)
+    r = subprocess.run([sys.executable, "-c", code], env=host_sanitize.env(), capture_output=True, text=True,
+                       timeout=900)
     last = [open(tmp_path / f).read() if (tmp_path / f).exists() else "none" for f in ("p1", "p2")]
     assert r.returncode == 0 and last == ["done", "done"], (last, r.stderr[-3000:])

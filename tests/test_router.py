@@ -1,5 +1,9 @@
 """Adapter pool + swap scheduler (ti_router_*): the policy on a NULL engine, read
 back through the decision log (prefetch / evict per adapter)."""
+import os
+import subprocess
+import sys
+
 import pytest
 
 import ti_b200 as ti
@@ -207,3 +211,23 @@ def test_router_matches_its_policy_model(seed):
         assert r.resident() == m.lru, step
         assert len(m.lru) <= max_res
     assert r.stats() == m.stats
+
+
+def test_router_model_under_sanitizers(tmp_path):
+    """router.cpp built with AddressSanitizer + UBSan runs the model-based test
+    (iterator and container misuse, overflow abort the child)."""
+    import host_sanitize
+
+    if not host_sanitize.runtime():
+        pytest.skip("gcc sanitizer runtimes not available")
+    lib = str(tmp_path / "libhost_asan.so")
+    ok, err = host_sanitize.build(lib)
+    assert ok, err
+    here = os.path.dirname(os.path.abspath(__file__))
+    code = (f"import sys; sys.path[:0] = [{here!r}, {os.path.join(os.path.dirname(here), 'tensor-inference_b200')!r}]; "
+            "import ti_b200 as ti, host_sanitize, test_router as T; "
+            f"host_sanitize.bind(ti, {lib!r}); "
+            "[T.test_router_matches_its_policy_model(s) for s in range(6)]; print('router ok')")
+    r = subprocess.run([sys.executable, "-c", code], env=host_sanitize.env(), capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0 and "router ok" in r.stdout, r.stderr[-3000:]
