@@ -41,6 +41,17 @@ enum {
 
 const char* ti_last_error(void);
 int ti_version(void); /* major*10000 + minor*100 + patch */
+/* Library start-up check: every visible CUDA device is an sm_100 part (B200),
+ * the only code this build carries; *n_devices (may be NULL) = their count.
+ * TI_ERR_UNSUPPORTED names the first device that is not, or reports that no
+ * device is visible.  Other entries do not require it; a caller calls it
+ * first to fail early on the wrong hardware.  (The reference initialises
+ * lazily: Device::cuda / cuBLAS handles, device.cu:15-43, ops.cu:30-40.) */
+ti_status ti_init(int* n_devices);
+/* Release what the library holds outside engines, PKM routers and GGUF files:
+ * the ops' cached RoPE tables and the unused blocks of every device's
+ * stream-ordered pool.  Call with no op in flight; the library stays usable. */
+ti_status ti_shutdown(void);
 
 /* ================================================================= device
  * replaces tensor::backend::Device (include/tensor/backend/device.hpp:10-42,

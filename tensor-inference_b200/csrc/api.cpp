@@ -55,6 +55,43 @@ extern "C" {
 const char* ti_last_error(void) { return g_last_error.c_str(); }
 int ti_version(void) { return 100; }
 
+ti_status ti_init(int* n_devices) {
+    clear_error();
+    int n = 0;
+    const cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return fail(TI_ERR_UNSUPPORTED, "ti_init: no CUDA device (%s)",
+                    e != cudaSuccess ? cudaGetErrorString(e) : "none visible");
+    }
+    for (int d = 0; d < n; ++d) {
+        int major = 0, minor = 0;
+        TI_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, d));
+        TI_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, d));
+        TI_CHECK(major == 10 && minor == 0, TI_ERR_UNSUPPORTED,
+                 "ti_init: device %d has compute capability %d.%d; this build runs on sm_100 (B200) only", d, major,
+                 minor);
+    }
+    if (n_devices) *n_devices = n;
+    return TI_OK;
+}
+
+ti_status ti_shutdown(void) {
+    clear_error();
+    rope_tables_release();
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return TI_OK;
+    }
+    for (int d = 0; d < n; ++d) {
+        cudaMemPool_t pool;
+        if (cudaDeviceGetDefaultMemPool(&pool, d) == cudaSuccess) cudaMemPoolTrimTo(pool, 0);
+    }
+    cudaGetLastError();
+    return TI_OK;
+}
+
 ti_status ti_device_count(int* count) {
     TI_CHECK(count, TI_ERR_INVALID, "ti_device_count: null");
     int n = 0;

@@ -58,6 +58,8 @@ struct DeviceGuard {
 
 // rope frequency table (ops.cu:235-278) computed on the host in float
 void rope_freqs(int head_dim, float theta, const ti_rope_scaling* sc, float* out);
+// free the device RoPE tables the ops cache (ops.cu)
+void rope_tables_release();
 
 // The uniform draws of one sequence's sampler, as the reference's engines
 // produce them: std::uniform_real_distribution<float>(0, 1) over

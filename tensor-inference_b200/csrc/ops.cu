@@ -278,10 +278,27 @@ __global__ void k_transpose(const T* __restrict__ x, T* __restrict__ out, int ro
 }
 
 // rope tables cached per (device, head_dim, theta, scaling)
+namespace {
+std::mutex g_rope_mu;
+std::map<std::tuple<int, int, float, int, float, float, float, int>, float*> g_rope_cache;
+}  // namespace
+
+void rope_tables_release() {
+    std::lock_guard<std::mutex> lk(g_rope_mu);
+    for (auto& kv : g_rope_cache) {
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(std::get<0>(kv.first));
+        cudaFree(kv.second);
+        cudaSetDevice(prev);
+    }
+    g_rope_cache.clear();
+}
+
 const float* rope_table(int dev, int hd, float theta, const void* scv) {
     const ti_rope_scaling* sc = reinterpret_cast<const ti_rope_scaling*>(scv);
-    static std::mutex mu;
-    static std::map<std::tuple<int, int, float, int, float, float, float, int>, float*> cache;
+    auto& mu = g_rope_mu;
+    auto& cache = g_rope_cache;
     ti_rope_scaling z = {0, 1.f, 1.f, 1.f, 8192};
     const ti_rope_scaling& s = sc ? *sc : z;
     auto key = std::make_tuple(dev, hd, theta, s.apply_scaling, s.factor, s.low_freq_factor, s.high_freq_factor,

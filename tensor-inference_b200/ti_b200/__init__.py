@@ -119,6 +119,8 @@ _SIGS = {
     "ti_seq_free": (C.c_int, [C.c_void_p, C.c_int]),
     "ti_seq_reset": (C.c_int, [C.c_void_p, C.c_int]),
     "ti_seq_len": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_int)]),
+    "ti_init": (C.c_int, [C.POINTER(C.c_int)]),
+    "ti_shutdown": (C.c_int, []),
     "ti_engine_seq_set_sampler": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(Sampling)]),
     "ti_op_sample": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(Sampling), C.POINTER(C.c_float),
                                C.c_void_p, C.c_void_p]),

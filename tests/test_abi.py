@@ -73,3 +73,19 @@ def test_shim_has_no_private_cxx_runtime(name):
     out = subprocess.run(["nm", "-D", "--defined-only", path], capture_output=True, text=True, check=True).stdout
     leaked = [l for l in out.splitlines() if re.search(r"_ZSt4cout|_ZNSo9_M_insert|codecvt", l)]
     assert not leaked, leaked[:5]
+
+
+def test_init_reports_the_hardware(lib):
+    # here: no CUDA device is visible, and ti_init says so instead of going on;
+    # on a B200 box it succeeds (tests/test_gpu_ops.py)
+    import torch
+
+    n = C.c_int(-1)
+    st = lib.ti_init(C.byref(n))
+    if torch.cuda.device_count() == 0:
+        assert st == 4  # TI_ERR_UNSUPPORTED
+        assert b"no CUDA device" in lib.ti_last_error()
+        assert n.value == -1
+    else:
+        assert st == 0 and n.value == torch.cuda.device_count()
+    assert lib.ti_shutdown() == 0

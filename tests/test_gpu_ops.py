@@ -240,3 +240,19 @@ def test_paged_attention_op(hd, nq, nkv):
         assert rel_err(f32(kp[page, :, p % 16]), f32(c["knew"][b])) < 1e-2
         np.testing.assert_array_equal(vp[page, :, p % 16],
                                       c["qkv"][b, (nq + nkv) * hd:].reshape(nkv, hd))
+
+
+def test_init_shutdown_and_ops_after_it():
+    # every device is an sm_100 part; shutdown frees the cached RoPE tables and
+    # the pools' unused blocks, and the ops rebuild what they need afterwards
+    n = C.c_int(0)
+    ti.check(lib().ti_init(C.byref(n)))
+    assert n.value >= 1
+    seq, heads, hd = 5, 4, 64
+    x = bf((seq, heads, hd), "rope-sd", 3, 1.0)
+    dx, do = DevBuf.from_array(x), DevBuf(x.nbytes)
+    ti.check(lib().ti_op_rope(dx.ptr, do.ptr, seq, heads, hd, 7, 500000.0, None, None))
+    before = do.to_array(x.shape, np.uint16)
+    ti.check(lib().ti_shutdown())
+    ti.check(lib().ti_op_rope(dx.ptr, do.ptr, seq, heads, hd, 7, 500000.0, None, None))
+    np.testing.assert_array_equal(do.to_array(x.shape, np.uint16), before)
