@@ -7,6 +7,7 @@
 
 namespace ti {
 ti_status engine_slot_info(ti_engine*, const char*, int*, size_t*, size_t*) { return TI_ERR_UNSUPPORTED; }
+void rope_tables_release() {}
 }  // namespace ti
 
 extern "C" ti_status ti_engine_load_tensor(ti_engine*, const char*, int, const void*, size_t) {
