@@ -1079,13 +1079,6 @@ ti_status read_err(ti_engine* e, int32_t word) {
     return TI_OK;
 }
 
-// One step for `B` sequences with host inputs; `window` is the sliding window
-// applied (prefill semantics) or -1 (decode semantics, as the reference).
-// prefill: the B entries are tokens len .. len + B - 1 of one sequence (seq_ids
-// all equal), decoded in one step; otherwise B distinct sequences, one token each
-// Replace the argmax of every sampled row (a sequence with a top-p / top-k
-// sampler; in a prefill step only the last entry's id is returned) by the
-// device sampler's pick.  `logits` holds the rows as sample_launch indexes them.
 // the sampler's row parameters and histograms (first sampled step or chain)
 ti_status sample_buffers(ti_engine* e) {
     const int MB = e->o.max_batch;
@@ -1109,6 +1102,9 @@ SampleRow sample_row(const SeqState& s) {
     return r;
 }
 
+// Replace the argmax of every sampled row (a sequence with a top-p / top-k
+// sampler; in a prefill step only the last entry's id is returned) by the
+// device sampler's pick.  `logits` holds the rows as sample_launch indexes them.
 ti_status sample_rows(ti_engine* e, int B, const int32_t* seq_ids, bool prefill, const uint16_t* logits, int seg,
                       size_t seg_stride, size_t row_stride, cudaStream_t stream) {
     if (ti_status st = sample_buffers(e)) return st;
@@ -1136,6 +1132,12 @@ ti_status sample_rows(ti_engine* e, int B, const int32_t* seq_ids, bool prefill,
     return TI_OK;
 }
 
+// One step for `B` sequences with host inputs; `window` is the sliding window
+// applied (prefill semantics) or -1 (decode semantics, as the reference).
+// prefill: the B entries are tokens len .. len + B - 1 of one sequence (seq_ids
+// all equal), decoded in one step; otherwise B distinct sequences, one token each.
+// sample: the returned ids are drawn by the sequences' samplers (greedy ones keep
+// the LM head's argmax)
 ti_status run_step(ti_engine* e, int B, const int32_t* seq_ids, const int32_t* tokens, const int32_t* adapters,
                    int window, int32_t* next_ids, int logits_mode, void* logits_out, cudaStream_t stream,
                    bool prefill = false, bool sample = false) {
