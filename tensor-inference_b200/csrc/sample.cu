@@ -97,6 +97,11 @@ TI_DEVICE_INLINE uint32_t tie_count(u128 base, uint64_t w, uint32_t c, u128 targ
     return lo;
 }
 
+// a row segment read 8 ids per 16-byte load: aligned start and whole loads
+TI_DEVICE_INLINE bool vec_ok(const uint16_t* row, int n) {
+    return (reinterpret_cast<uintptr_t>(row) & 15) == 0 && (n & 7) == 0;
+}
+
 struct SampleShared {
     u128 warp_w[kSampleWarps];
     uint32_t warp_c[kSampleWarps];
@@ -158,20 +163,35 @@ __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(SampleArgs a) {
     for (int i = tid; i < kKeys / 4; i += kSampleThreads) reinterpret_cast<uint4*>(hist)[i] = make_uint4(0, 0, 0, 0);
     __syncthreads();
 
-    // 2. count every logit value (warp-aggregated atomics); the largest value
+    // 2. count every logit value (warp-aggregated atomics); the largest value.
+    // Segments that are 16-byte aligned with a multiple of 8 ids are read 8 ids
+    // (one 16-byte load) per thread and iteration, the rest one id at a time.
     uint32_t kmax = 0;
+    auto count = [&](uint32_t key, bool valid) {
+        const unsigned act = __ballot_sync(0xffffffffu, valid);
+        if (valid) {
+            kmax = max(kmax, key);
+            const unsigned peers = __match_any_sync(act, key);
+            if (lane == __ffs(peers) - 1) atomicAdd(&hist[key], (uint32_t)__popc(peers));
+        }
+    };
     for (int s = 0; s < nseg; ++s) {
         const uint16_t* row = a.logits + (size_t)s * a.seg_stride + (size_t)b * a.row_stride;
         const int n = min(a.seg, a.vocab - s * a.seg);
-        for (int base = 0; base < n; base += kSampleThreads) {
-            const int i = base + tid;
-            const bool valid = i < n;
-            const unsigned act = __ballot_sync(0xffffffffu, valid);
-            if (valid) {
-                const uint32_t key = bf16_key(row[i]);
-                kmax = max(kmax, key);
-                const unsigned peers = __match_any_sync(act, key);
-                if (lane == __ffs(peers) - 1) atomicAdd(&hist[key], (uint32_t)__popc(peers));
+        if (vec_ok(row, n)) {
+            for (int base = 0; base < n; base += 8 * kSampleThreads) {
+                const int i = base + 8 * tid;
+                const bool valid = i < n;
+                uint4 v = make_uint4(0, 0, 0, 0);
+                if (valid) v = *reinterpret_cast<const uint4*>(row + i);
+                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) count(bf16_key((uint16_t)(w4[e >> 1] >> (16 * (e & 1)))), valid);
+            }
+        } else {
+            for (int base = 0; base < n; base += kSampleThreads) {
+                const int i = base + tid;
+                count(i < n ? bf16_key(row[i]) : 0u, i < n);
             }
         }
     }
@@ -275,27 +295,53 @@ __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(SampleArgs a) {
     }
     __syncthreads();
 
-    // 5. the pick_rank-th id (ascending) holding pick_key: ordered tile scan
+    // 5. the pick_rank-th id (ascending) holding pick_key: ordered tile scan.
+    // A tile gives each thread `per` consecutive ids (8 on the vector path, else 1),
+    // so ids run in (warp, lane, element) order: a shuffle scan of the threads'
+    // hit counts within the warp and a prefix over the warps' totals rank every hit.
     const uint32_t pkey = sh.pick_key, prank = sh.pick_rank;
     uint32_t seen = 0;
     int tile = 0;
     for (int s = 0; s < nseg && seen < prank; ++s) {
         const uint16_t* row = a.logits + (size_t)s * a.seg_stride + (size_t)b * a.row_stride;
         const int n = min(a.seg, a.vocab - s * a.seg);
-        for (int base = 0; base < n && seen < prank; base += kSampleThreads, ++tile) {
-            const int i = base + tid;
-            const bool hit = i < n && bf16_key(row[i]) == pkey;
-            const unsigned bal = __ballot_sync(0xffffffffu, hit);
+        const bool vec = vec_ok(row, n);
+        const int per = vec ? 8 : 1;
+        for (int base = 0; base < n && seen < prank; base += per * kSampleThreads, ++tile) {
+            const int i0 = base + per * tid;
+            uint32_t hits = 0;  // bit e: id i0 + e holds pick_key
+            if (vec) {
+                if (i0 < n) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(row + i0);
+                    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        if (bf16_key((uint16_t)(w4[e >> 1] >> (16 * (e & 1)))) == pkey) hits |= 1u << e;
+                }
+            } else if (i0 < n && bf16_key(row[i0]) == pkey) {
+                hits = 1;
+            }
+            const uint32_t mine = (uint32_t)__popc(hits);
+            uint32_t incl = mine;  // inclusive scan of the hit counts over the warp's lanes
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += t;
+            }
             uint32_t* cnt = sh.tile_cnt[tile & 1];
-            if (lane == 0) cnt[warp] = (uint32_t)__popc(bal);
+            if (lane == 31) cnt[warp] = incl;
             __syncthreads();
             uint32_t before = 0, all = 0;
             for (int w2 = 0; w2 < kSampleWarps; ++w2) {
                 if (w2 == warp) before = all;
                 all += cnt[w2];
             }
-            if (hit && seen + before + (uint32_t)__popc(bal & ((1u << lane) - 1)) + 1 == prank)
-                sh.pick_id = s * a.seg + i;
+            const uint32_t first = seen + before + incl - mine;  // hits before this thread's ids
+            if (mine && first < prank && prank <= first + mine) {
+                uint32_t need = prank - first, h = hits;
+                while (--need) h &= h - 1;  // drop the need-1 lowest hits
+                sh.pick_id = s * a.seg + i0 + (__ffs(h) - 1);
+            }
             seen += all;  // block-uniform
         }
     }
