@@ -264,3 +264,29 @@ def test_engine_draws_drive_the_reference_sampler_ids(ref):
     u = ti.sampler_draws(ti.SAMPLE_TOP_P, 12, seed=31, temperature=0.9, p=0.9)
     assert ref(x, TOP_P, temperature=0.9, p=0.9, seed=31, n=12) == [oracle.sample_top_p(x, 0.9, 0.9, float(v))
                                                                       for v in u]
+
+
+# ---------------------------------------------------------------- committed fixtures
+def test_oracle_matches_committed_reference_ids():
+    """tests/golden/sampling.npz: the reference's own sampler ids (made by
+    tests/golden/make_sampling_golden.py from oracle/_ref/libref.so); checked
+    without the reference build."""
+    g = np.load(os.path.join(ROOT, "tests", "golden", "sampling.npz"))
+    settings = g["settings"]
+    n_rows = sum(1 for k in g.files if k.startswith("row"))
+    checked = 0
+    for ri in range(n_rows):
+        x = g[f"row{ri}"]
+        for si, (kind, t, p, k) in enumerate(settings):
+            kind, k = int(kind), int(k)
+            want = g[f"ids_{ri}_{si}"].tolist()
+            u = oracle.sample_draws(int(g[f"seed_{ri}_{si}"][0]), len(want))
+            if kind == TOP_P:
+                got = [oracle.sample_top_p(x, float(t), float(p), float(v)) for v in u]
+            elif kind == TOP_K:
+                got = [oracle.sample_top_k(x, float(t), k, float(u[0]))]
+            else:
+                got = [oracle.argmax(x)]
+            assert got == want, (ri, si)
+            checked += len(want)
+    assert checked > 200
