@@ -8,6 +8,7 @@ dequantisation) must match the oracle's dequantise-then-fp32-dot path within 5e-
 max-abs relative for Q4_0 (the tolerance the spec states for Q4_0) and 2e-2
 for Q8_0, with greedy ids equal up to recorded near-ties."""
 import ctypes as C
+import os
 
 import numpy as np
 import pytest
@@ -116,9 +117,21 @@ def test_quantised_decode_b1(wf):
 
 @pytest.mark.parametrize("wf", [ti.WFMT_Q4_0, ti.WFMT_Q8_0])
 def test_quantised_decode_batched(wf):
-    # 3 tokens (shared-memory activations) and 19 tokens (chunks of 8 on the GEMV)
+    # 3 tokens (GEMV, shared-memory activations) and 19 tokens (the tcgen05 GEMM)
     _parity(dict(SMALL, weight_format=wf), [4, 9, 2], steps=3)
     _parity(dict(SMALL, weight_format=wf), [2 + b % 5 for b in range(19)], steps=2)
+
+
+@pytest.mark.skipif(os.environ.get("TI_TEST_PENDING") != "1",
+                    reason="eight-token quantised GEMV not yet run on a B200 (set TI_TEST_PENDING=1)")
+@pytest.mark.parametrize("wf", [ti.WFMT_Q4_0, ti.WFMT_Q8_0])
+def test_quantised_gemv_eight_tokens_qwen7b_shapes(wf, monkeypatch):
+    # TI_TC_MIN_BATCH=9 keeps a batch of 8 on the GEMV (its 8-token instance; the
+    # 18944-column down projection in launches of 2 tokens): the alternative to the
+    # tcgen05 path for a quantised batch of 8
+    monkeypatch.setenv("TI_TC_MIN_BATCH", "9")
+    kw = dict(ti.PRESETS["qwen25_7b"], n_layers=2, weight_format=wf)
+    _parity(kw, [2 + b % 3 for b in range(8)], steps=2)
 
 
 def test_q4_qwen7b_shapes_bias():
