@@ -3,7 +3,7 @@
  *
  * carbon-os/tensor-inference (the reference) has no C ABI (its README.md:32
  * only announces one); its compute boundary is the C++ interface
- * tensor::backend::{Device, Tensor, ops} (include/tensor/backend/*.hpp) and
+ * tensor::backend::{Device, Tensor, ops} (include/tensor/backend/{device,tensor,ops}.hpp) and
  * the models::CausalLM concept (include/tensor/models/concepts.hpp:16-23).
  * Each entry point below names the reference interface it replaces.
  *
