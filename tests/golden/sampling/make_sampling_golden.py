@@ -1,11 +1,11 @@
 """Generate the sampled ids that pin the oracle's samplers to the reference.
 
-Runs on the CPU (no GPU):  python tests/golden/make_sampling_golden.py
+Runs on the CPU (no GPU):  python tests/golden/sampling/make_sampling_golden.py
 
 The reference's own Greedy / TopP / TopK (src/inference/sampling/greedy.cpp,
 top_p.cpp, compiled from its unchanged sources into oracle/_ref/libref.so with
 the ref_sample entry of oracle/ref/ref_shim.cpp) sample seeded fp32 logits
-rows held in host tensors; sampling.npz next to this file records the rows, the
+rows held in host tensors; reference_ids.npz next to this file records the rows, the
 sampler settings, the seeds and the reference's ids (a seeded TopP: 12 calls
 on one thread, so 12 successive draws; TopK and Greedy: one call).
 tests/test_sampling.py checks the oracle against these ids where the reference
@@ -18,7 +18,7 @@ import sys
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-ROOT = os.path.dirname(os.path.dirname(HERE))
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(HERE)))
 sys.path.insert(0, ROOT)
 
 import oracle  # noqa: E402
@@ -61,7 +61,7 @@ def main():
             assert rc == 0, err.value
             out[f"ids_{ri}_{si}"] = ids
             out[f"seed_{ri}_{si}"] = np.array([seed], np.uint64)
-    path = os.path.join(HERE, "sampling.npz")
+    path = os.path.join(HERE, "reference_ids.npz")
     np.savez_compressed(path, **out)
     print("wrote", path)
 

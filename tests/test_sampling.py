@@ -268,10 +268,10 @@ def test_engine_draws_drive_the_reference_sampler_ids(ref):
 
 # ---------------------------------------------------------------- committed fixtures
 def test_oracle_matches_committed_reference_ids():
-    """tests/golden/sampling.npz: the reference's own sampler ids (made by
-    tests/golden/make_sampling_golden.py from oracle/_ref/libref.so); checked
-    without the reference build."""
-    g = np.load(os.path.join(ROOT, "tests", "golden", "sampling.npz"))
+    """tests/golden/sampling/reference_ids.npz: the reference's own sampler ids
+    (made by tests/golden/sampling/make_sampling_golden.py from
+    oracle/_ref/libref.so); checked without the reference build."""
+    g = np.load(os.path.join(ROOT, "tests", "golden", "sampling", "reference_ids.npz"))
     settings = g["settings"]
     n_rows = sum(1 for k in g.files if k.startswith("row"))
     checked = 0
