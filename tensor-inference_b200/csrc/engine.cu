@@ -707,6 +707,10 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
     // next layer's qkv or the LM head; the LM head warms layer 0 for the next step)
     const char* next_env = std::getenv("TI_GEMV_NEXT_KB");
     const int next_kb = next_env ? std::atoi(next_env) : 640;
+    // TI_GEMV_NEXT2=1: the q+k+v GEMV spends what its budget leaves after the o
+    // projection on gate|up, so HBM keeps streaming while attention runs
+    const char* next2_env = std::getenv("TI_GEMV_NEXT2");
+    const bool next2 = next2_env && std::atoi(next2_env) == 1;
     auto set_next = [&](GemvArgs& a, const void* w, int N, int K, int U) {
         a.next_w = w;
         a.next_wfmt = w == e->lm_head ? kWBf16 : e->wf;
@@ -826,6 +830,13 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             q.bias = l.bqkv;
             q.err = e->err;
             set_next(q, l.wo, H, QW, 1);
+            if (next2) {
+                q.next2_w = l.wgu;
+                q.next2_wfmt = e->wf;
+                q.next2_N = I;
+                q.next2_K = H;
+                q.next2_U = 2;
+            }
             if (lora_on(0)) {
                 if (ti_status st = prenorm(q)) return st;
                 if (ti_status st = shrink(0, q.x, q.x_stride, q.norm_w)) return st;

@@ -242,6 +242,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint8_t* NW = reinterpret_cast<const uint8_t*>(a.next_w);
                     prefetch_l2_bulk(NW + (size_t)r0 * nrb, (uint32_t)(rows * nrb));
                     if (a.next_U == 2) prefetch_l2_bulk(NW + ((size_t)a.next_N + r0) * nrb, (uint32_t)(rows * nrb));
+                    // the budget left over: the first rows of the GEMV after the next one
+                    const long long left = (long long)a.next_bytes - (long long)rows * nrb * a.next_U;
+                    const int G3 = min(G, a.next2_N);
+                    if (a.next2_w && left > 0 && cta < G3) {
+                        const int s0 = (int)((long long)cta * a.next2_N / G3);
+                        const int s1 = (int)((long long)(cta + 1) * a.next2_N / G3);
+                        const size_t nrb2 = wrow_bytes(a.next2_K, a.next2_wfmt);
+                        const int rows2 = min(s1 - s0, (int)(left / (long long)(nrb2 * a.next2_U)));
+                        if (rows2 > 0) {
+                            const uint8_t* NW2 = reinterpret_cast<const uint8_t*>(a.next2_w);
+                            prefetch_l2_bulk(NW2 + (size_t)s0 * nrb2, (uint32_t)(rows2 * nrb2));
+                            if (a.next2_U == 2)
+                                prefetch_l2_bulk(NW2 + ((size_t)a.next2_N + s0) * nrb2, (uint32_t)(rows2 * nrb2));
+                        }
+                    }
                 }
             }
         }

@@ -143,6 +143,11 @@ struct GemvArgs {
     // next kernel's CTA with the same index will stream first
     const void* next_w = nullptr;
     int next_N = 0, next_K = 0, next_U = 1, next_bytes = 0, next_wfmt = kWBf16;
+    // when set, what `next_bytes` leaves after the next GEMV's rows goes to the
+    // first rows of the GEMV after it (the q+k+v GEMV's budget, beyond the small
+    // o projection, warms gate|up while attention runs)
+    const void* next2_w = nullptr;
+    int next2_N = 0, next2_K = 0, next2_U = 1, next2_wfmt = kWBf16;
     int* err = nullptr;
 };
 
