@@ -52,6 +52,13 @@ ti_status ti_init(int* n_devices);
  * the ops' cached RoPE tables and the unused blocks of every device's
  * stream-ordered pool.  Call with no op in flight; the library stays usable. */
 ti_status ti_shutdown(void);
+/* Health check of the bounded device waits that guard every wait on another
+ * CTA, kernel or rank (no counterpart in the reference, which never waits on
+ * the device): on `device`, a wait on a flag nothing writes and a wait on an
+ * mbarrier nothing completes, each limited to limit_us (1 .. 10^7).  TI_OK when
+ * both gave up and set their error bits; waited_us[0..1] (may be NULL) = how
+ * long each waited.  TI_ERR_STATE when a wait did not report giving up. */
+ti_status ti_selftest_waits(int device, int limit_us, double* waited_us);
 
 /* ================================================================= device
  * replaces tensor::backend::Device (include/tensor/backend/device.hpp:10-42,

@@ -76,15 +76,18 @@ TI_DEVICE_INLINE uint64_t global_ns() {
 // Bounded wait: returns false (and sets `err_bit` in *err) if the phase did not
 // complete within kWaitNs of wall time (or kSpinLimit polls).
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
-TI_DEVICE_INLINE bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int err_bit) {
+TI_DEVICE_INLINE bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err, int err_bit, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (uint32_t i = 0; i < kSpinLimit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255u) == 255u && global_ns() - t0 > kWaitNs) break;
+        if ((i & 255u) == 255u && global_ns() - t0 > limit_ns) break;
     }
     if (err) atomicOr(err, err_bit);
     return false;
+}
+TI_DEVICE_INLINE bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int err_bit) {
+    return mbar_wait_for(bar, parity, err, err_bit, kWaitNs);
 }
 
 // ------------------------------------------------------------------ bulk copies (TMA, non-tensor)
@@ -132,17 +135,21 @@ TI_DEVICE_INLINE void st_release_sys(unsigned int* p, unsigned int v) {
 // a peer may be seconds behind (building or loading a graph) without being dead.
 constexpr uint64_t kPeerWaitNs = 30000000000ull;  // 30 s
 constexpr uint32_t kPeerSpinLimit = 1u << 31;
-TI_DEVICE_INLINE bool wait_seq_sys(const unsigned int* p, unsigned int seq, int* err, int err_bit) {
+TI_DEVICE_INLINE bool wait_seq_sys_for(const unsigned int* p, unsigned int seq, int* err, int err_bit,
+                                       uint64_t limit_ns) {
     if ((int)(ld_acquire_sys(p) - seq) >= 0) return true;
     // an earlier wait of this step already gave up: do not wait again
     if (err && (*reinterpret_cast<volatile int*>(err) & err_bit)) return false;
     const uint64_t t0 = global_ns();
     for (uint32_t i = 0; i < kPeerSpinLimit; ++i) {
         if ((int)(ld_acquire_sys(p) - seq) >= 0) return true;
-        if ((i & 63u) == 63u && global_ns() - t0 > kPeerWaitNs) break;
+        if ((i & 63u) == 63u && global_ns() - t0 > limit_ns) break;
     }
     if (err) atomicOr(err, err_bit);
     return false;
+}
+TI_DEVICE_INLINE bool wait_seq_sys(const unsigned int* p, unsigned int seq, int* err, int err_bit) {
+    return wait_seq_sys_for(p, seq, err, err_bit, kPeerWaitNs);
 }
 
 // ------------------------------------------------------------------ loads

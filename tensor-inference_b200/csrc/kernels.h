@@ -306,6 +306,10 @@ struct SampleArgs {
     int32_t* draw_ctr = nullptr;
     int32_t* chain_tokens = nullptr;
 };
+// bounded-wait self-test (small.cu): a flag and an mbarrier that nothing completes
+cudaError_t wait_selftest_launch(const unsigned int* flag, uint64_t limit_ns, int* err, unsigned long long* elapsed,
+                                 cudaStream_t s);
+
 size_t sample_scratch_bytes(int nb);
 cudaError_t sample_launch(const SampleArgs& a, int nb, cudaStream_t s);
 

@@ -2,6 +2,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "internal.h"
 #include "kernels.h"
 #include "synth.cuh"
 
@@ -366,4 +367,57 @@ cudaError_t fill_kv_launch(uint16_t* kpool, uint16_t* vpool, size_t layer_elems,
     return cudaGetLastError();
 }
 
+
+// ------------------------------------------------------------------ wait self-test
+// The bounded waits on a flag nobody writes and on an mbarrier nobody arrives
+// at, each limited to limit_ns: both must give up, set their error bits and
+// report how long they waited (ns) in elapsed[0] / elapsed[1].
+__global__ void k_wait_selftest(const unsigned int* flag, uint64_t limit_ns, int* err, unsigned long long* elapsed) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    uint64_t t0 = global_ns();
+    wait_seq_sys_for(flag, 1u, err, kErrTimeoutPeer, limit_ns);
+    elapsed[0] = global_ns() - t0;
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    t0 = global_ns();
+    mbar_wait_for(&bar, 0, err, kErrTimeoutFull, limit_ns);
+    elapsed[1] = global_ns() - t0;
+}
+
+cudaError_t wait_selftest_launch(const unsigned int* flag, uint64_t limit_ns, int* err, unsigned long long* elapsed,
+                                 cudaStream_t s) {
+    void* args[] = {&flag, &limit_ns, &err, &elapsed};
+    return cudaLaunchKernel(reinterpret_cast<const void*>(&k_wait_selftest), dim3(1), dim3(32), args, 0, s);
+}
+
 }  // namespace ti
+
+using namespace ti;
+
+extern "C" ti_status ti_selftest_waits(int device, int limit_us, double* waited_us) {
+    clear_error();
+    TI_CHECK(limit_us >= 1 && limit_us <= 10000000, TI_ERR_INVALID, "selftest_waits: limit %d us out of range",
+             limit_us);
+    DeviceGuard g(device);
+    uint8_t* buf = nullptr;  // [flag u32][err i32][pad][elapsed u64 x 2]
+    TI_CUDA(cudaMalloc(&buf, 64));
+    cudaError_t e = cudaMemset(buf, 0, 64);
+    int err = 0;
+    unsigned long long el[2] = {0, 0};
+    if (e == cudaSuccess)
+        e = wait_selftest_launch(reinterpret_cast<const unsigned int*>(buf), (uint64_t)limit_us * 1000,
+                                 reinterpret_cast<int*>(buf + 4), reinterpret_cast<unsigned long long*>(buf + 16), 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(&err, buf + 4, 4, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(el, buf + 16, 16, cudaMemcpyDeviceToHost);
+    cudaFree(buf);
+    TI_CHECK(e == cudaSuccess, TI_ERR_CUDA, "selftest_waits: %s", cudaGetErrorString(e));
+    if (waited_us) {
+        waited_us[0] = el[0] / 1000.0;
+        waited_us[1] = el[1] / 1000.0;
+    }
+    TI_CHECK((err & (kErrTimeoutPeer | kErrTimeoutFull)) == (kErrTimeoutPeer | kErrTimeoutFull), TI_ERR_STATE,
+             "selftest_waits: the waits did not report giving up (error bits 0x%x)", err);
+    return TI_OK;
+}

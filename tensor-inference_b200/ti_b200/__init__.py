@@ -121,6 +121,7 @@ _SIGS = {
     "ti_seq_len": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_int)]),
     "ti_init": (C.c_int, [C.POINTER(C.c_int)]),
     "ti_shutdown": (C.c_int, []),
+    "ti_selftest_waits": (C.c_int, [C.c_int, C.c_int, C.POINTER(C.c_double)]),
     "ti_engine_seq_set_sampler": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(Sampling)]),
     "ti_op_sample": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(Sampling), C.POINTER(C.c_float),
                                C.c_void_p, C.c_void_p]),

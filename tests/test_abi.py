@@ -89,3 +89,9 @@ def test_init_reports_the_hardware(lib):
     else:
         assert st == 0 and n.value == torch.cuda.device_count()
     assert lib.ti_shutdown() == 0
+
+
+def test_selftest_waits_validates_before_any_device_work(lib):
+    out = (C.c_double * 2)()
+    for bad in (0, -5, 10_000_001):
+        assert lib.ti_selftest_waits(0, bad, out) == 1  # TI_ERR_INVALID

@@ -1,6 +1,7 @@
 """Parity of every ti_op_* kernel (the tensor::backend::ops replacements) with
 the oracle's restatement of the same reference op, on seeded inputs."""
 import ctypes as C
+import os
 
 import numpy as np
 import pytest
@@ -256,3 +257,17 @@ def test_init_shutdown_and_ops_after_it():
     ti.check(lib().ti_shutdown())
     ti.check(lib().ti_op_rope(dx.ptr, do.ptr, seq, heads, hd, 7, 500000.0, None, None))
     np.testing.assert_array_equal(do.to_array(x.shape, np.uint16), before)
+
+
+@pytest.mark.skipif(os.environ.get("TI_TEST_PENDING") != "1",
+                    reason="wait self-test not yet run on a B200 (set TI_TEST_PENDING=1)")
+def test_bounded_waits_give_up_and_report():
+    # a flag nothing writes and an mbarrier nothing completes, 20 ms each: both
+    # waits end, set their error bits, and the context stays usable
+    waited = (C.c_double * 2)()
+    ti.check(lib().ti_selftest_waits(0, 20000, waited))
+    for w in waited:
+        assert 20000.0 <= w < 2e6, list(waited)
+    x = bf((3, 4, 64), "after-wait", 5, 1.0)
+    dx, do = DevBuf.from_array(x), DevBuf(x.nbytes)
+    ti.check(lib().ti_op_rope(dx.ptr, do.ptr, 3, 4, 64, 0, 10000.0, None, None))
