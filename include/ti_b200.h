@@ -222,8 +222,11 @@ ti_status ti_engine_load_tensor(ti_engine* e, const char* name, int dtype, const
  * ti_engine_load_gguf uploads every model tensor under the reference's name
  * (q/k rows of llama-architecture files put back in the reference's RoPE
  * order; gemma norm weights stored as 1 + w put back to w; tensors of the
- * engine's block type passed as blocks, all others converted to bf16). */
-enum { TI_GGML_F32 = 0, TI_GGML_F16 = 1, TI_GGML_Q4_0 = 2, TI_GGML_Q8_0 = 8, TI_GGML_BF16 = 30 };
+ * engine's block type passed as blocks, all others converted to bf16: f32,
+ * f16, bf16, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0 and the k-quants Q2_K .. Q6_K). */
+enum { TI_GGML_F32 = 0, TI_GGML_F16 = 1, TI_GGML_Q4_0 = 2, TI_GGML_Q4_1 = 3, TI_GGML_Q5_0 = 6, TI_GGML_Q5_1 = 7,
+       TI_GGML_Q8_0 = 8, TI_GGML_Q2_K = 10, TI_GGML_Q3_K = 11, TI_GGML_Q4_K = 12, TI_GGML_Q5_K = 13,
+       TI_GGML_Q6_K = 14, TI_GGML_BF16 = 30 };
 typedef struct ti_gguf ti_gguf;
 ti_status ti_gguf_open(const char* path, ti_gguf** out);
 ti_status ti_gguf_close(ti_gguf* g);

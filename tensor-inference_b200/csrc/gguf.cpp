@@ -98,6 +98,14 @@ size_t type_bytes(int type, int64_t n) {
         case TI_GGML_F16: case TI_GGML_BF16: return (size_t)n * 2;
         case TI_GGML_Q4_0: return n % 32 ? 0 : (size_t)n / 32 * 18;
         case TI_GGML_Q8_0: return n % 32 ? 0 : (size_t)n / 32 * 34;
+        case TI_GGML_Q4_1: return n % 32 ? 0 : (size_t)n / 32 * 20;
+        case TI_GGML_Q5_0: return n % 32 ? 0 : (size_t)n / 32 * 22;
+        case TI_GGML_Q5_1: return n % 32 ? 0 : (size_t)n / 32 * 24;
+        case TI_GGML_Q2_K: return n % 256 ? 0 : (size_t)n / 256 * 84;
+        case TI_GGML_Q3_K: return n % 256 ? 0 : (size_t)n / 256 * 110;
+        case TI_GGML_Q4_K: return n % 256 ? 0 : (size_t)n / 256 * 144;
+        case TI_GGML_Q5_K: return n % 256 ? 0 : (size_t)n / 256 * 176;
+        case TI_GGML_Q6_K: return n % 256 ? 0 : (size_t)n / 256 * 210;
         default: return 0;
     }
 }
@@ -172,6 +180,118 @@ uint16_t float_to_bf16(float f) {
     return (uint16_t)(u >> 16);
 }
 
+inline float half_at(const uint8_t* p) {
+    uint16_t h;
+    std::memcpy(&h, p, 2);
+    return half_to_float(h);
+}
+
+// 6-bit scale (and min) j of a Q4_K / Q5_K super-block's 12 packed bytes: sub-blocks
+// 0-3 keep theirs in the low 6 bits of bytes j and j + 4; sub-blocks 4-7 take their
+// low 4 bits from the nibbles of byte j + 4 and their top 2 bits from the top bits
+// of bytes j - 4 (scale) and j (min)
+inline void k4_scale_min(const uint8_t* s, int j, int* sc, int* mn) {
+    if (j < 4) {
+        *sc = s[j] & 63;
+        *mn = s[j + 4] & 63;
+    } else {
+        *sc = (s[j + 4] & 0x0f) | ((s[j - 4] >> 6) << 4);
+        *mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+// 6-bit signed scale i (16 per Q3_K super-block, biased by 32): the low 4 bits are
+// the nibbles of bytes 0-7 (i < 8: low, else high nibble of byte i - 8), the top 2
+// bits come from bytes 8-11 (byte 8 + i % 4, bit pair i / 4)
+inline int k3_scale(const uint8_t* s, int i) {
+    const int lo = i < 8 ? (s[i] & 0x0f) : (s[i - 8] >> 4);
+    const int hi = (s[8 + (i & 3)] >> (2 * (i >> 2))) & 3;
+    return (lo | (hi << 4)) - 32;
+}
+
+// The block formats of the ggml quantisation types beyond Q4_0 / Q8_0 (GGUF's
+// published layouts), decoded element by element: element e of a block, where
+// its code bits sit, and the scale (and offset) of its group.
+void block_to_float(int type, const uint8_t* b, float* y) {
+    switch (type) {
+        case TI_GGML_Q4_1: {  // 32: fp16 d, fp16 m, 16 bytes of nibbles; x = d q + m
+            const float d = half_at(b), m = half_at(b + 2);
+            for (int e = 0; e < 32; ++e) y[e] = d * (float)((b[4 + (e & 15)] >> (4 * (e >> 4))) & 15) + m;
+            break;
+        }
+        case TI_GGML_Q5_0:    // 32: fp16 d, 32 fifth bits (u32), nibbles; x = d (q - 16)
+        case TI_GGML_Q5_1: {  // 32: fp16 d, fp16 m, fifth bits, nibbles; x = d q + m
+            const bool one = type == TI_GGML_Q5_1;
+            const float d = half_at(b), m = one ? half_at(b + 2) : 0.0f;
+            const uint8_t* qh = b + (one ? 4 : 2);
+            const uint8_t* qs = qh + 4;
+            uint32_t hb;
+            std::memcpy(&hb, qh, 4);
+            for (int e = 0; e < 32; ++e) {
+                const int q = ((qs[e & 15] >> (4 * (e >> 4))) & 15) | (int)(((hb >> e) & 1u) << 4);
+                y[e] = one ? d * (float)q + m : d * (float)(q - 16);
+            }
+            break;
+        }
+        case TI_GGML_Q2_K: {  // 256: 16 scale|min bytes, 64 bytes of 2-bit codes, fp16 d, dmin
+            const uint8_t* sc = b;
+            const uint8_t* qs = b + 16;
+            const float d = half_at(b + 80), dmin = half_at(b + 82);
+            for (int e = 0; e < 256; ++e) {
+                const int h = e >> 7, r = e & 127, j = r >> 5, second = (r >> 4) & 1, l = r & 15;
+                const int q = (qs[32 * h + 16 * second + l] >> (2 * j)) & 3;
+                const uint8_t s = sc[8 * h + 2 * j + second];
+                y[e] = d * (float)(s & 15) * (float)q - dmin * (float)(s >> 4);
+            }
+            break;
+        }
+        case TI_GGML_Q3_K: {  // 256: 32 bytes of high bits, 64 bytes of 2-bit codes, 12 scale bytes, fp16 d
+            const uint8_t* hm = b;
+            const uint8_t* qs = b + 32;
+            const uint8_t* sc = b + 96;
+            const float d = half_at(b + 108);
+            for (int e = 0; e < 256; ++e) {
+                const int h = e >> 7, r = e & 127, j = r >> 5, second = (r >> 4) & 1, l = r & 15;
+                const int lo = (qs[32 * h + 16 * second + l] >> (2 * j)) & 3;
+                const int high = (hm[16 * second + l] >> (4 * h + j)) & 1;
+                y[e] = d * (float)k3_scale(sc, 8 * h + 2 * j + second) * (float)(lo - (high ? 0 : 4));
+            }
+            break;
+        }
+        case TI_GGML_Q4_K:    // 256: fp16 d, dmin, 12 scale bytes, 128 bytes of nibbles
+        case TI_GGML_Q5_K: {  // 256: fp16 d, dmin, 12 scale bytes, 32 bytes of fifth bits, nibbles
+            const bool five = type == TI_GGML_Q5_K;
+            const float d = half_at(b), dmin = half_at(b + 2);
+            const uint8_t* sc = b + 4;
+            const uint8_t* qh = b + 16;
+            const uint8_t* qs = b + (five ? 48 : 16);
+            for (int e = 0; e < 256; ++e) {
+                const int c = e >> 6, r = e & 63, upper = r >> 5, l = r & 31;
+                int q = (qs[32 * c + l] >> (4 * upper)) & 15;
+                if (five) q |= ((qh[l] >> (2 * c + upper)) & 1) << 4;
+                int s = 0, mn = 0;
+                k4_scale_min(sc, 2 * c + upper, &s, &mn);
+                y[e] = d * (float)s * (float)q - dmin * (float)mn;
+            }
+            break;
+        }
+        case TI_GGML_Q6_K: {  // 256: 128 bytes of low nibbles, 64 bytes of high bit pairs, 16 int8 scales, fp16 d
+            const uint8_t* ql = b;
+            const uint8_t* qh = b + 128;
+            const int8_t* sc = reinterpret_cast<const int8_t*>(b + 192);
+            const float d = half_at(b + 208);
+            for (int e = 0; e < 256; ++e) {
+                const int h = e >> 7, r = e & 127, k = r >> 5, l = r & 31;
+                const int lo = (ql[64 * h + l + 32 * (k & 1)] >> (4 * (k >> 1))) & 15;
+                const int hi = (qh[32 * h + l] >> (2 * k)) & 3;
+                y[e] = d * (float)sc[8 * h + (l >> 4) + 2 * k] * (float)((lo | (hi << 4)) - 32);
+            }
+            break;
+        }
+        default: break;
+    }
+}
+
 // one row of n elements of a ggml type -> float
 void row_to_float(int type, const uint8_t* src, int64_t n, float* out) {
     switch (type) {
@@ -212,7 +332,13 @@ void row_to_float(int type, const uint8_t* src, int64_t n, float* out) {
                 for (int j = 0; j < 32; ++j) out[b * 32 + j] = d * (float)(int8_t)blk[2 + j];
             }
             break;
-        default: break;
+        default: {
+            const int64_t per = type_bytes(type, 256) == 0 ? 0 : (type_bytes(type, 32) ? 32 : 256);
+            if (!per) break;
+            const size_t bb = type_bytes(type, per);
+            for (int64_t b = 0; b < n / per; ++b) block_to_float(type, src + b * bb, out + b * per);
+            break;
+        }
     }
 }
 
@@ -563,7 +689,8 @@ ti_status ti_gguf_read(const ti_gguf* g, int i, int dtype, void* out, size_t byt
     TI_CHECK(g && out, TI_ERR_INVALID, "ti_gguf_read: null argument");
     TI_CHECK(i >= 0 && i < (int)g->tensors.size(), TI_ERR_INVALID, "tensor index %d out of range", i);
     const ti_gguf::Tensor& t = g->tensors[i];
-    TI_CHECK(t.bytes > 0, TI_ERR_UNSUPPORTED, "GGUF tensor '%s': ggml type %d not supported (f32, f16, bf16, q4_0, q8_0)",
+    TI_CHECK(t.bytes > 0, TI_ERR_UNSUPPORTED,
+             "GGUF tensor '%s': ggml type %d not supported (f32, f16, bf16, q4_0, q4_1, q5_0, q5_1, q8_0, q2_k .. q6_k)",
              t.name.c_str(), t.type);
     const int64_t cols = t.ne[0], rows = t.n_dims >= 2 ? t.ne[1] * t.ne[2] * t.ne[3] : 1;
     const int64_t heads = permute_heads(g, t.name);

@@ -51,7 +51,7 @@ def test_container_metadata_and_tensor_table(tmp_path):
                ("token_embd.weight", GGML_BF16, (64, 2), bf.tobytes()),
                ("blk.0.attn_v.weight", GGML_Q4_0, (64, 4), q4.tobytes()),
                ("blk.0.ffn_down.weight", GGML_Q8_0, (32, 2), q8.tobytes()),
-               ("blk.0.exotic.weight", 14, (256, 1), bytes(210))]  # a k-quant this reader does not decode
+               ("blk.0.exotic.weight", 16, (256, 1), bytes(66))]  # IQ2_XXS: a type this reader does not decode
     p = tmp_path / "m.gguf"
     write(p, meta, tensors)
     with ti.Gguf(p) as g:
@@ -241,3 +241,32 @@ def test_rope_factors(tmp_path):
         with pytest.raises(ti.TiError) as ei:
             g.rope_inv_freq(hd)  # the factor table fixes head_dim
         assert ei.value.status == ti.TI_ERR_INVALID
+
+
+# ggml type -> (elements per block, bytes per block, byte offsets of its fp16 scale fields)
+_BLOCKS = {3: (32, 20, (0, 2)), 6: (32, 22, (0,)), 7: (32, 24, (0, 2)), 10: (256, 84, (80, 82)),
+           11: (256, 110, (108,)), 12: (256, 144, (0, 2)), 13: (256, 176, (0, 2)), 14: (256, 210, (208,))}
+
+
+@pytest.mark.parametrize("gtype", sorted(_BLOCKS))
+def test_block_types_decode_as_the_gguf_package(tmp_path, gtype):
+    """Q4_1, Q5_0, Q5_1 and the k-quants Q2_K .. Q6_K: random blocks (finite fp16
+    scales) read back as bf16 equal the gguf package's dequantisation (the
+    llama.cpp project's Python reader) rounded to bf16."""
+    quants = pytest.importorskip("gguf.quants")
+    per, nbytes, halves = _BLOCKS[gtype]
+    rows, cols = 3, 512
+    rng = np.random.default_rng(gtype)
+    raw = rng.integers(0, 256, size=(rows, cols // per, nbytes), dtype=np.uint8)
+    for off in halves:
+        h = (rng.uniform(0.001, 0.05, size=(rows, cols // per)) * rng.choice([-1, 1], size=(rows, cols // per)))
+        raw[:, :, off:off + 2] = h.astype(np.float16).view(np.uint8).reshape(rows, cols // per, 2)
+    raw = raw.reshape(rows, -1)
+    want = quants.dequantize(raw, gtype).astype(np.float32).reshape(rows, cols)
+    p = tmp_path / "blocks.gguf"
+    write(p, _llama_meta(), [("blk.0.ffn_up.weight", gtype, (cols, rows), raw.tobytes())])
+    with ti.Gguf(p) as g:
+        inf = g.info(0)
+        assert inf["type"] == gtype and inf["bytes"] == raw.nbytes
+        got = g.read(0)
+    np.testing.assert_array_equal(got, oracle.f32_to_bf16(want))

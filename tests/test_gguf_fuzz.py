@@ -49,7 +49,11 @@ def _valid_file(path, override=None):
                ("blk.0.attn_q.weight", GGML_Q4_0, (64, 4), q4.tobytes()),
                ("blk.0.attn_k.weight", GGML_Q8_0, (64, 2), q8.tobytes()),
                ("blk.0.ffn_up.weight", GGML_F16, (64, 2), rng.standard_normal(128).astype(np.float16).tobytes()),
-               ("rope_freqs.weight", GGML_F32, (8,), np.ones(8, np.float32).tobytes())]
+               ("rope_freqs.weight", GGML_F32, (8,), np.ones(8, np.float32).tobytes()),
+               # k-quant and legacy block types decoded to bf16 (Q4_K, Q6_K, Q5_1)
+               ("blk.0.ffn_down.weight", 12, (256, 2), rng.integers(0, 256, 2 * 144, dtype=np.uint8).tobytes()),
+               ("blk.0.attn_v.weight", 14, (256, 2), rng.integers(0, 256, 2 * 210, dtype=np.uint8).tobytes()),
+               ("blk.0.attn_output.weight", 7, (64, 2), rng.integers(0, 256, 2 * 2 * 24, dtype=np.uint8).tobytes())]
     write(path, meta, tensors)
 
 
