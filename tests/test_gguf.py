@@ -270,3 +270,65 @@ def test_block_types_decode_as_the_gguf_package(tmp_path, gtype):
         assert inf["type"] == gtype and inf["bytes"] == raw.nbytes
         got = g.read(0)
     np.testing.assert_array_equal(got, oracle.f32_to_bf16(want))
+
+
+def test_files_written_by_the_gguf_package(tmp_path):
+    """Interoperability: a file written by the llama.cpp project's GGUFWriter
+    (its own metadata encoding, alignment padding and tensor table) reads back
+    with the same metadata, tensor table and values, and gives the model
+    description its metadata states."""
+    gg = pytest.importorskip("gguf")
+    from gguf import GGMLQuantizationType as Q
+    from gguf import quants
+
+    rng = np.random.default_rng(5)
+    H, I, heads, kv, V = 256, 512, 4, 2, 1000
+    p = tmp_path / "official.gguf"
+    w = gg.GGUFWriter(str(p), "llama")
+    w.add_block_count(1)
+    w.add_context_length(2048)
+    w.add_embedding_length(H)
+    w.add_feed_forward_length(I)
+    w.add_head_count(heads)
+    w.add_head_count_kv(kv)
+    w.add_layer_norm_rms_eps(1e-5)
+    w.add_rope_freq_base(500000.0)
+    w.add_string("general.name", "interop")
+    w.add_array("tokenizer.ggml.tokens", ["<s>", "</s>", "x"])
+    emb = rng.standard_normal((V, H)).astype(np.float32)
+    norm = rng.standard_normal(H).astype(np.float32)
+    up = rng.standard_normal((I, H)).astype(np.float32)
+    down = rng.standard_normal((H, I)).astype(np.float32)
+    gate = rng.standard_normal((I, H)).astype(np.float16)
+    q4 = quants.quantize(up, Q.Q4_0)
+    q8 = quants.quantize(down, Q.Q8_0)
+    w.add_tensor("token_embd.weight", emb)
+    w.add_tensor("output_norm.weight", norm)
+    w.add_tensor("blk.0.ffn_up.weight", q4, raw_dtype=Q.Q4_0)
+    w.add_tensor("blk.0.ffn_down.weight", q8, raw_dtype=Q.Q8_0)
+    w.add_tensor("blk.0.ffn_gate.weight", gate)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    with ti.Gguf(p) as g:
+        assert len(g) == 5
+        assert g.meta_str("general.architecture") == "llama" and g.meta_str("general.name") == "interop"
+        assert g.meta_int("llama.block_count") == 1 and g.meta_int("llama.embedding_length") == H
+        assert g.meta_array_len("tokenizer.ggml.tokens") == 3
+        assert abs(g.meta_float("llama.rope.freq_base") - 500000.0) < 1e-3
+        d = g.model_desc()
+        assert (d.hidden, d.intermediate, d.n_heads, d.n_kv_heads, d.head_dim, d.vocab, d.n_layers) == \
+            (H, I, heads, kv, H // heads, V, 1)
+        info = {g.info(i)["name"]: g.info(i) for i in range(len(g))}
+        assert info["blk.0.ffn_up.weight"]["type"] == ti.GGML_Q4_0 and info["blk.0.ffn_up.weight"]["dims"] == (H, I)
+        assert info["blk.0.ffn_down.weight"]["type"] == ti.GGML_Q8_0
+        assert info["blk.0.ffn_gate.weight"]["type"] == ti.GGML_F16
+        checks = [("token_embd.weight", emb), ("output_norm.weight", norm[None, :]),
+                  ("blk.0.ffn_up.weight", quants.dequantize(q4, Q.Q4_0)),
+                  ("blk.0.ffn_down.weight", quants.dequantize(q8, Q.Q8_0)),
+                  ("blk.0.ffn_gate.weight", gate.astype(np.float32))]
+        for name, ref in checks:
+            got = g.read(g.find(name))
+            np.testing.assert_array_equal(got, oracle.f32_to_bf16(np.asarray(ref, np.float32)).reshape(got.shape))
+        np.testing.assert_array_equal(g.read(g.find("blk.0.ffn_up.weight"), ti.DTYPE_Q4_0).reshape(q4.shape), q4)
