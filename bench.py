@@ -302,6 +302,40 @@ def measure_70b_tp(ti, torch, stream, peak, world, rank, dev, steps, warmup=3):
                       "7 projections (round-robin); K/V context synthetic"}
 
 
+def measure_ttft(ti, torch, prompt_len=512, chunks=(16, 64, 128), dev=0, reps=3):
+    """Time to first token of a `prompt_len`-token prompt on the Llama-3-8B shape:
+    ti_engine_prefill_chunked (batched prefill, `chunk` tokens per step) against
+    one decode step per prompt token; host-timed around the whole call (it
+    returns the first generated id), best of `reps`."""
+    import numpy as np
+
+    desc = ti.model_desc(**ti.PRESETS["llama3_8b"])
+    mb = max(chunks)
+    eng = ti.Engine(desc, device=dev, max_batch=mb, max_seqs=2, max_seq_len=prompt_len + 16)
+    out = {"prompt": prompt_len}
+    try:
+        eng.init_synthetic(0, 0.02)
+        ids = np.random.default_rng(1).integers(0, desc.vocab, size=prompt_len, dtype=np.int32)
+        for chunk in (1,) + tuple(chunks):
+            best = None
+            for _ in range(reps + 1):  # the first run captures this chunk's graphs
+                sid = eng.seq_create()
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                if chunk == 1:
+                    eng.prefill(sid, ids)
+                else:
+                    eng.prefill(sid, ids, chunk=chunk)
+                dt = time.perf_counter() - t0
+                eng.seq_free(sid)
+                best = dt if best is None or dt < best else best
+            out[f"chunk{chunk}_ms"] = round(best * 1e3, 2)
+        eng.check()
+    finally:
+        eng.close()
+    return out
+
+
 def kernel_roofline(ti, torch, eng, stream, peak, iters=64):
     """dominant kernel (gate|up GEMV, 2 x 14336 x 4096 bf16 = 235 MB per launch)
     timed alone with CUDA events on its launch stream, cycling layers so every
@@ -537,6 +571,10 @@ def run_ours(args, rank, world):
         eng.close()  # the 8B engine's 15 GB is not needed for the Qwen legs
         qwen = {name: extra(measure_qwen_lora, ti, torch, stream, peak, wf, max(4, args.steps // 4), 3, dev)
                 for name, wf in (("bf16", ti.WFMT_BF16), ("q4_0", ti.WFMT_Q4_0))}
+    ttft = None
+    if args.ttft and world == 1:
+        eng.close()
+        ttft = extra(measure_ttft, ti, torch, dev=dev)
     r70 = None
     if args.big and world > 1:
         eng.close()
@@ -590,6 +628,8 @@ def run_ours(args, rank, world):
             line["qwen7b_lora_b8"] = dict(qwen, config="Qwen2.5-7B shape, rank-16 LoRA q/k/v/o, batch 8, 256-token prompt")
         if r70:
             line["llama70b_tp_b64_lora"] = r70
+        if ttft:
+            line["ttft_8b"] = ttft
         if pkm and "error" not in pkm:
             # FP32 issue peak: 148 SMs x 128 lanes x SM clock during the run
             clk = (line["clocks"].get("sm_mhz") or 1965.0) * 1e6
@@ -619,6 +659,9 @@ def main():
     ap.add_argument("--no-70b", dest="big", action="store_false",
                     help="skip the Llama-3-70B tensor-parallel leg (config 5, N >= 2 only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ttft", action="store_true",
+                    help="also time a 512-token prefill (batched, chunks of 16/64/128, and token by token) on the 8B "
+                         "shape: the line's ttft_8b field")
     ap.add_argument("--profile", action="store_true", help="short ncu workload (see run_profile)")
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--prompt", type=int, default=32)
