@@ -161,12 +161,17 @@ def prefill_lockstep(eng, sids, prompts, adapters=None):
 
 
 def measure_batch(ti, torch, eng, B, steps, warmup, stream, peak, measure_e2e=True, prompt=None, adapters=None,
-                  lora_bytes=0, world=1):
+                  lora_bytes=0, world=1, sampler=None):
+    """sampler: (kind, temperature, p, k, seed) set on every sequence (device
+    sampling in the chain and in the e2e steps), None = greedy"""
     import numpy as np
 
     desc = eng.desc
     prompt = prompt or PROMPT
     sids = [eng.seq_create() for _ in range(B)]
+    if sampler:
+        for s in sids:
+            eng.set_sampler(s, *sampler)
     prompts = np.random.default_rng(0).integers(0, desc.vocab, size=(B, prompt), dtype=np.int32)
     t0 = time.perf_counter()
     first = prefill_lockstep(eng, sids, prompts, adapters)
@@ -566,6 +571,15 @@ def run_ours(args, rank, world):
     if args.b32:
         r32 = measure_batch(ti, torch, eng, 32, max(2, args.steps // 4), min(args.warmup, 3), stream, peak,
                             measure_e2e=False, world=world)
+    sampled = None
+    if args.sampled and world == 1:
+        # the same batch-1 step with a seeded top-p sampler (the reference's TopP defaults, t=0.8)
+        rs = extra(measure_batch, ti, torch, eng, 1, args.steps, args.warmup, stream, peak,
+                   sampler=(ti.SAMPLE_TOP_P, 0.8, 0.95, 0, 1234))
+        sampled = rs if "error" in rs else {
+            "tok_s": round(rs["tok_s"], 2), "ms_per_step": round(rs["ms_per_step"], 4),
+            "e2e_tok_s": round(rs["e2e"]["value"], 2), "greedy_ms_per_step": round(r1["ms_per_step"], 4),
+            "config": "config 2 at batch 1, top-p 0.95, temperature 0.8, seeded; sampled on the device"}
     qwen = None
     if args.qwen and world == 1:
         eng.close()  # the 8B engine's 15 GB is not needed for the Qwen legs
@@ -630,6 +644,8 @@ def run_ours(args, rank, world):
             line["llama70b_tp_b64_lora"] = r70
         if ttft:
             line["ttft_8b"] = ttft
+        if sampled:
+            line["sampled_b1"] = sampled
         if pkm and "error" not in pkm:
             # FP32 issue peak: 148 SMs x 128 lanes x SM clock during the run
             clk = (line["clocks"].get("sm_mhz") or 1965.0) * 1e6
@@ -659,6 +675,8 @@ def main():
     ap.add_argument("--no-70b", dest="big", action="store_false",
                     help="skip the Llama-3-70B tensor-parallel leg (config 5, N >= 2 only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sampled", action="store_true",
+                    help="also measure batch-1 decode with device top-p sampling: the line's sampled_b1 field")
     ap.add_argument("--ttft", action="store_true",
                     help="also time a 512-token prefill (batched, chunks of 16/64/128, and token by token) on the 8B "
                          "shape: the line's ttft_8b field")
