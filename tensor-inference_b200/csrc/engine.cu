@@ -1314,8 +1314,7 @@ static size_t gguf_row_bytes(int K, int wf) { return (size_t)K / 32 * (wf == kWQ
 
 // A linear weight of a Q4_0 / Q8_0 engine: bf16 rows are quantised on the
 // device (the GGUF definition, bit for bit), GGUF blocks are repacked.
-static ti_status load_quantized(ti_engine* e, const Slot& s, const char* name, int dtype, const void* host,
-                                size_t bytes) {
+static ti_status load_quantized(const Slot& s, const char* name, int dtype, const void* host, size_t bytes) {
     const int K = (int)s.nc;  // local row length (a column window of whole blocks under TP)
     const int gguf = s.wf == kWQ4 ? TI_DTYPE_Q4_0 : TI_DTYPE_Q8_0;
     TI_CHECK(dtype == TI_DTYPE_BF16 || dtype == gguf, TI_ERR_UNSUPPORTED,
@@ -1348,7 +1347,7 @@ ti_status ti_engine_load_tensor(ti_engine* e, const char* name, int dtype, const
     const Slot& s = e->slots[it->second];
     if (s.wf != kWBf16) {
         DeviceGuard g(e->dev);
-        return load_quantized(e, s, name, dtype, host, bytes);
+        return load_quantized(s, name, dtype, host, bytes);
     }
     TI_CHECK(dtype == TI_DTYPE_BF16, TI_ERR_UNSUPPORTED, "tensor '%s': dtype %d (bf16 expected)", name, dtype);
     TI_CHECK(bytes == s.rows * s.cols * 2, TI_ERR_INVALID, "tensor '%s': %zu bytes, expected %zu", name, bytes,

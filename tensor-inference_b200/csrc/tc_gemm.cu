@@ -289,7 +289,7 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                                    : (uint32_t)kbs * (kTcABytes + xatom);
             auto load_w = [&](int tile, int kb, int s) {
                 uint8_t* st = smem + (size_t)s * a.stage_bytes;
-                if (kQ) {
+                if constexpr (kQ) {
                     // the codes and fp16 scales of kbs*64 columns of 128 rows (two halves of 64 for GLU)
                     const int xc = kb * kbs * a.cb, xs = kb * kbs * 4;
                     if (kGlu) {
@@ -302,18 +302,18 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                         tma_load_2d_hint(st + a.w_off, &tmw, xc, tile * kTcBM, &full[s], pol);
                         tma_load_2d_hint(st + a.s_off, &tms, xs, tile * kTcBM, &full[s], pol);
                     }
-                    return;
-                }
-                // kbs adjacent 64-column atoms of each weight row back to back, so
-                // DRAM sees kbs * 128 contiguous bytes per row
-                for (int j = 0; j < kbs; ++j) {
-                    const int x = (kb * kbs + j) * kTcBK;
-                    uint8_t* at = st + (size_t)j * kTcABytes;
-                    if (kGlu) {
-                        tma_load_2d_hint(at, &tmw, x, tile * 64, &full[s], pol);
-                        tma_load_2d_hint(at + kTcABytes / 2, &tmw, x, a.N + tile * 64, &full[s], pol);
-                    } else {
-                        tma_load_2d_hint(at, &tmw, x, tile * kTcBM, &full[s], pol);
+                } else {
+                    // kbs adjacent 64-column atoms of each weight row back to back, so
+                    // DRAM sees kbs * 128 contiguous bytes per row
+                    for (int j = 0; j < kbs; ++j) {
+                        const int x = (kb * kbs + j) * kTcBK;
+                        uint8_t* at = st + (size_t)j * kTcABytes;
+                        if (kGlu) {
+                            tma_load_2d_hint(at, &tmw, x, tile * 64, &full[s], pol);
+                            tma_load_2d_hint(at + kTcABytes / 2, &tmw, x, a.N + tile * 64, &full[s], pol);
+                        } else {
+                            tma_load_2d_hint(at, &tmw, x, tile * kTcBM, &full[s], pol);
+                        }
                     }
                 }
             };
