@@ -241,6 +241,13 @@ ti_status ti_gguf_meta_int(const ti_gguf* g, const char* key, int64_t* v);
 ti_status ti_gguf_meta_float(const ti_gguf* g, const char* key, double* v);
 ti_status ti_gguf_meta_string(const ti_gguf* g, const char* key, const char** v);
 ti_status ti_gguf_meta_array_len(const ti_gguf* g, const char* key, int64_t* n);
+/* Element i of array metadata (tokenizer.ggml.tokens / scores / token_type and the
+ * like): a string as bytes and length (not NUL-terminated; valid while the file
+ * is open), an integer of any integer or bool element type, or a float of f32 /
+ * f64 elements.  TI_ERR_INVALID for another element type or an index out of range. */
+ti_status ti_gguf_meta_array_string(const ti_gguf* g, const char* key, int64_t i, const char** str, size_t* len);
+ti_status ti_gguf_meta_array_int(const ti_gguf* g, const char* key, int64_t i, int64_t* value);
+ti_status ti_gguf_meta_array_float(const ti_gguf* g, const char* key, int64_t i, double* value);
 /* architecture llama / qwen2 / gemma from "{arch}.*" metadata (block_count,
  * embedding_length, feed_forward_length, attention.head_count[_kv],
  * attention.key_length, attention.layer_norm_rms_epsilon, rope.freq_base);

@@ -51,6 +51,8 @@ struct ti_gguf {
         std::string s;       // string values
         uint32_t elem = 0;   // array element type
         uint64_t n = 0;      // array length
+        const uint8_t* data = nullptr;  // array elements in the mapping
+        std::vector<uint64_t> str_at;   // string arrays: offset of element k's length field from `data`
     };
     std::map<std::string, Meta> meta;
     struct Tensor {
@@ -464,8 +466,14 @@ ti_status ti_gguf_open(const char* path, ti_gguf** out) {
         } else if (v.type == kArr) {
             v.elem = r.get<uint32_t>();
             v.n = r.get<uint64_t>();
+            v.data = r.p;
             if (v.elem == kStr) {
-                for (uint64_t k = 0; k < v.n && r.ok; ++k) r.skip(r.get<uint64_t>());
+                if (v.n > g->size / 8) return bad("metadata array longer than the file");
+                v.str_at.reserve((size_t)v.n);
+                for (uint64_t k = 0; k < v.n && r.ok; ++k) {
+                    v.str_at.push_back((uint64_t)(r.p - v.data));
+                    r.skip(r.get<uint64_t>());
+                }
             } else if (v.elem == kArr || scalar_size(v.elem) == 0) {
                 return bad("unsupported metadata array element type");
             } else {
@@ -596,6 +604,72 @@ ti_status ti_gguf_meta_array_len(const ti_gguf* g, const char* key, int64_t* n) 
     const ti_gguf::Meta* m = find_meta(g, key);
     TI_CHECK(m && m->type == kArr, TI_ERR_NOT_FOUND, "no array metadata '%s'", key);
     *n = (int64_t)m->n;
+    return TI_OK;
+}
+
+// element i of array metadata `key`, whose elements must be of a type `ok` accepts
+static ti_status array_elem(const ti_gguf* g, const char* key, int64_t i, const ti_gguf::Meta** out,
+                            bool (*ok)(uint32_t)) {
+    TI_CHECK(g && key, TI_ERR_INVALID, "gguf array element: null argument");
+    const ti_gguf::Meta* m = find_meta(g, key);
+    TI_CHECK(m && m->type == kArr, TI_ERR_NOT_FOUND, "no array metadata '%s'", key);
+    TI_CHECK(ok(m->elem), TI_ERR_INVALID, "array metadata '%s' holds element type %u", key, m->elem);
+    TI_CHECK(i >= 0 && (uint64_t)i < m->n, TI_ERR_INVALID, "array metadata '%s': index %lld of %llu", key,
+             (long long)i, (unsigned long long)m->n);
+    *out = m;
+    return TI_OK;
+}
+
+ti_status ti_gguf_meta_array_string(const ti_gguf* g, const char* key, int64_t i, const char** str, size_t* len) {
+    ti::clear_error();
+    TI_CHECK(str && len, TI_ERR_INVALID, "ti_gguf_meta_array_string: null argument");
+    const ti_gguf::Meta* m = nullptr;
+    if (ti_status st = array_elem(g, key, i, &m, [](uint32_t t) { return t == (uint32_t)kStr; })) return st;
+    const uint8_t* at = m->data + m->str_at[(size_t)i];
+    uint64_t n = 0;
+    std::memcpy(&n, at, 8);
+    *str = reinterpret_cast<const char*>(at + 8);
+    *len = (size_t)n;
+    return TI_OK;
+}
+
+ti_status ti_gguf_meta_array_int(const ti_gguf* g, const char* key, int64_t i, int64_t* v) {
+    ti::clear_error();
+    TI_CHECK(v, TI_ERR_INVALID, "ti_gguf_meta_array_int: null argument");
+    const ti_gguf::Meta* m = nullptr;
+    if (ti_status st = array_elem(g, key, i, &m, [](uint32_t t) {
+            return t == kU8 || t == kI8 || t == kU16 || t == kI16 || t == kU32 || t == kI32 || t == kU64 ||
+                   t == kI64 || t == kBool;
+        }))
+        return st;
+    const uint8_t* at = m->data + (size_t)i * scalar_size(m->elem);
+    switch (m->elem) {
+        case kU8: *v = *at; break;
+        case kI8: *v = (int8_t)*at; break;
+        case kBool: *v = *at != 0; break;
+        case kU16: { uint16_t x; std::memcpy(&x, at, 2); *v = x; break; }
+        case kI16: { int16_t x; std::memcpy(&x, at, 2); *v = x; break; }
+        case kU32: { uint32_t x; std::memcpy(&x, at, 4); *v = x; break; }
+        case kI32: { int32_t x; std::memcpy(&x, at, 4); *v = x; break; }
+        case kU64: { uint64_t x; std::memcpy(&x, at, 8); *v = (int64_t)x; break; }
+        default: { int64_t x; std::memcpy(&x, at, 8); *v = x; break; }
+    }
+    return TI_OK;
+}
+
+ti_status ti_gguf_meta_array_float(const ti_gguf* g, const char* key, int64_t i, double* v) {
+    ti::clear_error();
+    TI_CHECK(v, TI_ERR_INVALID, "ti_gguf_meta_array_float: null argument");
+    const ti_gguf::Meta* m = nullptr;
+    if (ti_status st = array_elem(g, key, i, &m, [](uint32_t t) { return t == kF32 || t == kF64; })) return st;
+    const uint8_t* at = m->data + (size_t)i * scalar_size(m->elem);
+    if (m->elem == kF32) {
+        float x;
+        std::memcpy(&x, at, 4);
+        *v = x;
+    } else {
+        std::memcpy(v, at, 8);
+    }
     return TI_OK;
 }
 

@@ -164,6 +164,10 @@ _SIGS = {
     "ti_gguf_meta_float": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_double)]),
     "ti_gguf_meta_string": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_char_p)]),
     "ti_gguf_meta_array_len": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_int64)]),
+    "ti_gguf_meta_array_string": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int64, C.POINTER(C.c_void_p),
+                                            C.POINTER(C.c_size_t)]),
+    "ti_gguf_meta_array_int": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int64, C.POINTER(C.c_int64)]),
+    "ti_gguf_meta_array_float": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int64, C.POINTER(C.c_double)]),
     "ti_gguf_model_desc": (C.c_int, [C.c_void_p, C.c_void_p]),
     "ti_gguf_reference_name": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t]),
     "ti_gguf_read": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t]),
@@ -470,6 +474,33 @@ class Gguf:
         v = C.c_int64()
         check(lib().ti_gguf_meta_array_len(self.h, key.encode(), C.byref(v)))
         return v.value
+
+    def meta_array(self, key):
+        """array metadata as a list: str (decoded as UTF-8), int or float elements"""
+        n = self.meta_array_len(key)
+        k = key.encode()
+        if n == 0:
+            return []
+        p, ln = C.c_void_p(), C.c_size_t()
+        if lib().ti_gguf_meta_array_string(self.h, k, 0, C.byref(p), C.byref(ln)) == TI_OK:
+            out = []
+            for i in range(n):
+                check(lib().ti_gguf_meta_array_string(self.h, k, i, C.byref(p), C.byref(ln)))
+                out.append(C.string_at(p, ln.value).decode(errors="replace"))
+            return out
+        iv = C.c_int64()
+        if lib().ti_gguf_meta_array_int(self.h, k, 0, C.byref(iv)) == TI_OK:
+            out = []
+            for i in range(n):
+                check(lib().ti_gguf_meta_array_int(self.h, k, i, C.byref(iv)))
+                out.append(iv.value)
+            return out
+        fv = C.c_double()
+        out = []
+        for i in range(n):
+            check(lib().ti_gguf_meta_array_float(self.h, k, i, C.byref(fv)))
+            out.append(fv.value)
+        return out
 
     def model_desc(self):
         d = ModelDesc()

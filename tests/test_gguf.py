@@ -332,3 +332,31 @@ def test_files_written_by_the_gguf_package(tmp_path):
             got = g.read(g.find(name))
             np.testing.assert_array_equal(got, oracle.f32_to_bf16(np.asarray(ref, np.float32)).reshape(got.shape))
         np.testing.assert_array_equal(g.read(g.find("blk.0.ffn_up.weight"), ti.DTYPE_Q4_0).reshape(q4.shape), q4)
+        assert g.meta_array("tokenizer.ggml.tokens") == ["<s>", "</s>", "x"]
+
+
+def test_metadata_arrays(tmp_path):
+    """Elements of array metadata: strings (the vocabulary), integers of every
+    width, floats; wrong element types and indices are errors."""
+    import ctypes as C
+
+    toks = ["<s>", "</s>", "héllo", "", "▁the"]
+    meta = [m for m in _llama_meta() if m[0] != "tokenizer.ggml.tokens"] + list((
+                              ("tokenizer.ggml.tokens", ARR, (STR, toks)),
+                              ("tokenizer.ggml.scores", ARR, (F32, [0.0, -1.5, 2.25, 3.0, -4.0])),
+                              ("tokenizer.ggml.token_type", ARR, (I32, [1, 3, 1, -1, 6])),
+                              ("x.u8s", ARR, (U8, [0, 255, 7])), ("x.u64s", ARR, (U64, [1 << 40, 5])),
+                              ("x.f64s", ARR, (F64, [0.5, -2.0])), ("x.bools", ARR, (BOOL, [1, 0]))))
+    p = tmp_path / "arrays.gguf"
+    write(p, meta, [("token_embd.weight", GGML_F32, (64, 2), bytes(512))])
+    with ti.Gguf(p) as g:
+        assert g.meta_array("tokenizer.ggml.tokens") == toks
+        assert g.meta_array("tokenizer.ggml.scores") == [0.0, -1.5, 2.25, 3.0, -4.0]
+        assert g.meta_array("tokenizer.ggml.token_type") == [1, 3, 1, -1, 6]
+        assert g.meta_array("x.u8s") == [0, 255, 7] and g.meta_array("x.u64s") == [1 << 40, 5]
+        assert g.meta_array("x.f64s") == [0.5, -2.0] and g.meta_array("x.bools") == [1, 0]
+        v = C.c_int64()
+        assert ti.lib().ti_gguf_meta_array_int(g.h, b"x.u8s", 3, C.byref(v)) == ti.TI_ERR_INVALID
+        assert ti.lib().ti_gguf_meta_array_int(g.h, b"x.u8s", -1, C.byref(v)) == ti.TI_ERR_INVALID
+        assert ti.lib().ti_gguf_meta_array_int(g.h, b"tokenizer.ggml.tokens", 0, C.byref(v)) == ti.TI_ERR_INVALID
+        assert ti.lib().ti_gguf_meta_array_int(g.h, b"llama.block_count", 0, C.byref(v)) == ti.TI_ERR_NOT_FOUND

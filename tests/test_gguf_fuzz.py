@@ -82,8 +82,8 @@ def _exercise(ti, path):
                         g.read(i, dt)
                     except ti.TiError:
                         pass
-        for key in KEYS:
-            for f in (g.meta_int, g.meta_float, g.meta_str, g.meta_array_len):
+        for key in KEYS + ["x.arr"]:
+            for f in (g.meta_int, g.meta_float, g.meta_str, g.meta_array_len, g.meta_array):
                 try:
                     f(key)
                 except ti.TiError:
