@@ -216,3 +216,31 @@ def test_oracle_lora_matches_numpy(orc):
 
 def test_rb_helper():
     assert rb(np.float32(1.0 + 2**-9)) == np.float32(1.0)
+
+
+@pytest.mark.parametrize("qtype", ["q4_0", "q8_0"])
+def test_gguf_quantisers_match_the_gguf_package(orc, qtype):
+    """The oracle's Q4_0 / Q8_0 quantiser and dequantiser (restated from the
+    format's published definition) produce the same block bytes and values as
+    the llama.cpp project's own Python implementation (gguf.quants), on values
+    with ties, zeros, a wide range and exact block maxima."""
+    quants = pytest.importorskip("gguf.quants")
+    from gguf import GGMLQuantizationType as Q
+
+    rng = np.random.default_rng(11)
+    rows = [rng.standard_normal(4096).astype(np.float32),
+            (rng.standard_normal(4096) * 1e-3).astype(np.float32),
+            rng.integers(-8, 8, 4096).astype(np.float32),
+            np.zeros(4096, np.float32),
+            (rng.standard_normal(4096) * 300).astype(np.float32)]
+    L = orc.lib()
+    t, nb, q_fn, d_fn = ((Q.Q4_0, 18, L.orc_q4_0_quantize, L.orc_q4_0_dequantize) if qtype == "q4_0" else
+                         (Q.Q8_0, 34, L.orc_q8_0_quantize, L.orc_q8_0_dequantize))
+    for x in rows:
+        ref = quants.quantize(x[None, :], t).reshape(-1)
+        got = np.empty(x.size // 32 * nb, np.uint8)
+        q_fn(orc.ptr(x), x.size, orc.ptr(got))
+        np.testing.assert_array_equal(got, ref)
+        back = np.empty(x.size, np.float32)
+        d_fn(orc.ptr(got), x.size, orc.ptr(back))
+        np.testing.assert_array_equal(back, quants.dequantize(ref[None, :], t).reshape(-1))
