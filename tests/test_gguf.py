@@ -360,3 +360,32 @@ def test_metadata_arrays(tmp_path):
         assert ti.lib().ti_gguf_meta_array_int(g.h, b"x.u8s", -1, C.byref(v)) == ti.TI_ERR_INVALID
         assert ti.lib().ti_gguf_meta_array_int(g.h, b"tokenizer.ggml.tokens", 0, C.byref(v)) == ti.TI_ERR_INVALID
         assert ti.lib().ti_gguf_meta_array_int(g.h, b"llama.block_count", 0, C.byref(v)) == ti.TI_ERR_NOT_FOUND
+
+
+@pytest.mark.parametrize("arch", ["llama", "qwen2", "gemma"])
+def test_tensor_names_match_the_gguf_package(tmp_path, arch):
+    """The reader's llama.cpp -> reference (Hugging Face) name mapping against the
+    llama.cpp project's own map (gguf.get_tensor_name_map) in the other direction:
+    every tensor of a 3-layer model comes back under its reference name."""
+    gg = pytest.importorskip("gguf")
+    arch_enum = {"llama": gg.MODEL_ARCH.LLAMA, "qwen2": gg.MODEL_ARCH.QWEN2, "gemma": gg.MODEL_ARCH.GEMMA}[arch]
+    names = ["model.embed_tokens.weight", "model.norm.weight", "lm_head.weight"]
+    for i in range(3):
+        p = f"model.layers.{i}."
+        names += [p + n for n in ("self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight",
+                                  "self_attn.o_proj.weight", "mlp.gate_proj.weight", "mlp.up_proj.weight",
+                                  "mlp.down_proj.weight", "input_layernorm.weight",
+                                  "post_attention_layernorm.weight")]
+        if arch == "qwen2":
+            names += [p + n for n in ("self_attn.q_proj.bias", "self_attn.k_proj.bias", "self_attn.v_proj.bias")]
+    m = gg.get_tensor_name_map(arch_enum, 3)
+    pairs = [(n, m.get_name(n, try_suffixes=(".weight", ".bias"))) for n in names]
+    # gemma ties the LM head to the embeddings: its files carry no output matrix
+    assert [n for n, gn in pairs if gn is None] == (["lm_head.weight"] if arch == "gemma" else [])
+    names = [n for n, gn in pairs if gn is not None]
+    gnames = [gn for _, gn in pairs if gn is not None]
+    p = tmp_path / "names.gguf"
+    meta = [("general.architecture", STR, arch)]
+    write(p, meta, [(g, GGML_F32, (32,), bytes(128)) for g in gnames])
+    with ti.Gguf(p) as g:
+        assert [g.reference_name(i) for i in range(len(g))] == names
