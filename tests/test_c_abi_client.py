@@ -74,3 +74,47 @@ def test_client_ids_equal_the_ctypes_engine(tmp_path, mode):
         want.append(int(eng.decode([sid], [want[-1]])[0]))
     eng.close()
     assert got == want
+
+
+def test_gguf_client_from_plain_c(tmp_path):
+    """The GGUF half of the ABI needs no GPU: tests/c_gguf_client.c (strict C99)
+    reads a file's model description, vocabulary and tensors, and prints what
+    the Python binding reads from the same file."""
+    import ti_b200 as ti
+    from gguf_writer import ARR, F32, GGML_F32, GGML_Q4_0, STR, U32, write
+
+    if not os.path.exists(ti.LIB_PATH):
+        pytest.skip("libti_b200.so not built")
+    exe = str(tmp_path / "c_gguf_client")
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I" + INC,
+                        os.path.join(HERE, "c_gguf_client.c"), "-o", exe, "-L" + PKG, "-lti_b200",
+                        "-Wl,-rpath," + PKG], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    rng = np.random.default_rng(2)
+    toks = ["<s>", "</s>", "hello", "wor ld"]
+    meta = [("general.architecture", STR, "llama"), ("llama.block_count", U32, 1),
+            ("llama.embedding_length", U32, 64), ("llama.feed_forward_length", U32, 128),
+            ("llama.attention.head_count", U32, 4), ("llama.attention.head_count_kv", U32, 2),
+            ("llama.attention.layer_norm_rms_epsilon", F32, 1e-5), ("tokenizer.ggml.tokens", ARR, (STR, toks))]
+    q4 = rng.integers(0, 256, size=(128, 2, 18), dtype=np.uint8)
+    q4[:, :, 0:2] = np.full((128, 2), 0.01, np.float16).view(np.uint8).reshape(128, 2, 2)
+    tensors = [("token_embd.weight", GGML_F32, (64, 4), rng.standard_normal(256).astype(np.float32).tobytes()),
+               ("blk.0.ffn_up.weight", GGML_Q4_0, (64, 128), q4.tobytes()),
+               ("blk.0.ffn_down.weight", 12, (256, 64), rng.integers(0, 256, 64 * 144, dtype=np.uint8).tobytes())]
+    path = tmp_path / "c.gguf"
+    write(path, meta, tensors)
+    out = subprocess.run([exe, str(path)], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    lines = out.stdout.splitlines()
+    with ti.Gguf(path) as g:
+        d = g.model_desc()
+        assert lines[0] == (f"desc arch {d.arch} hidden {d.hidden} layers {d.n_layers} heads {d.n_heads} "
+                            f"kv {d.n_kv_heads} head_dim {d.head_dim} inter {d.intermediate} vocab {d.vocab} "
+                            f"wfmt {d.weight_format}")
+        assert lines[1:1 + len(toks)] == [f"token {i} {t}" for i, t in enumerate(toks)]
+        want = []
+        for i in range(len(g)):
+            inf = g.info(i)
+            total = int(g.read(i).astype(np.uint64).sum())
+            want.append(f"tensor {inf['name']} type {inf['type']} ref {g.reference_name(i)} bf16sum {total}")
+        assert lines[1 + len(toks):] == want
