@@ -118,3 +118,23 @@ def test_gguf_client_from_plain_c(tmp_path):
             total = int(g.read(i).astype(np.uint64).sum())
             want.append(f"tensor {inf['name']} type {inf['type']} ref {g.reference_name(i)} bf16sum {total}")
         assert lines[1 + len(toks):] == want
+
+
+def test_integration_cpp_snippets_compile(tmp_path):
+    """The C++ blocks of INTEGRATION.md (the reference-side DecodeEngine binding)
+    compile against include/ti_b200.h and the reference's own headers."""
+    import re
+
+    ref_inc = os.environ.get("TI_REFERENCE_INCLUDE", "/root/reference/include")
+    if not os.path.isdir(ref_inc):
+        pytest.skip("reference headers not present")
+    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    blocks = re.findall(r"```cpp\n(.*?)```", text, flags=re.S)
+    assert blocks
+    nlohmann = "/opt/prime-rl/.venv/lib/python3.12/site-packages/include/cudnn_frontend/thirdparty"
+    for i, code in enumerate(blocks):
+        src = tmp_path / f"snippet{i}.cpp"
+        src.write_text(code)
+        r = subprocess.run(["g++", "-std=c++20", "-fsyntax-only", "-Wall", "-Wextra", "-I" + INC, "-I" + ref_inc,
+                            "-I" + nlohmann, "-I/usr/local/cuda/include", str(src)], capture_output=True, text=True)
+        assert r.returncode == 0, (i, r.stderr[-2000:])
