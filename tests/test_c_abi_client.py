@@ -138,3 +138,30 @@ def test_integration_cpp_snippets_compile(tmp_path):
         r = subprocess.run(["g++", "-std=c++20", "-fsyntax-only", "-Wall", "-Wextra", "-I" + INC, "-I" + ref_inc,
                             "-I" + nlohmann, "-I/usr/local/cuda/include", str(src)], capture_output=True, text=True)
         assert r.returncode == 0, (i, r.stderr[-2000:])
+
+
+def test_integration_c_and_python_snippets(tmp_path):
+    """INTEGRATION.md's C blocks compile as strict C99 inside a function, and its
+    Python blocks parse and name only attributes the ti_b200 binding has."""
+    import ast
+    import re
+
+    import ti_b200 as ti
+
+    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    for i, code in enumerate(re.findall(r"```c\n(.*?)```", text, flags=re.S)):
+        src = tmp_path / f"c{i}.c"
+        src.write_text('#include "ti_b200.h"\nvoid snippet(void) {\n' + code + "}\n")
+        r = subprocess.run(["gcc", "-std=c99", "-Wall", "-pedantic", "-Werror", "-Wno-unused-variable",
+                            "-Wno-unused-but-set-variable", "-I" + INC, "-fsyntax-only", str(src)],
+                           capture_output=True, text=True)
+        assert r.returncode == 0, (i, r.stderr)
+    engine_methods = set(dir(ti.Engine)) | set(dir(ti.Gguf))
+    for code in re.findall(r"```python\n(.*?)```", text, flags=re.S):
+        tree = ast.parse(code)
+        for node in ast.walk(tree):
+            if isinstance(node, ast.Attribute) and isinstance(node.value, ast.Name):
+                if node.value.id == "ti":
+                    assert hasattr(ti, node.attr), node.attr
+                elif node.value.id in ("eng", "g"):
+                    assert node.attr in engine_methods, node.attr
