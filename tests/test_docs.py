@@ -15,8 +15,8 @@ ROOTS = ("tensor-inference_b200/", "tests/", "oracle/", "profiles/", "include/ti
 @pytest.mark.parametrize("doc", ["DESIGN.md", "INTEGRATION.md", "README.md", "profiles/README.md"])
 def test_documents_name_existing_files(doc):
     missing = []
-    for tok in re.findall(r"`([^`\\s]+)`", open(os.path.join(ROOT, doc)).read()):
-        path = re.sub(r":\\d[\\d,\\-]*$", "", tok.split("::")[0].rstrip(",.;:"))
+    for tok in re.findall(r"`([^`\s]+)`", open(os.path.join(ROOT, doc)).read()):
+        path = re.sub(r":\d[\d,\-]*$", "", tok.split("::")[0].rstrip(",.;:"))
         if not path.startswith(ROOTS) or any(c in path for c in "*{…<"):
             continue
         if not any(os.path.exists(os.path.join(ROOT, p)) for p in (path, os.path.join("tensor-inference_b200", path))):
