@@ -244,3 +244,32 @@ def test_gguf_quantisers_match_the_gguf_package(orc, qtype):
         back = np.empty(x.size, np.float32)
         d_fn(orc.ptr(got), x.size, orc.ptr(back))
         np.testing.assert_array_equal(back, quants.dequantize(ref[None, :], t).reshape(-1))
+
+
+def test_oracle_under_sanitizers(tmp_path):
+    """The oracle (the parity anchor) built with AddressSanitizer + UBSan passes
+    its known-answer and sampling tests in a child process."""
+    import os
+    import subprocess
+    import sys
+
+    import host_sanitize
+
+    if not host_sanitize.runtime():
+        pytest.skip("gcc sanitizer runtimes not available")
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    lib = str(tmp_path / "liboracle_asan.so")
+    r = subprocess.run(["g++", "-O1", "-g", "-fsanitize=address,undefined", "-fno-sanitize-recover=all",
+                        "-fno-omit-frame-pointer", "-march=x86-64-v3", "-ffp-contract=off", "-fPIC", "-std=c++17",
+                        "-pthread", "-shared", "-o", lib, os.path.join(root, "oracle", "oracle.cpp")],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]
+    code = (f"import sys; sys.path[:0] = [{root!r}, {here!r}, {os.path.join(root, 'tensor-inference_b200')!r}]; "
+            f"import oracle; oracle.LIB_PATH = {lib!r}; import pytest; "
+            "sys.exit(pytest.main(['-q', '-x', '-p', 'no:cacheprovider', "
+            "'-k', 'not sanitizers and not agrees and not distribution', "  # the long statistical sweeps
+            f"{os.path.join(here, 'test_oracle_kat.py')!r}, {os.path.join(here, 'test_sampling.py')!r}]))")
+    r = subprocess.run([sys.executable, "-c", code], env=host_sanitize.env(), capture_output=True, text=True,
+                       timeout=900, cwd=root)
+    assert r.returncode == 0, (r.stdout[-2000:], r.stderr[-2000:])
