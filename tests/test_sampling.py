@@ -290,3 +290,23 @@ def test_oracle_matches_committed_reference_ids():
             assert got == want, (ri, si)
             checked += len(want)
     assert checked > 200
+
+
+@pytest.mark.parametrize("kind,temperature,p,k", [(oracle.SAMPLE_TOP_P, 1.0, 0.9, 0), (oracle.SAMPLE_TOP_P, 0.6, 1.0, 0),
+                                                   (oracle.SAMPLE_TOP_K, 1.2, 0.0, 50)])
+def test_exact_form_pick_is_monotone_in_the_draw(kind, temperature, p, k):
+    """The pick is the first token whose running weight reaches ceil(u W): with
+    draws sorted ascending, the picks' positions in the sampler's order (logit
+    descending, ties by ascending id) never decrease, and u = 0 picks the first."""
+    rng = np.random.default_rng(31)
+    for vocab in (50, 3000):
+        x = oracle.f32_to_bf16((rng.standard_normal(vocab) * 2).astype(np.float32))
+        xf = oracle.bf16_to_f32(x)
+        order = sorted(range(vocab), key=lambda i: (-xf[i], i))
+        pos = {tok: j for j, tok in enumerate(order)}
+        us = np.sort(np.concatenate([[0.0], oracle.sample_draws(vocab, 400)]))
+        picks = [pos[oracle.sample_exact(x, kind, temperature, p, k, float(u))] for u in us]
+        assert picks[0] == 0
+        assert all(a <= b for a, b in zip(picks, picks[1:]))
+        if kind == oracle.SAMPLE_TOP_K:
+            assert max(picks) < k
