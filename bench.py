@@ -1,6 +1,9 @@
 """Benchmark: Llama-3-8B-shape bf16 greedy decode on B200 (benchmark configuration 2).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B] [--no-b32]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-b32] [--no-qwen]
+                    [--no-70b] [--no-cpu-baseline] [--sampled] [--ttft]
+    python bench.py --profile [--layers L] [--prompt P] [--batch B] [--kernel KIND] [--ctx C]
+                    [--preset NAME] [--adapters A] [--lora-rank R] [--timeline trace.json]
 
 Prints ONE JSON line (rank 0).  `value` is decode tokens/s at batch 1 measured
 on the device (CUDA events around K chained decode steps, inputs resident in
@@ -9,6 +12,11 @@ HBM); `e2e` is the same metric through the public C ABI call
 descriptor and the D2H read of the greedy ids are inside the timed region.
 Weights (15 GB) are far larger than L2 (126 MB), so every step streams them
 from HBM; no L2 flush is needed.
+
+Opt-in extra fields: --sampled (batch 1 with device top-p sampling), --ttft (time
+to first token of a 512-token prompt).  --profile runs a short workload for ncu
+(or, with --timeline, traces the decode graph's kernels through the PyTorch
+profiler and prints their in-graph timeline); it never prints a bench line.
 
 --impl reference times the reference's decode step on the host CPU: the
 reference ships no CPU implementation (its every op is CUDA), so the CPU
