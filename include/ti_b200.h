@@ -306,8 +306,9 @@ typedef struct ti_sampling {
 /* The sampler of the ids ti_engine_decode / ti_engine_prefill(_chunked) return
  * for this sequence from now on; NULL or TI_SAMPLE_GREEDY restores greedy.
  * Under tensor parallelism every rank sets the same seeded sampler (ranks then
- * draw identical ids).  A bound device chain (ti_engine_bind, one GPU) samples
- * too: bind draws every step the sequence's reserved pages allow ahead, from a
+ * draw identical ids).  A bound device chain (ti_engine_bind) samples too (under
+ * tensor parallelism its graph all-gathers the logits before the sampler): bind
+ * draws every step the sequence's reserved pages allow ahead, from a
  * copy of its engine, and ti_engine_unbind advances the engine past the steps
  * taken, so the ids equal those of step-by-step decoding.  ti_seq_create starts
  * greedy; ti_seq_reset keeps the sampler. */

@@ -974,12 +974,23 @@ ti_status enqueue_step(ti_engine* e, int B, cudaStream_t s, int* launches, bool 
             if (ti_status st = enqueue_kernel(e, B, k, li, s, launches, lora, prefill)) return st;
     if (ti_status st = enqueue_kernel(e, B, kKLmHead, 0, s, launches, lora)) return st;
     if (!sample) return TI_OK;
-    TI_CHECK(e->tp.tp == 1 && e->d_draws && e->d_srows, TI_ERR_STATE, "sampled device chain: buffers not set up");
+    TI_CHECK(e->d_draws && e->d_srows, TI_ERR_STATE, "sampled device chain: buffers not set up");
     SampleArgs a;
-    a.logits = e->logits;
     a.vocab = e->V;
-    a.seg = e->V;
-    a.row_stride = (size_t)e->V;
+    if (e->tp.tp == 1) {
+        a.logits = e->logits;
+        a.seg = e->V;
+        a.row_stride = (size_t)e->V;
+    } else {
+        // every rank samples the same gathered rows ([rank][b][j]) with the same draws
+        const ncclResult_t r = nccl_api()->AllGather(e->logits, e->lgather, (size_t)B * e->Vl, ncclBfloat16, e->comm,
+                                                     s);
+        TI_CHECK(r == ncclSuccess, TI_ERR_CUDA, "ncclAllGather (sampled chain): %s", nccl_api()->GetErrorString(r));
+        a.logits = e->lgather;
+        a.seg = e->Vl;
+        a.seg_stride = (size_t)B * e->Vl;
+        a.row_stride = (size_t)e->Vl;
+    }
     a.rows = e->d_srows;
     a.hist = e->shist;
     a.out = e->out;
@@ -1618,8 +1629,6 @@ ti_status ti_engine_bind(ti_engine* e, int B, const int32_t* seq_ids, const int3
         if (ti_status st = seq_check(e, seq_ids[b])) return st;
         TI_CHECK(first_tokens[b] >= 0 && first_tokens[b] < e->V, TI_ERR_INVALID, "token out of range");
         const SeqState& s = e->seqs[seq_ids[b]];
-        TI_CHECK(s.smp.cfg.kind == TI_SAMPLE_GREEDY || e->tp.tp == 1, TI_ERR_UNSUPPORTED,
-                 "sequence %d samples top-p / top-k: a bound device chain samples on one GPU only", seq_ids[b]);
         TI_CHECK((int)s.pages.size() * kPageTokens > s.len, TI_ERR_STATE,
                  "sequence %d has no reserved page for its next token (ti_seq_reserve)", seq_ids[b]);
         h[4 + b] = first_tokens[b];

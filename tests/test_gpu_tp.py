@@ -204,3 +204,68 @@ def test_tp2_device_sampling(sampler):
     # vocabulary-parallel logits gathered from both ranks, sampled identically on each
     prompts = [oracle.fill_ids(f"ts{b}", n, b, SMALL["vocab"]) for b, n in enumerate((4, 9))]
     _run_tp(SMALL, prompts, steps=3, tol=2e-2, std=0.5, sampler=sampler)
+
+
+def _rank_chain(rank, world, nid, kw, prompts, steps, sampler, q):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    sys.path.insert(0, os.path.join(ROOT, "tensor-inference_b200"))
+    try:
+        import ti_b200 as tl
+
+        B = len(prompts)
+        eng = tl.Engine(tl.model_desc(**kw), device=rank, max_batch=B, max_seqs=B, max_seq_len=128, tp_size=world,
+                        tp_rank=rank, nccl_id=nid)
+        eng.init_synthetic(0, 0.5)
+        sids = [eng.seq_create() for _ in prompts]
+        first = []
+        for sid, p in zip(sids, prompts):
+            eng.set_sampler(sid, *sampler)
+            first.append(int(eng.prefill(sid, p)))
+            eng.seq_reserve(sid, len(p) + steps + 1)
+        eng.bind(sids, first)
+        for _ in range(steps):
+            eng.decode_device()
+        last = [int(v) for v in eng.unbind(steps)]
+        eng.check()
+        eng.close()
+        q.put((rank, first, last))
+    except BaseException as e:
+        q.put((rank, "error", repr(e)))
+        q.close()
+        q.join_thread()
+        os._exit(1)
+
+
+@pytest.mark.skipif(os.environ.get("TI_TEST_PENDING") != "1",
+                    reason="sampled device chains not yet run on a B200 (set TI_TEST_PENDING=1)")
+def test_tp2_sampled_device_chain_ranks_agree():
+    # the chain's graph all-gathers the logits before the sampler: both ranks feed
+    # themselves the same ids step after step
+    _need(2)
+    prompts = [oracle.fill_ids(f"tc{b}", n, b, SMALL["vocab"]) for b, n in enumerate((5, 8))]
+    nid = ti.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    sampler = (ti.SAMPLE_TOP_P, 0.9, 0.9, 0, 77)
+    procs = [ctx.Process(target=_rank_chain, args=(r, 2, nid, SMALL, prompts, 6, sampler, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        deadline = time.monotonic() + 300
+        while len(res) < 2:
+            try:
+                r = q.get(timeout=5)
+            except queue.Empty:
+                gone = [(i, p.exitcode) for i, p in enumerate(procs) if p.exitcode not in (None, 0)]
+                assert not gone, f"rank process(es) exited without a result: {gone}"
+                assert time.monotonic() < deadline, "ranks did not report within 300 s"
+                continue
+            assert r[1] != "error", r
+            res[r[0]] = r
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert res[0][1:] == res[1][1:]
