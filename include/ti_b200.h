@@ -134,9 +134,13 @@ ti_status ti_op_paged_attention(const void* qkv, int batch, int n_heads, int n_k
  * fully reserved by another framework's allocator).  No counterpart in the
  * reference.  Calls no allocator: the scratch is a fixed 8 MiB array that every
  * GPU loading this library holds until exit.  The first call on a device looks
- * up that array's device address (make it before any stream capture).  Sizes
- * whose scratch exceeds 8 MiB return TI_ERR_INVALID.  All calls share the
- * array, so calls that overlap on the GPU race; order them on one stream. */
+ * up that array's device address (make it before any stream capture); that
+ * address belongs to the device's CUDA context, so do not call this entry on a
+ * device after resetting it (cudaDeviceReset).  Sizes whose scratch exceeds
+ * 8 MiB return TI_ERR_INVALID.  All calls share the array, so calls that
+ * overlap on the GPU race; order them on one stream.  As with
+ * ti_op_paged_attention, out-of-range page ids or positions found on the device
+ * are skipped, not reported: validate page tables on the host. */
 ti_status ti_op_paged_attention_noalloc(const void* qkv, int batch, int n_heads, int n_kv, int head_dim,
                                         const int32_t* pos, const int32_t* seq, const int32_t* page_table,
                                         int pt_stride, void* k_pages, void* v_pages, int n_pages, int max_len,

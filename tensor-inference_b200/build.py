@@ -70,7 +70,7 @@ def build(verbose=False, ptxas_info=False):
         raise RuntimeError("nvcc failed:\n" + "\n".join(errs))
     objs = [o for o, _ in results]
     if not os.path.exists(LIB) or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart_static", "-ldl", "-lrt", "-lpthread"]
+        cmd = [NVCC] + ARCH + ["-shared", "-Xlinker", "--no-undefined", "-o", LIB] + objs + ["-lcudart_static", "-ldl", "-lrt", "-lpthread"]
         if verbose:
             print(" ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)

@@ -110,11 +110,23 @@ extern "C" ti_status ti_op_paged_attention(const void* qkv, int batch, int n_hea
 // call made on that device; make that first call before any stream capture.
 // All calls share the one array and it keeps the last call's contents, so
 // calls that overlap on the GPU (different streams, or different host threads
-// without ordering) race on it; order them on one stream.
+// without ordering) race on it; order them on one stream.  The cached address
+// belongs to the device's current CUDA context: a caller that destroys that
+// context (cudaDeviceReset) must not call this entry on that device afterwards.
 constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB per device
 static __device__ __align__(256) unsigned char g_paged_attn_scratch[kNoAllocScratchBytes];
 
 namespace {
+
+// The RoPE frequency table travels as a kernel argument (copied by value at
+// launch), so no host buffer has to outlive the call.
+struct FreqTable {
+    float f[128];
+};
+
+__global__ void k_store_freqs(FreqTable t, float* dst, int n) {
+    if ((int)threadIdx.x < n) dst[threadIdx.x] = t.f[threadIdx.x];
+}
 
 std::mutex g_scratch_mu;
 void* g_scratch_addr[64] = {};
@@ -174,10 +186,12 @@ extern "C" ti_status ti_op_paged_attention_noalloc(const void* qkv, int batch, i
     a.err = nullptr;
 
     cudaStream_t s = (cudaStream_t)stream;
-    // the same host-computed table as the pool-backed entry (ops.cu:235-278)
-    float host_freqs[128];
-    rope_freqs(head_dim, theta, scaling, host_freqs);
-    TI_CUDA(cudaMemcpyAsync(freqs, host_freqs, (size_t)head_dim / 2 * 4, cudaMemcpyHostToDevice, s));
+    // the same host-computed table as the pool-backed entry (ops.cu:235-278),
+    // written into the scratch by a one-warp-pair kernel that carries it by value
+    FreqTable t;
+    rope_freqs(head_dim, theta, scaling, t.f);
+    k_store_freqs<<<1, 128, 0, s>>>(t, freqs, head_dim / 2);
+    TI_CUDA(cudaGetLastError());
     // the merge counters must start at zero whatever the previous call left
     TI_CUDA(cudaMemsetAsync(counters, 0, nctr * 4, s));
     TI_CUDA(attn_launch(a, s, false));

@@ -95,3 +95,24 @@ def test_selftest_waits_validates_before_any_device_work(lib):
     out = (C.c_double * 2)()
     for bad in (0, -5, 10_000_001):
         assert lib.ti_selftest_waits(0, bad, out) == 1  # TI_ERR_INVALID
+
+
+BUILT_LIBRARIES = [
+    os.path.join(PKG, "libti_b200.so"),
+    os.path.join(SHIM, "libtensor_backend_b200.so"),
+    os.path.join(SHIM, "libref_models_on_b200.so"),
+    os.path.join(ROOT, "oracle", "_build", "liboracle.so"),
+    os.path.join(ROOT, "oracle", "_ref", "libref.so"),
+]
+
+
+@pytest.mark.parametrize("path", BUILT_LIBRARIES, ids=os.path.basename)
+def test_every_built_library_resolves_all_symbols(path):
+    """Open each library with RTLD_NOW in a fresh interpreter: an undefined symbol
+    (a source file missing from a link) fails here, on the CPU, instead of at the
+    first GPU test that loads the library."""
+    if not os.path.exists(path):
+        pytest.skip(f"{os.path.basename(path)} not built (its sources are not present here)")
+    code = f"import ctypes, os; ctypes.CDLL({path!r}, mode=os.RTLD_NOW)"
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]

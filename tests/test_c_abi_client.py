@@ -1,7 +1,7 @@
 """The C ABI from plain C: tests/c_abi_client.c compiles as strict C99 (and the
 header as C11 and C++17) with every warning an error, links against
 libti_b200.so alone, and, without a B200, stops at ti_init with a clear error.
-On a B200 (collected with TI_TEST_PENDING=1 until it has run there) its greedy
+On a B200 its greedy
 and top-p ids equal those of the same engine driven through ctypes."""
 import os
 import subprocess
@@ -50,8 +50,6 @@ def test_client_builds_and_reports_missing_hardware(tmp_path):
 
 
 @pytest.mark.gpu
-@pytest.mark.skipif(os.environ.get("TI_TEST_PENDING") != "1",
-                    reason="C client not yet run on a B200 (set TI_TEST_PENDING=1)")
 @pytest.mark.parametrize("mode", ["greedy", "p"])
 def test_client_ids_equal_the_ctypes_engine(tmp_path, mode):
     import ti_b200 as ti
@@ -118,50 +116,3 @@ def test_gguf_client_from_plain_c(tmp_path):
             total = int(g.read(i).astype(np.uint64).sum())
             want.append(f"tensor {inf['name']} type {inf['type']} ref {g.reference_name(i)} bf16sum {total}")
         assert lines[1 + len(toks):] == want
-
-
-def test_integration_cpp_snippets_compile(tmp_path):
-    """The C++ blocks of INTEGRATION.md (the reference-side DecodeEngine binding)
-    compile against include/ti_b200.h and the reference's own headers."""
-    import re
-
-    ref_inc = os.environ.get("TI_REFERENCE_INCLUDE", "/root/reference/include")
-    if not os.path.isdir(ref_inc):
-        pytest.skip("reference headers not present")
-    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
-    blocks = re.findall(r"```cpp\n(.*?)```", text, flags=re.S)
-    assert blocks
-    nlohmann = "/opt/prime-rl/.venv/lib/python3.12/site-packages/include/cudnn_frontend/thirdparty"
-    for i, code in enumerate(blocks):
-        src = tmp_path / f"snippet{i}.cpp"
-        src.write_text(code)
-        r = subprocess.run(["g++", "-std=c++20", "-fsyntax-only", "-Wall", "-Wextra", "-I" + INC, "-I" + ref_inc,
-                            "-I" + nlohmann, "-I/usr/local/cuda/include", str(src)], capture_output=True, text=True)
-        assert r.returncode == 0, (i, r.stderr[-2000:])
-
-
-def test_integration_c_and_python_snippets(tmp_path):
-    """INTEGRATION.md's C blocks compile as strict C99 inside a function, and its
-    Python blocks parse and name only attributes the ti_b200 binding has."""
-    import ast
-    import re
-
-    import ti_b200 as ti
-
-    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
-    for i, code in enumerate(re.findall(r"```c\n(.*?)```", text, flags=re.S)):
-        src = tmp_path / f"c{i}.c"
-        src.write_text('#include "ti_b200.h"\nvoid snippet(void) {\n' + code + "}\n")
-        r = subprocess.run(["gcc", "-std=c99", "-Wall", "-pedantic", "-Werror", "-Wno-unused-variable",
-                            "-Wno-unused-but-set-variable", "-I" + INC, "-fsyntax-only", str(src)],
-                           capture_output=True, text=True)
-        assert r.returncode == 0, (i, r.stderr)
-    engine_methods = set(dir(ti.Engine)) | set(dir(ti.Gguf))
-    for code in re.findall(r"```python\n(.*?)```", text, flags=re.S):
-        tree = ast.parse(code)
-        for node in ast.walk(tree):
-            if isinstance(node, ast.Attribute) and isinstance(node.value, ast.Name):
-                if node.value.id == "ti":
-                    assert hasattr(ti, node.attr), node.attr
-                elif node.value.id in ("eng", "g"):
-                    assert node.attr in engine_methods, node.attr

@@ -1,5 +1,5 @@
-"""Every reference citation in the repository (code comments, docstrings and
-the documents) names a file that exists in the reference and lines within it:
+"""Every reference citation in the repository's code (comments and docstrings)
+names a file that exists in the reference and lines within it:
 full paths (src/..., include/...) and bare file names (ops.cu:46-88), which
 must resolve to exactly one reference file.  Needs the reference tree; skipped
 where it is absent."""
@@ -10,9 +10,8 @@ import re
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF = os.environ.get("TI_REFERENCE_DIR", "/root/reference")
+REF = os.environ.get("TI_REFERENCE_DIR") or os.path.join(os.path.dirname(ROOT), "reference")
 SKIP_DIRS = ("_work", "baseline", "oracle/_ref", "gpurun_out")
-OWN_DOCS_OF_THE_BUILD = ("SURVEY.md", "BASELINE.md")
 FULL = re.compile(r"((?:src|include|tools|docs)/[\w./-]+\.(?:cpp|hpp|cu|h|md|txt|json)):(\d+)(?:-(\d+))?")
 BARE = re.compile(r"(?<![\w/])([A-Za-z_]\w*\.(?:cpp|hpp|cu|md|txt)):(\d+)(?:-(\d+))?")
 
@@ -21,9 +20,9 @@ def _sources():
     out = []
     for f in glob.glob(os.path.join(ROOT, "**", "*"), recursive=True):
         rel = os.path.relpath(f, ROOT)
-        if rel.startswith(SKIP_DIRS) or rel in OWN_DOCS_OF_THE_BUILD or not os.path.isfile(f):
+        if rel.startswith(SKIP_DIRS) or not os.path.isfile(f):
             continue
-        if rel.endswith((".md", ".cu", ".cuh", ".cpp", ".h", ".py", ".c")):
+        if rel.endswith((".cu", ".cuh", ".cpp", ".h", ".py", ".c")):
             out.append(rel)
     return out
 

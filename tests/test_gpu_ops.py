@@ -259,8 +259,6 @@ def test_init_shutdown_and_ops_after_it():
     np.testing.assert_array_equal(do.to_array(x.shape, np.uint16), before)
 
 
-@pytest.mark.skipif(os.environ.get("TI_TEST_PENDING") != "1",
-                    reason="wait self-test not yet run on a B200 (set TI_TEST_PENDING=1)")
 def test_bounded_waits_give_up_and_report():
     # a flag nothing writes and an mbarrier nothing completes, 20 ms each: both
     # waits end, set their error bits, and the context stays usable

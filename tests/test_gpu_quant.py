@@ -122,8 +122,6 @@ def test_quantised_decode_batched(wf):
     _parity(dict(SMALL, weight_format=wf), [2 + b % 5 for b in range(19)], steps=2)
 
 
-@pytest.mark.skipif(os.environ.get("TI_TEST_PENDING") != "1",
-                    reason="eight-token quantised GEMV not yet run on a B200 (set TI_TEST_PENDING=1)")
 @pytest.mark.parametrize("wf", [ti.WFMT_Q4_0, ti.WFMT_Q8_0])
 def test_quantised_gemv_eight_tokens_qwen7b_shapes(wf, monkeypatch):
     # TI_TC_MIN_BATCH=9 keeps a batch of 8 on the GEMV (its 8-token instance; the

@@ -10,10 +10,7 @@ logit value as the reference's own sampler (pinned against its code).
 
 Draws: the engine's per-sequence std::mt19937_64 gives the reference's
 sequence, which oracle.sample_draws reproduces (top-p: u_0, u_1, ...; top-k:
-u_0 at every step).
-
-These tests are collected only with TI_TEST_PENDING=1 until the kernel
-has passed them on a B200."""
+u_0 at every step)."""
 import ctypes as C
 import os
 
@@ -24,9 +21,7 @@ import oracle
 import ti_b200 as ti
 from gpu_util import DevBuf
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("TI_TEST_PENDING") != "1",
-                                 reason="device sampler not yet run on a B200 (set TI_TEST_PENDING=1)")]
+pytestmark = pytest.mark.gpu
 
 P, K = oracle.SAMPLE_TOP_P, oracle.SAMPLE_TOP_K
 SMALL = dict(arch=ti.ARCH_LLAMA, hidden=256, n_layers=2, n_heads=4, n_kv_heads=2, head_dim=64, intermediate=512,

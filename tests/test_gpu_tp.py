@@ -197,8 +197,6 @@ def test_tp2_lora_tensor_core_batch():
     _run_tp(SMALL, prompts, steps=2, tol=2e-2, adapters=ads, per_seq=[b % 3 - 1 for b in range(12)])
 
 
-@pytest.mark.skipif(os.environ.get("TI_TEST_PENDING") != "1",
-                    reason="device sampler not yet run on a B200 (set TI_TEST_PENDING=1)")
 @pytest.mark.parametrize("sampler", [(ti.SAMPLE_TOP_P, 0.8, 0.9, 0, 17), (ti.SAMPLE_TOP_K, 1.0, 0.0, 25, 18)])
 def test_tp2_device_sampling(sampler):
     # vocabulary-parallel logits gathered from both ranks, sampled identically on each
@@ -236,8 +234,6 @@ def _rank_chain(rank, world, nid, kw, prompts, steps, sampler, q):
         os._exit(1)
 
 
-@pytest.mark.skipif(os.environ.get("TI_TEST_PENDING") != "1",
-                    reason="sampled device chains not yet run on a B200 (set TI_TEST_PENDING=1)")
 def test_tp2_sampled_device_chain_ranks_agree():
     # the chain's graph all-gathers the logits before the sampler: both ranks feed
     # themselves the same ids step after step
