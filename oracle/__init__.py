@@ -87,6 +87,7 @@ _SIGS = {
     "orc_seq_create": (P, [P, I]),
     "orc_seq_destroy": (None, [P]),
     "orc_seq_len": (I, [P]),
+    "orc_seq_fill_synthetic": (I, [P, I, U64, F]),
     "orc_model_forward": (I, [P, P, P, I, I, P, P]),
     "orc_seq_last_hidden": (I, [P, P, I]),
     "orc_seq_read_kv": (I, [P, I, I, P, I]),
@@ -245,6 +246,10 @@ class Seq:
         if rc != 0:
             raise ValueError(f"oracle forward failed ({rc})")
         return lb, lf
+
+    def fill_synthetic(self, length, seed=0, std=1.0):
+        """`length` cached tokens with seeded K/V rows in every layer (no prefill)"""
+        assert lib().orc_seq_fill_synthetic(self.h, length, seed, std) == 0
 
     def read_kv(self, layer, which, length):
         d = self.m.desc

@@ -907,6 +907,19 @@ extern "C" orc_seq* orc_seq_create(orc_model* m, int max_seq) {
 extern "C" void orc_seq_destroy(orc_seq* s) { delete s; }
 extern "C" int orc_seq_len(const orc_seq* s) { return s->len; }
 
+// A context of `len` cached tokens with seeded N(0, std) K/V rows in every
+// layer (no prefill), for timing decode steps at a given context length.
+extern "C" int orc_seq_fill_synthetic(orc_seq* s, int len, uint64_t seed, float std_) {
+    if (len < 0 || len > s->max_seq) return 1;
+    const size_t n = (size_t)len * s->m->d.n_kv_heads * s->m->d.head_dim;
+    for (size_t li = 0; li < s->k.size(); ++li) {
+        orc_fill_bf16(s->k[li].data(), n, seed, 2 * li + 1, std_);
+        orc_fill_bf16(s->v[li].data(), n, seed, 2 * li + 2, std_);
+    }
+    s->len = len;
+    return 0;
+}
+
 extern "C" int orc_seq_last_hidden(const orc_seq* s, uint16_t* out, int hidden) {
     if ((int)s->last_hidden.size() != hidden) return 1;
     std::memcpy(out, s->last_hidden.data(), (size_t)hidden * 2);

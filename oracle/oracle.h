@@ -142,6 +142,9 @@ typedef struct orc_seq orc_seq;
 orc_seq* orc_seq_create(orc_model* m, int max_seq);
 void orc_seq_destroy(orc_seq* s);
 int orc_seq_len(const orc_seq* s);
+/* A context of `len` cached tokens with seeded N(0, std) K/V rows in every layer
+ * (no prefill), for timing decode steps at a given context length. */
+int orc_seq_fill_synthetic(orc_seq* s, int len, uint64_t seed, float std_);
 /* One forward call (prefill when n > 1, decode when n == 1), as the reference's
  * Model::forward.  Writes bf16 logits of the LAST row to logits_bf16 (vocab),
  * fp32 logits (pre-rounding) of the last row to logits_f32; either may be NULL.
