@@ -112,11 +112,6 @@ TI_DEVICE_INLINE void mma_16816_bf16(float* c, const uint32_t* a, uint32_t b0, u
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
-TI_DEVICE_INLINE float ex2(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
 // byte offset of element (row, d) in a [HD/64][C][64] bf16 tile with 128-byte swizzled rows
 TI_DEVICE_INLINE uint32_t tile_off(int C, int row, int d) {
     const int hh = d >> 6, cc = (d & 63) >> 3;

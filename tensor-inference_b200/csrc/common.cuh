@@ -15,7 +15,7 @@ namespace ti {
 typedef __nv_bfloat16 bf16;
 
 // Error bits written by bounded device waits (engine error word).
-enum : int { kErrTimeoutFull = 1, kErrTimeoutEmpty = 2, kErrTimeoutPeer = 4, kErrBadIndex = 8 };
+enum : int { kErrTimeoutFull = 1, kErrTimeoutEmpty = 2, kErrTimeoutPeer = 4, kErrBadIndex = 8, kErrTimeoutGrid = 16 };
 // Iteration bound for every spin on an mbarrier or flag.  try_wait suspends
 // for a hardware-defined interval per call, so this is seconds of waiting.
 constexpr uint32_t kSpinLimit = 1u << 24;
@@ -28,6 +28,13 @@ TI_DEVICE_INLINE bf16 f2bf(float v) { return __float2bfloat16_rn(v); }
 TI_DEVICE_INLINE float round_bf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 TI_DEVICE_INLINE uint32_t pack_bf2(float lo, float hi) {
     return (uint32_t)__bfloat16_as_ushort(f2bf(lo)) | ((uint32_t)__bfloat16_as_ushort(f2bf(hi)) << 16);
+}
+
+// 2^x (ex2.approx, relative error about 2^-22; 2^-inf = +0)
+TI_DEVICE_INLINE float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 // ------------------------------------------------------------------ PDL
@@ -125,6 +132,11 @@ TI_DEVICE_INLINE void tma_load_2d(void* dst, const CUtensorMap* map, int x, int 
 TI_DEVICE_INLINE unsigned int ld_acquire_sys(const unsigned int* p) {
     unsigned int v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+TI_DEVICE_INLINE unsigned int ld_acquire_gpu(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 TI_DEVICE_INLINE void st_release_sys(unsigned int* p, unsigned int v) {

@@ -131,6 +131,11 @@ struct ti_engine {
     int* err = nullptr;
     float *part_o = nullptr, *part_ml = nullptr;
     unsigned int* counters = nullptr;
+    // attention fused into the o projection (single-token steps): per-CTA partials,
+    // per-kv-head tickets and the grid counters ([2]); fuse_ao: the step uses it
+    float* att_part = nullptr;
+    unsigned int *att_ticket = nullptr, *att_sync = nullptr;
+    bool fuse_ao = false;
     int attn_splits_n = 1, attn_max_chunk = 0;
     // tensor-core path (batches of tc_min..256 tokens): RMSNorm'd rows, partial
     // tiles shared between CTAs and their tickets
@@ -546,6 +551,21 @@ ti_status build(ti_engine* e) {
              ti_last_error());
     TI_CHECK(dalloc_t(e, &e->counters, (size_t)B * nkv, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s", ti_last_error());
     TI_CUDA(cudaMemset(e->counters, 0, (size_t)B * nkv * 4));
+    {
+        // single-token steps run attention inside the o projection's GEMV
+        // (TI_FUSED_ATTN=0: the separate attention kernel instead)
+        const char* env = std::getenv("TI_FUSED_ATTN");
+        e->fuse_ao = !(env && std::atoi(env) == 0) && G <= 8 && (hd == 64 || hd == 128) && e->sms >= nkv &&
+                     (nq * hd) % 128 == 0;
+        if (e->fuse_ao) {
+            TI_CHECK(dalloc_t(e, &e->att_part, (size_t)e->sms * G * (hd + 2), &e->bytes_work) == TI_OK, TI_ERR_OOM,
+                     "%s", ti_last_error());
+            TI_CHECK(dalloc_t(e, &e->att_ticket, (size_t)nkv + 2, &e->bytes_work) == TI_OK, TI_ERR_OOM, "%s",
+                     ti_last_error());
+            TI_CUDA(cudaMemset(e->att_ticket, 0, ((size_t)nkv + 2) * 4));
+            e->att_sync = e->att_ticket + nkv;
+        }
+    }
     TI_CUDA(cudaDeviceSynchronize());
     return TI_OK;
 }
@@ -813,6 +833,9 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             g.lora.sec2 = QW + nkv * hd;
         }
     };
+    // a single-token decode step whose o projection has no LoRA runs attention
+    // inside the o projection's GEMV (attn_fused.cuh): no attention launch
+    const bool fused_ao = e->fuse_ao && B == 1 && !prefill && !lora_on(1) && !(e->xn && B >= e->tc_min);
     switch (kind) {
         case kKQkv: {
             GemvArgs q;
@@ -845,6 +868,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             return gemm(q, kEpiStore, H, e->qkv_rows, 0);
         }
         case kKAttn: {
+            if (fused_ao) return TI_OK;
             int mc = 0;
             const int splits = attn_splits(B, nkv, hd, e->o.max_seq_len, e->sms, &mc);
             AttnArgs at;
@@ -898,6 +922,27 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             ov.resid_stride = H;
             ov.err = e->err;
             set_next(ov, l.wgu, I, H, 2);
+            if (fused_ao) {
+                GemvAttn& t = ov.att;
+                t.qkv = e->qkv;
+                t.nq = nq;
+                t.nkv = nkv;
+                t.hd = hd;
+                t.pos = e->dd_pos();
+                t.seq = e->dd_seq();
+                t.page_table = e->page_table;
+                t.pt_stride = e->pt_stride;
+                t.kc = e->kpool + (size_t)li * e->kv_layer_elems;
+                t.vc = e->vpool + (size_t)li * e->kv_layer_elems;
+                t.n_pages = e->n_pages;
+                t.freqs = e->freqs;
+                t.scale = 1.0f / sqrtf((float)hd);  // ops.cu:455
+                t.window = d.arch == TI_ARCH_MISTRAL ? e->d_desc + 1 : nullptr;
+                t.out = e->attn;
+                t.part = e->att_part;
+                t.ticket = e->att_ticket;
+                t.sync = e->att_sync;
+            }
             if (lora_on(1)) {
                 if (ti_status st = shrink(1, e->attn, QW, nullptr)) return st;
                 set_lora(ov, 1);
@@ -1095,7 +1140,7 @@ ti_status read_err(ti_engine* e, int32_t word) {
     if (word) {
         int zero = 0;
         cudaMemcpy(e->err, &zero, 4, cudaMemcpyHostToDevice);
-        return fail(word & (kErrTimeoutFull | kErrTimeoutEmpty | kErrTimeoutPeer) ? TI_ERR_TIMEOUT : TI_ERR_STATE,
+        return fail(word & (kErrTimeoutFull | kErrTimeoutEmpty | kErrTimeoutPeer | kErrTimeoutGrid) ? TI_ERR_TIMEOUT : TI_ERR_STATE,
                     "device reported error bits 0x%x", word);
     }
     return TI_OK;

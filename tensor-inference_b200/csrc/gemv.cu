@@ -29,6 +29,7 @@
 //     wait for one another.
 //   epilogue warp: per stage, sums the 16 warp partials of each row in warp
 //     order (deterministic) and applies the fused epilogue.
+#include "attn_fused.cuh"
 #include "common.cuh"
 #include "kernels.h"
 #include "lora_epi.cuh"
@@ -48,13 +49,14 @@ constexpr int kRowsMax = 12;  // rows per stage (per unit) upper bound, for one 
 
 struct GemvSmem {
     uint32_t stage_bytes, stages_off, full_off, empty_off, pfull_off, pempty_off, part_off, red_off, xs_off, epi_off,
-        total;
+        att_off, total;
 };
 
 // rows_cap: most rows one CTA owns; the epilogue warp keeps their residual
 // (nb rows) and bias values in shared memory
+// att_bytes: the fused attention phase's region (0 without it)
 __host__ __device__ inline GemvSmem gemv_smem_layout(int K, int wf, int units, int rows_per_stage, int stages,
-                                                     int nb, bool x_in_smem, int rows_cap) {
+                                                     int nb, bool x_in_smem, int rows_cap, uint32_t att_bytes = 0) {
     GemvSmem L;
     uint32_t sb = (uint32_t)(rows_per_stage * units * wrow_bytes(K, wf));
     sb = (sb + 127u) & ~127u;
@@ -79,6 +81,9 @@ __host__ __device__ inline GemvSmem gemv_smem_layout(int K, int wf, int units, i
     o = (o + 15u) & ~15u;
     L.epi_off = o;
     o += (uint32_t)(nb + 1) * rows_cap * 2;
+    o = (o + 15u) & ~15u;
+    L.att_off = o;
+    o += att_bytes;
     o = (o + 15u) & ~15u;
     L.total = o;
     return L;
@@ -165,7 +170,11 @@ TI_DEVICE_INLINE float dot8_f32w(const float2 w[4], const uint4 x, float acc) {
 // XR == 0: NB tokens, activation slices in shared memory.
 // RG: compile-time bound on rows per stage (per unit).
 // WF: weight row format (kWBf16 / kWQ4 / kWQ8).
-template <int NB, int EPI, int XR, int RG, int WF>
+// ATT > 0: one token whose decode attention (attn_fused.cuh) the consumer warps
+//   run first; it writes x (= a.att.out), which the prologue then reads from L2.
+//   The instance fixes the head geometry: 1 / 2 head_dim 128 with <= 4 / <= 8
+//   q heads per kv head, 3 / 4 head_dim 64 likewise.
+template <int NB, int EPI, int XR, int RG, int WF, int ATT = 0>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemv(const GemvArgs a, const int rows_per_stage, const int stages, const int pf) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -174,7 +183,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int XRR = XS ? 1 : XR;
     const int K = a.K;
     const int rows_cap = (a.N + (int)gridDim.x - 1) / (int)gridDim.x;
-    const GemvSmem L = gemv_smem_layout(K, WF, U, rows_per_stage, stages, NB, XS, rows_cap);
+    const uint32_t att_bytes = ATT ? gemv_attn_smem(a.att.nq / a.att.nkv, a.att.hd, a.att.warps) : 0u;
+    const GemvSmem L = gemv_smem_layout(K, WF, U, rows_per_stage, stages, NB, XS, rows_cap, att_bytes);
     const size_t rb = wrow_bytes(K, WF);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.full_off);
     uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L.empty_off);
@@ -392,7 +402,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     // ------------------------------------------------------------ consumers: prologue
-    pdl_wait();  // x is produced by the previous kernel
+    if constexpr (ATT > 0) attn_fused_prefetch(a.att, warp, lane, cta, G);
+    pdl_wait();  // x (or, with ATT, the token's q|k|v) is produced by the previous kernel
+    if constexpr (ATT > 0) {
+        constexpr int AHD = ATT <= 2 ? 128 : 64, AGM = ATT % 2 == 1 ? 4 : 8;
+        attn_fused_phase<AHD, AGM>(a.att, reinterpret_cast<float*>(smem + L.att_off), threadIdx.x,
+                                   kConsumerWarps * 32, cta, G, a.err);
+    }
     const int cols_per_warp = K / kConsumerWarps;
     const int col0 = warp * cols_per_warp;
     const int n_sc = cols_per_warp / 8;  // 16-byte sub-chunks per warp row slice
@@ -406,7 +422,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int j = 0; j < XRR; ++j) {
                 const int sc = j * 32 + lane;
-                xr[j] = sc < n_sc ? *reinterpret_cast<const uint4*>(a.x + col0 + sc * 8) : make_uint4(0, 0, 0, 0);
+                // with ATT, x was written by other CTAs of this grid: read it from L2
+                xr[j] = sc >= n_sc  ? make_uint4(0, 0, 0, 0)
+                        : ATT > 0   ? __ldcg(reinterpret_cast<const uint4*>(a.x + col0 + sc * 8))
+                                    : *reinterpret_cast<const uint4*>(a.x + col0 + sc * 8);
                 if (norm) ss = sumsq8(xr[j], ss);
             }
             if (norm) {
@@ -584,9 +603,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ host side
-template <int NB, int EPI, int XR, int RG, int WF>
+template <int NB, int EPI, int XR, int RG, int WF, int ATT = 0>
 static const void* fn() {
-    return reinterpret_cast<const void*>(&k_gemv<NB, EPI, XR, RG, WF>);
+    return reinterpret_cast<const void*>(&k_gemv<NB, EPI, XR, RG, WF, ATT>);
+}
+
+// fused attention + o projection: one token, the o projection's epilogues
+// (residual, or the tensor-parallel store), activation slice in registers;
+// geo = the ATT head-geometry index
+template <int EPI, int WF, int XR>
+static const void* pick_att_geo(int geo) {
+    switch (geo) {
+        case 1: return fn<1, EPI, XR, kRowsMax, WF, 1>();
+        case 2: return fn<1, EPI, XR, kRowsMax, WF, 2>();
+        case 3: return fn<1, EPI, XR, kRowsMax, WF, 3>();
+        case 4: return fn<1, EPI, XR, kRowsMax, WF, 4>();
+        default: return nullptr;
+    }
+}
+template <int EPI, int WF>
+static const void* pick_att(int xr, int geo) {
+    switch (xr) {
+        case 1: return pick_att_geo<EPI, WF, 1>(geo);
+        case 2: return pick_att_geo<EPI, WF, 2>(geo);
+        default: return nullptr;
+    }
 }
 
 template <int EPI, int WF>
@@ -659,11 +700,32 @@ bool gemv_plan(const GemvArgs& a, int epi, int device, GemvPlan* plan, std::stri
     int stages = (int)std::min<size_t>(8, std::max<size_t>(2, (size_t)tune_kb("TI_GEMV_RING_KB", 200) * 1024 / stage_bytes));
     const int grid = std::min(num_sms(device), a.N);
     const int rows_cap = (a.N + grid - 1) / grid;
+    // fused attention: one token, the o projection's epilogues, a supported head geometry;
+    // merge slots for as many page-scoring warps as ~20 KB of shared memory holds
+    const bool att = a.att.nq > 0;
+    int att_warps = 0, att_geo = 0;
+    uint32_t att_bytes = 0;
+    if (att) {
+        const int G = a.att.nkv > 0 && a.att.nq % a.att.nkv == 0 ? a.att.nq / a.att.nkv : 0;
+        if (a.nb != 1 || (epi != kEpiResid && epi != kEpiStore) || (xr != 1 && xr != 2) || G < 1 ||
+            G > kAttnFusedMaxGroup || (a.att.hd != 64 && a.att.hd != 128) || grid < a.att.nkv ||
+            a.K != a.att.nq * a.att.hd || !a.att.out || !a.att.part || !a.att.ticket || !a.att.sync) {
+            if (why) *why = "gemv: fused attention needs one token, head_dim 64/128, <= 8 q heads per kv head";
+            return false;
+        }
+        att_geo = (a.att.hd == 128 ? 1 : 3) + (G > 4 ? 1 : 0);
+        const int fl = 20 * 1024 / 4 - (G + 2) * a.att.hd;
+        att_warps = std::max(1, std::min(kConsumerWarps, fl / (G * (a.att.hd + 2))));
+        // TI_ATT_WARPS caps them (a test makes warps take several pages at short contexts)
+        if (const char* v = std::getenv("TI_ATT_WARPS"))
+            if (std::atoi(v) >= 1) att_warps = std::min(att_warps, std::atoi(v));
+        att_bytes = gemv_attn_smem(G, a.att.hd, att_warps);
+    }
     int max_smem = 0;
     cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
     GemvSmem L;
     for (;;) {
-        L = gemv_smem_layout(a.K, a.wfmt, U, rps, stages, nbt, xs, rows_cap);
+        L = gemv_smem_layout(a.K, a.wfmt, U, rps, stages, nbt, xs, rows_cap, att_bytes);
         if ((int)L.total <= max_smem) break;
         if (stages > 2) --stages;
         else if (rps > 1) --rps;
@@ -673,7 +735,17 @@ bool gemv_plan(const GemvArgs& a, int epi, int device, GemvPlan* plan, std::stri
         }
     }
     const void* f = nullptr;
-    switch (a.wfmt * 4 + epi) {
+    if (att) {
+        switch (a.wfmt * 4 + epi) {
+            case kEpiStore: f = pick_att<kEpiStore, kWBf16>(xr, att_geo); break;
+            case kEpiResid: f = pick_att<kEpiResid, kWBf16>(xr, att_geo); break;
+            case 4 * kWQ4 + kEpiStore: f = pick_att<kEpiStore, kWQ4>(xr, att_geo); break;
+            case 4 * kWQ4 + kEpiResid: f = pick_att<kEpiResid, kWQ4>(xr, att_geo); break;
+            case 4 * kWQ8 + kEpiStore: f = pick_att<kEpiStore, kWQ8>(xr, att_geo); break;
+            case 4 * kWQ8 + kEpiResid: f = pick_att<kEpiResid, kWQ8>(xr, att_geo); break;
+            default: break;
+        }
+    } else switch (a.wfmt * 4 + epi) {
         case kEpiStore: f = pick<kEpiStore, kWBf16>(a.nb, xr); break;
         case kEpiResid: f = pick<kEpiResid, kWBf16>(a.nb, xr); break;
         case kEpiGlu: f = pick<kEpiGlu, kWBf16>(a.nb, xr); break;
@@ -697,6 +769,7 @@ bool gemv_plan(const GemvArgs& a, int epi, int device, GemvPlan* plan, std::stri
     }
     plan->rows_per_stage = rps;
     plan->stages = stages;
+    plan->att_warps = att_warps;
     plan->grid = grid;
     plan->smem = L.total;
     plan->func = f;
@@ -708,6 +781,7 @@ bool gemv_plan(const GemvArgs& a, int epi, int device, GemvPlan* plan, std::stri
 cudaError_t gemv_launch(const GemvArgs& a, int epi, const GemvPlan& plan, cudaStream_t s, bool pdl) {
     (void)epi;
     GemvArgs args = a;
+    args.att.warps = plan.att_warps;
     int rps = plan.rows_per_stage, st = plan.stages, pf = plan.prefetch;
     void* params[] = {&args, &rps, &st, &pf};
     return launch_pdl(plan.func, dim3(plan.grid), dim3(kThreads), plan.smem, s, params, pdl);

@@ -107,6 +107,36 @@ __host__ __device__ inline size_t wrow_bytes(int K, int wf) {
     return wf == kWQ4 ? (size_t)K / 2 + (size_t)K / 16 : wf == kWQ8 ? (size_t)K + (size_t)K / 16 : (size_t)K * 2;
 }
 
+// Decode attention of one token run inside the o-projection GEMV, ahead of its
+// prologue: the work of ops::rope x2, the K/V cache write, ops::slice x2 and
+// ops::attention for one layer (llama_model.cpp:147-182).  The kernel's x is
+// the attention output, written by the kernel itself.
+struct GemvAttn {
+    const uint16_t* qkv = nullptr;  // the token's q|k|v before RoPE, bf16 [(nq + 2 nkv) * hd]
+    int nq = 0, nkv = 0, hd = 0;    // nq = 0: off
+    const int32_t* pos = nullptr;   // [1] tokens already cached for the sequence (device)
+    const int32_t* seq = nullptr;   // [1] the sequence's page-table row (device)
+    const int32_t* page_table = nullptr;
+    int pt_stride = 0;
+    uint16_t* kc = nullptr;  // this layer's K pages [n_pages][nkv][16][hd] bf16
+    uint16_t* vc = nullptr;  // V pages, same layout
+    int n_pages = 0;
+    const float* freqs = nullptr;  // [hd / 2] RoPE frequencies
+    float scale = 0.f;             // 1 / sqrt(hd)
+    const int* window = nullptr;   // device sliding window (Mistral), or window_const when null; <= 0 = none
+    int window_const = -1;
+    uint16_t* out = nullptr;  // attention output bf16 [nq * hd] (the GEMV's x)
+    float* part = nullptr;    // [grid][nq / nkv][hd + 2] per-CTA partials
+    unsigned int* ticket = nullptr;  // [nkv] arrivals per kv head (zero; the merging CTA resets)
+    unsigned int* sync = nullptr;    // [2] heads merged, CTAs past the wait (zero; the last CTA resets)
+    int warps = 0;                   // consumer warps that score pages (shared-memory merge slots)
+};
+// shared memory of the attention phase: rotated q [G][hd], the token's k and v
+// [2][hd], merge slots [warps][G][hd + 2] (fp32), one flag
+__host__ __device__ inline uint32_t gemv_attn_smem(int G, int hd, int warps) {
+    return (uint32_t)(((size_t)G * hd + 2 * (size_t)hd + (size_t)warps * G * (hd + 2)) * 4 + 16);
+}
+
 struct GemvArgs {
     const void* W = nullptr;  // [rows, K] in format wfmt; kEpiGlu: gate rows [0,N) then up rows [N,2N)
     int wfmt = kWBf16;
@@ -148,12 +178,14 @@ struct GemvArgs {
     // o projection, warms gate|up while attention runs)
     const void* next2_w = nullptr;
     int next2_N = 0, next2_K = 0, next2_U = 1, next2_wfmt = kWBf16;
+    GemvAttn att;  // one token: its decode attention runs first and produces x
     int* err = nullptr;
 };
 
 struct GemvPlan {
     int rows_per_stage = 1;
     int stages = 3;
+    int att_warps = 0;  // fused attention: page-scoring warps (GemvAttn::warps)
     int prefetch = 0;  // L2 prefetch window, in stages beyond the smem ring
     int grid = 0;
     size_t smem = 0;

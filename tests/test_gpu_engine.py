@@ -28,9 +28,9 @@ def _pair(kw, seed=0, std=0.02, max_batch=1, max_seq_len=256, **eopts):
     return eng, m
 
 
-def _run_parity(kw, prompt_lens, steps, seed=0, std=0.02, check_kv=True):
+def _run_parity(kw, prompt_lens, steps, seed=0, std=0.02, check_kv=True, max_seq_len=256):
     B = len(prompt_lens)
-    eng, m = _pair(kw, seed, std, max_batch=B)
+    eng, m = _pair(kw, seed, std, max_batch=B, max_seq_len=max_seq_len)
     V = kw["vocab"]
     sids, oseqs, feed = [], [], []
     ties = 0
@@ -38,7 +38,7 @@ def _run_parity(kw, prompt_lens, steps, seed=0, std=0.02, check_kv=True):
         ids = oracle.fill_ids(f"prompt{b}", n, seed + b, V)
         sid = eng.seq_create()
         nxt, lb = eng.prefill(sid, ids, logits=ti.LOGITS_BF16)
-        os_ = m.new_seq(512)
+        os_ = m.new_seq(max(512, max_seq_len))
         _, lf = os_.forward(ids)
         ties += not check_step(nxt, lb, lf, f"prefill b{b}")
         sids.append(sid)
