@@ -20,8 +20,10 @@ profiler and prints their in-graph timeline); it never prints a bench line.
 
 --impl reference times the reference's decode step on the host CPU: the
 reference ships no CPU implementation (its every op is CUDA), so the CPU
-restatement of its algorithm (oracle/) is timed, multi-threaded, on a bounded
-sample (2 of 32 layers + LM head, extrapolated linearly).
+restatement of its algorithm (oracle/) is timed, multi-threaded, at full depth
+(32 layers + LM head, 512-token context) for the given steps.  Its line also
+carries ref_gpu_b1: the reference's own unchanged CUDA path (oracle/_ref) on the
+same GPU at batch 1 (--no-ref-gpu skips it).
 """
 import argparse
 import json
@@ -106,8 +108,10 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ reference arm / CPU baseline
 def cpu_baseline(sample_layers=2, steps=2):
-    """Oracle (CPU restatement of the reference) timed on the host cores:
-    8B shapes, `sample_layers` decoder layers + LM head, extrapolated to 32 layers."""
+    """Oracle (CPU restatement of the reference) timed on the host cores on a
+    bounded sample of the benchmark step: 8B shapes, `sample_layers` decoder
+    layers + LM head at the benchmark's 512-token context (seeded synthetic K/V),
+    extrapolated to 32 layers."""
     import numpy as np
 
     import oracle
@@ -116,11 +120,10 @@ def cpu_baseline(sample_layers=2, steps=2):
     kw = dict(ti.PRESETS["llama3_8b"], n_layers=sample_layers)
     m = oracle.Model(**kw)
     m.init_synthetic(0, 0.02)
-    s = m.new_seq(64)
-    ids = oracle.fill_ids("prompt", 16, 0, kw["vocab"])
-    s.forward(ids[:8])  # short context so the sample is dominated by weight streaming
+    s = m.new_seq(PROMPT + steps + 8)
+    s.fill_synthetic(PROMPT, seed=1)
     t_step = []
-    tok = int(ids[8])
+    tok = 7
     for _ in range(steps):
         t0 = time.perf_counter()
         _, lf = s.forward([tok])
@@ -138,22 +141,149 @@ def cpu_baseline(sample_layers=2, steps=2):
     t_layer = max(1e-9, (t_sample - t_head) / sample_layers)
     t_full = t_head + 32 * t_layer
     return {"value": 1.0 / t_full, "unit": "tok/s", "cores": oracle.lib().orc_get_threads(), "kind": "port",
-            "sample": f"Llama-3-8B shapes, {sample_layers} of 32 layers + LM head timed per decode step "
-                      f"(ctx 9, best of {steps}), extrapolated linearly to 32 layers: "
+            "sample": f"Llama-3-8B shapes, {sample_layers} of 32 layers + LM head timed per decode step at a "
+                      f"{PROMPT}-token context (best of {steps}), extrapolated linearly to 32 layers: "
                       f"{t_layer * 1e3:.1f} ms/layer, {t_head * 1e3:.1f} ms LM head"}
+
+
+def reference_cpu_decode(steps, warmup):
+    """The benchmark step on the host cores: the CPU restatement of the
+    reference's decode path (oracle/; the reference ships no CPU implementation,
+    its every op is CUDA) at full depth, Llama-3-8B shape, batch 1, greedy, after
+    a 512-token context (seeded synthetic K/V instead of a CPU prefill);
+    `warmup` untimed steps, then `steps` timed steps."""
+    import numpy as np
+
+    import oracle
+    import ti_b200 as ti
+
+    m = oracle.Model(**ti.PRESETS["llama3_8b"])
+    m.init_synthetic(0, 0.02)
+    s = m.new_seq(PROMPT + warmup + steps + 8)
+    s.fill_synthetic(PROMPT, seed=1)
+    tok = 7
+    for _ in range(warmup):
+        tok = int(np.argmax(s.forward([tok])[1]))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        tok = int(np.argmax(s.forward([tok])[1]))
+    dt = (time.perf_counter() - t0) / max(1, steps)
+    return dt, oracle.lib().orc_get_threads()
+
+
+def write_aliased_checkpoint(d, kw):
+    """A safetensors checkpoint of the model shape `kw` (Llama) whose layers all
+    point at one layer's seeded N(0, 0.02) bytes: a 2.6 GB file for the 8B shape.
+    The reference's loader copies every tensor into its own device buffer
+    (llama_model.cpp:32-82), so the device streams a full-size model per step."""
+    import struct
+
+    import oracle
+
+    H, I, hd, V = kw["hidden"], kw["intermediate"], kw["head_dim"], kw["vocab"]
+    QW, KW = kw["n_heads"] * hd, kw["n_kv_heads"] * hd
+    blobs = {"embed": ((V, H), "model.embed_tokens.weight"), "norm": ((H,), "model.norm.weight"),
+             "head": ((V, H), "lm_head.weight"), "in_norm": ((H,), "input_layernorm"),
+             "post_norm": ((H,), "post_attention_layernorm"), "q": ((QW, H), "self_attn.q_proj"),
+             "k": ((KW, H), "self_attn.k_proj"), "v": ((KW, H), "self_attn.v_proj"), "o": ((H, QW), "self_attn.o_proj"),
+             "gate": ((I, H), "mlp.gate_proj"), "up": ((I, H), "mlp.up_proj"), "down": ((H, I), "mlp.down_proj")}
+    data, offs, off = [], {}, 0
+    for key, (shape, name) in blobs.items():
+        a = oracle.fill_bf16(name, shape, 0, 0.02)
+        offs[key] = (shape, off, off + a.nbytes)
+        off += a.nbytes
+        data.append(a)
+    header = {}
+    for key, name in (("embed", "model.embed_tokens.weight"), ("norm", "model.norm.weight"), ("head", "lm_head.weight")):
+        shape, b, e = offs[key]
+        header[name] = {"dtype": "BF16", "shape": list(shape), "data_offsets": [b, e]}
+    for i in range(kw["n_layers"]):
+        for key in ("in_norm", "post_norm", "q", "k", "v", "o", "gate", "up", "down"):
+            shape, b, e = offs[key]
+            base = blobs[key][1]
+            name = f"model.layers.{i}.{base}.weight"
+            header[name] = {"dtype": "BF16", "shape": list(shape), "data_offsets": [b, e]}
+    hb = json.dumps(header).encode()
+    hb += b" " * ((8 - len(hb) % 8) % 8)
+    with open(os.path.join(d, "model.safetensors"), "wb") as f:
+        f.write(struct.pack("<Q", len(hb)))
+        f.write(hb)
+        for a in data:
+            f.write(a.tobytes())
+    cfg = {"architectures": ["LlamaForCausalLM"], "model_type": "llama", "hidden_size": H, "intermediate_size": I,
+           "num_hidden_layers": kw["n_layers"], "num_attention_heads": kw["n_heads"],
+           "num_key_value_heads": kw["n_kv_heads"], "vocab_size": V, "rms_norm_eps": kw["rms_eps"],
+           "rope_theta": kw["rope_theta"], "max_position_embeddings": 8192, "bos_token_id": 1, "eos_token_id": 2,
+           "tie_word_embeddings": False, "torch_dtype": "bfloat16"}
+    with open(os.path.join(d, "config.json"), "w") as f:
+        json.dump(cfg, f)
+
+
+def reference_gpu_decode(steps, warmup):
+    """The reference's own CUDA decode path on this GPU: its unchanged backend,
+    parser and Llama model code (oracle/_ref/libref.so, compiled for sm_100a from
+    its sources), Llama-3-8B shape, batch 1 (the reference has no batching): a
+    512-token prompt in one forward call, then per token Model::forward and the
+    reference's own Greedy::sample, host-timed (its ops synchronise)."""
+    import ctypes as C
+    import shutil
+    import tempfile
+
+    import numpy as np
+
+    import ti_b200 as ti
+
+    path = os.path.join(ROOT, "oracle", "_ref", "libref.so")
+    if not os.path.exists(path):
+        return {"unavailable": "oracle/_ref/libref.so not built (needs the reference sources at build time)"}
+    ref = C.CDLL(path)
+    ref.ref_time_decode.restype = C.c_int
+    ref.ref_time_decode.argtypes = [C.c_char_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                    C.POINTER(C.c_double), C.POINTER(C.c_int32), C.c_char_p, C.c_int]
+    kw = dict(ti.PRESETS["llama3_8b"])
+    root = "/dev/shm" if os.path.isdir("/dev/shm") else None
+    d = tempfile.mkdtemp(prefix="ti_refckpt_", dir=root)
+    try:
+        write_aliased_checkpoint(d, kw)
+        prompt = np.random.default_rng(0).integers(0, kw["vocab"], size=PROMPT, dtype=np.int32)
+        ms, last = C.c_double(0), C.c_int32(0)
+        err = C.create_string_buffer(512)
+        rc = ref.ref_time_decode(d.encode(), prompt.ctypes.data, PROMPT, warmup, steps, PROMPT + warmup + steps + 8,
+                                 C.byref(ms), C.byref(last), err, 512)
+        if rc != 0:
+            return {"unavailable": f"reference decode failed: {err.value.decode()[:200]}"}
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    return {"tok_s": round(1e3 / ms.value, 2), "ms_per_step": round(ms.value, 3), "steps": steps, "warmup": warmup,
+            "config": "Llama-3-8B shape, batch 1, 512-token prompt, greedy; the reference's unchanged CUDA path "
+                      "(cuBLAS GEMMs, per-op allocation) on this B200; layers share one layer's values on disk, "
+                      "each is its own device buffer"}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    cb = cpu_baseline()
-    line = {"metric": METRIC, "impl": "reference", "value": cb["value"], "unit": "tok/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / cb["value"], "higher_is_better": True,
+    dt, cores = reference_cpu_decode(args.steps, args.warmup)
+    v = 1.0 / dt
+    cb = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
+          "sample": f"the whole benchmark step: Llama-3-8B shape, 32 layers + LM head, batch 1, "
+                    f"{PROMPT}-token context (synthetic K/V), {args.steps} timed steps after {args.warmup} warm-up"}
+    line = {"metric": METRIC, "impl": "reference", "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "Llama-3-8B-shape bf16 greedy decode, batch 1, 512-token prompt (CPU oracle)",
-                       "batch": 1},
+            "config": {"workload": "Llama-3-8B-shape bf16 greedy decode, batch 1, 512-token context "
+                                   "(CPU restatement of the reference's path; the reference has no CPU backend)",
+                       "batch": 1, "prompt": PROMPT, "layers": 32},
             "cpu_baseline": cb,
-            "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if not args.no_ref_gpu:
+        import torch
+
+        if torch.cuda.is_available():
+            try:
+                line["ref_gpu_b1"] = reference_gpu_decode(max(4, args.steps), min(args.warmup, 3))
+            except Exception as exc:  # noqa: BLE001 - the extra leg reports its failure; the line stands
+                line["ref_gpu_b1"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
     print(json.dumps(line), flush=True)
 
 
@@ -683,6 +813,8 @@ def main():
     ap.add_argument("--no-70b", dest="big", action="store_false",
                     help="skip the Llama-3-70B tensor-parallel leg (config 5, N >= 2 only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ref-gpu", dest="no_ref_gpu", action="store_true",
+                    help="reference arm: skip the reference's own CUDA path on this GPU (the line's ref_gpu_b1)")
     ap.add_argument("--sampled", action="store_true",
                     help="also measure batch-1 decode with device top-p sampling: the line's sampled_b1 field")
     ap.add_argument("--ttft", action="store_true",

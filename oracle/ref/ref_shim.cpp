@@ -16,6 +16,8 @@
 #include <tensor/parser/config.hpp>
 #include <tensor/parser/weight_map.hpp>
 
+#include <algorithm>
+#include <chrono>
 #include <cstdio>
 #include <cstring>
 #include <exception>
@@ -86,6 +88,40 @@ extern "C" int ref_run(const char* model_dir, int arch, const char* adapter_dir,
             }
             default: std::snprintf(err, err_len, "unknown arch %d", arch); return 2;
         }
+        return 0;
+    } catch (const std::exception& e) {
+        std::snprintf(err, err_len, "%s", e.what());
+        return 1;
+    }
+}
+
+// Decode-step timing of the reference's own CUDA path on this GPU (Llama
+// model files, llama_model.cpp:210-238): the prompt in one forward call, then
+// n_warm + n_steps single-token steps, each followed by the reference's own
+// Greedy::sample (greedy.cpp:11-36, as Generator::generate does per token,
+// generator.cpp:24-84), its id fed back.  ms_per_step: wall time of the last
+// n_steps steps over n_steps; the reference's ops synchronise the device.
+extern "C" int ref_time_decode(const char* model_dir, const int32_t* prompt, int n_prompt, int n_warm, int n_steps,
+                               int max_seq, double* ms_per_step, int32_t* last_id, char* err, int err_len) {
+    try {
+        const auto dev = tensor::backend::Device::cuda(0);
+        auto wm = tensor::parser::WeightMap::open(model_dir);
+        auto cfg = tensor::parser::ModelConfig::from_dir(model_dir);
+        auto m = tensor::models::llama::LlamaModel::load(wm, cfg, dev);
+        auto cache = m.make_cache((std::size_t)max_seq);
+        std::vector<int32_t> ids(prompt, prompt + n_prompt);
+        auto lg = m.forward(ids, cache);
+        const int vocab = (int)m.vocab_size();
+        int32_t tok = tensor::inference::sampling::Greedy{}.sample(lg);
+        auto t0 = std::chrono::steady_clock::now();
+        for (int i = 0; i < n_warm + n_steps; ++i) {
+            if (i == n_warm) t0 = std::chrono::steady_clock::now();
+            lg = m.forward(std::vector<int32_t>{((tok % vocab) + vocab) % vocab}, cache);
+            tok = tensor::inference::sampling::Greedy{}.sample(lg);
+        }
+        const auto t1 = std::chrono::steady_clock::now();
+        *ms_per_step = std::chrono::duration<double, std::milli>(t1 - t0).count() / std::max(1, n_steps);
+        *last_id = tok;
         return 0;
     } catch (const std::exception& e) {
         std::snprintf(err, err_len, "%s", e.what());

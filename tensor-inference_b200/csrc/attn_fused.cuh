@@ -4,9 +4,11 @@
 // Replaces, for one layer and one new token, the reference's ops::rope(q, k)
 // (ops.cu:210-312), the cudaMemcpy of K/V into the cache (llama_model.cpp:155-171),
 // ops::slice x2 and ops::attention (ops.cu:444-544).  While these warps work,
-// the GEMV's producer warp is already streaming the o-projection's weight rows
-// into the shared-memory ring, so HBM does not idle during attention; the
-// separate attention kernel and its launch are gone.
+// the GEMV's producer warp has the CTA's o-projection weight rows prefetched
+// HBM -> L2 (a path that does not delay the warps' own loads), so HBM does not
+// idle during attention; the shared-memory fills from L2 start once the CTA's
+// latency-bound loads are done (the `go` barrier).  The separate attention
+// kernel and its launch are gone.
 //
 // Work split: CTA c serves kv head h = c % nkv (grid >= nkv), together with the
 // other CTAs of that head; the attended pages [lo/16, pos/16] are dealt out
@@ -75,11 +77,13 @@ TI_DEVICE_INLINE void attn_fused_prefetch(const GemvAttn& t, int warp, int lane,
 }
 
 // The phase, run by `nthr` consumer threads (tid in [0, nthr)) of CTA `cta` of
-// `grid`; `sm` is gemv_attn_smem(G, HD, t.warps) bytes of shared memory.
-// GM: compile-time bound on the q heads per kv head (4 or 8).
-// Named barrier 2 synchronises the consumer threads.
+// `grid`; `sm` is gemv_attn_smem(G, HD, t.warps, nh) bytes of shared memory.
+// GM: compile-time bound on the q heads per kv head (4 or 8).  `go` (one
+// arrival) releases the producer's shared-memory fills once this CTA's
+// latency-bound loads are done.  Named barrier 2 synchronises the consumer threads.
 template <int HD, int GM>
-TI_DEVICE_INLINE void attn_fused_phase(const GemvAttn& t, float* sm, int tid, int nthr, int cta, int grid, int* err) {
+TI_DEVICE_INLINE void attn_fused_phase(const GemvAttn& t, float* sm, int tid, int nthr, int cta, int grid,
+                                       uint64_t* go, int* err) {
     constexpr int HALF = HD / 2;
     constexpr int DL = HD / 32;  // P.V dims per lane
     constexpr int NC = HD / 8;   // 8-element chunks of a row
@@ -93,6 +97,7 @@ TI_DEVICE_INLINE void attn_fused_phase(const GemvAttn& t, float* sm, int tid, in
     float* vn = kn + HD;      // [HD]
     float* slots = vn + HD;   // [aw][G][HD + 2]
     int* flag = reinterpret_cast<int*>(slots + (size_t)aw * G * (HD + 2));
+    float* mw = reinterpret_cast<float*>(flag + 4);  // merging CTA: [nh][G] (max, then weight; sum)
     const AttnSpan sp = attn_span(t);
     const int pos = sp.pos, lo = sp.lo;
 
@@ -279,29 +284,46 @@ TI_DEVICE_INLINE void attn_fused_phase(const GemvAttn& t, float* sm, int tid, in
     }
     __threadfence();
     named_bar(2, nthr);
-    if (tid == 0) *flag = atomicAdd(&t.ticket[h], 1u) == (unsigned int)(nh - 1);
+    if (tid == 0) {
+        *flag = atomicAdd(&t.ticket[h], 1u) == (unsigned int)(nh - 1);
+        if (!*flag) mbar_arrive(go);  // nothing latency-bound left here but the wait
+    }
     named_bar(2, nthr);
 
     // ---- the last CTA of kv head h merges the head's CTAs in CTA order
     if (*flag) {
         __threadfence();
+        // every partial's (max, sum), all loads in flight together
+        for (int idx = tid; idx < nh * G; idx += nthr) {
+            const int j = idx / G, g = idx - j * G;
+            const float* pj = t.part + ((size_t)(h + j * nkv) * G + g) * (HD + 2);
+            mw[2 * idx] = __ldcg(pj + HD);
+            mw[2 * idx + 1] = __ldcg(pj + HD + 1);
+        }
+        named_bar(2, nthr);
+        // per q head: the overall max, each partial's weight 2^(m_j - M) (0 when
+        // empty) in place of its max, and the total sum (in qs, free by now)
+        if (tid < G) {
+            float M = -INFINITY;
+            for (int j = 0; j < nh; ++j)
+                if (mw[2 * (j * G + tid) + 1] > 0.f) M = fmaxf(M, mw[2 * (j * G + tid)]);
+            float L = 0.f;
+            for (int j = 0; j < nh; ++j) {
+                const float lj = mw[2 * (j * G + tid) + 1];
+                const float w = lj > 0.f ? ex2(mw[2 * (j * G + tid)] - M) : 0.f;
+                mw[2 * (j * G + tid)] = w;
+                L = fmaf(lj, w, L);
+            }
+            qs[tid] = L;
+        }
+        named_bar(2, nthr);
         for (int idx = tid; idx < G * HD; idx += nthr) {
             const int g = idx / HD, d = idx - g * HD;
-            float M = -INFINITY;
-            for (int j = 0; j < nh; ++j) {
-                const float* pj = t.part + ((size_t)(h + j * nkv) * G + g) * (HD + 2);
-                if (__ldcg(pj + HD + 1) > 0.f) M = fmaxf(M, __ldcg(pj + HD));
-            }
-            float L = 0.f, O = 0.f;
-            for (int j = 0; j < nh; ++j) {
-                const float* pj = t.part + ((size_t)(h + j * nkv) * G + g) * (HD + 2);
-                const float lj = __ldcg(pj + HD + 1);
-                if (lj > 0.f) {
-                    const float f = ex2(__ldcg(pj + HD) - M);
-                    L = fmaf(lj, f, L);
-                    O = fmaf(__ldcg(pj + d), f, O);
-                }
-            }
+            float O = 0.f;
+#pragma unroll 8
+            for (int j = 0; j < nh; ++j)
+                O = fmaf(__ldcg(t.part + ((size_t)(h + j * nkv) * G + g) * (HD + 2) + d), mw[2 * (j * G + g)], O);
+            const float L = qs[g];
             t.out[(size_t)(h * G + g) * HD + d] = __bfloat16_as_ushort(f2bf(L > 0.f ? O / L : 0.f));
         }
         __threadfence();
@@ -309,6 +331,7 @@ TI_DEVICE_INLINE void attn_fused_phase(const GemvAttn& t, float* sm, int tid, in
         if (tid == 0) {
             atomicExch(&t.ticket[h], 0u);
             atomicAdd(&t.sync[0], 1u);
+            mbar_arrive(go);
         }
     }
 

@@ -48,8 +48,8 @@ constexpr int kPartSlots = 8;  // stages of partial sums in flight to the epilog
 constexpr int kRowsMax = 12;  // rows per stage (per unit) upper bound, for one token
 
 struct GemvSmem {
-    uint32_t stage_bytes, stages_off, full_off, empty_off, pfull_off, pempty_off, part_off, red_off, xs_off, epi_off,
-        att_off, total;
+    uint32_t stage_bytes, stages_off, full_off, empty_off, pfull_off, pempty_off, go_off, part_off, red_off, xs_off,
+        epi_off, att_off, total;
 };
 
 // rows_cap: most rows one CTA owns; the epilogue warp keeps their residual
@@ -71,6 +71,8 @@ __host__ __device__ inline GemvSmem gemv_smem_layout(int K, int wf, int units, i
     o += 8 * kPartSlots;
     L.pempty_off = o;
     o += 8 * kPartSlots;
+    L.go_off = o;  // ATT: the consumers' go for the producer's shared-memory fills
+    o += 8;
     L.part_off = o;
     o += kPartSlots * rows_per_stage * units * nb * kConsumerWarps * 4;
     L.red_off = o;
@@ -183,13 +185,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int XRR = XS ? 1 : XR;
     const int K = a.K;
     const int rows_cap = (a.N + (int)gridDim.x - 1) / (int)gridDim.x;
-    const uint32_t att_bytes = ATT ? gemv_attn_smem(a.att.nq / a.att.nkv, a.att.hd, a.att.warps) : 0u;
+    const uint32_t att_bytes =
+        ATT ? gemv_attn_smem(a.att.nq / a.att.nkv, a.att.hd, a.att.warps, ((int)gridDim.x + a.att.nkv - 1) / a.att.nkv)
+            : 0u;
     const GemvSmem L = gemv_smem_layout(K, WF, U, rows_per_stage, stages, NB, XS, rows_cap, att_bytes);
     const size_t rb = wrow_bytes(K, WF);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.full_off);
     uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L.empty_off);
     uint64_t* pfull = reinterpret_cast<uint64_t*>(smem + L.pfull_off);
     uint64_t* pempty = reinterpret_cast<uint64_t*>(smem + L.pempty_off);
+    uint64_t* go = reinterpret_cast<uint64_t*>(smem + L.go_off);
     float* part = reinterpret_cast<float*>(smem + L.part_off);
     float* red = reinterpret_cast<float*>(smem + L.red_off);
     const int slot_floats = rows_per_stage * U * NB * kConsumerWarps;
@@ -208,6 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&pfull[p], kConsumerWarps);
             mbar_init(&pempty[p], 1);
         }
+        mbar_init(go, 1);
         fence_barrier_init();
     }
     __syncthreads();
@@ -228,6 +234,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 prefetch_l2_bulk(W + (size_t)row0 * row_bytes, bytes);
                 if (U == 2) prefetch_l2_bulk(W + ((size_t)a.N + row0) * row_bytes, bytes);
             };
+            if constexpr (ATT > 0) {
+                // while the consumers attend, the CTA's rows go HBM -> L2 only; the
+                // shared-memory fills (from L2) wait for the consumers' go, so the
+                // attention's latency-bound loads do not queue behind them
+                for (int g = 0; g < n_groups; ++g) prefetch(g);
+                mbar_wait(go, 0, a.err, kErrTimeoutFull);
+            }
             for (int g = stages; g < min(n_groups, stages + pf); ++g) prefetch(g);
             for (int g = 0; g < n_groups; ++g) {
                 const int s = g % stages, use = g / stages;
@@ -407,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (ATT > 0) {
         constexpr int AHD = ATT <= 2 ? 128 : 64, AGM = ATT % 2 == 1 ? 4 : 8;
         attn_fused_phase<AHD, AGM>(a.att, reinterpret_cast<float*>(smem + L.att_off), threadIdx.x,
-                                   kConsumerWarps * 32, cta, G, a.err);
+                                   kConsumerWarps * 32, cta, G, go, a.err);
     }
     const int cols_per_warp = K / kConsumerWarps;
     const int col0 = warp * cols_per_warp;
@@ -719,7 +732,7 @@ bool gemv_plan(const GemvArgs& a, int epi, int device, GemvPlan* plan, std::stri
         // TI_ATT_WARPS caps them (a test makes warps take several pages at short contexts)
         if (const char* v = std::getenv("TI_ATT_WARPS"))
             if (std::atoi(v) >= 1) att_warps = std::min(att_warps, std::atoi(v));
-        att_bytes = gemv_attn_smem(G, a.att.hd, att_warps);
+        att_bytes = gemv_attn_smem(G, a.att.hd, att_warps, (grid + a.att.nkv - 1) / a.att.nkv);
     }
     int max_smem = 0;
     cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);

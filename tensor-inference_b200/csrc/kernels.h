@@ -132,9 +132,10 @@ struct GemvAttn {
     int warps = 0;                   // consumer warps that score pages (shared-memory merge slots)
 };
 // shared memory of the attention phase: rotated q [G][hd], the token's k and v
-// [2][hd], merge slots [warps][G][hd + 2] (fp32), one flag
-__host__ __device__ inline uint32_t gemv_attn_smem(int G, int hd, int warps) {
-    return (uint32_t)(((size_t)G * hd + 2 * (size_t)hd + (size_t)warps * G * (hd + 2)) * 4 + 16);
+// [2][hd], merge slots [warps][G][hd + 2], one flag (16 bytes), the merging
+// CTA's per-partial (max, sum) [nh][G][2] (fp32; nh = CTAs per kv head)
+__host__ __device__ inline uint32_t gemv_attn_smem(int G, int hd, int warps, int nh) {
+    return (uint32_t)(((size_t)G * hd + 2 * (size_t)hd + (size_t)warps * G * (hd + 2) + (size_t)nh * G * 2) * 4 + 16);
 }
 
 struct GemvArgs {
