@@ -363,6 +363,25 @@ def measure_batch(ti, torch, eng, B, steps, warmup, stream, peak, measure_e2e=Tr
     return res
 
 
+def measure_tinyllama(ti, torch, stream, peak, dev=0, warmup=8, steps=128, prompt=128):
+    """Benchmark configuration 1, the shape the reference's run_llama tool
+    decodes: TinyLlama-1.1B shape (22 layers), seeded N(0, 0.02) bf16 weights, a
+    128-token prompt of ids uniform in [0, 32000), greedy decode of 128 tokens at
+    batch 1, device-timed over those 128 steps (after `warmup` untimed steps)"""
+    desc = ti.model_desc(**ti.PRESETS["tinyllama"])
+    eng = ti.Engine(desc, device=dev, max_batch=1, max_seqs=1, max_seq_len=prompt + 2 * (warmup + steps) + 16)
+    try:
+        eng.init_synthetic(0, 0.02)
+        r = measure_batch(ti, torch, eng, 1, steps, warmup, stream, peak, measure_e2e=False, prompt=prompt)
+    finally:
+        eng.close()
+    return {"tok_s": round(r["tok_s"], 1), "ms_per_step": round(r["ms_per_step"], 4),
+            "step_gbs": round(r["step_gbs"], 1), "frac_measured": round(r["step_frac_measured"], 4),
+            "frac_nominal_8tbs": round(r["step_frac_nominal"], 4), "bytes_per_step": r["step_bytes"],
+            "ctx_avg": r["ctx_avg"],
+            "config": "TinyLlama-1.1B shape, 22 layers, 128-token prompt, 128 greedy steps, batch 1"}
+
+
 def measure_qwen_lora(ti, torch, stream, peak, wf, steps, warmup, dev=0):
     """Benchmark configuration 3: Qwen2.5-7B shape, rank-16 LoRA on q/k/v/o (A ~ N(0, 0.02),
     B ~ N(0, 0.001), alpha 32), batch 8, 256-token prompts; weights bf16 or GGUF Q4_0"""
@@ -705,6 +724,7 @@ def run_ours(args, rank, world):
             return {"error": f"{type(exc).__name__}: {exc}"[:300]}
 
     pkm = extra(measure_pkm, ti, torch, stream) if world == 1 else None
+    tiny = extra(measure_tinyllama, ti, torch, stream, peak, dev) if world == 1 else None
     r32 = None
     if args.b32:
         r32 = measure_batch(ti, torch, eng, 32, max(2, args.steps // 4), min(args.warmup, 3), stream, peak,
@@ -778,6 +798,8 @@ def run_ours(args, rank, world):
                            "ctx_avg": r32["ctx_avg"]}
         if qwen:
             line["qwen7b_lora_b8"] = dict(qwen, config="Qwen2.5-7B shape, rank-16 LoRA q/k/v/o, batch 8, 256-token prompt")
+        if tiny:
+            line["tinyllama_b1"] = tiny
         if r70:
             line["llama70b_tp_b64_lora"] = r70
         if ttft:

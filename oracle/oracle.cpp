@@ -201,19 +201,43 @@ static inline float dot_bf16_f32(const uint16_t* a, const float* b, int K) {
     return (float)s;
 }
 
-// ops.cu:94-148 — C[M,N] = A[M,K] @ B[N,K]^T, fp32 accumulate, bf16 output.
-extern "C" void orc_matmul_t_bf16_f32out(const uint16_t* a, const uint16_t* b, float* c, int M, int N, int K) {
+// The same sum as dot_bf16 over operands already widened to fp32 (the widening
+// is exact): 16 independent fp32 partial sums combined in double.
+static inline float dot_f32_fixed(const float* a, const float* b, int K) {
+    float acc[16] = {0};
+    int k = 0;
+    for (; k + 16 <= K; k += 16)
+        for (int j = 0; j < 16; ++j) acc[j] += a[k + j] * b[k + j];
+    double s = 0;
+    for (int j = 0; j < 16; ++j) s += acc[j];
+    for (; k < K; ++k) s += (double)a[k] * b[k];
+    return (float)s;
+}
+
+// C[m, n] = store(dot(A[m], B[n])): A widened once, each B row once per thread
+template <class F>
+static void matmul_rows(const uint16_t* a, const uint16_t* b, int M, int N, int K, F store) {
+    std::vector<float> af((size_t)M * K);
+    parallel_for((size_t)M * K, [&](size_t i0, size_t i1) {
+        for (size_t i = i0; i < i1; ++i) af[i] = bf(a[i]);
+    }, 1 << 16);
     parallel_for((size_t)N, [&](size_t n0, size_t n1) {
-        for (size_t n = n0; n < n1; ++n)
-            for (int m = 0; m < M; ++m) c[(size_t)m * N + n] = dot_bf16(a + (size_t)m * K, b + n * (size_t)K, K);
+        std::vector<float> row((size_t)K);
+        for (size_t n = n0; n < n1; ++n) {
+            const uint16_t* bn = b + n * (size_t)K;
+            for (int k = 0; k < K; ++k) row[k] = bf(bn[k]);
+            for (int m = 0; m < M; ++m) store((size_t)m * N + n, dot_f32_fixed(af.data() + (size_t)m * K, row.data(), K));
+        }
     }, 16);
 }
 
+// ops.cu:94-148 — C[M,N] = A[M,K] @ B[N,K]^T, fp32 accumulate, bf16 output.
+extern "C" void orc_matmul_t_bf16_f32out(const uint16_t* a, const uint16_t* b, float* c, int M, int N, int K) {
+    matmul_rows(a, b, M, N, K, [&](size_t i, float v) { c[i] = v; });
+}
+
 extern "C" void orc_matmul_t_bf16(const uint16_t* a, const uint16_t* b, uint16_t* c, int M, int N, int K) {
-    parallel_for((size_t)N, [&](size_t n0, size_t n1) {
-        for (size_t n = n0; n < n1; ++n)
-            for (int m = 0; m < M; ++m) c[(size_t)m * N + n] = tobf(dot_bf16(a + (size_t)m * K, b + n * (size_t)K, K));
-    }, 16);
+    matmul_rows(a, b, M, N, K, [&](size_t i, float v) { c[i] = tobf(v); });
 }
 
 extern "C" void orc_matmul_t_f32(const float* a, const float* b, float* c, int M, int N, int K) {
