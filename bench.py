@@ -248,8 +248,16 @@ def reference_gpu_decode(steps, warmup):
         prompt = np.random.default_rng(0).integers(0, kw["vocab"], size=PROMPT, dtype=np.int32)
         ms, last = C.c_double(0), C.c_int32(0)
         err = C.create_string_buffer(512)
-        rc = ref.ref_time_decode(d.encode(), prompt.ctypes.data, PROMPT, warmup, steps, PROMPT + warmup + steps + 8,
-                                 C.byref(ms), C.byref(last), err, 512)
+        # the reference's loader logs to stdout: keep this process's stdout for the JSON line
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            rc = ref.ref_time_decode(d.encode(), prompt.ctypes.data, PROMPT, warmup, steps,
+                                     PROMPT + warmup + steps + 8, C.byref(ms), C.byref(last), err, 512)
+        finally:
+            os.dup2(saved, 1)
+            os.close(saved)
         if rc != 0:
             return {"unavailable": f"reference decode failed: {err.value.decode()[:200]}"}
     finally:

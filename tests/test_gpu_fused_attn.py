@@ -1,5 +1,5 @@
-"""Single-token decode steps run attention inside the o projection's GEMV
-(csrc/attn_fused.cuh): RoPE of q and k, the K/V row into its page, paged GQA
+"""With TI_FUSED_ATTN=1, single-token decode steps run attention inside the o
+projection's GEMV (csrc/attn_fused.cuh): RoPE of q and k, the K/V row into its page, paged GQA
 attention and the o projection in one kernel, the GEMV's weight stream running
 while the consumer warps attend.  These cases stress its work split against the
 CPU oracle (restating llama_model.cpp:147-187 and ops.cu:210-312, 444-544):
@@ -16,6 +16,11 @@ from gpu_util import LOGIT_TOL, rel_err
 from test_gpu_engine import _run_parity
 
 pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _fused(monkeypatch):
+    monkeypatch.setenv("TI_FUSED_ATTN", "1")  # opt-in path
 
 
 @pytest.mark.parametrize("warps", [None, "1", "3"])
