@@ -112,6 +112,39 @@ TI_DEVICE_INLINE void mma_16816_bf16(float* c, const uint32_t* a, uint32_t b0, u
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+// cluster merge: offsets in the ring (free after the warps' merge, whose
+// [warps][16][128] fp32 area ends at 64 KB): partial output [G][hd] (<= 16 KB),
+// (max, sum) per q head, split 0's weights [n_splits][G][2]
+constexpr uint32_t kClusterPartOff = 64u * 1024u;
+constexpr uint32_t kClusterMlOff = kClusterPartOff + 16u * 1024u;
+constexpr uint32_t kClusterWOff = kClusterMlOff + 256u;
+constexpr int kAttnMaxCluster = 8;  // portable cluster size
+static_assert(kClusterWOff + kAttnMaxCluster * kAttnMaxGroup * 8 <= kAttnStages * kAttnStageBytes, "ring holds it");
+
+// all threads of every CTA of the cluster (release / acquire: shared-memory writes
+// before it are visible to the cluster's reads after it)
+TI_DEVICE_INLINE void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// load from the same shared-memory offset in cluster CTA `rank`
+TI_DEVICE_INLINE float ld_dsmem_f32(const float* p, int rank) {
+    uint32_t ra;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(p)), "r"(rank));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+    return v;
+}
+TI_DEVICE_INLINE float4 ld_dsmem_f32x4(const float* p, int rank) {
+    uint32_t ra;
+    float4 v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(p)), "r"(rank));
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(ra)
+                 : "memory");
+    return v;
+}
+
 // byte offset of element (row, d) in a [HD/64][C][64] bf16 tile with 128-byte swizzled rows
 TI_DEVICE_INLINE uint32_t tile_off(int C, int row, int d) {
     const int hh = d >> 6, cc = (d & 63) >> 3;
@@ -515,11 +548,70 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
             dst[1] = f2bf(O.y / l);
             dst[2] = f2bf(O.z / l);
             dst[3] = f2bf(O.w / l);
+        } else if (a.cluster) {
+            *reinterpret_cast<float4*>(ring + kClusterPartOff + (size_t)e * 4) = O;
         } else {
             *reinterpret_cast<float4*>(a.part_o + (pbase + g) * HD + d) = O;
         }
     }
     if (a.n_splits == 1) return;
+
+    if (a.cluster) {
+        // ---- the splits of this (token, kv head) are one thread-block cluster: each
+        //      leaves its partial in its own shared memory, split 0 reads them all
+        //      through distributed shared memory and merges in split order.  Every
+        //      thread of every CTA passes both cluster barriers (no early exit).
+        float* cml = reinterpret_cast<float*>(ring + kClusterMlOff);
+        if (tid < G) {
+            cml[2 * tid] = hml[2 * tid];
+            cml[2 * tid + 1] = hml[2 * tid + 1];
+        }
+        cluster_sync_all();
+        if (split == 0) {
+            float* wsg = reinterpret_cast<float*>(ring + kClusterWOff);  // [n_splits][G] (max, then weight; sum)
+            for (int idx = tid; idx < a.n_splits * G; idx += kAttnThreads) {
+                const int sp = idx / G, g = idx - sp * G;
+                wsg[2 * idx] = ld_dsmem_f32(cml + 2 * g, sp);
+                wsg[2 * idx + 1] = ld_dsmem_f32(cml + 2 * g + 1, sp);
+            }
+            __syncthreads();
+            if (tid < G) {
+                float M = -INFINITY;
+                for (int sp = 0; sp < a.n_splits; ++sp)
+                    if (wsg[2 * (sp * G + tid) + 1] > 0.f) M = fmaxf(M, wsg[2 * (sp * G + tid)]);
+                float Ls = 0.f;
+                for (int sp = 0; sp < a.n_splits; ++sp) {
+                    const float l = wsg[2 * (sp * G + tid) + 1];
+                    const float w = l > 0.f ? ex2(wsg[2 * (sp * G + tid)] - M) : 0.f;
+                    wsg[2 * (sp * G + tid)] = w;
+                    Ls = fmaf(l, w, Ls);
+                }
+                hml[2 * tid + 1] = Ls;
+            }
+            __syncthreads();
+            const float* cpo = reinterpret_cast<const float*>(ring + kClusterPartOff);
+            for (int e = tid * 4; e < G * HD; e += kAttnThreads * 4) {
+                const int g = e / HD;
+                float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int sp = 0; sp < a.n_splits; ++sp) {
+                    const float w = wsg[2 * (sp * G + g)];
+                    const float4 v = ld_dsmem_f32x4(cpo + e, sp);
+                    O.x = fmaf(v.x, w, O.x);
+                    O.y = fmaf(v.y, w, O.y);
+                    O.z = fmaf(v.z, w, O.z);
+                    O.w = fmaf(v.w, w, O.w);
+                }
+                const float inv = hml[2 * g + 1];
+                bf16* dst = reinterpret_cast<bf16*>(a.out) + (size_t)b * a.out_stride + (size_t)h * G * HD + e;
+                dst[0] = f2bf(O.x / inv);
+                dst[1] = f2bf(O.y / inv);
+                dst[2] = f2bf(O.z / inv);
+                dst[3] = f2bf(O.w / inv);
+            }
+        }
+        cluster_sync_all();  // the other splits' shared memory stays until split 0 has read it
+        return;
+    }
 
     // ---- partial results, merged by the last CTA of this (token, kv head)
     if (tid < G) {
@@ -654,7 +746,14 @@ int attn_splits(int nb, int nkv, int hd, int max_len, int sms, int* max_chunk) {
             }
         }
     }
-    const int n = (stages + spp - 1) / spp;
+    int n = (stages + spp - 1) / spp;
+    // up to 8 splits merge inside a thread-block cluster, without the global
+    // partials' round trips: take 8 when that leaves at most 4 stages per split
+    if (!(env && std::atoi(env) >= 1) && n > kAttnMaxCluster &&
+        (stages + kAttnMaxCluster - 1) / kAttnMaxCluster <= 4) {
+        spp = (stages + kAttnMaxCluster - 1) / kAttnMaxCluster;
+        n = (stages + spp - 1) / spp;
+    }
     *max_chunk = spp * ct;
     return n;
 }
@@ -698,7 +797,25 @@ cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s, bool pdl) {
     }
     AttnArgs args = a;
     void* params[] = {&tk, &tv, &args};
-    return launch_pdl(f, dim3(a.n_splits, a.nkv, a.nb), dim3(kAttnThreads), smem, s, params, pdl);
+    if (a.n_splits < 2 || a.n_splits > kAttnMaxCluster)
+        return launch_pdl(f, dim3(a.n_splits, a.nkv, a.nb), dim3(kAttnThreads), smem, s, params, pdl);
+    // the splits of each (token, kv head) as one cluster (merge in distributed shared memory)
+    args.cluster = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.n_splits, a.nkv, a.nb);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)a.n_splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelExC(&cfg, f, params);
 }
 
 }  // namespace ti

@@ -213,6 +213,7 @@ void gguf_from_rows(const uint8_t* rows, int nr, int K, size_t rb, int wf, uint8
 struct TcPlan {
     int np = 0;  // tokens padded to a multiple of 32 (MMA N)
     int tiles = 0, kbs = 1, kblocks = 0, kpc = 0, grid = 0, stages = 0;  // kpc: k-blocks per CTA (stream-K)
+    int pf = 0;  // weight k-blocks prefetched HBM -> L2 ahead of the ring's loads
     uint32_t stage_bytes = 0, tmem_cols = 0;
     uint32_t w_off = 0, x_off = 0, s_off = 0;  // stage layout (weights / tokens / GGUF scales)
     int cb = 0, n_abuf = 0, threads = 0;       // GGUF: code bytes per atom row, dequantised buffers
@@ -253,6 +254,10 @@ struct AttnArgs {
     float* part_o = nullptr;   // [nb, nkv, n_splits, group, hd]
     float* part_ml = nullptr;  // [nb, nkv, n_splits, group, 2]
     unsigned int* counters = nullptr;  // [nb, nkv] (zero; reset by the last CTA)
+    // set by attn_launch: the n_splits (<= 8) CTAs of a (token, kv head) run as one
+    // thread-block cluster and merge through distributed shared memory (part_o,
+    // part_ml and counters unused)
+    int cluster = 0;
     uint16_t* out = nullptr;  // [nb, out_stride]
     int out_stride = 0;
     int* err = nullptr;

@@ -11,11 +11,19 @@
 // CPU and the GPU), and the argmin takes the lowest index among equal minima, so
 // addresses are bit-identical to the CPU restatement.
 //
-// Tiling: a CTA owns 32 queries of one half and streams the codebook through
-// shared memory in tiles of 64 codes; operands are stored dimension-major so a
-// thread reads 2 queries and 4 codes as vectors; each thread keeps the running
-// (distance, index) minimum of its (query, code-column) pairs; a final
-// shared-memory merge across code columns keeps the first minimum.
+// Tiling: a CTA owns 64 queries and streams the codebook of each half in tiles
+// of 128 codes and chunks of 32 dimensions (the accumulators of a code tile stay
+// in registers across its chunks, so every distance keeps the canonical order).
+// The codebooks are stored dimension-major (transposed once, at create time, and
+// padded to whole 128-code tiles), so a code chunk is a straight cp.async copy;
+// query chunks are read as float4 rows and written transposed, lanes across
+// queries (no shared-memory bank conflicts).  Both are double-buffered.  Thread
+// (qg, cg) keeps 4 queries x 8 codes: per dimension one 16-byte load of its
+// queries, two of its codes, and 16 packed f32x2 subtractions + 16 packed FMAs
+// (each lane individually rounded: the same sequence as the scalar form).  Each
+// thread keeps the running (distance, index) minimum of its queries over its
+// codes, in ascending code order; the 16 threads of a query group merge by
+// shuffles, lower index first among equal distances.
 #include <cstring>
 #include <vector>
 
@@ -26,88 +34,140 @@
 namespace ti {
 
 constexpr int kPkmThreads = 256;
-constexpr int kPkmQ = 32;  // queries per CTA
-constexpr int kPkmC = 64;  // codes per tile
-// 256 threads = 16 query pairs x 16 code quads
+constexpr int kPkmQ = 64;    // queries per CTA
+constexpr int kPkmC = 128;   // codes per tile
+constexpr int kPkmDc = 32;   // dimensions per chunk
+// 256 threads = 16 query groups (4 queries) x 16 code groups (8 codes)
 
+TI_DEVICE_INLINE float2 sub2(float2 a, float2 b) {
+    unsigned long long av = *reinterpret_cast<unsigned long long*>(&a);
+    unsigned long long bv = *reinterpret_cast<unsigned long long*>(&b);
+    unsigned long long r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(av), "l"(bv));
+    return *reinterpret_cast<float2*>(&r);
+}
+TI_DEVICE_INLINE void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+TI_DEVICE_INLINE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+TI_DEVICE_INLINE void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// ct1 / ct2: dimension-major codebooks [D][ncp] (ncp = n_codes padded to 128)
 template <int D>
 __global__ void __launch_bounds__(kPkmThreads) k_pkm_assign(const float* __restrict__ queries, int n,
-                                                            const float* __restrict__ c1, const float* __restrict__ c2,
-                                                            int n_codes, const int32_t* __restrict__ table,
+                                                            const float* __restrict__ ct1, const float* __restrict__ ct2,
+                                                            int n_codes, int ncp, const int32_t* __restrict__ table,
                                                             int32_t* __restrict__ addr, int32_t* __restrict__ adapter) {
-    extern __shared__ __align__(16) float sm[];
-    float* qs = sm;               // [D][kPkmQ]
-    float* cs = qs + D * kPkmQ;   // [D][kPkmC]
-    __shared__ float best_d[kPkmQ][16];
-    __shared__ int best_i[kPkmQ][16];
+    // dynamic: qs [2][kPkmDc][kPkmQ] then cs [2][kPkmDc][kPkmC] (48 KB)
+    extern __shared__ __align__(16) float pkm_sm[];
+    auto qs = reinterpret_cast<float(*)[kPkmDc][kPkmQ]>(pkm_sm);
+    auto cs = reinterpret_cast<float(*)[kPkmDc][kPkmC]>(pkm_sm + 2 * kPkmDc * kPkmQ);
     __shared__ int half_idx[2][kPkmQ];
     const int tid = threadIdx.x;
-    const int qp = tid / 16, cq = tid % 16;  // query pair, code quad
+    const int qg = tid >> 4, cg = tid & 15;
     const int q0 = blockIdx.x * kPkmQ;
+    constexpr int NCH = D / kPkmDc;
+    const int ntile = ncp / kPkmC;
+    const int total = 2 * ntile * NCH;  // iterations: (half, code tile, chunk)
 
-    for (int half = 0; half < 2; ++half) {
-        const float* C = half ? c2 : c1;
-        __syncthreads();
-        // queries of this half, dimension-major
-        for (int i = tid; i < kPkmQ * D; i += kPkmThreads) {
-            const int q = i / D, t = i % D;
-            qs[t * kPkmQ + q] = (q0 + q < n) ? queries[(size_t)(q0 + q) * (2 * D) + half * D + t] : 0.f;
+    // loads of iteration it into buffer b: the code chunk by cp.async, the query chunk into registers
+    float4 qreg[2];
+    auto issue = [&](int it, int b) {
+        const int half = it / (ntile * NCH), rem = it % (ntile * NCH);
+        const int tile = rem / NCH, ch = rem % NCH;
+        const float* C = (half ? ct2 : ct1) + (size_t)(ch * kPkmDc) * ncp + tile * kPkmC;
+#pragma unroll
+        for (int r = 0; r < kPkmDc * kPkmC / 4 / kPkmThreads; ++r) {
+            const int i = tid + r * kPkmThreads;  // 16-byte piece: row i / 32, column (i % 32) * 4
+            cp_async16(&cs[b][i >> 5][(i & 31) * 4], C + (size_t)(i >> 5) * ncp + (i & 31) * 4);
         }
-        float bd[2] = {INFINITY, INFINITY};
-        int bi[2] = {0x7fffffff, 0x7fffffff};
-        for (int c0 = 0; c0 < n_codes; c0 += kPkmC) {
-            __syncthreads();
-            for (int i = tid; i < kPkmC * D; i += kPkmThreads) {
-                const int c = i / D, t = i % D;
-                cs[t * kPkmC + c] = (c0 + c < n_codes) ? C[(size_t)(c0 + c) * D + t] : 0.f;
-            }
-            __syncthreads();
-            float acc[2][4] = {};
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int i = tid + r * kPkmThreads;  // query i % 64, dimensions 4 * (i / 64) ..
+            const int q = i & (kPkmQ - 1), t4 = i >> 6;
+            qreg[r] = q0 + q < n ? __ldg(reinterpret_cast<const float4*>(queries + (size_t)(q0 + q) * (2 * D) +
+                                                                           half * D + ch * kPkmDc + t4 * 4))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    auto store_q = [&](int b) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int i = tid + r * kPkmThreads;
+            const int q = i & (kPkmQ - 1), t4 = i >> 6;
+            qs[b][t4 * 4 + 0][q] = qreg[r].x;
+            qs[b][t4 * 4 + 1][q] = qreg[r].y;
+            qs[b][t4 * 4 + 2][q] = qreg[r].z;
+            qs[b][t4 * 4 + 3][q] = qreg[r].w;
+        }
+    };
+
+    float2 acc[4][4];  // [query][code pair]
+    float bd[4];
+    int bi[4];
+    issue(0, 0);
+    store_q(0);
+    cp_async_commit();
+    for (int it = 0; it < total; ++it) {
+        const int b = it & 1;
+        const int half = it / (ntile * NCH), rem = it % (ntile * NCH);
+        const int tile = rem / NCH, ch = rem % NCH;
+        if (it + 1 < total) issue(it + 1, b ^ 1);  // buffer b^1 was read by iteration it - 1, before the barrier
+        cp_async_commit();
+        cp_async_wait_1();  // this iteration's code chunk has landed
+        __syncthreads();
+        if (rem == 0) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) bd[j] = INFINITY, bi[j] = 0x7fffffff;
+        }
+        if (ch == 0) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int p = 0; p < 4; ++p) acc[j][p] = make_float2(0.f, 0.f);
+        }
 #pragma unroll 4
-            for (int t = 0; t < D; ++t) {
-                const float2 qv = *reinterpret_cast<const float2*>(&qs[t * kPkmQ + qp * 2]);
-                const float4 cv = *reinterpret_cast<const float4*>(&cs[t * kPkmC + cq * 4]);
-                const float qa[2] = {qv.x, qv.y};
-                const float ca[4] = {cv.x, cv.y, cv.z, cv.w};
+        for (int t = 0; t < kPkmDc; ++t) {
+            const float4 qv = *reinterpret_cast<const float4*>(&qs[b][t][qg * 4]);
+            const float4 ca = *reinterpret_cast<const float4*>(&cs[b][t][cg * 8]);
+            const float4 cb = *reinterpret_cast<const float4*>(&cs[b][t][cg * 8 + 4]);
+            const float qa[4] = {qv.x, qv.y, qv.z, qv.w};
+            const float2 cp[4] = {make_float2(ca.x, ca.y), make_float2(ca.z, ca.w), make_float2(cb.x, cb.y),
+                                  make_float2(cb.z, cb.w)};
 #pragma unroll
-                for (int a = 0; a < 2; ++a)
+            for (int j = 0; j < 4; ++j)
 #pragma unroll
-                    for (int b = 0; b < 4; ++b) {
-                        const float d = __fsub_rn(qa[a], ca[b]);
-                        acc[a][b] = __fmaf_rn(d, d, acc[a][b]);
-                    }
-            }
-#pragma unroll
-            for (int a = 0; a < 2; ++a)
-#pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const int k = c0 + cq * 4 + b;  // ascending within the thread: strict < keeps the first
-                    if (k < n_codes && acc[a][b] < bd[a]) {
-                        bd[a] = acc[a][b];
-                        bi[a] = k;
-                    }
+                for (int p = 0; p < 4; ++p) {
+                    const float2 d = sub2(make_float2(qa[j], qa[j]), cp[p]);
+                    acc[j][p] = ffma2(d, d, acc[j][p]);
                 }
         }
-        // merge the 16 code columns of each query: smaller distance, then lower index
+        if (ch == NCH - 1) {
+            // the tile's distances are complete: running minimum in ascending code order
 #pragma unroll
-        for (int a = 0; a < 2; ++a) {
-            best_d[qp * 2 + a][cq] = bd[a];
-            best_i[qp * 2 + a][cq] = bi[a];
-        }
-        __syncthreads();
-        if (tid < kPkmQ) {
-            float d = best_d[tid][0];
-            int k = best_i[tid][0];
-            for (int j = 1; j < 16; ++j) {
-                const float dj = best_d[tid][j];
-                const int kj = best_i[tid][j];
-                if (dj < d || (dj == d && kj < k)) {
-                    d = dj;
-                    k = kj;
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {
+                    const int k = tile * kPkmC + cg * 8 + p * 2;
+                    if (k < n_codes && acc[j][p].x < bd[j]) bd[j] = acc[j][p].x, bi[j] = k;
+                    if (k + 1 < n_codes && acc[j][p].y < bd[j]) bd[j] = acc[j][p].y, bi[j] = k + 1;
+                }
+            if (tile == ntile - 1) {
+                // merge the 16 code groups of each query: smaller distance, then lower index
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+#pragma unroll
+                    for (int o = 1; o < 16; o <<= 1) {
+                        const float od = __shfl_xor_sync(0xffffffffu, bd[j], o);
+                        const int oi = __shfl_xor_sync(0xffffffffu, bi[j], o);
+                        if (od < bd[j] || (od == bd[j] && oi < bi[j])) bd[j] = od, bi[j] = oi;
+                    }
+                    if (cg == 0) half_idx[half][qg * 4 + j] = bi[j];
                 }
             }
-            half_idx[half][tid] = k;
         }
+        __syncthreads();  // buffer b is refilled by the next iteration's issue
+        if (it + 1 < total) store_q(b ^ 1);
     }
     __syncthreads();
     if (tid < kPkmQ && q0 + tid < n) {
@@ -117,10 +177,17 @@ __global__ void __launch_bounds__(kPkmThreads) k_pkm_assign(const float* __restr
     }
 }
 
-static size_t pkm_smem(int D) { return (size_t)D * (kPkmQ + kPkmC) * 4; }
+// dimension-major copy of a codebook: ct[t][k] = c[k][t] (codes k >= n_codes zero)
+__global__ void k_pkm_transpose(const float* __restrict__ c, int n_codes, int D, int ncp, float* __restrict__ ct) {
+    const size_t total = (size_t)D * ncp;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / ncp), k = (int)(i % ncp);
+        ct[i] = k < n_codes ? c[(size_t)k * D + t] : 0.f;
+    }
+}
 
-cudaError_t pkm_assign_launch(const float* queries, int n, const float* c1, const float* c2, int n_codes, int D,
-                              const int32_t* table, int32_t* addr, int32_t* adapter, cudaStream_t s) {
+cudaError_t pkm_assign_launch(const float* queries, int n, const float* ct1, const float* ct2, int n_codes, int ncp,
+                              int D, const int32_t* table, int32_t* addr, int32_t* adapter, cudaStream_t s) {
     const void* f = nullptr;
     switch (D) {
         case 32: f = reinterpret_cast<const void*>(&k_pkm_assign<32>); break;
@@ -130,13 +197,17 @@ cudaError_t pkm_assign_launch(const float* queries, int n, const float* c1, cons
         case 512: f = reinterpret_cast<const void*>(&k_pkm_assign<512>); break;
         default: return cudaErrorInvalidValue;
     }
-    const size_t smem = pkm_smem(D);
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-    }
-    void* args[] = {&queries, &n, &c1, &c2, &n_codes, &table, &addr, &adapter};
+    if (ncp % kPkmC != 0 || ncp < n_codes) return cudaErrorInvalidValue;
+    void* args[] = {&queries, &n, &ct1, &ct2, &n_codes, &ncp, &table, &addr, &adapter};
+    const size_t smem = (size_t)2 * kPkmDc * (kPkmQ + kPkmC) * 4;  // 48 KB: above the default with the static part
+    cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
     return cudaLaunchKernel(f, dim3((n + kPkmQ - 1) / kPkmQ), dim3(kPkmThreads), args, smem, s);
+}
+
+cudaError_t pkm_transpose_launch(const float* c, int n_codes, int D, int ncp, float* ct, cudaStream_t s) {
+    k_pkm_transpose<<<256, 256, 0, s>>>(c, n_codes, D, ncp, ct);
+    return cudaGetLastError();
 }
 
 }  // namespace ti
@@ -144,8 +215,8 @@ cudaError_t pkm_assign_launch(const float* queries, int n, const float* c1, cons
 using namespace ti;
 
 struct ti_pkm {
-    int dev = 0, n_codes = 0, D = 0;
-    float *c1 = nullptr, *c2 = nullptr;
+    int dev = 0, n_codes = 0, D = 0, ncp = 0;
+    float *c1 = nullptr, *c2 = nullptr;  // dimension-major [D][ncp] (ncp = n_codes padded to 128)
     int32_t* table = nullptr;           // device [n_codes^2]
     std::vector<int32_t> h_table;
 };
@@ -164,13 +235,21 @@ ti_status ti_pkm_create(int device, int n_codes, int half_dim, const float* c1_h
     p->dev = device;
     p->n_codes = n_codes;
     p->D = half_dim;
+    p->ncp = (n_codes + 127) / 128 * 128;
     const size_t cb = (size_t)n_codes * half_dim * 4;
+    const size_t ctb = (size_t)p->ncp * half_dim * 4;
     const size_t tb = (size_t)n_codes * n_codes * 4;
-    cudaError_t e = cudaMalloc(&p->c1, cb);
-    if (e == cudaSuccess) e = cudaMalloc(&p->c2, cb);
+    float* stage = nullptr;  // row-major upload, transposed on the device
+    cudaError_t e = cudaMalloc(&p->c1, ctb);
+    if (e == cudaSuccess) e = cudaMalloc(&p->c2, ctb);
     if (e == cudaSuccess) e = cudaMalloc(&p->table, tb);
-    if (e == cudaSuccess) e = cudaMemcpy(p->c1, c1_host, cb, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemcpy(p->c2, c2_host, cb, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMalloc(&stage, cb);
+    if (e == cudaSuccess) e = cudaMemcpy(stage, c1_host, cb, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = pkm_transpose_launch(stage, n_codes, half_dim, p->ncp, p->c1, 0);
+    if (e == cudaSuccess) e = cudaMemcpy(stage, c2_host, cb, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = pkm_transpose_launch(stage, n_codes, half_dim, p->ncp, p->c2, 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaFree(stage);
     if (e == cudaSuccess) e = cudaMemset(p->table, 0xff, tb);
     if (e != cudaSuccess) {
         cudaGetLastError();
@@ -208,7 +287,7 @@ ti_status ti_pkm_register(ti_pkm* p, const float* centroids_host, const int32_t*
     TI_CUDA(cudaMalloc(&dq, qb));
     cudaError_t e = cudaMalloc(&da, (size_t)n * 4);
     if (e == cudaSuccess) e = cudaMemcpy(dq, centroids_host, qb, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = pkm_assign_launch(dq, n, p->c1, p->c2, p->n_codes, p->D, nullptr, da, nullptr, 0);
+    if (e == cudaSuccess) e = pkm_assign_launch(dq, n, p->c1, p->c2, p->n_codes, p->ncp, p->D, nullptr, da, nullptr, 0);
     std::vector<int32_t> addr((size_t)n);
     if (e == cudaSuccess) e = cudaMemcpy(addr.data(), da, (size_t)n * 4, cudaMemcpyDeviceToHost);
     cudaFree(dq);
@@ -226,7 +305,7 @@ ti_status ti_pkm_register(ti_pkm* p, const float* centroids_host, const int32_t*
 ti_status ti_pkm_query(ti_pkm* p, const float* queries, int n, int32_t* addr, int32_t* adapter, void* stream) {
     TI_CHECK(p && queries && addr && n >= 0, TI_ERR_INVALID, "pkm_query: bad argument");
     if (n == 0) return TI_OK;
-    TI_CUDA(pkm_assign_launch(queries, n, p->c1, p->c2, p->n_codes, p->D, p->table, addr, adapter,
+    TI_CUDA(pkm_assign_launch(queries, n, p->c1, p->c2, p->n_codes, p->ncp, p->D, p->table, addr, adapter,
                               (cudaStream_t)stream));
     return TI_OK;
 }
@@ -243,7 +322,7 @@ ti_status ti_pkm_query_host(ti_pkm* p, const float* queries, int n, int32_t* add
     cudaError_t e = cudaMalloc(&dout, (size_t)n * 8);
     if (e == cudaSuccess) e = cudaMemcpy(dq, queries, qb, cudaMemcpyHostToDevice);
     if (e == cudaSuccess)
-        e = pkm_assign_launch(dq, n, p->c1, p->c2, p->n_codes, p->D, p->table, dout, dout + n, 0);
+        e = pkm_assign_launch(dq, n, p->c1, p->c2, p->n_codes, p->ncp, p->D, p->table, dout, dout + n, 0);
     if (e == cudaSuccess) e = cudaMemcpy(addr, dout, (size_t)n * 4, cudaMemcpyDeviceToHost);
     if (e == cudaSuccess && adapter) e = cudaMemcpy(adapter, dout + n, (size_t)n * 4, cudaMemcpyDeviceToHost);
     cudaFree(dq);

@@ -66,6 +66,11 @@ TI_DEVICE_INLINE void tma_load_2d_hint(void* dst, const CUtensorMap* map, int x,
         "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
         : "memory");
 }
+// L2 prefetch of one tiled box (no shared-memory destination, no multicast)
+TI_DEVICE_INLINE void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y)
+                 : "memory");
+}
 TI_DEVICE_INLINE void tmap_prefetch(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
@@ -126,6 +131,7 @@ struct TcKernelArgs {
     int kbs;
     int kpc;             // k-blocks per CTA: CTA c owns global k-blocks [c * kpc, (c + 1) * kpc)
     int stages;
+    int pf;              // the producer prefetches weight k-block it + pf into L2 as it loads k-block it
     // stage layout: bf16: [kbs weight atoms][kbs token atoms]; GGUF: [kbs token atoms]
     // [codes: 128 rows x kbs*cb bytes][scales: 128 rows x kbs*4 bytes], dequantised
     // into n_abuf bf16 operand buffers of kbs atoms after the ring
@@ -317,6 +323,35 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                     }
                 }
             };
+            // the same boxes as load_w, HBM -> L2 only: keeps pf more k-blocks of
+            // weights in flight than the shared-memory ring holds
+            auto prefetch_w = [&](int it) {
+                const long g = g_begin + it;
+                if (a.pf <= 0 || g >= g_end) return;
+                const int tile = (int)(g / a.kblocks), kb = (int)(g % a.kblocks);
+                if constexpr (kQ) {
+                    const int xc = kb * kbs * a.cb, xs = kb * kbs * 4;
+                    if (kGlu) {
+                        tma_prefetch_2d(&tmw, xc, tile * 64);
+                        tma_prefetch_2d(&tmw, xc, a.N + tile * 64);
+                        tma_prefetch_2d(&tms, xs, tile * 64);
+                        tma_prefetch_2d(&tms, xs, a.N + tile * 64);
+                    } else {
+                        tma_prefetch_2d(&tmw, xc, tile * kTcBM);
+                        tma_prefetch_2d(&tms, xs, tile * kTcBM);
+                    }
+                } else {
+                    for (int j = 0; j < kbs; ++j) {
+                        const int x = (kb * kbs + j) * kTcBK;
+                        if (kGlu) {
+                            tma_prefetch_2d(&tmw, x, tile * 64);
+                            tma_prefetch_2d(&tmw, x, a.N + tile * 64);
+                        } else {
+                            tma_prefetch_2d(&tmw, x, tile * kTcBM);
+                        }
+                    }
+                }
+            };
             auto load_x = [&](int kb, int s) {
                 uint8_t* xt = smem + (size_t)s * a.stage_bytes + a.x_off;
                 for (int j = 0; j < kbs; ++j)
@@ -330,6 +365,7 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                 load_w(tile, kb, it);
                 return true;
             });
+            for (int it = first; it < first + a.pf; ++it) prefetch_w(it);
             // 2. the token tiles of those stages, once the previous kernel is done
             pdl_wait();
             walk([&](int, int kb, int it) {
@@ -349,6 +385,7 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                 mbar_arrive_expect_tx(&full[s], tx);
                 load_w(tile, kb, s);
                 load_x(kb, s);
+                prefetch_w(it + a.pf);
                 issued = it + 1;
                 return true;
             });
@@ -926,6 +963,9 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
         return false;
     }
     p->smem = tc_smem_layout(p->stages, p->stage_bytes, np, p->n_abuf, best_kbs).total;
+    // L2 prefetch window in k-blocks beyond the ring (TI_TC_PF overrides)
+    const char* pfe = std::getenv("TI_TC_PF");
+    p->pf = pfe ? std::max(0, std::atoi(pfe)) : 0;
     uint32_t cols = 32;
     while (cols < (uint32_t)(2 * np)) cols <<= 1;
     p->tmem_cols = cols;
@@ -968,6 +1008,7 @@ cudaError_t tc_launch(const GemvArgs& g, int epi, const TcPlan& p, float* ws, un
     a.kbs = p.kbs;
     a.kpc = p.kpc;
     a.stages = p.stages;
+    a.pf = p.pf;
     a.stage_bytes = p.stage_bytes;
     a.w_off = p.w_off;
     a.x_off = p.x_off;
