@@ -112,10 +112,14 @@ TI_DEVICE_INLINE void mma_16816_bf16(float* c, const uint32_t* a, uint32_t b0, u
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
-// cluster merge: offsets in the ring (free after the warps' merge, whose
-// [warps][16][128] fp32 area ends at 64 KB): partial output [G][hd] (<= 16 KB),
-// (max, sum) per q head, split 0's weights [n_splits][G][2]
-constexpr uint32_t kClusterPartOff = 64u * 1024u;
+// the warps' merge area over the ring: [warps][16 q heads][kRedStride] fp32; the
+// row stride of 128 + 8 floats puts the 64-bit stores of a half-warp (8 rows x 4
+// column pairs) on 32 distinct banks and keeps rows 16-byte aligned
+constexpr int kRedStride = 136;
+// cluster merge: offsets in the ring (free after the warps' merge, whose area ends
+// below 72 KB): partial output [G][hd] (<= 16 KB), (max, sum) per q head, split 0's
+// weights [n_splits][G][2]
+constexpr uint32_t kClusterPartOff = 72u * 1024u;
 constexpr uint32_t kClusterMlOff = kClusterPartOff + 16u * 1024u;
 constexpr uint32_t kClusterWOff = kClusterMlOff + 256u;
 constexpr int kAttnMaxCluster = 8;  // portable cluster size
@@ -267,29 +271,48 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
             if (!early(st)) issue(st, pt + pg0);
 
     // ---- RoPE on the group's q heads and the new k (ops.cu:224-232); v as is
+    // all of a thread's q/k/v loads are issued before any of them is used (one
+    // round trip to L2, not one per task)
     const uint16_t* row = a.qkv + (size_t)b * a.qkv_stride;
-    for (int task = tid; task < (G + 1) * HALF; task += kAttnThreads) {
-        const int hh = task / HALF, i = task - hh * HALF;
-        const uint16_t* src = hh < G ? row + (size_t)(h * G + hh) * HD : row + (size_t)(a.nq + h) * HD;
-        const float x0 = __uint_as_float((uint32_t)src[i] << 16);
-        const float x1 = __uint_as_float((uint32_t)src[i + HALF] << 16);
-        const float ang = (float)pos * a.freqs[i];
-        const float c = cosf(ang), s = sinf(ang);
-        const float y0 = x0 * c - x1 * s, y1 = x0 * s + x1 * c;
-        if (hh < G) {
-            *reinterpret_cast<bf16*>(qs + tile_off(16, hh, i)) = f2bf(y0);
-            *reinterpret_cast<bf16*>(qs + tile_off(16, hh, i + HALF)) = f2bf(y1);
-        } else {
-            kn[i] = round_bf(y0);
-            kn[i + HALF] = round_bf(y1);
+    constexpr int kRopeMax = ((kAttnMaxGroup + 1) * HALF + kAttnThreads - 1) / kAttnThreads;
+    const int n_task = (G + 1) * HALF;
+    float rx0[kRopeMax], rx1[kRopeMax], rf[kRopeMax];
+#pragma unroll
+    for (int k = 0; k < kRopeMax; ++k) {
+        const int task = tid + k * kAttnThreads;
+        if (task < n_task) {
+            const int hh = task / HALF, i = task - hh * HALF;
+            const uint16_t* src = hh < G ? row + (size_t)(h * G + hh) * HD : row + (size_t)(a.nq + h) * HD;
+            rx0[k] = __uint_as_float((uint32_t)src[i] << 16);
+            rx1[k] = __uint_as_float((uint32_t)src[i + HALF] << 16);
+            rf[k] = a.freqs[i];
+        }
+    }
+    const float vval = tid < HD ? __uint_as_float((uint32_t)row[(size_t)(a.nq + a.nkv + h) * HD + tid] << 16) : 0.f;
+#pragma unroll
+    for (int k = 0; k < kRopeMax; ++k) {
+        const int task = tid + k * kAttnThreads;
+        if (task < n_task) {
+            const int hh = task / HALF, i = task - hh * HALF;
+            const float x0 = rx0[k], x1 = rx1[k];
+            const float ang = (float)pos * rf[k];
+            const float c = cosf(ang), s = sinf(ang);
+            const float y0 = x0 * c - x1 * s, y1 = x0 * s + x1 * c;
+            if (hh < G) {
+                *reinterpret_cast<bf16*>(qs + tile_off(16, hh, i)) = f2bf(y0);
+                *reinterpret_cast<bf16*>(qs + tile_off(16, hh, i + HALF)) = f2bf(y1);
+            } else {
+                kn[i] = round_bf(y0);
+                kn[i + HALF] = round_bf(y1);
+            }
         }
     }
     for (int task = tid; task < (16 - G) * HD; task += kAttnThreads) {  // padding heads
         const int hh = G + task / HD, d = task % HD;
         *reinterpret_cast<bf16*>(qs + tile_off(16, hh, d)) = f2bf(0.f);
     }
-    for (int d = tid; d < HD; d += kAttnThreads)
-        vn[d] = __uint_as_float((uint32_t)row[(size_t)(a.nq + a.nkv + h) * HD + d] << 16);
+    static_assert(HD <= kAttnThreads, "one v element per thread");
+    if (tid < HD) vn[tid] = vval;
     __syncthreads();
 
     // lane-constant parts of the swizzled ldmatrix addresses (the row's low 3 bits
@@ -511,7 +534,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         hml[2 * tid + 1] = Ls;
     }
     __syncthreads();
-    float* red = reinterpret_cast<float*>(ring);  // [warps][16][DW]
+    float* red = reinterpret_cast<float*>(ring);  // [warps][16][kRedStride]
+    static_assert(kAttnWarps * 16 * kRedStride * 4 <= kClusterPartOff, "merge area below the cluster partials");
     {
         const float M0 = hml[2 * gq], M1 = hml[2 * (gq + 8)];
         const float f0 = m0 == -INFINITY ? 0.f : ex2(m0 - M0);
@@ -519,8 +543,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
 #pragma unroll
         for (int n = 0; n < NT; ++n) {
             const int d = n * 8 + qq * 2;
-            *reinterpret_cast<float2*>(red + ((size_t)warp * 16 + gq) * DW + d) = make_float2(o[n][0] * f0, o[n][1] * f0);
-            *reinterpret_cast<float2*>(red + ((size_t)warp * 16 + gq + 8) * DW + d) =
+            *reinterpret_cast<float2*>(red + ((size_t)warp * 16 + gq) * kRedStride + d) =
+                make_float2(o[n][0] * f0, o[n][1] * f0);
+            *reinterpret_cast<float2*>(red + ((size_t)warp * 16 + gq + 8) * kRedStride + d) =
                 make_float2(o[n][2] * f1, o[n][3] * f1);
         }
     }
@@ -535,7 +560,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
 #pragma unroll
         for (int w = 0; w < kAttnWarps; ++w) {
             if (part_of(w) != part) continue;
-            const float4 v = *reinterpret_cast<const float4*>(red + ((size_t)w * 16 + g) * DW + dl);
+            const float4 v = *reinterpret_cast<const float4*>(red + ((size_t)w * 16 + g) * kRedStride + dl);
             O.x += v.x;
             O.y += v.y;
             O.z += v.z;
@@ -592,14 +617,19 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
             const float* cpo = reinterpret_cast<const float*>(ring + kClusterPartOff);
             for (int e = tid * 4; e < G * HD; e += kAttnThreads * 4) {
                 const int g = e / HD;
+                float4 v[kAttnMaxCluster];  // every split's values in flight together
+#pragma unroll
+                for (int sp = 0; sp < kAttnMaxCluster; ++sp)
+                    if (sp < a.n_splits) v[sp] = ld_dsmem_f32x4(cpo + e, sp);
                 float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int sp = 0; sp < a.n_splits; ++sp) {
+#pragma unroll
+                for (int sp = 0; sp < kAttnMaxCluster; ++sp) {
+                    if (sp >= a.n_splits) break;
                     const float w = wsg[2 * (sp * G + g)];
-                    const float4 v = ld_dsmem_f32x4(cpo + e, sp);
-                    O.x = fmaf(v.x, w, O.x);
-                    O.y = fmaf(v.y, w, O.y);
-                    O.z = fmaf(v.z, w, O.z);
-                    O.w = fmaf(v.w, w, O.w);
+                    O.x = fmaf(v[sp].x, w, O.x);
+                    O.y = fmaf(v[sp].y, w, O.y);
+                    O.z = fmaf(v[sp].z, w, O.z);
+                    O.w = fmaf(v[sp].w, w, O.w);
                 }
                 const float inv = hml[2 * g + 1];
                 bf16* dst = reinterpret_cast<bf16*>(a.out) + (size_t)b * a.out_stride + (size_t)h * G * HD + e;
