@@ -41,6 +41,9 @@ sys.path.insert(0, os.path.join(ROOT, "tensor-inference_b200"))
 METRIC = "decode tok/s at B=1/32 (8B shape) and % of HBM roofline at 1/2/4/8 B200"
 PROMPT = 512
 NOMINAL_HBM_GBS = 8000.0
+# one gate|up GEMV launch of the 8B shape under ncu: dram__bytes_read.sum +
+# dram__bytes_write.sum (profiles/gemv_weight_stream_8b.md)
+GATEUP_TRAFFIC_BYTES = 273213184
 
 
 def measured_peaks():
@@ -524,14 +527,14 @@ def kernel_roofline(ti, torch, eng, stream, peak, iters=64):
     torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1) / iters
     gbs = nbytes / (ms * 1e-3) / 1e9
-    traffic = None
-    prof = os.path.join(ROOT, "profiles", "gemv_weight_stream_8b.md")
-    if os.path.exists(prof):
-        for ln in open(prof):
-            if ln.startswith("traffic_bytes_per_launch"):
-                traffic = int(ln.split(":")[1].split()[0])
+    # DRAM bytes (read + write) of one launch of this kernel, from an ncu capture
+    # (dram__bytes_read.sum + dram__bytes_write.sum); a constant of this build,
+    # not measured by this run.  It includes the L2 warm-up of the next kernel's rows.
+    traffic = GATEUP_TRAFFIC_BYTES if tp == 1 else None
     return {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
-            "traffic": traffic, "traffic_source": "profiles/gemv_weight_stream_8b.md (ncu, incl. next-kernel L2 warm-up)", "kernel": "k_gemv<1,kEpiGlu> (gate|up + RMSNorm + SiLU*up, 8B layer)",
+            "traffic": traffic,
+            "traffic_source": "ncu capture of this kernel (profiles/gemv_weight_stream_8b.md), stated constant",
+            "kernel": "k_gemv<1,kEpiGlu> (gate|up + RMSNorm + SiLU*up, 8B layer)",
             "bytes_per_launch": nbytes, "us_per_launch": round(ms * 1e3, 2)}
 
 
