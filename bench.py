@@ -626,6 +626,11 @@ def run_profile(args):
     torch.cuda.set_device(0)
     ts = torch.cuda.Stream()
     torch.cuda.set_stream(ts)
+    if args.preset == "pkm":
+        # configuration 4 alone: `--steps` queries of 65,536 (NVTX range "kernels")
+        r = measure_pkm(ti, torch, ts.cuda_stream, iters=args.steps)
+        print(f"profile: pkm {r['ms']:.4f} ms per 65,536 queries")
+        return
     desc = ti.model_desc(**dict(ti.PRESETS[args.preset], n_layers=args.layers))
     ctx = args.ctx or args.prompt
     lora = dict(max_adapters=args.adapters, max_lora_rank=args.lora_rank, lora_proj_mask=0x7F) \
@@ -859,7 +864,8 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--kernel", type=int, default=None, help="profile: launch only this kernel kind")
     ap.add_argument("--ctx", type=int, default=0, help="profile: synthetic cached context of this length")
-    ap.add_argument("--preset", default="llama3_8b", help="profile: model shape (ti_b200.PRESETS)")
+    ap.add_argument("--preset", default="llama3_8b",
+                    help="profile: model shape (ti_b200.PRESETS), or pkm for the PKM router workload alone")
     ap.add_argument("--adapters", type=int, default=0, help="profile: LoRA adapters on all projections")
     ap.add_argument("--lora-rank", type=int, default=64, help="profile: rank of those adapters")
     ap.add_argument("--timeline", default=None,
