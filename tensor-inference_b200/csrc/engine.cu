@@ -136,6 +136,15 @@ struct ti_engine {
     float* att_part = nullptr;
     unsigned int *att_ticket = nullptr, *att_sync = nullptr;
     bool fuse_ao = false;
+    // tensor parallelism while a step is enqueued (fold_recv): a row-parallel
+    // projection's receive (no LoRA on it) is held here and run by the next GEMV's
+    // prologue, or launched as its own kernel when the next kernel cannot take it
+    bool fold_recv = false;
+    struct PendingRecv {
+        bool on = false;
+        GemvRecv r;
+        int B = 0, H = 0;
+    } pend;
     int attn_splits_n = 1, attn_max_chunk = 0;
     // tensor-core path (batches of tc_min..256 tokens): RMSNorm'd rows, partial
     // tiles shared between CTAs and their tickets
@@ -602,6 +611,11 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
                 c.ps.signal = b0 + chunk >= B ? a.ps.signal : 0;  // the last chunk publishes
             }
             if (a.resid) c.resid = a.resid + (size_t)b0 * resid_stride;
+            if (a.recv.tp) {
+                c.recv.inbox = a.recv.inbox + (size_t)b0 * a.K;
+                c.recv.resid = a.recv.resid + (size_t)b0 * a.K;
+                c.recv.x_out = a.recv.x_out + (size_t)b0 * a.K;
+            }
             if (a.lora.adapter) {
                 c.lora.adapter = a.lora.adapter + b0;
                 c.lora.t = a.lora.t + (size_t)b0 * a.lora.t_stride;
@@ -675,7 +689,8 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         a.resid = nullptr;
         if (e->peer_ar) {
             // the projection's epilogue writes into every rank's inbox; the receive
-            // kernel waits for all ranks and adds the rank-ordered sum to the residual
+            // (wait for all ranks, rank-ordered sum + residual) runs in the next GEMV's
+            // prologue when it can, else as k_tp_recv_resid
             const int ph = kind == kKO ? 0 : 1;
             const int MB = e->o.max_batch;
             a.ps.tp = e->tp.tp;
@@ -688,6 +703,22 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             a.ps.seq_add = li + 1;
             a.ps.ticket = reinterpret_cast<unsigned int*>(e->par + e->off_ticket) + ph;
             if (ti_status st = gemm(a, kEpiStore, x_stride_elems, H, 0)) return st;
+            if (e->fold_recv && !lora) {
+                GemvRecv& r = e->pend.r;
+                r.inbox = reinterpret_cast<const float*>(e->par + e->off_in[ph]);
+                r.src_stride = (size_t)MB * H;
+                r.flags = reinterpret_cast<const unsigned int*>(e->par + e->off_flags[ph]);
+                r.tp = e->tp.tp;
+                r.epoch = e->epoch;
+                r.seq_mul = d.n_layers;
+                r.seq_add = li + 1;
+                r.resid = resid;
+                r.x_out = out;
+                e->pend.B = B;
+                e->pend.H = H;
+                e->pend.on = true;
+                return TI_OK;
+            }
             TI_CUDA(tp_recv_resid_launch(reinterpret_cast<const float*>(e->par + e->off_in[ph]), (size_t)MB * H,
                                          reinterpret_cast<const unsigned int*>(e->par + e->off_flags[ph]), e->tp.tp,
                                          e->epoch, d.n_layers, li + 1, resid, out, B, H, lora,
@@ -742,6 +773,22 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         a.next_U = U;
         a.next_bytes = next_kb * 1024;
     };
+    // a receive held by the previous row-parallel projection: into this GEMV's
+    // prologue, or as its own kernel when this kernel cannot take it (tensor-core
+    // batch, or a LoRA shrink that reads x first)
+    auto take_recv = [&](GemvArgs& g, bool can_fuse) -> ti_status {
+        if (!e->pend.on) return TI_OK;
+        e->pend.on = false;
+        if (can_fuse && !(e->xn && B >= e->tc_min && B <= 256)) {
+            g.recv = e->pend.r;
+            return TI_OK;
+        }
+        const GemvRecv& r = e->pend.r;
+        TI_CUDA(tp_recv_resid_launch(r.inbox, r.src_stride, r.flags, r.tp, r.epoch, r.seq_mul, r.seq_add, r.resid,
+                                     r.x_out, e->pend.B, e->pend.H, nullptr, nullptr, 0, e->err, s, true));
+        if (launches) ++*launches;
+        return TI_OK;
+    };
     if (kind == kKLmHead) {
         GemvArgs lm;
         lm.W = e->lm_head;
@@ -761,6 +808,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
         lm.chain_pos = e->dd_pos();
         lm.err = e->err;
         set_next(lm, e->layers[0].wqkv, e->qkv_rows, H, 1);
+        if (ti_status st = take_recv(lm, true)) return st;
         if (e->tp.tp == 1) return gemm(lm, kEpiLmHead, H, e->Vl, 0);
         // vocabulary-parallel: local keys carry global indices; max over the group
         lm.key_offset = e->tp.v0;
@@ -856,6 +904,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             q.bias = l.bqkv;
             q.err = e->err;
             set_next(q, l.wo, H, QW, 1);
+            if (ti_status st = take_recv(q, !lora_on(0))) return st;
             if (next2) {
                 q.next2_w = l.wgu;
                 q.next2_wfmt = e->wf;
@@ -973,6 +1022,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             gu.out_stride = I;
             gu.act = gemma ? 1 : 0;
             gu.err = e->err;
+            if (ti_status st = take_recv(gu, !lora_on(2))) return st;
             set_next(gu, l.wdown, H, I, 1);
             if (lora_on(2)) {
                 if (ti_status st = prenorm(gu)) return st;
@@ -1016,11 +1066,24 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
 // in `out` and in the chain's next tokens, each with its row's next pre-generated draw
 ti_status enqueue_step(ti_engine* e, int B, cudaStream_t s, int* launches, bool lora, bool prefill,
                        bool sample = false) {
+    // row-parallel receives fold into the next GEMV within this step only
+    struct FoldScope {
+        ti_engine* e;
+        explicit FoldScope(ti_engine* x) : e(x) {
+            e->fold_recv = e->peer_ar;
+            e->pend.on = false;
+        }
+        ~FoldScope() {
+            e->fold_recv = false;
+            e->pend.on = false;
+        }
+    } fold(e);
     if (ti_status st = enqueue_kernel(e, B, kKEmbed, 0, s, launches, lora)) return st;
     for (int li = 0; li < e->d.n_layers; ++li)
         for (int k : {kKQkv, kKAttn, kKO, kKGateUp, kKDown})
             if (ti_status st = enqueue_kernel(e, B, k, li, s, launches, lora, prefill)) return st;
     if (ti_status st = enqueue_kernel(e, B, kKLmHead, 0, s, launches, lora)) return st;
+    TI_CHECK(!e->pend.on, TI_ERR_STATE, "a tensor-parallel receive was left without a consumer");
     if (!sample) return TI_OK;
     TI_CHECK(e->d_draws && e->d_srows, TI_ERR_STATE, "sampled device chain: buffers not set up");
     SampleArgs a;

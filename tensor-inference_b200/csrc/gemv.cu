@@ -168,6 +168,27 @@ TI_DEVICE_INLINE float dot8_f32w(const float2 w[4], const uint4 x, float acc) {
     return acc;
 }
 
+// x[b, col .. col + 8) from the tensor-parallel inboxes (GemvRecv): rank-ordered
+// fp32 sum, rounded to bf16, plus the bf16 residual, rounded (small.cu,
+// k_tp_recv_resid); `store`: also into x_out
+TI_DEVICE_INLINE uint4 recv_x8(const GemvRecv& r, int b, int K, int col, bool store) {
+    float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int rr = 0; rr < r.tp; ++rr) {  // rank order
+        const float* p = r.inbox + (size_t)rr * r.src_stride + (size_t)b * K + col;
+        const float4 u = __ldcv(reinterpret_cast<const float4*>(p));
+        const float4 v = __ldcv(reinterpret_cast<const float4*>(p + 4));
+        s[0] += u.x, s[1] += u.y, s[2] += u.z, s[3] += u.w, s[4] += v.x, s[5] += v.y, s[6] += v.z, s[7] += v.w;
+    }
+    const uint4 rv = *reinterpret_cast<const uint4*>(r.resid + (size_t)b * K + col);
+    uint4 o;
+    o.x = pack_bf2(bf_lo(rv.x) + round_bf(s[0]), bf_hi(rv.x) + round_bf(s[1]));
+    o.y = pack_bf2(bf_lo(rv.y) + round_bf(s[2]), bf_hi(rv.y) + round_bf(s[3]));
+    o.z = pack_bf2(bf_lo(rv.z) + round_bf(s[4]), bf_hi(rv.z) + round_bf(s[5]));
+    o.w = pack_bf2(bf_lo(rv.w) + round_bf(s[6]), bf_hi(rv.w) + round_bf(s[7]));
+    if (store) *reinterpret_cast<uint4*>(r.x_out + (size_t)b * K + col) = o;
+    return o;
+}
+
 // XR > 0: NB == 1, the lane's XR sub-chunks of the activation slice in registers.
 // XR == 0: NB tokens, activation slices in shared memory.
 // RG: compile-time bound on rows per stage (per unit).
@@ -422,6 +443,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         attn_fused_phase<AHD, AGM>(a.att, reinterpret_cast<float*>(smem + L.att_off), threadIdx.x,
                                    kConsumerWarps * 32, cta, G, go, a.err);
     }
+    const bool recv = a.recv.tp > 0;
+    if (recv) {
+        // every rank's partial sums of the row-parallel projection have landed (bounded wait)
+        if (threadIdx.x == 0) {
+            const unsigned int seq = peer_seq(*a.recv.epoch, a.recv.seq_mul, a.recv.seq_add);
+            for (int r = 0; r < a.recv.tp; ++r)
+                if (!wait_seq_sys(a.recv.flags + r, seq, a.err, kErrTimeoutPeer)) break;
+        }
+        named_bar(1, kConsumerWarps * 32);
+    }
     const int cols_per_warp = K / kConsumerWarps;
     const int col0 = warp * cols_per_warp;
     const int n_sc = cols_per_warp / 8;  // 16-byte sub-chunks per warp row slice
@@ -437,6 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int sc = j * 32 + lane;
                 // with ATT, x was written by other CTAs of this grid: read it from L2
                 xr[j] = sc >= n_sc  ? make_uint4(0, 0, 0, 0)
+                        : recv      ? recv_x8(a.recv, 0, K, col0 + sc * 8, cta == 0)
                         : ATT > 0   ? __ldcg(reinterpret_cast<const uint4*>(a.x + col0 + sc * 8))
                                     : *reinterpret_cast<const uint4*>(a.x + col0 + sc * 8);
                 if (norm) ss = sumsq8(xr[j], ss);
@@ -464,7 +496,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int sc = lane; sc < n_sc; sc += 32) {
                     const int c = col0 + sc * 8;
                     uint4 v = make_uint4(0, 0, 0, 0);
-                    if (b < a.nb) v = *reinterpret_cast<const uint4*>(a.x + (size_t)b * a.x_stride + c);
+                    if (b < a.nb)
+                        v = recv ? recv_x8(a.recv, b, K, c, cta == 0)
+                                 : *reinterpret_cast<const uint4*>(a.x + (size_t)b * a.x_stride + c);
                     if (norm) ss[b] = sumsq8(v, ss[b]);
                     *reinterpret_cast<uint4*>(xs + ((size_t)b * K + c) * 2) = v;
                 }

@@ -138,6 +138,22 @@ __host__ __device__ inline uint32_t gemv_attn_smem(int G, int hd, int warps, int
     return (uint32_t)(((size_t)G * hd + 2 * (size_t)hd + (size_t)warps * G * (hd + 2) + (size_t)nh * G * 2) * 4 + 16);
 }
 
+// The receive half of the tensor-parallel all-reduce, run in a GEMV's prologue
+// instead of a kernel of its own: once every rank's flag for the phase has reached
+// its sequence number (bounded wait), x[b, k] = bf16(resid[b, k] + bf16(sum over
+// ranks r, in rank order, of inbox[r * src_stride + b * K + k])) — the arithmetic
+// of k_tp_recv_resid — and CTA 0 also stores x to x_out for later kernels.
+struct GemvRecv {
+    const float* inbox = nullptr;         // this rank's inbox blocks, [tp][src_stride] fp32
+    size_t src_stride = 0;
+    const unsigned int* flags = nullptr;  // this rank's flags [tp]
+    int tp = 0;                           // 0: off (x is read from GemvArgs::x)
+    const int* epoch = nullptr;
+    int seq_mul = 1, seq_add = 0;
+    const uint16_t* resid = nullptr;  // [nb, K] bf16
+    uint16_t* x_out = nullptr;        // [nb, K] bf16
+};
+
 struct GemvArgs {
     const void* W = nullptr;  // [rows, K] in format wfmt; kEpiGlu: gate rows [0,N) then up rows [N,2N)
     int wfmt = kWBf16;
@@ -180,6 +196,7 @@ struct GemvArgs {
     const void* next2_w = nullptr;
     int next2_N = 0, next2_K = 0, next2_U = 1, next2_wfmt = kWBf16;
     GemvAttn att;  // one token: its decode attention runs first and produces x
+    GemvRecv recv;  // tensor parallelism: x is the all-reduce's receive, computed here
     int* err = nullptr;
 };
 
