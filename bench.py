@@ -631,7 +631,8 @@ def run_profile(args):
         r = measure_pkm(ti, torch, ts.cuda_stream, iters=args.steps)
         print(f"profile: pkm {r['ms']:.4f} ms per 65,536 queries")
         return
-    desc = ti.model_desc(**dict(ti.PRESETS[args.preset], n_layers=args.layers))
+    wf = {"bf16": ti.WFMT_BF16, "q4_0": ti.WFMT_Q4_0, "q8_0": ti.WFMT_Q8_0}[args.wfmt]
+    desc = ti.model_desc(**dict(ti.PRESETS[args.preset], n_layers=args.layers, weight_format=wf))
     ctx = args.ctx or args.prompt
     lora = dict(max_adapters=args.adapters, max_lora_rank=args.lora_rank, lora_proj_mask=0x7F) \
         if args.adapters else {}
@@ -866,6 +867,8 @@ def main():
     ap.add_argument("--ctx", type=int, default=0, help="profile: synthetic cached context of this length")
     ap.add_argument("--preset", default="llama3_8b",
                     help="profile: model shape (ti_b200.PRESETS), or pkm for the PKM router workload alone")
+    ap.add_argument("--wfmt", default="bf16", choices=["bf16", "q4_0", "q8_0"],
+                    help="profile: storage format of the layers' linear weights")
     ap.add_argument("--adapters", type=int, default=0, help="profile: LoRA adapters on all projections")
     ap.add_argument("--lora-rank", type=int, default=64, help="profile: rank of those adapters")
     ap.add_argument("--timeline", default=None,

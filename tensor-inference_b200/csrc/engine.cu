@@ -636,7 +636,7 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
     };
 
     // batches of tc_min..256 tokens: RMSNorm pass (when the GEMV would fuse it) +
-    // tcgen05 GEMM (GGUF weights dequantised to bf16 operands in shared memory;
+    // tcgen05 GEMM (GGUF weights dequantised to bf16 operands in TMEM;
     // the LoRA expansion precomputed and added in its epilogue)
     auto gemm = [&](GemvArgs a, int epi, int x_stride_elems, int out_stride, int resid_stride) -> ti_status {
         if (!(e->xn && B >= e->tc_min && B <= 256))
@@ -657,10 +657,31 @@ ti_status enqueue_kernel(ti_engine* e, int B, int kind, int li, cudaStream_t s, 
             a.lora.dval = e->ldval;
             a.lora.dval_stride = rows;
         }
-        TcPlan plan;
-        if (!tc_plan(a, epi, e->dev, e->tc_ws_floats, &plan, &why)) return fail(TI_ERR_UNSUPPORTED, "%s", why.c_str());
-        TI_CUDA(tc_launch(a, epi, plan, e->tc_ws, e->tc_ctr, s, true));
-        if (launches) ++*launches;
+        // GGUF weights: launches of at most 128 tokens (the dequantised operands share
+        // TMEM with the accumulators); the last launch publishes a tensor-parallel send
+        const int chunk = a.wfmt != kWBf16 ? 128 : B;
+        for (int b0 = 0; b0 < B; b0 += chunk) {
+            GemvArgs c = a;
+            c.nb = std::min(chunk, B - b0);
+            if (b0 > 0) {
+                c.x = a.x + (size_t)b0 * a.x_stride;
+                c.out = a.out + (size_t)b0 * a.out_stride;
+                if (a.resid) c.resid = a.resid + (size_t)b0 * a.resid_stride;
+                if (a.partial) c.partial = a.partial + (size_t)b0 * a.out_stride;
+                for (int r = 0; r < a.ps.tp; ++r) c.ps.inbox[r] = a.ps.inbox[r] + (size_t)b0 * a.out_stride;
+                if (a.lora.adapter) {
+                    c.lora.adapter = a.lora.adapter + b0;
+                    c.lora.t = a.lora.t + (size_t)b0 * a.lora.t_stride;
+                    if (a.lora.dval) c.lora.dval = a.lora.dval + (size_t)b0 * a.lora.dval_stride;
+                }
+            }
+            if (a.ps.tp) c.ps.signal = b0 + chunk >= B ? a.ps.signal : 0;
+            TcPlan plan;
+            if (!tc_plan(c, epi, e->dev, e->tc_ws_floats, &plan, &why))
+                return fail(TI_ERR_UNSUPPORTED, "%s", why.c_str());
+            TI_CUDA(tc_launch(c, epi, plan, e->tc_ws, e->tc_ctr, s, true));
+            if (launches) ++*launches;
+        }
         return TI_OK;
     };
 

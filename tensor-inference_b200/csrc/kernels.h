@@ -234,6 +234,9 @@ struct TcPlan {
     uint32_t stage_bytes = 0, tmem_cols = 0;
     uint32_t w_off = 0, x_off = 0, s_off = 0;  // stage layout (weights / tokens / GGUF scales)
     int cb = 0, n_abuf = 0, threads = 0;       // GGUF: code bytes per atom row, dequantised buffers
+    int a_tmem = 0;                            // GGUF: dequantised buffers in TMEM (else shared memory)
+    uint32_t a_col = 0;                        // GGUF, a_tmem: TMEM column of dequantised buffer 0
+    int n_iss = 1;                             // MMA-issuing warps (GGUF with TMEM operands: up to 4)
     size_t smem = 0;
     size_t ws_floats = 0;  // partial-tile workspace this launch needs
     const void* func = nullptr;

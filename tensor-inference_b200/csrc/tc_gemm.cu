@@ -26,6 +26,15 @@
 //               lanes 32*(w%4)..+31 = 32 weight rows), fused epilogue, stores.
 //               Double-buffered TMEM lets the epilogue of one tile overlap the
 //               main loop of the next.
+//   warps 6-13  GGUF Q4_0 / Q8_0 weights only (448 threads): the ring holds the
+//               raw codes (128-byte swizzled boxes) and fp16 scales; each thread
+//               dequantises one weight row's half stage to bf16 pairs.  Up to 128
+//               tokens the pairs go to TMEM (tcgen05.st into 2-3 operand buffers
+//               above the accumulators) and the MMA reads A from TMEM, so shared
+//               memory carries only the 0.56 (Q4_0) or 1.06 (Q8_0) bytes per
+//               weight that HBM delivers; past 128 tokens they go to swizzled
+//               shared-memory atoms (the engine launches GGUF batches in 128-token
+//               pieces, so that form serves direct callers only).
 // Work split (stream-K): the row tiles x k-blocks of the GEMM, tile-major, are
 // cut into equal contiguous ranges, one per CTA, so every SM streams the same
 // number of weight bytes whatever the tile count.  A tile inside one range is
@@ -50,12 +59,15 @@ namespace ti {
 namespace {
 
 constexpr int kTcThreads = 192;    // bf16 weights: TMA, MMA, 4 epilogue warps
-constexpr int kTcThreadsQ = 448;   // GGUF weights: + 8 dequantising warps
+constexpr int kTcThreadsQ = 512;   // GGUF weights: + 8 dequantising warps + 2 more MMA issuers
+constexpr int kTcMaxIss = 3;       // MMA-issuing warps at most (warp 1, then warps 14, 15)
 constexpr int kTcBM = 128;        // weight rows per tile (MMA M)
 constexpr int kTcBK = 64;         // K elements per swizzle atom: one 128-byte row
 constexpr uint32_t kTcABytes = kTcBM * kTcBK * 2;  // 16 KB weight atom (128 rows x 64 K)
 constexpr int kTcMaxTokens = 256;  // MMA N limit
 constexpr size_t kTcSmemBudget = 220 * 1024;
+constexpr int kTcMaxAbuf = 4;      // GGUF: dequantised operand buffers at most
+constexpr int kTcQbs = 4;          // GGUF: atoms per stage (a 16-byte scales box)
 
 // ------------------------------------------------------------------ tcgen05 / TMA wrappers
 TI_DEVICE_INLINE void tma_load_2d_hint(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
@@ -97,6 +109,62 @@ TI_DEVICE_INLINE void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, ui
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
         : "memory");
 }
+// 32 lanes x 16 consecutive fp32 columns (thread i <- lane base+i)
+TI_DEVICE_INLINE void tmem_ld16(uint32_t taddr, float* v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+// bf16x2 arithmetic, each lane rounded once to nearest even
+TI_DEVICE_INLINE uint32_t bsub2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+TI_DEVICE_INLINE uint32_t bmul2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+TI_DEVICE_INLINE uint32_t bfma2(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// (lo, hi) fp32 -> bf16x2, round to nearest even
+TI_DEVICE_INLINE uint32_t cvt_bf2(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+// the same with A (M=128 rows x K=16, bf16 pairs along 8 columns) read from TMEM
+TI_DEVICE_INLINE void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
+        "}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+// 32 lanes x 32 consecutive 32-bit columns (thread i -> lane base+i).  No memory clobber:
+// it writes TMEM only, and tcgen05.wait::st (volatile, after it) orders it for the MMA
+TI_DEVICE_INLINE void tmem_st32(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+        "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+        "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+        "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]));
+}
 TI_DEVICE_INLINE void tc_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
@@ -133,10 +201,15 @@ struct TcKernelArgs {
     int stages;
     int pf;              // the producer prefetches weight k-block it + pf into L2 as it loads k-block it
     // stage layout: bf16: [kbs weight atoms][kbs token atoms]; GGUF: [kbs token atoms]
-    // [codes: 128 rows x kbs*cb bytes][scales: 128 rows x kbs*4 bytes], dequantised
-    // into n_abuf bf16 operand buffers of kbs atoms after the ring
+    // [codes: kbs*cb/128 column blocks of 128 rows x 128 bytes, 128-byte swizzle]
+    // [scales: 128 rows x kbs*4 bytes], dequantised into n_abuf bf16 operand
+    // buffers of kbs atoms (TMEM, or shared memory after the ring)
     uint32_t w_off, x_off, s_off;
     int cb, n_abuf;
+    int a_tmem;      // dequantised operand buffers in TMEM columns [a_col + b * kbs * 32, ...) (else shared memory)
+    uint32_t a_col;
+    int n_iss;       // MMA-issuing warps: issuer i takes K steps i, i + n_iss, ... of each stage into its
+                     // own accumulator pair, TMEM columns [(2i + buf) * np, +np); the epilogue sums them in order
     uint32_t stage_bytes, tmem_cols;
     uint16_t* out;
     int out_stride;
@@ -173,9 +246,9 @@ __host__ __device__ inline TcSmem tc_smem_layout(int stages, uint32_t stage_byte
     L.empty = o;
     o += 8u * stages;
     L.afull = o;
-    o += 16;
+    o += 8 * kTcMaxAbuf;
     L.aempty = o;
-    o += 16;
+    o += 8 * kTcMaxAbuf;
     L.tfull = o;
     o += 16;
     L.tempty = o;
@@ -201,7 +274,7 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
               const __grid_constant__ CUtensorMap tms, const TcKernelArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const TcSmem L = tc_smem_layout(a.stages, a.stage_bytes, a.np, a.n_abuf, a.kbs);
+    const TcSmem L = tc_smem_layout(a.stages, a.stage_bytes, a.np, a.a_tmem ? 0 : a.n_abuf, a.kbs);
     uint64_t* afull = reinterpret_cast<uint64_t*>(smem + L.afull);
     uint64_t* aempty = reinterpret_cast<uint64_t*>(smem + L.aempty);
     constexpr bool kQ = WF != kWBf16;
@@ -223,15 +296,17 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
         pdl_trigger();
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&empty[s], a.n_iss);  // one tcgen05.commit per issuer
         }
         for (int j = 0; j < 2; ++j) {
-            mbar_init(&tfull[j], 1);
+            mbar_init(&tfull[j], a.n_iss);
             mbar_init(&tempty[j], 4);
-            mbar_init(&afull[j], 8);   // the dequantising warps
-            mbar_init(&aempty[j], 1);  // tcgen05.commit
         }
-        mbar_init(drain, 1);
+        for (int j = 0; j < kTcMaxAbuf; ++j) {
+            mbar_init(&afull[j], 8);         // the dequantising warps
+            mbar_init(&aempty[j], a.n_iss);  // tcgen05.commit
+        }
+        mbar_init(drain, a.n_iss);
         misc[1] = 0;
         fence_barrier_init();
     }
@@ -296,16 +371,23 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
             auto load_w = [&](int tile, int kb, int s) {
                 uint8_t* st = smem + (size_t)s * a.stage_bytes;
                 if constexpr (kQ) {
-                    // the codes and fp16 scales of kbs*64 columns of 128 rows (two halves of 64 for GLU)
+                    // the codes (128-byte column blocks) and fp16 scales of kbs*64 columns
+                    // of 128 rows (two halves of 64 rows for GLU)
                     const int xc = kb * kbs * a.cb, xs = kb * kbs * 4;
+                    for (int h = 0; h < kbs * a.cb / 128; ++h) {
+                        uint8_t* cbk = st + a.w_off + (size_t)h * kTcBM * 128;
+                        if (kGlu) {
+                            tma_load_2d_hint(cbk, &tmw, xc + h * 128, tile * 64, &full[s], pol);
+                            tma_load_2d_hint(cbk + 64 * 128, &tmw, xc + h * 128, a.N + tile * 64, &full[s], pol);
+                        } else {
+                            tma_load_2d_hint(cbk, &tmw, xc + h * 128, tile * kTcBM, &full[s], pol);
+                        }
+                    }
                     if (kGlu) {
-                        const uint32_t half_c = 64u * kbs * a.cb, half_s = 64u * kbs * 4;
-                        tma_load_2d_hint(st + a.w_off, &tmw, xc, tile * 64, &full[s], pol);
-                        tma_load_2d_hint(st + a.w_off + half_c, &tmw, xc, a.N + tile * 64, &full[s], pol);
+                        const uint32_t half_s = 64u * kbs * 4;
                         tma_load_2d_hint(st + a.s_off, &tms, xs, tile * 64, &full[s], pol);
                         tma_load_2d_hint(st + a.s_off + half_s, &tms, xs, a.N + tile * 64, &full[s], pol);
                     } else {
-                        tma_load_2d_hint(st + a.w_off, &tmw, xc, tile * kTcBM, &full[s], pol);
                         tma_load_2d_hint(st + a.s_off, &tms, xs, tile * kTcBM, &full[s], pol);
                     }
                 } else {
@@ -331,13 +413,18 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                 const int tile = (int)(g / a.kblocks), kb = (int)(g % a.kblocks);
                 if constexpr (kQ) {
                     const int xc = kb * kbs * a.cb, xs = kb * kbs * 4;
+                    for (int h = 0; h < kbs * a.cb / 128; ++h) {
+                        if (kGlu) {
+                            tma_prefetch_2d(&tmw, xc + h * 128, tile * 64);
+                            tma_prefetch_2d(&tmw, xc + h * 128, a.N + tile * 64);
+                        } else {
+                            tma_prefetch_2d(&tmw, xc + h * 128, tile * kTcBM);
+                        }
+                    }
                     if (kGlu) {
-                        tma_prefetch_2d(&tmw, xc, tile * 64);
-                        tma_prefetch_2d(&tmw, xc, a.N + tile * 64);
                         tma_prefetch_2d(&tms, xs, tile * 64);
                         tma_prefetch_2d(&tms, xs, a.N + tile * 64);
                     } else {
-                        tma_prefetch_2d(&tmw, xc, tile * kTcBM);
                         tma_prefetch_2d(&tms, xs, tile * kTcBM);
                     }
                 } else {
@@ -393,9 +480,14 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
             for (int j = max(0, issued - S); j < issued; ++j)
                 if (!mbar_wait(&full[j % S], (j / S) & 1, a.err, kErrTimeoutFull)) break;
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
+    } else if (warp == 1 || (kQ && warp >= 14)) {
+        // ------------------------------------------------------------ MMA issuers
+        // A small tcgen05.mma blocks its issuing thread for about a hundred cycles
+        // whatever N is, so one thread issuing M=128, N=32, K=16 steps reaches about
+        // a third of the rate dequantised GGUF weights arrive at; issuers in separate
+        // warps, each into its own accumulators, add up (A from TMEM).
+        const int iss = warp == 1 ? 0 : warp - 13;
+        if (lane == 0 && iss < a.n_iss) {
             const uint32_t idesc = idesc_bf16(np);
             int it = 0, j = 0;
             bool issued = false;
@@ -406,7 +498,7 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                     return false;
                 }
                 tc_fence_after();
-                const uint32_t d = tmem + (uint32_t)(buf * np);
+                const uint32_t d = tmem + (uint32_t)((2 * iss + buf) * np);
                 for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % S;
                     if (misc[1] || !mbar_wait(&full[s], (it / S) & 1, a.err, kErrTimeoutFull)) {
@@ -420,15 +512,28 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                     }
                     tc_fence_after();
                     const uint32_t st_addr = smem_u32(smem + (size_t)s * a.stage_bytes);
-                    const uint32_t a_addr =
-                        kQ ? smem_u32(smem + L.abuf + (size_t)ab * a.kbs * kTcABytes) : st_addr + a.w_off;
                     const uint32_t b_addr = st_addr + a.x_off;
-                    for (int jj = 0; jj < a.kbs; ++jj)
+                    if (kQ && a.a_tmem) {
+                        // weights from TMEM: atom jj in 32 columns of bf16 pairs, 8 per K=16 step
+                        // K step m = 4 * atom + k of the stage (16 columns of bf16 pairs = 8 TMEM columns)
+                        const uint32_t a_t = tmem + a.a_col + (uint32_t)(ab * a.kbs * 32);
+                        const uint64_t b_d = smem_desc_sw128(b_addr);
+                        for (int m = iss; m < a.kbs * (kTcBK / 16); m += a.n_iss) {
+                            const int jj = m >> 2, k = m & 3;
+                            tc_mma_ts(d, a_t + (uint32_t)(m * 8),
+                                      b_d + (uint64_t)((jj * (uint32_t)np * kTcBK * 2 + k * 32) >> 4), idesc,
+                                      (kb > kb0 || m > iss) ? 1u : 0u);
+                        }
+                    } else {
+                        const uint32_t a_addr =
+                            kQ ? smem_u32(smem + L.abuf + (size_t)ab * a.kbs * kTcABytes) : st_addr + a.w_off;
+                        for (int jj = 0; jj < a.kbs; ++jj)
 #pragma unroll
-                        for (int k = 0; k < kTcBK / 16; ++k)
-                            tc_mma(d, smem_desc_sw128(a_addr + jj * kTcABytes + k * 32),
-                                   smem_desc_sw128(b_addr + jj * (uint32_t)np * kTcBK * 2 + k * 32), idesc,
-                                   (kb > kb0 || jj > 0 || k > 0) ? 1u : 0u);
+                            for (int k = 0; k < kTcBK / 16; ++k)
+                                tc_mma(d, smem_desc_sw128(a_addr + jj * kTcABytes + k * 32),
+                                       smem_desc_sw128(b_addr + jj * (uint32_t)np * kTcBK * 2 + k * 32), idesc,
+                                       (kb > kb0 || jj > 0 || k > 0) ? 1u : 0u);
+                    }
                     tc_commit(&empty[s]);
                     if (kQ) tc_commit(&aempty[ab]);
                     issued = true;
@@ -437,70 +542,127 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                 ++j;
                 return true;
             });
-            // all MMAs retired before TMEM is released
+            // all MMAs retired before TMEM is released (every issuer has MMAs when any has)
             if (issued) {
                 tc_commit(drain);
                 mbar_wait(drain, 0, a.err, kErrTimeoutFull);
             }
         }
-    } else if (kQ && warp >= 6) {
+    } else if (kQ && warp >= 6 && warp < 14) {
         // ------------------------------------------------------------ dequantising warps
-        // thread -> (row, half of the stage's atoms): the exact value d*(q-8) (Q4_0) or
-        // d*q (Q8_0), rounded to bf16, into the 128-byte-swizzled operand atoms
-        const int ct = threadIdx.x - 192;
-        const int row = ct >> 1, half = ct & 1;
-        const int kbs = a.kbs, cb = a.cb;
+        // thread -> one weight row (lane of the TMEM quarter warp % 4 may address) and
+        // half of the stage's 4 atoms (warps 6..9 the first two, 10..13 the last two).
+        // Each value is the exact d*(q-8) (Q4_0) or d*q (Q8_0) rounded once to bf16.
+        // Codes are read through the 128-byte swizzle the TMA wrote them with, so
+        // each 8-row phase of a 16-byte load hits 8 distinct bank groups.
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const int part = (warp - 6) >> 2;
         walk([&](int, int, int it) {
             const int s = it % S, ab = it % a.n_abuf;
             if (misc[1] || !mbar_wait(&full[s], (it / S) & 1, a.err, kErrTimeoutFull)) {
                 misc[1] = 1;
                 return false;
             }
-            if (misc[1] || !mbar_wait(&aempty[ab], ((it / a.n_abuf) & 1) ^ 1, a.err, kErrTimeoutEmpty)) {
-                misc[1] = 1;
-                return false;
-            }
             const uint8_t* st = smem + (size_t)s * a.stage_bytes;
-            const uint8_t* codes = st + a.w_off + (size_t)row * kbs * cb;
-            const uint8_t* scl = st + a.s_off + (size_t)row * kbs * 4;
-            uint8_t* A = smem + L.abuf + (size_t)ab * kbs * kTcABytes;
-            for (int j = half * (kbs / 2); j < (half + 1) * (kbs / 2); ++j) {
-                const float d0 = __half2float(*reinterpret_cast<const __half*>(scl + j * 4));
-                const float d1 = __half2float(*reinterpret_cast<const __half*>(scl + j * 4 + 2));
+            const uint8_t* crow = st + a.w_off + (size_t)row * 128;
+            const uint4 sc = *reinterpret_cast<const uint4*>(st + a.s_off + (size_t)row * kTcQbs * 4);
+            // the scales of this thread's two atoms (register selects, no local array)
+            const uint32_t scw[2] = {part ? sc.z : sc.x, part ? sc.w : sc.y};
+            bool buf_free = false;  // the operand buffer is waited for after the first atom's math
+            // both atoms' code words loaded up front (their latency overlaps the first atom's math)
+            constexpr int kWords = WF == kWQ4 ? 8 : 16;  // code words of one atom row
+            uint32_t qa[kTcQbs / 2][kWords];
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const float d = c < 4 ? d0 : d1;  // 8-element chunk c of 32-element block c / 4
-                    const float2 dd = make_float2(d, d);
-                    // code bytes placed under the exponent of 2^23 (float = 2^23 + byte), the
-                    // bias subtracted exactly, times d exactly, rounded once to bf16
-                    uint32_t lo, hi;
-                    float2 bias;
-                    if constexpr (WF == kWQ4) {
-                        const uint32_t q = *reinterpret_cast<const uint32_t*>(codes + j * 32 + c * 4);
-                        lo = q & 0x0F0F0F0Fu;  // elements 0, 2, 4, 6
-                        hi = (q >> 4) & 0x0F0F0F0Fu;  // elements 1, 3, 5, 7
-                        bias = make_float2(-8388616.0f, -8388616.0f);  // 2^23 + 8
-                    } else {
-                        const uint2 q = *reinterpret_cast<const uint2*>(codes + j * 64 + c * 8);
-                        const uint32_t u0 = q.x ^ 0x80808080u, u1 = q.y ^ 0x80808080u;  // int8 -> q + 128
-                        lo = __byte_perm(u0, u1, 0x6420);
-                        hi = __byte_perm(u0, u1, 0x7531);
-                        bias = make_float2(-8388736.0f, -8388736.0f);  // 2^23 + 128
-                    }
-                    uint32_t w[4];
+            for (int jj = 0; jj < kTcQbs / 2; ++jj)
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 m = make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7440u | e)),
-                                                     __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440u | e)));
-                        const float2 v = ffma2(ffma2(m, make_float2(1.f, 1.f), bias), dd, make_float2(0.f, 0.f));
-                        w[e] = pack_bf2(v.x, v.y);
+                for (int t = 0; t < kWords / 4; ++t) {
+                    const int L = (part * (kTcQbs / 2) + jj) * (kWords / 4) + t;  // 16-byte chunk of the row
+                    const uint4 v = *reinterpret_cast<const uint4*>(crow + (size_t)(L >> 3) * kTcBM * 128 +
+                                                                    (((L & 7) ^ (row & 7)) << 4));
+                    qa[jj][4 * t] = v.x;
+                    qa[jj][4 * t + 1] = v.y;
+                    qa[jj][4 * t + 2] = v.z;
+                    qa[jj][4 * t + 3] = v.w;
+                }
+#pragma unroll
+            for (int jj = 0; jj < kTcQbs / 2; ++jj) {
+                const int j = part * (kTcQbs / 2) + jj;
+                const uint32_t* q = qa[jj];
+                const float d0 = __half2float(__ushort_as_half((unsigned short)(scw[jj] & 0xFFFFu)));
+                const float d1 = __half2float(__ushort_as_half((unsigned short)(scw[jj] >> 16)));
+                uint32_t w[32];
+                if constexpr (WF == kWQ4) {
+                    // All in bf16x2 (no per-element conversion).  Per block, d = dh + dl with
+                    // dh = bf16(d) and dl = d - dh (at most 3 significant bits, exact in
+                    // bf16).  Per pair, P = (128 + q_even, 128 + 8 q_odd) built from the
+                    // code bits, a = P - (136, 192) = (q - 8, 8 (q - 8)) exactly, and
+                    // fma(a, (dh, dh/8), a * (dl, dl/8)) is d (q - 8) rounded once: the
+                    // addend a * dl has at most 7 significant bits, so it is exact.
+                    uint32_t dh[2], dl[2];
+                    const float df[2] = {d0, d1};
+#pragma unroll
+                    for (int b = 0; b < 2; ++b) {
+                        dh[b] = cvt_bf2(df[b], df[b] * 0.125f);
+                        const float dlf = df[b] - __uint_as_float(dh[b] << 16);
+                        dl[b] = cvt_bf2(dlf, dlf * 0.125f);
                     }
-                    *reinterpret_cast<uint4*>(A + (size_t)j * kTcABytes + row * 128 + ((c ^ (row & 7)) << 4)) =
-                        make_uint4(w[0], w[1], w[2], w[3]);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {  // 8-element chunk c of 32-element block c / 4
+                        const uint32_t qw = q[c], qs = q[c] >> 1;
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {  // byte e: element 2e (low nibble), 2e+1 (high)
+                            const uint32_t t = __byte_perm(qw, qs, (uint32_t)e | ((uint32_t)(e + 4) << 8));
+                            const uint32_t P = (t & 0x0078000Fu) | 0x43004300u;
+                            const uint32_t av = bsub2(P, 0x43404308u);  // (136, 192)
+                            w[c * 4 + e] = bfma2(av, dh[c >> 2], bmul2(av, dl[c >> 2]));
+                        }
+                    }
+                } else {
+                    // the int8 code byte u = q + 128 under the exponent of 2^15 (m = 2^15 + u)
+                    // and fma(m, d, -(2^15 + 128) d) = d q exactly (constant and result fit
+                    // 24 bits, for finite scales), rounded once to bf16
+                    const float2 dd0 = make_float2(d0, d0), dd1 = make_float2(d1, d1);
+                    const float2 cc0 = make_float2(-32896.0f * d0, -32896.0f * d0);
+                    const float2 cc1 = make_float2(-32896.0f * d1, -32896.0f * d1);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const float2 dd = c < 4 ? dd0 : dd1, cc = c < 4 ? cc0 : cc1;
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {  // elements 2e, 2e+1 of the chunk
+                            const uint32_t u = q[2 * c + (e >> 1)] ^ 0x80808080u;
+                            const uint32_t m0 = __byte_perm(u, 0x47000000u, 0x7404u | ((2 * (e & 1)) << 4));
+                            const uint32_t m1 = __byte_perm(u, 0x47000000u, 0x7404u | ((2 * (e & 1) + 1) << 4));
+                            const float2 v = ffma2(make_float2(__uint_as_float(m0), __uint_as_float(m1)), dd, cc);
+                            w[c * 4 + e] = cvt_bf2(v.x, v.y);
+                        }
+                    }
+                }
+                if (!buf_free) {
+                    if (misc[1] || !mbar_wait(&aempty[ab], ((it / a.n_abuf) & 1) ^ 1, a.err, kErrTimeoutEmpty)) {
+                        misc[1] = 1;
+                        return false;
+                    }
+                    if (a.a_tmem) tc_fence_after();
+                    buf_free = true;
+                }
+                if (a.a_tmem) {
+                    tmem_st32(tmem + ((uint32_t)(quarter * 32) << 16) + a.a_col + (uint32_t)((ab * kTcQbs + j) * 32), w);
+                } else {
+                    uint8_t* A = smem + L.abuf + (size_t)(ab * kTcQbs + j) * kTcABytes + (size_t)row * 128;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c)
+                        *reinterpret_cast<uint4*>(A + ((c ^ (row & 7)) << 4)) =
+                            make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
                 }
             }
-            // generic-proxy writes -> the tensor cores' async-proxy reads
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            if (a.a_tmem) {
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                tc_fence_before();
+            } else {
+                // generic-proxy writes -> the tensor cores' async-proxy reads
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&afull[ab]);
             return true;
@@ -526,6 +688,18 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
             if (misc[3]) return false;
             tc_fence_after();
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * np);
+            // 32 token columns of this row: the issuers' accumulators summed in issuer order
+            auto ld_acc = [&](int c, float* v) {
+                tmem_ld32(tbase + (uint32_t)(c * 32), v);
+                for (int i = 1; i < a.n_iss; ++i)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        float w[16];
+                        tmem_ld16(tbase + (uint32_t)(2 * i * np + c * 32 + h * 16), w);
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) v[h * 16 + k] += w[k];
+                    }
+            };
             // row handled by this thread: GLU tiles hold 64 gate rows then the 64 matching up rows
             const int n = kGlu ? tile * 64 + (rl & 63) : tile * kTcBM + rl;
             const bool row_ok = n < a.N;
@@ -639,7 +813,7 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
             if (c_lo == c_hi) {
                 for (int c = 0; c < nchunks; ++c) {
                     float v[32];
-                    tmem_ld32(tbase + (uint32_t)(c * 32), v);
+                    ld_acc(c, v);
                     if (c == nchunks - 1) {
                         // accumulator fully read: hand it back to the MMA warp
                         tc_fence_before();
@@ -653,7 +827,7 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                 float* wsp = a.ws + ((size_t)blockIdx.x * 2 + (first ? 0 : 1)) * (size_t)np * kTcBM;
                 for (int c = 0; c < nchunks; ++c) {
                     float v[32];
-                    tmem_ld32(tbase + (uint32_t)(c * 32), v);
+                    ld_acc(c, v);
 #pragma unroll
                     for (int i = 0; i < 32; ++i) __stcg(wsp + (size_t)(c * 32 + i) * kTcBM + rl, v[i]);
                 }
@@ -848,7 +1022,7 @@ const void* tc_func(int epi, int wf) {
 
 // uint8 [rows, cols] with row pitch `pitch` bytes; box = box_cols x box_rows, no swizzle
 bool make_tmap_u8(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch, uint32_t box_cols,
-                  uint32_t box_rows) {
+                  uint32_t box_rows, bool sw128) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     const cuuint64_t dims[2] = {cols, rows};
@@ -856,8 +1030,8 @@ bool make_tmap_u8(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols
     const cuuint32_t box[2] = {box_cols, box_rows};
     const cuuint32_t estr[2] = {1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+              CU_TENSOR_MAP_INTERLEAVE_NONE, sw128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
@@ -933,6 +1107,9 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
         return false;
     }
     p->cb = g.wfmt == kWQ4 ? 32 : g.wfmt == kWQ8 ? 64 : 0;  // code bytes per 64-column atom row
+    p->a_tmem = 0;
+    p->a_col = 0;
+    p->n_iss = 1;
     if (!q) {
         p->stage_bytes = (uint32_t)best_kbs * (kTcABytes + xatom);
         p->w_off = 0;
@@ -955,20 +1132,39 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
         if (2 * abuf + 2 * ((size_t)p->stage_bytes + 16) > kTcSmemBudget - Lq.total) p->n_abuf = 1;
         const char* qb = std::getenv("TI_TC_QBUF");
         if (qb && std::atoi(qb) == 1) p->n_abuf = 1;
+        // up to 128 tokens the dequantised operands live in TMEM columns above the two
+        // accumulators (the whole 512 columns: one CTA per SM, as the ring's shared
+        // memory already forces), so shared memory carries only the raw codes
+        const char* qt = std::getenv("TI_TC_QTMEM");
+        if (np <= 128 && !(qt && std::atoi(qt) == 0)) {
+            p->a_tmem = 1;
+            // as many issuers (up to 3) as leave two operand buffers
+            p->n_iss = kTcMaxIss;
+            while (p->n_iss > 1 && 2 * p->n_iss * np > 256) --p->n_iss;
+            const char* qi = std::getenv("TI_TC_QISS");
+            if (qi && std::atoi(qi) >= 1) p->n_iss = std::min(p->n_iss, std::atoi(qi));
+            p->a_col = (uint32_t)(2 * p->n_iss * np + 127) / 128 * 128;
+            p->n_abuf = std::min(kTcMaxAbuf, (int)((512 - p->a_col) / (uint32_t)(best_kbs * 32)));
+        }
     }
-    const size_t abuf_bytes = (size_t)p->n_abuf * best_kbs * kTcABytes;
+    const size_t abuf_bytes = p->a_tmem ? 0 : (size_t)p->n_abuf * best_kbs * kTcABytes;
     p->stages = (int)std::min<size_t>(12, (kTcSmemBudget - L0.total - abuf_bytes) / (p->stage_bytes + 16));
     if (p->stages < 2) {
         if (why) *why = "tc_gemm: token tile too large for a two-stage ring";
         return false;
     }
-    p->smem = tc_smem_layout(p->stages, p->stage_bytes, np, p->n_abuf, best_kbs).total;
+    p->smem = tc_smem_layout(p->stages, p->stage_bytes, np, p->a_tmem ? 0 : p->n_abuf, best_kbs).total;
+    if (p->a_tmem && 2 * p->smem <= 228 * 1024) {
+        // a second CTA on the SM could hold TMEM columns this one waits for
+        if (why) *why = "tc_gemm: TMEM operands need one CTA per SM";
+        return false;
+    }
     // L2 prefetch window in k-blocks beyond the ring (TI_TC_PF overrides)
     const char* pfe = std::getenv("TI_TC_PF");
     p->pf = pfe ? std::max(0, std::atoi(pfe)) : 0;
     uint32_t cols = 32;
     while (cols < (uint32_t)(2 * np)) cols <<= 1;
-    p->tmem_cols = cols;
+    p->tmem_cols = p->a_tmem ? 512u : cols;
     p->func = tc_func(epi, g.wfmt);
     p->threads = q ? kTcThreadsQ : kTcThreads;
     if (!p->func) {
@@ -991,9 +1187,10 @@ cudaError_t tc_launch(const GemvArgs& g, int epi, const TcPlan& p, float* ws, un
         const uint64_t pitch = wrow_bytes(g.K, g.wfmt);
         const uint64_t code_bytes = (uint64_t)g.K * p.cb / 64;
         const uint8_t* base = reinterpret_cast<const uint8_t*>(g.W);
-        if (!make_tmap_u8(&mw, base, wrows, code_bytes, pitch, (uint32_t)p.kbs * p.cb, box_rows))
-            return cudaErrorInvalidValue;
-        if (!make_tmap_u8(&ms, base + code_bytes, wrows, (uint64_t)g.K / 16, pitch, (uint32_t)p.kbs * 4, box_rows))
+        // codes in boxes of 128 bytes x rows, 128-byte swizzle (the dequantising warps' bank pattern)
+        if (!make_tmap_u8(&mw, base, wrows, code_bytes, pitch, 128, box_rows, true)) return cudaErrorInvalidValue;
+        if (!make_tmap_u8(&ms, base + code_bytes, wrows, (uint64_t)g.K / 16, pitch, (uint32_t)p.kbs * 4, box_rows,
+                          false))
             return cudaErrorInvalidValue;
     }
     if (!make_tmap_bf16_sw128(&mx, g.x, g.nb, g.K, g.x_stride, p.np)) return cudaErrorInvalidValue;
@@ -1015,6 +1212,9 @@ cudaError_t tc_launch(const GemvArgs& g, int epi, const TcPlan& p, float* ws, un
     a.s_off = p.s_off;
     a.cb = p.cb;
     a.n_abuf = p.n_abuf;
+    a.a_tmem = p.a_tmem;
+    a.a_col = p.a_col;
+    a.n_iss = p.n_iss;
     a.tmem_cols = p.tmem_cols;
     a.out = g.out;
     a.out_stride = g.out_stride;

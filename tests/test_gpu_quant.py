@@ -144,3 +144,11 @@ def test_quantised_tensor_core_batch_qwen7b_shapes(wf):
     # (the dequantised weight is rounded to bf16 for the bf16 x bf16 MMA: <= 2^-9 relative)
     kw = dict(ti.PRESETS["qwen25_7b"], n_layers=2, weight_format=wf)
     _parity(kw, [2 + b % 3 for b in range(12)], steps=2)
+
+
+@pytest.mark.parametrize("wf", [ti.WFMT_Q4_0, ti.WFMT_Q8_0])
+@pytest.mark.parametrize("B", [64, 100, 136])
+def test_quantised_tensor_core_wide_batches(wf, B):
+    # 64 / 100 tokens: the dequantised operands in TMEM (3 and 2 buffers above the
+    # accumulators); 136 tokens: past TMEM's room, the shared-memory operand buffers
+    _parity(dict(SMALL, weight_format=wf), [1 + b % 4 for b in range(B)], steps=1)
