@@ -367,7 +367,9 @@ ti_status ti_engine_decode(ti_engine* e, int batch, const int32_t* seq_ids, cons
  * ti_engine_decode_device call runs one step whose input tokens are the
  * previous step's ids (greedy, or drawn by the sequence's sampler), all on the
  * device (no host synchronisation).  Sequences must have pages reserved
- * (ti_seq_reserve) for the steps run. */
+ * (ti_seq_reserve) for the steps run.  `stream` is a stream of the engine's
+ * device, whatever device is current for the caller (0: that device's default
+ * stream, the one ti_engine_unbind with stream 0 reads the ids on). */
 ti_status ti_engine_bind(ti_engine* e, int batch, const int32_t* seq_ids, const int32_t* first_tokens,
                          const int32_t* adapter_ids);
 ti_status ti_engine_decode_device(ti_engine* e, void* stream);

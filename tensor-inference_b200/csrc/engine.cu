@@ -1808,6 +1808,10 @@ ti_status ti_engine_bind(ti_engine* e, int B, const int32_t* seq_ids, const int3
 
 ti_status ti_engine_decode_device(ti_engine* e, void* stream) {
     TI_CHECK(e && e->bound_batch > 0, TI_ERR_STATE, "engine not bound");
+    // stream 0 is the engine device's default stream (unbind reads the ids there): without
+    // the guard a caller whose current device is another one would launch the step on that
+    // device's default stream, unordered with unbind's copy
+    DeviceGuard dg(e->dev);
     GraphEntry* g = nullptr;
     if (ti_status st = get_graph(e, e->bound_batch, e->bound_lora, &g, false, e->bound_sample)) return st;
     TI_CUDA(cudaGraphLaunch(g->exec, (cudaStream_t)stream));

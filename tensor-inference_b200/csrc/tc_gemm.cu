@@ -58,7 +58,7 @@ namespace ti {
 
 namespace {
 
-constexpr int kTcThreads = 192;    // bf16 weights: TMA, MMA, 4 epilogue warps
+constexpr int kTcThreads = 224;    // bf16 weights: TMA, MMA, 4 epilogue warps, a second MMA issuer
 constexpr int kTcThreadsQ = 512;   // GGUF weights: + 8 dequantising warps + 2 more MMA issuers
 constexpr int kTcMaxIss = 3;       // MMA-issuing warps at most (warp 1, then warps 14, 15)
 constexpr int kTcBM = 128;        // weight rows per tile (MMA M)
@@ -480,13 +480,14 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
             for (int j = max(0, issued - S); j < issued; ++j)
                 if (!mbar_wait(&full[j % S], (j / S) & 1, a.err, kErrTimeoutFull)) break;
         }
-    } else if (warp == 1 || (kQ && warp >= 14)) {
+    } else if (warp == 1 || (kQ && warp >= 14) || (!kQ && warp == 6)) {
         // ------------------------------------------------------------ MMA issuers
         // A small tcgen05.mma blocks its issuing thread for about a hundred cycles
         // whatever N is, so one thread issuing M=128, N=32, K=16 steps reaches about
         // a third of the rate dequantised GGUF weights arrive at; issuers in separate
-        // warps, each into its own accumulators, add up (A from TMEM).
-        const int iss = warp == 1 ? 0 : warp - 13;
+        // warps, each into its own accumulators, add up (A from TMEM; from shared memory
+        // two issuers still double the rate).  Issuers: warp 1, then 14, 15 (GGUF) or 6 (bf16).
+        const int iss = warp == 1 ? 0 : kQ ? warp - 13 : 1;
         if (lane == 0 && iss < a.n_iss) {
             const uint32_t idesc = idesc_bf16(np);
             int it = 0, j = 0;
@@ -527,12 +528,23 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                     } else {
                         const uint32_t a_addr =
                             kQ ? smem_u32(smem + L.abuf + (size_t)ab * a.kbs * kTcABytes) : st_addr + a.w_off;
-                        for (int jj = 0; jj < a.kbs; ++jj)
+                        if (a.n_iss == 1) {
+                            for (int jj = 0; jj < a.kbs; ++jj)
 #pragma unroll
-                            for (int k = 0; k < kTcBK / 16; ++k)
-                                tc_mma(d, smem_desc_sw128(a_addr + jj * kTcABytes + k * 32),
-                                       smem_desc_sw128(b_addr + jj * (uint32_t)np * kTcBK * 2 + k * 32), idesc,
-                                       (kb > kb0 || jj > 0 || k > 0) ? 1u : 0u);
+                                for (int k = 0; k < kTcBK / 16; ++k)
+                                    tc_mma(d, smem_desc_sw128(a_addr + jj * kTcABytes + k * 32),
+                                           smem_desc_sw128(b_addr + jj * (uint32_t)np * kTcBK * 2 + k * 32), idesc,
+                                           (kb > kb0 || jj > 0 || k > 0) ? 1u : 0u);
+                        } else {
+                            // K step m = 4 * atom + k; issuer iss takes m = iss, iss + n_iss, ...
+                            const uint64_t a_d = smem_desc_sw128(a_addr), b_d = smem_desc_sw128(b_addr);
+                            for (int m = iss; m < a.kbs * (kTcBK / 16); m += a.n_iss) {
+                                const int jj = m >> 2, k = m & 3;
+                                tc_mma(d, a_d + (uint64_t)((jj * kTcABytes + k * 32) >> 4),
+                                       b_d + (uint64_t)((jj * (uint32_t)np * kTcBK * 2 + k * 32) >> 4), idesc,
+                                       (kb > kb0 || m > iss) ? 1u : 0u);
+                            }
+                        }
                     }
                     tc_commit(&empty[s]);
                     if (kQ) tc_commit(&aempty[ab]);
@@ -1110,6 +1122,11 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
     p->a_tmem = 0;
     p->a_col = 0;
     p->n_iss = 1;
+    if (!q && 4 * np <= 512) {
+        // bf16: two issuers (four np-column accumulators) while TMEM holds them
+        const char* bi = std::getenv("TI_TC_ISS");
+        p->n_iss = bi && std::atoi(bi) == 1 ? 1 : 2;
+    }
     if (!q) {
         p->stage_bytes = (uint32_t)best_kbs * (kTcABytes + xatom);
         p->w_off = 0;
@@ -1163,7 +1180,7 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
     const char* pfe = std::getenv("TI_TC_PF");
     p->pf = pfe ? std::max(0, std::atoi(pfe)) : 0;
     uint32_t cols = 32;
-    while (cols < (uint32_t)(2 * np)) cols <<= 1;
+    while (cols < (uint32_t)(2 * p->n_iss * np)) cols <<= 1;
     p->tmem_cols = p->a_tmem ? 512u : cols;
     p->func = tc_func(epi, g.wfmt);
     p->threads = q ? kTcThreadsQ : kTcThreads;
