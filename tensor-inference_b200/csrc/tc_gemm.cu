@@ -26,7 +26,7 @@
 //               lanes 32*(w%4)..+31 = 32 weight rows), fused epilogue, stores.
 //               Double-buffered TMEM lets the epilogue of one tile overlap the
 //               main loop of the next.
-//   warps 6-13  GGUF Q4_0 / Q8_0 weights only (448 threads): the ring holds the
+//   warps 6-13  GGUF Q4_0 / Q8_0 weights only (512 threads): the ring holds the
 //               raw codes (128-byte swizzled boxes) and fp16 scales; each thread
 //               dequantises one weight row's half stage to bf16 pairs.  Up to 128
 //               tokens the pairs go to TMEM (tcgen05.st into 2-3 operand buffers
@@ -35,6 +35,9 @@
 //               weight that HBM delivers; past 128 tokens they go to swizzled
 //               shared-memory atoms (the engine launches GGUF batches in 128-token
 //               pieces, so that form serves direct callers only).
+//   warps 14-15 GGUF with TMEM operands: two more MMA issuers (a small tcgen05.mma
+//               blocks its issuing thread ~100 cycles, so issuers in separate
+//               warps add up); bf16: warp 6 is the second issuer (224 threads).
 // Work split (stream-K): the row tiles x k-blocks of the GEMM, tile-major, are
 // cut into equal contiguous ranges, one per CTA, so every SM streams the same
 // number of weight bytes whatever the tile count.  A tile inside one range is
@@ -59,7 +62,10 @@ namespace ti {
 namespace {
 
 constexpr int kTcThreads = 224;    // bf16 weights: TMA, MMA, 4 epilogue warps, a second MMA issuer
-constexpr int kTcThreadsQ = 512;   // GGUF weights: + 8 dequantising warps + 2 more MMA issuers
+// GGUF: dequantising warps (warps 6..13).  16 (one atom per thread per stage) measured
+// slower: 24 warps leave 80 registers a thread and the epilogue spills.
+constexpr int kTcDeqWarps = 8;
+constexpr int kTcThreadsQ = 32 * (6 + kTcDeqWarps + 2);  // GGUF weights: + dequantising warps + 2 more MMA issuers
 constexpr int kTcMaxIss = 3;       // MMA-issuing warps at most (warp 1, then warps 14, 15)
 constexpr int kTcBM = 128;        // weight rows per tile (MMA M)
 constexpr int kTcBK = 64;         // K elements per swizzle atom: one 128-byte row
@@ -68,6 +74,7 @@ constexpr int kTcMaxTokens = 256;  // MMA N limit
 constexpr size_t kTcSmemBudget = 220 * 1024;
 constexpr int kTcMaxAbuf = 4;      // GGUF: dequantised operand buffers at most
 constexpr int kTcQbs = 4;          // GGUF: atoms per stage (a 16-byte scales box)
+constexpr int kTcAtPerThr = kTcQbs * 4 / kTcDeqWarps;  // GGUF: atoms one dequantising thread takes per stage
 
 // ------------------------------------------------------------------ tcgen05 / TMA wrappers
 TI_DEVICE_INLINE void tma_load_2d_hint(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
@@ -303,7 +310,7 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
             mbar_init(&tempty[j], 4);
         }
         for (int j = 0; j < kTcMaxAbuf; ++j) {
-            mbar_init(&afull[j], 8);         // the dequantising warps
+            mbar_init(&afull[j], kTcDeqWarps);  // the dequantising warps
             mbar_init(&aempty[j], a.n_iss);  // tcgen05.commit
         }
         mbar_init(drain, a.n_iss);
@@ -480,14 +487,15 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
             for (int j = max(0, issued - S); j < issued; ++j)
                 if (!mbar_wait(&full[j % S], (j / S) & 1, a.err, kErrTimeoutFull)) break;
         }
-    } else if (warp == 1 || (kQ && warp >= 14) || (!kQ && warp == 6)) {
+    } else if (warp == 1 || (kQ && warp >= 6 + kTcDeqWarps) || (!kQ && warp == 6)) {
         // ------------------------------------------------------------ MMA issuers
         // A small tcgen05.mma blocks its issuing thread for about a hundred cycles
         // whatever N is, so one thread issuing M=128, N=32, K=16 steps reaches about
         // a third of the rate dequantised GGUF weights arrive at; issuers in separate
         // warps, each into its own accumulators, add up (A from TMEM; from shared memory
-        // two issuers still double the rate).  Issuers: warp 1, then 14, 15 (GGUF) or 6 (bf16).
-        const int iss = warp == 1 ? 0 : kQ ? warp - 13 : 1;
+        // two issuers still double the rate).  Issuers: warp 1, then the two after the
+        // dequantising warps (GGUF) or warp 6 (bf16).
+        const int iss = warp == 1 ? 0 : kQ ? warp - (5 + kTcDeqWarps) : 1;
         if (lane == 0 && iss < a.n_iss) {
             const uint32_t idesc = idesc_bf16(np);
             int it = 0, j = 0;
@@ -560,10 +568,10 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                 mbar_wait(drain, 0, a.err, kErrTimeoutFull);
             }
         }
-    } else if (kQ && warp >= 6 && warp < 14) {
+    } else if (kQ && warp >= 6 && warp < 6 + kTcDeqWarps) {
         // ------------------------------------------------------------ dequantising warps
         // thread -> one weight row (lane of the TMEM quarter warp % 4 may address) and
-        // half of the stage's 4 atoms (warps 6..9 the first two, 10..13 the last two).
+        // kTcAtPerThr of the stage's 4 atoms (part p of the warps 6 + 4p .. 9 + 4p).
         // Each value is the exact d*(q-8) (Q4_0) or d*q (Q8_0) rounded once to bf16.
         // Codes are read through the 128-byte swizzle the TMA wrote them with, so
         // each 8-row phase of a 16-byte load hits 8 distinct bank groups.
@@ -579,17 +587,22 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
             const uint8_t* st = smem + (size_t)s * a.stage_bytes;
             const uint8_t* crow = st + a.w_off + (size_t)row * 128;
             const uint4 sc = *reinterpret_cast<const uint4*>(st + a.s_off + (size_t)row * kTcQbs * 4);
-            // the scales of this thread's two atoms (register selects, no local array)
-            const uint32_t scw[2] = {part ? sc.z : sc.x, part ? sc.w : sc.y};
+            // the scales of this thread's atoms (register selects, no local array)
+            uint32_t scw[kTcAtPerThr];
+#pragma unroll
+            for (int jj = 0; jj < kTcAtPerThr; ++jj) {
+                const int j = part * kTcAtPerThr + jj;
+                scw[jj] = j == 0 ? sc.x : j == 1 ? sc.y : j == 2 ? sc.z : sc.w;
+            }
             bool buf_free = false;  // the operand buffer is waited for after the first atom's math
             // both atoms' code words loaded up front (their latency overlaps the first atom's math)
             constexpr int kWords = WF == kWQ4 ? 8 : 16;  // code words of one atom row
-            uint32_t qa[kTcQbs / 2][kWords];
+            uint32_t qa[kTcAtPerThr][kWords];
 #pragma unroll
-            for (int jj = 0; jj < kTcQbs / 2; ++jj)
+            for (int jj = 0; jj < kTcAtPerThr; ++jj)
 #pragma unroll
                 for (int t = 0; t < kWords / 4; ++t) {
-                    const int L = (part * (kTcQbs / 2) + jj) * (kWords / 4) + t;  // 16-byte chunk of the row
+                    const int L = (part * kTcAtPerThr + jj) * (kWords / 4) + t;  // 16-byte chunk of the row
                     const uint4 v = *reinterpret_cast<const uint4*>(crow + (size_t)(L >> 3) * kTcBM * 128 +
                                                                     (((L & 7) ^ (row & 7)) << 4));
                     qa[jj][4 * t] = v.x;
@@ -598,8 +611,8 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                     qa[jj][4 * t + 3] = v.w;
                 }
 #pragma unroll
-            for (int jj = 0; jj < kTcQbs / 2; ++jj) {
-                const int j = part * (kTcQbs / 2) + jj;
+            for (int jj = 0; jj < kTcAtPerThr; ++jj) {
+                const int j = part * kTcAtPerThr + jj;
                 const uint32_t* q = qa[jj];
                 const float d0 = __half2float(__ushort_as_half((unsigned short)(scw[jj] & 0xFFFFu)));
                 const float d1 = __half2float(__ushort_as_half((unsigned short)(scw[jj] >> 16)));
