@@ -18,8 +18,9 @@
 // padded to whole 128-code tiles), so a code chunk is a straight cp.async copy;
 // query chunks are read as float4 rows and written transposed, lanes across
 // queries (no shared-memory bank conflicts).  Both are double-buffered.  Thread
-// (qg, cg) keeps 4 queries x 8 codes: per dimension one 16-byte load of its
-// queries, two of its codes, and 16 packed f32x2 subtractions + 16 packed FMAs
+// (qg, cg) keeps 4 queries x 8 codes (codes 4cg..4cg+3 and 64+4cg..64+4cg+3 of the
+// tile, so each 8-lane phase of a code load is 128 contiguous bytes): per dimension
+// one 16-byte load of its queries, two of its codes, and 16 packed f32x2 subtractions + 16 packed FMAs
 // (each lane individually rounded: the same sequence as the scalar form).  Each
 // thread keeps the running (distance, index) minimum of its queries over its
 // codes, in ascending code order; the 16 threads of a query group merge by
@@ -129,8 +130,10 @@ __global__ void __launch_bounds__(kPkmThreads) k_pkm_assign(const float* __restr
 #pragma unroll 4
         for (int t = 0; t < kPkmDc; ++t) {
             const float4 qv = *reinterpret_cast<const float4*>(&qs[b][t][qg * 4]);
-            const float4 ca = *reinterpret_cast<const float4*>(&cs[b][t][cg * 8]);
-            const float4 cb = *reinterpret_cast<const float4*>(&cs[b][t][cg * 8 + 4]);
+            // codes 4 cg .. 4 cg + 3 and 64 + 4 cg .. 64 + 4 cg + 3: each 8-lane phase of a
+            // 16-byte load reads 128 contiguous bytes (no bank conflict)
+            const float4 ca = *reinterpret_cast<const float4*>(&cs[b][t][cg * 4]);
+            const float4 cb = *reinterpret_cast<const float4*>(&cs[b][t][kPkmC / 2 + cg * 4]);
             const float qa[4] = {qv.x, qv.y, qv.z, qv.w};
             const float2 cp[4] = {make_float2(ca.x, ca.y), make_float2(ca.z, ca.w), make_float2(cb.x, cb.y),
                                   make_float2(cb.z, cb.w)};
@@ -148,7 +151,7 @@ __global__ void __launch_bounds__(kPkmThreads) k_pkm_assign(const float* __restr
             for (int j = 0; j < 4; ++j)
 #pragma unroll
                 for (int p = 0; p < 4; ++p) {
-                    const int k = tile * kPkmC + cg * 8 + p * 2;
+                    const int k = tile * kPkmC + (p < 2 ? cg * 4 + p * 2 : kPkmC / 2 + cg * 4 + (p - 2) * 2);
                     if (k < n_codes && acc[j][p].x < bd[j]) bd[j] = acc[j][p].x, bi[j] = k;
                     if (k + 1 < n_codes && acc[j][p].y < bd[j]) bd[j] = acc[j][p].y, bi[j] = k + 1;
                 }
