@@ -241,7 +241,7 @@ struct TcKernelArgs {
 
 // Shared memory after the stage ring (offsets from the 1024-aligned base).
 struct TcSmem {
-    uint32_t abuf, full, empty, afull, aempty, tfull, tempty, drain, misc, xch, best, total;
+    uint32_t abuf, full, empty, xfull, afull, aempty, tfull, tempty, drain, misc, xch, best, total;
 };
 __host__ __device__ inline TcSmem tc_smem_layout(int stages, uint32_t stage_bytes, int np, int n_abuf, int kbs) {
     TcSmem L;
@@ -251,6 +251,8 @@ __host__ __device__ inline TcSmem tc_smem_layout(int stages, uint32_t stage_byte
     L.full = o;
     o += 8u * stages;
     L.empty = o;
+    o += 8u * stages;
+    L.xfull = o;  // GGUF: the stage's token tile (full[] then covers its codes and scales only)
     o += 8u * stages;
     L.afull = o;
     o += 8 * kTcMaxAbuf;
@@ -287,6 +289,7 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
     constexpr bool kQ = WF != kWBf16;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.full);
     uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L.empty);
+    uint64_t* xfull = reinterpret_cast<uint64_t*>(smem + L.xfull);
     uint64_t* tfull = reinterpret_cast<uint64_t*>(smem + L.tfull);
     uint64_t* tempty = reinterpret_cast<uint64_t*>(smem + L.tempty);
     uint64_t* drain = reinterpret_cast<uint64_t*>(smem + L.drain);
@@ -303,6 +306,7 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
         pdl_trigger();
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
+            mbar_init(&xfull[s], 1);
             mbar_init(&empty[s], a.n_iss);  // one tcgen05.commit per issuer
         }
         for (int j = 0; j < 2; ++j) {
@@ -373,8 +377,11 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
             const uint64_t pol = l2_policy_evict_first();
             const int kbs = a.kbs;
             const uint32_t xatom = (uint32_t)np * kTcBK * 2;
-            const uint32_t tx = kQ ? (uint32_t)kbs * xatom + (uint32_t)kTcBM * kbs * (a.cb + 4)
-                                   : (uint32_t)kbs * (kTcABytes + xatom);
+            // GGUF: full[] counts the codes and scales and xfull[] the token tile, so the
+            // dequantising warps can start on the first ring pass while the previous
+            // kernel (which produces the tokens) is still finishing
+            const uint32_t tx = kQ ? (uint32_t)kTcBM * kbs * (a.cb + 4) : (uint32_t)kbs * (kTcABytes + xatom);
+            const uint32_t tx_x = (uint32_t)kbs * xatom;
             auto load_w = [&](int tile, int kb, int s) {
                 uint8_t* st = smem + (size_t)s * a.stage_bytes;
                 if constexpr (kQ) {
@@ -449,7 +456,7 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
             auto load_x = [&](int kb, int s) {
                 uint8_t* xt = smem + (size_t)s * a.stage_bytes + a.x_off;
                 for (int j = 0; j < kbs; ++j)
-                    tma_load_2d(xt + (size_t)j * xatom, &tmx, (kb * kbs + j) * kTcBK, 0, &full[s]);
+                    tma_load_2d(xt + (size_t)j * xatom, &tmx, (kb * kbs + j) * kTcBK, 0, kQ ? &xfull[s] : &full[s]);
             };
             // 1. weights of the first pass of the ring: they do not depend on the
             //    previous kernel, so they stream while it finishes
@@ -464,6 +471,7 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
             pdl_wait();
             walk([&](int, int kb, int it) {
                 if (it >= first) return false;
+                if (kQ) mbar_arrive_expect_tx(&xfull[it], tx_x);
                 load_x(kb, it);
                 return true;
             });
@@ -477,6 +485,7 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                     return false;
                 }
                 mbar_arrive_expect_tx(&full[s], tx);
+                if (kQ) mbar_arrive_expect_tx(&xfull[s], tx_x);
                 load_w(tile, kb, s);
                 load_x(kb, s);
                 prefetch_w(it + a.pf);
@@ -484,8 +493,10 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                 return true;
             });
             // copies still in flight land before the CTA exits
-            for (int j = max(0, issued - S); j < issued; ++j)
+            for (int j = max(0, issued - S); j < issued; ++j) {
                 if (!mbar_wait(&full[j % S], (j / S) & 1, a.err, kErrTimeoutFull)) break;
+                if (kQ && !mbar_wait(&xfull[j % S], (j / S) & 1, a.err, kErrTimeoutFull)) break;
+            }
         }
     } else if (warp == 1 || (kQ && warp >= 6 + kTcDeqWarps) || (!kQ && warp == 6)) {
         // ------------------------------------------------------------ MMA issuers
@@ -510,7 +521,8 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
                 const uint32_t d = tmem + (uint32_t)((2 * iss + buf) * np);
                 for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % S;
-                    if (misc[1] || !mbar_wait(&full[s], (it / S) & 1, a.err, kErrTimeoutFull)) {
+                    if (misc[1] || !mbar_wait(&full[s], (it / S) & 1, a.err, kErrTimeoutFull) ||
+                        (kQ && !mbar_wait(&xfull[s], (it / S) & 1, a.err, kErrTimeoutFull))) {
                         misc[1] = 1;
                         return false;
                     }
@@ -1159,7 +1171,7 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
         p->n_abuf = 2;
         const size_t abuf = (size_t)best_kbs * kTcABytes;
         const TcSmem Lq = tc_smem_layout(0, 0, np, 0, 0);
-        if (2 * abuf + 2 * ((size_t)p->stage_bytes + 16) > kTcSmemBudget - Lq.total) p->n_abuf = 1;
+        if (2 * abuf + 2 * ((size_t)p->stage_bytes + 24) > kTcSmemBudget - Lq.total) p->n_abuf = 1;
         const char* qb = std::getenv("TI_TC_QBUF");
         if (qb && std::atoi(qb) == 1) p->n_abuf = 1;
         // up to 128 tokens the dequantised operands live in TMEM columns above the two
@@ -1178,7 +1190,7 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
         }
     }
     const size_t abuf_bytes = p->a_tmem ? 0 : (size_t)p->n_abuf * best_kbs * kTcABytes;
-    p->stages = (int)std::min<size_t>(12, (kTcSmemBudget - L0.total - abuf_bytes) / (p->stage_bytes + 16));
+    p->stages = (int)std::min<size_t>(12, (kTcSmemBudget - L0.total - abuf_bytes) / (p->stage_bytes + 24));  // + full, empty, xfull
     if (p->stages < 2) {
         if (why) *why = "tc_gemm: token tile too large for a two-stage ring";
         return false;
