@@ -236,7 +236,8 @@ struct TcPlan {
     int cb = 0, n_abuf = 0, threads = 0;       // GGUF: code bytes per atom row, dequantised buffers
     int a_tmem = 0;                            // GGUF: dequantised buffers in TMEM (else shared memory)
     uint32_t a_col = 0;                        // GGUF, a_tmem: TMEM column of dequantised buffer 0
-    int n_iss = 1;                             // MMA-issuing warps (GGUF with TMEM operands: up to 4)
+    int n_iss = 1;                             // MMA-issuing warps (GGUF with TMEM operands: up to 3)
+    int n_acc = 2;                             // accumulators per issuer (2: double-buffered across units)
     size_t smem = 0;
     size_t ws_floats = 0;  // partial-tile workspace this launch needs
     const void* func = nullptr;

@@ -215,8 +215,9 @@ struct TcKernelArgs {
     int cb, n_abuf;
     int a_tmem;      // dequantised operand buffers in TMEM columns [a_col + b * kbs * 32, ...) (else shared memory)
     uint32_t a_col;
+    int n_acc;       // accumulators per issuer: 2 (the epilogue of one unit overlaps the next) or 1
     int n_iss;       // MMA-issuing warps: issuer i takes K steps i, i + n_iss, ... of each stage into its
-                     // own accumulator pair, TMEM columns [(2i + buf) * np, +np); the epilogue sums them in order
+                     // own accumulators, TMEM columns [(i * n_acc + buf) * np, +np); the epilogue sums them in order
     uint32_t stage_bytes, tmem_cols;
     uint16_t* out;
     int out_stride;
@@ -512,13 +513,13 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
             int it = 0, j = 0;
             bool issued = false;
             units([&](int, int kb0, int kb1, bool) {
-                const int buf = j & 1;
-                if (misc[1] || !mbar_wait(&tempty[buf], ((j >> 1) & 1) ^ 1, a.err, kErrTimeoutEmpty)) {
+                const int buf = j % a.n_acc;
+                if (misc[1] || !mbar_wait(&tempty[buf], ((j / a.n_acc) & 1) ^ 1, a.err, kErrTimeoutEmpty)) {
                     misc[1] = 1;
                     return false;
                 }
                 tc_fence_after();
-                const uint32_t d = tmem + (uint32_t)((2 * iss + buf) * np);
+                const uint32_t d = tmem + (uint32_t)((iss * a.n_acc + buf) * np);
                 for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % S;
                     if (misc[1] || !mbar_wait(&full[s], (it / S) & 1, a.err, kErrTimeoutFull) ||
@@ -712,12 +713,12 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
         pdl_wait();  // residual rows are the previous kernel's output
         int j = 0;
         units([&](int tile, int, int, bool first) {
-            const int buf = j & 1;
+            const int buf = j % a.n_acc;
             // one leader waits for the accumulator and the named barrier hands the
             // outcome to all four warps, so they stop (or go on) together: a
             // barrier that some warps skip would never complete
             if (et == 0) {
-                const bool ok = misc[1] == 0 && mbar_wait(&tfull[buf], (j >> 1) & 1, a.err, kErrTimeoutFull);
+                const bool ok = misc[1] == 0 && mbar_wait(&tfull[buf], (j / a.n_acc) & 1, a.err, kErrTimeoutFull);
                 misc[3] = ok ? 0u : 1u;
                 if (!ok) misc[1] = 1;
             }
@@ -732,7 +733,7 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kTcThreads : kTcThreadsQ, 1)
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         float w[16];
-                        tmem_ld16(tbase + (uint32_t)(2 * i * np + c * 32 + h * 16), w);
+                        tmem_ld16(tbase + (uint32_t)(i * a.n_acc * np + c * 32 + h * 16), w);
 #pragma unroll
                         for (int k = 0; k < 16; ++k) v[h * 16 + k] += w[k];
                     }
@@ -1147,6 +1148,7 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
     p->a_tmem = 0;
     p->a_col = 0;
     p->n_iss = 1;
+    p->n_acc = 2;
     if (!q && 4 * np <= 512) {
         // bf16: two issuers (four np-column accumulators) while TMEM holds them
         const char* bi = std::getenv("TI_TC_ISS");
@@ -1185,7 +1187,9 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
             while (p->n_iss > 1 && 2 * p->n_iss * np > 256) --p->n_iss;
             const char* qi = std::getenv("TI_TC_QISS");
             if (qi && std::atoi(qi) >= 1) p->n_iss = std::min(p->n_iss, std::atoi(qi));
-            p->a_col = (uint32_t)(2 * p->n_iss * np + 127) / 128 * 128;
+            const char* qa = std::getenv("TI_TC_QACC");
+            if (qa && std::atoi(qa) == 1) p->n_acc = 1;
+            p->a_col = (uint32_t)(p->n_acc * p->n_iss * np + 127) / 128 * 128;
             p->n_abuf = std::min(kTcMaxAbuf, (int)((512 - p->a_col) / (uint32_t)(best_kbs * 32)));
         }
     }
@@ -1205,7 +1209,7 @@ bool tc_plan(const GemvArgs& g, int epi, int device, size_t ws_floats_cap, TcPla
     const char* pfe = std::getenv("TI_TC_PF");
     p->pf = pfe ? std::max(0, std::atoi(pfe)) : 0;
     uint32_t cols = 32;
-    while (cols < (uint32_t)(2 * p->n_iss * np)) cols <<= 1;
+    while (cols < (uint32_t)(p->n_acc * p->n_iss * np)) cols <<= 1;
     p->tmem_cols = p->a_tmem ? 512u : cols;
     p->func = tc_func(epi, g.wfmt);
     p->threads = q ? kTcThreadsQ : kTcThreads;
@@ -1257,6 +1261,7 @@ cudaError_t tc_launch(const GemvArgs& g, int epi, const TcPlan& p, float* ws, un
     a.a_tmem = p.a_tmem;
     a.a_col = p.a_col;
     a.n_iss = p.n_iss;
+    a.n_acc = p.n_acc;
     a.tmem_cols = p.tmem_cols;
     a.out = g.out;
     a.out_stride = g.out_stride;
