@@ -134,8 +134,8 @@ ti_status ti_op_paged_attention(const void* qkv, int batch, int n_heads, int n_k
  * fully reserved by another framework's allocator).  No counterpart in the
  * reference.  Calls no allocator: the scratch is a fixed 8 MiB array that every
  * GPU loading this library holds until exit.  The first call on a device looks
- * up that array's device address (make it before any stream capture); that
- * address belongs to the device's CUDA context, so do not call this entry on a
+ * up that array's device address with a synchronous runtime query; that address
+ * belongs to the device's CUDA context, so do not call this entry on a
  * device after resetting it (cudaDeviceReset).  Sizes whose scratch exceeds
  * 8 MiB return TI_ERR_INVALID.  All calls share the array, so calls that
  * overlap on the GPU race; order them on one stream.  As with
