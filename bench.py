@@ -295,7 +295,7 @@ def run_reference(args, rank, world):
                 line["ref_gpu_b1"] = reference_gpu_decode(max(4, args.steps), min(args.warmup, 3))
             except Exception as exc:  # noqa: BLE001 - the extra leg reports its failure; the line stands
                 line["ref_gpu_b1"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ------------------------------------------------------------------ our arm
@@ -795,7 +795,10 @@ def run_ours(args, rank, world):
             "data": "synthetic (seeded N(0,0.02) bf16 weights, uniform random 512-token prompts)",
             "config": {"workload": "Llama-3-8B-shape bf16 greedy decode, batch 1, 512-token prompt",
                        "batch": 1, "prompt": PROMPT, "ctx_avg": r1["ctx_avg"],
-                       "parallelism": "single" if world == 1 else f"tp{world} (NCCL all-reduce after o/down)",
+                       "parallelism": "single" if world == 1 else
+                       f"tp{world} (all-reduce after o/down: " +
+                       ("NCCL)" if os.environ.get("TI_TP_ALLREDUCE") == "nccl" else
+                        "fused into the projection epilogue over NVLink peer memory)"),
                        "l2": "weights (15 GB) >> L2 (126 MB): every step streams from HBM; no flush"},
             "e2e": {k: (round(v, 3) if isinstance(v, float) else v) for k, v in r1["e2e"].items()},
             "roofline": roof,
@@ -832,7 +835,7 @@ def run_ours(args, rank, world):
             line["pkm"] = pkm
         if cb:
             line["cpu_baseline"] = cb
-        print(json.dumps(line), flush=True)
+        emit(line)
     eng.close()
     if world > 1:
         import torch.distributed as dist
@@ -841,7 +844,23 @@ def run_ours(args, rank, world):
         dist.destroy_process_group()
 
 
+# The JSON line goes to the process's original stdout; everything else the run prints
+# (NCCL's version banner, the reference's loader) goes to stderr, so stdout holds
+# exactly one line.
+_JSON_FD = None
+
+
+def emit(line):
+    text = (json.dumps(line) + "\n").encode()
+    if _JSON_FD is None:
+        sys.stdout.write(text.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, text)
+
+
 def main():
+    global _JSON_FD
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=64)
@@ -878,6 +897,10 @@ def main():
     args.warmup = max(3, args.warmup)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    if not args.profile:
+        sys.stdout.flush()
+        _JSON_FD = os.dup(1)
+        os.dup2(2, 1)
     if args.profile:
         run_profile(args)
     elif args.impl == "reference":
