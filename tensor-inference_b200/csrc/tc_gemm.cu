@@ -12,16 +12,17 @@
 // (padded to a multiple of 32; rows past the batch are zero-filled by TMA).
 // D = W_tile (128 x K) * X^T (K x np) accumulates in TMEM, fp32.
 //
-// Structure (one persistent CTA per SM, 192 threads):
+// Structure (one persistent CTA per SM; bf16 weights 224 threads, GGUF 512):
 //   warp 0      TMA producer: 2-D tiled bulk-tensor loads (128-byte swizzle) of
 //               the weight tile (L2 evict-first) and the token tile into a
 //               ring of shared-memory stages.  Weight loads of the first ring
 //               are issued before griddepcontrol.wait, overlapping the previous
 //               kernel's tail (weights do not depend on it).
-//   warp 1      allocates TMEM (two accumulators of np columns) and one lane
+//   warp 1      allocates TMEM and, with the other issuer warps below, one lane
 //               issues tcgen05.mma (kind::f16, bf16 x bf16 -> fp32, M=128,
-//               N=np, K=16 per instruction, 4 per stage); tcgen05.commit frees
-//               each stage and signals a finished accumulator.
+//               N=np, K=16 per instruction, 16 per stage split over the issuers,
+//               each into its own two accumulators of np columns); tcgen05.commit
+//               frees each stage and signals a finished accumulator.
 //   warps 2-5   epilogue: tcgen05.ld of the accumulator (warp w owns TMEM
 //               lanes 32*(w%4)..+31 = 32 weight rows), fused epilogue, stores.
 //               Double-buffered TMEM lets the epilogue of one tile overlap the
